@@ -1,0 +1,289 @@
+"""Python handle on the test oracle. TEST INFRASTRUCTURE, NOT PRODUCT CODE.
+
+Two libraries sit behind it:
+
+* ``oracle/_build/liborc.so`` -- our f64 C restatement of the reference algorithms (restate.c),
+  each function citing the reference file:line it follows;
+* ``oracle/_ref/libref_cpu.so`` / ``libref_cudafb.so`` -- the reference's own C sources
+  (ffi/pufferffi.c, ffi/pufferblas.c, ffi/puffercuda.cu) compiled where they lie, used to pin the
+  restatement and, on the GPU box, as the timed CPU baseline of the reference arm.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU legs import this module.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import struct
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_ORC = None
+_REF_CPU = None
+_REF_CUDAFB = None
+
+_dp = C.POINTER(C.c_double)
+_sz = C.c_size_t
+_d = C.c_double
+
+
+def _ptr(a):
+    return a.ctypes.data_as(_dp) if a is not None else None
+
+
+def build():
+    """Compile liborc.so (and, when the reference tree is present, oracle/_ref)."""
+    import subprocess
+
+    subprocess.check_call(["make", "-s", "-C", HERE, "all"])
+    if os.path.isdir(os.environ.get("PL_REFERENCE_DIR", "/root/reference")):
+        subprocess.check_call(["make", "-s", "-C", HERE, "ref"])
+
+
+def orc():
+    global _ORC
+    if _ORC is None:
+        path = os.path.join(HERE, "_build", "liborc.so")
+        if not os.path.exists(path):
+            build()
+        lib = C.CDLL(path)
+        lib.orc_rng_next.restype = C.c_uint64
+        lib.orc_rng_next.argtypes = [C.POINTER(C.c_uint64)]
+        lib.orc_vtrace.argtypes = [_dp] * 4 + [_sz, _sz] + [_d] * 4 + [_dp]
+        lib.orc_vtrace_mingru.argtypes = [_dp] * 5 + [_sz, _sz] + [_d] * 4 + [_dp]
+        lib.orc_adv_l1.argtypes = [_dp, _sz, _sz, _dp]
+        lib.orc_gae_soa.argtypes = [_dp] * 3 + [_sz, _sz, _d, _d, _dp]
+        lib.orc_shuffle_perm.argtypes = [_sz, _sz, C.c_uint64, _dp]
+        lib.orc_normalize_adv.argtypes = [_dp, _sz, _dp]
+        lib.orc_frob_norm.restype = _d
+        lib.orc_frob_norm.argtypes = [_dp, C.c_int, C.c_int]
+        lib.orc_newton_schulz.argtypes = [_dp, C.c_int, C.c_int, _d, _dp, C.c_int, _dp]
+        lib.orc_muon_stepmat.argtypes = [_dp, _dp, _dp, C.c_int, C.c_int, _d, _d, _d, _d, _dp, C.c_int, _dp, _dp]
+        lib.orc_muon_stepvec.argtypes = [_dp, _dp, _dp, C.c_int, _d, _d, _d, _dp, _dp]
+        lib.orc_mlp_param_count.restype = _sz
+        lib.orc_mlp_param_count.argtypes = [_sz] * 4
+        lib.orc_mlp_ppo_grad.argtypes = [_dp] * 7 + [_sz] * 5 + [C.c_int] + [_d] * 4 + [_dp] * 3
+        lib.orc_grad_clip.argtypes = [_dp, _sz, _d, _d]
+        lib.orc_apply_muon.argtypes = [_dp, _dp] + [_sz] * 4 + [_d] * 4 + [_dp, C.c_int]
+        lib.orc_train_update.argtypes = ([_dp] * 8 + [_sz] * 5 + [C.c_int] + [_sz] * 2 + [_d] * 9
+                                         + [_dp, C.c_int])
+        lib.orc_init_mlp.restype = C.c_uint64
+        lib.orc_init_mlp.argtypes = [_sz, _sz, _sz, C.c_uint64, _dp]
+        lib.orc_cosine_lr.restype = _d
+        lib.orc_cosine_lr.argtypes = [_d, _d, _sz, _sz]
+        _ORC = lib
+    return _ORC
+
+
+# ---------------------------------------------------------------------------------------------
+# The reference's PufferLib-tuned Newton-Schulz table (Puffer/Float/Muon.lean:64-67) and the
+# single-row quintic schedule BASELINE's timing configs name.
+MUON_COEFFS = np.array([[4.0848, -6.8946, 2.9270], [3.9505, -6.3029, 2.6377], [3.7418, -5.5913, 2.3037],
+                        [2.8769, -3.1427, 1.2046], [2.8366, -3.0525, 1.2012]], dtype=np.float64)
+QUINTIC_COEFFS = np.array([[3.4445, -4.7750, 2.0315]] * 5, dtype=np.float64)
+
+
+def f64(a):
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float64))
+
+
+def vtrace(rew, val, term, imp, B, T, gamma, lam, rho, c):
+    out = np.zeros(B * T)
+    rew, val, term, imp = map(f64, (rew, val, term, imp))
+    orc().orc_vtrace(_ptr(rew), _ptr(val), _ptr(term), _ptr(imp), B, T, gamma, lam, rho, c, _ptr(out))
+    return out
+
+
+def vtrace_mingru(rew, val, term, imp, bootv, B, T, gamma, lam, rho, c):
+    out = np.zeros(B * T)
+    rew, val, term, imp, bootv = map(f64, (rew, val, term, imp, bootv))
+    orc().orc_vtrace_mingru(_ptr(rew), _ptr(val), _ptr(term), _ptr(imp), _ptr(bootv), B, T, gamma, lam, rho, c,
+                            _ptr(out))
+    return out
+
+
+def adv_l1(adv, N, T):
+    out = np.zeros(N)
+    adv = f64(adv)
+    orc().orc_adv_l1(_ptr(adv), N, T, _ptr(out))
+    return out
+
+
+def gae_soa(vals, rews, terms, N, T, gamma, lam):
+    out = np.zeros(2 * N * T)
+    vals, rews, terms = map(f64, (vals, rews, terms))
+    orc().orc_gae_soa(_ptr(vals), _ptr(rews), _ptr(terms), N, T, gamma, lam, _ptr(out))
+    return out
+
+
+def shuffle_perm(NT, epochs, rng):
+    out = np.zeros(NT * epochs)
+    orc().orc_shuffle_perm(NT, epochs, C.c_uint64(rng & 0xFFFFFFFFFFFFFFFF), _ptr(out))
+    return out
+
+
+def normalize_adv(adv):
+    adv = f64(adv)
+    out = np.zeros_like(adv)
+    orc().orc_normalize_adv(_ptr(adv), adv.size, _ptr(out))
+    return out
+
+
+def frob_norm(X, rows, cols):
+    X = f64(X)
+    return orc().orc_frob_norm(_ptr(X), rows, cols)
+
+
+def newton_schulz(X0, rows, cols, eps, coeffs=MUON_COEFFS):
+    X0 = f64(X0)
+    co = f64(coeffs)
+    out = np.zeros(rows * cols)
+    orc().orc_newton_schulz(_ptr(X0), rows, cols, eps, _ptr(co), co.shape[0], _ptr(out))
+    return out
+
+
+def muon_stepmat(W, G, M, rows, cols, lr, wd, mu, eps, coeffs=MUON_COEFFS):
+    W, G, M = map(f64, (W, G, M))
+    co = f64(coeffs)
+    nW = np.zeros(rows * cols)
+    nM = np.zeros(rows * cols)
+    orc().orc_muon_stepmat(_ptr(W), _ptr(G), _ptr(M), rows, cols, lr, wd, mu, eps, _ptr(co), co.shape[0], _ptr(nW),
+                           _ptr(nM))
+    return nW, nM
+
+
+def param_count(D, H, A, L=1):
+    return int(orc().orc_mlp_param_count(D, H, A, L))
+
+
+def mlp_ppo_grad(params, obs, acts, advs, rets, olps, N, D, H, A, L=1, act=0, vf=0.5, ent=0.01, clip=0.2, ov=None,
+                 vfClip=0.0):
+    P = param_count(D, H, A, L)
+    g = np.zeros(P)
+    nlp = np.zeros(N)
+    nv = np.zeros(N)
+    params, obs, acts, advs, rets, olps = map(f64, (params, obs, acts, advs, rets, olps))
+    ovp = _ptr(f64(ov)) if ov is not None else None
+    orc().orc_mlp_ppo_grad(_ptr(params), _ptr(obs), _ptr(acts), _ptr(advs), _ptr(rets), _ptr(olps), ovp, N, D, H,
+                           A, L, act, vf, ent, clip, vfClip, _ptr(g), _ptr(nlp), _ptr(nv))
+    return g, nlp, nv
+
+
+def grad_clip(g, maxNorm, sc):
+    g = f64(g).copy()
+    orc().orc_grad_clip(_ptr(g), g.size, maxNorm, sc)
+    return g
+
+
+def apply_muon(pm, g, D, H, A, L, lr, wd, mu, eps, coeffs=MUON_COEFFS):
+    pm = f64(pm).copy()
+    g = f64(g)
+    co = f64(coeffs)
+    orc().orc_apply_muon(_ptr(pm), _ptr(g), D, H, A, L, lr, wd, mu, eps, _ptr(co), co.shape[0])
+    return pm
+
+
+def train_update(pm, obs, acts, adv, ret, olp, perm, NT, D, H, A, epochs, numMB, lr, wd, mu, eps, vf, ent, clip,
+                 L=1, act=0, ov=None, vfClip=0.0, maxGradNorm=0.0, coeffs=MUON_COEFFS):
+    pm = f64(pm).copy()
+    obs, acts, adv, ret, olp, perm = map(f64, (obs, acts, adv, ret, olp, perm))
+    co = f64(coeffs)
+    ovp = _ptr(f64(ov)) if ov is not None else None
+    orc().orc_train_update(_ptr(pm), _ptr(obs), _ptr(acts), _ptr(adv), _ptr(ret), _ptr(olp), ovp, _ptr(perm), NT,
+                           D, H, A, L, act, epochs, numMB, lr, wd, mu, eps, vf, ent, clip, vfClip, maxGradNorm,
+                           _ptr(co), co.shape[0])
+    return pm
+
+
+def init_mlp(din, H, dout, seed):
+    P = H * din + H + dout * H + dout
+    flat = np.zeros(P)
+    s = orc().orc_init_mlp(din, H, dout, C.c_uint64(seed), _ptr(flat))
+    return flat, int(s)
+
+
+def cosine_lr(lr, min_ratio, u, updates):
+    return float(orc().orc_cosine_lr(lr, min_ratio, u, updates))
+
+
+# ---------------------------------------------------------------------------------------------
+# The reference's own C, loaded with a malloc-backed Lean object shim (include/lean_compat).
+_libc = C.CDLL(None)
+_libc.malloc.restype = C.c_void_p
+_libc.malloc.argtypes = [C.c_size_t]
+_SARRAY_DATA = 24  # m_rc(4) + packed tag word(4) + m_size(8) + m_capacity(8)
+
+
+def ref_available():
+    return os.path.exists(os.path.join(HERE, "_ref", "libref_cpu.so"))
+
+
+def ref_cpu():
+    global _REF_CPU
+    if _REF_CPU is None:
+        _REF_CPU = C.CDLL(os.path.join(HERE, "_ref", "libref_cpu.so"))
+    return _REF_CPU
+
+
+def ref_cudafb():
+    """puffercuda.cu built for its host fallbacks. Loading it on a machine WITH a GPU would send its
+    calls to the reference's own kernels, so it is refused whenever a device is visible."""
+    global _REF_CUDAFB
+    if _REF_CUDAFB is None:
+        try:
+            import torch
+
+            if torch.cuda.is_available():
+                raise RuntimeError("libref_cudafb.so is for golden-vector generation on a GPU-less host only")
+        except ImportError:
+            pass
+        _REF_CUDAFB = C.CDLL(os.path.join(HERE, "_ref", "libref_cudafb.so"))
+    return _REF_CUDAFB
+
+
+def lean_float_array(a) -> int:
+    """A fresh Lean FloatArray (rc 1) holding a copy of `a`; the callee consumes it (lean_dec)."""
+    a = f64(a).ravel()
+    n = a.size
+    p = _libc.malloc(_SARRAY_DATA + 8 * max(n, 1))
+    hdr = struct.pack("<iIQQ", 1, (248 << 24) | (8 << 16), n, n)
+    C.memmove(p, hdr, len(hdr))
+    if n:
+        C.memmove(p + _SARRAY_DATA, a.ctypes.data, 8 * n)
+    return p
+
+
+def read_float_array(p) -> np.ndarray:
+    n = struct.unpack("<Q", C.string_at(p + 8, 8))[0]
+    return np.frombuffer(C.string_at(p + _SARRAY_DATA, 8 * n), dtype=np.float64).copy()
+
+
+def ctor_field(p, i) -> int:
+    return struct.unpack("<Q", C.string_at(p + 8 + 8 * i, 8))[0]
+
+
+def ctor_tag(p) -> int:
+    return C.string_at(p + 7, 1)[0]
+
+
+def ref_call(lib, name, restype, *args):
+    f = getattr(lib, name)
+    f.restype = restype
+    conv = []
+    for a in args:
+        if isinstance(a, float):
+            conv.append(C.c_double(a))
+        elif isinstance(a, tuple) and a[0] == "u64":
+            conv.append(C.c_uint64(a[1]))
+        elif isinstance(a, tuple) and a[0] == "u8":
+            conv.append(C.c_uint8(a[1]))
+        elif isinstance(a, tuple) and a[0] == "obj":
+            conv.append(C.c_void_p(a[1]))
+        else:
+            conv.append(C.c_size_t(a))
+    return f(*conv)
+
+
+def FA(a):
+    return ("obj", lean_float_array(a))

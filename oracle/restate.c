@@ -1,0 +1,554 @@
+/* oracle/restate.c -- TEST INFRASTRUCTURE, NOT PRODUCT CODE.
+ *
+ * A CPU restatement, in plain f64 C, of the reference algorithms on the PPO+Muon update path.
+ * Each function cites the reference file:line it follows (paths are relative to the reference
+ * project root). Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+ * arm call into this library, and only as the checker or the timed CPU baseline; the product
+ * library never links or loads it.
+ *
+ * Pinning: the f64 functions here are checked bit-for-bit against the reference's own C code
+ * compiled from its sources (oracle/_ref, see oracle/Makefile) on the seeded known-answer inputs
+ * of the reference's verify-* modes; the resulting vectors are committed under tests/golden/.
+ *
+ * Build with -O2 -ffp-contract=off (no fused multiply-add), which is what makes the f64 folds
+ * reproduce the reference's IEEE op order exactly (lakefile.lean:69-71, 101-103). */
+#include <math.h>
+#include <stddef.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define ORC_GOLD 0x9E3779B97F4A7C15ULL
+
+/* ---------------------------------------------------------------- PRNG -------------------- */
+/* rngNext: one splitmix64 step (Puffer/RL/Train.lean:18-24). Returns the word; *s advances by GOLD. */
+uint64_t orc_rng_next(uint64_t* s) {
+  uint64_t sp = *s + ORC_GOLD;
+  *s = sp;
+  uint64_t z = sp;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+/* uniform01: top 53 bits over 2^53 (Puffer/RL/Train.lean:27-28). */
+double orc_uniform01(uint64_t w) { return (double)(w >> 11) / 9007199254740992.0; }
+/* randF lo hi: lo + (hi-lo)*uniform01 (Exe/Puffer.lean:65-67). */
+double orc_randF(double lo, double hi, uint64_t* s) {
+  uint64_t w = orc_rng_next(s);
+  return lo + (hi - lo) * orc_uniform01(w);
+}
+
+/* ---------------------------------------------------------------- advantage scans ---------- */
+/* computePuffAdvantageV applied to each of B rows of a B x T row-major batch
+ * (Puffer/RL/VecTrain.lean:98-114): adv[T-1]=0; t=T-2..0; terminal = term != 0. */
+void orc_vtrace(const double* rew, const double* val, const double* term, const double* imp, size_t B, size_t T,
+                double gamma, double lam, double rhoClip, double cClip, double* adv) {
+  for (size_t b = 0; b < B; b++) {
+    const double* rw = rew + b * T;
+    const double* vv = val + b * T;
+    const double* tm = term + b * T;
+    const double* im = imp + b * T;
+    double* ad = adv + b * T;
+    for (size_t t = 0; t < T; t++) ad[t] = 0.0;
+    double lastA = 0.0;
+    for (size_t i = 0; i + 1 < T; i++) {
+      size_t t = T - 2 - i;
+      double nnt = (tm[t] != 0.0) ? 0.0 : 1.0;
+      double iv = im[t];
+      double rho = iv < rhoClip ? iv : rhoClip;
+      double c = iv < cClip ? iv : cClip;
+      double rr = rw[t];
+      double r = rr > 1.0 ? 1.0 : (rr < -1.0 ? -1.0 : rr);
+      double delta = rho * (r + gamma * vv[t + 1] * nnt - vv[t]);
+      lastA = delta + gamma * lam * c * lastA * nnt;
+      ad[t] = lastA;
+    }
+  }
+}
+
+/* vtraceMinGRUFlat (Puffer/RL/VecTrain.lean:122-139): scalar delta rho*r + gamma*V'*nnt - V, the last
+ * step bootstrapped from bootv[row], terminal = term > 0.5, t = T-1..0. `min` is Lean's Float min
+ * (a <= b ? a : b), identical to the `<` ternary on finite inputs. */
+void orc_vtrace_mingru(const double* rew, const double* val, const double* term, const double* imp,
+                       const double* bootv, size_t B, size_t T, double gamma, double lam, double rhoClip,
+                       double cClip, double* adv) {
+  for (size_t e = 0; e < B; e++) {
+    double lastA = 0.0;
+    for (size_t i = 0; i < T; i++) {
+      size_t t = T - 1 - i, idx = e * T + t;
+      double nnt = term[idx] > 0.5 ? 0.0 : 1.0;
+      double vNext = (t + 1 < T) ? val[e * T + t + 1] : bootv[e];
+      double rho = imp[idx] <= rhoClip ? imp[idx] : rhoClip;
+      double c = imp[idx] <= cClip ? imp[idx] : cClip;
+      double rr = rew[idx];
+      double r = rr > 1.0 ? 1.0 : (rr < -1.0 ? -1.0 : rr);
+      double delta = rho * r + gamma * vNext * nnt - val[idx];
+      lastA = delta + gamma * lam * c * lastA * nnt;
+      adv[idx] = lastA;
+    }
+  }
+}
+
+/* Sigma_t |adv[e,t]| per segment, sequential in t (the host prioSample's inner sum,
+ * ffi/pufferffi.c:1094-1106 consumes it; device twin ffi/puffercuda.cu:311-312). */
+void orc_adv_l1(const double* adv, size_t N, size_t T, double* out) {
+  for (size_t e = 0; e < N; e++) {
+    double s = 0.0;
+    for (size_t t = 0; t < T; t++) s += fabs(adv[e * T + t]);
+    out[e] = s;
+  }
+}
+
+/* Truncated GAE over env segments with returns (the MLP trainer's buildBatchSoA; the reference's C twin is
+ * ffi/pufferffi.c:946-971). It is computePuffAdvantageV with rho = c = 1, so it is restated through
+ * orc_vtrace's recurrence with the importance factors fixed at one. out = [adv(NT); ret(NT)]. */
+void orc_gae_soa(const double* vals, const double* rews, const double* terms, size_t N, size_t T, double gamma,
+                 double lam, double* out) {
+  size_t NT = N * T;
+  double* adv = out;
+  double* ret = out + NT;
+  for (size_t e = 0; e < N; e++) {
+    size_t base = e * T;
+    for (size_t t = 0; t < T; t++) adv[base + t] = 0.0;
+    double lastA = 0.0;
+    for (size_t i = 0; i + 1 < T; i++) {
+      size_t t = base + (T - 2 - i);
+      double nnt = (terms[t] != 0.0) ? 0.0 : 1.0;
+      double rr = rews[t];
+      double r = rr > 1.0 ? 1.0 : (rr < -1.0 ? -1.0 : rr);
+      double delta = r + gamma * vals[t + 1] * nnt - vals[t];
+      lastA = delta + gamma * lam * lastA * nnt;
+      adv[t] = lastA;
+    }
+  }
+  for (size_t t = 0; t < NT; t++) ret[t] = adv[t] + vals[t];
+}
+
+/* ---------------------------------------------------------------- bookkeeping -------------- */
+/* shuffleIdx (Puffer/RL/VecTrain.lean:240-252) once per epoch, states chained, f64-encoded into
+ * perm[epochs*NT] (the flat layout ffi/pufferffi.c:1017-1041 returns). */
+void orc_shuffle_perm(size_t NT, size_t epochs, uint64_t rng, double* out) {
+  size_t* a = (size_t*)malloc(sizeof(size_t) * (NT ? NT : 1));
+  uint64_t s = rng;
+  for (size_t e = 0; e < epochs; e++) {
+    for (size_t i = 0; i < NT; i++) a[i] = i;
+    for (size_t i = 0; i < NT; i++) {
+      size_t j = NT - 1 - i;
+      uint64_t w = orc_rng_next(&s);
+      size_t k = (size_t)(w % (uint64_t)(j + 1));
+      size_t tmp = a[j];
+      a[j] = a[k];
+      a[k] = tmp;
+    }
+    for (size_t i = 0; i < NT; i++) out[e * NT + i] = (double)a[i];
+  }
+  free(a);
+}
+
+/* mkBatchArrays-style row gather: dst rows = src rows at idx (ffi/pufferffi.c:1046-1081 semantics). */
+void orc_gather_minibatch(const double* obs, const double* act, const double* adv, const double* ret,
+                          const double* olp, const double* idx, size_t Nmb, size_t D, double* mbObs, double* mbAct,
+                          double* mbAdv, double* mbRet, double* mbOlp) {
+  for (size_t k = 0; k < Nmb; k++) {
+    size_t r = (size_t)idx[k];
+    memcpy(mbObs + k * D, obs + r * D, sizeof(double) * D);
+    mbAct[k] = act[r];
+    mbAdv[k] = adv[r];
+    mbRet[k] = ret[r];
+    mbOlp[k] = olp[r];
+  }
+}
+
+/* normalizeAdv (Puffer/RL/NNTrain.lean:274-279): sequential folds, population std, +1e-8. */
+void orc_normalize_adv(const double* adv, size_t n, double* out) {
+  double dn = (double)n;
+  double s = 0.0;
+  for (size_t i = 0; i < n; i++) s = s + adv[i];
+  double mean = s / dn;
+  double v = 0.0;
+  for (size_t i = 0; i < n; i++) v = v + (adv[i] - mean) * (adv[i] - mean);
+  double std = sqrt(v / dn);
+  for (size_t i = 0; i < n; i++) out[i] = (adv[i] - mean) / (std + 1e-8);
+}
+
+/* ---------------------------------------------------------------- Muon --------------------- */
+/* PufferLib's tuned 5-row quintic schedule (Puffer/Float/Muon.lean:64-67). */
+const double ORC_MUON_COEFFS[5][3] = {{4.0848, -6.8946, 2.9270}, {3.9505, -6.3029, 2.6377},
+                                      {3.7418, -5.5913, 2.3037}, {2.8769, -3.1427, 1.2046},
+                                      {2.8366, -3.0525, 1.2012}};
+
+/* matmul (Puffer/Float/Muon.lean:19-31): C[i][j] = fold_l s + A[i][l]*B[l][j] from 0.0. */
+static void orc_matmul(const double* A, const double* B, int m, int k, int n, double* C) {
+  for (int i = 0; i < m; i++)
+    for (int j = 0; j < n; j++) {
+      double s = 0.0;
+      for (int l = 0; l < k; l++) s = s + A[(long)i * k + l] * B[(long)l * n + j];
+      C[(long)i * n + j] = s;
+    }
+}
+static void orc_transpose(const double* X, int rows, int cols, double* Xt) {
+  for (int i = 0; i < rows; i++)
+    for (int j = 0; j < cols; j++) Xt[(long)j * rows + i] = X[(long)i * cols + j];
+}
+/* frobNorm (Puffer/Float/Muon.lean:45-46): two-level fold (per-row sum of squares, then rows). */
+double orc_frob_norm(const double* X, int rows, int cols) {
+  double s = 0.0;
+  for (int i = 0; i < rows; i++) {
+    double rs = 0.0;
+    for (int j = 0; j < cols; j++) {
+      double x = X[(long)i * cols + j];
+      rs = rs + x * x;
+    }
+    s = s + rs;
+  }
+  return sqrt(s);
+}
+
+/* newtonSchulzWith (Puffer/Float/Muon.lean:74-90) over an arbitrary `iters` x 3 coefficient table:
+ * X = X0 / (frob + eps); per row (a,b,c): rows<=cols: A=X X^T, AX, A(AX); else A=X^T X, XA, (XA)A;
+ * X = a X + b (AX|XA) + c (AAX|XAA). */
+void orc_newton_schulz(const double* X0, int rows, int cols, double eps, const double* coeffs, int iters,
+                       double* Xout) {
+  long n = (long)rows * cols;
+  int mn = rows < cols ? rows : cols;
+  double* Xt = (double*)malloc(sizeof(double) * n);
+  double* A = (double*)malloc(sizeof(double) * (long)mn * mn);
+  double* P = (double*)malloc(sizeof(double) * n);
+  double* Q = (double*)malloc(sizeof(double) * n);
+  double inv = 1.0 / (orc_frob_norm(X0, rows, cols) + eps);
+  for (long i = 0; i < n; i++) Xout[i] = inv * X0[i];
+  for (int it = 0; it < iters; it++) {
+    double a = coeffs[3 * it + 0], b = coeffs[3 * it + 1], c = coeffs[3 * it + 2];
+    orc_transpose(Xout, rows, cols, Xt);
+    if (rows <= cols) {
+      orc_matmul(Xout, Xt, rows, cols, rows, A);
+      orc_matmul(A, Xout, rows, rows, cols, P);
+      orc_matmul(A, P, rows, rows, cols, Q);
+    } else {
+      orc_matmul(Xt, Xout, cols, rows, cols, A);
+      orc_matmul(Xout, A, rows, cols, cols, P);
+      orc_matmul(P, A, rows, cols, cols, Q);
+    }
+    for (long i = 0; i < n; i++) Xout[i] = a * Xout[i] + b * P[i] + c * Q[i];
+  }
+  free(Xt);
+  free(A);
+  free(P);
+  free(Q);
+}
+
+/* stepMat (Puffer/Float/Muon.lean:94-102): newMom = mu*mom + 1*g; upd = 1*g + mu*newMom;
+ * W' = (1 - lr*wd) W + (lr*sqrt(max(1, rows/cols))) NS(upd)   (ascent form). */
+void orc_muon_stepmat(const double* W, const double* G, const double* M, int rows, int cols, double lr, double wd,
+                      double mu, double eps, const double* coeffs, int iters, double* nW, double* nM) {
+  long n = (long)rows * cols;
+  double* u = (double*)malloc(sizeof(double) * n);
+  double* X = (double*)malloc(sizeof(double) * n);
+  for (long i = 0; i < n; i++) {
+    nM[i] = mu * M[i] + 1.0 * G[i];
+    u[i] = 1.0 * G[i] + mu * nM[i];
+  }
+  orc_newton_schulz(u, rows, cols, eps, coeffs, iters, X);
+  double r = (double)rows / (double)cols;
+  double scale = sqrt(1.0 <= r ? r : 1.0);
+  double c1 = 1.0 - lr * wd, c2 = lr * scale;
+  for (long i = 0; i < n; i++) nW[i] = c1 * W[i] + c2 * X[i];
+  free(u);
+  free(X);
+}
+
+/* stepVec (Puffer/Float/Muon.lean:105-108). */
+void orc_muon_stepvec(const double* b, const double* g, const double* m, int n, double lr, double wd, double mu,
+                      double* nb, double* nm) {
+  for (int i = 0; i < n; i++) {
+    double newm = mu * m[i] + g[i];
+    double upd = g[i] + mu * newm;
+    nb[i] = b[i] * (1.0 - lr * wd) + lr * upd;
+    nm[i] = newm;
+  }
+}
+
+/* ---------------------------------------------------------------- MLP PPO gradient --------- */
+/* Activation of the hidden layers: 0 = ReLU (every reference MLP kernel, ffi/pufferblas.c:721),
+ * 1 = GELU tanh form 0.5 x (1 + tanh(0.7978845608028654 (x + 0.044715 x^3))) (Puffer/Net/Forward.lean:271-273). */
+static double orc_act(double z, int act) {
+  if (act == 0) return z > 0.0 ? z : 0.0;
+  double u = 0.7978845608028654 * (z + 0.044715 * z * z * z);
+  return 0.5 * z * (1.0 + tanh(u));
+}
+static double orc_act_grad(double z, int act) {
+  if (act == 0) return z > 0.0 ? 1.0 : 0.0;
+  double u = 0.7978845608028654 * (z + 0.044715 * z * z * z);
+  double t = tanh(u);
+  return 0.5 * (1.0 + t) + 0.5 * z * (1.0 - t * t) * 0.7978845608028654 * (1.0 + 3.0 * 0.044715 * z * z);
+}
+
+/* Parameter count of the flat layout [W1(H*D)|b1(H)|{W_l(H*H)|b_l(H)} for l=2..L|Wo(O*H)|bo(O)];
+ * L = 1 is the reference's [W1|b1|W2|b2] (ffi/puffercuda.cu:746, Puffer/RL/FFITrain.lean:136). */
+size_t orc_mlp_param_count(size_t D, size_t H, size_t A, size_t L) {
+  size_t O = A + 1;
+  return H * D + H + (L - 1) * (H * H + H) + O * H + O;
+}
+
+/* Summed PPO-objective gradient over N rows (gradient ASCENT convention), generalised to L hidden
+ * layers. Per row it is the reference's scalar backward: forward, log-softmax WITHOUT max subtraction,
+ * ratio = exp(logp_a - old), clipped surrogate branch choice, entropy term, value term with optional
+ * PufferLib value clip (ffi/pufferffi.c:87-140 and :142-208; ffi/pufferblas.c:699-747).
+ * ov == NULL or vfClip <= 0 selects the unclipped value gradient. newlp/newval may be NULL. */
+void orc_mlp_ppo_grad(const double* params, const double* obs, const double* acts, const double* advs,
+                      const double* rets, const double* olps, const double* ov, size_t N, size_t D, size_t H,
+                      size_t A, size_t L, int act, double vfCoef, double entCoef, double clipEps, double vfClip,
+                      double* g, double* newlp, double* newval) {
+  size_t O = A + 1;
+  size_t P = orc_mlp_param_count(D, H, A, L);
+  for (size_t i = 0; i < P; i++) g[i] = 0.0;
+  /* layer offsets */
+  size_t* oW = (size_t*)malloc(sizeof(size_t) * (L + 1));
+  size_t* ob = (size_t*)malloc(sizeof(size_t) * (L + 1));
+  size_t off = 0;
+  for (size_t l = 0; l <= L; l++) {
+    size_t in = (l == 0) ? D : H, outd = (l == L) ? O : H;
+    oW[l] = off;
+    off += outd * in;
+    ob[l] = off;
+    off += outd;
+  }
+  double* z = (double*)malloc(sizeof(double) * L * H);
+  double* h = (double*)malloc(sizeof(double) * L * H);
+  double* out = (double*)malloc(sizeof(double) * O);
+  double* dout = (double*)malloc(sizeof(double) * O);
+  double* dh = (double*)malloc(sizeof(double) * H);
+  double* dz = (double*)malloc(sizeof(double) * H);
+  double* pk = (double*)malloc(sizeof(double) * (A ? A : 1));
+  for (size_t n = 0; n < N; n++) {
+    const double* x = obs + n * D;
+    /* forward */
+    for (size_t l = 0; l < L; l++) {
+      const double* in = (l == 0) ? x : h + (l - 1) * H;
+      size_t nin = (l == 0) ? D : H;
+      for (size_t j = 0; j < H; j++) {
+        const double* w = params + oW[l] + j * nin;
+        double acc = 0.0;
+        for (size_t k = 0; k < nin; k++) acc += w[k] * in[k];
+        double zz = params[ob[l] + j] + acc;
+        z[l * H + j] = zz;
+        h[l * H + j] = orc_act(zz, act);
+      }
+    }
+    const double* hl = h + (L - 1) * H;
+    for (size_t k = 0; k < O; k++) {
+      const double* w = params + oW[L] + k * H;
+      double acc = 0.0;
+      for (size_t j = 0; j < H; j++) acc += w[j] * hl[j];
+      out[k] = params[ob[L] + k] + acc;
+    }
+    /* PPO objective backward */
+    size_t a = (size_t)acts[n];
+    double adv = advs[n], ret = rets[n], oldLogp = olps[n];
+    double sumexp = 0.0;
+    for (size_t k = 0; k < A; k++) sumexp += exp(out[k]);
+    double lse = log(sumexp);
+    double pout = 0.0;
+    for (size_t k = 0; k < A; k++) {
+      pk[k] = exp(out[k] - lse);
+      pout += pk[k] * out[k];
+    }
+    double logpA = out[a] - lse;
+    double ratio = exp(logpA - oldLogp);
+    double lo = 1.0 - clipEps, hi = 1.0 + clipEps;
+    double ratioC = ratio < lo ? lo : (ratio > hi ? hi : ratio);
+    double surr1 = adv * ratio, surr2 = adv * ratioC;
+    double dPol;
+    if (surr1 <= surr2)
+      dPol = adv * ratio;
+    else {
+      double cg = (lo < ratio && ratio < hi) ? 1.0 : 0.0;
+      dPol = adv * cg * ratio;
+    }
+    for (size_t k = 0; k < A; k++) {
+      double dp = dPol * (((k == a) ? 1.0 : 0.0) - pk[k]);
+      double de = entCoef * pk[k] * (pout - out[k]);
+      dout[k] = dp + de;
+    }
+    double vnew = out[A], dv;
+    if (ov && vfClip > 0.0) {
+      double vold = ov[n], d = vnew - vold;
+      double vclip = vold + (d < -vfClip ? -vfClip : (d > vfClip ? vfClip : d));
+      double du = (vnew - ret) * (vnew - ret), dc = (vclip - ret) * (vclip - ret);
+      if (du >= dc)
+        dv = vnew - ret;
+      else if (d > -vfClip && d < vfClip)
+        dv = vnew - ret;
+      else
+        dv = 0.0;
+    } else
+      dv = vnew - ret;
+    dout[A] = -vfCoef * dv;
+    if (newlp) newlp[n] = logpA;
+    if (newval) newval[n] = vnew;
+    /* backward: head */
+    for (size_t j = 0; j < H; j++) dh[j] = 0.0;
+    for (size_t k = 0; k < O; k++) {
+      double dk = dout[k];
+      double* gw = g + oW[L] + k * H;
+      const double* w = params + oW[L] + k * H;
+      for (size_t j = 0; j < H; j++) {
+        gw[j] += dk * hl[j];
+        dh[j] += dk * w[j];
+      }
+      g[ob[L] + k] += dk;
+    }
+    /* hidden layers, top to bottom */
+    for (size_t l = L; l-- > 0;) {
+      const double* in = (l == 0) ? x : h + (l - 1) * H;
+      size_t nin = (l == 0) ? D : H;
+      for (size_t j = 0; j < H; j++) dz[j] = dh[j] * orc_act_grad(z[l * H + j], act);
+      if (act == 0)
+        for (size_t j = 0; j < H; j++) dz[j] = (z[l * H + j] > 0.0) ? dh[j] : 0.0;
+      for (size_t j = 0; j < nin && l > 0; j++) dh[j] = 0.0;
+      for (size_t j = 0; j < H; j++) {
+        double* gw = g + oW[l] + j * nin;
+        const double* w = params + oW[l] + j * nin;
+        for (size_t k = 0; k < nin; k++) {
+          gw[k] += dz[j] * in[k];
+          if (l > 0) dh[k] += dz[j] * w[k];
+        }
+        g[ob[l] + j] += dz[j];
+      }
+    }
+  }
+  free(oW);
+  free(ob);
+  free(z);
+  free(h);
+  free(out);
+  free(dout);
+  free(dh);
+  free(dz);
+  free(pk);
+}
+
+/* Global-norm clip of a summed gradient to the clipped MEAN gradient (the resident drivers' formula,
+ * ffi/puffercuda.cu:5122-5131 / Puffer/RL/MinGRUTrain.lean:640-648): gnorm = sqrt(sum (g*sc)^2),
+ * cc = (maxNorm > 0 && gnorm > maxNorm ? maxNorm/gnorm : 1) * sc, g *= cc. maxNorm <= 0 is the bare
+ * mean scale g *= sc. Sequential fold. */
+void orc_grad_clip(double* g, size_t P, double maxNorm, double sc) {
+  if (maxNorm > 0.0) {
+    double ss = 0.0;
+    for (size_t i = 0; i < P; i++) {
+      double x = g[i] * sc;
+      ss = ss + x * x;
+    }
+    double gnorm = sqrt(ss);
+    double cc = ((maxNorm > 0.0 && gnorm > maxNorm) ? maxNorm / gnorm : 1.0) * sc;
+    for (size_t i = 0; i < P; i++) g[i] = g[i] * cc;
+  } else {
+    for (size_t i = 0; i < P; i++) g[i] = sc * g[i];
+  }
+}
+
+/* Muon over the whole flat MLP: every weight matrix via stepMat, every bias via stepVec, in layer order
+ * (applyMuon, Puffer/RL/NNTrain.lean:379-388, generalised to L hidden layers). pm = [params(P); mom(P)]
+ * updated in place; g is the already-scaled gradient. */
+void orc_apply_muon(double* pm, const double* g, size_t D, size_t H, size_t A, size_t L, double lr, double wd,
+                    double mu, double eps, const double* coeffs, int iters) {
+  size_t O = A + 1;
+  size_t P = orc_mlp_param_count(D, H, A, L);
+  double* par = pm;
+  double* mom = pm + P;
+  size_t off = 0;
+  for (size_t l = 0; l <= L; l++) {
+    size_t in = (l == 0) ? D : H, outd = (l == L) ? O : H;
+    size_t n = outd * in;
+    double* nW = (double*)malloc(sizeof(double) * n);
+    double* nM = (double*)malloc(sizeof(double) * n);
+    orc_muon_stepmat(par + off, g + off, mom + off, (int)outd, (int)in, lr, wd, mu, eps, coeffs, iters, nW, nM);
+    memcpy(par + off, nW, sizeof(double) * n);
+    memcpy(mom + off, nM, sizeof(double) * n);
+    free(nW);
+    free(nM);
+    off += n;
+    orc_muon_stepvec(par + off, g + off, mom + off, (int)outd, lr, wd, mu, par + off, mom + off);
+    off += outd;
+  }
+}
+
+/* One whole update over resident columns (the semantics of lean_cuda_train_update_resident,
+ * ffi/puffercuda.cu:1187-1294, generalised to L hidden layers): for each epoch e and minibatch m,
+ * rows perm[e*NT + lo .. hi) with mbSize = NT/numMB and the last minibatch taking the remainder;
+ * gather, normalizeAdv over the minibatch, summed gradient, clip to the mean, Muon in place.
+ * ov may be NULL (unclipped value loss). pm = [params; mom] updated in place. */
+void orc_train_update(double* pm, const double* obs, const double* acts, const double* adv, const double* ret,
+                      const double* olp, const double* ov, const double* perm, size_t NT, size_t D, size_t H,
+                      size_t A, size_t L, int act, size_t epochs, size_t numMB, double lr, double wd, double mu,
+                      double eps, double vfCoef, double entCoef, double clipEps, double vfClip, double maxGradNorm,
+                      const double* coeffs, int iters) {
+  size_t P = orc_mlp_param_count(D, H, A, L);
+  size_t mbSize = NT / numMB;
+  if (mbSize < 1) mbSize = 1;
+  double* mbObs = (double*)malloc(sizeof(double) * NT * D);
+  double* mbAct = (double*)malloc(sizeof(double) * NT);
+  double* mbAdv = (double*)malloc(sizeof(double) * NT);
+  double* mbAdvN = (double*)malloc(sizeof(double) * NT);
+  double* mbRet = (double*)malloc(sizeof(double) * NT);
+  double* mbOlp = (double*)malloc(sizeof(double) * NT);
+  double* mbOv = (double*)malloc(sizeof(double) * NT);
+  double* g = (double*)malloc(sizeof(double) * P);
+  int useVClip = (ov != NULL && vfClip > 0.0);
+  for (size_t e = 0; e < epochs; e++)
+    for (size_t m = 0; m < numMB; m++) {
+      size_t lo = m * mbSize;
+      size_t hi = (m + 1 == numMB) ? NT : (m + 1) * mbSize;
+      if (hi > NT) hi = NT;
+      if (hi <= lo) continue;
+      size_t Nmb = hi - lo;
+      const double* idx = perm + e * NT + lo;
+      orc_gather_minibatch(obs, acts, adv, ret, olp, idx, Nmb, D, mbObs, mbAct, mbAdv, mbRet, mbOlp);
+      if (useVClip)
+        for (size_t k = 0; k < Nmb; k++) mbOv[k] = ov[(size_t)idx[k]];
+      orc_normalize_adv(mbAdv, Nmb, mbAdvN);
+      orc_mlp_ppo_grad(pm, mbObs, mbAct, mbAdvN, mbRet, mbOlp, useVClip ? mbOv : NULL, Nmb, D, H, A, L, act, vfCoef,
+                       entCoef, clipEps, vfClip, g, NULL, NULL);
+      orc_grad_clip(g, P, maxGradNorm, 1.0 / (double)Nmb);
+      orc_apply_muon(pm, g, D, H, A, L, lr, wd, mu, eps, coeffs, iters);
+    }
+  free(mbObs);
+  free(mbAct);
+  free(mbAdv);
+  free(mbAdvN);
+  free(mbRet);
+  free(mbOlp);
+  free(mbOv);
+  free(g);
+}
+
+/* ---------------------------------------------------------------- init --------------------- */
+/* randMat (Puffer/RL/NNTrain.lean:392-403): entries uniform01*(2 scale) - scale, row-major. */
+void orc_rand_mat(size_t rows, size_t cols, double scale, uint64_t* s, double* out) {
+  for (size_t i = 0; i < rows * cols; i++) {
+    uint64_t w = orc_rng_next(s);
+    out[i] = orc_uniform01(w) * (2.0 * scale) - scale;
+  }
+}
+/* initMLP (Puffer/RL/NNTrain.lean:418-422) flattened (flattenMLP, FFITrain.lean:136): Kaiming-uniform,
+ * bound sqrt(2)/sqrt(din) for W1 and 1/sqrt(H) for W2, biases zero. Returns the advanced state. */
+uint64_t orc_init_mlp(size_t din, size_t H, size_t dout, uint64_t rng, double* flat) {
+  uint64_t s = rng;
+  double* W1 = flat;
+  double* b1 = W1 + H * din;
+  double* W2 = b1 + H;
+  double* b2 = W2 + dout * H;
+  orc_rand_mat(H, din, sqrt(2.0) * (1.0 / sqrt((double)din)), &s, W1);
+  orc_rand_mat(dout, H, 1.0 / sqrt((double)H), &s, W2);
+  for (size_t j = 0; j < H; j++) b1[j] = 0.0;
+  for (size_t k = 0; k < dout; k++) b2[k] = 0.0;
+  return s;
+}
+
+/* cosineLr (Puffer/RL/FFITrain.lean:115-120). */
+double orc_cosine_lr(double lr, double minLrRatio, size_t u, size_t updates) {
+  if (u == 0) return lr;
+  double lrMin = lr * minLrRatio;
+  double ratio = (double)u / (double)(updates > 1 ? updates : 1);
+  return lrMin + 0.5 * (lr - lrMin) * (1.0 + cos(3.14159265358979323846 * ratio));
+}
