@@ -1,0 +1,208 @@
+/* pufferlean_b200 -- B200 (sm_100a) implementation of pufferlean's PPO+Muon training update.
+ *
+ * Plain C ABI: host or device pointers, sizes, scalars, status codes. No Lean, torch or CUDA
+ * types cross it (streams are passed as void*). Each entry point names the reference symbol it
+ * replaces (file:line within the reference project). The reference's Lean `@[extern]` symbols
+ * (lean_cuda_*, lean_ffi_*) are provided on top of this ABI by the adapter declared in
+ * include/pufferlean_lean.h.
+ *
+ * Conventions shared with the reference:
+ *  - f64 host arrays in row-major order; parameter vectors use the flat layout
+ *    [W1(H*D) | b1(H) | W2(O*H) | b2(O)], O = A+1 (logits then value), and the policy handle owns
+ *    the combined [params(P); mom(P)] buffer (ffi/puffercuda.cu:6100-6116);
+ *  - gradients are of the PPO OBJECTIVE and Muon ascends (ffi/pufferblas.c:1397-1398);
+ *  - bf16 = 1 selects the bf16 tensor-core tier (fp32 accumulate, f64 master weights and momentum);
+ *    bf16 = 0 the tight tier (fp32 GEMMs, f64 Newton-Schulz in the reference's op order).
+ *
+ * Every function returns PL_OK (0) or a negative status; pl_last_error() describes the failure.
+ * There is no CPU fallback: without a usable device, calls fail with PL_ERR_NO_DEVICE.
+ */
+#ifndef PUFFERLEAN_B200_H
+#define PUFFERLEAN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PL_OK 0
+#define PL_ERR_INVALID (-1)
+#define PL_ERR_CUDA (-2)
+#define PL_ERR_NOMEM (-3)
+#define PL_ERR_UNSUPPORTED (-4)
+#define PL_ERR_DEVICE_TIMEOUT (-5)
+#define PL_ERR_NO_DEVICE (-6)
+#define PL_ERR_COMM (-7)
+
+/* Message for the calling thread's most recent failure ("" if none). */
+const char* pl_last_error(void);
+/* Number of CUDA devices visible to this process. */
+int pl_device_count(void);
+/* Selects the device later calls from this thread use (default 0). */
+int pl_set_device(int device);
+/* Number of this library's kernels launched since load (all threads, all devices). */
+uint64_t pl_kernel_launch_count(void);
+
+/* ------------------------------------------------------------------ advantage scans ----------- */
+
+/* V-trace, vector-delta form, f64, bit-exact with the reference's scan (host buffers, B*T row-major).
+ * Replaces lean_cuda_vtrace (ffi/puffercuda.cu:94-136; Puffer/Float/CUDA.lean:20-22). */
+int pl_vtrace(const double* rew, const double* val, const double* term, const double* imp, size_t B, size_t T,
+              double gamma, double lam, double rhoClip, double cClip, double* adv);
+
+/* V-trace, MinGRU scalar-delta form with bootstrap bootv[B], f64, bit-exact.
+ * Replaces lean_cuda_vtrace_mingru (ffi/puffercuda.cu:171-216; Puffer/Float/CUDA.lean:29-31). */
+int pl_vtrace_mingru(const double* rew, const double* val, const double* term, const double* imp,
+                     const double* bootv, size_t B, size_t T, double gamma, double lam, double rhoClip,
+                     double cClip, double* adv);
+
+/* Device-resident scans (all pointers device pointers; stream may be NULL).
+ * bootv == NULL selects the vector form (adv[T-1] = 0), else the MinGRU form. adv_l1, if not NULL,
+ * receives sum_t |adv[b,t]| per segment (the k_vtrace_mingru + k_adv_l1 pair,
+ * ffi/puffercuda.cu:146-167, 311-312). The f32 form is the fast tier (warp per segment,
+ * shuffle-based reverse scan); the f64 form keeps the reference's sequential op order. */
+int pl_vtrace_f32_dev(const float* rew, const float* val, const float* term, const float* imp, const float* bootv,
+                      size_t B, size_t T, double gamma, double lam, double rhoClip, double cClip, float* adv,
+                      float* adv_l1, void* stream);
+int pl_vtrace_f64_dev(const double* rew, const double* val, const double* term, const double* imp,
+                      const double* bootv, size_t B, size_t T, double gamma, double lam, double rhoClip,
+                      double cClip, double* adv, double* adv_l1, void* stream);
+
+/* ------------------------------------------------------------------ host bookkeeping ---------- */
+
+/* Per-epoch Fisher-Yates with splitmix64, f64-encoded, bit-exact.
+ * Replaces lean_ffi_shuffle_perm (ffi/pufferffi.c:1017-1041). out has epochs*NT entries. */
+int pl_shuffle_perm(size_t NT, size_t epochs, uint64_t rng, double* out);
+/* Truncated GAE + returns over env segments (row e*T+t), bit-exact. out = [adv(NT); ret(NT)].
+ * Replaces lean_ffi_gae_soa (ffi/pufferffi.c:946-971). */
+int pl_gae_soa(const double* vals, const double* rews, const double* terms, size_t N, size_t T, double gamma,
+               double lam, double* out);
+
+/* ------------------------------------------------------------------ Muon ---------------------- */
+
+/* One Muon step of one matrix in the tight tier (f64 Newton-Schulz, reference op order, bit-exact).
+ * out = [newW(rows*cols); newMom(rows*cols)].
+ * Replaces lean_cuda_muon_stepmat (ffi/puffercuda.cu:559-631; Puffer/Float/CUDA.lean:37-39). */
+int pl_muon_stepmat(const double* W, const double* G, const double* M, size_t rows, size_t cols, double lr,
+                    double wd, double mu, double eps, double* out);
+
+/* Newton-Schulz orthogonalisation of a batch of equally shaped bf16 matrices on the device
+ * (tensor cores, fp32 accumulate): X[b] <- NS(X[b] / (||X[b]||_F + eps)) with an iters x 3
+ * coefficient table (host, row-major). X is batch x rows x cols, updated in place. The batch may be
+ * the local shard of a larger set (see pl_ns_batched_sharded_dev). */
+int pl_ns_batched_bf16_dev(void* X, size_t batch, size_t rows, size_t cols, double eps, const double* coeffs,
+                           size_t iters, void* stream);
+
+/* ------------------------------------------------------------------ MLP PPO -------------------- */
+
+/* Summed PPO-objective gradient of the one-hidden-layer MLP (host buffers).
+ * Replaces lean_cuda_mlp_ppo_grad (ffi/puffercuda.cu:748-816; Puffer/Float/CUDA.lean:45-47). */
+int pl_mlp_ppo_grad(const double* params, const double* obs, const double* acts, const double* advs,
+                    const double* rets, const double* oldlps, size_t N, size_t H, size_t D, size_t A,
+                    double vfCoef, double entCoef, double clipEps, uint8_t bf16, double* g);
+
+/* (adv - mean) / (std + 1e-8), population std.
+ * Replaces lean_cuda_adv_normalize (ffi/puffercuda.cu:836-855; Puffer/Float/CUDA.lean:50-52). */
+int pl_adv_normalize(const double* adv, size_t n, double* out);
+
+/* One resident step: normalize -> mean gradient -> Muon. pm/pm_out = [params; mom] (2P).
+ * Replaces lean_cuda_train_step (ffi/puffercuda.cu:988-1080; Puffer/Float/CUDA.lean:61-63). */
+int pl_train_step(const double* pm, const double* obs, const double* acts, const double* advRaw,
+                  const double* rets, const double* oldlps, size_t N, size_t H, size_t D, size_t A, double lr,
+                  double wd, double mu, double eps, double vfCoef, double entCoef, double clipEps, uint8_t bf16,
+                  double* pm_out);
+
+/* Whole update (all epochs x minibatches) with host-threaded [params; mom].
+ * Replaces lean_cuda_train_update (ffi/puffercuda.cu:1094-1167; Puffer/Float/CUDA.lean:72-75). */
+int pl_train_update(const double* pm, const double* obs, const double* acts, const double* adv,
+                    const double* ret, const double* olp, const double* perm, size_t NT, size_t D, size_t H,
+                    size_t A, size_t epochs, size_t numMB, double lr, double wd, double mu, double eps,
+                    double vfCoef, double entCoef, double clipEps, uint8_t bf16, double* pm_out);
+
+/* Device-resident policy: [params(P); mom(P)] f64 in device memory behind an opaque handle.
+ * Replace lean_cuda_policy_load / _download / _free (ffi/puffercuda.cu:6100-6116). */
+int pl_policy_load(const double* pm, size_t P, size_t* handle);
+int pl_policy_download(size_t handle, size_t P, double* pm_out);
+int pl_policy_free(size_t handle);
+
+/* Whole update on the resident policy, updated in place; params0_out receives params[0].
+ * oldVal may be NULL / oldValN < NT (value clip off); vfClip <= 0 and maxGradNorm <= 0 select
+ * the unclipped arithmetic, as in the reference.
+ * Replaces lean_cuda_train_update_resident (ffi/puffercuda.cu:1187-1294; Puffer/Float/CUDA.lean:241-244). */
+int pl_train_update_resident(size_t handle, const double* obs, const double* acts, const double* adv,
+                             const double* ret, const double* olp, const double* oldVal, size_t oldValN,
+                             const double* perm, size_t NT, size_t D, size_t H, size_t A, size_t epochs,
+                             size_t numMB, double lr, double wd, double mu, double eps, double vfCoef,
+                             double entCoef, double clipEps, double vfClip, double maxGradNorm, uint8_t bf16,
+                             double* params0_out);
+
+/* Network shape beyond the reference's single hidden layer. L hidden layers of width H (L = 1 is the
+ * reference layout), hidden activation act (0 = ReLU as in the reference, 1 = GELU tanh form,
+ * Puffer/Net/Forward.lean:271-273), and the Newton-Schulz coefficient table (NULL = the reference's
+ * tuned 5-row table, Puffer/Float/Muon.lean:64-67). Flat layout
+ * [W1|b1|W2|b2|...|W_L|b_L|W_out|b_out]. */
+typedef struct {
+  size_t L;
+  int act;
+  const double* ns_coeffs; /* iters x 3, row-major; NULL = reference table */
+  size_t ns_iters;
+} pl_mlp_arch;
+
+/* Parameter count of the flat layout for (D, H, A, L). */
+size_t pl_mlp_param_count(size_t D, size_t H, size_t A, size_t L);
+
+/* Deep variant of pl_train_update_resident (no reference symbol: the reference MLP has one hidden
+ * layer, ffi/puffercuda.cu:746). Same conventions plus `arch`. */
+int pl_train_update_resident_deep(size_t handle, const pl_mlp_arch* arch, const double* obs, const double* acts,
+                                  const double* adv, const double* ret, const double* olp, const double* oldVal,
+                                  size_t oldValN, const double* perm, size_t NT, size_t D, size_t H, size_t A,
+                                  size_t epochs, size_t numMB, double lr, double wd, double mu, double eps,
+                                  double vfCoef, double entCoef, double clipEps, double vfClip, double maxGradNorm,
+                                  uint8_t bf16, double* params0_out);
+
+/* ------------------------------------------------------------------ update sessions ------------ */
+/* A session binds a policy handle to fixed shapes and keeps the rollout columns and every
+ * per-minibatch buffer resident, so an update can be run from device memory alone (the form the
+ * reference reaches when its rollout leaves the obs trajectory on the device, ffi/puffercuda.cu:1226-1228).
+ * pl_train_update_resident(_deep) is a session created on first use plus one host upload per call. */
+typedef struct pl_update pl_update;
+typedef struct {
+  size_t NT, D, H, A, epochs, numMB;
+  pl_mlp_arch arch;
+  double wd, mu, eps, vfCoef, entCoef, clipEps, vfClip, maxGradNorm;
+  uint8_t bf16;
+  uint8_t use_old_values; /* value clip needs the old-value column */
+  /* data-parallel group: rank/world; comm = an ncclComm_t created by the caller, or NULL at world 1 */
+  int rank, world;
+  void* comm;
+} pl_update_desc;
+
+int pl_update_create(size_t handle, const pl_update_desc* desc, pl_update** out);
+/* Host columns (f64, the reference ABI's form); uploaded and converted on the device. perm is the
+ * epochs*NT f64-encoded shuffle. oldVal may be NULL when desc->use_old_values is 0. */
+int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, const double* adv,
+                          const double* ret, const double* olp, const double* oldVal, const double* perm,
+                          void* stream);
+/* Device columns: obs as fp32 [NT x D], the rest f64 [NT] (perm f64 [epochs*NT]). Copied into the
+ * session's own layout on the device. */
+int pl_update_set_columns_dev(pl_update* u, const float* obs, const double* acts, const double* adv,
+                              const double* ret, const double* olp, const double* oldVal, const double* perm,
+                              void* stream);
+/* Runs every epoch x minibatch of one update at learning rate lr on `stream`. */
+int pl_update_run(pl_update* u, double lr, void* stream);
+/* Kernels launched by the last pl_update_run (this library's own kernels). */
+uint64_t pl_update_last_launches(const pl_update* u);
+int pl_update_destroy(pl_update* u);
+
+/* ------------------------------------------------------------------ dashboard losses ----------- */
+/* The reference's 7-loss channel [policy, value, entropy, total, old_kl, kl, clipfrac]
+ * (ffi/puffercuda.cu:251-262, 336-352). */
+int pl_loss_enable(uint8_t on);
+int pl_read_losses(double out[7]);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,37 @@
+/* Test hooks of pufferlean_b200: direct access to the tcgen05 GEMM and its epilogues on device
+ * pointers, so kernel numerics can be checked against a plain fp32 reference. Not part of the
+ * reference's interface; no reference counterpart. */
+#ifndef PUFFERLEAN_B200_TESTING_H
+#define PUFFERLEAN_B200_TESTING_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+  /* operands: bf16 device storage, rows x cols with cols contiguous, leading dimension ld */
+  const void* a; long a_rows, a_cols, a_ld, a_bstride; int a_mn;
+  const void* b; long b_rows, b_cols, b_ld, b_bstride; int b_mn;
+  int M, N, K, bn, epi, batch, k_splits;
+  /* epilogue (see pl_gemm.cuh EpiArgs) */
+  void* out; long ldo, out_bstride; int out_rows, out_cols;
+  float alpha, beta;
+  const void* aux; long ld_aux, aux_bstride;
+  const float* bias;
+  void* out2; long ldo2;
+  float* colsum; long ld_colsum;
+  int act;
+  const int* act_idx; const float* adv; const float* ret; const float* olp; const float* ov;
+  int A; float vf, ent, clip, vfclip;
+  float* newlp; float* newval; float* loss_part;
+} pl_test_gemm_args;
+
+int pl_test_gemm(const pl_test_gemm_args* g, void* stream);
+/* Reads and clears the device-side bounded-wait error word (0 = none). */
+int pl_test_device_error(unsigned* code);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

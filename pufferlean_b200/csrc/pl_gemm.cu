@@ -1,0 +1,93 @@
+// Host side of the tcgen05 GEMM: TMA tensor maps, kernel-instance dispatch, launch.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "pl_gemm.cuh"
+#include "pl_runtime.h"
+
+namespace pl {
+
+using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, int, int, int, EpiArgs);
+
+// Instance tables live in the pl_gemm_inst_*.cu translation units.
+GemmKernel gemm_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+// 3-D bf16 tensor map over {cols (contiguous), rows, batch} with a {64, box_rows, 1} box and the
+// 128-byte swizzle the UMMA descriptors expect. Out-of-range elements read as zero.
+static int make_map(CUtensorMap* map, const Operand& op, uint32_t box_rows) {
+  auto enc = encode_fn();
+  PL_REQUIRE(enc != nullptr, PL_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  PL_REQUIRE(((uintptr_t)op.ptr & 15) == 0, PL_ERR_INVALID, "GEMM operand base not 16-byte aligned");
+  PL_REQUIRE(op.ld % 8 == 0 && op.ld >= op.cols, PL_ERR_INVALID, "GEMM operand ld=%ld must be >= cols and a multiple of 8",
+             op.ld);
+  long bstride = op.batch > 1 ? op.bstride : op.ld * op.rows;
+  PL_REQUIRE(bstride % 8 == 0, PL_ERR_INVALID, "GEMM operand batch stride must be a multiple of 8 elements");
+  cuuint64_t dims[3] = {(cuuint64_t)op.cols, (cuuint64_t)op.rows, (cuuint64_t)(op.batch > 0 ? op.batch : 1)};
+  cuuint64_t strides[2] = {(cuuint64_t)op.ld * 2, (cuuint64_t)bstride * 2};
+  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(op.ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  PL_REQUIRE(r == CUDA_SUCCESS, PL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%ld cols=%ld ld=%ld", (int)r,
+             op.rows, op.cols, op.ld);
+  return PL_OK;
+}
+
+int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const Operand& B, int M, int N, int K,
+                int batch, const EpiArgs& ep_in, cudaStream_t st) {
+  PL_REQUIRE(M > 0 && N > 0 && K > 0, PL_ERR_INVALID, "GEMM with empty extent M=%d N=%d K=%d", M, N, K);
+  // Operand storage must cover the logical extents the tiles index.
+  PL_REQUIRE(a_mn ? (A.rows >= K && A.cols >= M) : (A.rows >= M && A.cols >= K), PL_ERR_INVALID,
+             "GEMM A storage %ldx%ld too small for M=%d K=%d", A.rows, A.cols, M, K);
+  PL_REQUIRE(b_mn ? (B.rows >= K && B.cols >= N) : (B.rows >= N && B.cols >= K), PL_ERR_INVALID,
+             "GEMM B storage %ldx%ld too small for N=%d K=%d", B.rows, B.cols, N, K);
+  uint32_t smem = 0;
+  GemmKernel k = gemm_instance(bn, epi, a_mn, b_mn, &smem);
+  PL_REQUIRE(k != nullptr, PL_ERR_UNSUPPORTED, "no GEMM instance bn=%d epi=%d a_mn=%d b_mn=%d", bn, epi, (int)a_mn,
+             (int)b_mn);
+  if (epi == EPI_PPO) PL_REQUIRE(N <= bn, PL_ERR_INVALID, "PPO head needs all %d outputs in one tile (bn=%d)", N, bn);
+  CUtensorMap ma, mb;
+  int rc = make_map(&ma, A, a_mn ? 64 : 128);
+  if (rc) return rc;
+  rc = make_map(&mb, B, b_mn ? 64 : (uint32_t)bn);
+  if (rc) return rc;
+  EpiArgs ep = ep_in;
+  if (!ep.err) ep.err = device_error_word();
+  int splits = ep.k_splits > 1 ? ep.k_splits : 1;
+  PL_REQUIRE(splits == 1 || batch == 1, PL_ERR_INVALID, "split-K and batching are exclusive");
+  dim3 grid((unsigned)ceil_div(N, bn), (unsigned)ceil_div(M, 128), (unsigned)(splits > 1 ? splits : batch));
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    static void* configured[256];
+    static int nconf = 0;
+    bool found = false;
+    for (int i = 0; i < nconf; i++)
+      if (configured[i] == (void*)k) found = true;
+    if (!found) {
+      PL_CUDA(cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      if (nconf < 256) configured[nconf++] = (void*)k;
+    }
+  }
+  k<<<grid, 192, smem, st>>>(ma, mb, M, N, K, ep);
+  count_launch();
+  PL_LAUNCH("tc_gemm_kernel");
+  return PL_OK;
+}
+
+}  // namespace pl

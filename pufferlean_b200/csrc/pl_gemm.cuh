@@ -1,0 +1,481 @@
+// Warp-specialised tcgen05 GEMM for sm_100a with fused epilogues for the PPO+Muon update.
+//
+//   D[M x N] = sum_k A[m,k] * B[n,k]            (bf16 operands, fp32 accumulate in TMEM)
+//
+// A and B each arrive either K-major (row m / n holds its K values contiguously) or MN-major
+// (row k holds the M / N values contiguously); the choice is a template flag per operand, so the
+// forward (X W^T), data-gradient (dZ W) and weight-gradient (dZ^T X) products of every layer all
+// read the tensors where they already lie, with no transposed copies.
+//
+// CTA = 6 warps: warp 0 issues TMA tile loads into a STAGES-deep shared-memory ring, warp 1 owns
+// the TMEM accumulator (128 lanes x BN fp32 columns) and issues tcgen05.mma from one thread,
+// warps 2-5 drain TMEM through tcgen05.ld and run the epilogue. Tiles are BM=128 x BN, BK=64
+// (one 128-byte swizzle atom of bf16 per row).
+#pragma once
+#include "pl_common.cuh"
+#include "pl_tc.cuh"
+
+namespace pl {
+
+enum EpiKind : int {
+  EPI_F32 = 0,    // out(f32)  = alpha*acc (+ beta*aux)            [wgrad, split-K partials, tests]
+  EPI_BF16 = 1,   // out(bf16) = alpha*acc (+ beta*aux)            [Newton-Schulz chain]
+  EPI_FWD = 2,    // z = acc + bias; out(bf16) = act(z); out2(bf16) = z (GELU only)
+  EPI_DGRAD = 3,  // out(bf16) = acc * act'(aux); column partial sums of it  [bias grads]
+  EPI_PPO = 4,    // logits+value = acc + bias -> PPO objective gradient dOut(bf16) + column sums
+};
+
+struct EpiArgs {
+  void* out;
+  long ldo;          // elements
+  long out_bstride;  // elements per blockIdx.z (batch or split-K slice)
+  int out_rows, out_cols;  // stores are masked to rows < out_rows, cols < out_cols
+  float alpha, beta;
+  const __nv_bfloat16* aux;
+  long ld_aux, aux_bstride;
+  const float* bias;
+  void* out2;
+  long ldo2;
+  float* colsum;  // [gridDim.y][ld_colsum] per-CTA column partial sums (fixed-order reduced later)
+  long ld_colsum;
+  int act;        // 0 ReLU, 1 GELU (tanh form)
+  // PPO head (EPI_PPO): one row per thread, per-row columns of the minibatch
+  const int* act_idx;
+  const float* adv;
+  const float* ret;
+  const float* olp;
+  const float* ov;  // NULL = unclipped value loss
+  int A;
+  float vf, ent, clip, vfclip;
+  float* newlp;
+  float* newval;
+  float* loss_part;  // [gridDim.y][8] optional per-CTA loss partials
+  unsigned* err;
+  int k_splits;      // >1: blockIdx.z is a split-K slice; else blockIdx.z is the batch index
+};
+
+__device__ __forceinline__ float act_fwd(float z, int act) {
+  if (act == 0) return z > 0.f ? z : 0.f;
+  float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
+  return 0.5f * z * (1.f + tanhf(u));
+}
+__device__ __forceinline__ float act_grad(float z, int act) {
+  if (act == 0) return z > 0.f ? 1.f : 0.f;
+  float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
+  float t = tanhf(u);
+  return 0.5f * (1.f + t) + 0.5f * z * (1.f - t * t) * 0.7978845608028654f * (1.f + 3.f * 0.044715f * z * z);
+}
+
+// Sums each of 16 per-lane values over the 32 lanes of a warp with 16 shuffles (a butterfly that
+// halves the live values each step). Lane L returns the total of column (L >> 1). Fixed order.
+__device__ __forceinline__ float warp_colsum16(const float (&v)[16], int lane) {
+  float a[8], b[4], c[2];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    bool hi = lane & 16;
+    float send = hi ? v[j] : v[j + 8], keep = hi ? v[j + 8] : v[j];
+    a[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    bool hi = lane & 8;
+    float send = hi ? a[j] : a[j + 4], keep = hi ? a[j + 4] : a[j];
+    b[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    bool hi = lane & 4;
+    float send = hi ? b[j] : b[j + 2], keep = hi ? b[j + 2] : b[j];
+    c[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  bool hi = lane & 2;
+  float send = hi ? c[0] : c[1], keep = hi ? c[1] : c[0];
+  float d = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  return d + __shfl_xor_sync(0xffffffffu, d, 1);
+}
+
+__device__ __forceinline__ void store_row16_bf16(__nv_bfloat16* p, const float (&v)[16], int nvalid, bool vec) {
+  if (vec && nvalid == 16) {
+    uint4 w[2];
+    uint32_t* u = reinterpret_cast<uint32_t*>(w);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+      u[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    reinterpret_cast<uint4*>(p)[0] = w[0];
+    reinterpret_cast<uint4*>(p)[1] = w[1];
+  } else {
+    for (int j = 0; j < nvalid; j++) p[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+__device__ __forceinline__ void store_row16_f32(float* p, const float (&v)[16], int nvalid, bool vec) {
+  if (vec && nvalid == 16) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) reinterpret_cast<float4*>(p)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+    for (int j = 0; j < nvalid; j++) p[j] = v[j];
+  }
+}
+__device__ __forceinline__ void load_row16_bf16(const __nv_bfloat16* p, float (&v)[16], int nvalid, bool vec) {
+  if (vec && nvalid == 16) {
+    uint4 w[2];
+    w[0] = reinterpret_cast<const uint4*>(p)[0];
+    w[1] = reinterpret_cast<const uint4*>(p)[1];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(w);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      float2 f = __bfloat1622float2(h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; j++) v[j] = (j < nvalid) ? __bfloat162float(p[j]) : 0.f;
+  }
+}
+
+template <int BN>
+struct GemmSmem {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
+  // ring + barriers + tmem slot + epilogue column-reduction scratch [4][BN] + row scratch
+  static constexpr uint32_t TOTAL = 1024 + STAGES * STAGE_BYTES + 256 + 4 * BN * 4 + 4 * 32 * 8 * 4;
+};
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                   int K, EpiArgs ep) {
+  using S = GemmSmem<BN>;
+  constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES;
+  constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* full = (uint64_t*)(sB + STAGES * S::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = (uint32_t*)(accum + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  float* red = (float*)(smem + STAGES * S::STAGE_BYTES + 256);  // [4][BN]
+  float* rowscr = red + 4 * BN;                                  // [4 warps][32 lanes][8]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y, bz = blockIdx.z;
+  const int total_kb = (K + BK - 1) / BK;
+  int kb_begin = 0, kb_end = total_kb, batch = bz;
+  if (ep.k_splits > 1) {
+    int per = (total_kb + ep.k_splits - 1) / ep.k_splits;
+    kb_begin = bz * per;
+    kb_end = min(total_kb, kb_begin + per);
+    batch = 0;
+  }
+  const int num_kb = kb_end > kb_begin ? kb_end - kb_begin : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(accum, 1);
+    *abort_flag = 0;
+    tc::fence_mbar_init();
+    tc::tma_prefetch_desc(&tmA);
+    tc::tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, BN);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int issued = 0;
+      for (int i = 0; i < num_kb; i++) {
+        const int s = i % STAGES;
+        if (i >= STAGES) {
+          if (!tc::mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, ep.err, PL_ERR_MBAR_TIMEOUT | 1)) {
+            *abort_flag = 1;
+            break;
+          }
+        }
+        if (*abort_flag) break;
+        const int k0 = (kb_begin + i) * BK;
+        tc::mbar_expect_tx(&full[s], S::STAGE_BYTES);
+        uint8_t* a = sA + s * S::A_BYTES;
+        uint8_t* b = sB + s * S::B_BYTES;
+        if (!A_MN) {
+          tc::tma_load_3d(a, &tmA, &full[s], k0, m_tile * BM, batch);
+        } else {
+          tc::tma_load_3d(a, &tmA, &full[s], m_tile * BM, k0, batch);
+          tc::tma_load_3d(a + 8192, &tmA, &full[s], m_tile * BM + 64, k0, batch);
+        }
+        if (!B_MN) {
+          tc::tma_load_3d(b, &tmB, &full[s], k0, n_tile * BN, batch);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; j++) tc::tma_load_3d(b + j * 8192, &tmB, &full[s], n_tile * BN + 64 * j, k0, batch);
+        }
+        issued = i + 1;
+      }
+      // Drain: every load this thread issued must have landed before the CTA can retire.
+      for (int i = issued - STAGES > 0 ? issued - STAGES : 0; i < issued; i++)
+        tc::mbar_wait(&full[i % STAGES], (i / STAGES) & 1, ep.err, PL_ERR_MBAR_TIMEOUT | 2);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer (one thread)
+      bool any = false;
+      for (int i = 0; i < num_kb; i++) {
+        const int s = i % STAGES;
+        if (!tc::mbar_wait(&full[s], (i / STAGES) & 1, ep.err, PL_ERR_MBAR_TIMEOUT | 3)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t a_addr = tc::smem_u32(sA + s * S::A_BYTES);
+        const uint32_t b_addr = tc::smem_u32(sB + s * S::B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; kk++) {
+          // K-major: the 16-element K slice is 32 bytes further along the swizzled row;
+          // MN-major: it is 16 rows (2 groups of 8 rows x 128 B) further down.
+          const uint64_t ad = A_MN ? tc::sw128_desc(a_addr + kk * 2048, 8192, 1024) : tc::sw128_desc(a_addr + kk * 32, 16, 1024);
+          const uint64_t bd = B_MN ? tc::sw128_desc(b_addr + kk * 2048, 8192, 1024) : tc::sw128_desc(b_addr + kk * 32, 16, 1024);
+          tc::umma_bf16(tmem_base, ad, bd, IDESC, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::umma_commit(&empty[s]);
+        any = true;
+      }
+      tc::umma_commit(accum);
+      if (any) tc::mbar_wait(accum, 0, ep.err, PL_ERR_MBAR_TIMEOUT | 4);
+    }
+  } else {
+    // ---------------- epilogue warps 2..5
+    const int sub = warp & 3;
+    const int row = m_tile * BM + sub * 32 + lane;
+    const bool row_ok = row < ep.out_rows;
+    const uint32_t t_row = tmem_base + ((uint32_t)(sub * 32) << 16);
+    bool have_acc = tc::mbar_wait(accum, 0, ep.err, PL_ERR_MBAR_TIMEOUT | 5) && num_kb > 0 && !*abort_flag;
+    tc::tc_fence_after();
+
+    if constexpr (EPI == EPI_PPO) {
+      // one thread = one minibatch row; BN covers every logit + the value column
+      const int A = ep.A;
+      int a = 0;
+      float adv = 0.f, ret = 0.f, olp = 0.f, vold = 0.f;
+      if (row_ok) {
+        a = ep.act_idx[row];
+        adv = ep.adv[row];
+        ret = ep.ret[row];
+        olp = ep.olp[row];
+        if (ep.ov) vold = ep.ov[row];
+      }
+      float mx = -INFINITY, se = 0.f, xa = 0.f, vnew = 0.f;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tc::tmem_ld16(t_row + c0, r);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const int k = c0 + j;
+          const float x = (have_acc ? __uint_as_float(r[j]) : 0.f) + (k < ep.out_cols ? ep.bias[k] : 0.f);
+          if (k < A) {
+            if (x > mx) {
+              se = se * expf(mx - x) + 1.f;
+              mx = x;
+            } else {
+              se += expf(x - mx);
+            }
+            if (k == a) xa = x;
+          }
+          if (k == A) vnew = x;
+        }
+      }
+      const float lse = mx + logf(se);
+      float pout = 0.f;
+      for (int c0 = 0; c0 < BN && c0 < A; c0 += 16) {
+        uint32_t r[16];
+        tc::tmem_ld16(t_row + c0, r);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const int k = c0 + j;
+          if (k < A) {
+            const float x = (have_acc ? __uint_as_float(r[j]) : 0.f) + ep.bias[k];
+            pout += expf(x - lse) * x;
+          }
+        }
+      }
+      const float logpA = xa - lse;
+      const float ratio = expf(logpA - olp);
+      const float lo = 1.f - ep.clip, hi = 1.f + ep.clip;
+      const float ratioC = ratio < lo ? lo : (ratio > hi ? hi : ratio);
+      const float surr1 = adv * ratio, surr2 = adv * ratioC;
+      float dPol;
+      if (surr1 <= surr2)
+        dPol = adv * ratio;
+      else
+        dPol = adv * ((lo < ratio && ratio < hi) ? 1.f : 0.f) * ratio;
+      float dv = vnew - ret;
+      if (ep.ov && ep.vfclip > 0.f) {
+        const float dd = vnew - vold;
+        const float vc = vold + (dd < -ep.vfclip ? -ep.vfclip : (dd > ep.vfclip ? ep.vfclip : dd));
+        const float du = (vnew - ret) * (vnew - ret), cc = (vc - ret) * (vc - ret);
+        if (!(du >= cc) && !(dd > -ep.vfclip && dd < ep.vfclip)) dv = 0.f;
+      }
+      const float dval = -ep.vf * dv;
+      if (row_ok) {
+        if (ep.newlp) ep.newlp[row] = logpA;
+        if (ep.newval) ep.newval[row] = vnew;
+      }
+      if (ep.loss_part) {
+        // per-row loss terms (PufferLib decomposition): pg loss, value loss, entropy, old-kl proxy, clipfrac
+        float ent_row = lse - pout;
+        float lt[6] = {row_ok ? -fminf(surr1, surr2) : 0.f, row_ok ? 0.5f * (vnew - ret) * (vnew - ret) : 0.f,
+                       row_ok ? ent_row : 0.f, row_ok ? (ratio - 1.f) - logf(ratio) : 0.f,
+                       row_ok ? -logf(ratio) : 0.f, row_ok ? (fabsf(ratio - 1.f) > ep.clip ? 1.f : 0.f) : 0.f};
+#pragma unroll
+        for (int q = 0; q < 6; q++) {
+          float v = lt[q];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == 0) rowscr[sub * 8 + q] = v;
+        }
+      }
+      __nv_bfloat16* outp = (__nv_bfloat16*)ep.out + (long)row * ep.ldo;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tc::tmem_ld16(t_row + c0, r);
+        tc::tmem_wait_ld();
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const int k = c0 + j;
+          float d = 0.f;
+          if (row_ok) {
+            if (k < A) {
+              const float x = (have_acc ? __uint_as_float(r[j]) : 0.f) + ep.bias[k];
+              const float p = expf(x - lse);
+              d = dPol * ((k == a ? 1.f : 0.f) - p) + ep.ent * p * (pout - x);
+            } else if (k == A) {
+              d = dval;
+            }
+          }
+          v[j] = d;
+        }
+        if (row_ok) {
+          const int nvalid = min(16, (int)(ep.ldo - c0));
+          if (nvalid > 0) store_row16_bf16(outp + c0, v, nvalid, (ep.ldo % 8) == 0);
+        }
+        const float cs = warp_colsum16(v, lane);
+        if ((lane & 1) == 0) red[sub * BN + c0 + (lane >> 1)] = cs;
+      }
+      tc::named_bar_sync(1, 128);
+      const int t = threadIdx.x - 64;
+      for (int c = t; c < BN; c += 128) {
+        if (c < ep.out_cols)
+          ep.colsum[(long)m_tile * ep.ld_colsum + c] = ((red[c] + red[BN + c]) + red[2 * BN + c]) + red[3 * BN + c];
+      }
+      if (ep.loss_part && t < 6)
+        ep.loss_part[(long)m_tile * 8 + t] = ((rowscr[t] + rowscr[8 + t]) + rowscr[16 + t]) + rowscr[24 + t];
+    } else {
+      const int n_base = n_tile * BN;
+      const bool do_colsum = (EPI == EPI_DGRAD) && ep.colsum != nullptr;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        const int n0 = n_base + c0;
+        if (n0 >= ep.out_cols) break;  // warp-uniform
+        uint32_t r[16];
+        tc::tmem_ld16(t_row + c0, r);
+        tc::tmem_wait_ld();
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] = have_acc ? __uint_as_float(r[j]) : 0.f;
+        const int nvalid = min(16, ep.out_cols - n0);
+        if constexpr (EPI == EPI_F32 || EPI == EPI_BF16) {
+          if (row_ok) {
+            float x[16];
+            if (ep.aux) {
+              load_row16_bf16(ep.aux + (long)batch * ep.aux_bstride + (long)row * ep.ld_aux + n0, x, nvalid,
+                              (ep.ld_aux % 8) == 0);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = ep.alpha * v[j] + (ep.aux ? ep.beta * x[j] : 0.f);
+            const long off = (long)bz * ep.out_bstride + (long)row * ep.ldo + n0;
+            if constexpr (EPI == EPI_F32)
+              store_row16_f32((float*)ep.out + off, v, nvalid, (ep.ldo % 4) == 0);
+            else
+              store_row16_bf16((__nv_bfloat16*)ep.out + off, v, nvalid, (ep.ldo % 8) == 0);
+          }
+        } else if constexpr (EPI == EPI_FWD) {
+          if (row_ok) {
+            float z[16], h[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+              z[j] = v[j] + ((n0 + j) < ep.out_cols ? ep.bias[n0 + j] : 0.f);
+              h[j] = act_fwd(z[j], ep.act);
+            }
+            store_row16_bf16((__nv_bfloat16*)ep.out + (long)row * ep.ldo + n0, h, nvalid, (ep.ldo % 8) == 0);
+            if (ep.out2)
+              store_row16_bf16((__nv_bfloat16*)ep.out2 + (long)row * ep.ldo2 + n0, z, nvalid, (ep.ldo2 % 8) == 0);
+          }
+        } else if constexpr (EPI == EPI_DGRAD) {
+          float x[16];
+          if (row_ok) {
+            load_row16_bf16(ep.aux + (long)row * ep.ld_aux + n0, x, nvalid, (ep.ld_aux % 8) == 0);
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = (j < nvalid) ? v[j] * act_grad(x[j], ep.act) : 0.f;
+            store_row16_bf16((__nv_bfloat16*)ep.out + (long)row * ep.ldo + n0, v, nvalid, (ep.ldo % 8) == 0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = 0.f;
+          }
+          if (do_colsum) {
+            const float cs = warp_colsum16(v, lane);
+            if ((lane & 1) == 0) red[sub * BN + c0 + (lane >> 1)] = cs;
+          }
+        }
+      }
+      if (do_colsum) {
+        tc::named_bar_sync(1, 128);
+        const int t = threadIdx.x - 64;
+        for (int c = t; c < BN; c += 128) {
+          const int n = n_base + c;
+          if (n < ep.out_cols)
+            ep.colsum[(long)m_tile * ep.ld_colsum + n] = ((red[c] + red[BN + c]) + red[2 * BN + c]) + red[3 * BN + c];
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, BN);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+struct Operand {
+  const void* ptr;  // bf16
+  long rows, cols;  // storage: rows x cols, cols contiguous (cols = the inner dimension)
+  long ld;          // elements between rows (>= cols, multiple of 8)
+  long batch;       // number of stacked matrices (>= 1)
+  long bstride;     // elements between stacked matrices
+};
+
+// C[M x N] = A * B^T with operands given by their storage; a_mn / b_mn say whether the operand is
+// stored MN-major (storage rows = K) or K-major (storage rows = M or N).
+int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const Operand& B, int M, int N, int K,
+                int batch, const EpiArgs& ep, cudaStream_t st);
+
+}  // namespace pl

@@ -1,0 +1,171 @@
+// Muon, tight tier: f64 Nesterov -> Frobenius normalise -> Newton-Schulz -> decoupled decay,
+// every arithmetic step rounded on its own (no fused multiply-add) and folded in the order of the
+// reference's executable oracle (Puffer/Float/Muon.lean:19-108, whose C twin is
+// ffi/pufferblas.c:1369-1406), so the step is bit-identical to it. Used for parity and for the
+// bf16 = 0 training tier; the bf16 tier orthogonalises on the tensor cores (pl_ns.cu).
+#include "pl_common.cuh"
+#include "pl_muon.cuh"
+#include "pl_runtime.h"
+
+namespace pl {
+
+__constant__ double c_ns_coeffs[64][3];
+
+// newMom = mu*mom + g ; upd = g + mu*newMom   (gs scales g first when != 1: g*gs)
+__global__ void nesterov_f64_kernel(const double* __restrict__ g, const double* __restrict__ m, double* nm,
+                                    double* u, double mu, double gs, long n) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const double gi = gs == 1.0 ? g[i] : __dmul_rn(g[i], gs);
+  const double newm = __dadd_rn(__dmul_rn(mu, m[i]), gi);
+  nm[i] = newm;
+  u[i] = __dadd_rn(gi, __dmul_rn(mu, newm));
+}
+
+// Two-level Frobenius fold: per-row sums (one thread per row, sequential in the column), then a
+// single thread folds the rows in order; out = 1 / (sqrt(total) + eps).
+__global__ void frob_rows_f64_kernel(const double* __restrict__ x, int rows, int cols, double* rowsum) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows) return;
+  const double* r = x + (long)i * cols;
+  double s = 0.0;
+  for (int j = 0; j < cols; j++) s = __dadd_rn(s, __dmul_rn(r[j], r[j]));
+  rowsum[i] = s;
+}
+__global__ void frob_fold_f64_kernel(const double* __restrict__ rowsum, int rows, double eps, double* inv) {
+  if (threadIdx.x || blockIdx.x) return;
+  double s = 0.0;
+  for (int i = 0; i < rows; i++) s = __dadd_rn(s, rowsum[i]);
+  inv[0] = __ddiv_rn(1.0, __dadd_rn(__dsqrt_rn(s), eps));
+}
+__global__ void scale_f64_kernel(const double* __restrict__ u, const double* __restrict__ inv, double* x, long n) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) x[i] = __dmul_rn(inv[0], u[i]);
+}
+__global__ void transpose_f64_kernel(const double* __restrict__ X, int rows, int cols, double* Xt) {
+  long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)rows * cols) return;
+  int i = (int)(idx / cols), j = (int)(idx % cols);
+  Xt[(long)j * rows + i] = X[idx];
+}
+// C[m x n] = A[m x k] B[k x n], s = s + A[i][l]*B[l][j] from 0 (Puffer/Float/Muon.lean:19-31)
+__global__ void matmul_f64_kernel(const double* __restrict__ A, const double* __restrict__ B, int m, int k, int n,
+                                  double* C) {
+  long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)m * n) return;
+  int i = (int)(idx / n), j = (int)(idx % n);
+  double s = 0.0;
+  for (int l = 0; l < k; l++) s = __dadd_rn(s, __dmul_rn(A[(long)i * k + l], B[(long)l * n + j]));
+  C[idx] = s;
+}
+__global__ void lincomb3_f64_kernel(double* X, const double* __restrict__ P, const double* __restrict__ Q, int it,
+                                    long n) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const double a = c_ns_coeffs[it][0], b = c_ns_coeffs[it][1], c = c_ns_coeffs[it][2];
+  X[i] = __dadd_rn(__dadd_rn(__dmul_rn(a, X[i]), __dmul_rn(b, P[i])), __dmul_rn(c, Q[i]));
+}
+__global__ void finalize_f64_kernel(const double* __restrict__ W, const double* __restrict__ X, double c1, double c2,
+                                    double* nW, long n) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) nW[i] = __dadd_rn(__dmul_rn(c1, W[i]), __dmul_rn(c2, X[i]));
+}
+// stepVec (Puffer/Float/Muon.lean:105-108); g pre-scaled by gs when gs != 1.
+__global__ void stepvec_f64_kernel(double* b, double* m, const double* __restrict__ g, double lr, double wd,
+                                   double mu, double gs, long n) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const double gi = gs == 1.0 ? g[i] : __dmul_rn(g[i], gs);
+  const double newm = __dadd_rn(__dmul_rn(mu, m[i]), gi);
+  const double upd = __dadd_rn(gi, __dmul_rn(mu, newm));
+  b[i] = __dadd_rn(__dmul_rn(b[i], __dsub_rn(1.0, __dmul_rn(lr, wd))), __dmul_rn(lr, upd));
+  m[i] = newm;
+}
+
+int set_ns_coeffs(const double* coeffs, int iters, cudaStream_t st) {
+  PL_REQUIRE(iters >= 0 && iters <= 64, PL_ERR_INVALID, "Newton-Schulz iterations %d out of range", iters);
+  if (iters) PL_CUDA(cudaMemcpyToSymbolAsync(c_ns_coeffs, coeffs, sizeof(double) * 3 * iters, 0,
+                                             cudaMemcpyHostToDevice, st));
+  return PL_OK;
+}
+
+const double kMuonCoeffs[5][3] = {{4.0848, -6.8946, 2.9270}, {3.9505, -6.3029, 2.6377}, {3.7418, -5.5913, 2.3037},
+                                  {2.8769, -3.1427, 1.2046}, {2.8366, -3.0525, 1.2012}};
+
+size_t exact_ws_doubles(int rows, int cols) {
+  long n = (long)rows * cols;
+  int mn = rows < cols ? rows : cols;
+  return (size_t)(5 * n + (long)mn * mn + rows + 8);
+}
+
+// In place on (W, M): W <- stepMat(W, g*gs, M). ws holds exact_ws_doubles(rows, cols) doubles.
+int muon_mat_exact(int rows, int cols, double* W, double* M, const double* G, double gs, double lr, double wd,
+                   double mu, double eps, int iters, double* ws, cudaStream_t st) {
+  const long n = (long)rows * cols;
+  const int mn = rows < cols ? rows : cols;
+  double *U = ws, *X = U + n, *Xt = X + n, *P = Xt + n, *Q = P + n, *Am = Q + n, *rs = Am + (long)mn * mn,
+         *inv = rs + rows;
+  const int B = 256;
+  const unsigned gN = (unsigned)ceil_div(n, B);
+  nesterov_f64_kernel<<<gN, B, 0, st>>>(G, M, M, U, mu, gs, n);
+  frob_rows_f64_kernel<<<(unsigned)ceil_div(rows, 128), 128, 0, st>>>(U, rows, cols, rs);
+  frob_fold_f64_kernel<<<1, 32, 0, st>>>(rs, rows, eps, inv);
+  scale_f64_kernel<<<gN, B, 0, st>>>(U, inv, X, n);
+  count_launch(4);
+  for (int it = 0; it < iters; it++) {
+    transpose_f64_kernel<<<gN, B, 0, st>>>(X, rows, cols, Xt);
+    if (rows <= cols) {
+      matmul_f64_kernel<<<(unsigned)ceil_div((long)rows * rows, B), B, 0, st>>>(X, Xt, rows, cols, rows, Am);
+      matmul_f64_kernel<<<gN, B, 0, st>>>(Am, X, rows, rows, cols, P);
+      matmul_f64_kernel<<<gN, B, 0, st>>>(Am, P, rows, rows, cols, Q);
+    } else {
+      matmul_f64_kernel<<<(unsigned)ceil_div((long)cols * cols, B), B, 0, st>>>(Xt, X, cols, rows, cols, Am);
+      matmul_f64_kernel<<<gN, B, 0, st>>>(X, Am, rows, cols, cols, P);
+      matmul_f64_kernel<<<gN, B, 0, st>>>(P, Am, rows, cols, cols, Q);
+    }
+    lincomb3_f64_kernel<<<gN, B, 0, st>>>(X, P, Q, it, n);
+    count_launch(5);
+  }
+  const double r = (double)rows / (double)cols;
+  const double scale = sqrt(1.0 <= r ? r : 1.0);
+  volatile double lrwd = lr * wd;
+  const double c1 = 1.0 - lrwd, c2 = lr * scale;
+  finalize_f64_kernel<<<gN, B, 0, st>>>(W, X, c1, c2, W, n);
+  count_launch();
+  PL_LAUNCH("muon_mat_exact");
+  return PL_OK;
+}
+
+int stepvec_launch(double* b, double* m, const double* g, double lr, double wd, double mu, double gs, long n,
+                   cudaStream_t st) {
+  if (n <= 0) return PL_OK;
+  stepvec_f64_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(b, m, g, lr, wd, mu, gs, n);
+  count_launch();
+  PL_LAUNCH("stepvec_f64_kernel");
+  return PL_OK;
+}
+
+}  // namespace pl
+
+extern "C" int pl_muon_stepmat(const double* W, const double* G, const double* M, size_t rows, size_t cols, double lr,
+                               double wd, double mu, double eps, double* out) {
+  int rc = pl::require_device();
+  if (rc) return rc;
+  PL_REQUIRE(W && G && M && out, PL_ERR_INVALID, "pl_muon_stepmat: NULL buffer");
+  const size_t n = rows * cols;
+  if (n == 0) return PL_OK;
+  const size_t wsd = pl::exact_ws_doubles((int)rows, (int)cols);
+  double* d = (double*)pl::scratch(1, sizeof(double) * (3 * n + wsd));
+  if (!d) return PL_ERR_NOMEM;
+  double *dW = d, *dM = d + n, *dG = d + 2 * n, *ws = d + 3 * n;
+  PL_CUDA(cudaMemcpy(dW, W, 8 * n, cudaMemcpyHostToDevice));
+  PL_CUDA(cudaMemcpy(dM, M, 8 * n, cudaMemcpyHostToDevice));
+  PL_CUDA(cudaMemcpy(dG, G, 8 * n, cudaMemcpyHostToDevice));
+  rc = pl::set_ns_coeffs(&pl::kMuonCoeffs[0][0], 5, 0);
+  if (rc) return rc;
+  rc = pl::muon_mat_exact((int)rows, (int)cols, dW, dM, dG, 1.0, lr, wd, mu, eps, 5, ws, 0);
+  if (rc) return rc;
+  PL_CUDA(cudaMemcpy(out, dW, 8 * n, cudaMemcpyDeviceToHost));
+  PL_CUDA(cudaMemcpy(out + n, dM, 8 * n, cudaMemcpyDeviceToHost));
+  return PL_OK;
+}

@@ -1,0 +1,18 @@
+// Muon building blocks shared by the update driver.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace pl {
+extern const double kMuonCoeffs[5][3];
+// Loads an iters x 3 Newton-Schulz table into constant memory (used by the f64 tier).
+int set_ns_coeffs(const double* coeffs, int iters, cudaStream_t st);
+// f64 workspace (in doubles) muon_mat_exact needs for one rows x cols matrix.
+size_t exact_ws_doubles(int rows, int cols);
+// Tight-tier Muon step of one matrix, in place on W and M (bit-exact with the reference oracle).
+int muon_mat_exact(int rows, int cols, double* W, double* M, const double* G, double gs, double lr, double wd,
+                   double mu, double eps, int iters, double* ws, cudaStream_t st);
+// stepVec on n bias entries, in place on b and m.
+int stepvec_launch(double* b, double* m, const double* g, double lr, double wd, double mu, double gs, long n,
+                   cudaStream_t st);
+}  // namespace pl

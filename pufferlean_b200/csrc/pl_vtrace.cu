@@ -1,0 +1,294 @@
+// Advantage scans over B segments x T steps (row-major, row b holds segment b's horizon).
+//
+//  * exact tier (f64): the reference's sequential backward scan with its IEEE op order, every
+//    product and sum rounded on its own (__dmul_rn / __dadd_rn, no fused multiply-add), so the
+//    result is bit-identical to ffi/puffercuda.cu:69-90 (vector form) and :146-167 (MinGRU form).
+//  * fast tier (fp32): one warp per segment. Each lane owns a contiguous run of T/32 steps, loaded
+//    with vector loads; the recurrence A_t = delta_t + k_t * A_{t+1} is a composition of affine
+//    maps, so each lane folds its run into one map (k, delta), a 5-step shuffle suffix scan
+//    composes the maps of the lanes to its right, and the lane then replays its run backwards
+//    from the scanned boundary value. sum_t |A_t| per segment falls out of the same registers.
+#include "pl_common.cuh"
+#include "pl_runtime.h"
+
+namespace pl {
+
+// ---------------------------------------------------------------- exact f64
+template <bool MINGRU>
+__global__ void vtrace_f64_kernel(const double* __restrict__ rew, const double* __restrict__ val,
+                                  const double* __restrict__ term, const double* __restrict__ imp,
+                                  const double* __restrict__ bootv, double* __restrict__ adv,
+                                  double* __restrict__ adv_l1, int B, int T, double gamma, double lam,
+                                  double rhoClip, double cClip) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= B) return;
+  const long base = (long)row * T;
+  const double* rw = rew + base;
+  const double* vv = val + base;
+  const double* tm = term + base;
+  const double* im = imp + base;
+  double* ad = adv + base;
+  const double gl = __dmul_rn(gamma, lam);
+  double last = 0.0;
+  if (!MINGRU) {
+    if (T > 0) ad[T - 1] = 0.0;
+    for (int t = T - 2; t >= 0; t--) {
+      const double nnt = (tm[t] != 0.0) ? 0.0 : 1.0;
+      const double iv = im[t];
+      const double rho = iv < rhoClip ? iv : rhoClip;
+      const double c = iv < cClip ? iv : cClip;
+      const double rr = rw[t];
+      const double r = rr > 1.0 ? 1.0 : (rr < -1.0 ? -1.0 : rr);
+      // rho * (r + gamma*V[t+1]*nnt - V[t])
+      const double delta = __dmul_rn(rho, __dsub_rn(__dadd_rn(r, __dmul_rn(__dmul_rn(gamma, vv[t + 1]), nnt)), vv[t]));
+      // delta + gamma*lam*c*last*nnt
+      last = __dadd_rn(delta, __dmul_rn(__dmul_rn(__dmul_rn(gl, c), last), nnt));
+      ad[t] = last;
+    }
+  } else {
+    for (int t = T - 1; t >= 0; t--) {
+      const double nnt = (tm[t] > 0.5) ? 0.0 : 1.0;
+      const double vNext = (t + 1 < T) ? vv[t + 1] : bootv[row];
+      const double iv = im[t];
+      const double rho = iv < rhoClip ? iv : rhoClip;
+      const double c = iv < cClip ? iv : cClip;
+      const double rr = rw[t];
+      const double r = rr > 1.0 ? 1.0 : (rr < -1.0 ? -1.0 : rr);
+      // rho*r + gamma*vNext*nnt - V[t]
+      const double delta = __dsub_rn(__dadd_rn(__dmul_rn(rho, r), __dmul_rn(__dmul_rn(gamma, vNext), nnt)), vv[t]);
+      last = __dadd_rn(delta, __dmul_rn(__dmul_rn(__dmul_rn(gl, c), last), nnt));
+      ad[t] = last;
+    }
+  }
+  if (adv_l1) {
+    double s = 0.0;
+    for (int t = 0; t < T; t++) s = __dadd_rn(s, fabs(ad[t]));
+    adv_l1[row] = s;
+  }
+}
+
+// ---------------------------------------------------------------- fast fp32
+template <int EPL>
+__device__ __forceinline__ void load_run(const float* __restrict__ p, int t0, int T, bool vec, float (&x)[EPL],
+                                         float fill) {
+  if (vec && t0 + EPL <= T) {
+    if constexpr (EPL == 4) {
+      float4 q = *reinterpret_cast<const float4*>(p + t0);
+      x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
+      return;
+    } else if constexpr (EPL == 2) {
+      float2 q = *reinterpret_cast<const float2*>(p + t0);
+      x[0] = q.x; x[1] = q.y;
+      return;
+    } else if constexpr (EPL == 8) {
+      float4 q0 = *reinterpret_cast<const float4*>(p + t0);
+      float4 q1 = *reinterpret_cast<const float4*>(p + t0 + 4);
+      x[0] = q0.x; x[1] = q0.y; x[2] = q0.z; x[3] = q0.w;
+      x[4] = q1.x; x[5] = q1.y; x[6] = q1.z; x[7] = q1.w;
+      return;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < EPL; e++) x[e] = (t0 + e < T) ? p[t0 + e] : fill;
+}
+
+template <int EPL, bool MINGRU>
+__global__ void __launch_bounds__(256) vtrace_f32_kernel(const float* __restrict__ rew, const float* __restrict__ val,
+                                                         const float* __restrict__ term, const float* __restrict__ imp,
+                                                         const float* __restrict__ bootv, float* __restrict__ adv,
+                                                         float* __restrict__ adv_l1, int B, int T, float gamma,
+                                                         float lam, float rhoClip, float cClip) {
+  const int lane = threadIdx.x & 31;
+  const long seg = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (seg >= B) return;  // warp-uniform
+  const long base = seg * T;
+  const int t0 = lane * EPL;
+  // vector loads need every row start aligned to the run width
+  constexpr uintptr_t ALIGN = EPL >= 4 ? 16 : EPL * 4;
+  const uintptr_t orp = (uintptr_t)(rew + base) | (uintptr_t)(val + base) | (uintptr_t)(term + base) |
+                        (uintptr_t)(imp + base) | (uintptr_t)(adv + base);
+  const bool vec = EPL > 1 && (T % EPL) == 0 && (orp % ALIGN) == 0;
+  float r[EPL], v[EPL], d[EPL], im[EPL];
+  load_run<EPL>(rew + base, t0, T, vec, r, 0.f);
+  load_run<EPL>(val + base, t0, T, vec, v, 0.f);
+  load_run<EPL>(term + base, t0, T, vec, d, 0.f);
+  load_run<EPL>(imp + base, t0, T, vec, im, 1.f);
+  // value one step past this lane's run: the first value of the next lane (or the bootstrap)
+  float v_after = __shfl_down_sync(0xffffffffu, v[0], 1);
+  const float boot = MINGRU ? bootv[seg] : 0.f;
+  const float gl = gamma * lam;
+  float k[EPL], dl[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; e++) {
+    const int t = t0 + e;
+    const float vn = (e + 1 < EPL) ? v[e + 1] : v_after;
+    const float rc = fminf(fmaxf(r[e], -1.f), 1.f);
+    const float rho = im[e] < rhoClip ? im[e] : rhoClip;
+    const float c = im[e] < cClip ? im[e] : cClip;
+    if (t >= T) {  // past the horizon: identity map
+      k[e] = 1.f;
+      dl[e] = 0.f;
+    } else if (!MINGRU) {
+      const float nnt = (d[e] != 0.f) ? 0.f : 1.f;
+      if (t == T - 1) {  // A[T-1] = 0
+        k[e] = 0.f;
+        dl[e] = 0.f;
+      } else {
+        dl[e] = rho * (rc + gamma * vn * nnt - v[e]);
+        k[e] = gl * c * nnt;
+      }
+    } else {
+      const float nnt = (d[e] > 0.5f) ? 0.f : 1.f;
+      const float vnx = (t == T - 1) ? boot : vn;
+      dl[e] = rho * rc + gamma * vnx * nnt - v[e];
+      k[e] = (t == T - 1) ? 0.f : gl * c * nnt;  // A_T enters as 0
+    }
+  }
+  // fold this lane's run into one affine map F(x) = KK*x + DD (applied to A at the run's end)
+  float KK = 1.f, DD = 0.f;
+#pragma unroll
+  for (int e = EPL - 1; e >= 0; e--) {
+    DD = dl[e] + k[e] * DD;
+    KK = k[e] * KK;
+  }
+  // inclusive suffix scan of maps over lanes: lane l -> F_l o F_{l+1} o ... o F_31
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const float K2 = __shfl_down_sync(0xffffffffu, KK, off);
+    const float D2 = __shfl_down_sync(0xffffffffu, DD, off);
+    if (lane + off < 32) {
+      DD = DD + KK * D2;
+      KK = KK * K2;
+    }
+  }
+  float A = __shfl_down_sync(0xffffffffu, DD, 1);  // value entering this run from the right
+  if (lane == 31) A = 0.f;
+  float out[EPL];
+  float l1 = 0.f;
+#pragma unroll
+  for (int e = EPL - 1; e >= 0; e--) {
+    A = dl[e] + k[e] * A;
+    out[e] = A;
+    if (t0 + e < T) l1 += fabsf(A);
+  }
+  float* ad = adv + base;
+  if (vec && t0 + EPL <= T) {
+    if constexpr (EPL == 4) {
+      *reinterpret_cast<float4*>(ad + t0) = make_float4(out[0], out[1], out[2], out[3]);
+    } else if constexpr (EPL == 2) {
+      *reinterpret_cast<float2*>(ad + t0) = make_float2(out[0], out[1]);
+    } else if constexpr (EPL == 8) {
+      *reinterpret_cast<float4*>(ad + t0) = make_float4(out[0], out[1], out[2], out[3]);
+      *reinterpret_cast<float4*>(ad + t0 + 4) = make_float4(out[4], out[5], out[6], out[7]);
+    } else {
+      ad[t0] = out[0];
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; e++)
+      if (t0 + e < T) ad[t0 + e] = out[e];
+  }
+  if (adv_l1) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    if (lane == 0) adv_l1[seg] = l1;
+  }
+}
+
+template <bool MINGRU>
+static int launch_f32(const float* rew, const float* val, const float* term, const float* imp, const float* bootv,
+                      int B, int T, float g, float l, float rho, float c, float* adv, float* l1, cudaStream_t st) {
+  const int warps = 8;
+  dim3 grid((unsigned)ceil_div(B, warps)), block(32 * warps);
+  if (T <= 32)
+    vtrace_f32_kernel<1, MINGRU><<<grid, block, 0, st>>>(rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
+  else if (T <= 64)
+    vtrace_f32_kernel<2, MINGRU><<<grid, block, 0, st>>>(rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
+  else if (T <= 128)
+    vtrace_f32_kernel<4, MINGRU><<<grid, block, 0, st>>>(rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
+  else if (T <= 256)
+    vtrace_f32_kernel<8, MINGRU><<<grid, block, 0, st>>>(rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
+  else
+    return set_error(PL_ERR_UNSUPPORTED, "fp32 V-trace supports horizons up to 256 (T=%d)", T);
+  count_launch();
+  PL_LAUNCH("vtrace_f32_kernel");
+  return PL_OK;
+}
+
+int vtrace_f64_launch(const double* rew, const double* val, const double* term, const double* imp,
+                      const double* bootv, int B, int T, double g, double l, double rho, double c, double* adv,
+                      double* l1, cudaStream_t st) {
+  dim3 grid((unsigned)ceil_div(B, 128)), block(128);
+  if (bootv)
+    vtrace_f64_kernel<true><<<grid, block, 0, st>>>(rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
+  else
+    vtrace_f64_kernel<false><<<grid, block, 0, st>>>(rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
+  count_launch();
+  PL_LAUNCH("vtrace_f64_kernel");
+  return PL_OK;
+}
+
+int vtrace_f32_launch(const float* rew, const float* val, const float* term, const float* imp, const float* bootv,
+                      int B, int T, double g, double l, double rho, double c, float* adv, float* l1,
+                      cudaStream_t st) {
+  if (bootv) return launch_f32<true>(rew, val, term, imp, bootv, B, T, (float)g, (float)l, (float)rho, (float)c, adv, l1, st);
+  return launch_f32<false>(rew, val, term, imp, bootv, B, T, (float)g, (float)l, (float)rho, (float)c, adv, l1, st);
+}
+
+static int vtrace_host(const double* rew, const double* val, const double* term, const double* imp,
+                       const double* bootv, size_t B, size_t T, double g, double l, double rho, double c,
+                       double* adv) {
+  int rc = require_device();
+  if (rc) return rc;
+  PL_REQUIRE(rew && val && term && imp && adv, PL_ERR_INVALID, "V-trace: NULL buffer");
+  const size_t n = B * T;
+  if (n == 0) return PL_OK;
+  double* d = (double*)scratch(0, sizeof(double) * (5 * n + B));
+  if (!d) return PL_ERR_NOMEM;
+  double *dR = d, *dV = d + n, *dT = d + 2 * n, *dI = d + 3 * n, *dA = d + 4 * n, *dB = d + 5 * n;
+  PL_CUDA(cudaMemcpy(dR, rew, 8 * n, cudaMemcpyHostToDevice));
+  PL_CUDA(cudaMemcpy(dV, val, 8 * n, cudaMemcpyHostToDevice));
+  PL_CUDA(cudaMemcpy(dT, term, 8 * n, cudaMemcpyHostToDevice));
+  PL_CUDA(cudaMemcpy(dI, imp, 8 * n, cudaMemcpyHostToDevice));
+  if (bootv) PL_CUDA(cudaMemcpy(dB, bootv, 8 * B, cudaMemcpyHostToDevice));
+  rc = vtrace_f64_launch(dR, dV, dT, dI, bootv ? dB : nullptr, (int)B, (int)T, g, l, rho, c, dA, nullptr, 0);
+  if (rc) return rc;
+  PL_CUDA(cudaMemcpy(adv, dA, 8 * n, cudaMemcpyDeviceToHost));
+  return PL_OK;
+}
+
+}  // namespace pl
+
+extern "C" {
+
+int pl_vtrace(const double* rew, const double* val, const double* term, const double* imp, size_t B, size_t T,
+              double gamma, double lam, double rhoClip, double cClip, double* adv) {
+  return pl::vtrace_host(rew, val, term, imp, nullptr, B, T, gamma, lam, rhoClip, cClip, adv);
+}
+
+int pl_vtrace_mingru(const double* rew, const double* val, const double* term, const double* imp,
+                     const double* bootv, size_t B, size_t T, double gamma, double lam, double rhoClip, double cClip,
+                     double* adv) {
+  PL_REQUIRE(bootv || B * T == 0, PL_ERR_INVALID, "V-trace MinGRU form needs bootv");
+  return pl::vtrace_host(rew, val, term, imp, bootv, B, T, gamma, lam, rhoClip, cClip, adv);
+}
+
+int pl_vtrace_f32_dev(const float* rew, const float* val, const float* term, const float* imp, const float* bootv,
+                      size_t B, size_t T, double gamma, double lam, double rhoClip, double cClip, float* adv,
+                      float* adv_l1, void* stream) {
+  if (B * T == 0) return PL_OK;
+  PL_REQUIRE(B < (1u << 31) && T < (1u << 31), PL_ERR_INVALID, "V-trace extents too large");
+  return pl::vtrace_f32_launch(rew, val, term, imp, bootv, (int)B, (int)T, gamma, lam, rhoClip, cClip, adv, adv_l1,
+                               (cudaStream_t)stream);
+}
+
+int pl_vtrace_f64_dev(const double* rew, const double* val, const double* term, const double* imp,
+                      const double* bootv, size_t B, size_t T, double gamma, double lam, double rhoClip,
+                      double cClip, double* adv, double* adv_l1, void* stream) {
+  if (B * T == 0) return PL_OK;
+  PL_REQUIRE(B < (1u << 31) && T < (1u << 31), PL_ERR_INVALID, "V-trace extents too large");
+  return pl::vtrace_f64_launch(rew, val, term, imp, bootv, (int)B, (int)T, gamma, lam, rhoClip, cClip, adv, adv_l1,
+                               (cudaStream_t)stream);
+}
+
+}  // extern "C"
