@@ -42,6 +42,7 @@ struct EpiArgs {
   // PPO head (EPI_PPO): one row per thread, per-row columns of the minibatch
   const int* act_idx;
   const float* adv;
+  const double* adv_ms;  // optional [mean, std+1e-8]: adv is then normalised in the epilogue
   const float* ret;
   const float* olp;
   const float* ov;  // NULL = unclipped value loss
@@ -95,7 +96,7 @@ __device__ __forceinline__ float warp_colsum16(const float (&v)[16], int lane) {
 }
 
 __device__ __forceinline__ void store_row16_bf16(__nv_bfloat16* p, const float (&v)[16], int nvalid, bool vec) {
-  if (vec && nvalid == 16) {
+  if (vec && nvalid == 16 && ((uintptr_t)p & 15) == 0) {
     uint4 w[2];
     uint32_t* u = reinterpret_cast<uint32_t*>(w);
 #pragma unroll
@@ -110,7 +111,7 @@ __device__ __forceinline__ void store_row16_bf16(__nv_bfloat16* p, const float (
   }
 }
 __device__ __forceinline__ void store_row16_f32(float* p, const float (&v)[16], int nvalid, bool vec) {
-  if (vec && nvalid == 16) {
+  if (vec && nvalid == 16 && ((uintptr_t)p & 15) == 0) {
 #pragma unroll
     for (int j = 0; j < 4; j++) reinterpret_cast<float4*>(p)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   } else {
@@ -118,7 +119,7 @@ __device__ __forceinline__ void store_row16_f32(float* p, const float (&v)[16], 
   }
 }
 __device__ __forceinline__ void load_row16_bf16(const __nv_bfloat16* p, float (&v)[16], int nvalid, bool vec) {
-  if (vec && nvalid == 16) {
+  if (vec && nvalid == 16 && ((uintptr_t)p & 15) == 0) {
     uint4 w[2];
     w[0] = reinterpret_cast<const uint4*>(p)[0];
     w[1] = reinterpret_cast<const uint4*>(p)[1];
@@ -276,6 +277,7 @@ __global__ void __launch_bounds__(192, 1)
       if (row_ok) {
         a = ep.act_idx[row];
         adv = ep.adv[row];
+        if (ep.adv_ms) adv = (float)(((double)adv - ep.adv_ms[0]) / ep.adv_ms[1]);
         ret = ep.ret[row];
         olp = ep.olp[row];
         if (ep.ov) vold = ep.ov[row];

@@ -21,6 +21,7 @@ GemmKernel gemm_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem) 
   PL_INST(128, true, false, EPI_F32)
   PL_INST(128, true, true, EPI_F32)
   PL_INST(256, false, false, EPI_F32)
+  PL_INST(256, false, true, EPI_F32)
   PL_INST(256, true, true, EPI_F32)
   // bf16 output with optional fused axpby (Newton-Schulz chain)
   PL_INST(128, false, false, EPI_BF16)

@@ -1,0 +1,66 @@
+// The MLP PPO+Muon update session: device layout of the rollout columns, the per-minibatch
+// activations and the optimizer state, and the launchers of the memory-bound kernels.
+#pragma once
+#include <vector>
+
+#include "pl_common.cuh"
+
+namespace pl {
+
+// One linear layer of the flat parameter vector: W at params[oW] (out x in, row-major), b at
+// params[ob] (out). Padded extents (in_p, out_p: multiples of 64) size the bf16 shadow copies.
+struct Layer {
+  int in, out, in_p, out_p;
+  size_t oW, ob;
+};
+
+// Newton-Schulz workspace of the largest matrix (wide layout: m = min(rows,cols) rows of
+// n = max(rows,cols) contiguous values).
+struct NsWork {
+  __nv_bfloat16 *X0 = nullptr, *X1 = nullptr, *G = nullptr, *B = nullptr;
+  float* Xf = nullptr;
+  double* U = nullptr;
+  double* part = nullptr;
+  long ldx = 0, ldg = 0;
+};
+
+int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
+                   long xbs, float* out_f32, long ld_out, long obs, cudaStream_t st);
+int ns_run(int m, int n, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx, float* out_f32,
+           long ld_out, cudaStream_t st);
+
+// launchers (pl_mlp_kernels.cu)
+int launch_obs_to_bf16_f64(const double* src, long NT, int D, int Dp, __nv_bfloat16* dst, cudaStream_t st);
+int launch_obs_to_bf16_f32(const float* src, long NT, int D, int Dp, __nv_bfloat16* dst, cudaStream_t st);
+int launch_obs_to_f32_f64(const double* src, long n, float* dst, cudaStream_t st);
+int launch_columns(const double* act, const double* ret, const double* olp, const double* ov, long NT, int* act_i,
+                   float* ret_f, float* olp_f, float* ov_f, cudaStream_t st);
+int launch_perm(const double* perm, long n, int* out, cudaStream_t st);
+int launch_gather(bool bf16, const int* idx, int Nmb, const void* obs, int rowElems, void* X, const int* act_c,
+                  const double* adv_c, const float* ret_c, const float* olp_c, const float* ov_c, int* mb_act,
+                  float* mb_adv, float* mb_ret, float* mb_olp, float* mb_ov, double* part, double* ms,
+                  cudaStream_t st);
+int launch_colsum_reduce(const float* part, int tiles, long ld, int ncols, float* out, cudaStream_t st);
+int launch_splitk_reduce(const float* part, int S, long n, float* out, cudaStream_t st);
+int launch_gradnorm(const float* g, long P, double sc, double maxNorm, double* part, double* cc, cudaStream_t st);
+int launch_nesterov(const float* g, const double* cc, double* mom, double* u, double mu, long n, double* part,
+                    int* nparts, cudaStream_t st);
+int launch_ns_input(const double* u, const double* part, int nparts, int rows, int cols, double eps,
+                    __nv_bfloat16* X, long ldx, cudaStream_t st);
+int launch_ns_finalize(const float* Xf, long ldx, int rows, int cols, double c1, double c2, double* W,
+                       __nv_bfloat16* Wb, long ldw, cudaStream_t st);
+int launch_stepvec_fast(const float* g, const double* cc, double* b, double* m, float* bf, double lr, double wd,
+                        double mu, int n, cudaStream_t st);
+int launch_w_to_bf16(const double* W, int rows, int cols, __nv_bfloat16* Wb, long ldw, cudaStream_t st);
+int launch_f64_to_f32(const double* s, long n, float* d, cudaStream_t st);
+int launch_f32_to_f64(const float* s, long n, double* d, cudaStream_t st);
+int launch_sgemm(int M, int N, int K, const float* A, long ars, long acs, const float* B, long brs, long bcs, float* C,
+                 long ldc, float alpha, cudaStream_t st);
+int launch_bias_act_f32(float* Z, float* H, const float* b, long M, int N, int act, cudaStream_t st);
+int launch_act_grad_f32(float* dH, const float* Z, long n, int act, cudaStream_t st);
+int launch_ppo_rows_f32(const float* Out, int M, int A, const int* act, const float* adv, const double* ms,
+                        const float* ret, const float* olp, const float* ov, float vf, float ent, float clip,
+                        float vfclip, float* dOut, float* newlp, float* newval, cudaStream_t st);
+int launch_colsum_f32(const float* Mx, long rows, int N, float* out, cudaStream_t st);
+
+}  // namespace pl

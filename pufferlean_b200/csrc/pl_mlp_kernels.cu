@@ -1,0 +1,508 @@
+// Memory-bound kernels of the MLP PPO+Muon update: column conversion, minibatch gather with the
+// advantage statistics, fixed-order reductions (bias gradients, split-K slices, global grad
+// norm), the Muon steps around Newton-Schulz (Nesterov, normalise, finalise into the f64 master
+// weights and their bf16 shadow), and the fp32 SIMT kernels of the tight (bf16 = 0) tier.
+//
+// Every reduction has a fixed partition and a fixed fold order, so a run is bit-reproducible.
+#include "pl_common.cuh"
+#include "pl_gemm.cuh"
+#include "pl_mlp.cuh"
+#include "pl_runtime.h"
+
+namespace pl {
+
+constexpr int kRedBlocks = 296;  // 2 x 148 SMs: fixed partition of every grid-wide reduction
+
+__device__ __forceinline__ double block_sum_f64(double v, double* sh) {
+  // fixed-shape tree over a 256-thread block
+  const int t = threadIdx.x;
+  sh[t] = v;
+  __syncthreads();
+  for (int s = 128; s > 0; s >>= 1) {
+    if (t < s) sh[t] += sh[t + s];
+    __syncthreads();
+  }
+  double r = sh[0];
+  __syncthreads();
+  return r;
+}
+
+// ---------------------------------------------------------------- columns
+// obs rows (f64 or f32, D wide) -> bf16 rows Dp wide, zero padded.
+template <typename T>
+__global__ void obs_to_bf16_kernel(const T* __restrict__ src, long NT, int D, int Dp, __nv_bfloat16* dst) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  long n = NT * Dp;
+  for (; i < n; i += (long)gridDim.x * blockDim.x) {
+    long r = i / Dp;
+    int c = (int)(i - r * Dp);
+    dst[i] = __float2bfloat16_rn(c < D ? (float)src[r * D + c] : 0.f);
+  }
+}
+template <typename T>
+__global__ void obs_to_f32_kernel(const T* __restrict__ src, long n, float* dst) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    dst[i] = (float)src[i];
+}
+// scalar columns: act (f64 index) -> int32, perm (f64) -> int32, the rest f64 -> f32 (adv stays f64)
+__global__ void columns_kernel(const double* __restrict__ act, const double* __restrict__ ret,
+                               const double* __restrict__ olp, const double* __restrict__ ov, long NT, int* act_i,
+                               float* ret_f, float* olp_f, float* ov_f) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < NT; i += (long)gridDim.x * blockDim.x) {
+    act_i[i] = (int)act[i];
+    ret_f[i] = (float)ret[i];
+    olp_f[i] = (float)olp[i];
+    if (ov) ov_f[i] = (float)ov[i];
+  }
+}
+__global__ void perm_kernel(const double* __restrict__ perm, long n, int* out) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    out[i] = (int)perm[i];
+}
+
+// ---------------------------------------------------------------- gather + advantage statistics
+// Row k of the minibatch = column row idx[k]. One warp per row for the obs copy (16-byte vectors);
+// scalars by lane 0. Each block folds sum(adv), sum(adv^2) of its rows into part[blockIdx.x].
+template <bool BF16>
+__global__ void __launch_bounds__(256) gather_kernel(const int* __restrict__ idx, int Nmb, const void* __restrict__ obs,
+                                                     int rowElems, void* X, const int* __restrict__ act_c,
+                                                     const double* __restrict__ adv_c, const float* __restrict__ ret_c,
+                                                     const float* __restrict__ olp_c, const float* __restrict__ ov_c,
+                                                     int* mb_act, float* mb_adv, float* mb_ret, float* mb_olp,
+                                                     float* mb_ov, double* part) {
+  __shared__ double sh[256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows_per_block = (Nmb + gridDim.x - 1) / gridDim.x;
+  const int r0 = blockIdx.x * rows_per_block, r1 = min(Nmb, r0 + rows_per_block);
+  double s1 = 0.0, s2 = 0.0;
+  for (int k = r0 + warp; k < r1; k += 8) {
+    const long src = idx[k];
+    const int vec_elems = BF16 ? 8 : 4;  // 16 bytes
+    // 16-byte vectors only when every row starts 16-byte aligned (always for the padded bf16 rows)
+    const int nvec = (rowElems % vec_elems == 0) ? rowElems / vec_elems : 0;
+    const uint4* s = reinterpret_cast<const uint4*>((const char*)obs + src * rowElems * (BF16 ? 2 : 4));
+    uint4* d = reinterpret_cast<uint4*>((char*)X + (long)k * rowElems * (BF16 ? 2 : 4));
+    for (int v = lane; v < nvec; v += 32) d[v] = s[v];
+    if (!BF16) {
+      const float* sf = (const float*)obs + src * rowElems;
+      float* df = (float*)X + (long)k * rowElems;
+      for (int c = nvec * 4 + lane; c < rowElems; c += 32) df[c] = sf[c];
+    }
+    if (lane == 0) {
+      const double a = adv_c[src];
+      mb_act[k] = act_c[src];
+      mb_adv[k] = (float)a;
+      mb_ret[k] = ret_c[src];
+      mb_olp[k] = olp_c[src];
+      if (mb_ov) mb_ov[k] = ov_c[src];
+      s1 += a;
+      s2 += a * a;
+    }
+  }
+  s1 = block_sum_f64(s1, sh);
+  s2 = block_sum_f64(s2, sh);
+  if (threadIdx.x == 0) {
+    part[2 * blockIdx.x] = s1;
+    part[2 * blockIdx.x + 1] = s2;
+  }
+}
+// ms = [mean, std + 1e-8] (population std), folded over the block partials in order.
+__global__ void adv_stats_kernel(const double* __restrict__ part, int nb, int n, double* ms) {
+  if (threadIdx.x || blockIdx.x) return;
+  double s1 = 0.0, s2 = 0.0;
+  for (int b = 0; b < nb; b++) {
+    s1 += part[2 * b];
+    s2 += part[2 * b + 1];
+  }
+  const double mean = s1 / (double)n;
+  double var = s2 / (double)n - mean * mean;
+  if (var < 0.0) var = 0.0;
+  ms[0] = mean;
+  ms[1] = sqrt(var) + 1e-8;
+}
+
+// ---------------------------------------------------------------- fixed-order reductions
+// out[c] = sum_t part[t*ld + c], t ascending (bias gradients from per-CTA column partials)
+__global__ void colsum_reduce_kernel(const float* __restrict__ part, int tiles, long ld, int ncols, float* out) {
+  int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= ncols) return;
+  float s = 0.f;
+  for (int t = 0; t < tiles; t++) s += part[(long)t * ld + c];
+  out[c] = s;
+}
+// out[i] = sum_s part[s*n + i], s ascending (split-K slices)
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int S, long n, float* out) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int z = 0; z < S; z++) s += part[(long)z * n + i];
+    out[i] = s;
+  }
+}
+// Global gradient norm of g*sc: fixed grid of kRedBlocks blocks x 256 threads, strided f64 sums.
+__global__ void __launch_bounds__(256) gradnorm_part_kernel(const float* __restrict__ g, long P, double sc,
+                                                            double* part) {
+  __shared__ double sh[256];
+  double s = 0.0;
+  for (long i = (long)blockIdx.x * 256 + threadIdx.x; i < P; i += (long)gridDim.x * 256) {
+    const double x = (double)g[i] * sc;
+    s += x * x;
+  }
+  s = block_sum_f64(s, sh);
+  if (threadIdx.x == 0) part[blockIdx.x] = s;
+}
+// cc = (maxNorm > 0 && gnorm > maxNorm ? maxNorm/gnorm : 1) * sc   (maxNorm <= 0: cc = sc)
+__global__ void gradnorm_final_kernel(const double* __restrict__ part, int nb, double maxNorm, double sc, double* cc) {
+  if (threadIdx.x || blockIdx.x) return;
+  double s = 0.0;
+  for (int b = 0; b < nb; b++) s += part[b];
+  const double gnorm = sqrt(s);
+  cc[0] = ((maxNorm > 0.0 && gnorm > maxNorm) ? maxNorm / gnorm : 1.0) * sc;
+  cc[1] = gnorm;
+}
+
+// ---------------------------------------------------------------- Muon around Newton-Schulz
+// m <- mu*m + g*cc ; u = g*cc + mu*m (f64); per-block partial sums of u^2 (fixed grid).
+__global__ void __launch_bounds__(256) nesterov_kernel(const float* __restrict__ g, const double* __restrict__ cc,
+                                                       double* mom, double* u, double mu, long n, double* part) {
+  __shared__ double sh[256];
+  const double c = cc[0];
+  double s = 0.0;
+  for (long i = (long)blockIdx.x * 256 + threadIdx.x; i < n; i += (long)gridDim.x * 256) {
+    const double gi = (double)g[i] * c;
+    const double m = mu * mom[i] + gi;
+    mom[i] = m;
+    const double ui = gi + mu * m;
+    u[i] = ui;
+    s += ui * ui;
+  }
+  s = block_sum_f64(s, sh);
+  if (threadIdx.x == 0) part[blockIdx.x] = s;
+}
+// X = u / (||u||_F + eps) as bf16, stored wide: for rows > cols the matrix is transposed so that
+// X is min(rows,cols) x max(rows,cols) with the long side contiguous (ld = ldx).
+__global__ void ns_input_kernel(const double* __restrict__ u, const double* __restrict__ part, int nparts,
+                                int rows, int cols, double eps, __nv_bfloat16* X, long ldx) {
+  __shared__ double inv_s;
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int b = 0; b < nparts; b++) s += part[b];
+    inv_s = 1.0 / (sqrt(s) + eps);
+  }
+  __syncthreads();
+  const double inv = inv_s;
+  const long n = (long)rows * cols;
+  const bool tr = rows > cols;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / cols, c = i - r * cols;
+    const __nv_bfloat16 v = __float2bfloat16_rn((float)(inv * u[i]));
+    if (tr)
+      X[c * ldx + r] = v;
+    else
+      X[r * ldx + c] = v;
+  }
+}
+// W <- c1*W + c2*X (f64 master, rows x cols row-major) and the bf16 shadow Wb (ldw), from the
+// fp32 Newton-Schulz result Xf (wide layout, ldx; transposed back when rows > cols).
+__global__ void ns_finalize_kernel(const float* __restrict__ Xf, long ldx, int rows, int cols, double c1, double c2,
+                                   double* W, __nv_bfloat16* Wb, long ldw) {
+  const long n = (long)rows * cols;
+  const bool tr = rows > cols;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / cols, c = i - r * cols;
+    const double x = (double)(tr ? Xf[c * ldx + r] : Xf[r * ldx + c]);
+    const double w = c1 * W[i] + c2 * x;
+    W[i] = w;
+    if (Wb) Wb[r * ldw + c] = __float2bfloat16_rn((float)w);
+  }
+}
+// stepVec on a bias with the scaled gradient g*cc, plus its fp32 shadow.
+__global__ void stepvec_fast_kernel(const float* __restrict__ g, const double* __restrict__ cc, double* b, double* m,
+                                    float* bf, double lr, double wd, double mu, int n) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const double gi = (double)g[i] * cc[0];
+  const double newm = mu * m[i] + gi;
+  const double upd = gi + mu * newm;
+  const double nb = b[i] * (1.0 - lr * wd) + lr * upd;
+  b[i] = nb;
+  m[i] = newm;
+  if (bf) bf[i] = (float)nb;
+}
+// f64 master weights -> bf16 shadow (padded, ld) / fp32 copies
+__global__ void w_to_bf16_kernel(const double* __restrict__ W, int rows, int cols, __nv_bfloat16* Wb, long ldw) {
+  const long n = (long)rows * cols;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / cols, c = i - r * cols;
+    Wb[r * ldw + c] = __float2bfloat16_rn((float)W[i]);
+  }
+}
+__global__ void f64_to_f32_kernel(const double* __restrict__ s, long n, float* d) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) d[i] = (float)s[i];
+}
+__global__ void f32_to_f64_kernel(const float* __restrict__ s, long n, double* d) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) d[i] = (double)s[i];
+}
+
+// ---------------------------------------------------------------- tight tier (fp32 SIMT)
+// C[m,n] = alpha * sum_k A(m,k) B(n,k), A(m,k) = A[m*ars + k*acs], B(n,k) = B[n*brs + k*bcs]
+__global__ void __launch_bounds__(256) sgemm_kernel(int M, int N, int K, const float* __restrict__ A, long ars, long acs,
+                                                    const float* __restrict__ B, long brs, long bcs, float* C, long ldc,
+                                                    float alpha) {
+  __shared__ float As[16][65], Bs[16][65];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      const int kk = i / 64, mm = i % 64;
+      const int m = m0 + mm, n = n0 + mm, k = k0 + kk;
+      As[kk][mm] = (m < M && k < K) ? A[(long)m * ars + (long)k * acs] : 0.f;
+      Bs[kk][mm] = (n < N && k < K) ? B[(long)n * brs + (long)k * bcs] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; kk++) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        a[i] = As[kk][ty * 4 + i];
+        b[i] = Bs[kk][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] += a[i] * b[j];
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
+      if (m < M && n < N) C[(long)m * ldc + n] = alpha * acc[i][j];
+    }
+}
+// Z <- Z + b (row-major M x N), H = act(Z)
+__global__ void bias_act_f32_kernel(float* Z, float* H, const float* __restrict__ b, long M, int N, int act) {
+  const long n = M * N;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float z = Z[i] + b[i % N];
+    Z[i] = z;
+    if (H) H[i] = act_fwd(z, act);
+  }
+}
+// dZ = dH * act'(Z)
+__global__ void act_grad_f32_kernel(float* dH, const float* __restrict__ Z, long n, int act) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    dH[i] = (act == 0) ? (Z[i] > 0.f ? dH[i] : 0.f) : dH[i] * act_grad(Z[i], act);
+}
+// Per-row PPO objective gradient on fp32 logits Out[M x O] (the reference's k_ppo_dout math,
+// ffi/puffercuda.cu:171-185, with the value clip of :133-141): dOut[M x O].
+__global__ void ppo_rows_f32_kernel(const float* __restrict__ Out, int M, int A, const int* __restrict__ act,
+                                    const float* __restrict__ adv, const double* __restrict__ ms,
+                                    const float* __restrict__ ret, const float* __restrict__ olp,
+                                    const float* __restrict__ ov, float vf, float ent, float clip, float vfclip,
+                                    float* dOut, float* newlp, float* newval) {
+  int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= M) return;
+  const int O = A + 1;
+  const float* out = Out + (long)n * O;
+  float* d = dOut + (long)n * O;
+  const int a = act[n];
+  float ad = adv[n];
+  if (ms) ad = (float)(((double)ad - ms[0]) / ms[1]);
+  const float rt = ret[n], ol = olp[n];
+  float se = 0.f;
+  for (int k = 0; k < A; k++) se += expf(out[k]);
+  const float lse = logf(se);
+  float pout = 0.f;
+  for (int k = 0; k < A; k++) pout += expf(out[k] - lse) * out[k];
+  const float logpA = out[a] - lse, ratio = expf(logpA - ol);
+  const float lo = 1.f - clip, hi = 1.f + clip;
+  const float rc = ratio < lo ? lo : (ratio > hi ? hi : ratio);
+  const float s1 = ad * ratio, s2 = ad * rc;
+  const float dPol = (s1 <= s2) ? ad * ratio : ad * ((lo < ratio && ratio < hi) ? 1.f : 0.f) * ratio;
+  for (int k = 0; k < A; k++) {
+    const float p = expf(out[k] - lse);
+    d[k] = dPol * ((k == a ? 1.f : 0.f) - p) + ent * p * (pout - out[k]);
+  }
+  const float vnew = out[A];
+  float dv = vnew - rt;
+  if (ov && vfclip > 0.f) {
+    const float vold = ov[n], dd = vnew - vold;
+    const float vcl = vold + (dd < -vfclip ? -vfclip : (dd > vfclip ? vfclip : dd));
+    if (!((vnew - rt) * (vnew - rt) >= (vcl - rt) * (vcl - rt)) && !(dd > -vfclip && dd < vfclip)) dv = 0.f;
+  }
+  d[A] = -vf * dv;
+  if (newlp) newlp[n] = logpA;
+  if (newval) newval[n] = vnew;
+}
+// gb[c] = sum_n M[n*N + c] (sequential per column, deterministic)
+__global__ void colsum_f32_kernel(const float* __restrict__ Mx, long rows, int N, float* out) {
+  int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= N) return;
+  float s = 0.f;
+  for (long n = 0; n < rows; n++) s += Mx[n * N + c];
+  out[c] = s;
+}
+
+// ---------------------------------------------------------------- host launchers
+static inline unsigned grid_for(long n, int block = 256, long cap = 148 * 16) {
+  long g = (n + block - 1) / block;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return (unsigned)g;
+}
+
+int launch_obs_to_bf16_f64(const double* src, long NT, int D, int Dp, __nv_bfloat16* dst, cudaStream_t st) {
+  obs_to_bf16_kernel<double><<<grid_for(NT * Dp), 256, 0, st>>>(src, NT, D, Dp, dst);
+  count_launch();
+  PL_LAUNCH("obs_to_bf16_kernel");
+  return PL_OK;
+}
+int launch_obs_to_bf16_f32(const float* src, long NT, int D, int Dp, __nv_bfloat16* dst, cudaStream_t st) {
+  obs_to_bf16_kernel<float><<<grid_for(NT * Dp), 256, 0, st>>>(src, NT, D, Dp, dst);
+  count_launch();
+  PL_LAUNCH("obs_to_bf16_kernel");
+  return PL_OK;
+}
+int launch_obs_to_f32_f64(const double* src, long n, float* dst, cudaStream_t st) {
+  obs_to_f32_kernel<double><<<grid_for(n), 256, 0, st>>>(src, n, dst);
+  count_launch();
+  PL_LAUNCH("obs_to_f32_kernel");
+  return PL_OK;
+}
+int launch_columns(const double* act, const double* ret, const double* olp, const double* ov, long NT, int* act_i,
+                   float* ret_f, float* olp_f, float* ov_f, cudaStream_t st) {
+  columns_kernel<<<grid_for(NT), 256, 0, st>>>(act, ret, olp, ov, NT, act_i, ret_f, olp_f, ov_f);
+  count_launch();
+  PL_LAUNCH("columns_kernel");
+  return PL_OK;
+}
+int launch_perm(const double* perm, long n, int* out, cudaStream_t st) {
+  perm_kernel<<<grid_for(n), 256, 0, st>>>(perm, n, out);
+  count_launch();
+  PL_LAUNCH("perm_kernel");
+  return PL_OK;
+}
+int launch_gather(bool bf16, const int* idx, int Nmb, const void* obs, int rowElems, void* X, const int* act_c,
+                  const double* adv_c, const float* ret_c, const float* olp_c, const float* ov_c, int* mb_act,
+                  float* mb_adv, float* mb_ret, float* mb_olp, float* mb_ov, double* part, double* ms,
+                  cudaStream_t st) {
+  const int nb = (int)(Nmb < kRedBlocks * 8 ? (Nmb + 7) / 8 : kRedBlocks);
+  if (bf16)
+    gather_kernel<true><<<nb, 256, 0, st>>>(idx, Nmb, obs, rowElems, X, act_c, adv_c, ret_c, olp_c, ov_c, mb_act,
+                                            mb_adv, mb_ret, mb_olp, mb_ov, part);
+  else
+    gather_kernel<false><<<nb, 256, 0, st>>>(idx, Nmb, obs, rowElems, X, act_c, adv_c, ret_c, olp_c, ov_c, mb_act,
+                                             mb_adv, mb_ret, mb_olp, mb_ov, part);
+  adv_stats_kernel<<<1, 32, 0, st>>>(part, nb, Nmb, ms);
+  count_launch(2);
+  PL_LAUNCH("gather_kernel");
+  return PL_OK;
+}
+int launch_colsum_reduce(const float* part, int tiles, long ld, int ncols, float* out, cudaStream_t st) {
+  colsum_reduce_kernel<<<(unsigned)ceil_div(ncols, 128), 128, 0, st>>>(part, tiles, ld, ncols, out);
+  count_launch();
+  PL_LAUNCH("colsum_reduce_kernel");
+  return PL_OK;
+}
+int launch_splitk_reduce(const float* part, int S, long n, float* out, cudaStream_t st) {
+  splitk_reduce_kernel<<<grid_for(n), 256, 0, st>>>(part, S, n, out);
+  count_launch();
+  PL_LAUNCH("splitk_reduce_kernel");
+  return PL_OK;
+}
+int launch_gradnorm(const float* g, long P, double sc, double maxNorm, double* part, double* cc, cudaStream_t st) {
+  gradnorm_part_kernel<<<kRedBlocks, 256, 0, st>>>(g, P, sc, part);
+  gradnorm_final_kernel<<<1, 32, 0, st>>>(part, kRedBlocks, maxNorm, sc, cc);
+  count_launch(2);
+  PL_LAUNCH("gradnorm_kernel");
+  return PL_OK;
+}
+int launch_nesterov(const float* g, const double* cc, double* mom, double* u, double mu, long n, double* part,
+                    int* nparts, cudaStream_t st) {
+  const int nb = (int)(n < (long)kRedBlocks * 256 ? ceil_div(n, 256) : kRedBlocks);
+  nesterov_kernel<<<nb, 256, 0, st>>>(g, cc, mom, u, mu, n, part);
+  *nparts = nb;
+  count_launch();
+  PL_LAUNCH("nesterov_kernel");
+  return PL_OK;
+}
+int launch_ns_input(const double* u, const double* part, int nparts, int rows, int cols, double eps,
+                    __nv_bfloat16* X, long ldx, cudaStream_t st) {
+  ns_input_kernel<<<grid_for((long)rows * cols), 256, 0, st>>>(u, part, nparts, rows, cols, eps, X, ldx);
+  count_launch();
+  PL_LAUNCH("ns_input_kernel");
+  return PL_OK;
+}
+int launch_ns_finalize(const float* Xf, long ldx, int rows, int cols, double c1, double c2, double* W,
+                       __nv_bfloat16* Wb, long ldw, cudaStream_t st) {
+  ns_finalize_kernel<<<grid_for((long)rows * cols), 256, 0, st>>>(Xf, ldx, rows, cols, c1, c2, W, Wb, ldw);
+  count_launch();
+  PL_LAUNCH("ns_finalize_kernel");
+  return PL_OK;
+}
+int launch_stepvec_fast(const float* g, const double* cc, double* b, double* m, float* bf, double lr, double wd,
+                        double mu, int n, cudaStream_t st) {
+  stepvec_fast_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(g, cc, b, m, bf, lr, wd, mu, n);
+  count_launch();
+  PL_LAUNCH("stepvec_fast_kernel");
+  return PL_OK;
+}
+int launch_w_to_bf16(const double* W, int rows, int cols, __nv_bfloat16* Wb, long ldw, cudaStream_t st) {
+  w_to_bf16_kernel<<<grid_for((long)rows * cols), 256, 0, st>>>(W, rows, cols, Wb, ldw);
+  count_launch();
+  PL_LAUNCH("w_to_bf16_kernel");
+  return PL_OK;
+}
+int launch_f64_to_f32(const double* s, long n, float* d, cudaStream_t st) {
+  f64_to_f32_kernel<<<grid_for(n), 256, 0, st>>>(s, n, d);
+  count_launch();
+  PL_LAUNCH("f64_to_f32_kernel");
+  return PL_OK;
+}
+int launch_f32_to_f64(const float* s, long n, double* d, cudaStream_t st) {
+  f32_to_f64_kernel<<<grid_for(n), 256, 0, st>>>(s, n, d);
+  count_launch();
+  PL_LAUNCH("f32_to_f64_kernel");
+  return PL_OK;
+}
+int launch_sgemm(int M, int N, int K, const float* A, long ars, long acs, const float* B, long brs, long bcs, float* C,
+                 long ldc, float alpha, cudaStream_t st) {
+  dim3 grid((unsigned)ceil_div(N, 64), (unsigned)ceil_div(M, 64));
+  sgemm_kernel<<<grid, 256, 0, st>>>(M, N, K, A, ars, acs, B, brs, bcs, C, ldc, alpha);
+  count_launch();
+  PL_LAUNCH("sgemm_kernel");
+  return PL_OK;
+}
+int launch_bias_act_f32(float* Z, float* H, const float* b, long M, int N, int act, cudaStream_t st) {
+  bias_act_f32_kernel<<<grid_for(M * N), 256, 0, st>>>(Z, H, b, M, N, act);
+  count_launch();
+  PL_LAUNCH("bias_act_f32_kernel");
+  return PL_OK;
+}
+int launch_act_grad_f32(float* dH, const float* Z, long n, int act, cudaStream_t st) {
+  act_grad_f32_kernel<<<grid_for(n), 256, 0, st>>>(dH, Z, n, act);
+  count_launch();
+  PL_LAUNCH("act_grad_f32_kernel");
+  return PL_OK;
+}
+int launch_ppo_rows_f32(const float* Out, int M, int A, const int* act, const float* adv, const double* ms,
+                        const float* ret, const float* olp, const float* ov, float vf, float ent, float clip,
+                        float vfclip, float* dOut, float* newlp, float* newval, cudaStream_t st) {
+  ppo_rows_f32_kernel<<<(unsigned)ceil_div(M, 128), 128, 0, st>>>(Out, M, A, act, adv, ms, ret, olp, ov, vf, ent, clip,
+                                                                  vfclip, dOut, newlp, newval);
+  count_launch();
+  PL_LAUNCH("ppo_rows_f32_kernel");
+  return PL_OK;
+}
+int launch_colsum_f32(const float* Mx, long rows, int N, float* out, cudaStream_t st) {
+  colsum_f32_kernel<<<(unsigned)ceil_div(N, 128), 128, 0, st>>>(Mx, rows, N, out);
+  count_launch();
+  PL_LAUNCH("colsum_f32_kernel");
+  return PL_OK;
+}
+
+}  // namespace pl

@@ -1,0 +1,906 @@
+// The PPO+Muon update of the feed-forward policy: one session per (policy handle, shapes), every
+// buffer resident, epochs x minibatches run back to back on one stream.
+//
+// Per minibatch (bf16 tier):
+//   gather rows of the resident columns through the epoch's shuffle (+ advantage mean/std)
+//   forward   H_l = act(H_{l-1} W_l^T + b_l)             tcgen05 GEMM, bias+act epilogue
+//   head      logits/value = H_L W_o^T + b_o -> dOut     tcgen05 GEMM, PPO-objective-gradient epilogue
+//   backward  dW_l = dZ_l^T H_{l-1} (MN-major operands, split-K, fixed-order slice sum)
+//             dZ_{l-1} = (dZ_l W_l) * act'(Z_{l-1})      tcgen05 GEMM, act' epilogue + bias column sums
+//   clip      global grad norm of the mean gradient (fixed-order f64 reduction)
+//   Muon      f64 Nesterov -> Frobenius normalise -> Newton-Schulz on the tensor cores ->
+//             f64 decoupled-decay ascent step on the master weights + their bf16 shadow
+// The tight tier (bf16 = 0) runs the same sequence with fp32 SIMT GEMMs and the f64 Newton-Schulz
+// of the reference oracle. Semantics follow lean_cuda_train_update_resident
+// (ffi/puffercuda.cu:1187-1294): mbSize = NT/numMB with the last minibatch taking the remainder,
+// gradients summed over rows then scaled to the mean (and clipped when maxGradNorm > 0), value
+// clip when old values are supplied and vfClip > 0.
+#include <math.h>
+#include <string.h>
+
+#include <mutex>
+#include <vector>
+
+#include "pl_gemm.cuh"
+#include "pl_mlp.cuh"
+#include "pl_muon.cuh"
+#include "pl_runtime.h"
+
+using namespace pl;
+
+struct pl_update {
+  pl_update_desc d;
+  int dev = 0;
+  double* pm = nullptr;  // [params(P); mom(P)] f64 (policy handle)
+  size_t P = 0;
+  int L = 1, O = 0, Op = 64, Dp = 64, Hp = 64;
+  long mbSize = 0, mbMax = 0;
+  bool fast = true;
+  std::vector<Layer> layers;
+  std::vector<double> coeffs;
+  int iters = 5;
+  std::vector<void*> allocs;
+  // columns
+  void* obs = nullptr;  // fast: bf16 [NT x Dp]; tight: f32 [NT x D]
+  int* act_c = nullptr;
+  double* adv_c = nullptr;
+  float *ret_c = nullptr, *olp_c = nullptr, *ov_c = nullptr;
+  int* perm = nullptr;
+  double* stage = nullptr;
+  size_t stage_elems = 0;
+  // minibatch
+  void* X = nullptr;
+  std::vector<void*> Hs, Zs;
+  void* dZ[2] = {nullptr, nullptr};
+  void* dOut = nullptr;
+  float* Out = nullptr;  // tight tier logits
+  int* mb_act = nullptr;
+  float *mb_adv = nullptr, *mb_ret = nullptr, *mb_olp = nullptr, *mb_ov = nullptr;
+  double* adv_part = nullptr;
+  double* ms = nullptr;
+  float* colpart = nullptr;
+  float* splitk = nullptr;
+  size_t splitk_elems = 0;
+  float* grad = nullptr;
+  double* gn_part = nullptr;
+  double* cc = nullptr;
+  float* loss_part = nullptr;
+  // parameters in compute precision
+  std::vector<__nv_bfloat16*> Wb;  // fast tier shadows (out_p x in_p)
+  std::vector<float*> Wf;          // tight tier fp32 weights (out x in)
+  std::vector<float*> bf;          // fp32 biases (out_p)
+  NsWork ns;
+  double* exact_ws = nullptr;
+  uint64_t launches = 0;
+  bool grad_only = false;  // pl_mlp_ppo_grad: no normalisation, no optimizer step
+  bool alloc_failed = false;
+  bool loss_on = false;
+  double losses[7] = {0, 0, 0, 0, 0, 0, 0};
+};
+
+namespace {
+
+static std::mutex g_mu;
+static bool g_loss_on = false;
+static double g_losses[7] = {0, 0, 0, 0, 0, 0, 0};
+
+template <typename T>
+static T* dalloc(pl_update* u, size_t n) {
+  void* p = nullptr;
+  if (n == 0) n = 1;
+  if (cudaMalloc(&p, n * sizeof(T)) != cudaSuccess) {
+    cudaGetLastError();
+    u->alloc_failed = true;
+    set_error(PL_ERR_NOMEM, "cudaMalloc of %zu bytes failed", n * sizeof(T));
+    return nullptr;
+  }
+  u->allocs.push_back(p);
+  return (T*)p;
+}
+
+static void free_all(pl_update* u) {
+  for (void* p : u->allocs) cudaFree(p);
+  u->allocs.clear();
+}
+
+static int build_layout(pl_update* u) {
+  const pl_update_desc& d = u->d;
+  u->L = (int)(d.arch.L ? d.arch.L : 1);
+  u->O = (int)d.A + 1;
+  u->Op = u->O <= 64 ? 64 : 128;
+  u->Dp = (int)round_up((long)d.D, 64);
+  u->Hp = (int)round_up((long)d.H, 64);
+  u->layers.clear();
+  size_t off = 0;
+  for (int l = 0; l <= u->L; l++) {
+    Layer ly;
+    ly.in = l == 0 ? (int)d.D : (int)d.H;
+    ly.out = l == u->L ? u->O : (int)d.H;
+    ly.in_p = l == 0 ? u->Dp : u->Hp;
+    ly.out_p = l == u->L ? u->Op : u->Hp;
+    ly.oW = off;
+    off += (size_t)ly.out * ly.in;
+    ly.ob = off;
+    off += (size_t)ly.out;
+    u->layers.push_back(ly);
+  }
+  u->P = off;
+  u->mbSize = (long)(d.NT / d.numMB);
+  if (u->mbSize < 1) u->mbSize = 1;
+  u->mbMax = (long)d.NT - (long)(d.numMB - 1) * u->mbSize;
+  if (u->mbMax < u->mbSize) u->mbMax = u->mbSize;
+  if (u->mbMax > (long)d.NT) u->mbMax = (long)d.NT;
+  return PL_OK;
+}
+
+static int alloc_session(pl_update* u) {
+  const pl_update_desc& d = u->d;
+  const long NT = (long)d.NT, M = u->mbMax;
+  const int L = u->L;
+  const bool fast = u->fast;
+  const size_t es = fast ? 2 : 4;  // activation element size
+  (void)es;
+  // columns
+  if (fast)
+    u->obs = dalloc<__nv_bfloat16>(u, (size_t)NT * u->Dp);
+  else
+    u->obs = dalloc<float>(u, (size_t)NT * d.D);
+  u->act_c = dalloc<int>(u, NT);
+  u->adv_c = dalloc<double>(u, NT);
+  u->ret_c = dalloc<float>(u, NT);
+  u->olp_c = dalloc<float>(u, NT);
+  u->ov_c = d.use_old_values ? dalloc<float>(u, NT) : nullptr;
+  u->perm = dalloc<int>(u, (size_t)d.epochs * NT);
+  u->stage_elems = (size_t)std::min<long>(std::max<long>(NT * 8, (long)d.epochs * NT), 1L << 25);
+  if (u->stage_elems < (size_t)NT) u->stage_elems = NT;
+  if (u->stage_elems < u->P) u->stage_elems = u->P;  // the tight tier widens the gradient here
+  u->stage = dalloc<double>(u, u->stage_elems);
+  // minibatch
+  const int mt = (int)ceil_div(M, 128);
+  if (fast) {
+    u->X = dalloc<__nv_bfloat16>(u, (size_t)M * u->Dp);
+    for (int l = 0; l < L; l++) {
+      u->Hs.push_back(dalloc<__nv_bfloat16>(u, (size_t)M * u->Hp));
+      u->Zs.push_back(d.arch.act == 1 ? (void*)dalloc<__nv_bfloat16>(u, (size_t)M * u->Hp) : nullptr);
+    }
+    u->dZ[0] = dalloc<__nv_bfloat16>(u, (size_t)M * u->Hp);
+    u->dZ[1] = dalloc<__nv_bfloat16>(u, (size_t)M * u->Hp);
+    u->dOut = dalloc<__nv_bfloat16>(u, (size_t)M * u->Op);
+  } else {
+    u->X = dalloc<float>(u, (size_t)M * d.D);
+    for (int l = 0; l < L; l++) {
+      u->Hs.push_back(dalloc<float>(u, (size_t)M * d.H));
+      u->Zs.push_back(dalloc<float>(u, (size_t)M * d.H));
+    }
+    u->dZ[0] = dalloc<float>(u, (size_t)M * d.H);
+    u->dZ[1] = dalloc<float>(u, (size_t)M * d.H);
+    u->dOut = dalloc<float>(u, (size_t)M * u->O);
+    u->Out = dalloc<float>(u, (size_t)M * u->O);
+  }
+  u->mb_act = dalloc<int>(u, M);
+  u->mb_adv = dalloc<float>(u, M);
+  u->mb_ret = dalloc<float>(u, M);
+  u->mb_olp = dalloc<float>(u, M);
+  u->mb_ov = d.use_old_values ? dalloc<float>(u, M) : nullptr;
+  u->adv_part = dalloc<double>(u, 2 * 4096);
+  u->ms = dalloc<double>(u, 4);
+  u->colpart = dalloc<float>(u, (size_t)mt * std::max(u->Hp, u->Op));
+  u->grad = dalloc<float>(u, u->P);
+  u->gn_part = dalloc<double>(u, 4096);
+  u->cc = dalloc<double>(u, 4);
+  u->loss_part = dalloc<float>(u, (size_t)mt * 8);
+  // split-K slices for the largest weight gradient
+  size_t maxw = 0;
+  for (auto& ly : u->layers) maxw = std::max(maxw, (size_t)ly.out * ly.in);
+  u->splitk_elems = maxw * 8;
+  u->splitk = fast ? dalloc<float>(u, u->splitk_elems) : nullptr;
+  // parameters in compute precision
+  for (auto& ly : u->layers) {
+    if (fast) {
+      u->Wb.push_back(dalloc<__nv_bfloat16>(u, (size_t)ly.out_p * ly.in_p));
+      u->Wf.push_back(nullptr);
+    } else {
+      u->Wb.push_back(nullptr);
+      u->Wf.push_back(dalloc<float>(u, (size_t)ly.out * ly.in));
+    }
+    u->bf.push_back(dalloc<float>(u, ly.out_p));
+  }
+  // Muon workspace
+  long mmax = 0, nmax = 0, nprod = 0;
+  for (auto& ly : u->layers) {
+    long m = std::min(ly.out, ly.in), n = std::max(ly.out, ly.in);
+    mmax = std::max(mmax, m);
+    nmax = std::max(nmax, n);
+    nprod = std::max(nprod, (long)ly.out * ly.in);
+  }
+  const long ldx = round_up(nmax, 64), ldg = round_up(mmax, 64);
+  if (fast) {
+    u->ns.ldx = ldx;
+    u->ns.ldg = ldg;
+    u->ns.X0 = dalloc<__nv_bfloat16>(u, (size_t)round_up(mmax, 128) * ldx);
+    u->ns.X1 = dalloc<__nv_bfloat16>(u, (size_t)round_up(mmax, 128) * ldx);
+    u->ns.G = dalloc<__nv_bfloat16>(u, (size_t)round_up(mmax, 128) * ldg);
+    u->ns.B = dalloc<__nv_bfloat16>(u, (size_t)round_up(mmax, 128) * ldg);
+    u->ns.Xf = dalloc<float>(u, (size_t)mmax * ldx);
+    u->ns.U = dalloc<double>(u, nprod);
+    u->ns.part = dalloc<double>(u, 4096);
+    for (void* p : {(void*)u->ns.X0, (void*)u->ns.X1, (void*)u->ns.G, (void*)u->ns.B})
+      if (p) cudaMemset(p, 0, 1);  // touch
+  } else {
+    size_t ws = 0;
+    for (auto& ly : u->layers) ws = std::max(ws, exact_ws_doubles(ly.out, ly.in));
+    u->exact_ws = dalloc<double>(u, ws);
+  }
+  if (u->alloc_failed) return PL_ERR_NOMEM;
+  // zero the padded shadow weights/biases once; their pads stay zero for the session
+  for (size_t l = 0; l < u->layers.size(); l++) {
+    if (u->Wb[l]) PL_CUDA(cudaMemset(u->Wb[l], 0, sizeof(__nv_bfloat16) * u->layers[l].out_p * u->layers[l].in_p));
+    PL_CUDA(cudaMemset(u->bf[l], 0, sizeof(float) * u->layers[l].out_p));
+  }
+  if (fast) {
+    PL_CUDA(cudaMemset(u->X, 0, sizeof(__nv_bfloat16) * M * u->Dp));
+    PL_CUDA(cudaMemset(u->ns.X0, 0, sizeof(__nv_bfloat16) * round_up(mmax, 128) * ldx));
+    PL_CUDA(cudaMemset(u->ns.X1, 0, sizeof(__nv_bfloat16) * round_up(mmax, 128) * ldx));
+  }
+  return PL_OK;
+}
+
+// f64 master -> compute-precision copies of every layer (after load and after each Muon step).
+static int refresh_shadows(pl_update* u, cudaStream_t st) {
+  for (size_t l = 0; l < u->layers.size(); l++) {
+    const Layer& ly = u->layers[l];
+    int rc;
+    if (u->fast)
+      rc = launch_w_to_bf16(u->pm + ly.oW, ly.out, ly.in, u->Wb[l], ly.in_p, st);
+    else
+      rc = launch_f64_to_f32(u->pm + ly.oW, (long)ly.out * ly.in, u->Wf[l], st);
+    if (rc) return rc;
+    rc = launch_f64_to_f32(u->pm + ly.ob, ly.out, u->bf[l], st);
+    if (rc) return rc;
+  }
+  return PL_OK;
+}
+
+static int pick_bn(int N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
+
+// Weight gradient dW[out x in] = sum_rows dZ[row, out] * Hin[row, in] into grad (f32, row-major)
+static int wgrad_fast(pl_update* u, const void* dZ, long ldz, int out, const void* Hin, long ldh, int in, int Nmb,
+                      float* dst, cudaStream_t st) {
+  Operand A{dZ, Nmb, out, ldz, 1, 0};
+  Operand B{Hin, Nmb, in, ldh, 1, 0};
+  const int bn = in <= 128 ? 128 : 256;
+  const long tiles = ceil_div(out, 128) * ceil_div(in, bn);
+  const long kb = ceil_div(Nmb, 64);
+  int S = (int)std::min<long>(std::max<long>(1, (2 * 148 + tiles - 1) / tiles), 8);
+  while (S > 1 && kb / S < 4) S--;
+  while (S > 1 && (size_t)S * out * in > u->splitk_elems) S--;
+  EpiArgs e{};
+  e.ldo = in;
+  e.out_rows = out;
+  e.out_cols = in;
+  e.alpha = 1.f;
+  if (S == 1) {
+    e.out = dst;
+    return gemm_launch(bn, EPI_F32, true, true, A, B, out, in, Nmb, 1, e, st);
+  }
+  e.out = u->splitk;
+  e.out_bstride = (long)out * in;
+  e.k_splits = S;
+  int rc = gemm_launch(bn, EPI_F32, true, true, A, B, out, in, Nmb, 1, e, st);
+  if (rc) return rc;
+  return launch_splitk_reduce(u->splitk, S, (long)out * in, dst, st);
+}
+
+static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool last, cudaStream_t st) {
+  const pl_update_desc& d = u->d;
+  const int L = u->L;
+  const int act = d.arch.act;
+  const int mt = (int)ceil_div(Nmb, 128);
+  int rc = launch_gather(true, idx, Nmb, u->obs, u->Dp, u->X, u->act_c, u->adv_c, u->ret_c, u->olp_c, u->ov_c,
+                         u->mb_act, u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st);
+  if (rc) return rc;
+  // ---- forward
+  const void* hin = u->X;
+  long ldin = u->Dp;
+  for (int l = 0; l < L; l++) {
+    const Layer& ly = u->layers[l];
+    Operand A{hin, Nmb, ly.in, ldin, 1, 0};
+    Operand B{u->Wb[l], ly.out, ly.in, ly.in_p, 1, 0};
+    EpiArgs e{};
+    e.out = u->Hs[l];
+    e.ldo = u->Hp;
+    e.out_rows = Nmb;
+    e.out_cols = ly.out;
+    e.bias = u->bf[l];
+    e.out2 = u->Zs[l];
+    e.ldo2 = u->Hp;
+    e.act = act;
+    rc = gemm_launch(pick_bn(ly.out), EPI_FWD, false, false, A, B, Nmb, ly.out, ly.in, 1, e, st);
+    if (rc) return rc;
+    hin = u->Hs[l];
+    ldin = u->Hp;
+  }
+  // ---- PPO head: logits + value -> objective gradient dOut
+  const Layer& hd = u->layers[L];
+  {
+    Operand A{hin, Nmb, hd.in, ldin, 1, 0};
+    Operand B{u->Wb[L], hd.out, hd.in, hd.in_p, 1, 0};
+    EpiArgs e{};
+    e.out = u->dOut;
+    e.ldo = u->Op;
+    e.out_rows = Nmb;
+    e.out_cols = hd.out;
+    e.bias = u->bf[L];
+    e.colsum = u->colpart;
+    e.ld_colsum = u->Op;
+    e.act_idx = u->mb_act;
+    e.adv = u->mb_adv;
+    e.adv_ms = u->grad_only ? nullptr : u->ms;
+    e.ret = u->mb_ret;
+    e.olp = u->mb_olp;
+    e.ov = u->mb_ov;
+    e.A = (int)d.A;
+    e.vf = (float)d.vfCoef;
+    e.ent = (float)d.entCoef;
+    e.clip = (float)d.clipEps;
+    e.vfclip = (float)d.vfClip;
+    e.loss_part = last && u->loss_on ? u->loss_part : nullptr;
+    rc = gemm_launch(u->Op, EPI_PPO, false, false, A, B, Nmb, hd.out, hd.in, 1, e, st);
+    if (rc) return rc;
+    rc = launch_colsum_reduce(u->colpart, mt, u->Op, hd.out, u->grad + hd.ob, st);
+    if (rc) return rc;
+  }
+  // ---- backward
+  const void* dcur = u->dOut;
+  long ldd = u->Op;
+  int dsel = 0;
+  for (int l = L; l >= 0; l--) {
+    const Layer& ly = u->layers[l];
+    const void* hprev = l == 0 ? u->X : u->Hs[l - 1];
+    const long ldprev = l == 0 ? u->Dp : u->Hp;
+    rc = wgrad_fast(u, dcur, ldd, ly.out, hprev, ldprev, ly.in, Nmb, u->grad + ly.oW, st);
+    if (rc) return rc;
+    if (l == 0) break;
+    // dZ_{l-1} = (dcur W_l) * act'(Z_{l-1})
+    const Layer& lp = u->layers[l - 1];
+    Operand A{dcur, Nmb, ly.out, ldd, 1, 0};
+    Operand B{u->Wb[l], ly.out, ly.in, ly.in_p, 1, 0};  // MN-major: rows = K (= out), cols = N (= in)
+    EpiArgs e{};
+    e.out = u->dZ[dsel];
+    e.ldo = u->Hp;
+    e.out_rows = Nmb;
+    e.out_cols = lp.out;
+    e.aux = (const __nv_bfloat16*)(act == 1 ? u->Zs[l - 1] : u->Hs[l - 1]);
+    e.ld_aux = u->Hp;
+    e.act = act;
+    e.colsum = u->colpart;
+    e.ld_colsum = u->Hp;
+    rc = gemm_launch(pick_bn(lp.out), EPI_DGRAD, false, true, A, B, Nmb, lp.out, ly.out, 1, e, st);
+    if (rc) return rc;
+    rc = launch_colsum_reduce(u->colpart, mt, u->Hp, lp.out, u->grad + lp.ob, st);
+    if (rc) return rc;
+    dcur = u->dZ[dsel];
+    ldd = u->Hp;
+    dsel ^= 1;
+  }
+  if (u->grad_only) return PL_OK;
+  // ---- clip to the mean gradient, then Muon on every layer
+  rc = launch_gradnorm(u->grad, (long)u->P, 1.0 / (double)Nmb, d.maxGradNorm, u->gn_part, u->cc, st);
+  if (rc) return rc;
+  for (size_t l = 0; l < u->layers.size(); l++) {
+    const Layer& ly = u->layers[l];
+    const long n = (long)ly.out * ly.in;
+    int nparts = 0;
+    rc = launch_nesterov(u->grad + ly.oW, u->cc, u->pm + u->P + ly.oW, u->ns.U, d.mu, n, u->ns.part, &nparts, st);
+    if (rc) return rc;
+    const int m = std::min(ly.out, ly.in), nn = std::max(ly.out, ly.in);
+    rc = launch_ns_input(u->ns.U, u->ns.part, nparts, ly.out, ly.in, d.eps, u->ns.X0, u->ns.ldx, st);
+    if (rc) return rc;
+    rc = ns_run(m, nn, u->coeffs.data(), u->iters, u->ns, u->ns.X0, u->ns.ldx, u->ns.Xf, u->ns.ldx, st);
+    if (rc) return rc;
+    const double r = (double)ly.out / (double)ly.in;
+    const double scale = sqrt(r > 1.0 ? r : 1.0);
+    rc = launch_ns_finalize(u->ns.Xf, u->ns.ldx, ly.out, ly.in, 1.0 - lr * d.wd, lr * scale, u->pm + ly.oW, u->Wb[l],
+                            ly.in_p, st);
+    if (rc) return rc;
+    rc = launch_stepvec_fast(u->grad + ly.ob, u->cc, u->pm + ly.ob, u->pm + u->P + ly.ob, u->bf[l], lr, d.wd, d.mu,
+                             ly.out, st);
+    if (rc) return rc;
+  }
+  return PL_OK;
+}
+
+static int minibatch_tight(pl_update* u, const int* idx, int Nmb, double lr, bool last, cudaStream_t st) {
+  (void)last;
+  const pl_update_desc& d = u->d;
+  const int L = u->L, act = d.arch.act, D = (int)d.D, H = (int)d.H, O = u->O;
+  int rc = launch_gather(false, idx, Nmb, u->obs, D, u->X, u->act_c, u->adv_c, u->ret_c, u->olp_c, u->ov_c, u->mb_act,
+                         u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st);
+  if (rc) return rc;
+  const float* hin = (const float*)u->X;
+  int nin = D;
+  for (int l = 0; l < L; l++) {
+    rc = launch_sgemm(Nmb, H, nin, hin, nin, 1, u->Wf[l], nin, 1, (float*)u->Zs[l], H, 1.f, st);
+    if (rc) return rc;
+    rc = launch_bias_act_f32((float*)u->Zs[l], (float*)u->Hs[l], u->bf[l], Nmb, H, act, st);
+    if (rc) return rc;
+    hin = (const float*)u->Hs[l];
+    nin = H;
+  }
+  rc = launch_sgemm(Nmb, O, H, hin, H, 1, u->Wf[L], H, 1, u->Out, O, 1.f, st);
+  if (rc) return rc;
+  rc = launch_bias_act_f32(u->Out, nullptr, u->bf[L], Nmb, O, 0, st);
+  if (rc) return rc;
+  rc = launch_ppo_rows_f32(u->Out, Nmb, (int)d.A, u->mb_act, u->mb_adv, u->grad_only ? nullptr : u->ms, u->mb_ret,
+                           u->mb_olp, u->mb_ov, (float)d.vfCoef, (float)d.entCoef, (float)d.clipEps, (float)d.vfClip,
+                           (float*)u->dOut, nullptr, nullptr, st);
+  if (rc) return rc;
+  const float* dcur = (const float*)u->dOut;
+  int nd = O;
+  int dsel = 0;
+  for (int l = L; l >= 0; l--) {
+    const Layer& ly = u->layers[l];
+    const float* hprev = l == 0 ? (const float*)u->X : (const float*)u->Hs[l - 1];
+    // bias grad
+    rc = launch_colsum_f32(dcur, Nmb, nd, u->grad + ly.ob, st);
+    if (rc) return rc;
+    // dW[o, i] = sum_n dcur[n, o] hprev[n, i]
+    rc = launch_sgemm(ly.out, ly.in, Nmb, dcur, 1, nd, hprev, 1, ly.in, u->grad + ly.oW, ly.in, 1.f, st);
+    if (rc) return rc;
+    if (l == 0) break;
+    // dH[n, i] = sum_o dcur[n, o] W[o, i]
+    float* dn = (float*)u->dZ[dsel];
+    rc = launch_sgemm(Nmb, ly.in, ly.out, dcur, nd, 1, u->Wf[l], 1, ly.in, dn, ly.in, 1.f, st);
+    if (rc) return rc;
+    rc = launch_act_grad_f32(dn, (const float*)u->Zs[l - 1], (long)Nmb * ly.in, act, st);
+    if (rc) return rc;
+    dcur = dn;
+    nd = ly.in;
+    dsel ^= 1;
+  }
+  if (u->grad_only) return PL_OK;
+  rc = launch_gradnorm(u->grad, (long)u->P, 1.0 / (double)Nmb, d.maxGradNorm, u->gn_part, u->cc, st);
+  if (rc) return rc;
+  // f64 tight Muon: widen the gradient, scale by cc on the host-free path (the scale is a device
+  // scalar, read back once per minibatch: this tier is the parity tier, not the fast path)
+  double cc = 0;
+  PL_CUDA(cudaMemcpyAsync(&cc, u->cc, sizeof(double), cudaMemcpyDeviceToHost, st));
+  PL_CUDA(cudaStreamSynchronize(st));
+  double* g64 = u->stage;  // P <= stage size is checked at creation
+  rc = launch_f32_to_f64(u->grad, (long)u->P, g64, st);
+  if (rc) return rc;
+  rc = set_ns_coeffs(u->coeffs.data(), u->iters, st);
+  if (rc) return rc;
+  for (size_t l = 0; l < u->layers.size(); l++) {
+    const Layer& ly = u->layers[l];
+    rc = muon_mat_exact(ly.out, ly.in, u->pm + ly.oW, u->pm + u->P + ly.oW, g64 + ly.oW, cc, lr, d.wd, d.mu, d.eps,
+                        u->iters, u->exact_ws, st);
+    if (rc) return rc;
+    rc = stepvec_launch(u->pm + ly.ob, u->pm + u->P + ly.ob, g64 + ly.ob, lr, d.wd, d.mu, cc, ly.out, st);
+    if (rc) return rc;
+  }
+  return refresh_shadows(u, st);
+}
+
+static int reduce_losses(pl_update* u, int Nmb, cudaStream_t st) {
+  const int mt = (int)ceil_div(Nmb, 128);
+  std::vector<float> h((size_t)mt * 8);
+  PL_CUDA(cudaMemcpyAsync(h.data(), u->loss_part, sizeof(float) * h.size(), cudaMemcpyDeviceToHost, st));
+  PL_CUDA(cudaStreamSynchronize(st));
+  double s[6] = {0, 0, 0, 0, 0, 0};
+  for (int t = 0; t < mt; t++)
+    for (int q = 0; q < 6; q++) s[q] += h[(size_t)t * 8 + q];
+  for (int q = 0; q < 6; q++) s[q] /= (double)Nmb;
+  const pl_update_desc& d = u->d;
+  // [policy, value, entropy, total, old_kl, kl, clipfrac]
+  u->losses[0] = s[0];
+  u->losses[1] = s[1];
+  u->losses[2] = s[2];
+  u->losses[3] = s[0] + d.vfCoef * s[1] - d.entCoef * s[2];
+  u->losses[4] = s[4];
+  u->losses[5] = s[3];
+  u->losses[6] = s[5];
+  std::lock_guard<std::mutex> g(g_mu);
+  memcpy(g_losses, u->losses, sizeof(g_losses));
+  return PL_OK;
+}
+
+}  // namespace
+
+// ================================================================================ C ABI
+extern "C" {
+
+size_t pl_mlp_param_count(size_t D, size_t H, size_t A, size_t L) {
+  if (L == 0) L = 1;
+  return H * D + H + (L - 1) * (H * H + H) + (A + 1) * H + A + 1;
+}
+
+int pl_update_create(size_t handle, const pl_update_desc* desc, pl_update** out) {
+  int rc = require_device();
+  if (rc) return rc;
+  PL_REQUIRE(desc && out, PL_ERR_INVALID, "pl_update_create: NULL argument");
+  PL_REQUIRE(handle != 0, PL_ERR_INVALID, "pl_update_create: policy handle is 0");
+  const pl_update_desc& d = *desc;
+  PL_REQUIRE(d.NT > 0 && d.D > 0 && d.H > 0 && d.A > 0 && d.epochs > 0 && d.numMB > 0, PL_ERR_INVALID,
+             "empty update shape (NT=%zu D=%zu H=%zu A=%zu epochs=%zu numMB=%zu)", d.NT, d.D, d.H, d.A, d.epochs,
+             d.numMB);
+  PL_REQUIRE(d.A + 1 <= 128, PL_ERR_UNSUPPORTED, "at most 127 discrete actions (A=%zu)", d.A);
+  PL_REQUIRE(d.NT < (1ul << 31) && d.epochs * d.NT < (1ul << 31), PL_ERR_UNSUPPORTED, "NT x epochs must fit int32");
+  PL_REQUIRE(d.arch.act == 0 || d.arch.act == 1, PL_ERR_INVALID, "activation must be 0 (ReLU) or 1 (GELU)");
+  pl_update* u = new pl_update();
+  u->d = d;
+  u->fast = d.bf16 != 0;
+  cudaGetDevice(&u->dev);
+  u->pm = (double*)handle;
+  if (d.arch.ns_coeffs && d.arch.ns_iters) {
+    u->coeffs.assign(d.arch.ns_coeffs, d.arch.ns_coeffs + 3 * d.arch.ns_iters);
+    u->iters = (int)d.arch.ns_iters;
+  } else {
+    u->coeffs.assign(&kMuonCoeffs[0][0], &kMuonCoeffs[0][0] + 15);
+    u->iters = 5;
+  }
+  build_layout(u);
+  rc = alloc_session(u);
+  if (!rc && !u->fast && u->stage_elems < u->P) rc = set_error(PL_ERR_UNSUPPORTED, "tight tier staging too small");
+  if (!rc) rc = refresh_shadows(u, 0);
+  if (!rc) rc = (cudaDeviceSynchronize() == cudaSuccess) ? PL_OK : check_cuda(cudaGetLastError(), "session init");
+  if (rc) {
+    free_all(u);
+    delete u;
+    return rc;
+  }
+  *out = u;
+  return PL_OK;
+}
+
+int pl_update_destroy(pl_update* u) {
+  if (!u) return PL_OK;
+  cudaDeviceSynchronize();
+  free_all(u);
+  delete u;
+  return PL_OK;
+}
+
+uint64_t pl_update_last_launches(const pl_update* u) { return u ? u->launches : 0; }
+
+}  // extern "C"
+
+// Uploads n doubles from host through the staging buffer into dst via `fn(stage, count, offset)`.
+template <typename F>
+static int staged(pl_update* u, const double* host, size_t n, cudaStream_t st, F fn) {
+  for (size_t off = 0; off < n; off += u->stage_elems) {
+    const size_t c = std::min(u->stage_elems, n - off);
+    PL_CUDA(cudaMemcpyAsync(u->stage, host + off, c * sizeof(double), cudaMemcpyHostToDevice, st));
+    int rc = fn(u->stage, c, off);
+    if (rc) return rc;
+  }
+  return PL_OK;
+}
+
+extern "C" {
+
+int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, const double* adv, const double* ret,
+                          const double* olp, const double* oldVal, const double* perm, void* stream) {
+  PL_REQUIRE(u && obs && acts && adv && ret && olp && perm, PL_ERR_INVALID, "pl_update_set_columns: NULL column");
+  PL_REQUIRE(!u->d.use_old_values || oldVal, PL_ERR_INVALID, "value clip needs the old-value column");
+  cudaStream_t st = (cudaStream_t)stream;
+  const pl_update_desc& d = u->d;
+  const long NT = (long)d.NT;
+  const int D = (int)d.D;
+  // obs: whole rows per chunk
+  const size_t rows_per = std::max<size_t>(1, u->stage_elems / d.D);
+  for (size_t r0 = 0; r0 < (size_t)NT; r0 += rows_per) {
+    const size_t nr = std::min(rows_per, (size_t)NT - r0);
+    PL_CUDA(cudaMemcpyAsync(u->stage, obs + r0 * D, nr * D * sizeof(double), cudaMemcpyHostToDevice, st));
+    int rc = u->fast ? launch_obs_to_bf16_f64(u->stage, (long)nr, D, u->Dp, (__nv_bfloat16*)u->obs + r0 * u->Dp, st)
+                     : launch_obs_to_f32_f64(u->stage, (long)nr * D, (float*)u->obs + r0 * D, st);
+    if (rc) return rc;
+  }
+  PL_CUDA(cudaMemcpyAsync(u->adv_c, adv, NT * sizeof(double), cudaMemcpyHostToDevice, st));
+  // act/ret/olp/ov -> int32 / f32 through staging (4 columns)
+  double* s = u->stage;
+  const size_t per = u->stage_elems / 4;
+  for (size_t off = 0; off < (size_t)NT; off += per) {
+    const size_t c = std::min(per, (size_t)NT - off);
+    PL_CUDA(cudaMemcpyAsync(s, acts + off, c * 8, cudaMemcpyHostToDevice, st));
+    PL_CUDA(cudaMemcpyAsync(s + per, ret + off, c * 8, cudaMemcpyHostToDevice, st));
+    PL_CUDA(cudaMemcpyAsync(s + 2 * per, olp + off, c * 8, cudaMemcpyHostToDevice, st));
+    if (u->ov_c) PL_CUDA(cudaMemcpyAsync(s + 3 * per, oldVal + off, c * 8, cudaMemcpyHostToDevice, st));
+    int rc = launch_columns(s, s + per, s + 2 * per, u->ov_c ? s + 3 * per : nullptr, (long)c, u->act_c + off,
+                            u->ret_c + off, u->olp_c + off, u->ov_c ? u->ov_c + off : nullptr, st);
+    if (rc) return rc;
+  }
+  return staged(u, perm, d.epochs * d.NT, st, [&](double* sp, size_t c, size_t off) {
+    return launch_perm(sp, (long)c, u->perm + off, st);
+  });
+}
+
+int pl_update_set_columns_dev(pl_update* u, const float* obs, const double* acts, const double* adv,
+                              const double* ret, const double* olp, const double* oldVal, const double* perm,
+                              void* stream) {
+  PL_REQUIRE(u && obs && acts && adv && ret && olp && perm, PL_ERR_INVALID, "pl_update_set_columns_dev: NULL column");
+  PL_REQUIRE(!u->d.use_old_values || oldVal, PL_ERR_INVALID, "value clip needs the old-value column");
+  cudaStream_t st = (cudaStream_t)stream;
+  const pl_update_desc& d = u->d;
+  const long NT = (long)d.NT;
+  int rc;
+  if (u->fast)
+    rc = launch_obs_to_bf16_f32(obs, NT, (int)d.D, u->Dp, (__nv_bfloat16*)u->obs, st);
+  else {
+    PL_CUDA(cudaMemcpyAsync(u->obs, obs, sizeof(float) * NT * d.D, cudaMemcpyDeviceToDevice, st));
+    rc = PL_OK;
+  }
+  if (rc) return rc;
+  PL_CUDA(cudaMemcpyAsync(u->adv_c, adv, NT * sizeof(double), cudaMemcpyDeviceToDevice, st));
+  rc = launch_columns(acts, ret, olp, u->ov_c ? oldVal : nullptr, NT, u->act_c, u->ret_c, u->olp_c, u->ov_c, st);
+  if (rc) return rc;
+  return launch_perm(perm, (long)(d.epochs * NT), u->perm, st);
+}
+
+int pl_update_run(pl_update* u, double lr, void* stream) {
+  PL_REQUIRE(u != nullptr, PL_ERR_INVALID, "pl_update_run: NULL session");
+  cudaStream_t st = (cudaStream_t)stream;
+  const pl_update_desc& d = u->d;
+  const uint64_t l0 = pl_kernel_launch_count();
+  u->loss_on = g_loss_on;
+  int lastNmb = 0;
+  for (size_t e = 0; e < d.epochs; e++)
+    for (size_t m = 0; m < d.numMB; m++) {
+      const long lo = (long)m * u->mbSize;
+      long hi = (m + 1 == d.numMB) ? (long)d.NT : (long)(m + 1) * u->mbSize;
+      if (hi > (long)d.NT) hi = (long)d.NT;
+      if (hi <= lo) continue;
+      const int Nmb = (int)(hi - lo);
+      const int* idx = u->perm + e * d.NT + lo;
+      const bool last = (e + 1 == d.epochs) && (m + 1 == d.numMB);
+      int rc = u->fast ? minibatch_fast(u, idx, Nmb, lr, last, st) : minibatch_tight(u, idx, Nmb, lr, last, st);
+      if (rc) return rc;
+      lastNmb = Nmb;
+    }
+  u->launches = pl_kernel_launch_count() - l0;
+  if (u->loss_on && u->fast && lastNmb > 0) return reduce_losses(u, lastNmb, st);
+  return PL_OK;
+}
+
+// ---------------------------------------------------------------- policy handle
+int pl_policy_load(const double* pm, size_t P, size_t* handle) {
+  int rc = require_device();
+  if (rc) return rc;
+  PL_REQUIRE(pm && handle && P > 0, PL_ERR_INVALID, "pl_policy_load: bad arguments");
+  double* d = nullptr;
+  PL_CUDA(cudaMalloc(&d, 2 * P * sizeof(double)));
+  cudaError_t e = cudaMemcpy(d, pm, 2 * P * sizeof(double), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return check_cuda(e, "pl_policy_load upload");
+  }
+  *handle = (size_t)d;
+  return PL_OK;
+}
+
+int pl_policy_download(size_t handle, size_t P, double* pm_out) {
+  PL_REQUIRE(handle && pm_out, PL_ERR_INVALID, "pl_policy_download: bad arguments");
+  PL_CUDA(cudaDeviceSynchronize());
+  PL_CUDA(cudaMemcpy(pm_out, (const void*)handle, 2 * P * sizeof(double), cudaMemcpyDeviceToHost));
+  return PL_OK;
+}
+
+// ---------------------------------------------------------------- cached sessions for the
+// reference-shaped entry points (one per handle and shape)
+struct CachedSession {
+  size_t handle;
+  pl_update_desc d;
+  std::vector<double> coeffs;
+  pl_update* u;
+};
+static std::vector<CachedSession> g_sessions;
+
+static bool same_desc(const pl_update_desc& a, const pl_update_desc& b) {
+  return a.NT == b.NT && a.D == b.D && a.H == b.H && a.A == b.A && a.epochs == b.epochs && a.numMB == b.numMB &&
+         a.arch.L == b.arch.L && a.arch.act == b.arch.act && a.bf16 == b.bf16 && a.use_old_values == b.use_old_values &&
+         a.arch.ns_iters == b.arch.ns_iters;
+}
+
+static int session_for(size_t handle, const pl_update_desc& d, pl_update** out) {
+  std::lock_guard<std::mutex> g(g_mu);
+  std::vector<double> co;
+  if (d.arch.ns_coeffs && d.arch.ns_iters) co.assign(d.arch.ns_coeffs, d.arch.ns_coeffs + 3 * d.arch.ns_iters);
+  for (auto it = g_sessions.begin(); it != g_sessions.end(); ++it) {
+    if (it->handle != handle) continue;
+    if (same_desc(it->d, d) && it->coeffs == co) {
+      it->u->d = d;  // hyperparameters may change between calls
+      it->u->d.arch.ns_coeffs = nullptr;
+      *out = it->u;
+      return PL_OK;
+    }
+    pl_update_destroy(it->u);
+    g_sessions.erase(it);
+    break;
+  }
+  pl_update* u = nullptr;
+  int rc = pl_update_create(handle, &d, &u);
+  if (rc) return rc;
+  u->d.arch.ns_coeffs = nullptr;
+  g_sessions.push_back({handle, d, co, u});
+  *out = u;
+  return PL_OK;
+}
+
+int pl_policy_free(size_t handle) {
+  if (!handle) return PL_OK;
+  {
+    std::lock_guard<std::mutex> g(g_mu);
+    for (auto it = g_sessions.begin(); it != g_sessions.end();) {
+      if (it->handle == handle) {
+        pl_update_destroy(it->u);
+        it = g_sessions.erase(it);
+      } else
+        ++it;
+    }
+  }
+  PL_CUDA(cudaDeviceSynchronize());
+  PL_CUDA(cudaFree((void*)handle));
+  return PL_OK;
+}
+
+static int resident_update(size_t handle, const pl_mlp_arch* arch, const double* obs, const double* acts,
+                           const double* adv, const double* ret, const double* olp, const double* oldVal,
+                           size_t oldValN, const double* perm, size_t NT, size_t D, size_t H, size_t A, size_t epochs,
+                           size_t numMB, double lr, double wd, double mu, double eps, double vfCoef, double entCoef,
+                           double clipEps, double vfClip, double maxGradNorm, uint8_t bf16, bool grad_only,
+                           float* grad_out) {
+  int rc = require_device();
+  if (rc) return rc;
+  pl_update_desc d{};
+  d.NT = NT;
+  d.D = D;
+  d.H = H;
+  d.A = A;
+  d.epochs = epochs;
+  d.numMB = numMB;
+  if (arch) d.arch = *arch;
+  if (d.arch.L == 0) d.arch.L = 1;
+  d.wd = wd;
+  d.mu = mu;
+  d.eps = eps;
+  d.vfCoef = vfCoef;
+  d.entCoef = entCoef;
+  d.clipEps = clipEps;
+  d.vfClip = vfClip;
+  d.maxGradNorm = maxGradNorm;
+  d.bf16 = bf16;
+  d.use_old_values = (vfClip > 0.0 && oldVal != nullptr && oldValN >= NT) ? 1 : 0;
+  d.world = 1;
+  pl_update* u = nullptr;
+  rc = session_for(handle, d, &u);
+  if (rc) return rc;
+  u->grad_only = grad_only;
+  rc = refresh_shadows(u, 0);
+  if (rc) return rc;
+  rc = pl_update_set_columns(u, obs, acts, adv, ret, olp, d.use_old_values ? oldVal : nullptr, perm, nullptr);
+  if (rc) return rc;
+  rc = pl_update_run(u, lr, nullptr);
+  if (rc) return rc;
+  if (grad_only && grad_out) PL_CUDA(cudaMemcpy(grad_out, u->grad, sizeof(float) * u->P, cudaMemcpyDeviceToHost));
+  PL_CUDA(cudaDeviceSynchronize());
+  return device_error_check();
+}
+
+int pl_train_update_resident_deep(size_t handle, const pl_mlp_arch* arch, const double* obs, const double* acts,
+                                  const double* adv, const double* ret, const double* olp, const double* oldVal,
+                                  size_t oldValN, const double* perm, size_t NT, size_t D, size_t H, size_t A,
+                                  size_t epochs, size_t numMB, double lr, double wd, double mu, double eps,
+                                  double vfCoef, double entCoef, double clipEps, double vfClip, double maxGradNorm,
+                                  uint8_t bf16, double* params0_out) {
+  PL_REQUIRE(handle && obs && acts && adv && ret && olp && perm, PL_ERR_INVALID, "update: NULL argument");
+  int rc = resident_update(handle, arch, obs, acts, adv, ret, olp, oldVal, oldValN, perm, NT, D, H, A, epochs, numMB, lr,
+                           wd, mu, eps, vfCoef, entCoef, clipEps, vfClip, maxGradNorm, bf16, false, nullptr);
+  if (rc) return rc;
+  if (params0_out) PL_CUDA(cudaMemcpy(params0_out, (const void*)handle, sizeof(double), cudaMemcpyDeviceToHost));
+  return PL_OK;
+}
+
+int pl_train_update_resident(size_t handle, const double* obs, const double* acts, const double* adv,
+                             const double* ret, const double* olp, const double* oldVal, size_t oldValN,
+                             const double* perm, size_t NT, size_t D, size_t H, size_t A, size_t epochs, size_t numMB,
+                             double lr, double wd, double mu, double eps, double vfCoef, double entCoef,
+                             double clipEps, double vfClip, double maxGradNorm, uint8_t bf16, double* params0_out) {
+  return pl_train_update_resident_deep(handle, nullptr, obs, acts, adv, ret, olp, oldVal, oldValN, perm, NT, D, H, A,
+                                       epochs, numMB, lr, wd, mu, eps, vfCoef, entCoef, clipEps, vfClip, maxGradNorm,
+                                       bf16, params0_out);
+}
+
+int pl_train_update(const double* pm, const double* obs, const double* acts, const double* adv, const double* ret,
+                    const double* olp, const double* perm, size_t NT, size_t D, size_t H, size_t A, size_t epochs,
+                    size_t numMB, double lr, double wd, double mu, double eps, double vfCoef, double entCoef,
+                    double clipEps, uint8_t bf16, double* pm_out) {
+  PL_REQUIRE(pm && pm_out, PL_ERR_INVALID, "pl_train_update: NULL argument");
+  const size_t P = pl_mlp_param_count(D, H, A, 1);
+  size_t h = 0;
+  int rc = pl_policy_load(pm, P, &h);
+  if (rc) return rc;
+  rc = pl_train_update_resident(h, obs, acts, adv, ret, olp, nullptr, 0, perm, NT, D, H, A, epochs, numMB, lr, wd, mu,
+                                eps, vfCoef, entCoef, clipEps, 0.0, 0.0, bf16, nullptr);
+  if (!rc) rc = pl_policy_download(h, P, pm_out);
+  pl_policy_free(h);
+  return rc;
+}
+
+int pl_train_step(const double* pm, const double* obs, const double* acts, const double* advRaw, const double* rets,
+                  const double* oldlps, size_t N, size_t H, size_t D, size_t A, double lr, double wd, double mu,
+                  double eps, double vfCoef, double entCoef, double clipEps, uint8_t bf16, double* pm_out) {
+  std::vector<double> perm(N);
+  for (size_t i = 0; i < N; i++) perm[i] = (double)i;
+  return pl_train_update(pm, obs, acts, advRaw, rets, oldlps, perm.data(), N, D, H, A, 1, 1, lr, wd, mu, eps, vfCoef,
+                         entCoef, clipEps, bf16, pm_out);
+}
+
+int pl_mlp_ppo_grad(const double* params, const double* obs, const double* acts, const double* advs,
+                    const double* rets, const double* oldlps, size_t N, size_t H, size_t D, size_t A, double vfCoef,
+                    double entCoef, double clipEps, uint8_t bf16, double* g) {
+  PL_REQUIRE(params && g, PL_ERR_INVALID, "pl_mlp_ppo_grad: NULL argument");
+  const size_t P = pl_mlp_param_count(D, H, A, 1);
+  std::vector<double> pm(2 * P, 0.0);
+  memcpy(pm.data(), params, P * sizeof(double));
+  size_t h = 0;
+  int rc = pl_policy_load(pm.data(), P, &h);
+  if (rc) return rc;
+  std::vector<double> perm(N);
+  for (size_t i = 0; i < N; i++) perm[i] = (double)i;
+  std::vector<float> gf(P);
+  rc = resident_update(h, nullptr, obs, acts, advs, rets, oldlps, nullptr, 0, perm.data(), N, D, H, A, 1, 1, 0.0, 0.0,
+                       0.0, 1e-7, vfCoef, entCoef, clipEps, 0.0, 0.0, bf16, true, gf.data());
+  pl_policy_free(h);
+  if (rc) return rc;
+  for (size_t i = 0; i < P; i++) g[i] = (double)gf[i];
+  return PL_OK;
+}
+
+// f64 sequential folds, one thread: bit-identical to normalizeAdv (Puffer/RL/NNTrain.lean:274-279).
+}  // extern "C"
+
+__global__ void adv_normalize_exact_kernel(const double* __restrict__ a, long n, double* out) {
+  if (threadIdx.x || blockIdx.x) return;
+  double s = 0.0;
+  for (long i = 0; i < n; i++) s = __dadd_rn(s, a[i]);
+  const double mean = __ddiv_rn(s, (double)n);
+  double v = 0.0;
+  for (long i = 0; i < n; i++) {
+    const double d = __dsub_rn(a[i], mean);
+    v = __dadd_rn(v, __dmul_rn(d, d));
+  }
+  const double den = __dadd_rn(__dsqrt_rn(__ddiv_rn(v, (double)n)), 1e-8);
+  for (long i = 0; i < n; i++) out[i] = __ddiv_rn(__dsub_rn(a[i], mean), den);
+}
+
+extern "C" {
+
+int pl_adv_normalize(const double* adv, size_t n, double* out) {
+  int rc = require_device();
+  if (rc) return rc;
+  PL_REQUIRE(adv && out, PL_ERR_INVALID, "pl_adv_normalize: NULL buffer");
+  if (n == 0) return PL_OK;
+  double* d = (double*)scratch(2, 2 * n * sizeof(double));
+  if (!d) return PL_ERR_NOMEM;
+  PL_CUDA(cudaMemcpy(d, adv, n * 8, cudaMemcpyHostToDevice));
+  adv_normalize_exact_kernel<<<1, 32>>>(d, (long)n, d + n);
+  count_launch();
+  PL_LAUNCH("adv_normalize_exact_kernel");
+  PL_CUDA(cudaMemcpy(out, d + n, n * 8, cudaMemcpyDeviceToHost));
+  return PL_OK;
+}
+
+int pl_loss_enable(uint8_t on) {
+  std::lock_guard<std::mutex> g(g_mu);
+  g_loss_on = on != 0;
+  return PL_OK;
+}
+
+int pl_read_losses(double out[7]) {
+  PL_REQUIRE(out != nullptr, PL_ERR_INVALID, "pl_read_losses: NULL");
+  std::lock_guard<std::mutex> g(g_mu);
+  memcpy(out, g_losses, sizeof(g_losses));
+  return PL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,200 @@
+"""GPU parity of the PPO+Muon update through the C-ABI, against the reference's own outputs and the
+pinned oracle.
+
+Reference bars (Exe/Puffer.lean verify modes): gradient f32 < 1e-4 abs and bf16 < 0.2 abs
+(verify-ppo-grad-gpu); whole step f32 < 1e-3 and bf16 < 0.2 (verify-train-step-gpu). The spec's
+bf16 bar for GEMM and Newton-Schulz outputs: 2e-2 relative Frobenius norm.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import pufferlean_b200 as plb  # noqa: E402
+from oracle import kat  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def load(name):
+    return np.load(os.path.join(GOLD, name + ".npz"))
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def rel(a, b):
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+# ------------------------------------------------------------------------------------------------ KATs
+def test_adv_normalize_kat_bit_exact():
+    f = load("advnorm")
+    assert np.array_equal(plb.cuda_adv_normalize(f["adv"], f["adv"].size), f["out"])
+
+
+@pytest.mark.parametrize("bf16,tol", [(0, 1e-4), (1, 0.2)])
+def test_ppo_grad_kat(bf16, tol):
+    f = load("ppo_grad")
+    N, D, H, A, vf, ent, clip, _ = f["meta"]
+    N, D, H, A = int(N), int(D), int(H), int(A)
+    g = plb.cuda_mlp_ppo_grad(f["params"], f["obs"], f["acts"], f["advs"], f["rets"], f["olps"], N, H, D, A, vf, ent,
+                              clip, bf16)
+    d = np.abs(g - f["g_blas"]).max()
+    assert d < tol, d
+    if bf16:
+        assert rel(g, f["g_blas"]) < 2e-2
+
+
+@pytest.mark.parametrize("bf16,tol", [(0, 1e-3), (1, 0.2)])
+def test_train_step_kat(bf16, tol):
+    f = load("train_step")
+    N, D, H, A, vf, ent, clip, lr, wd, mu, eps = f["meta"]
+    N, D, H, A = int(N), int(D), int(H), int(A)
+    pm = np.concatenate([f["params"], f["mom"]])
+    out = plb.cuda_train_step(pm, f["obs"], f["acts"], f["adv"], f["rets"], f["olps"], N, H, D, A, lr, wd, mu, eps, vf,
+                              ent, clip, bf16)
+    P = f["params"].size
+    assert np.abs(out[:P] - f["out"][:P]).max() < tol
+    assert np.abs(out[P:] - f["out"][P:]).max() < tol
+
+
+@pytest.mark.parametrize("bf16,tol", [(0, 1e-3), (1, 0.2)])
+def test_train_update_kat(bf16, tol):
+    f = load("train_update")
+    NT, D, H, A, E, MB, vf, ent, clip, lr, wd, mu, eps, seed = f["meta"]
+    NT, D, H, A, E, MB = (int(x) for x in (NT, D, H, A, E, MB))
+    perm = plb.shuffle_perm(NT, E, int(seed))
+    assert np.array_equal(perm, f["perm"])
+    out = plb.cuda_train_update(f["pm0"], f["obs"], f["acts"], f["adv"], f["rets"], f["olps"], perm, NT, D, H, A, E,
+                                MB, lr, wd, mu, eps, vf, ent, clip, bf16)
+    assert np.abs(out - f["out"]).max() < tol
+
+
+# ------------------------------------------------------------------------------------------------ deep / resident
+def _problem(NT, D, H, A, L, seed, act):
+    g = np.random.default_rng(seed)
+    P = O.param_count(D, H, A, L)
+    pm = np.zeros(2 * P)
+    # Xavier-like init per layer; biases small
+    off = 0
+    for l in range(L + 1):
+        fin = D if l == 0 else H
+        fout = A + 1 if l == L else H
+        lim = np.sqrt(6.0 / (fin + fout))
+        pm[off:off + fout * fin] = g.uniform(-lim, lim, fout * fin)
+        off += fout * fin
+        pm[off:off + fout] = g.uniform(-0.05, 0.05, fout)
+        off += fout
+    obs = g.standard_normal(NT * D)
+    acts = g.integers(0, A, NT).astype(float)
+    adv = g.standard_normal(NT)
+    ret = g.standard_normal(NT)
+    olp = np.log(np.full(NT, 1.0 / A)) + g.normal(0, 0.1, NT)
+    ov = ret + g.normal(0, 0.3, NT)
+    return P, pm, obs, acts, adv, ret, olp, ov
+
+
+def _run_resident(pm, P, arch, obs, acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, lr, vfclip, maxgn, bf16):
+    h = plb.policy_load(pm, P)
+    try:
+        out0 = np.zeros(1)
+        a = _Arch(arch[0], arch[1], None, 0)
+        L = plb.lib()
+        L.pl_train_update_resident_deep.argtypes = ([C.c_size_t, C.POINTER(_Arch)] + [C.POINTER(C.c_double)] * 6 +
+                                                    [C.c_size_t, C.POINTER(C.c_double)] + [C.c_size_t] * 6 +
+                                                    [C.c_double] * 9 + [C.c_uint8, C.POINTER(C.c_double)])
+        arrs = [np.ascontiguousarray(x, dtype=np.float64) for x in (obs, acts, adv, ret, olp, ov, perm)]
+        p = [x.ctypes.data_as(C.POINTER(C.c_double)) for x in arrs]
+        rc = L.pl_train_update_resident_deep(h, C.byref(a), p[0], p[1], p[2], p[3], p[4], p[5], NT, p[6], NT, D, H, A,
+                                             E, MB, lr, 0.0, 0.95, 1e-7, 0.5, 0.01, 0.2, vfclip, maxgn, bf16,
+                                             out0.ctypes.data_as(C.POINTER(C.c_double)))
+        assert rc == 0, L.pl_last_error()
+        return plb.policy_download(h, P), out0[0]
+    finally:
+        plb.policy_free(h)
+
+
+class _Arch(C.Structure):
+    _fields_ = [("L", C.c_size_t), ("act", C.c_int), ("ns_coeffs", C.POINTER(C.c_double)), ("ns_iters", C.c_size_t)]
+
+
+@pytest.mark.parametrize("L,act", [(1, 0), (3, 1)])
+def test_deep_update_tight_tier_vs_oracle(L, act):
+    NT, D, H, A, E, MB = 1024, 20, 96, 7, 2, 4
+    P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, A, L, 11 + L, act)
+    perm = O.shuffle_perm(NT, E, 77)
+    ref = O.train_update(pm, obs, acts, adv, ret, olp, perm, NT, D, H, A, E, MB, 0.02, 0.0, 0.95, 1e-7, 0.5, 0.01, 0.2,
+                         L=L, act=act, ov=ov, vfClip=0.2, maxGradNorm=0.5)
+    got, p0 = _run_resident(pm, P, (L, act), obs, acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, 0.02, 0.2, 0.5, 0)
+    assert p0 == got[0]
+    assert np.abs(got - ref).max() < 1e-3
+    assert rel(got[:P] - pm[:P], ref[:P] - pm[:P]) < 1e-3
+
+
+@pytest.mark.parametrize("L,act", [(1, 0), (3, 1)])
+def test_deep_update_bf16_tier_vs_oracle(L, act):
+    NT, D, H, A, E, MB = 2048, 20, 192, 7, 1, 2
+    P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, A, L, 21 + L, act)
+    perm = O.shuffle_perm(NT, E, 78)
+    ref = O.train_update(pm, obs, acts, adv, ret, olp, perm, NT, D, H, A, E, MB, 0.02, 0.0, 0.95, 1e-7, 0.5, 0.01, 0.2,
+                         L=L, act=act, ov=ov, vfClip=0.2, maxGradNorm=0.5)
+    got, _ = _run_resident(pm, P, (L, act), obs, acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, 0.02, 0.2, 0.5, 1)
+    # The reference's own bf16 bar for a whole step is 0.2 absolute (verify-train-step-gpu).
+    assert np.abs(got - ref).max() < 0.2
+    # Parameter deltas: bf16 rounding of the activations and gradients (about 2e-2 relative on each
+    # gradient block) passes through Newton-Schulz, which maps every singular direction of the
+    # momentum to unit scale and so amplifies the rounding in the weak directions; the deltas agree
+    # to 15% relative Frobenius (and in direction to cosine > 0.99).
+    dg, dr = got[:P] - pm[:P], ref[:P] - pm[:P]
+    assert rel(dg, dr) < 0.15
+    assert float(dg @ dr / (np.linalg.norm(dg) * np.linalg.norm(dr))) > 0.99
+    # momentum is a linear function of the gradients: the gradient bar applies
+    assert rel(got[P:], ref[P:]) < 3e-2
+
+
+def test_bf16_update_is_deterministic():
+    NT, D, H, A, E, MB, L = 4096, 33, 128, 5, 2, 4, 2
+    P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, A, L, 5, 1)
+    perm = O.shuffle_perm(NT, E, 79)
+    a, _ = _run_resident(pm, P, (L, 1), obs, acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, 0.02, 0.2, 0.5, 1)
+    b, _ = _run_resident(pm, P, (L, 1), obs, acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, 0.02, 0.2, 0.5, 1)
+    assert np.array_equal(a, b)
+
+
+def test_bf16_gradient_matches_oracle():
+    NT, D, H, A = 3000, 50, 256, 9
+    P, pm, obs, acts, adv, ret, olp, _ = _problem(NT, D, H, A, 1, 8, 0)
+    g = plb.cuda_mlp_ppo_grad(pm[:P], obs, acts, adv, ret, olp, NT, H, D, A, 0.5, 0.01, 0.2, 1)
+    ref, _, _ = O.mlp_ppo_grad(pm[:P], obs, acts, adv, ret, olp, NT, D, H, A)
+    # per parameter block. Each block is the end of a chain of bf16 GEMMs (forward, data gradient,
+    # weight gradient) whose operands are rounded to bf16 (8-bit significand): 3e-2 relative. The
+    # single-GEMM bar of 2e-2 is checked in test_gpu_kernels.py.
+    offs = [0, H * D, H * D + H, H * D + H + (A + 1) * H, P]
+    for a, b in zip(offs[:-1], offs[1:]):
+        assert rel(g[a:b], ref[a:b]) < 3e-2, (a, b, rel(g[a:b], ref[a:b]))
+
+
+# ------------------------------------------------------------------------------------------------ batched NS
+@pytest.mark.parametrize("batch,rows,cols", [(4, 128, 256), (3, 512, 512), (2, 256, 128), (5, 64, 64)])
+def test_batched_newton_schulz(batch, rows, cols):
+    torch.manual_seed(rows + cols)
+    X = torch.randn(batch, rows, cols, device="cuda").to(torch.bfloat16)
+    Xin = X.double().cpu().numpy()
+    co = np.ascontiguousarray(O.QUINTIC_COEFFS)
+    rc = plb.lib().pl_ns_batched_bf16_dev(X.data_ptr(), batch, rows, cols, 1e-7,
+                                          co.ctypes.data_as(C.POINTER(C.c_double)), 5, None)
+    assert rc == 0, plb.lib().pl_last_error()
+    torch.cuda.synchronize()
+    got = X.double().cpu().numpy()
+    for b in range(batch):
+        ref = O.newton_schulz(Xin[b].ravel(), rows, cols, 1e-7, co).reshape(rows, cols)
+        assert rel(got[b], ref) < 2e-2, (b, rel(got[b], ref))
