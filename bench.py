@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""PPO+Muon update throughput on B200 (the north-star metric of BASELINE.json).
+
+One step = one whole PPO+Muon update of the C5 large-MLP policy: the
+advantage scan over the rollout columns, then 4 epochs x 16 minibatches of 262,144 rows, each
+minibatch = gather, forward (obs 1024 -> 5 x 2048 GELU -> 64 logits + value), PPO objective
+gradient, backward, grad-norm clip, Muon (Newton-Schulz) on every weight matrix. Inputs are seeded
+synthetic rollout columns already resident in HBM (obs 17 GB fp32 > L2, so no flush is needed).
+
+value    samples/s = world x N_envs x horizon / device time of one update (max over ranks)
+e2e      the same update through the reference-facing C-ABI call (pl_train_update_resident) from
+         pinned HOST buffers, with the host GAE and shuffle, H2D copies and the params[0] read-back
+         inside the timed region
+roofline the tcgen05 GEMM kernels of the step (forward, PPO head, data and weight gradients),
+         timed live with CUDA events on the launch stream; achieved = algorithmic flops / time
+cpu_baseline  the CPU restatement (oracle/cpu_port.py, numpy f64 on all host cores) on a bounded
+         sample, scaled to one update
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c5|c1]
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "PPO+Muon update samples/sec at 1/2/4/8 B200; NS/GEMM % tensor peak"
+QUINTIC = [(3.4445, -4.7750, 2.0315)] * 5
+
+WORKLOADS = {
+    # 65536 envs x 64, obs 1024, 4 hidden 2048 (+ the 1024->2048 encoder), 64 actions
+    "c5": dict(name="C5 large-MLP PPO+Muon update (configs[4])", N=65536, T=64, D=1024, H=2048, L=5, A=64, act=1,
+               Nmb=262144, epochs=4, obs="normal", rew="normal", done=0.01, lr=0.02),
+    # CartPole-shaped, 1024 envs x 64, obs 4, hidden 128, 2 actions
+    "c1": dict(name="C1 CartPole-shaped PPO+Muon update (configs[0])", N=1024, T=64, D=4, H=128, L=1, A=2, act=1,
+               Nmb=16384, epochs=4, obs="normal", rew="bern", done=0.01, lr=0.02),
+}
+
+
+class Arch(C.Structure):
+    _fields_ = [("L", C.c_size_t), ("act", C.c_int), ("ns_coeffs", C.POINTER(C.c_double)), ("ns_iters", C.c_size_t)]
+
+
+class Desc(C.Structure):
+    _fields_ = [("NT", C.c_size_t), ("D", C.c_size_t), ("H", C.c_size_t), ("A", C.c_size_t), ("epochs", C.c_size_t),
+                ("numMB", C.c_size_t), ("arch", Arch), ("wd", C.c_double), ("mu", C.c_double), ("eps", C.c_double),
+                ("vfCoef", C.c_double), ("entCoef", C.c_double), ("clipEps", C.c_double), ("vfClip", C.c_double),
+                ("maxGradNorm", C.c_double), ("bf16", C.c_uint8), ("use_old_values", C.c_uint8), ("rank", C.c_int),
+                ("world", C.c_int), ("comm", C.c_void_p)]
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops_sustained", d.get("bf16_tflops")), d.get("hbm_gbs"), "measured"
+    return 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def xavier_pm(D, H, A, L, seed):
+    g = np.random.default_rng(seed)
+    P = H * D + H + (L - 1) * (H * H + H) + (A + 1) * H + A + 1
+    pm = np.zeros(2 * P)
+    off = 0
+    for l in range(L + 1):
+        fin = D if l == 0 else H
+        fout = A + 1 if l == L else H
+        lim = np.sqrt(6.0 / (fin + fout))
+        pm[off:off + fout * fin] = g.uniform(-lim, lim, fout * fin)
+        off += fout * fin + fout
+    return P, pm
+
+
+def check(rc, L):
+    if rc != 0:
+        raise RuntimeError(L.pl_last_error().decode())
+
+
+def run_ours(args, wl, rank, world, local_rank):
+    import torch
+
+    import pufferlean_b200 as plb
+
+    torch.cuda.set_device(local_rank)
+    L = plb.lib()
+    check(L.pl_set_device(local_rank), L)
+    dp = C.POINTER(C.c_double)
+    vp = C.c_void_p
+    L.pl_update_create.argtypes = [C.c_size_t, C.POINTER(Desc), C.POINTER(vp)]
+    L.pl_update_set_columns_dev.argtypes = [vp] * 9
+    L.pl_update_set_advantages_dev.argtypes = [vp] * 5 + [C.c_size_t] + [C.c_double] * 4 + [vp]
+    L.pl_update_run.argtypes = [vp, C.c_double, vp]
+    L.pl_update_profile.argtypes = [vp, C.c_int]
+    L.pl_update_profile_read.argtypes = [vp, dp, dp, dp]
+    L.pl_update_destroy.argtypes = [vp]
+
+    N, T, D, H, Lh, A = wl["N"], wl["T"], wl["D"], wl["H"], wl["L"], wl["A"]
+    NT = N * T
+    Nmb, E = wl["Nmb"], wl["epochs"]
+    numMB = NT // Nmb
+    seed = 1234 + rank
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    obs = torch.randn(NT, D, device="cuda", generator=gen) if wl["obs"] == "normal" else \
+        torch.rand(NT, D, device="cuda", generator=gen)
+    acts = torch.randint(0, A, (NT,), device="cuda", generator=gen).double()
+    rew = torch.randn(NT, device="cuda", generator=gen) if wl["rew"] == "normal" else \
+        (torch.rand(NT, device="cuda", generator=gen) < 0.5).float()
+    val = torch.randn(NT, device="cuda", generator=gen)
+    term = (torch.rand(NT, device="cuda", generator=gen) < wl["done"]).float()
+    olp = (torch.full((NT,), float(np.log(1.0 / A)), device="cuda", dtype=torch.float64) +
+           0.05 * torch.randn(NT, device="cuda", generator=gen, dtype=torch.float64))
+    perm_h = plb.shuffle_perm(NT, E, 0xC5 + rank)
+    perm = torch.from_numpy(perm_h).cuda()
+    P, pm = xavier_pm(D, H, A, Lh, 42)
+    handle = plb.policy_load(pm, P)
+    co = np.ascontiguousarray(np.array(QUINTIC, dtype=np.float64))
+    desc = Desc(NT=NT, D=D, H=H, A=A, epochs=E, numMB=numMB, arch=Arch(Lh, wl["act"], co.ctypes.data_as(dp), 5),
+                wd=0.0, mu=0.95, eps=1e-12, vfCoef=0.5, entCoef=0.01, clipEps=0.2, vfClip=0.2, maxGradNorm=1.5,
+                bf16=1, use_old_values=1, rank=rank, world=world, comm=None)
+    u = vp()
+    check(L.pl_update_create(handle, C.byref(desc), C.byref(u)), L)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step():
+        check(L.pl_update_set_columns_dev(u, obs.data_ptr(), acts.data_ptr(), None, None, olp.data_ptr(), None,
+                                          perm.data_ptr(), stream), L)
+        check(L.pl_update_set_advantages_dev(u, rew.data_ptr(), val.data_ptr(), term.data_ptr(), None, T, 0.995, 0.90,
+                                             1.0, 1.0, stream), L)
+        check(L.pl_update_run(u, wl["lr"], stream), L)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    check(L.pl_update_profile(u, 1), L)
+    l0 = L.pl_kernel_launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            step()
+        ev1.record()
+        torch.cuda.synchronize()
+    launches = L.pl_kernel_launch_count() - l0
+    ms = ev0.elapsed_time(ev1) / args.steps
+    pms, pfl, pln = (C.c_double * 8)(), (C.c_double * 8)(), (C.c_double * 8)()
+    check(L.pl_update_profile_read(u, pms, pfl, pln), L)
+    check(L.pl_update_profile(u, 0), L)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * NT / (ms / 1e3)
+    peak_tf, peak_hbm, peak_kind = peaks()
+    gemm_ms = sum(pms[i] for i in range(4))
+    gemm_fl = sum(pfl[i] for i in range(4))
+    gemm_n = sum(pln[i] for i in range(4))
+    achieved = gemm_fl / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
+    ns_tf = pfl[4] / (pms[4] / 1e3) / 1e12 if pms[4] > 0 else 0.0
+    prof = {k: {"ms_per_step": pms[i] / args.steps, "tflops": (pfl[i] / (pms[i] / 1e3) / 1e12) if pms[i] > 0 and
+                pfl[i] > 0 else None, "launches_per_step": pln[i] / args.steps}
+            for i, k in enumerate(["fwd_gemm", "ppo_head_gemm", "dgrad_gemm", "wgrad_gemm", "newton_schulz",
+                                   "gather_stats", "optimizer_elementwise"])}
+    L.pl_update_destroy(u)
+    del obs
+    torch.cuda.empty_cache()
+
+    out = {
+        "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; obs/rewards N(0,1), dones Bern(0.01))",
+        "config": {"workload": wl["name"], "N_envs_per_gpu": N, "horizon": T, "obs_dim": D, "hidden": H,
+                   "hidden_layers": Lh, "actions": A, "activation": "gelu" if wl["act"] else "relu",
+                   "minibatch_rows_per_gpu": Nmb, "epochs": E, "minibatches_per_epoch": numMB,
+                   "ns_coeffs": "quintic (3.4445,-4.7750,2.0315) x5", "params": P,
+                   "l2": "no flush: the obs column alone (fp32 %.1f GB) exceeds L2" % (NT * D * 4 / 1e9),
+                   "parallelism": f"dp{world}"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": achieved / peak_tf if peak_tf else None, "traffic": None,
+                     "kernel": "tc_gemm_kernel (all forward/PPO-head/dgrad/wgrad launches of the step)",
+                     "launches_per_step": gemm_n / args.steps, "peak_kind": peak_kind + " (bf16 sustained)"},
+        "newton_schulz": {"tflops": ns_tf, "frac": ns_tf / peak_tf if peak_tf else None,
+                          "ms_per_step": pms[4] / args.steps},
+        "profile": prof,
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+    }
+    return out, dict(handle=handle, P=P, pm=pm)
+
+
+def run_e2e(args, wl, state, rank, world, local_rank):
+    """The same update through pl_train_update_resident with pinned host buffers: host GAE and
+    shuffle (the reference's per-update host C), H2D of the f64 columns, the update, the 8-byte
+    params[0] read-back."""
+    import torch
+
+    import pufferlean_b200 as plb
+
+    N, T, D, H, Lh, A = wl["N"], wl["T"], wl["D"], wl["H"], wl["L"], wl["A"]
+    NT = N * T
+    E, Nmb = wl["epochs"], wl["Nmb"]
+    numMB = NT // Nmb
+    gen = torch.Generator(device="cuda").manual_seed(99 + rank)
+    obs_h = torch.empty(NT * D, dtype=torch.float64, pin_memory=True)
+    chunk = 1 << 27
+    for o in range(0, NT * D, chunk):
+        n = min(chunk, NT * D - o)
+        obs_h[o:o + n].copy_(torch.randn(n, device="cuda", generator=gen, dtype=torch.float64))
+    g = np.random.default_rng(7 + rank)
+    cols = {k: torch.empty(NT, dtype=torch.float64, pin_memory=True) for k in ("acts", "olp", "val", "rew", "term")}
+    cols["acts"].copy_(torch.from_numpy(g.integers(0, A, NT).astype(np.float64)))
+    cols["olp"].copy_(torch.from_numpy(np.log(1.0 / A) + 0.05 * g.standard_normal(NT)))
+    cols["val"].copy_(torch.from_numpy(g.standard_normal(NT)))
+    cols["rew"].copy_(torch.from_numpy(g.standard_normal(NT)))
+    cols["term"].copy_(torch.from_numpy((g.random(NT) < wl["done"]).astype(np.float64)))
+    gae = torch.empty(2 * NT, dtype=torch.float64, pin_memory=True)
+    perm = torch.empty(E * NT, dtype=torch.float64, pin_memory=True)
+    L = plb.lib()
+    dp = C.POINTER(C.c_double)
+    L.pl_train_update_resident_deep.argtypes = ([C.c_size_t, C.POINTER(Arch)] + [dp] * 6 + [C.c_size_t, dp] +
+                                                [C.c_size_t] * 6 + [C.c_double] * 9 + [C.c_uint8, dp])
+    L.pl_gae_soa.argtypes = [dp] * 3 + [C.c_size_t, C.c_size_t, C.c_double, C.c_double, dp]
+    L.pl_shuffle_perm.argtypes = [C.c_size_t, C.c_size_t, C.c_uint64, dp]
+    co = np.ascontiguousarray(np.array(QUINTIC, dtype=np.float64))
+    arch = Arch(Lh, wl["act"], co.ctypes.data_as(dp), 5)
+    out0 = np.zeros(1)
+
+    def P_(t):
+        return C.cast(t.data_ptr(), dp)
+
+    def step(i):
+        check(L.pl_gae_soa(P_(cols["val"]), P_(cols["rew"]), P_(cols["term"]), N, T, 0.995, 0.90, P_(gae)), L)
+        check(L.pl_shuffle_perm(NT, E, 0xE2E + i, P_(perm)), L)
+        adv = C.cast(gae.data_ptr(), dp)
+        ret = C.cast(gae.data_ptr() + 8 * NT, dp)
+        check(L.pl_train_update_resident_deep(state["handle"], C.byref(arch), P_(obs_h), P_(cols["acts"]), adv, ret,
+                                              P_(cols["olp"]), P_(cols["val"]), NT, P_(perm), NT, D, H, A, E, numMB,
+                                              wl["lr"], 0.0, 0.95, 1e-12, 0.5, 0.01, 0.2, 0.2, 1.5, 1,
+                                              out0.ctypes.data_as(dp)), L)
+
+    step(0)
+    if world > 1:
+        torch.distributed.barrier()
+    k = max(1, min(args.steps, 3))
+    t0 = time.perf_counter()
+    for i in range(k):
+        step(i + 1)
+    dt = (time.perf_counter() - t0) / k
+    if world > 1:
+        t = torch.tensor([dt], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        dt = float(t.item())
+    h2d = 8 * (NT * D + 5 * NT + E * NT)
+    return {"value": world * NT / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 8,
+            "steps": k, "s_per_step": dt, "path": "pl_train_update_resident_deep (C-ABI, pinned host f64 columns, "
+                                                  "host GAE + shuffle in the timed region)"}
+
+
+def cpu_baseline(wl, steps=1):
+    from oracle import cpu_port
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        threads = max([x.get("num_threads", 1) for x in threadpool_info()] or [os.cpu_count()])
+    except Exception:
+        threads = os.cpu_count()
+    vals, det = [], None
+    for s in range(steps):
+        per_update, det = cpu_port.timed_update_sample(wl["D"], wl["H"], wl["A"], wl["L"], wl["act"], wl["Nmb"],
+                                                       wl["epochs"], wl["N"] * wl["T"] // wl["Nmb"],
+                                                       QUINTIC, rows=4096, seed=s)
+        vals.append(wl["N"] * wl["T"] / per_update)
+    return {"value": float(np.mean(vals)), "unit": "samples/s", "cores": int(threads), "kind": "port",
+            "sample": ("numpy f64 restatement of the reference's pufferblas CPU update (oracle/cpu_port.py): one "
+                       f"minibatch gradient on {det['rows']} rows ({det['t_rows']:.2f} s) + one whole-network Muon "
+                       f"step ({det['t_muon']:.2f} s), scaled to {wl['epochs']} epochs x "
+                       f"{wl['N'] * wl['T'] // wl['Nmb']} minibatches of {wl['Nmb']} rows")}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c5")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        base = cpu_baseline(wl, steps=max(1, min(args.steps, 2)))
+        line = {"metric": METRIC, "value": base["value"], "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f64", "data": "synthetic (seeded)", "impl": "reference",
+                "config": {"workload": wl["name"], "parallelism": "host cores"},
+                "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    if world > 1:
+        import datetime
+
+        import torch
+
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    out, state = run_ours(args, wl, rank, world, local_rank)
+    if not args.no_e2e:
+        out["e2e"] = run_e2e(args, wl, state, rank, world, local_rank)
+    import pufferlean_b200 as plb
+
+    plb.policy_free(state["handle"])
+    if rank == 0:
+        if not args.no_cpu and world == 1:
+            out["cpu_baseline"] = cpu_baseline(wl)
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch
+
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -90,8 +90,8 @@ int pl_muon_stepmat(const double* W, const double* G, const double* M, size_t ro
 
 /* Newton-Schulz orthogonalisation of a batch of equally shaped bf16 matrices on the device
  * (tensor cores, fp32 accumulate): X[b] <- NS(X[b] / (||X[b]||_F + eps)) with an iters x 3
- * coefficient table (host, row-major). X is batch x rows x cols, updated in place. The batch may be
- * the local shard of a larger set (see pl_ns_batched_sharded_dev). */
+ * coefficient table (host, row-major). X is batch x rows x cols, updated in place; rows and cols are
+ * multiples of 8. Tall matrices are orthogonalised through their transpose. */
 int pl_ns_batched_bf16_dev(void* X, size_t batch, size_t rows, size_t cols, double eps, const double* coeffs,
                            size_t iters, void* stream);
 
@@ -186,14 +186,29 @@ int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, c
                           const double* ret, const double* olp, const double* oldVal, const double* perm,
                           void* stream);
 /* Device columns: obs as fp32 [NT x D], the rest f64 [NT] (perm f64 [epochs*NT]). Copied into the
- * session's own layout on the device. */
+ * session's own layout on the device. adv, ret and oldVal may be NULL when
+ * pl_update_set_advantages_dev computes them on the device. */
 int pl_update_set_columns_dev(pl_update* u, const float* obs, const double* acts, const double* adv,
                               const double* ret, const double* olp, const double* oldVal, const double* perm,
                               void* stream);
+/* Advantages on the device for the session's columns: the fp32 V-trace scan in its vector form
+ * over N = NT/T segments of horizon T (row e*T + t, the layout of ffi/pufferffi.c:946), with
+ * importance ratios `imp` (NULL = all ones, which is truncated GAE), then ret = adv + val. The old
+ * value column of the value clip is set to val. rew/val/term/imp are device fp32 [NT]. */
+int pl_update_set_advantages_dev(pl_update* u, const float* rew, const float* val, const float* term,
+                                 const float* imp, size_t T, double gamma, double lam, double rhoClip, double cClip,
+                                 void* stream);
 /* Runs every epoch x minibatch of one update at learning rate lr on `stream`. */
 int pl_update_run(pl_update* u, double lr, void* stream);
 /* Kernels launched by the last pl_update_run (this library's own kernels). */
 uint64_t pl_update_last_launches(const pl_update* u);
+/* Per-class kernel timing with CUDA events on the launch stream while `on` (classes: 0 forward GEMM,
+ * 1 PPO-head GEMM, 2 data-gradient GEMM, 3 weight-gradient GEMM incl. split-K sum, 4 Newton-Schulz
+ * GEMMs, 5 gather/statistics, 6 optimizer elementwise and reductions). pl_update_profile_read
+ * synchronizes and returns, per class, total milliseconds, algorithmic flops and launches since
+ * profiling was switched on. */
+int pl_update_profile(pl_update* u, int on);
+int pl_update_profile_read(pl_update* u, double ms[8], double flops[8], double launches[8]);
 int pl_update_destroy(pl_update* u);
 
 /* ------------------------------------------------------------------ dashboard losses ----------- */

@@ -50,7 +50,7 @@ __global__ void columns_kernel(const double* __restrict__ act, const double* __r
                                float* ret_f, float* olp_f, float* ov_f) {
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < NT; i += (long)gridDim.x * blockDim.x) {
     act_i[i] = (int)act[i];
-    ret_f[i] = (float)ret[i];
+    if (ret) ret_f[i] = (float)ret[i];
     olp_f[i] = (float)olp[i];
     if (ov) ov_f[i] = (float)ov[i];
   }

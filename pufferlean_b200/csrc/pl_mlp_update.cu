@@ -74,6 +74,15 @@ struct pl_update {
   uint64_t launches = 0;
   bool grad_only = false;  // pl_mlp_ppo_grad: no normalisation, no optimizer step
   bool alloc_failed = false;
+  float* adv_f = nullptr;  // fp32 scan output of pl_update_set_advantages_dev
+  // profiling: CUDA events around each launch group, per class
+  bool prof = false;
+  std::vector<cudaEvent_t> ev;
+  size_t ev_used = 0;
+  std::vector<int> ev_cls;
+  double prof_flops[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  double prof_launch[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  double prof_ms[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   bool loss_on = false;
   double losses[7] = {0, 0, 0, 0, 0, 0, 0};
 };
@@ -102,6 +111,45 @@ static void free_all(pl_update* u) {
   for (void* p : u->allocs) cudaFree(p);
   u->allocs.clear();
 }
+
+// Profiling spans: an event before and after each launch group, recorded on the launch stream.
+struct Span {
+  pl_update* u;
+  int cls;
+  cudaStream_t st;
+  double flops;
+  Span(pl_update* u_, int c, cudaStream_t s, double f) : u(u_), cls(c), st(s), flops(f) {
+    if (!u->prof) return;
+    while (u->ev.size() < u->ev_used + 2) {
+      cudaEvent_t e;
+      cudaEventCreate(&e);
+      u->ev.push_back(e);
+    }
+    cudaEventRecord(u->ev[u->ev_used], st);
+  }
+  ~Span() {
+    if (!u->prof) return;
+    cudaEventRecord(u->ev[u->ev_used + 1], st);
+    u->ev_cls.push_back(cls);
+    u->ev_used += 2;
+    u->prof_flops[cls] += flops;
+    u->prof_launch[cls] += 1;
+  }
+};
+
+static void prof_collect(pl_update* u) {
+  if (u->ev_used == 0) return;
+  cudaDeviceSynchronize();
+  for (size_t i = 0; i < u->ev_cls.size(); i++) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, u->ev[2 * i], u->ev[2 * i + 1]);
+    u->prof_ms[u->ev_cls[i]] += ms;
+  }
+  u->ev_cls.clear();
+  u->ev_used = 0;
+}
+
+static inline double gf(long M, long N, long K) { return 2.0 * (double)M * (double)N * (double)K; }
 
 static int build_layout(pl_update* u) {
   const pl_update_desc& d = u->d;
@@ -296,8 +344,12 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
   const int L = u->L;
   const int act = d.arch.act;
   const int mt = (int)ceil_div(Nmb, 128);
-  int rc = launch_gather(true, idx, Nmb, u->obs, u->Dp, u->X, u->act_c, u->adv_c, u->ret_c, u->olp_c, u->ov_c,
-                         u->mb_act, u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st);
+  int rc;
+  {
+    Span sp(u, 5, st, 0);
+    rc = launch_gather(true, idx, Nmb, u->obs, u->Dp, u->X, u->act_c, u->adv_c, u->ret_c, u->olp_c, u->ov_c, u->mb_act,
+                       u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st);
+  }
   if (rc) return rc;
   // ---- forward
   const void* hin = u->X;
@@ -315,7 +367,10 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
     e.out2 = u->Zs[l];
     e.ldo2 = u->Hp;
     e.act = act;
-    rc = gemm_launch(pick_bn(ly.out), EPI_FWD, false, false, A, B, Nmb, ly.out, ly.in, 1, e, st);
+    {
+      Span sp(u, 0, st, gf(Nmb, ly.out, ly.in));
+      rc = gemm_launch(pick_bn(ly.out), EPI_FWD, false, false, A, B, Nmb, ly.out, ly.in, 1, e, st);
+    }
     if (rc) return rc;
     hin = u->Hs[l];
     ldin = u->Hp;
@@ -345,9 +400,15 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
     e.clip = (float)d.clipEps;
     e.vfclip = (float)d.vfClip;
     e.loss_part = last && u->loss_on ? u->loss_part : nullptr;
-    rc = gemm_launch(u->Op, EPI_PPO, false, false, A, B, Nmb, hd.out, hd.in, 1, e, st);
+    {
+      Span sp(u, 1, st, gf(Nmb, hd.out, hd.in));
+      rc = gemm_launch(u->Op, EPI_PPO, false, false, A, B, Nmb, hd.out, hd.in, 1, e, st);
+    }
     if (rc) return rc;
-    rc = launch_colsum_reduce(u->colpart, mt, u->Op, hd.out, u->grad + hd.ob, st);
+    {
+      Span sp(u, 6, st, 0);
+      rc = launch_colsum_reduce(u->colpart, mt, u->Op, hd.out, u->grad + hd.ob, st);
+    }
     if (rc) return rc;
   }
   // ---- backward
@@ -358,7 +419,10 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
     const Layer& ly = u->layers[l];
     const void* hprev = l == 0 ? u->X : u->Hs[l - 1];
     const long ldprev = l == 0 ? u->Dp : u->Hp;
-    rc = wgrad_fast(u, dcur, ldd, ly.out, hprev, ldprev, ly.in, Nmb, u->grad + ly.oW, st);
+    {
+      Span sp(u, 3, st, gf(ly.out, ly.in, Nmb));
+      rc = wgrad_fast(u, dcur, ldd, ly.out, hprev, ldprev, ly.in, Nmb, u->grad + ly.oW, st);
+    }
     if (rc) return rc;
     if (l == 0) break;
     // dZ_{l-1} = (dcur W_l) * act'(Z_{l-1})
@@ -375,9 +439,15 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
     e.act = act;
     e.colsum = u->colpart;
     e.ld_colsum = u->Hp;
-    rc = gemm_launch(pick_bn(lp.out), EPI_DGRAD, false, true, A, B, Nmb, lp.out, ly.out, 1, e, st);
+    {
+      Span sp(u, 2, st, gf(Nmb, lp.out, ly.out));
+      rc = gemm_launch(pick_bn(lp.out), EPI_DGRAD, false, true, A, B, Nmb, lp.out, ly.out, 1, e, st);
+    }
     if (rc) return rc;
-    rc = launch_colsum_reduce(u->colpart, mt, u->Hp, lp.out, u->grad + lp.ob, st);
+    {
+      Span sp(u, 6, st, 0);
+      rc = launch_colsum_reduce(u->colpart, mt, u->Hp, lp.out, u->grad + lp.ob, st);
+    }
     if (rc) return rc;
     dcur = u->dZ[dsel];
     ldd = u->Hp;
@@ -385,26 +455,38 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
   }
   if (u->grad_only) return PL_OK;
   // ---- clip to the mean gradient, then Muon on every layer
-  rc = launch_gradnorm(u->grad, (long)u->P, 1.0 / (double)Nmb, d.maxGradNorm, u->gn_part, u->cc, st);
+  {
+    Span sp(u, 6, st, 0);
+    rc = launch_gradnorm(u->grad, (long)u->P, 1.0 / (double)Nmb, d.maxGradNorm, u->gn_part, u->cc, st);
+  }
   if (rc) return rc;
   for (size_t l = 0; l < u->layers.size(); l++) {
     const Layer& ly = u->layers[l];
     const long n = (long)ly.out * ly.in;
     int nparts = 0;
-    rc = launch_nesterov(u->grad + ly.oW, u->cc, u->pm + u->P + ly.oW, u->ns.U, d.mu, n, u->ns.part, &nparts, st);
-    if (rc) return rc;
     const int m = std::min(ly.out, ly.in), nn = std::max(ly.out, ly.in);
-    rc = launch_ns_input(u->ns.U, u->ns.part, nparts, ly.out, ly.in, d.eps, u->ns.X0, u->ns.ldx, st);
+    {
+      Span sp(u, 6, st, 0);
+      rc = launch_nesterov(u->grad + ly.oW, u->cc, u->pm + u->P + ly.oW, u->ns.U, d.mu, n, u->ns.part, &nparts, st);
+      if (!rc) rc = launch_ns_input(u->ns.U, u->ns.part, nparts, ly.out, ly.in, d.eps, u->ns.X0, u->ns.ldx, st);
+    }
     if (rc) return rc;
-    rc = ns_run(m, nn, u->coeffs.data(), u->iters, u->ns, u->ns.X0, u->ns.ldx, u->ns.Xf, u->ns.ldx, st);
+    {
+      // algorithmic Newton-Schulz flops per step: 4 m^2 n + 2 m^3
+      Span sp(u, 4, st, (double)u->iters * (4.0 * m * (double)m * nn + 2.0 * m * (double)m * m));
+      rc = ns_run(m, nn, u->coeffs.data(), u->iters, u->ns, u->ns.X0, u->ns.ldx, u->ns.Xf, u->ns.ldx, st);
+    }
     if (rc) return rc;
     const double r = (double)ly.out / (double)ly.in;
     const double scale = sqrt(r > 1.0 ? r : 1.0);
-    rc = launch_ns_finalize(u->ns.Xf, u->ns.ldx, ly.out, ly.in, 1.0 - lr * d.wd, lr * scale, u->pm + ly.oW, u->Wb[l],
-                            ly.in_p, st);
-    if (rc) return rc;
-    rc = launch_stepvec_fast(u->grad + ly.ob, u->cc, u->pm + ly.ob, u->pm + u->P + ly.ob, u->bf[l], lr, d.wd, d.mu,
-                             ly.out, st);
+    {
+      Span sp(u, 6, st, 0);
+      rc = launch_ns_finalize(u->ns.Xf, u->ns.ldx, ly.out, ly.in, 1.0 - lr * d.wd, lr * scale, u->pm + ly.oW, u->Wb[l],
+                              ly.in_p, st);
+      if (!rc)
+        rc = launch_stepvec_fast(u->grad + ly.ob, u->cc, u->pm + ly.ob, u->pm + u->P + ly.ob, u->bf[l], lr, d.wd, d.mu,
+                                 ly.out, st);
+    }
     if (rc) return rc;
   }
   return PL_OK;
@@ -556,6 +638,7 @@ int pl_update_create(size_t handle, const pl_update_desc* desc, pl_update** out)
 int pl_update_destroy(pl_update* u) {
   if (!u) return PL_OK;
   cudaDeviceSynchronize();
+  for (cudaEvent_t e : u->ev) cudaEventDestroy(e);
   free_all(u);
   delete u;
   return PL_OK;
@@ -618,8 +701,8 @@ int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, c
 int pl_update_set_columns_dev(pl_update* u, const float* obs, const double* acts, const double* adv,
                               const double* ret, const double* olp, const double* oldVal, const double* perm,
                               void* stream) {
-  PL_REQUIRE(u && obs && acts && adv && ret && olp && perm, PL_ERR_INVALID, "pl_update_set_columns_dev: NULL column");
-  PL_REQUIRE(!u->d.use_old_values || oldVal, PL_ERR_INVALID, "value clip needs the old-value column");
+  // adv / ret / oldVal may be NULL when pl_update_set_advantages_dev provides them
+  PL_REQUIRE(u && obs && acts && olp && perm, PL_ERR_INVALID, "pl_update_set_columns_dev: NULL column");
   cudaStream_t st = (cudaStream_t)stream;
   const pl_update_desc& d = u->d;
   const long NT = (long)d.NT;
@@ -631,10 +714,63 @@ int pl_update_set_columns_dev(pl_update* u, const float* obs, const double* acts
     rc = PL_OK;
   }
   if (rc) return rc;
-  PL_CUDA(cudaMemcpyAsync(u->adv_c, adv, NT * sizeof(double), cudaMemcpyDeviceToDevice, st));
-  rc = launch_columns(acts, ret, olp, u->ov_c ? oldVal : nullptr, NT, u->act_c, u->ret_c, u->olp_c, u->ov_c, st);
+  if (adv) PL_CUDA(cudaMemcpyAsync(u->adv_c, adv, NT * sizeof(double), cudaMemcpyDeviceToDevice, st));
+  rc = launch_columns(acts, ret, olp, (u->ov_c && oldVal) ? oldVal : nullptr, NT, u->act_c, ret ? u->ret_c : nullptr,
+                      u->olp_c, (u->ov_c && oldVal) ? u->ov_c : nullptr, st);
   if (rc) return rc;
   return launch_perm(perm, (long)(d.epochs * NT), u->perm, st);
+}
+
+__global__ void adv_columns_kernel(const float* __restrict__ a, const float* __restrict__ val, long n, double* adv_c,
+                                   float* ret_c, float* ov_c) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float ad = a[i];
+    adv_c[i] = (double)ad;
+    ret_c[i] = ad + val[i];
+    if (ov_c) ov_c[i] = val[i];
+  }
+}
+
+int pl_update_set_advantages_dev(pl_update* u, const float* rew, const float* val, const float* term,
+                                 const float* imp, size_t T, double gamma, double lam, double rhoClip, double cClip,
+                                 void* stream) {
+  PL_REQUIRE(u && rew && val && term && T > 0, PL_ERR_INVALID, "pl_update_set_advantages_dev: bad arguments");
+  PL_REQUIRE(u->d.NT % T == 0, PL_ERR_INVALID, "NT=%zu is not a whole number of T=%zu segments", u->d.NT, T);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!u->adv_f) {
+    u->adv_f = dalloc<float>(u, u->d.NT);
+    if (!u->adv_f) return PL_ERR_NOMEM;
+  }
+  int rc = pl_vtrace_f32_dev(rew, val, term, imp, nullptr, u->d.NT / T, T, gamma, lam, rhoClip, cClip, u->adv_f,
+                             nullptr, stream);
+  if (rc) return rc;
+  adv_columns_kernel<<<(unsigned)std::min<long>(ceil_div((long)u->d.NT, 256), 148 * 16), 256, 0, st>>>(
+      u->adv_f, val, (long)u->d.NT, u->adv_c, u->ret_c, u->ov_c);
+  count_launch();
+  PL_LAUNCH("adv_columns_kernel");
+  return PL_OK;
+}
+
+int pl_update_profile(pl_update* u, int on) {
+  PL_REQUIRE(u != nullptr, PL_ERR_INVALID, "pl_update_profile: NULL session");
+  if (on && !u->prof) {
+    for (int i = 0; i < 8; i++) u->prof_ms[i] = u->prof_flops[i] = u->prof_launch[i] = 0;
+    u->ev_used = 0;
+    u->ev_cls.clear();
+  }
+  u->prof = on != 0;
+  return PL_OK;
+}
+
+int pl_update_profile_read(pl_update* u, double ms[8], double flops[8], double launches[8]) {
+  PL_REQUIRE(u != nullptr, PL_ERR_INVALID, "pl_update_profile_read: NULL session");
+  prof_collect(u);
+  for (int i = 0; i < 8; i++) {
+    if (ms) ms[i] = u->prof_ms[i];
+    if (flops) flops[i] = u->prof_flops[i];
+    if (launches) launches[i] = u->prof_launch[i];
+  }
+  return PL_OK;
 }
 
 int pl_update_run(pl_update* u, double lr, void* stream) {
@@ -658,6 +794,7 @@ int pl_update_run(pl_update* u, double lr, void* stream) {
       lastNmb = Nmb;
     }
   u->launches = pl_kernel_launch_count() - l0;
+  if (u->prof && u->ev_used > 16384) prof_collect(u);
   if (u->loss_on && u->fast && lastNmb > 0) return reduce_losses(u, lastNmb, st);
   return PL_OK;
 }

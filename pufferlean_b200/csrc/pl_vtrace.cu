@@ -106,13 +106,18 @@ __global__ void __launch_bounds__(256) vtrace_f32_kernel(const float* __restrict
   // vector loads need every row start aligned to the run width
   constexpr uintptr_t ALIGN = EPL >= 4 ? 16 : EPL * 4;
   const uintptr_t orp = (uintptr_t)(rew + base) | (uintptr_t)(val + base) | (uintptr_t)(term + base) |
-                        (uintptr_t)(imp + base) | (uintptr_t)(adv + base);
+                        (imp ? (uintptr_t)(imp + base) : 0) | (uintptr_t)(adv + base);
   const bool vec = EPL > 1 && (T % EPL) == 0 && (orp % ALIGN) == 0;
   float r[EPL], v[EPL], d[EPL], im[EPL];
   load_run<EPL>(rew + base, t0, T, vec, r, 0.f);
   load_run<EPL>(val + base, t0, T, vec, v, 0.f);
   load_run<EPL>(term + base, t0, T, vec, d, 0.f);
-  load_run<EPL>(imp + base, t0, T, vec, im, 1.f);
+  if (imp)
+    load_run<EPL>(imp + base, t0, T, vec, im, 1.f);
+  else {
+#pragma unroll
+    for (int e = 0; e < EPL; e++) im[e] = 1.f;  // no importance ratios: rho = c = min(1, clip)
+  }
   // value one step past this lane's run: the first value of the next lane (or the bootstrap)
   float v_after = __shfl_down_sync(0xffffffffu, v[0], 1);
   const float boot = MINGRU ? bootv[seg] : 0.f;
