@@ -70,7 +70,14 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
   if (!ep.err) ep.err = device_error_word();
   int splits = ep.k_splits > 1 ? ep.k_splits : 1;
   PL_REQUIRE(splits == 1 || batch == 1, PL_ERR_INVALID, "split-K and batching are exclusive");
-  dim3 grid((unsigned)ceil_div(N, bn), (unsigned)ceil_div(M, 128), (unsigned)(splits > 1 ? splits : batch));
+  ep.nbatch = batch;
+  static int num_sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && num_sms[dev] == 0) cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const long tiles = ceil_div(N, bn) * ceil_div(M, 128) * (long)(splits > 1 ? splits : batch);
+  const int sms = (dev >= 0 && dev < 64 && num_sms[dev] > 0) ? num_sms[dev] : 148;
+  dim3 grid((unsigned)(tiles < sms ? tiles : sms), 1, 1);
   static std::mutex mu;
   {
     std::lock_guard<std::mutex> g(mu);
@@ -84,7 +91,7 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
       if (nconf < 256) configured[nconf++] = (void*)k;
     }
   }
-  k<<<grid, 192, smem, st>>>(ma, mb, M, N, K, ep);
+  k<<<grid, 320, smem, st>>>(ma, mb, M, N, K, ep);
   count_launch();
   PL_LAUNCH("tc_gemm_kernel");
   return PL_OK;

@@ -7,10 +7,11 @@
 // forward (X W^T), data-gradient (dZ W) and weight-gradient (dZ^T X) products of every layer all
 // read the tensors where they already lie, with no transposed copies.
 //
-// CTA = 6 warps: warp 0 issues TMA tile loads into a STAGES-deep shared-memory ring, warp 1 owns
-// the TMEM accumulator (128 lanes x BN fp32 columns) and issues tcgen05.mma from one thread,
-// warps 2-5 drain TMEM through tcgen05.ld and run the epilogue. Tiles are BM=128 x BN, BK=64
-// (one 128-byte swizzle atom of bf16 per row).
+// CTA = 10 warps: warp 0 issues TMA tile loads into a STAGES-deep shared-memory ring, warp 1 owns
+// two TMEM accumulators (128 lanes x BN fp32 columns each) and issues tcgen05.mma from one thread,
+// warps 2-9 drain TMEM through tcgen05.ld and run the epilogue while the next tile accumulates.
+// Tiles are BM=128 x BN, BK=64 (one 128-byte swizzle atom of bf16 per row); the kernel is
+// persistent, one CTA per SM.
 #pragma once
 #include "pl_common.cuh"
 #include "pl_tc.cuh"
@@ -52,7 +53,8 @@ struct EpiArgs {
   float* newval;
   float* loss_part;  // [gridDim.y][8] optional per-CTA loss partials
   unsigned* err;
-  int k_splits;      // >1: blockIdx.z is a split-K slice; else blockIdx.z is the batch index
+  int k_splits;      // >1: the z index of a tile is its split-K slice; else its batch index
+  int nbatch;        // number of stacked matrices (z extent when k_splits <= 1)
 };
 
 __device__ __forceinline__ float act_fwd(float z, int act) {
@@ -136,6 +138,25 @@ __device__ __forceinline__ void load_row16_bf16(const __nv_bfloat16* p, float (&
   }
 }
 
+// tanh on the SFU (tanh.approx.f32, relative error about 2^-11): used where the result is
+// rounded to bf16 anyway.
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float act_fwd_fast(float z, int act) {
+  if (act == 0) return z > 0.f ? z : 0.f;
+  const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
+  return 0.5f * z * (1.f + tanh_fast(u));
+}
+__device__ __forceinline__ float act_grad_fast(float z, int act) {
+  if (act == 0) return z > 0.f ? 1.f : 0.f;
+  const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
+  const float t = tanh_fast(u);
+  return 0.5f * (1.f + t) + 0.5f * z * (1.f - t * t) * 0.7978845608028654f * (1.f + 3.f * 0.044715f * z * z);
+}
+
 template <int BN>
 struct GemmSmem {
   static constexpr int BM = 128, BK = 64;
@@ -147,50 +168,282 @@ struct GemmSmem {
   static constexpr uint32_t TOTAL = 1024 + STAGES * STAGE_BYTES + 256 + 4 * BN * 4 + 4 * 32 * 8 * 4;
 };
 
+// Tile coordinates of linear tile t: n fastest (consecutive tiles share the A row-panel, which
+// the CTAs running at the same time then read once from HBM), then m, then the z slice.
+struct TileIdx {
+  int n, m, z;
+};
+__device__ __forceinline__ TileIdx tile_of(int t, int num_n, int num_m) {
+  TileIdx r;
+  r.n = t % num_n;
+  const int q = t / num_n;
+  r.m = q % num_m;
+  r.z = q / num_m;
+  return r;
+}
+
+// Epilogue of one 128 x BN accumulator tile held in TMEM columns [tcol, tcol + BN).
+// Runs on the 4 epilogue warps; warp `sub` owns TMEM lanes / tile rows [32 sub, 32 sub + 32).
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row, int m_tile, int n_tile, int bz,
+                                              int batch, bool have_acc, int sub, int half, int lane, float* red,
+                                              float* rowscr) {
+  constexpr int BM = 128;
+  const int row = m_tile * BM + sub * 32 + lane;
+  const bool row_ok = row < ep.out_rows;
+  if constexpr (EPI == EPI_PPO) {
+    // one thread = one minibatch row; BN covers every logit + the value column. The second group of
+    // epilogue warps has no columns of its own here and only joins the barriers.
+    if (half) {
+      tc::named_bar_sync(1, 256);
+      tc::named_bar_sync(1, 256);
+      return;
+    }
+    const int A = ep.A;
+    int a = 0;
+    float adv = 0.f, ret = 0.f, olp = 0.f, vold = 0.f;
+    if (row_ok) {
+      a = ep.act_idx[row];
+      adv = ep.adv[row];
+      if (ep.adv_ms) adv = (float)(((double)adv - ep.adv_ms[0]) / ep.adv_ms[1]);
+      ret = ep.ret[row];
+      olp = ep.olp[row];
+      if (ep.ov) vold = ep.ov[row];
+    }
+    float mx = -INFINITY, se = 0.f, xa = 0.f, vnew = 0.f;
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t r[16];
+      tc::tmem_ld16(t_row + c0, r);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const int k = c0 + j;
+        const float x = (have_acc ? __uint_as_float(r[j]) : 0.f) + (k < ep.out_cols ? ep.bias[k] : 0.f);
+        if (k < A) {
+          if (x > mx) {
+            se = se * expf(mx - x) + 1.f;
+            mx = x;
+          } else {
+            se += expf(x - mx);
+          }
+          if (k == a) xa = x;
+        }
+        if (k == A) vnew = x;
+      }
+    }
+    const float lse = mx + logf(se);
+    float pout = 0.f;
+    for (int c0 = 0; c0 < BN && c0 < A; c0 += 16) {
+      uint32_t r[16];
+      tc::tmem_ld16(t_row + c0, r);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const int k = c0 + j;
+        if (k < A) {
+          const float x = (have_acc ? __uint_as_float(r[j]) : 0.f) + ep.bias[k];
+          pout += expf(x - lse) * x;
+        }
+      }
+    }
+    const float logpA = xa - lse;
+    const float ratio = expf(logpA - olp);
+    const float lo = 1.f - ep.clip, hi = 1.f + ep.clip;
+    const float ratioC = ratio < lo ? lo : (ratio > hi ? hi : ratio);
+    const float surr1 = adv * ratio, surr2 = adv * ratioC;
+    float dPol;
+    if (surr1 <= surr2)
+      dPol = adv * ratio;
+    else
+      dPol = adv * ((lo < ratio && ratio < hi) ? 1.f : 0.f) * ratio;
+    float dv = vnew - ret;
+    if (ep.ov && ep.vfclip > 0.f) {
+      const float dd = vnew - vold;
+      const float vc = vold + (dd < -ep.vfclip ? -ep.vfclip : (dd > ep.vfclip ? ep.vfclip : dd));
+      const float du = (vnew - ret) * (vnew - ret), cc = (vc - ret) * (vc - ret);
+      if (!(du >= cc) && !(dd > -ep.vfclip && dd < ep.vfclip)) dv = 0.f;
+    }
+    const float dval = -ep.vf * dv;
+    if (row_ok) {
+      if (ep.newlp) ep.newlp[row] = logpA;
+      if (ep.newval) ep.newval[row] = vnew;
+    }
+    if (ep.loss_part) {
+      // per-row loss terms (PufferLib decomposition): pg loss, value loss, entropy, kl, old kl, clipfrac
+      const float ent_row = lse - pout;
+      float lt[6] = {row_ok ? -fminf(surr1, surr2) : 0.f, row_ok ? 0.5f * (vnew - ret) * (vnew - ret) : 0.f,
+                     row_ok ? ent_row : 0.f, row_ok ? (ratio - 1.f) - logf(ratio) : 0.f,
+                     row_ok ? -logf(ratio) : 0.f, row_ok ? (fabsf(ratio - 1.f) > ep.clip ? 1.f : 0.f) : 0.f};
+#pragma unroll
+      for (int q = 0; q < 6; q++) {
+        float v = lt[q];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) rowscr[sub * 8 + q] = v;
+      }
+    }
+    __nv_bfloat16* outp = (__nv_bfloat16*)ep.out + (long)row * ep.ldo;
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t r[16];
+      tc::tmem_ld16(t_row + c0, r);
+      tc::tmem_wait_ld();
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const int k = c0 + j;
+        float d = 0.f;
+        if (row_ok) {
+          if (k < A) {
+            const float x = (have_acc ? __uint_as_float(r[j]) : 0.f) + ep.bias[k];
+            const float p = expf(x - lse);
+            d = dPol * ((k == a ? 1.f : 0.f) - p) + ep.ent * p * (pout - x);
+          } else if (k == A) {
+            d = dval;
+          }
+        }
+        v[j] = d;
+      }
+      if (row_ok) {
+        const int nvalid = min(16, (int)(ep.ldo - c0));
+        if (nvalid > 0) store_row16_bf16(outp + c0, v, nvalid, (ep.ldo % 8) == 0);
+      }
+      const float cs = warp_colsum16(v, lane);
+      if ((lane & 1) == 0) red[sub * BN + c0 + (lane >> 1)] = cs;
+    }
+    tc::named_bar_sync(1, 256);
+    const int t = threadIdx.x - 64;
+    for (int c = t; c < BN; c += 128) {
+      if (c < ep.out_cols)
+        ep.colsum[(long)m_tile * ep.ld_colsum + c] = ((red[c] + red[BN + c]) + red[2 * BN + c]) + red[3 * BN + c];
+    }
+    if (ep.loss_part && t < 6)
+      ep.loss_part[(long)m_tile * 8 + t] = ((rowscr[t] + rowscr[8 + t]) + rowscr[16 + t]) + rowscr[24 + t];
+    tc::named_bar_sync(1, 256);  // scratch is reused by the next tile
+  } else {
+    const int n_base = n_tile * BN;
+    const bool do_colsum = (EPI == EPI_DGRAD) && ep.colsum != nullptr;
+    // this warp's half of the tile's columns, drained 32 at a time (two TMEM loads per wait)
+    const int cb = half * (BN / 2), ce = cb + BN / 2;
+    uint32_t rr[2][16];
+    for (int c32 = cb; c32 < ce; c32 += 32) {
+      if (n_base + c32 >= ep.out_cols) break;  // warp-uniform
+      tc::tmem_ld16(t_row + c32, rr[0]);
+      tc::tmem_ld16(t_row + c32 + 16, rr[1]);
+      tc::tmem_wait_ld();
+#pragma unroll
+     for (int hh = 0; hh < 2; hh++) {
+      const int c0 = c32 + 16 * hh;
+      const int n0 = n_base + c0;
+      if (n0 >= ep.out_cols) break;  // warp-uniform
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) v[j] = have_acc ? __uint_as_float(rr[hh][j]) : 0.f;
+      const int nvalid = min(16, ep.out_cols - n0);
+      if constexpr (EPI == EPI_F32 || EPI == EPI_BF16) {
+        if (row_ok) {
+          float x[16];
+          if (ep.aux) {
+            load_row16_bf16(ep.aux + (long)batch * ep.aux_bstride + (long)row * ep.ld_aux + n0, x, nvalid,
+                            (ep.ld_aux % 8) == 0);
+          }
+#pragma unroll
+          for (int j = 0; j < 16; j++) v[j] = ep.alpha * v[j] + (ep.aux ? ep.beta * x[j] : 0.f);
+          const long off = (long)bz * ep.out_bstride + (long)row * ep.ldo + n0;
+          if constexpr (EPI == EPI_F32)
+            store_row16_f32((float*)ep.out + off, v, nvalid, (ep.ldo % 4) == 0);
+          else
+            store_row16_bf16((__nv_bfloat16*)ep.out + off, v, nvalid, (ep.ldo % 8) == 0);
+        }
+      } else if constexpr (EPI == EPI_FWD) {
+        if (row_ok) {
+          float z[16], h[16];
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            z[j] = v[j] + ((n0 + j) < ep.out_cols ? ep.bias[n0 + j] : 0.f);
+            h[j] = act_fwd_fast(z[j], ep.act);
+          }
+          store_row16_bf16((__nv_bfloat16*)ep.out + (long)row * ep.ldo + n0, h, nvalid, (ep.ldo % 8) == 0);
+          if (ep.out2)
+            store_row16_bf16((__nv_bfloat16*)ep.out2 + (long)row * ep.ldo2 + n0, z, nvalid, (ep.ldo2 % 8) == 0);
+        }
+      } else if constexpr (EPI == EPI_DGRAD) {
+        float x[16];
+        if (row_ok) {
+          load_row16_bf16(ep.aux + (long)row * ep.ld_aux + n0, x, nvalid, (ep.ld_aux % 8) == 0);
+#pragma unroll
+          for (int j = 0; j < 16; j++) v[j] = (j < nvalid) ? v[j] * act_grad_fast(x[j], ep.act) : 0.f;
+          store_row16_bf16((__nv_bfloat16*)ep.out + (long)row * ep.ldo + n0, v, nvalid, (ep.ldo % 8) == 0);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; j++) v[j] = 0.f;
+        }
+        if (do_colsum) {
+          const float cs = warp_colsum16(v, lane);
+          if ((lane & 1) == 0) red[sub * BN + c0 + (lane >> 1)] = cs;
+        }
+      }
+     }
+    }
+    if (do_colsum) {
+      tc::named_bar_sync(1, 256);
+      const int t = threadIdx.x - 64;
+      for (int c = t; c < BN; c += 256) {
+        const int n = n_base + c;
+        if (n < ep.out_cols)
+          ep.colsum[(long)m_tile * ep.ld_colsum + n] = ((red[c] + red[BN + c]) + red[2 * BN + c]) + red[3 * BN + c];
+      }
+      tc::named_bar_sync(1, 256);  // scratch is reused by the next tile
+    }
+  }
+}
+
+// Persistent kernel: gridDim.x CTAs (at most one per SM) walk the linear tile list. The TMEM holds
+// two 128 x BN fp32 accumulators, so the MMA warp fills one while the epilogue warps drain the
+// other: the epilogue of tile j overlaps the main loop of tile j+1.
 template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                    int K, EpiArgs ep) {
   using S = GemmSmem<BN>;
   constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES;
   constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+  constexpr uint32_t TMEM_COLS = 2 * BN;  // 128, 256 or 512: a power of two
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
   uint64_t* full = (uint64_t*)(sB + STAGES * S::B_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = (uint32_t*)(accum + 1);
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   float* red = (float*)(smem + STAGES * S::STAGE_BYTES + 256);  // [4][BN]
-  float* rowscr = red + 4 * BN;                                  // [4 warps][32 lanes][8]
+  float* rowscr = red + 4 * BN;                                  // [4 warps][8]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x, m_tile = blockIdx.y, bz = blockIdx.z;
+  const int num_n = (N + BN - 1) / BN, num_m = (M + BM - 1) / BM;
+  const int num_z = ep.k_splits > 1 ? ep.k_splits : (ep.nbatch > 1 ? ep.nbatch : 1);
+  const int total_tiles = num_n * num_m * num_z;
   const int total_kb = (K + BK - 1) / BK;
-  int kb_begin = 0, kb_end = total_kb, batch = bz;
-  if (ep.k_splits > 1) {
-    int per = (total_kb + ep.k_splits - 1) / ep.k_splits;
-    kb_begin = bz * per;
-    kb_end = min(total_kb, kb_begin + per);
-    batch = 0;
-  }
-  const int num_kb = kb_end > kb_begin ? kb_end - kb_begin : 0;
+  const int per_split = ep.k_splits > 1 ? (total_kb + ep.k_splits - 1) / ep.k_splits : total_kb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
     }
-    tc::mbar_init(accum, 1);
+    for (int b = 0; b < 2; b++) {
+      tc::mbar_init(&acc_full[b], 1);
+      tc::mbar_init(&acc_empty[b], 8);  // one arrival per epilogue warp
+    }
     *abort_flag = 0;
     tc::fence_mbar_init();
     tc::tma_prefetch_desc(&tmA);
     tc::tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, BN);
+    tc::tmem_alloc(tmem_slot, TMEM_COLS);
     tc::tmem_relinquish();
   }
   tc::tc_fence_before();
@@ -198,271 +451,129 @@ __global__ void __launch_bounds__(192, 1)
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  auto kb_range = [&](int z, int& b0, int& b1) {
+    if (ep.k_splits > 1) {
+      b0 = z * per_split;
+      b1 = min(total_kb, b0 + per_split);
+      if (b1 < b0) b1 = b0;
+    } else {
+      b0 = 0;
+      b1 = total_kb;
+    }
+  };
+
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer
-      int issued = 0;
-      for (int i = 0; i < num_kb; i++) {
-        const int s = i % STAGES;
-        if (i >= STAGES) {
-          if (!tc::mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, ep.err, PL_ERR_MBAR_TIMEOUT | 1)) {
+      // ---------------- TMA producer: one ring across all tiles of this CTA
+      long it = 0;
+      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+        const TileIdx ti = tile_of(t, num_n, num_m);
+        const int batch = ep.k_splits > 1 ? 0 : ti.z;
+        int b0, b1;
+        kb_range(ti.z, b0, b1);
+        for (int kb = b0; kb < b1; kb++, it++) {
+          const int s = (int)(it % STAGES);
+          if (it >= STAGES &&
+              !tc::mbar_wait(&empty[s], (uint32_t)(((it / STAGES) - 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 1)) {
             *abort_flag = 1;
             break;
           }
-        }
-        if (*abort_flag) break;
-        const int k0 = (kb_begin + i) * BK;
-        tc::mbar_expect_tx(&full[s], S::STAGE_BYTES);
-        uint8_t* a = sA + s * S::A_BYTES;
-        uint8_t* b = sB + s * S::B_BYTES;
-        if (!A_MN) {
-          tc::tma_load_3d(a, &tmA, &full[s], k0, m_tile * BM, batch);
-        } else {
-          tc::tma_load_3d(a, &tmA, &full[s], m_tile * BM, k0, batch);
-          tc::tma_load_3d(a + 8192, &tmA, &full[s], m_tile * BM + 64, k0, batch);
-        }
-        if (!B_MN) {
-          tc::tma_load_3d(b, &tmB, &full[s], k0, n_tile * BN, batch);
-        } else {
+          const int k0 = kb * BK;
+          tc::mbar_expect_tx(&full[s], S::STAGE_BYTES);
+          uint8_t* a = sA + s * S::A_BYTES;
+          uint8_t* b = sB + s * S::B_BYTES;
+          if (!A_MN) {
+            tc::tma_load_3d(a, &tmA, &full[s], k0, ti.m * BM, batch);
+          } else {
+            tc::tma_load_3d(a, &tmA, &full[s], ti.m * BM, k0, batch);
+            tc::tma_load_3d(a + 8192, &tmA, &full[s], ti.m * BM + 64, k0, batch);
+          }
+          if (!B_MN) {
+            tc::tma_load_3d(b, &tmB, &full[s], k0, ti.n * BN, batch);
+          } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; j++) tc::tma_load_3d(b + j * 8192, &tmB, &full[s], n_tile * BN + 64 * j, k0, batch);
+            for (int j = 0; j < BN / 64; j++)
+              tc::tma_load_3d(b + j * 8192, &tmB, &full[s], ti.n * BN + 64 * j, k0, batch);
+          }
         }
-        issued = i + 1;
       }
-      // Drain: every load this thread issued must have landed before the CTA can retire.
-      for (int i = issued - STAGES > 0 ? issued - STAGES : 0; i < issued; i++)
-        tc::mbar_wait(&full[i % STAGES], (i / STAGES) & 1, ep.err, PL_ERR_MBAR_TIMEOUT | 2);
+      // Drain: every load issued must have landed before the CTA retires.
+      for (long i = it - STAGES > 0 ? it - STAGES : 0; i < it; i++)
+        tc::mbar_wait(&full[i % STAGES], (uint32_t)((i / STAGES) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 2);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer (one thread)
-      bool any = false;
-      for (int i = 0; i < num_kb; i++) {
-        const int s = i % STAGES;
-        if (!tc::mbar_wait(&full[s], (i / STAGES) & 1, ep.err, PL_ERR_MBAR_TIMEOUT | 3)) {
+      long it = 0;
+      int j = 0;
+      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x, j++) {
+        const TileIdx ti = tile_of(t, num_n, num_m);
+        int b0, b1;
+        kb_range(ti.z, b0, b1);
+        const int buf = j & 1;
+        if (j >= 2 &&
+            !tc::mbar_wait(&acc_empty[buf], (uint32_t)(((j >> 1) - 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 3)) {
           *abort_flag = 1;
           break;
         }
         tc::tc_fence_after();
-        const uint32_t a_addr = tc::smem_u32(sA + s * S::A_BYTES);
-        const uint32_t b_addr = tc::smem_u32(sB + s * S::B_BYTES);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+        for (int kb = b0; kb < b1; kb++, it++) {
+          const int s = (int)(it % STAGES);
+          if (!tc::mbar_wait(&full[s], (uint32_t)((it / STAGES) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 4)) {
+            *abort_flag = 1;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t a_addr = tc::smem_u32(sA + s * S::A_BYTES);
+          const uint32_t b_addr = tc::smem_u32(sB + s * S::B_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; kk++) {
-          // K-major: the 16-element K slice is 32 bytes further along the swizzled row;
-          // MN-major: it is 16 rows (2 groups of 8 rows x 128 B) further down.
-          const uint64_t ad = A_MN ? tc::sw128_desc(a_addr + kk * 2048, 8192, 1024) : tc::sw128_desc(a_addr + kk * 32, 16, 1024);
-          const uint64_t bd = B_MN ? tc::sw128_desc(b_addr + kk * 2048, 8192, 1024) : tc::sw128_desc(b_addr + kk * 32, 16, 1024);
-          tc::umma_bf16(tmem_base, ad, bd, IDESC, (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; kk++) {
+            // K-major: the 16-element K slice is 32 bytes further along the swizzled row;
+            // MN-major: it is 16 rows (2 groups of 8 rows x 128 B) further down.
+            const uint64_t ad = A_MN ? tc::sw128_desc(a_addr + kk * 2048, 8192, 1024)
+                                     : tc::sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? tc::sw128_desc(b_addr + kk * 2048, 8192, 1024)
+                                     : tc::sw128_desc(b_addr + kk * 32, 16, 1024);
+            tc::umma_bf16(d_tmem, ad, bd, IDESC, (kb > b0 || kk > 0) ? 1u : 0u);
+          }
+          tc::umma_commit(&empty[s]);
         }
-        tc::umma_commit(&empty[s]);
-        any = true;
+        tc::umma_commit(&acc_full[buf]);  // also when the slice is empty: the epilogue then writes zeros
       }
-      tc::umma_commit(accum);
-      if (any) tc::mbar_wait(accum, 0, ep.err, PL_ERR_MBAR_TIMEOUT | 4);
+      // every MMA this thread issued must complete before TMEM is released
+      if (j > 0) tc::mbar_wait(&acc_full[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 5);
     }
   } else {
-    // ---------------- epilogue warps 2..5
+    // ---------------- epilogue warps 2..9: warp w reads TMEM lanes 32 (w % 4) .. +32 (its rows);
+    // warps w and w + 4 share those rows and split the tile's columns
     const int sub = warp & 3;
-    const int row = m_tile * BM + sub * 32 + lane;
-    const bool row_ok = row < ep.out_rows;
-    const uint32_t t_row = tmem_base + ((uint32_t)(sub * 32) << 16);
-    bool have_acc = tc::mbar_wait(accum, 0, ep.err, PL_ERR_MBAR_TIMEOUT | 5) && num_kb > 0 && !*abort_flag;
-    tc::tc_fence_after();
-
-    if constexpr (EPI == EPI_PPO) {
-      // one thread = one minibatch row; BN covers every logit + the value column
-      const int A = ep.A;
-      int a = 0;
-      float adv = 0.f, ret = 0.f, olp = 0.f, vold = 0.f;
-      if (row_ok) {
-        a = ep.act_idx[row];
-        adv = ep.adv[row];
-        if (ep.adv_ms) adv = (float)(((double)adv - ep.adv_ms[0]) / ep.adv_ms[1]);
-        ret = ep.ret[row];
-        olp = ep.olp[row];
-        if (ep.ov) vold = ep.ov[row];
+    const int half = (warp - 2) >> 2;
+    int j = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, j++) {
+      const TileIdx ti = tile_of(t, num_n, num_m);
+      int b0, b1;
+      kb_range(ti.z, b0, b1);
+      const int buf = j & 1;
+      const bool ok = tc::mbar_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 6);
+      if (!ok || *abort_flag) {
+        *abort_flag = 1;
+        break;
       }
-      float mx = -INFINITY, se = 0.f, xa = 0.f, vnew = 0.f;
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t r[16];
-        tc::tmem_ld16(t_row + c0, r);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const int k = c0 + j;
-          const float x = (have_acc ? __uint_as_float(r[j]) : 0.f) + (k < ep.out_cols ? ep.bias[k] : 0.f);
-          if (k < A) {
-            if (x > mx) {
-              se = se * expf(mx - x) + 1.f;
-              mx = x;
-            } else {
-              se += expf(x - mx);
-            }
-            if (k == a) xa = x;
-          }
-          if (k == A) vnew = x;
-        }
-      }
-      const float lse = mx + logf(se);
-      float pout = 0.f;
-      for (int c0 = 0; c0 < BN && c0 < A; c0 += 16) {
-        uint32_t r[16];
-        tc::tmem_ld16(t_row + c0, r);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const int k = c0 + j;
-          if (k < A) {
-            const float x = (have_acc ? __uint_as_float(r[j]) : 0.f) + ep.bias[k];
-            pout += expf(x - lse) * x;
-          }
-        }
-      }
-      const float logpA = xa - lse;
-      const float ratio = expf(logpA - olp);
-      const float lo = 1.f - ep.clip, hi = 1.f + ep.clip;
-      const float ratioC = ratio < lo ? lo : (ratio > hi ? hi : ratio);
-      const float surr1 = adv * ratio, surr2 = adv * ratioC;
-      float dPol;
-      if (surr1 <= surr2)
-        dPol = adv * ratio;
-      else
-        dPol = adv * ((lo < ratio && ratio < hi) ? 1.f : 0.f) * ratio;
-      float dv = vnew - ret;
-      if (ep.ov && ep.vfclip > 0.f) {
-        const float dd = vnew - vold;
-        const float vc = vold + (dd < -ep.vfclip ? -ep.vfclip : (dd > ep.vfclip ? ep.vfclip : dd));
-        const float du = (vnew - ret) * (vnew - ret), cc = (vc - ret) * (vc - ret);
-        if (!(du >= cc) && !(dd > -ep.vfclip && dd < ep.vfclip)) dv = 0.f;
-      }
-      const float dval = -ep.vf * dv;
-      if (row_ok) {
-        if (ep.newlp) ep.newlp[row] = logpA;
-        if (ep.newval) ep.newval[row] = vnew;
-      }
-      if (ep.loss_part) {
-        // per-row loss terms (PufferLib decomposition): pg loss, value loss, entropy, old-kl proxy, clipfrac
-        float ent_row = lse - pout;
-        float lt[6] = {row_ok ? -fminf(surr1, surr2) : 0.f, row_ok ? 0.5f * (vnew - ret) * (vnew - ret) : 0.f,
-                       row_ok ? ent_row : 0.f, row_ok ? (ratio - 1.f) - logf(ratio) : 0.f,
-                       row_ok ? -logf(ratio) : 0.f, row_ok ? (fabsf(ratio - 1.f) > ep.clip ? 1.f : 0.f) : 0.f};
-#pragma unroll
-        for (int q = 0; q < 6; q++) {
-          float v = lt[q];
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          if (lane == 0) rowscr[sub * 8 + q] = v;
-        }
-      }
-      __nv_bfloat16* outp = (__nv_bfloat16*)ep.out + (long)row * ep.ldo;
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t r[16];
-        tc::tmem_ld16(t_row + c0, r);
-        tc::tmem_wait_ld();
-        float v[16];
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const int k = c0 + j;
-          float d = 0.f;
-          if (row_ok) {
-            if (k < A) {
-              const float x = (have_acc ? __uint_as_float(r[j]) : 0.f) + ep.bias[k];
-              const float p = expf(x - lse);
-              d = dPol * ((k == a ? 1.f : 0.f) - p) + ep.ent * p * (pout - x);
-            } else if (k == A) {
-              d = dval;
-            }
-          }
-          v[j] = d;
-        }
-        if (row_ok) {
-          const int nvalid = min(16, (int)(ep.ldo - c0));
-          if (nvalid > 0) store_row16_bf16(outp + c0, v, nvalid, (ep.ldo % 8) == 0);
-        }
-        const float cs = warp_colsum16(v, lane);
-        if ((lane & 1) == 0) red[sub * BN + c0 + (lane >> 1)] = cs;
-      }
-      tc::named_bar_sync(1, 128);
-      const int t = threadIdx.x - 64;
-      for (int c = t; c < BN; c += 128) {
-        if (c < ep.out_cols)
-          ep.colsum[(long)m_tile * ep.ld_colsum + c] = ((red[c] + red[BN + c]) + red[2 * BN + c]) + red[3 * BN + c];
-      }
-      if (ep.loss_part && t < 6)
-        ep.loss_part[(long)m_tile * 8 + t] = ((rowscr[t] + rowscr[8 + t]) + rowscr[16 + t]) + rowscr[24 + t];
-    } else {
-      const int n_base = n_tile * BN;
-      const bool do_colsum = (EPI == EPI_DGRAD) && ep.colsum != nullptr;
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        const int n0 = n_base + c0;
-        if (n0 >= ep.out_cols) break;  // warp-uniform
-        uint32_t r[16];
-        tc::tmem_ld16(t_row + c0, r);
-        tc::tmem_wait_ld();
-        float v[16];
-#pragma unroll
-        for (int j = 0; j < 16; j++) v[j] = have_acc ? __uint_as_float(r[j]) : 0.f;
-        const int nvalid = min(16, ep.out_cols - n0);
-        if constexpr (EPI == EPI_F32 || EPI == EPI_BF16) {
-          if (row_ok) {
-            float x[16];
-            if (ep.aux) {
-              load_row16_bf16(ep.aux + (long)batch * ep.aux_bstride + (long)row * ep.ld_aux + n0, x, nvalid,
-                              (ep.ld_aux % 8) == 0);
-            }
-#pragma unroll
-            for (int j = 0; j < 16; j++) v[j] = ep.alpha * v[j] + (ep.aux ? ep.beta * x[j] : 0.f);
-            const long off = (long)bz * ep.out_bstride + (long)row * ep.ldo + n0;
-            if constexpr (EPI == EPI_F32)
-              store_row16_f32((float*)ep.out + off, v, nvalid, (ep.ldo % 4) == 0);
-            else
-              store_row16_bf16((__nv_bfloat16*)ep.out + off, v, nvalid, (ep.ldo % 8) == 0);
-          }
-        } else if constexpr (EPI == EPI_FWD) {
-          if (row_ok) {
-            float z[16], h[16];
-#pragma unroll
-            for (int j = 0; j < 16; j++) {
-              z[j] = v[j] + ((n0 + j) < ep.out_cols ? ep.bias[n0 + j] : 0.f);
-              h[j] = act_fwd(z[j], ep.act);
-            }
-            store_row16_bf16((__nv_bfloat16*)ep.out + (long)row * ep.ldo + n0, h, nvalid, (ep.ldo % 8) == 0);
-            if (ep.out2)
-              store_row16_bf16((__nv_bfloat16*)ep.out2 + (long)row * ep.ldo2 + n0, z, nvalid, (ep.ldo2 % 8) == 0);
-          }
-        } else if constexpr (EPI == EPI_DGRAD) {
-          float x[16];
-          if (row_ok) {
-            load_row16_bf16(ep.aux + (long)row * ep.ld_aux + n0, x, nvalid, (ep.ld_aux % 8) == 0);
-#pragma unroll
-            for (int j = 0; j < 16; j++) v[j] = (j < nvalid) ? v[j] * act_grad(x[j], ep.act) : 0.f;
-            store_row16_bf16((__nv_bfloat16*)ep.out + (long)row * ep.ldo + n0, v, nvalid, (ep.ldo % 8) == 0);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; j++) v[j] = 0.f;
-          }
-          if (do_colsum) {
-            const float cs = warp_colsum16(v, lane);
-            if ((lane & 1) == 0) red[sub * BN + c0 + (lane >> 1)] = cs;
-          }
-        }
-      }
-      if (do_colsum) {
-        tc::named_bar_sync(1, 128);
-        const int t = threadIdx.x - 64;
-        for (int c = t; c < BN; c += 128) {
-          const int n = n_base + c;
-          if (n < ep.out_cols)
-            ep.colsum[(long)m_tile * ep.ld_colsum + n] = ((red[c] + red[BN + c]) + red[2 * BN + c]) + red[3 * BN + c];
-        }
-      }
+      tc::tc_fence_after();
+      const uint32_t t_row = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(sub * 32) << 16);
+      epilogue_tile<BN, EPI>(ep, t_row, ti.m, ti.n, ti.z, ep.k_splits > 1 ? 0 : ti.z, b1 > b0, sub, half, lane, red,
+                             rowscr);
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&acc_empty[buf])) : "memory");
     }
   }
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem_base, BN);
+    tc::tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 

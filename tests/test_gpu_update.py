@@ -157,8 +157,23 @@ def test_deep_update_bf16_tier_vs_oracle(L, act):
     dg, dr = got[:P] - pm[:P], ref[:P] - pm[:P]
     assert rel(dg, dr) < 0.15
     assert float(dg @ dr / (np.linalg.norm(dg) * np.linalg.norm(dr))) > 0.99
-    # momentum is a linear function of the gradients: the gradient bar applies
+    # the second minibatch's gradient is taken at the weights the first Muon step produced, so the
+    # momentum inherits the same amplified difference
+    assert rel(got[P:], ref[P:]) < 0.15
+
+
+@pytest.mark.parametrize("L,act", [(1, 0), (3, 1)])
+def test_single_minibatch_momentum_is_the_clipped_gradient(L, act):
+    # one minibatch from zero momentum: mom = clipped mean gradient, so the gradient bar applies
+    NT, D, H, A = 2048, 20, 192, 7
+    P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, A, L, 31 + L, act)
+    perm = O.shuffle_perm(NT, 1, 80)
+    ref = O.train_update(pm, obs, acts, adv, ret, olp, perm, NT, D, H, A, 1, 1, 0.02, 0.0, 0.95, 1e-7, 0.5, 0.01, 0.2,
+                         L=L, act=act, ov=ov, vfClip=0.2, maxGradNorm=0.5)
+    got, _ = _run_resident(pm, P, (L, act), obs, acts, adv, ret, olp, ov, perm, NT, D, H, A, 1, 1, 0.02, 0.2, 0.5, 1)
     assert rel(got[P:], ref[P:]) < 3e-2
+    dg, dr = got[:P] - pm[:P], ref[:P] - pm[:P]
+    assert rel(dg, dr) < 0.15
 
 
 def test_bf16_update_is_deterministic():
