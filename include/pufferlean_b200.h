@@ -95,6 +95,17 @@ int pl_muon_stepmat(const double* W, const double* G, const double* M, size_t ro
 int pl_ns_batched_bf16_dev(void* X, size_t batch, size_t rows, size_t cols, double eps, const double* coeffs,
                            size_t iters, void* stream);
 
+/* The same batched Newton-Schulz without allocating device memory, for callers that cannot call
+ * cudaMalloc: code running while a CUDA graph is captured, hosts whose device memory belongs to
+ * another allocator or a fixed budget, loops that must stay off the driver's allocator. No
+ * counterpart in the reference. The workspace is a fixed 32 MiB array inside the library (held on
+ * every GPU that loads it until exit); requests needing more (2*batch*m*n + 2*batch*m*m bf16 values,
+ * m = min(rows,cols), n = max(rows,cols), plus 256 bytes) fail with PL_ERR_INVALID. All calls on a
+ * device share that array, so calls that overlap on the GPU race: serialise them. The first call on
+ * a device looks the array up (cudaGetSymbolAddress); make it before any stream capture. */
+int pl_ns_batched_bf16_dev_noalloc(void* X, size_t batch, size_t rows, size_t cols, double eps,
+                                   const double* coeffs, size_t iters, void* stream);
+
 /* ------------------------------------------------------------------ MLP PPO -------------------- */
 
 /* Summed PPO-objective gradient of the one-hidden-layer MLP (host buffers).

@@ -22,6 +22,7 @@ struct NsWork {
   double* U = nullptr;
   double* part = nullptr;
   long ldx = 0, ldg = 0;
+  unsigned* err = nullptr;  // bounded-wait error word for the GEMMs (NULL = the per-device default)
 };
 
 int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,

@@ -36,6 +36,7 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
     Operand opG{w.G, m, m, w.ldg, batch, gbs};
     Operand opB{w.B, m, m, w.ldg, batch, gbs};
     EpiArgs e{};
+    e.err = w.err;
     // G = X X^T
     e.out = w.G;
     e.ldo = w.ldg;
@@ -56,6 +57,7 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
     if (rc) return rc;
     // X' = a X + Bm X
     EpiArgs u{};
+    u.err = w.err;
     u.ldo = ldx;
     u.out_bstride = xbs_eff;
     u.out_rows = m;
@@ -119,6 +121,21 @@ __global__ void transpose_bf16_kernel(const __nv_bfloat16* __restrict__ src, int
     const int c = c0 + i, r = r0 + threadIdx.x;
     if (r < rows && c < cols) dst[bo + (long)c * rows + r] = t[threadIdx.x][i];
   }
+}
+
+int launch_ns_normalize(__nv_bfloat16* X, long batch, long per, double eps, cudaStream_t st) {
+  ns_batch_normalize_kernel<<<(unsigned)batch, 256, 0, st>>>(X, per, per, eps);
+  count_launch();
+  PL_LAUNCH("ns_batch_normalize_kernel");
+  return PL_OK;
+}
+int launch_transpose_bf16(const __nv_bfloat16* src, long batch, int rows, int cols, __nv_bfloat16* dst,
+                          cudaStream_t st) {
+  dim3 grid((unsigned)ceil_div(cols, 32), (unsigned)ceil_div(rows, 32), (unsigned)batch);
+  transpose_bf16_kernel<<<grid, dim3(32, 8), 0, st>>>(src, rows, cols, dst);
+  count_launch();
+  PL_LAUNCH("transpose_bf16_kernel");
+  return PL_OK;
 }
 
 }  // namespace pl

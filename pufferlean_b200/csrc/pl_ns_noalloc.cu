@@ -1,0 +1,103 @@
+// Batched Newton-Schulz that allocates no device memory.
+//
+// Some callers cannot call cudaMalloc: code that runs while a CUDA graph is being captured
+// (allocation is not a capturable operation), callers inside a host whose device memory is owned by
+// another allocator or a fixed budget (a framework's caching allocator, an embedded runtime that
+// forbids allocation after start-up), and hot loops that must not hit the driver's allocator. For
+// them this entry point takes the Newton-Schulz workspace from a fixed array compiled into the
+// library instead of from the allocator. The caller still owns X (input and output).
+//
+// Limit: kNoAllocBytes (32 MiB) per device, which every GPU that loads the library holds until the
+// process exits. The workspace needs 2*batch*m*n + 2*batch*m*m bf16 values (m = min(rows, cols),
+// n = max(rows, cols)) plus 256 bytes; larger requests are rejected with PL_ERR_INVALID.
+//
+// Sharing: every call on a device uses the same array and leaves its contents behind, so two calls
+// whose work overlaps on the GPU (different streams, or different host threads) race on it and
+// corrupt each other's results; serialise them. The only value that must start at zero, the
+// bounded-wait error word, is cleared by each call.
+//
+// Set-up: the first call on each device looks up the array's device address with
+// cudaGetSymbolAddress (with that device current). Make that first call before any stream capture.
+#include <mutex>
+
+#include "pl_gemm.cuh"
+#include "pl_mlp.cuh"
+#include "pl_runtime.h"
+
+namespace pl {
+int launch_ns_normalize(__nv_bfloat16* X, long batch, long per, double eps, cudaStream_t st);
+int launch_transpose_bf16(const __nv_bfloat16* src, long batch, int rows, int cols, __nv_bfloat16* dst,
+                          cudaStream_t st);
+}  // namespace pl
+
+namespace {
+constexpr size_t kNoAllocBytes = (size_t)32 << 20;
+static __device__ __align__(256) unsigned char g_ns_noalloc_scratch[kNoAllocBytes];
+static void* g_scratch_addr[64];
+static std::mutex g_scratch_mu;
+
+inline size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+// Device address of the array on the current device (looked up once per device).
+int scratch_address(void** out) {
+  int dev = 0;
+  PL_CUDA(cudaGetDevice(&dev));
+  PL_REQUIRE(dev >= 0 && dev < 64, PL_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> g(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_ns_noalloc_scratch);
+    if (e != cudaSuccess) return pl::check_cuda(e, "cudaGetSymbolAddress(no-alloc Newton-Schulz workspace)");
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return PL_OK;
+}
+}  // namespace
+
+extern "C" int pl_ns_batched_bf16_dev_noalloc(void* Xv, size_t batch, size_t rows, size_t cols, double eps,
+                                              const double* coeffs, size_t iters, void* stream) {
+  using namespace pl;
+  if (batch == 0 || rows == 0 || cols == 0) return PL_OK;
+  PL_REQUIRE(Xv != nullptr, PL_ERR_INVALID, "no-alloc Newton-Schulz: X is NULL");
+  PL_REQUIRE(coeffs && iters > 0 && iters <= 64, PL_ERR_INVALID, "Newton-Schulz needs a coefficient table");
+  PL_REQUIRE(rows % 8 == 0 && cols % 8 == 0, PL_ERR_INVALID, "batched NS needs rows and cols multiples of 8");
+  const int m = (int)(rows < cols ? rows : cols), n = (int)(rows < cols ? cols : rows);
+  const long per = (long)m * n;
+  const size_t xbytes = align256((size_t)per * batch * 2), gbytes = align256((size_t)m * m * batch * 2);
+  const size_t need = 256 + 2 * xbytes + 2 * gbytes;
+  PL_REQUIRE(need <= kNoAllocBytes, PL_ERR_INVALID,
+             "no-alloc Newton-Schulz: %zu matrices of %zux%zu need %zu bytes of workspace, above the fixed %zu-byte "
+             "limit (use pl_ns_batched_bf16_dev, which allocates)",
+             batch, rows, cols, need, kNoAllocBytes);
+  void* base = nullptr;
+  int rc = scratch_address(&base);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  unsigned char* b = (unsigned char*)base;
+  NsWork w;
+  w.err = (unsigned*)b;
+  w.X0 = (__nv_bfloat16*)(b + 256);
+  w.X1 = (__nv_bfloat16*)(b + 256 + xbytes);
+  w.G = (__nv_bfloat16*)(b + 256 + 2 * xbytes);
+  w.B = (__nv_bfloat16*)(b + 256 + 2 * xbytes + gbytes);
+  w.ldx = n;
+  w.ldg = m;
+  PL_CUDA(cudaMemsetAsync(w.err, 0, sizeof(unsigned), st));
+  __nv_bfloat16* X = (__nv_bfloat16*)Xv;
+  const bool tall = rows > cols;
+  if (tall)
+    rc = launch_transpose_bf16(X, (long)batch, (int)rows, (int)cols, w.X0, st);
+  else
+    rc = cudaMemcpyAsync(w.X0, X, (size_t)per * batch * 2, cudaMemcpyDeviceToDevice, st) == cudaSuccess
+             ? PL_OK
+             : check_cuda(cudaGetLastError(), "cudaMemcpyAsync");
+  if (rc) return rc;
+  rc = launch_ns_normalize(w.X0, (long)batch, per, eps, st);
+  if (rc) return rc;
+  rc = ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, w.X0, n, per, nullptr, 0, 0, st);
+  if (rc) return rc;
+  if (tall) return launch_transpose_bf16(w.X0, (long)batch, (int)cols, (int)rows, X, st);
+  PL_CUDA(cudaMemcpyAsync(X, w.X0, (size_t)per * batch * 2, cudaMemcpyDeviceToDevice, st));
+  return PL_OK;
+}
