@@ -42,6 +42,9 @@ WORKLOADS = {
     # 65536 envs x 64, obs 1024, 4 hidden 2048 (+ the 1024->2048 encoder), 64 actions
     "c5": dict(name="C5 large-MLP PPO+Muon update (configs[4])", N=65536, T=64, D=1024, H=2048, L=5, A=64, act=1,
                Nmb=262144, epochs=4, obs="normal", rew="normal", done=0.01, lr=0.02),
+    # profiling case of C5: the same per-row shapes, 1024 envs, one minibatch of 65,536 rows
+    "c5p": dict(name="C5 per-row shapes, 1024 envs (profiling case)", N=1024, T=64, D=1024, H=2048, L=5, A=64,
+                act=1, Nmb=65536, epochs=1, obs="normal", rew="normal", done=0.01, lr=0.02),
     # CartPole-shaped, 1024 envs x 64, obs 4, hidden 128, 2 actions
     "c1": dict(name="C1 CartPole-shaped PPO+Muon update (configs[0])", N=1024, T=64, D=4, H=128, L=1, A=2, act=1,
                Nmb=16384, epochs=4, obs="normal", rew="bern", done=0.01, lr=0.02),
@@ -321,6 +324,107 @@ def run_e2e(args, wl, state, rank, world, local_rank):
                                                   "host GAE + shuffle in the timed region)"}
 
 
+def measure_vtrace_c2(reps=20):
+    """the fp32 V-trace scan over 4096 segments x 64, 20 B per element
+    (rewards, values, dones, importance ratios in; advantages out). One set is 5.2 MB and would sit
+    in L2, so 64 rotating sets (335 MB) are scanned back to back, each by its own launch inside one
+    CUDA graph; the single-set latency is reported beside it."""
+    import torch
+
+    import pufferlean_b200 as plb
+
+    L = plb.lib()
+    B, T, S = 4096, 64, 64
+    g = torch.Generator(device="cuda").manual_seed(2)
+    rew = torch.rand(S, B * T, device="cuda", generator=g) * 2 - 1
+    val = torch.randn(S, B * T, device="cuda", generator=g)
+    term = (torch.rand(S, B * T, device="cuda", generator=g) < 0.01).float()
+    imp = torch.exp(0.1 * torch.randn(S, B * T, device="cuda", generator=g))
+    adv = torch.empty(S, B * T, device="cuda")
+    st = torch.cuda.Stream()
+
+    def one(i, stream):
+        rc = L.pl_vtrace_f32_dev(rew[i].data_ptr(), val[i].data_ptr(), term[i].data_ptr(), imp[i].data_ptr(), None,
+                                 B, T, 0.995, 0.90, 1.0, 1.0, adv[i].data_ptr(), None, stream)
+        check(rc, L)
+
+    with torch.cuda.stream(st):
+        for i in range(S):
+            one(i, st.cuda_stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            for i in range(S):
+                one(i, torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        t_sets = e0.elapsed_time(e1) / reps / 1e3
+        # single-call latency (one set, L2-warm)
+        for _ in range(5):
+            one(0, st.cuda_stream)
+        e0.record(st)
+        for _ in range(100):
+            one(0, st.cuda_stream)
+        e1.record(st)
+        torch.cuda.synchronize()
+        t_one = e0.elapsed_time(e1) / 100 / 1e3
+    bytes_per_set = 20 * B * T
+    gbs = S * bytes_per_set / t_sets / 1e9
+    _, peak_hbm, kind = peaks()
+    del graph
+    return {"config": "configs[1]: 4096 segments x 64, fp32, gamma .995 lambda .90 rho=c=1",
+            "bytes_per_element": 20, "sets": S, "achieved_gbs": gbs, "peak_gbs": peak_hbm,
+            "frac": gbs / peak_hbm, "peak_kind": kind, "us_per_set": t_sets / S * 1e6,
+            "single_call_us": t_one * 1e6, "elements_per_s": S * B * T / t_sets}
+
+
+def measure_ns_c3(reps=5):
+    """Newton-Schulz (5 quintic steps) on 64 each of 128x128, 512x512 and
+    512x2048 bf16 matrices; algorithmic flops 5 (4 m^2 n + 2 m^3) per matrix, 1.035e12 in all."""
+    import torch
+
+    import pufferlean_b200 as plb
+
+    L = plb.lib()
+    co = np.ascontiguousarray(np.array(QUINTIC, dtype=np.float64))
+    dp = C.POINTER(C.c_double)
+    groups = [(64, 128, 128), (64, 512, 512), (64, 512, 2048)]
+    g = torch.Generator(device="cuda").manual_seed(3)
+    Xs = [torch.randn(b, r, c, device="cuda", generator=g).to(torch.bfloat16) for b, r, c in groups]
+    flops = sum(b * 5 * (4 * min(r, c) ** 2 * max(r, c) + 2 * min(r, c) ** 3) for b, r, c in groups)
+
+    def run():
+        for X, (b, r, c) in zip(Xs, groups):
+            check(L.pl_ns_batched_bf16_dev(X.data_ptr(), b, r, c, 1e-7, co.ctypes.data_as(dp), 5, None), L)
+
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / reps / 1e3
+    peak_tf, _, kind = peaks()
+    burst = None
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        burst = json.load(open(p)).get("bf16_tflops")
+    tf = flops / t / 1e12
+    return {"config": "configs[2]: 64 x {128^2, 512^2, 512x2048}, 5 quintic steps, bf16 in / fp32 acc",
+            "flops": flops, "ms": t * 1e3, "achieved_tflops": tf, "peak_tflops": burst or peak_tf,
+            "frac": tf / (burst or peak_tf), "peak_kind": kind + " (bf16 burst)"}
+
+
 def cpu_baseline(wl, steps=1):
     from oracle import cpu_port
 
@@ -352,6 +456,7 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c5")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the configs[1] / configs[2] kernel measurements")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -384,6 +489,9 @@ def main():
     import pufferlean_b200 as plb
 
     plb.policy_free(state["handle"])
+    if rank == 0 and not args.no_extra:
+        out["c2_vtrace"] = measure_vtrace_c2()
+        out["c3_newton_schulz"] = measure_ns_c3()
     if rank == 0:
         if not args.no_cpu and world == 1:
             out["cpu_baseline"] = cpu_baseline(wl)
