@@ -142,6 +142,25 @@ def check(rc, L):
         raise RuntimeError(L.pl_last_error().decode())
 
 
+def make_comm(L, rank, world):
+    """NCCL communicator of the library (one per rank); the 128-byte id travels over the
+    torch.distributed process group (plumbing only)."""
+    import torch
+
+    if world == 1:
+        return None
+    ident = (C.c_uint8 * 128)()
+    if rank == 0:
+        check(L.pl_comm_unique_id(ident), L)
+    t = torch.tensor(list(bytes(ident)), dtype=torch.uint8, device="cuda")
+    torch.distributed.broadcast(t, 0)
+    ident = (C.c_uint8 * 128)(*t.cpu().tolist())
+    comm = C.c_void_p()
+    L.pl_comm_create.argtypes = [C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]
+    check(L.pl_comm_create(rank, world, ident, C.byref(comm)), L)
+    return comm
+
+
 def run_ours(args, wl, rank, world, local_rank):
     import torch
 
@@ -180,9 +199,10 @@ def run_ours(args, wl, rank, world, local_rank):
     P, pm = xavier_pm(D, H, A, Lh, 42)
     handle = plb.policy_load(pm, P)
     co = np.ascontiguousarray(np.array(QUINTIC, dtype=np.float64))
+    comm = make_comm(L, rank, world)
     desc = Desc(NT=NT, D=D, H=H, A=A, epochs=E, numMB=numMB, arch=Arch(Lh, wl["act"], co.ctypes.data_as(dp), 5),
                 wd=0.0, mu=0.95, eps=1e-12, vfCoef=0.5, entCoef=0.01, clipEps=0.2, vfClip=0.2, maxGradNorm=1.5,
-                bf16=1, use_old_values=1, rank=rank, world=world, comm=None)
+                bf16=1, use_old_values=1, rank=rank, world=world, comm=comm)
     u = vp()
     check(L.pl_update_create(handle, C.byref(desc), C.byref(u)), L)
     stream = torch.cuda.current_stream().cuda_stream
@@ -228,7 +248,7 @@ def run_ours(args, wl, rank, world, local_rank):
     prof = {k: {"ms_per_step": pms[i] / args.steps, "tflops": (pfl[i] / (pms[i] / 1e3) / 1e12) if pms[i] > 0 and
                 pfl[i] > 0 else None, "launches_per_step": pln[i] / args.steps}
             for i, k in enumerate(["fwd_gemm", "ppo_head_gemm", "dgrad_gemm", "wgrad_gemm", "newton_schulz",
-                                   "gather_stats", "optimizer_elementwise"])}
+                                   "gather_stats", "optimizer_elementwise", "dp_collectives"])}
     L.pl_update_destroy(u)
     del obs
     torch.cuda.empty_cache()
@@ -253,7 +273,7 @@ def run_ours(args, wl, rank, world, local_rank):
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
     }
-    return out, dict(handle=handle, P=P, pm=pm)
+    return out, dict(handle=handle, P=P, pm=pm, comm=comm, desc=desc, co=co)
 
 
 def run_e2e(args, wl, state, rank, world, local_rank):
@@ -306,6 +326,25 @@ def run_e2e(args, wl, state, rank, world, local_rank):
                                               wl["lr"], 0.0, 0.95, 1e-12, 0.5, 0.01, 0.2, 0.2, 1.5, 1,
                                               out0.ctypes.data_as(dp)), L)
 
+    if world > 1:
+        # the reference's C-ABI is single-GPU; the data-parallel form of the same call is the session
+        # API fed from the same pinned host columns
+        vp = C.c_void_p
+        L.pl_update_create.argtypes = [C.c_size_t, C.POINTER(Desc), C.POINTER(vp)]
+        L.pl_update_set_columns.argtypes = [vp] * 9
+        L.pl_update_run.argtypes = [vp, C.c_double, vp]
+        L.pl_update_destroy.argtypes = [vp]
+        sess = vp()
+        check(L.pl_update_create(state["handle"], C.byref(state["desc"]), C.byref(sess)), L)
+
+        def step(i):  # noqa: F811
+            check(L.pl_gae_soa(P_(cols["val"]), P_(cols["rew"]), P_(cols["term"]), N, T, 0.995, 0.90, P_(gae)), L)
+            check(L.pl_shuffle_perm(NT, E, 0xE2E + 1000 * rank + i, P_(perm)), L)
+            check(L.pl_update_set_columns(sess, obs_h.data_ptr(), cols["acts"].data_ptr(), gae.data_ptr(),
+                                          gae.data_ptr() + 8 * NT, cols["olp"].data_ptr(), cols["val"].data_ptr(),
+                                          perm.data_ptr(), None), L)
+            check(L.pl_update_run(sess, wl["lr"], None), L)
+            cudart_memcpy_d2h(out0, state["handle"])  # synchronizes, then reads params[0]
     step(0)
     if world > 1:
         torch.distributed.barrier()
@@ -318,8 +357,11 @@ def run_e2e(args, wl, state, rank, world, local_rank):
         t = torch.tensor([dt], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         dt = float(t.item())
+    if world > 1:
+        L.pl_update_destroy(sess)
     h2d = 8 * (NT * D + 5 * NT + E * NT)
-    return {"value": world * NT / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 8,
+    return {"value": world * NT / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": 8 if world == 1 else 16,
             "steps": k, "s_per_step": dt, "path": "pl_train_update_resident_deep (C-ABI, pinned host f64 columns, "
                                                   "host GAE + shuffle in the timed region)"}
 
@@ -425,6 +467,18 @@ def measure_ns_c3(reps=5):
             "frac": tf / (burst or peak_tf), "peak_kind": kind + " (bf16 burst)"}
 
 
+def cudart_memcpy_d2h(dst, handle):
+    """8-byte read-back of params[0] from the resident policy (the reference's divergence guard)."""
+    import pufferlean_b200 as plb
+
+    L = plb.lib()
+    L.pl_policy_download.argtypes = [C.c_size_t, C.c_size_t, C.POINTER(C.c_double)]
+    buf = np.zeros(2)
+    # a 1-parameter download reads [params[0]; params[1]]: the first 16 bytes of the handle
+    check(L.pl_policy_download(handle, 1, buf.ctypes.data_as(C.POINTER(C.c_double))), L)
+    dst[0] = buf[0]
+
+
 def cpu_baseline(wl, steps=1):
     from oracle import cpu_port
 
@@ -489,6 +543,9 @@ def main():
     import pufferlean_b200 as plb
 
     plb.policy_free(state["handle"])
+    if state.get("comm"):
+        plb.lib().pl_comm_destroy.argtypes = [C.c_void_p]
+        plb.lib().pl_comm_destroy(state["comm"])
     if rank == 0 and not args.no_extra:
         out["c2_vtrace"] = measure_vtrace_c2()
         out["c3_newton_schulz"] = measure_ns_c3()

@@ -215,12 +215,28 @@ int pl_update_run(pl_update* u, double lr, void* stream);
 uint64_t pl_update_last_launches(const pl_update* u);
 /* Per-class kernel timing with CUDA events on the launch stream while `on` (classes: 0 forward GEMM,
  * 1 PPO-head GEMM, 2 data-gradient GEMM, 3 weight-gradient GEMM incl. split-K sum, 4 Newton-Schulz
- * GEMMs, 5 gather/statistics, 6 optimizer elementwise and reductions). pl_update_profile_read
+ * GEMMs, 5 gather/statistics, 6 optimizer elementwise and reductions, 7 data-parallel collectives).
+ * pl_update_profile_read
  * synchronizes and returns, per class, total milliseconds, algorithmic flops and launches since
  * profiling was switched on. */
 int pl_update_profile(pl_update* u, int on);
 int pl_update_profile_read(pl_update* u, double ms[8], double flops[8], double launches[8]);
 int pl_update_destroy(pl_update* u);
+
+/* ------------------------------------------------------------------ data parallelism ----------- */
+/* One process per GPU over NCCL (no reference counterpart: the reference is single-GPU,
+ * docs/KNOWN_GAPS.md:349). Rank 0 draws a 128-byte id, the caller hands it to every rank by any side
+ * channel, each rank creates its communicator on its current device and passes it to
+ * pl_update_create through pl_update_desc {rank, world, comm}. In a data-parallel update every rank
+ * gathers its own rows of each minibatch; the advantage statistics and the summed gradient are
+ * all-reduced; each weight matrix is orthogonalised by one owner rank (pl_muon_shard_plan) and the
+ * results are broadcast; every rank then applies the identical step. */
+int pl_comm_unique_id(uint8_t id[128]);
+int pl_comm_create(int rank, int world, const uint8_t id[128], void** comm);
+int pl_comm_destroy(void* comm);
+/* Owner rank of each of nmat matrices (rows[i] x cols[i]) for the sharded Newton-Schulz: greedy
+ * longest-processing-time by 4 m^2 n + 2 m^3 flops. Deterministic. */
+int pl_muon_shard_plan(const size_t* rows, const size_t* cols, size_t nmat, int world, int* owner);
 
 /* ------------------------------------------------------------------ dashboard losses ----------- */
 /* The reference's 7-loss channel [policy, value, entropy, total, old_kl, kl, clipfrac]

@@ -40,7 +40,8 @@ int launch_perm(const double* perm, long n, int* out, cudaStream_t st);
 int launch_gather(bool bf16, const int* idx, int Nmb, const void* obs, int rowElems, void* X, const int* act_c,
                   const double* adv_c, const float* ret_c, const float* olp_c, const float* ov_c, int* mb_act,
                   float* mb_adv, float* mb_ret, float* mb_olp, float* mb_ov, double* part, double* ms,
-                  cudaStream_t st);
+                  cudaStream_t st, double* sums = nullptr);
+int launch_adv_ms_from_sums(const double* sums, double* ms, cudaStream_t st);
 int launch_colsum_reduce(const float* part, int tiles, long ld, int ncols, float* out, cudaStream_t st);
 int launch_splitk_reduce(const float* part, int S, long n, float* out, cudaStream_t st);
 int launch_gradnorm(const float* g, long P, double sc, double maxNorm, double* part, double* cc, cudaStream_t st);

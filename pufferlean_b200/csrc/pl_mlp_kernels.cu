@@ -121,6 +121,28 @@ __global__ void adv_stats_kernel(const double* __restrict__ part, int nb, int n,
   ms[1] = sqrt(var) + 1e-8;
 }
 
+// Data-parallel form: the local (sum, sum of squares, count) folded in order, to be all-reduced.
+__global__ void adv_sums_kernel(const double* __restrict__ part, int nb, int n, double* sums) {
+  if (threadIdx.x || blockIdx.x) return;
+  double s1 = 0.0, s2 = 0.0;
+  for (int b = 0; b < nb; b++) {
+    s1 += part[2 * b];
+    s2 += part[2 * b + 1];
+  }
+  sums[0] = s1;
+  sums[1] = s2;
+  sums[2] = (double)n;
+}
+__global__ void adv_ms_from_sums_kernel(const double* __restrict__ sums, double* ms) {
+  if (threadIdx.x || blockIdx.x) return;
+  const double n = sums[2];
+  const double mean = sums[0] / n;
+  double var = sums[1] / n - mean * mean;
+  if (var < 0.0) var = 0.0;
+  ms[0] = mean;
+  ms[1] = sqrt(var) + 1e-8;
+}
+
 // ---------------------------------------------------------------- fixed-order reductions
 // out[c] = sum_t part[t*ld + c], t ascending (bias gradients from per-CTA column partials)
 __global__ void colsum_reduce_kernel(const float* __restrict__ part, int tiles, long ld, int ncols, float* out) {
@@ -386,10 +408,16 @@ int launch_perm(const double* perm, long n, int* out, cudaStream_t st) {
   PL_LAUNCH("perm_kernel");
   return PL_OK;
 }
+int launch_adv_ms_from_sums(const double* sums, double* ms, cudaStream_t st) {
+  adv_ms_from_sums_kernel<<<1, 32, 0, st>>>(sums, ms);
+  count_launch();
+  PL_LAUNCH("adv_ms_from_sums_kernel");
+  return PL_OK;
+}
 int launch_gather(bool bf16, const int* idx, int Nmb, const void* obs, int rowElems, void* X, const int* act_c,
                   const double* adv_c, const float* ret_c, const float* olp_c, const float* ov_c, int* mb_act,
                   float* mb_adv, float* mb_ret, float* mb_olp, float* mb_ov, double* part, double* ms,
-                  cudaStream_t st) {
+                  cudaStream_t st, double* sums) {
   const int nb = (int)(Nmb < kRedBlocks * 8 ? (Nmb + 7) / 8 : kRedBlocks);
   if (bf16)
     gather_kernel<true><<<nb, 256, 0, st>>>(idx, Nmb, obs, rowElems, X, act_c, adv_c, ret_c, olp_c, ov_c, mb_act,
@@ -397,7 +425,10 @@ int launch_gather(bool bf16, const int* idx, int Nmb, const void* obs, int rowEl
   else
     gather_kernel<false><<<nb, 256, 0, st>>>(idx, Nmb, obs, rowElems, X, act_c, adv_c, ret_c, olp_c, ov_c, mb_act,
                                              mb_adv, mb_ret, mb_olp, mb_ov, part);
-  adv_stats_kernel<<<1, 32, 0, st>>>(part, nb, Nmb, ms);
+  if (sums)
+    adv_sums_kernel<<<1, 32, 0, st>>>(part, nb, Nmb, sums);
+  else
+    adv_stats_kernel<<<1, 32, 0, st>>>(part, nb, Nmb, ms);
   count_launch(2);
   PL_LAUNCH("gather_kernel");
   return PL_OK;

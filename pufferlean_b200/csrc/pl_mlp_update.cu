@@ -21,6 +21,7 @@
 #include <mutex>
 #include <vector>
 
+#include "pl_comm.h"
 #include "pl_gemm.cuh"
 #include "pl_mlp.cuh"
 #include "pl_muon.cuh"
@@ -75,6 +76,11 @@ struct pl_update {
   bool grad_only = false;  // pl_mlp_ppo_grad: no normalisation, no optimizer step
   bool alloc_failed = false;
   float* adv_f = nullptr;  // fp32 scan output of pl_update_set_advantages_dev
+  // data parallelism
+  bool dp = false;             // world > 1 with a communicator
+  double* adv_sums = nullptr;  // [sum, sum of squares, count] of the minibatch's raw advantages
+  std::vector<int> owner;      // Newton-Schulz owner rank of each layer
+  std::vector<float*> xres;    // per-layer orthogonalised update (m x n wide layout, fp32)
   // profiling: CUDA events around each launch group, per class
   bool prof = false;
   std::vector<cudaEvent_t> ev;
@@ -279,6 +285,11 @@ static int alloc_session(pl_update* u) {
     for (auto& ly : u->layers) ws = std::max(ws, exact_ws_doubles(ly.out, ly.in));
     u->exact_ws = dalloc<double>(u, ws);
   }
+  if (u->dp) {
+    u->adv_sums = dalloc<double>(u, 4);
+    if (fast)
+      for (auto& ly : u->layers) u->xres.push_back(dalloc<float>(u, (size_t)ly.out * ly.in));
+  }
   if (u->alloc_failed) return PL_ERR_NOMEM;
   // zero the padded shadow weights/biases once; their pads stay zero for the session
   for (size_t l = 0; l < u->layers.size(); l++) {
@@ -339,6 +350,58 @@ static int wgrad_fast(pl_update* u, const void* dZ, long ldz, int out, const voi
   return launch_splitk_reduce(u->splitk, S, (long)out * in, dst, st);
 }
 
+// Data-parallel Muon: every rank advances the momentum of every layer; each layer's Newton-Schulz
+// runs on its owner rank only (pl_muon_shard_plan); one grouped broadcast hands every rank every
+// orthogonalised update; every rank then applies the identical f64 step, so the weights stay
+// bit-identical across ranks.
+static int muon_sharded(pl_update* u, double lr, cudaStream_t st) {
+  const pl_update_desc& d = u->d;
+  int rc = PL_OK;
+  for (size_t l = 0; l < u->layers.size(); l++) {
+    const Layer& ly = u->layers[l];
+    const long n = (long)ly.out * ly.in;
+    const int m = std::min(ly.out, ly.in), nn = std::max(ly.out, ly.in);
+    int nparts = 0;
+    {
+      Span sp(u, 6, st, 0);
+      rc = launch_nesterov(u->grad + ly.oW, u->cc, u->pm + u->P + ly.oW, u->ns.U, d.mu, n, u->ns.part, &nparts, st);
+      if (!rc && u->owner[l] == d.rank)
+        rc = launch_ns_input(u->ns.U, u->ns.part, nparts, ly.out, ly.in, d.eps, u->ns.X0, u->ns.ldx, st);
+    }
+    if (rc) return rc;
+    if (u->owner[l] != d.rank) continue;
+    Span sp(u, 4, st, (double)u->iters * (4.0 * m * (double)m * nn + 2.0 * m * (double)m * m));
+    rc = ns_run(m, nn, u->coeffs.data(), u->iters, u->ns, u->ns.X0, u->ns.ldx, u->xres[l], nn, st);
+    if (rc) return rc;
+  }
+  {
+    Span sp(u, 7, st, 0);
+    std::vector<float*> bufs;
+    std::vector<size_t> counts;
+    std::vector<int> roots;
+    for (size_t l = 0; l < u->layers.size(); l++) {
+      bufs.push_back(u->xres[l]);
+      counts.push_back((size_t)u->layers[l].out * u->layers[l].in);
+      roots.push_back(u->owner[l]);
+    }
+    rc = comm_broadcast_group(d.comm, bufs, counts, roots, st);
+    if (rc) return rc;
+  }
+  for (size_t l = 0; l < u->layers.size(); l++) {
+    const Layer& ly = u->layers[l];
+    const double r = (double)ly.out / (double)ly.in;
+    const double scale = sqrt(r > 1.0 ? r : 1.0);
+    Span sp(u, 6, st, 0);
+    rc = launch_ns_finalize(u->xres[l], std::max(ly.out, ly.in), ly.out, ly.in, 1.0 - lr * d.wd, lr * scale,
+                            u->pm + ly.oW, u->Wb[l], ly.in_p, st);
+    if (!rc)
+      rc = launch_stepvec_fast(u->grad + ly.ob, u->cc, u->pm + ly.ob, u->pm + u->P + ly.ob, u->bf[l], lr, d.wd, d.mu,
+                               ly.out, st);
+    if (rc) return rc;
+  }
+  return PL_OK;
+}
+
 static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool last, cudaStream_t st) {
   const pl_update_desc& d = u->d;
   const int L = u->L;
@@ -348,7 +411,10 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
   {
     Span sp(u, 5, st, 0);
     rc = launch_gather(true, idx, Nmb, u->obs, u->Dp, u->X, u->act_c, u->adv_c, u->ret_c, u->olp_c, u->ov_c, u->mb_act,
-                       u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st);
+                       u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st, u->dp ? u->adv_sums : nullptr);
+    // data parallel: the normalisation statistics are those of the whole (all-rank) minibatch
+    if (!rc && u->dp) rc = comm_allreduce_f64(d.comm, u->adv_sums, 3, st);
+    if (!rc && u->dp) rc = launch_adv_ms_from_sums(u->adv_sums, u->ms, st);
   }
   if (rc) return rc;
   // ---- forward
@@ -454,12 +520,21 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
     dsel ^= 1;
   }
   if (u->grad_only) return PL_OK;
+  long Nglob = Nmb;
+  if (u->dp) {
+    // ---- data parallel: sum the gradient over ranks (the mean is over the all-rank minibatch)
+    Span sp(u, 7, st, 0);
+    rc = comm_allreduce_f32(d.comm, u->grad, u->P, st);
+    if (rc) return rc;
+    Nglob = (long)Nmb * d.world;
+  }
   // ---- clip to the mean gradient, then Muon on every layer
   {
     Span sp(u, 6, st, 0);
-    rc = launch_gradnorm(u->grad, (long)u->P, 1.0 / (double)Nmb, d.maxGradNorm, u->gn_part, u->cc, st);
+    rc = launch_gradnorm(u->grad, (long)u->P, 1.0 / (double)Nglob, d.maxGradNorm, u->gn_part, u->cc, st);
   }
   if (rc) return rc;
+  if (u->dp) return muon_sharded(u, lr, st);
   for (size_t l = 0; l < u->layers.size(); l++) {
     const Layer& ly = u->layers[l];
     const long n = (long)ly.out * ly.in;
@@ -497,7 +572,10 @@ static int minibatch_tight(pl_update* u, const int* idx, int Nmb, double lr, boo
   const pl_update_desc& d = u->d;
   const int L = u->L, act = d.arch.act, D = (int)d.D, H = (int)d.H, O = u->O;
   int rc = launch_gather(false, idx, Nmb, u->obs, D, u->X, u->act_c, u->adv_c, u->ret_c, u->olp_c, u->ov_c, u->mb_act,
-                         u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st);
+                         u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st,
+                         u->dp ? u->adv_sums : nullptr);
+  if (!rc && u->dp) rc = comm_allreduce_f64(d.comm, u->adv_sums, 3, st);
+  if (!rc && u->dp) rc = launch_adv_ms_from_sums(u->adv_sums, u->ms, st);
   if (rc) return rc;
   const float* hin = (const float*)u->X;
   int nin = D;
@@ -541,9 +619,15 @@ static int minibatch_tight(pl_update* u, const int* idx, int Nmb, double lr, boo
     dsel ^= 1;
   }
   if (u->grad_only) return PL_OK;
-  rc = launch_gradnorm(u->grad, (long)u->P, 1.0 / (double)Nmb, d.maxGradNorm, u->gn_part, u->cc, st);
+  long Nglob = Nmb;
+  if (u->dp) {
+    rc = comm_allreduce_f32(d.comm, u->grad, u->P, st);
+    if (rc) return rc;
+    Nglob = (long)Nmb * d.world;
+  }
+  rc = launch_gradnorm(u->grad, (long)u->P, 1.0 / (double)Nglob, d.maxGradNorm, u->gn_part, u->cc, st);
   if (rc) return rc;
-  // f64 tight Muon: widen the gradient, scale by cc on the host-free path (the scale is a device
+  // f64 tight Muon (the parity tier runs it redundantly on every rank): widen the gradient, scale by cc on the host-free path (the scale is a device
   // scalar, read back once per minibatch: this tier is the parity tier, not the fast path)
   double cc = 0;
   PL_CUDA(cudaMemcpyAsync(&cc, u->cc, sizeof(double), cudaMemcpyDeviceToHost, st));
@@ -622,6 +706,22 @@ int pl_update_create(size_t handle, const pl_update_desc* desc, pl_update** out)
     u->iters = 5;
   }
   build_layout(u);
+  u->dp = d.world > 1;
+  if (u->dp) {
+    if (!d.comm || d.rank < 0 || d.rank >= d.world) {
+      delete u;
+      return set_error(PL_ERR_INVALID, "data-parallel session needs a communicator and 0 <= rank < world");
+    }
+    std::vector<size_t> rows, cols;
+    for (auto& ly : u->layers) {
+      rows.push_back((size_t)ly.out);
+      cols.push_back((size_t)ly.in);
+    }
+    u->owner.assign(u->layers.size(), 0);
+    pl_muon_shard_plan(rows.data(), cols.data(), rows.size(), d.world, u->owner.data());
+  } else {
+    u->owner.assign(u->layers.size(), 0);
+  }
   rc = alloc_session(u);
   if (!rc && !u->fast && u->stage_elems < u->P) rc = set_error(PL_ERR_UNSUPPORTED, "tight tier staging too small");
   if (!rc) rc = refresh_shadows(u, 0);
