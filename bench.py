@@ -362,8 +362,10 @@ def run_e2e(args, wl, state, rank, world, local_rank):
     h2d = 8 * (NT * D + 5 * NT + E * NT)
     return {"value": world * NT / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": 8 if world == 1 else 16,
-            "steps": k, "s_per_step": dt, "path": "pl_train_update_resident_deep (C-ABI, pinned host f64 columns, "
-                                                  "host GAE + shuffle in the timed region)"}
+            "steps": k, "s_per_step": dt,
+            "path": ("pl_train_update_resident_deep (the reference-facing C-ABI call)" if world == 1 else
+                     "pl_update_set_columns + pl_update_run on a data-parallel session (the C-ABI's DP form)") +
+                    ", pinned host f64 columns, host GAE + shuffle in the timed region"}
 
 
 def measure_vtrace_c2(reps=20):
