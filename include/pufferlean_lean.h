@@ -1,0 +1,69 @@
+/* The reference's Lean `@[extern]` symbols for the PPO+Muon update path, as provided by
+ * libpufferlean_lean.so (pufferlean_b200/csrc/pl_lean_abi.c) on top of include/pufferlean_b200.h.
+ * Signatures are those of the reference's definitions; each line names the Lean declaration and the
+ * reference definition it replaces. Requires <lean/lean.h> (Lean's own, or include/lean_compat). */
+#ifndef PUFFERLEAN_LEAN_H
+#define PUFFERLEAN_LEAN_H
+#include <lean/lean.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaVtraceFFI, Puffer/Float/CUDA.lean:20-22; replaces ffi/puffercuda.cu:94-136 */
+lean_obj_res lean_cuda_vtrace(lean_obj_arg rew, lean_obj_arg val, lean_obj_arg term, lean_obj_arg imp, size_t B,
+                              size_t T, double gamma, double lam, double rhoClip, double cClip);
+/* cudaVtraceMinGRUFFI, CUDA.lean:29-31; replaces ffi/puffercuda.cu:171-216 */
+lean_obj_res lean_cuda_vtrace_mingru(lean_obj_arg rew, lean_obj_arg val, lean_obj_arg term, lean_obj_arg imp,
+                                     lean_obj_arg bootv, size_t B, size_t T, double gamma, double lam, double rhoClip,
+                                     double cClip);
+/* cudaMuonStepMatFFI, CUDA.lean:37-39; replaces ffi/puffercuda.cu:559-631 */
+lean_obj_res lean_cuda_muon_stepmat(lean_obj_arg W, lean_obj_arg G, lean_obj_arg M, size_t rows, size_t cols,
+                                    double lr, double wd, double mu, double eps);
+/* cudaMlpPpoGradFFI, CUDA.lean:45-47; replaces ffi/puffercuda.cu:748-816 */
+lean_obj_res lean_cuda_mlp_ppo_grad(lean_obj_arg params, lean_obj_arg obs, lean_obj_arg acts, lean_obj_arg advs,
+                                    lean_obj_arg rets, lean_obj_arg olps, size_t N, size_t H, size_t D, size_t A,
+                                    double vf, double ent, double clip, uint8_t bf16);
+/* cudaAdvNormalizeFFI, CUDA.lean:50-52; replaces ffi/puffercuda.cu:836-855 */
+lean_obj_res lean_cuda_adv_normalize(lean_obj_arg adv, size_t n);
+/* cudaTrainStepFFI, CUDA.lean:61-63; replaces ffi/puffercuda.cu:988-1080 */
+lean_obj_res lean_cuda_train_step(lean_obj_arg pm, lean_obj_arg obs, lean_obj_arg acts, lean_obj_arg advRaw,
+                                  lean_obj_arg rets, lean_obj_arg olps, size_t N, size_t H, size_t D, size_t A,
+                                  double lr, double wd, double mu, double eps, double vf, double ent, double clip,
+                                  uint8_t bf16);
+/* cudaTrainUpdateFFI, CUDA.lean:72-75; replaces ffi/puffercuda.cu:1094-1167 */
+lean_obj_res lean_cuda_train_update(lean_obj_arg pm, lean_obj_arg obs, lean_obj_arg acts, lean_obj_arg adv,
+                                    lean_obj_arg ret, lean_obj_arg olp, lean_obj_arg perm, size_t NT, size_t D,
+                                    size_t H, size_t A, size_t epochs, size_t numMB, double lr, double wd, double mu,
+                                    double eps, double vf, double ent, double clip, uint8_t bf16);
+/* policyLoadFFI / policyDownloadFFI / policyFreeFFI, CUDA.lean:225-230; replace ffi/puffercuda.cu:6100-6116 */
+lean_obj_res lean_cuda_policy_load(lean_obj_arg pm, size_t P, lean_obj_arg w);
+lean_obj_res lean_cuda_policy_download(size_t handle, size_t P, lean_obj_arg w);
+lean_obj_res lean_cuda_policy_free(size_t handle, lean_obj_arg w);
+/* cudaTrainUpdateResidentFFI, CUDA.lean:241-244; replaces ffi/puffercuda.cu:1187-1294 */
+lean_obj_res lean_cuda_train_update_resident(size_t handle, lean_obj_arg obs, lean_obj_arg acts, lean_obj_arg adv,
+                                             lean_obj_arg ret, lean_obj_arg olp, lean_obj_arg ov, lean_obj_arg perm,
+                                             size_t NT, size_t D, size_t H, size_t A, size_t epochs, size_t numMB,
+                                             double lr, double wd, double mu, double eps, double vf, double ent,
+                                             double clip, double vfClip, double maxGradNorm, uint8_t bf16,
+                                             lean_obj_arg w);
+/* No reference symbol: the deep-MLP form (L hidden layers, act 0 ReLU / 1 GELU) of the call above */
+lean_obj_res lean_cuda_train_update_resident_deep(size_t handle, lean_obj_arg obs, lean_obj_arg acts,
+                                                  lean_obj_arg adv, lean_obj_arg ret, lean_obj_arg olp,
+                                                  lean_obj_arg ov, lean_obj_arg perm, size_t NT, size_t D, size_t H,
+                                                  size_t A, size_t L, uint8_t act, size_t epochs, size_t numMB,
+                                                  double lr, double wd, double mu, double eps, double vf, double ent,
+                                                  double clip, double vfClip, double maxGradNorm, uint8_t bf16,
+                                                  lean_obj_arg w);
+/* cudaMgLossEnableFFI / cudaMgReadLossesFFI, CUDA.lean:165-178; replace ffi/puffercuda.cu:336-352 */
+lean_obj_res lean_cuda_mg_loss_enable(uint8_t on, lean_obj_arg w);
+lean_obj_res lean_cuda_mg_read_losses(lean_obj_arg w);
+/* shufflePermFFI / gaeSoaFFI, Puffer/Float/FFI.lean; replace ffi/pufferffi.c:1017-1041 and :946-971 */
+lean_obj_res lean_ffi_shuffle_perm(size_t NT, size_t epochs, uint64_t rng);
+lean_obj_res lean_ffi_gae_soa(lean_obj_arg vals, lean_obj_arg rews, lean_obj_arg terms, size_t N, size_t T,
+                              double gamma, double lam);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,244 @@
+/* Lean-runtime adapter: the reference's `@[extern]` symbols for the PPO+Muon update path, each a
+ * thin unboxing shim over the plain C ABI of libpufferlean_b200.so.
+ *
+ * The Lean declarations (Puffer/Float/CUDA.lean, Puffer/Float/FFI.lean) stay as they are; linking
+ * this file (compiled against Lean's own lean.h) instead of ffi/puffercuda.cu's definitions routes
+ * the trainer through the B200 kernels. Conventions kept from the reference (Puffer/Float/CUDA.lean
+ * and ffi/puffercuda.cu): FloatArray arguments are owned (released with lean_dec), pure functions
+ * return a fresh FloatArray, IO functions take the world token and return an IO result.
+ *
+ * Failure behaviour (there is no CPU fallback): IO functions return an IO error carrying the
+ * library's message; pure functions print the message to stderr and return a NaN-filled array of
+ * the expected size, so a failure can never masquerade as a zero gradient or a zero advantage.
+ */
+#include <lean/lean.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "pufferlean_b200.h"
+
+static double* fa(b_lean_obj_arg a) { return lean_float_array_cptr(a); }
+static size_t fan(b_lean_obj_arg a) { return lean_sarray_size(a); }
+
+static lean_obj_res new_fa(size_t n) { return lean_alloc_sarray(sizeof(double), n, n); }
+
+static lean_obj_res pure_fail(lean_obj_res out, const char* what) {
+  fprintf(stderr, "pufferlean_b200: %s failed: %s\n", what, pl_last_error());
+  double* p = fa(out);
+  for (size_t i = 0; i < fan(out); i++) p[i] = NAN;
+  return out;
+}
+static lean_obj_res io_fail(const char* what) {
+  char buf[1200];
+  snprintf(buf, sizeof buf, "pufferlean_b200: %s failed: %s", what, pl_last_error());
+  return lean_io_result_mk_error(lean_mk_io_user_error(lean_mk_string(buf)));
+}
+
+/* ---------------------------------------------------------------- V-trace (CUDA.lean:20-31) */
+LEAN_EXPORT lean_obj_res lean_cuda_vtrace(lean_obj_arg rew, lean_obj_arg val, lean_obj_arg term, lean_obj_arg imp,
+                                          size_t B, size_t T, double gamma, double lam, double rhoClip,
+                                          double cClip) {
+  lean_obj_res out = new_fa(B * T);
+  int rc = pl_vtrace(fa(rew), fa(val), fa(term), fa(imp), B, T, gamma, lam, rhoClip, cClip, fa(out));
+  lean_dec(rew);
+  lean_dec(val);
+  lean_dec(term);
+  lean_dec(imp);
+  return rc ? pure_fail(out, "lean_cuda_vtrace") : out;
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_vtrace_mingru(lean_obj_arg rew, lean_obj_arg val, lean_obj_arg term,
+                                                 lean_obj_arg imp, lean_obj_arg bv, size_t B, size_t T, double gamma,
+                                                 double lam, double rhoClip, double cClip) {
+  lean_obj_res out = new_fa(B * T);
+  int rc = pl_vtrace_mingru(fa(rew), fa(val), fa(term), fa(imp), fa(bv), B, T, gamma, lam, rhoClip, cClip, fa(out));
+  lean_dec(rew);
+  lean_dec(val);
+  lean_dec(term);
+  lean_dec(imp);
+  lean_dec(bv);
+  return rc ? pure_fail(out, "lean_cuda_vtrace_mingru") : out;
+}
+
+/* ---------------------------------------------------------------- Muon (CUDA.lean:37-39) */
+LEAN_EXPORT lean_obj_res lean_cuda_muon_stepmat(lean_obj_arg W, lean_obj_arg G, lean_obj_arg M, size_t rows,
+                                                size_t cols, double lr, double wd, double mu, double eps) {
+  lean_obj_res out = new_fa(2 * rows * cols);
+  int rc = pl_muon_stepmat(fa(W), fa(G), fa(M), rows, cols, lr, wd, mu, eps, fa(out));
+  lean_dec(W);
+  lean_dec(G);
+  lean_dec(M);
+  return rc ? pure_fail(out, "lean_cuda_muon_stepmat") : out;
+}
+
+/* ---------------------------------------------------------------- MLP PPO (CUDA.lean:45-75) */
+LEAN_EXPORT lean_obj_res lean_cuda_mlp_ppo_grad(lean_obj_arg pa, lean_obj_arg obs, lean_obj_arg acts,
+                                                lean_obj_arg advs, lean_obj_arg rets, lean_obj_arg olps, size_t N,
+                                                size_t H, size_t D, size_t A, double vf, double ent, double clip,
+                                                uint8_t bf16) {
+  lean_obj_res out = new_fa(pl_mlp_param_count(D, H, A, 1));
+  int rc = pl_mlp_ppo_grad(fa(pa), fa(obs), fa(acts), fa(advs), fa(rets), fa(olps), N, H, D, A, vf, ent, clip, bf16,
+                           fa(out));
+  lean_dec(pa);
+  lean_dec(obs);
+  lean_dec(acts);
+  lean_dec(advs);
+  lean_dec(rets);
+  lean_dec(olps);
+  return rc ? pure_fail(out, "lean_cuda_mlp_ppo_grad") : out;
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_adv_normalize(lean_obj_arg adv, size_t n) {
+  lean_obj_res out = new_fa(n);
+  int rc = pl_adv_normalize(fa(adv), n, fa(out));
+  lean_dec(adv);
+  return rc ? pure_fail(out, "lean_cuda_adv_normalize") : out;
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_train_step(lean_obj_arg pm, lean_obj_arg obs, lean_obj_arg acts,
+                                              lean_obj_arg advRaw, lean_obj_arg rets, lean_obj_arg olps, size_t N,
+                                              size_t H, size_t D, size_t A, double lr, double wd, double mu,
+                                              double eps, double vf, double ent, double clip, uint8_t bf16) {
+  lean_obj_res out = new_fa(2 * pl_mlp_param_count(D, H, A, 1));
+  int rc = pl_train_step(fa(pm), fa(obs), fa(acts), fa(advRaw), fa(rets), fa(olps), N, H, D, A, lr, wd, mu, eps, vf,
+                         ent, clip, bf16, fa(out));
+  lean_dec(pm);
+  lean_dec(obs);
+  lean_dec(acts);
+  lean_dec(advRaw);
+  lean_dec(rets);
+  lean_dec(olps);
+  return rc ? pure_fail(out, "lean_cuda_train_step") : out;
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_train_update(lean_obj_arg pm, lean_obj_arg obs, lean_obj_arg acts,
+                                                lean_obj_arg adv, lean_obj_arg ret, lean_obj_arg olp,
+                                                lean_obj_arg perm, size_t NT, size_t D, size_t H, size_t A,
+                                                size_t epochs, size_t numMB, double lr, double wd, double mu,
+                                                double eps, double vf, double ent, double clip, uint8_t bf16) {
+  lean_obj_res out = new_fa(2 * pl_mlp_param_count(D, H, A, 1));
+  int rc = pl_train_update(fa(pm), fa(obs), fa(acts), fa(adv), fa(ret), fa(olp), fa(perm), NT, D, H, A, epochs, numMB,
+                           lr, wd, mu, eps, vf, ent, clip, bf16, fa(out));
+  lean_dec(pm);
+  lean_dec(obs);
+  lean_dec(acts);
+  lean_dec(adv);
+  lean_dec(ret);
+  lean_dec(olp);
+  lean_dec(perm);
+  return rc ? pure_fail(out, "lean_cuda_train_update") : out;
+}
+
+/* ---------------------------------------------------------------- resident policy (CUDA.lean:225-244) */
+LEAN_EXPORT lean_obj_res lean_cuda_policy_load(lean_obj_arg pm, size_t P, lean_obj_arg w) {
+  (void)w;
+  size_t h = 0;
+  int rc = pl_policy_load(fa(pm), P, &h);
+  lean_dec(pm);
+  if (rc) return io_fail("lean_cuda_policy_load");
+  return lean_io_result_mk_ok(lean_box_usize(h));
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_policy_download(size_t handle, size_t P, lean_obj_arg w) {
+  (void)w;
+  lean_obj_res out = new_fa(2 * P);
+  if (pl_policy_download(handle, P, fa(out))) {
+    lean_dec(out);
+    return io_fail("lean_cuda_policy_download");
+  }
+  return lean_io_result_mk_ok(out);
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_policy_free(size_t handle, lean_obj_arg w) {
+  (void)w;
+  if (pl_policy_free(handle)) return io_fail("lean_cuda_policy_free");
+  return lean_io_result_mk_ok(lean_box(0));
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_train_update_resident(size_t handle, lean_obj_arg obs, lean_obj_arg acts,
+                                                         lean_obj_arg adv, lean_obj_arg ret, lean_obj_arg olp,
+                                                         lean_obj_arg ov, lean_obj_arg perm, size_t NT, size_t D,
+                                                         size_t H, size_t A, size_t epochs, size_t numMB, double lr,
+                                                         double wd, double mu, double eps, double vf, double ent,
+                                                         double clip, double vfClip, double maxGradNorm, uint8_t bf16,
+                                                         lean_obj_arg w) {
+  (void)w;
+  lean_obj_res out = new_fa(1);
+  int rc = pl_train_update_resident(handle, fa(obs), fa(acts), fa(adv), fa(ret), fa(olp), fa(ov), fan(ov), fa(perm), NT,
+                                    D, H, A, epochs, numMB, lr, wd, mu, eps, vf, ent, clip, vfClip, maxGradNorm, bf16,
+                                    fa(out));
+  lean_dec(obs);
+  lean_dec(acts);
+  lean_dec(adv);
+  lean_dec(ret);
+  lean_dec(olp);
+  lean_dec(ov);
+  lean_dec(perm);
+  if (rc) {
+    lean_dec(out);
+    return io_fail("lean_cuda_train_update_resident");
+  }
+  return lean_io_result_mk_ok(out);
+}
+
+/* Deep variant (no reference symbol): L hidden layers of width H, act 0 = ReLU / 1 = GELU, the
+ * reference's Newton-Schulz table. Same conventions as lean_cuda_train_update_resident. */
+LEAN_EXPORT lean_obj_res lean_cuda_train_update_resident_deep(size_t handle, lean_obj_arg obs, lean_obj_arg acts,
+                                                              lean_obj_arg adv, lean_obj_arg ret, lean_obj_arg olp,
+                                                              lean_obj_arg ov, lean_obj_arg perm, size_t NT, size_t D,
+                                                              size_t H, size_t A, size_t L, uint8_t act, size_t epochs,
+                                                              size_t numMB, double lr, double wd, double mu,
+                                                              double eps, double vf, double ent, double clip,
+                                                              double vfClip, double maxGradNorm, uint8_t bf16,
+                                                              lean_obj_arg w) {
+  (void)w;
+  pl_mlp_arch arch = {L, (int)act, NULL, 0};
+  lean_obj_res out = new_fa(1);
+  int rc = pl_train_update_resident_deep(handle, &arch, fa(obs), fa(acts), fa(adv), fa(ret), fa(olp), fa(ov), fan(ov),
+                                         fa(perm), NT, D, H, A, epochs, numMB, lr, wd, mu, eps, vf, ent, clip, vfClip,
+                                         maxGradNorm, bf16, fa(out));
+  lean_dec(obs);
+  lean_dec(acts);
+  lean_dec(adv);
+  lean_dec(ret);
+  lean_dec(olp);
+  lean_dec(ov);
+  lean_dec(perm);
+  if (rc) {
+    lean_dec(out);
+    return io_fail("lean_cuda_train_update_resident_deep");
+  }
+  return lean_io_result_mk_ok(out);
+}
+
+/* ---------------------------------------------------------------- dashboard losses (CUDA.lean:165-178) */
+LEAN_EXPORT lean_obj_res lean_cuda_mg_loss_enable(uint8_t on, lean_obj_arg w) {
+  (void)w;
+  pl_loss_enable(on);
+  return lean_io_result_mk_ok(lean_box(0));
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_mg_read_losses(lean_obj_arg w) {
+  (void)w;
+  lean_obj_res out = new_fa(7);
+  pl_read_losses(fa(out));
+  return lean_io_result_mk_ok(out);
+}
+
+/* ---------------------------------------------------------------- host bookkeeping (FFI.lean) */
+LEAN_EXPORT lean_obj_res lean_ffi_shuffle_perm(size_t NT, size_t epochs, uint64_t rng) {
+  lean_obj_res out = new_fa(NT * epochs);
+  if (pl_shuffle_perm(NT, epochs, rng, fa(out))) return pure_fail(out, "lean_ffi_shuffle_perm");
+  return out;
+}
+
+LEAN_EXPORT lean_obj_res lean_ffi_gae_soa(lean_obj_arg vals, lean_obj_arg rews, lean_obj_arg terms, size_t N, size_t T,
+                                          double gamma, double lam) {
+  lean_obj_res out = new_fa(2 * N * T);
+  int rc = pl_gae_soa(fa(vals), fa(rews), fa(terms), N, T, gamma, lam, fa(out));
+  lean_dec(vals);
+  lean_dec(rews);
+  lean_dec(terms);
+  return rc ? pure_fail(out, "lean_ffi_gae_soa") : out;
+}

@@ -47,3 +47,50 @@ def test_host_bookkeeping_matches_oracle():
     vals, rews = g.standard_normal(200), g.uniform(-2, 2, 200)
     terms = (g.random(200) < 0.1).astype(float)
     assert np.array_equal(plb.gae_soa(vals, rews, terms, 10, 20, 0.995, 0.9), O.gae_soa(vals, rews, terms, 10, 20, 0.995, 0.9))
+
+
+# ---------------------------------------------------------------- Lean adapter (libpufferlean_lean.so)
+LEAN_LIB = os.path.join(os.path.dirname(plb.LIB_PATH), "libpufferlean_lean.so")
+
+
+def test_lean_adapter_exports_every_declared_symbol():
+    lib = C.CDLL(LEAN_LIB)
+    names = declared("pufferlean_lean.h")
+    assert len(names) >= 15
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_lean_adapter_host_bookkeeping_against_golden():
+    from oracle import oracle as O
+
+    lib = C.CDLL(LEAN_LIB)
+    g = np.load(os.path.join(ROOT, "tests", "golden", "shuffle.npz"))
+    for i in range(3):
+        NT, E, seed = (int(x) for x in g[f"args{i}"])
+        out = O.ref_call(lib, "lean_ffi_shuffle_perm", C.c_void_p, NT, E, ("u64", seed))
+        assert np.array_equal(O.read_float_array(out), g[f"perm{i}"])
+    g = np.load(os.path.join(ROOT, "tests", "golden", "gae.npz"))
+    N, T, gm, lm = g["meta"]
+    out = O.ref_call(lib, "lean_ffi_gae_soa", C.c_void_p, O.FA(g["vals"]), O.FA(g["rews"]), O.FA(g["terms"]), int(N),
+                     int(T), float(gm), float(lm))
+    assert np.array_equal(O.read_float_array(out), g["out"])
+
+
+def test_lean_adapter_pure_failure_is_nan_not_zero():
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is visible")
+    except ImportError:
+        pass
+    from oracle import oracle as O
+
+    lib = C.CDLL(LEAN_LIB)
+    out = O.ref_call(lib, "lean_cuda_vtrace", C.c_void_p, O.FA(np.zeros(6)), O.FA(np.zeros(6)), O.FA(np.zeros(6)),
+                     O.FA(np.ones(6)), 2, 3, 0.99, 0.95, 1.0, 1.0)
+    assert np.all(np.isnan(O.read_float_array(out)))
+    # IO functions report an IO error (constructor 1) instead
+    r = O.ref_call(lib, "lean_cuda_policy_load", C.c_void_p, O.FA(np.zeros(4)), 2, ("obj", 1))
+    assert O.ctor_tag(r) == 1
