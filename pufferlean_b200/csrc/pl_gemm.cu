@@ -1,6 +1,8 @@
 // Host side of the tcgen05 GEMM: TMA tensor maps, kernel-instance dispatch, launch.
 #include <cudaTypedefs.h>
 
+#include <string.h>
+
 #include <mutex>
 
 #include "pl_gemm.cuh"
@@ -8,7 +10,8 @@
 
 namespace pl {
 
-using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, int, int, int, EpiArgs);
+using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, int, int,
+                           int, EpiArgs);
 
 // Instance tables live in the pl_gemm_inst_*.cu translation units.
 GemmKernel gemm_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
@@ -48,6 +51,23 @@ static int make_map(CUtensorMap* map, const Operand& op, uint32_t box_rows) {
   return PL_OK;
 }
 
+// Store map of a bf16 output for the staged epilogue: {cols, rows, batch} with a {32, 32, 1} box, no
+// swizzle (the staging tile is dense row-major). Returns false when the output cannot take TMA
+// stores (alignment), in which case the epilogue writes directly.
+static bool make_store_map(CUtensorMap* map, const void* ptr, long rows, long cols, long ld, long batch, long bstride) {
+  auto enc = encode_fn();
+  if (!enc || !ptr || ((uintptr_t)ptr & 15) || (ld * 2) % 16 || ld < cols) return false;
+  if (batch > 1 && (bstride * 2) % 16) return false;
+  const long bs = batch > 1 ? bstride : ld * rows;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)(batch > 0 ? batch : 1)};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)((bs * 2 + 15) / 16 * 16)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const Operand& B, int M, int N, int K,
                 int batch, const EpiArgs& ep_in, cudaStream_t st) {
   PL_REQUIRE(M > 0 && N > 0 && K > 0, PL_ERR_INVALID, "GEMM with empty extent M=%d N=%d K=%d", M, N, K);
@@ -68,6 +88,18 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
   if (rc) return rc;
   EpiArgs ep = ep_in;
   if (!ep.err) ep.err = device_error_word();
+  CUtensorMap mc, mc2;
+  memset(&mc, 0, sizeof(mc));
+  memset(&mc2, 0, sizeof(mc2));
+  ep.tma_out = 0;
+  if (epi == EPI_FWD || epi == EPI_DGRAD || epi == EPI_BF16) {
+    bool ok = make_store_map(&mc, ep.out, ep.out_rows, ep.out_cols, ep.ldo, batch, ep.out_bstride);
+    if (ok && epi == EPI_FWD && ep.out2) ok = make_store_map(&mc2, ep.out2, ep.out_rows, ep.out_cols, ep.ldo2, 1, 0);
+    // the staged epilogue reads its aux tile with aligned 16-byte loads
+    if (ok && ep.aux && (((uintptr_t)ep.aux & 15) || (ep.ld_aux % 8) || (batch > 1 && (ep.aux_bstride % 8))))
+      ok = false;
+    ep.tma_out = ok ? 1 : 0;
+  }
   int splits = ep.k_splits > 1 ? ep.k_splits : 1;
   PL_REQUIRE(splits == 1 || batch == 1, PL_ERR_INVALID, "split-K and batching are exclusive");
   ep.nbatch = batch;
@@ -91,7 +123,7 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
       if (nconf < 256) configured[nconf++] = (void*)k;
     }
   }
-  k<<<grid, 320, smem, st>>>(ma, mb, M, N, K, ep);
+  k<<<grid, 320, smem, st>>>(ma, mb, mc, mc2, M, N, K, ep);
   count_launch();
   PL_LAUNCH("tc_gemm_kernel");
   return PL_OK;

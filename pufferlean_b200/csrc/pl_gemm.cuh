@@ -55,6 +55,7 @@ struct EpiArgs {
   unsigned* err;
   int k_splits;      // >1: the z index of a tile is its split-K slice; else its batch index
   int nbatch;        // number of stacked matrices (z extent when k_splits <= 1)
+  int tma_out;       // bf16 outputs leave through shared memory and TMA bulk stores (host-checked)
 };
 
 __device__ __forceinline__ float act_fwd(float z, int act) {
@@ -157,15 +158,24 @@ __device__ __forceinline__ float act_grad_fast(float z, int act) {
   return 0.5f * (1.f + t) + 0.5f * z * (1.f - t * t) * 0.7978845608028654f * (1.f + 3.f * 0.044715f * z * z);
 }
 
-template <int BN>
+// Shared memory: 1 KB alignment slack, the TMA ring, barriers, then the epilogue area: bf16 staging
+// tiles for the TMA bulk stores (per epilogue warp, one 32 x 32 tile per output) and the column
+// reduction scratch [4][BN] (+ per-warp loss partials). The ring takes what is left of 227 KB.
+template <int BN, int EPI>
 struct GemmSmem {
   static constexpr int BM = 128, BK = 64;
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
-  // ring + barriers + tmem slot + epilogue column-reduction scratch [4][BN] + row scratch
-  static constexpr uint32_t TOTAL = 1024 + STAGES * STAGE_BYTES + 256 + 4 * BN * 4 + 4 * 32 * 8 * 4;
+  static constexpr int NOUT = EPI == EPI_FWD ? 2 : ((EPI == EPI_DGRAD || EPI == EPI_BF16) ? 1 : 0);
+  static constexpr uint32_t STG_WARP = NOUT * 32 * 32 * 2;
+  static constexpr uint32_t STG_BYTES = 8 * STG_WARP;
+  static constexpr uint32_t RED_BYTES = (EPI == EPI_DGRAD || EPI == EPI_PPO) ? (4 * BN * 4 + 4 * 8 * 4) : 0;
+  static constexpr uint32_t FIXED = 1024 + 256 + STG_BYTES + RED_BYTES;
+  static constexpr int FIT = (int)((232448 - FIXED) / STAGE_BYTES);
+  static constexpr int STAGES = FIT > 8 ? 8 : FIT;
+  static constexpr uint32_t TOTAL = FIXED + STAGES * STAGE_BYTES;
+  static_assert(STAGES >= 2, "shared memory budget");
 };
 
 // Tile coordinates of linear tile t: n fastest (consecutive tiles share the A row-panel, which
@@ -184,10 +194,29 @@ __device__ __forceinline__ TileIdx tile_of(int t, int num_n, int num_m) {
 
 // Epilogue of one 128 x BN accumulator tile held in TMEM columns [tcol, tcol + BN).
 // Runs on the 4 epilogue warps; warp `sub` owns TMEM lanes / tile rows [32 sub, 32 sub + 32).
+// Writes this lane's 32 bf16 values (its row of a 32 x 32 tile) into a dense staging tile; the
+// 16-byte pieces go in a lane-rotated order so the 8 lanes of each store phase hit distinct banks.
+__device__ __forceinline__ void stage_row32(uint8_t* tile, int lane, const float (&v)[32]) {
+  uint4 w[4];
+  uint32_t* u = reinterpret_cast<uint32_t*>(w);
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+    u[j] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  uint4* row = reinterpret_cast<uint4*>(tile + lane * 64);
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int c = (j + (lane >> 1)) & 3;
+    row[c] = w[c];
+  }
+}
+
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row, int m_tile, int n_tile, int bz,
                                               int batch, bool have_acc, int sub, int half, int lane, float* red,
-                                              float* rowscr) {
+                                              float* rowscr, uint8_t* stg, const CUtensorMap* tmC,
+                                              const CUtensorMap* tmC2) {
   constexpr int BM = 128;
   const int row = m_tile * BM + sub * 32 + lane;
   const bool row_ok = row < ep.out_rows;
@@ -325,6 +354,92 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
     // this warp's half of the tile's columns, drained 32 at a time (two TMEM loads per wait)
     const int cb = half * (BN / 2), ce = cb + BN / 2;
     uint32_t rr[2][16];
+    constexpr bool STAGED_OK = (EPI == EPI_FWD || EPI == EPI_DGRAD || EPI == EPI_BF16);
+    if (STAGED_OK && ep.tma_out) {
+      // ---- staged path: 32 x 32 tiles through shared memory, TMA bulk stores (rows/cols past the
+      // logical extent are clipped by the tensor map). The bf16 aux row piece (Z for act', X for the
+      // Newton-Schulz axpby) is loaded one chunk ahead, so its latency hides under the current
+      // chunk's math and store.
+      const int row0 = m_tile * 128 + sub * 32;
+      constexpr bool HAS_AUX = (EPI == EPI_DGRAD || EPI == EPI_BF16);
+      const bool use_aux = HAS_AUX && ep.aux != nullptr && row_ok;
+      const __nv_bfloat16* aux_row =
+          use_aux ? ep.aux + (long)batch * ep.aux_bstride + (long)row * ep.ld_aux : nullptr;
+      uint4 pre[4];
+      auto prefetch = [&](int nc) {
+        if (nc + 32 <= ep.out_cols) {
+#pragma unroll
+          for (int i = 0; i < 4; i++) pre[i] = reinterpret_cast<const uint4*>(aux_row + nc)[i];
+        } else {
+          __align__(16) __nv_bfloat16 t[32];
+          for (int q = 0; q < 32; q++) t[q] = (nc + q < ep.out_cols) ? aux_row[nc + q] : __float2bfloat16_rn(0.f);
+#pragma unroll
+          for (int i = 0; i < 4; i++) pre[i] = reinterpret_cast<const uint4*>(t)[i];
+        }
+      };
+      if (use_aux && n_base + cb < ep.out_cols) prefetch(n_base + cb);
+      for (int c32 = cb; c32 < ce; c32 += 32) {
+        const int n0 = n_base + c32;
+        if (n0 >= ep.out_cols) break;  // warp-uniform
+        tc::tmem_ld16(t_row + c32, rr[0]);
+        tc::tmem_ld16(t_row + c32 + 16, rr[1]);
+        float aux[32];
+        if (use_aux) {
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(pre);
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            const float2 f = __bfloat1622float2(h[j]);
+            aux[2 * j] = f.x;
+            aux[2 * j + 1] = f.y;
+          }
+          if (c32 + 32 < ce && n0 + 32 < ep.out_cols) prefetch(n0 + 32);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j++) aux[j] = 0.f;
+        }
+        tc::tmem_wait_ld();
+        float v[32], z[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const float acc = have_acc ? __uint_as_float(rr[j >> 4][j & 15]) : 0.f;
+          if constexpr (EPI == EPI_FWD) {
+            z[j] = acc + ((n0 + j) < ep.out_cols ? ep.bias[n0 + j] : 0.f);
+            v[j] = act_fwd_fast(z[j], ep.act);
+          } else if constexpr (EPI == EPI_DGRAD) {
+            v[j] = (row_ok && n0 + j < ep.out_cols) ? acc * act_grad_fast(aux[j], ep.act) : 0.f;
+          } else {
+            v[j] = ep.alpha * acc + (ep.aux ? ep.beta * aux[j] : 0.f);
+          }
+        }
+        if (lane == 0) tc::bulk_wait_read<0>();  // the previous tile's stores have read the staging area
+        __syncwarp();
+        stage_row32(stg, lane, v);
+        if constexpr (EPI == EPI_FWD) {
+          if (ep.out2) stage_row32(stg + 2048, lane, z);
+        }
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tc::tma_store_3d(tmC, stg, n0, row0, batch);
+          if constexpr (EPI == EPI_FWD) {
+            if (ep.out2) tc::tma_store_3d(tmC2, stg + 2048, n0, row0, batch);
+          }
+          tc::bulk_commit();
+        }
+        if constexpr (EPI == EPI_DGRAD) {
+          if (do_colsum) {
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+              float w16[16];
+#pragma unroll
+              for (int j = 0; j < 16; j++) w16[j] = v[16 * hh + j];
+              const float cs = warp_colsum16(w16, lane);
+              if ((lane & 1) == 0) red[sub * BN + c32 + 16 * hh + (lane >> 1)] = cs;
+            }
+          }
+        }
+      }
+    } else
     for (int c32 = cb; c32 < ce; c32 += 32) {
       if (n_base + c32 >= ep.out_cols) break;  // warp-uniform
       tc::tmem_ld16(t_row + c32, rr[0]);
@@ -402,9 +517,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
 // other: the epilogue of tile j overlaps the main loop of tile j+1.
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(320, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, int M, int N,
                    int K, EpiArgs ep) {
-  using S = GemmSmem<BN>;
+  using S = GemmSmem<BN, EPI>;
   constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES;
   constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
   constexpr uint32_t TMEM_COLS = 2 * BN;  // 128, 256 or 512: a power of two
@@ -418,8 +534,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-  float* red = (float*)(smem + STAGES * S::STAGE_BYTES + 256);  // [4][BN]
-  float* rowscr = red + 4 * BN;                                  // [4 warps][8]
+  uint8_t* stg_base = smem + STAGES * S::STAGE_BYTES + 256;                     // [8 warps][STG_WARP]
+  float* red = (float*)(stg_base + S::STG_BYTES);                               // [4][BN]
+  float* rowscr = red + 4 * BN;                                                 // [4 warps][8]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_n = (N + BN - 1) / BN, num_m = (M + BM - 1) / BM;
@@ -563,11 +680,14 @@ __global__ void __launch_bounds__(320, 1)
       tc::tc_fence_after();
       const uint32_t t_row = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(sub * 32) << 16);
       epilogue_tile<BN, EPI>(ep, t_row, ti.m, ti.n, ti.z, ep.k_splits > 1 ? 0 : ti.z, b1 > b0, sub, half, lane, red,
-                             rowscr);
+                             rowscr, stg_base + (warp - 2) * S::STG_WARP, &tmC, &tmC2);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&acc_empty[buf])) : "memory");
     }
+    // bulk stores must finish reading shared memory (and land) before the CTA retires
+    if (lane == 0) tc::bulk_wait<0>();
+    __syncwarp();
   }
   tc::tc_fence_before();
   __syncthreads();

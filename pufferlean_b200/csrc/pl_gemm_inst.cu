@@ -3,11 +3,12 @@
 
 namespace pl {
 
-using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, int, int, int, EpiArgs);
+using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, int, int,
+                           int, EpiArgs);
 
 template <int BN, bool AM, bool BM_, int EPI>
 static GemmKernel inst(uint32_t* smem) {
-  *smem = GemmSmem<BN>::TOTAL;
+  *smem = GemmSmem<BN, EPI>::TOTAL;
   return &tc_gemm_kernel<BN, AM, BM_, EPI>;
 }
 
