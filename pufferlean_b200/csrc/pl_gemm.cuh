@@ -19,8 +19,8 @@
 namespace pl {
 
 enum EpiKind : int {
-  EPI_F32 = 0,    // out(f32)  = alpha*acc (+ beta*aux)            [wgrad, split-K partials, tests]
-  EPI_BF16 = 1,   // out(bf16) = alpha*acc (+ beta*aux)            [Newton-Schulz chain]
+  EPI_F32 = 0,    // out(f32)  = alpha*acc (+ beta*aux) (+ diag*I)  [wgrad, split-K partials, tests]
+  EPI_BF16 = 1,   // out(bf16) = alpha*acc (+ beta*aux) (+ diag*I)  [Newton-Schulz chain]
   EPI_FWD = 2,    // z = acc + bias; out(bf16) = act(z); out2(bf16) = z (GELU only)
   EPI_DGRAD = 3,  // out(bf16) = acc * act'(aux); column partial sums of it  [bias grads]
   EPI_PPO = 4,    // logits+value = acc + bias -> PPO objective gradient dOut(bf16) + column sums
@@ -56,6 +56,7 @@ struct EpiArgs {
   int k_splits;      // >1: the z index of a tile is its split-K slice; else its batch index
   int nbatch;        // number of stacked matrices (z extent when k_splits <= 1)
   int tma_out;       // bf16 outputs leave through shared memory and TMA bulk stores (host-checked)
+  float diag;        // EPI_F32 / EPI_BF16: added on the diagonal (row == column) of every matrix
 };
 
 __device__ __forceinline__ float act_fwd(float z, int act) {
@@ -408,7 +409,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
           } else if constexpr (EPI == EPI_DGRAD) {
             v[j] = (row_ok && n0 + j < ep.out_cols) ? acc * act_grad_fast(aux[j], ep.act) : 0.f;
           } else {
-            v[j] = ep.alpha * acc + (ep.aux ? ep.beta * aux[j] : 0.f);
+            v[j] = ep.alpha * acc + (ep.aux ? ep.beta * aux[j] : 0.f) + (row == n0 + j ? ep.diag : 0.f);
           }
         }
         if (lane == 0) tc::bulk_wait_read<0>();  // the previous tile's stores have read the staging area
@@ -462,7 +463,8 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
                             (ep.ld_aux % 8) == 0);
           }
 #pragma unroll
-          for (int j = 0; j < 16; j++) v[j] = ep.alpha * v[j] + (ep.aux ? ep.beta * x[j] : 0.f);
+          for (int j = 0; j < 16; j++)
+            v[j] = ep.alpha * v[j] + (ep.aux ? ep.beta * x[j] : 0.f) + (row == n0 + j ? ep.diag : 0.f);
           const long off = (long)bz * ep.out_bstride + (long)row * ep.ldo + n0;
           if constexpr (EPI == EPI_F32)
             store_row16_f32((float*)ep.out + off, v, nvalid, (ep.ldo % 4) == 0);

@@ -25,8 +25,16 @@ struct NsWork {
   unsigned* err = nullptr;  // bounded-wait error word for the GEMMs (NULL = the per-device default)
 };
 
+// final_bf16 (optional): the last step's bf16 output goes there (not an iterate buffer) instead of
+// back into X; result_at (optional): receives the iterate buffer that holds the bf16 result, and X
+// is then left as it is.
 int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
-                   long xbs, float* out_f32, long ld_out, long obs, cudaStream_t st);
+                   long xbs, float* out_f32, long ld_out, long obs, cudaStream_t st,
+                   __nv_bfloat16* final_bf16 = nullptr, __nv_bfloat16** result_at = nullptr);
+// Normalised wide-layout copy of a batch of row-major bf16 matrices (pl_ns.cu).
+long ns_prepare_parts(long per);
+int launch_ns_prepare(const __nv_bfloat16* X, long batch, int rows, int cols, double eps, double* part,
+                      __nv_bfloat16* dst, cudaStream_t st);
 int ns_run(int m, int n, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx, float* out_f32,
            long ld_out, cudaStream_t st);
 

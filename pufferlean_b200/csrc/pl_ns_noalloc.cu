@@ -9,7 +9,8 @@
 //
 // Limit: kNoAllocBytes (32 MiB) per device, which every GPU that loads the library holds until the
 // process exits. The workspace needs 2*batch*m*n + 2*batch*m*m bf16 values (m = min(rows, cols),
-// n = max(rows, cols)) plus 256 bytes; larger requests are rejected with PL_ERR_INVALID.
+// n = max(rows, cols)), one double per 16384 elements of every matrix for the norm, and 256 bytes;
+// larger requests are rejected with PL_ERR_INVALID.
 //
 // Sharing: every call on a device uses the same array and leaves its contents behind, so two calls
 // whose work overlaps on the GPU (different streams, or different host threads) race on it and
@@ -25,7 +26,6 @@
 #include "pl_runtime.h"
 
 namespace pl {
-int launch_ns_normalize(__nv_bfloat16* X, long batch, long per, double eps, cudaStream_t st);
 int launch_transpose_bf16(const __nv_bfloat16* src, long batch, int rows, int cols, __nv_bfloat16* dst,
                           cudaStream_t st);
 }  // namespace pl
@@ -65,7 +65,8 @@ extern "C" int pl_ns_batched_bf16_dev_noalloc(void* Xv, size_t batch, size_t row
   const int m = (int)(rows < cols ? rows : cols), n = (int)(rows < cols ? cols : rows);
   const long per = (long)m * n;
   const size_t xbytes = align256((size_t)per * batch * 2), gbytes = align256((size_t)m * m * batch * 2);
-  const size_t need = 256 + 2 * xbytes + 2 * gbytes;
+  const size_t pbytes = align256((size_t)batch * ns_prepare_parts(per) * sizeof(double));
+  const size_t need = 256 + 2 * xbytes + 2 * gbytes + pbytes;
   PL_REQUIRE(need <= kNoAllocBytes, PL_ERR_INVALID,
              "no-alloc Newton-Schulz: %zu matrices of %zux%zu need %zu bytes of workspace, above the fixed %zu-byte "
              "limit (use pl_ns_batched_bf16_dev, which allocates)",
@@ -81,23 +82,18 @@ extern "C" int pl_ns_batched_bf16_dev_noalloc(void* Xv, size_t batch, size_t row
   w.X1 = (__nv_bfloat16*)(b + 256 + xbytes);
   w.G = (__nv_bfloat16*)(b + 256 + 2 * xbytes);
   w.B = (__nv_bfloat16*)(b + 256 + 2 * xbytes + gbytes);
+  double* part = (double*)(b + 256 + 2 * xbytes + 2 * gbytes);
   w.ldx = n;
   w.ldg = m;
   PL_CUDA(cudaMemsetAsync(w.err, 0, sizeof(unsigned), st));
   __nv_bfloat16* X = (__nv_bfloat16*)Xv;
   const bool tall = rows > cols;
-  if (tall)
-    rc = launch_transpose_bf16(X, (long)batch, (int)rows, (int)cols, w.X0, st);
-  else
-    rc = cudaMemcpyAsync(w.X0, X, (size_t)per * batch * 2, cudaMemcpyDeviceToDevice, st) == cudaSuccess
-             ? PL_OK
-             : check_cuda(cudaGetLastError(), "cudaMemcpyAsync");
+  rc = launch_ns_prepare(X, (long)batch, (int)rows, (int)cols, eps, part, w.X0, st);
   if (rc) return rc;
-  rc = launch_ns_normalize(w.X0, (long)batch, per, eps, st);
+  __nv_bfloat16* res = nullptr;
+  rc = ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, w.X0, n, per, nullptr, 0, 0, st, tall ? nullptr : X,
+                      &res);
   if (rc) return rc;
-  rc = ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, w.X0, n, per, nullptr, 0, 0, st);
-  if (rc) return rc;
-  if (tall) return launch_transpose_bf16(w.X0, (long)batch, (int)cols, (int)rows, X, st);
-  PL_CUDA(cudaMemcpyAsync(X, w.X0, (size_t)per * batch * 2, cudaMemcpyDeviceToDevice, st));
+  if (tall) return launch_transpose_bf16(res, (long)batch, (int)cols, (int)rows, X, st);
   return PL_OK;
 }
