@@ -181,3 +181,62 @@ def synthetic_rollout(N: int, T: int, D: int, A: int, seed: int, obs_kind: str =
         rew = g.standard_normal(NT)
     term = (g.random(NT) < done_p).astype(np.float64)
     return obs, acts, rew, term
+
+
+def kat_mingru_grad():
+    """verify-mingru-grad-gpu (Exe/Puffer.lean:2398-2440): D=5 H=32 L=3 A=4 T=7, B=2 sequences, initMinGRU
+    seed 0x6A5D, a terminal at t=3 in every sequence; vf .5 ent .01 clip .2 vfClip .2. Returns the
+    per-sequence arrays and the time-major packing the batched kernel takes."""
+    from oracle import oracle as O
+
+    D, H, L, A, T, B = 5, 32, 3, 4, 7, 2
+    params, s = O.init_mingru(D, H, L, A, 0x6A5D)
+    rng = Rng(s)
+    seqs = {k: [] for k in ("obs", "act", "adv", "ret", "old", "term", "ov")}
+    for _ in range(B):
+        o, ac, ad, re, ol, tm, ov = [], [], [], [], [], [], []
+        for t in range(T):
+            for _ in range(D):
+                o.append(rng.randF(-1.0, 1.0))
+            ac.append(float(rng.next() % A))
+            ad.append(rng.randF(-1.0, 1.0))
+            re.append(rng.randF(0.0, 2.0))
+            ol.append(-1.0)
+            tm.append(1.0 if t == 3 else 0.0)
+            ov.append(rng.randF(-0.5, 0.5))
+        for k, v in zip(seqs, (o, ac, ad, re, ol, tm, ov)):
+            seqs[k].append(np.array(v))
+    obsTB = np.zeros(T * B * D)
+    scal = np.zeros(6 * T * B)
+    for b in range(B):
+        for t in range(T):
+            obsTB[(t * B + b) * D:(t * B + b + 1) * D] = seqs["obs"][b][t * D:(t + 1) * D]
+            for q, k in enumerate(("act", "adv", "ret", "old", "term", "ov")):
+                scal[q * T * B + t * B + b] = seqs[k][b][t]
+    return dict(D=D, H=H, L=L, A=A, T=T, B=B, K=3, vf=0.5, ent=0.01, clip=0.2, vfClip=0.2, params=params, seqs=seqs,
+                obsTB=obsTB, scal=scal)
+
+
+def kat_mingru_update(K=3, enc_act=0):
+    """A small whole MinGRU update (no reference verify mode exists for it): N=12 segments x T=6, D=5 H=16 L=2
+    A=3, 3 minibatches of 4 sampled segments, seed 0x3617. Rewards U(-1,1), dones Bernoulli(.15), actions
+    uniform, old log-probs U(-2,-0.5), values U(-1,1), bootstrap U(-1,1); initMinGRU(0x6A5E)."""
+    from oracle import oracle as O
+
+    N, T, D, H, L, A = 12, 6, 5, 16, 2, 3
+    params, _ = O.init_mingru(D, H, L, A, 0x6A5E, K)
+    rng = Rng(0x3617)
+    NT = N * T
+    obs = np.array([rng.randF(0.0, 1.0) for _ in range(NT * D)])
+    rew = np.array([rng.randF(-1.0, 1.0) for _ in range(NT)])
+    term = np.array([1.0 if rng.randF(0.0, 1.0) < 0.15 else 0.0 for _ in range(NT)])
+    act = np.array([float(rng.next() % A) for _ in range(NT)])
+    logp = np.array([rng.randF(-2.0, -0.5) for _ in range(NT)])
+    val0 = np.array([rng.randF(-1.0, 1.0) for _ in range(NT)])
+    boot = np.array([rng.randF(-1.0, 1.0) for _ in range(N)])
+    P = params.size
+    pm0 = np.concatenate([params, np.zeros(P)])
+    return dict(N=N, T=T, D=D, H=H, L=L, A=A, K=K, enc_act=enc_act, numMB=3, mbSegs=4, rng=0xC0FFEE, lr=0.02,
+                gamma=0.995, lam=0.90, rho=1.0, c=1.0, alpha=0.8, beta=0.2, wd=0.0, mu=0.95, eps=1e-7, vf=0.5,
+                ent=0.01, clip=0.2, vfClip=0.2, maxGradNorm=1.5, pm0=pm0, obs=obs, rew=rew, term=term, act=act,
+                logp=logp, val0=val0, boot=boot)

@@ -72,6 +72,18 @@ def orc():
         lib.orc_init_mlp.argtypes = [_sz, _sz, _sz, C.c_uint64, _dp]
         lib.orc_cosine_lr.restype = _d
         lib.orc_cosine_lr.argtypes = [_d, _d, _sz, _sz]
+        lib.orc_mg_param_count.restype = _sz
+        lib.orc_mg_param_count.argtypes = [_sz] * 5
+        lib.orc_mingru_grad_seq.argtypes = [_dp] * 8 + [_sz] * 6 + [C.c_int] + [_d] * 4 + [_dp] * 3
+        lib.orc_mingru_grad_batch.argtypes = [_dp] * 3 + [_sz] * 7 + [C.c_int] + [_d] * 4 + [_dp]
+        lib.orc_prio_sample.argtypes = [_dp, _sz, _sz, _d, _d, C.c_uint64, _dp, _dp]
+        lib.orc_gather_seq_minibatch.argtypes = [_dp] * 7 + [_sz, _sz, _dp]
+        lib.orc_apply_muon_mg.argtypes = [_dp, _dp] + [_sz] * 5 + [_d] * 4 + [_dp, C.c_int]
+        lib.orc_mingru_update.restype = C.c_uint64
+        lib.orc_mingru_update.argtypes = ([_dp] * 8 + [_sz] * 7 + [C.c_int] + [_sz] * 2 + [_d] * 6 + [C.c_uint64]
+                                          + [_d] * 9 + [_dp, C.c_int])
+        lib.orc_init_mingru.restype = C.c_uint64
+        lib.orc_init_mingru.argtypes = [_sz] * 5 + [C.c_uint64, _dp]
         _ORC = lib
     return _ORC
 
@@ -205,6 +217,73 @@ def init_mlp(din, H, dout, seed):
 
 def cosine_lr(lr, min_ratio, u, updates):
     return float(orc().orc_cosine_lr(lr, min_ratio, u, updates))
+
+
+# ---------------------------------------------------------------------------------------------
+# MinGRU (flattenMG layout; K = 3 is the reference layer, K = 2 the gate+candidate variant)
+def mg_param_count(D, H, L, A, K=3):
+    return int(orc().orc_mg_param_count(D, H, L, A, K))
+
+
+def init_mingru(D, H, L, A, seed, K=3):
+    flat = np.zeros(mg_param_count(D, H, L, A, K))
+    s = orc().orc_init_mingru(D, H, L, A, K, C.c_uint64(seed & 0xFFFFFFFFFFFFFFFF), _ptr(flat))
+    return flat, int(s)
+
+
+def mingru_grad_seq(params, obs, acts, advs, rets, olps, terms, ovs, T, H, D, L, A, K=3, enc_act=0, vf=0.5, ent=0.01,
+                    clip=0.2, vfClip=0.2):
+    P = mg_param_count(D, H, L, A, K)
+    g, nl, nv = np.zeros(P), np.zeros(T), np.zeros(T)
+    arrs = list(map(f64, (params, obs, acts, advs, rets, olps, terms, ovs)))
+    orc().orc_mingru_grad_seq(*[_ptr(a) for a in arrs], T, H, D, L, A, K, enc_act, vf, ent, clip, vfClip, _ptr(g),
+                              _ptr(nl), _ptr(nv))
+    return g, nl, nv
+
+
+def mingru_grad_batch(params, obsTB, scal, B, T, H, D, L, A, K=3, enc_act=0, vf=0.5, ent=0.01, clip=0.2, vfClip=0.2):
+    """[g(P); newlp(T*B); newval(T*B)] for B time-major packed sequences (scal = [act|adv|ret|old|term|ov])."""
+    P = mg_param_count(D, H, L, A, K)
+    out = np.zeros(P + 2 * T * B)
+    params, obsTB, scal = map(f64, (params, obsTB, scal))
+    orc().orc_mingru_grad_batch(_ptr(params), _ptr(obsTB), _ptr(scal), B, T, H, D, L, A, K, enc_act, vf, ent, clip,
+                                vfClip, _ptr(out))
+    return out
+
+
+def prio_sample(advL1, N, mbSegs, alpha, beta, rng):
+    seg, mp = np.zeros(mbSegs), np.zeros(mbSegs)
+    advL1 = f64(advL1)
+    orc().orc_prio_sample(_ptr(advL1), N, mbSegs, alpha, beta, C.c_uint64(rng & 0xFFFFFFFFFFFFFFFF), _ptr(seg),
+                          _ptr(mp))
+    return seg, mp
+
+
+def gather_seq_minibatch(act, logp, term, adv, value, seg, mbPrio, T, Bmb):
+    out = np.zeros(6 * T * Bmb)
+    arrs = list(map(f64, (act, logp, term, adv, value, seg, mbPrio)))
+    orc().orc_gather_seq_minibatch(*[_ptr(a) for a in arrs], T, Bmb, _ptr(out))
+    return out
+
+
+def apply_muon_mg(pm, g, D, H, L, A, lr, wd, mu, eps, K=3, coeffs=MUON_COEFFS):
+    pm = f64(pm).copy()
+    g, co = f64(g), f64(coeffs)
+    orc().orc_apply_muon_mg(_ptr(pm), _ptr(g), D, H, L, A, K, lr, wd, mu, eps, _ptr(co), co.shape[0])
+    return pm
+
+
+def mingru_update(pm, obs, rew, term, act, logp, val0, boot, N, T, D, H, L, A, numMB, mbSegs, rng, lr, K=3,
+                  enc_act=0, gamma=0.995, lam=0.90, rho=1.0, c=1.0, alpha=0.8, beta=0.2, wd=0.0, mu=0.95, eps=1e-7,
+                  vf=0.5, ent=0.01, clip=0.2, vfClip=0.2, maxGradNorm=1.5, coeffs=MUON_COEFFS):
+    """One whole MinGRU update (orc_mingru_update); returns (pm', rng')."""
+    pm = f64(pm).copy()
+    arrs = list(map(f64, (obs, rew, term, act, logp, val0, boot)))
+    co = f64(coeffs)
+    r = orc().orc_mingru_update(_ptr(pm), *[_ptr(a) for a in arrs], N, T, D, H, L, A, K, enc_act, numMB, mbSegs, gamma,
+                                lam, rho, c, alpha, beta, C.c_uint64(rng & 0xFFFFFFFFFFFFFFFF), lr, wd, mu, eps, vf,
+                                ent, clip, vfClip, maxGradNorm, _ptr(co), co.shape[0])
+    return pm, int(r)
 
 
 # ---------------------------------------------------------------------------------------------

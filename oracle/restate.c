@@ -552,3 +552,499 @@ double orc_cosine_lr(double lr, double minLrRatio, size_t u, size_t updates) {
   double ratio = (double)u / (double)(updates > 1 ? updates : 1);
   return lrMin + 0.5 * (lr - lrMin) * (1.0 + cos(3.14159265358979323846 * ratio));
 }
+
+/* ---------------------------------------------------------------- MinGRU -------------------- */
+/* Parameter count of the flattenMG layout (Puffer/RL/MinGRUTrain.lean:282-292):
+ * [wEnc(H*D) | bEnc(H) | L x layer(K*H x H) | wDec(A*H) | bDec(A) | wVal(H) | bVal(1)].
+ * K = 3 is the reference's [hid | gate | proj] layer (Puffer/Net/MinGRU.lean:9-17); K = 2 drops the
+ * highway projection ([hid | gate], output = the scan state). */
+size_t orc_mg_param_count(size_t D, size_t H, size_t L, size_t A, size_t K) {
+  return H * D + H + L * K * H * H + A * H + A + H + 1;
+}
+
+static double orc_sig(double x) { return 1.0 / (1.0 + exp(-x)); }
+
+/* One sequence of the MinGRU PPO gradient with truncated BPTT: the reference's scalar C
+ * (ffi/pufferffi.c:763-876, lean_ffi_mingru_ppo_grad_seq) op for op for K = 3 and encAct = 0,
+ * generalised to K = 2 (no highway) and a GELU encoder (encAct = 1, Puffer/Net/Forward.lean:271-273).
+ * Zero initial state; the state resets to zero after a terminal step and no gradient flows back across
+ * it. g[P] is zeroed and receives this sequence's summed ascent gradient; newlp/newval (T each, may be
+ * NULL) receive the taken action's log-prob and the value at every step. */
+void orc_mingru_grad_seq(const double* params, const double* obsAll, const double* actA, const double* advA,
+                         const double* retA, const double* oldA, const double* termA, const double* ovA, size_t T,
+                         size_t H, size_t D, size_t L, size_t A, size_t K, int encAct, double vfCoef,
+                         double entCoef, double clipEps, double vfClip, double* g, double* newlp, double* newval) {
+  const size_t wEncSz = H * D, layerSz = K * H * H;
+  const size_t P = orc_mg_param_count(D, H, L, A, K);
+  const double* wEnc = params;
+  const double* bEnc = params + wEncSz;
+  const double* layersBase = params + wEncSz + H;
+  const double* wDec = layersBase + L * layerSz;
+  const double* bDec = wDec + A * H;
+  const double* wVal = bDec + A;
+  const double* bVal = wVal + H;
+  for (size_t i = 0; i < P; i++) g[i] = 0.0;
+  double* gWEnc = g;
+  double* gBEnc = g + wEncSz;
+  double* gLayers = g + wEncSz + H;
+  double* gWDec = gLayers + L * layerSz;
+  double* gBDec = gWDec + A * H;
+  double* gWVal = gBDec + A;
+  double* gBVal = gWVal + H;
+  const size_t TLH = T * L * H;
+  double* hin = (double*)malloc(sizeof(double) * TLH);
+  double* prevS = (double*)malloc(sizeof(double) * TLH);
+  double* hidA = (double*)malloc(sizeof(double) * TLH);
+  double* gateA = (double*)malloc(sizeof(double) * TLH);
+  double* projA = (double*)malloc(sizeof(double) * TLH);
+  double* oA = (double*)malloc(sizeof(double) * TLH);
+  double* zEnc = (double*)malloc(sizeof(double) * T * H);
+  double* hfin = (double*)malloc(sizeof(double) * T * H);
+  double* lg = (double*)malloc(sizeof(double) * T * A);
+  double* val = (double*)malloc(sizeof(double) * T);
+  double* st = (double*)calloc(L * H, sizeof(double));
+  double* hb = (double*)malloc(sizeof(double) * H);
+  double* yb = (double*)malloc(sizeof(double) * K * H);
+  double* hnew = (double*)malloc(sizeof(double) * H);
+  for (size_t t = 0; t < T; t++) {
+    const double* obs = obsAll + t * D;
+    for (size_t i = 0; i < H; i++) {
+      double acc = 0.0;
+      const double* w = wEnc + i * D;
+      for (size_t k = 0; k < D; k++) acc += w[k] * obs[k];
+      double z = bEnc[i] + acc;
+      zEnc[t * H + i] = z;
+      hb[i] = encAct ? orc_act(z, 1) : z;
+    }
+    for (size_t l = 0; l < L; l++) {
+      const double* Wl = layersBase + l * layerSz;
+      size_t base = (t * L + l) * H;
+      for (size_t j = 0; j < H; j++) {
+        hin[base + j] = hb[j];
+        prevS[base + j] = st[l * H + j];
+      }
+      for (size_t r = 0; r < K * H; r++) {
+        double acc = 0.0;
+        const double* w = Wl + r * H;
+        for (size_t j = 0; j < H; j++) acc += w[j] * hb[j];
+        yb[r] = acc;
+      }
+      for (size_t j = 0; j < H; j++) {
+        double hidj = yb[j], gatej = yb[H + j], projj = K == 3 ? yb[2 * H + j] : 0.0;
+        double zj = orc_sig(gatej);
+        double gj = (hidj >= 0.0) ? (hidj + 0.5) : orc_sig(hidj);
+        double prevj = st[l * H + j];
+        double oj = (1.0 - zj) * prevj + zj * gj;
+        if (K == 3) {
+          double hgj = orc_sig(projj);
+          hnew[j] = hgj * oj + (1.0 - hgj) * hb[j];
+        } else {
+          hnew[j] = oj;
+        }
+        hidA[base + j] = hidj;
+        gateA[base + j] = gatej;
+        projA[base + j] = projj;
+        oA[base + j] = oj;
+        st[l * H + j] = oj;
+      }
+      for (size_t j = 0; j < H; j++) hb[j] = hnew[j];
+    }
+    for (size_t j = 0; j < H; j++) hfin[t * H + j] = hb[j];
+    for (size_t k = 0; k < A; k++) {
+      double acc = 0.0;
+      const double* w = wDec + k * H;
+      for (size_t j = 0; j < H; j++) acc += w[j] * hb[j];
+      lg[t * A + k] = bDec[k] + acc;
+    }
+    {
+      double acc = 0.0;
+      for (size_t j = 0; j < H; j++) acc += wVal[j] * hb[j];
+      val[t] = bVal[0] + acc;
+    }
+    if (termA[t] != 0.0)
+      for (size_t x = 0; x < L * H; x++) st[x] = 0.0;
+  }
+  double* dOnext = (double*)calloc(L * H, sizeof(double));
+  double* dprev = (double*)malloc(sizeof(double) * L * H);
+  double* dhn = (double*)malloc(sizeof(double) * H);
+  double* dhin = (double*)malloc(sizeof(double) * H);
+  double* dhf = (double*)malloc(sizeof(double) * H);
+  double* dyh = (double*)malloc(sizeof(double) * H);
+  double* dyg = (double*)malloc(sizeof(double) * H);
+  double* dyp = (double*)malloc(sizeof(double) * H);
+  double* pk = (double*)malloc(sizeof(double) * A);
+  for (size_t tt = T; tt-- > 0;) {
+    size_t t = tt;
+    const double* obs = obsAll + t * D;
+    const double* logits = lg + t * A;
+    double sumexp = 0.0;
+    for (size_t k = 0; k < A; k++) sumexp += exp(logits[k]);
+    double lse = log(sumexp);
+    double pout = 0.0;
+    for (size_t k = 0; k < A; k++) {
+      pk[k] = exp(logits[k] - lse);
+      pout += pk[k] * logits[k];
+    }
+    size_t a = (size_t)actA[t];
+    double adv = advA[t], ret = retA[t], oldLogp = oldA[t], vold = ovA[t];
+    double logpA = logits[a] - lse;
+    double ratio = exp(logpA - oldLogp);
+    double lo = 1.0 - clipEps, hi = 1.0 + clipEps;
+    double ratioC = ratio < lo ? lo : (ratio > hi ? hi : ratio);
+    double surr1 = adv * ratio, surr2 = adv * ratioC;
+    double dPol;
+    if (surr1 <= surr2)
+      dPol = adv * ratio;
+    else {
+      double cg = (lo < ratio && ratio < hi) ? 1.0 : 0.0;
+      dPol = adv * cg * ratio;
+    }
+    double vnew = val[t], dvloss_dv;
+    if (vfClip > 0.0) {
+      double dd = vnew - vold;
+      double vclip = vold + (dd < -vfClip ? -vfClip : (dd > vfClip ? vfClip : dd));
+      double du = (vnew - ret) * (vnew - ret), cc = (vclip - ret) * (vclip - ret);
+      if (du >= cc)
+        dvloss_dv = (vnew - ret);
+      else if (dd > -vfClip && dd < vfClip)
+        dvloss_dv = (vnew - ret);
+      else
+        dvloss_dv = 0.0;
+    } else {
+      dvloss_dv = (vnew - ret);
+    }
+    double dvalue = -vfCoef * dvloss_dv;
+    if (newlp) newlp[t] = logpA;
+    if (newval) newval[t] = vnew;
+    const double* hf = hfin + t * H;
+    for (size_t j = 0; j < H; j++) dhf[j] = 0.0;
+    for (size_t k = 0; k < A; k++) {
+      double dl = dPol * (((k == a) ? 1.0 : 0.0) - pk[k]) + entCoef * pk[k] * (pout - logits[k]);
+      double* gw = gWDec + k * H;
+      const double* w = wDec + k * H;
+      for (size_t j = 0; j < H; j++) {
+        gw[j] += dl * hf[j];
+        dhf[j] += dl * w[j];
+      }
+      gBDec[k] += dl;
+    }
+    for (size_t j = 0; j < H; j++) {
+      gWVal[j] += dvalue * hf[j];
+      dhf[j] += dvalue * wVal[j];
+    }
+    gBVal[0] += dvalue;
+    for (size_t j = 0; j < H; j++) dhn[j] = dhf[j];
+    for (size_t ll = L; ll-- > 0;) {
+      size_t l = ll;
+      size_t base = (t * L + l) * H;
+      const double* Wl = layersBase + l * layerSz;
+      double* Wg = gLayers + l * layerSz;
+      for (size_t j = 0; j < H; j++) dhin[j] = 0.0;
+      for (size_t j = 0; j < H; j++) {
+        double hidj = hidA[base + j], gatej = gateA[base + j], projj = projA[base + j], oj = oA[base + j],
+               prevj = prevS[base + j], hinj = hin[base + j];
+        double zj = orc_sig(gatej);
+        double gj = (hidj >= 0.0) ? (hidj + 0.5) : orc_sig(hidj);
+        double dhnj = dhn[j];
+        double do_;
+        if (K == 3) {
+          double hgj = orc_sig(projj);
+          double dhg = dhnj * (oj - hinj);
+          do_ = dhnj * hgj + dOnext[l * H + j];
+          dhin[j] += dhnj * (1.0 - hgj);
+          dyp[j] = dhg * hgj * (1.0 - hgj);
+        } else {
+          do_ = dhnj + dOnext[l * H + j];
+          dyp[j] = 0.0;
+        }
+        double dz = do_ * (gj - prevj);
+        dprev[l * H + j] = do_ * (1.0 - zj);
+        double dg = do_ * zj;
+        double dgate = dz * zj * (1.0 - zj);
+        double sg;
+        if (hidj >= 0.0)
+          sg = 1.0;
+        else {
+          double s = orc_sig(hidj);
+          sg = s * (1.0 - s);
+        }
+        dyh[j] = dg * sg;
+        dyg[j] = dgate;
+      }
+      for (size_t j = 0; j < H; j++) {
+        double dh_ = dyh[j];
+        double* gw = Wg + j * H;
+        const double* w = Wl + j * H;
+        for (size_t k = 0; k < H; k++) {
+          gw[k] += dh_ * hin[base + k];
+          dhin[k] += dh_ * w[k];
+        }
+        double dga = dyg[j];
+        double* gw2 = Wg + (H + j) * H;
+        const double* w2 = Wl + (H + j) * H;
+        for (size_t k = 0; k < H; k++) {
+          gw2[k] += dga * hin[base + k];
+          dhin[k] += dga * w2[k];
+        }
+        if (K == 3) {
+          double dpr = dyp[j];
+          double* gw3 = Wg + (2 * H + j) * H;
+          const double* w3 = Wl + (2 * H + j) * H;
+          for (size_t k = 0; k < H; k++) {
+            gw3[k] += dpr * hin[base + k];
+            dhin[k] += dpr * w3[k];
+          }
+        }
+      }
+      for (size_t j = 0; j < H; j++) dhn[j] = dhin[j];
+    }
+    for (size_t i = 0; i < H; i++) {
+      double de = encAct ? dhn[i] * orc_act_grad(zEnc[t * H + i], 1) : dhn[i];
+      gBEnc[i] += de;
+      double* gw = gWEnc + i * D;
+      for (size_t k = 0; k < D; k++) gw[k] += de * obs[k];
+    }
+    if (t > 0) {
+      double gate_ = (termA[t - 1] == 0.0) ? 1.0 : 0.0;
+      for (size_t x = 0; x < L * H; x++) dOnext[x] = dprev[x] * gate_;
+    }
+  }
+  free(hin); free(prevS); free(hidA); free(gateA); free(projA); free(oA); free(zEnc); free(hfin); free(lg);
+  free(val); free(st); free(hb); free(yb); free(hnew); free(dOnext); free(dprev); free(dhn); free(dhin);
+  free(dhf); free(dyh); free(dyg); free(dyp); free(pk);
+}
+
+/* The batched form the device kernel computes: B sequences packed time-major ([t*B + b] for the
+ * scalars, [(t*B + b)*D + j] for obs; the layout of lean_cuda_mingru_ppo_grad, ffi/puffercuda.cu:5206),
+ * summed over b in order 0..B-1 of the per-sequence gradients (the verify-mingru-grad-gpu check,
+ * Exe/Puffer.lean:2398-2440). out = [g(P); newlp(T*B); newval(T*B)], the last two time-major. */
+void orc_mingru_grad_batch(const double* params, const double* obsTB, const double* scal, size_t B, size_t T,
+                           size_t H, size_t D, size_t L, size_t A, size_t K, int encAct, double vfCoef,
+                           double entCoef, double clipEps, double vfClip, double* out) {
+  const size_t P = orc_mg_param_count(D, H, L, A, K), nb = T * B;
+  double* gb = (double*)malloc(sizeof(double) * P);
+  double* so = (double*)malloc(sizeof(double) * T * D);
+  double* sc = (double*)malloc(sizeof(double) * 6 * T);
+  double* nl = (double*)malloc(sizeof(double) * T);
+  double* nv = (double*)malloc(sizeof(double) * T);
+  for (size_t i = 0; i < P; i++) out[i] = 0.0;
+  for (size_t b = 0; b < B; b++) {
+    for (size_t t = 0; t < T; t++) {
+      for (size_t j = 0; j < D; j++) so[t * D + j] = obsTB[(t * B + b) * D + j];
+      for (size_t q = 0; q < 6; q++) sc[q * T + t] = scal[q * nb + t * B + b];
+    }
+    orc_mingru_grad_seq(params, so, sc, sc + T, sc + 2 * T, sc + 3 * T, sc + 4 * T, sc + 5 * T, T, H, D, L, A, K,
+                        encAct, vfCoef, entCoef, clipEps, vfClip, gb, nl, nv);
+    for (size_t i = 0; i < P; i++) out[i] = out[i] + gb[i];
+    for (size_t t = 0; t < T; t++) {
+      out[P + t * B + b] = nl[t];
+      out[P + nb + t * B + b] = nv[t];
+    }
+  }
+  free(gb); free(so); free(sc); free(nl); free(nv);
+}
+
+/* Prioritised segment sampling (ffi/pufferffi.c:1094-1125, lean_ffi_prio_sample):
+ * w_e = exp(alpha log(L1_e + 1e-12)), p_e = (w_e + 1e-6)/(sum w + 1e-6), cum = prefix sum (sequential),
+ * draw i: u = uniform01(splitmix64(rng + (i+1) GOLD)) * total, idx = first e with cum_e >= u,
+ * mbPrio_i = exp(-beta log(N p_idx + 1e-12)). segIdx is written as doubles. */
+void orc_prio_sample(const double* advL1, size_t N, size_t mbSegs, double prioAlpha, double annealBeta,
+                     uint64_t rng, double* idxArr, double* mpArr) {
+  double* prioW = (double*)malloc(N * sizeof(double));
+  double* prioProbs = (double*)malloc(N * sizeof(double));
+  double* cum = (double*)malloc(N * sizeof(double));
+  double sumW = 0.0;
+  for (size_t e = 0; e < N; e++) {
+    double w = exp(prioAlpha * log(advL1[e] + 1e-12));
+    prioW[e] = w;
+    sumW += w;
+  }
+  double denom = sumW + 1e-6, acc = 0.0;
+  for (size_t e = 0; e < N; e++) {
+    double p = (prioW[e] + 1e-6) / denom;
+    prioProbs[e] = p;
+    acc += p;
+    cum[e] = acc;
+  }
+  double total = acc;
+  for (size_t i = 0; i < mbSegs; i++) {
+    uint64_t z = rng + (uint64_t)(i + 1) * ORC_GOLD;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    z = z ^ (z >> 31);
+    double u = (double)(z >> 11) / 9007199254740992.0 * total;
+    size_t lo = 0, hi = N;
+    while (lo < hi) {
+      size_t mid = (lo + hi) >> 1;
+      if (cum[mid] >= u)
+        hi = mid;
+      else
+        lo = mid + 1;
+    }
+    size_t idx = (lo < N) ? lo : (N - 1);
+    idxArr[i] = (double)idx;
+    mpArr[i] = exp((-annealBeta) * log((double)N * prioProbs[idx] + 1e-12));
+  }
+  free(prioW);
+  free(prioProbs);
+  free(cum);
+}
+
+/* MinGRU minibatch scalar gather (ffi/pufferffi.c:1137-1176, lean_ffi_gather_seq_minibatch):
+ * advMean / advStd over the Bmb*T sampled advantages (bi outer, t inner, population std), then for
+ * os = t*Bmb + bi, si = seg[bi]*T + t: act = (double)(u64)act[si], adv = mbPrio[bi]*(a - mean)/(std + 1e-8),
+ * ret = a + v, old = logp[si], term = term[si] > 0.5, ov = v. out = [act|adv|ret|old|term|ov] (6 * T * Bmb). */
+void orc_gather_seq_minibatch(const double* actCol, const double* logpCol, const double* termCol,
+                              const double* advFlat, const double* valueBuf, const double* segIdx,
+                              const double* mbPrio, size_t T, size_t Bmb, double* out) {
+  size_t nb = T * Bmb;
+  double navd = (double)(nb > 0 ? nb : 1), sum = 0.0;
+  for (size_t bi = 0; bi < Bmb; bi++) {
+    size_t e = (size_t)segIdx[bi];
+    const double* ab = advFlat + e * T;
+    for (size_t t = 0; t < T; t++) sum += ab[t];
+  }
+  double advMean = sum / navd, sq = 0.0;
+  for (size_t bi = 0; bi < Bmb; bi++) {
+    size_t e = (size_t)segIdx[bi];
+    const double* ab = advFlat + e * T;
+    for (size_t t = 0; t < T; t++) {
+      double d = ab[t] - advMean;
+      sq += d * d;
+    }
+  }
+  double advStd = sqrt(sq / navd);
+  double* pact = out;
+  double* padv = out + nb;
+  double* pret = out + 2 * nb;
+  double* pold = out + 3 * nb;
+  double* pterm = out + 4 * nb;
+  double* pov = out + 5 * nb;
+  double stde = advStd + 1e-8;
+  for (size_t bi = 0; bi < Bmb; bi++) {
+    size_t e = (size_t)segIdx[bi];
+    double mp = mbPrio[bi];
+    for (size_t t = 0; t < T; t++) {
+      size_t si = e * T + t, os = t * Bmb + bi;
+      double a = advFlat[si], v = valueBuf[si];
+      pact[os] = (double)(unsigned long long)actCol[si];
+      padv[os] = mp * (a - advMean) / stde;
+      pret[os] = a + v;
+      pold[os] = logpCol[si];
+      pov[os] = v;
+      pterm[os] = termCol[si] > 0.5 ? 1.0 : 0.0;
+    }
+  }
+}
+
+/* applyMuonMG (Puffer/RL/MinGRUTrain.lean:265-279): stepMat on wEnc, every layer, wDec and wVal; stepVec
+ * on bEnc, bDec, bVal. pm = [params(P); mom(P)] in the flattenMG layout, updated in place; g is the
+ * already-clipped gradient. */
+void orc_apply_muon_mg(double* pm, const double* g, size_t D, size_t H, size_t L, size_t A, size_t K, double lr,
+                       double wd, double mu, double eps, const double* coeffs, int iters) {
+  size_t P = orc_mg_param_count(D, H, L, A, K);
+  double* par = pm;
+  double* mom = pm + P;
+  size_t off = 0;
+  size_t nmat = L + 3;
+  for (size_t q = 0; q <= nmat; q++) {
+    size_t rows, cols, bias;
+    if (q == 0) { rows = H; cols = D; bias = H; }
+    else if (q <= L) { rows = K * H; cols = H; bias = 0; }
+    else if (q == L + 1) { rows = A; cols = H; bias = A; }
+    else if (q == L + 2) { rows = 1; cols = H; bias = 1; }
+    else break;
+    size_t n = rows * cols;
+    double* nW = (double*)malloc(sizeof(double) * n);
+    double* nM = (double*)malloc(sizeof(double) * n);
+    orc_muon_stepmat(par + off, g + off, mom + off, (int)rows, (int)cols, lr, wd, mu, eps, coeffs, iters, nW, nM);
+    memcpy(par + off, nW, sizeof(double) * n);
+    memcpy(mom + off, nM, sizeof(double) * n);
+    free(nW);
+    free(nM);
+    off += n;
+    if (bias) {
+      orc_muon_stepvec(par + off, g + off, mom + off, (int)bias, lr, wd, mu, par + off, mom + off);
+      off += bias;
+    }
+  }
+}
+
+/* One MinGRU update over the rollout columns (the per-minibatch chain of Puffer/RL/MinGRUTrain.lean:800-850
+ * with the device-resident prep of ffi/puffercuda.cu:316-507): value := val0, ratio := 1; then per
+ * minibatch: V-trace (MinGRU form, bootstrap boot) with the live ratio/value buffers -> adv, sum |adv| per
+ * segment -> prioritised sampling (rng advances by mbSegs*GOLD) -> scalar gather + obs sequences ->
+ * summed BPTT gradient over the sampled segments -> value/ratio iterate (the last sampler of a segment
+ * writes) -> gradClipMG with sc = 1/(Bmb*T) -> applyMuonMG. Columns are rows e*T + t; obs is
+ * [(e*T + t)*D + j]. pm = [params; mom] updated in place. Returns the advanced rng. */
+uint64_t orc_mingru_update(double* pm, const double* obs, const double* rew, const double* term, const double* act,
+                           const double* logp, const double* val0, const double* boot, size_t N, size_t T,
+                           size_t D, size_t H, size_t L, size_t A, size_t K, int encAct, size_t numMB,
+                           size_t mbSegs, double gamma, double lam, double rhoClip, double cClip, double prioAlpha,
+                           double annealBeta, uint64_t rng, double lr, double wd, double mu, double eps,
+                           double vfCoef, double entCoef, double clipEps, double vfClip, double maxGradNorm,
+                           const double* coeffs, int iters) {
+  const size_t NT = N * T, P = orc_mg_param_count(D, H, L, A, K);
+  double* value = (double*)malloc(sizeof(double) * NT);
+  double* ratio = (double*)malloc(sizeof(double) * NT);
+  double* adv = (double*)malloc(sizeof(double) * NT);
+  double* l1 = (double*)malloc(sizeof(double) * N);
+  double* seg = (double*)malloc(sizeof(double) * mbSegs);
+  double* mp = (double*)malloc(sizeof(double) * mbSegs);
+  double* sc = (double*)malloc(sizeof(double) * 6 * T * mbSegs);
+  double* obsTB = (double*)malloc(sizeof(double) * T * mbSegs * D);
+  double* gout = (double*)malloc(sizeof(double) * (P + 2 * T * mbSegs));
+  memcpy(value, val0, sizeof(double) * NT);
+  for (size_t i = 0; i < NT; i++) ratio[i] = 1.0;
+  for (size_t mb = 0; mb < numMB; mb++) {
+    orc_vtrace_mingru(rew, value, term, ratio, boot, N, T, gamma, lam, rhoClip, cClip, adv);
+    orc_adv_l1(adv, N, T, l1);
+    orc_prio_sample(l1, N, mbSegs, prioAlpha, annealBeta, rng, seg, mp);
+    rng += (uint64_t)mbSegs * ORC_GOLD;
+    orc_gather_seq_minibatch(act, logp, term, adv, value, seg, mp, T, mbSegs, sc);
+    for (size_t t = 0; t < T; t++)
+      for (size_t b = 0; b < mbSegs; b++) {
+        size_t e = (size_t)seg[b];
+        memcpy(obsTB + (t * mbSegs + b) * D, obs + (e * T + t) * D, sizeof(double) * D);
+      }
+    orc_mingru_grad_batch(pm, obsTB, sc, mbSegs, T, H, D, L, A, K, encAct, vfCoef, entCoef, clipEps, vfClip, gout);
+    for (size_t b = 0; b < mbSegs; b++) {
+      size_t e = (size_t)seg[b];
+      for (size_t t = 0; t < T; t++) {
+        size_t si = e * T + t, os = t * mbSegs + b;
+        ratio[si] = exp(gout[P + os] - logp[si]);
+        value[si] = gout[P + T * mbSegs + os];
+      }
+    }
+    orc_grad_clip(gout, P, maxGradNorm, 1.0 / (double)(mbSegs * T));
+    orc_apply_muon_mg(pm, gout, D, H, L, A, K, lr, wd, mu, eps, coeffs, iters);
+  }
+  free(value); free(ratio); free(adv); free(l1); free(seg); free(mp); free(sc); free(obsTB); free(gout);
+  return rng;
+}
+
+/* initMinGRU (Puffer/RL/MinGRUTrain.lean:311-344) flattened: wEnc bound sqrt(2)/sqrt(D), layers
+ * (K*H x H each) 1/sqrt(H), wDec and wVal 1/sqrt(H), biases zero. Returns the advanced state. */
+uint64_t orc_init_mingru(size_t D, size_t H, size_t L, size_t A, size_t K, uint64_t rng, double* flat) {
+  uint64_t s = rng;
+  double* p = flat;
+  orc_rand_mat(H, D, sqrt(2.0) * (1.0 / sqrt((double)D)), &s, p);
+  p += H * D;
+  for (size_t j = 0; j < H; j++) p[j] = 0.0;
+  p += H;
+  for (size_t l = 0; l < L; l++) {
+    orc_rand_mat(K * H, H, 1.0 / sqrt((double)H), &s, p);
+    p += K * H * H;
+  }
+  double* wDec = p;
+  p += A * H;
+  double* bDec = p;
+  p += A;
+  double* wVal = p;
+  p += H;
+  orc_rand_mat(A, H, 1.0 / sqrt((double)H), &s, wDec);
+  orc_rand_mat(1, H, 1.0 / sqrt((double)H), &s, wVal);
+  for (size_t k = 0; k < A; k++) bDec[k] = 0.0;
+  p[0] = 0.0;
+  return s;
+}

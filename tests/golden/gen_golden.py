@@ -145,6 +145,83 @@ def main():
     pr = ref_call(cpu, "lean_ffi_prio_sample", VP, FA(L1), N, 64, mbSegs, 0.8, 0.2, ("u64", 0xABCDEF))
     np.savez(os.path.join(OUT, "prio.npz"), L1=L1, idx=arr(O.ctor_field(pr, 0)), mbPrio=arr(O.ctor_field(pr, 1)),
              meta=np.array([N, 64, mbSegs, 0.8, 0.2, 0xABCDEF], dtype=np.float64))
+    # MinGRU: the per-sequence BPTT gradient (verify-mingru-grad-gpu inputs), the minibatch scalar gather,
+    # and one whole update composed from the reference's own C pieces
+    k = kat.kat_mingru_grad()
+    s = k["seqs"]
+    per = []
+    for b in range(k["B"]):
+        per.append(arr(ref_call(cpu, "lean_ffi_mingru_ppo_grad_seq", VP, FA(k["params"]), FA(s["obs"][b]),
+                                FA(s["act"][b]), FA(s["adv"][b]), FA(s["ret"][b]), FA(s["old"][b]), FA(s["term"][b]),
+                                FA(s["ov"][b]), k["T"], k["H"], k["D"], k["L"], k["A"], k["vf"], k["ent"], k["clip"],
+                                k["vfClip"])))
+    np.savez(os.path.join(OUT, "mingru_grad.npz"), params=k["params"], obsTB=k["obsTB"], scal=k["scal"],
+             seq0=per[0], seq1=per[1],
+             meta=np.array([k["D"], k["H"], k["L"], k["A"], k["T"], k["B"], k["vf"], k["ent"], k["clip"],
+                            k["vfClip"]]))
+
+    rng = kat.Rng(0x6A7)
+    N, T, D, Bmb = 10, 5, 3, 7
+    cols = {x: np.array([rng.randF(-1.0, 1.0) for _ in range(N * T)]) for x in ("adv", "value", "logp")}
+    cols["act"] = np.array([float(rng.next() % 4) for _ in range(N * T)])
+    cols["term"] = np.array([1.0 if rng.randF(0.0, 1.0) < 0.2 else 0.0 for _ in range(N * T)])
+    seg = np.array([float(rng.next() % N) for _ in range(Bmb)])
+    mbp = np.array([rng.randF(0.2, 1.5) for _ in range(Bmb)])
+    obsCol = np.zeros(N * T * D)
+    g = arr(ref_call(cpu, "lean_ffi_gather_seq_minibatch", VP, FA(obsCol), FA(cols["act"]), FA(cols["logp"]),
+                     FA(cols["term"]), FA(cols["adv"]), FA(cols["value"]), FA(seg), FA(mbp), T, Bmb, D, N))
+    np.savez(os.path.join(OUT, "gather_seq.npz"), out=g, seg=seg, mbPrio=mbp, meta=np.array([N, T, D, Bmb]), **cols)
+
+    k = kat.kat_mingru_update()
+    N, T, D, H, L, A, K = (k[x] for x in ("N", "T", "D", "H", "L", "A", "K"))
+    P = O.mg_param_count(D, H, L, A, K)
+    pm = k["pm0"].copy()
+    value, ratio = k["val0"].copy(), np.ones(N * T)
+    r = k["rng"]
+    Bmb = k["mbSegs"]
+    for _ in range(k["numMB"]):
+        adv = arr(ref_call(cfb, "lean_cuda_vtrace_mingru", VP, FA(k["rew"]), FA(value), FA(k["term"]), FA(ratio),
+                           FA(k["boot"]), N, T, k["gamma"], k["lam"], k["rho"], k["c"]))
+        l1 = O.adv_l1(adv, N, T)
+        pr = ref_call(cpu, "lean_ffi_prio_sample", VP, FA(l1), N, T, Bmb, k["alpha"], k["beta"], ("u64", r))
+        seg, mbp = arr(O.ctor_field(pr, 0)), arr(O.ctor_field(pr, 1))
+        r = (r + Bmb * kat.GOLD) & kat.M64
+        sc = arr(ref_call(cpu, "lean_ffi_gather_seq_minibatch", VP, FA(np.zeros(N * T * D)), FA(k["act"]),
+                          FA(k["logp"]), FA(k["term"]), FA(adv), FA(value), FA(seg), FA(mbp), T, Bmb, D, N))
+        nb = T * Bmb
+        g = np.zeros(P)
+        newlp, newval = np.zeros(nb), np.zeros(nb)
+        for b in range(Bmb):
+            e = int(seg[b])
+            obs_seq = k["obs"][e * T * D:(e + 1) * T * D]
+            cs = [sc[q * nb + b:(q + 1) * nb:Bmb] for q in range(6)]
+            gs = arr(ref_call(cpu, "lean_ffi_mingru_ppo_grad_seq", VP, FA(pm[:P]), FA(obs_seq), *[FA(x) for x in cs],
+                              T, H, D, L, A, k["vf"], k["ent"], k["clip"], k["vfClip"]))
+            g = g + gs[:P]
+            newlp[b::Bmb] = gs[P:P + T]
+            newval[b::Bmb] = gs[P + T:]
+        for b in range(Bmb):
+            e = int(seg[b])
+            for t in range(T):
+                ratio[e * T + t] = np.exp(newlp[t * Bmb + b] - k["logp"][e * T + t])
+                value[e * T + t] = newval[t * Bmb + b]
+        gc = O.grad_clip(g, k["maxGradNorm"], 1.0 / nb)
+        off = 0
+        shapes = [(H, D, H)] + [(K * H, H, 0)] * L + [(A, H, A), (1, H, 1)]
+        for rows, cols_, nbias in shapes:
+            n = rows * cols_
+            o = arr(ref_call(cfb, "lean_cuda_muon_stepmat", VP, FA(pm[off:off + n]), FA(gc[off:off + n]),
+                             FA(pm[P + off:P + off + n]), rows, cols_, k["lr"], k["wd"], k["mu"], k["eps"]))
+            pm[off:off + n], pm[P + off:P + off + n] = o[:n], o[n:]
+            off += n
+            if nbias:
+                nb_, nm_ = np.zeros(nbias), np.zeros(nbias)
+                O.orc().orc_muon_stepvec(O._ptr(pm[off:off + nbias].copy()), O._ptr(gc[off:off + nbias].copy()),
+                                         O._ptr(pm[P + off:P + off + nbias].copy()), nbias, k["lr"], k["wd"], k["mu"],
+                                         O._ptr(nb_), O._ptr(nm_))
+                pm[off:off + nbias], pm[P + off:P + off + nbias] = nb_, nm_
+                off += nbias
+    np.savez(os.path.join(OUT, "mingru_update.npz"), out=pm, rng_out=np.array([r], dtype=np.uint64))
     print("golden fixtures written to", OUT)
 
 
