@@ -238,6 +238,94 @@ int pl_comm_destroy(void* comm);
  * longest-processing-time by 4 m^2 n + 2 m^3 flops. Deterministic. */
 int pl_muon_shard_plan(const size_t* rows, const size_t* cols, size_t nmat, int world, int* owner);
 
+/* ------------------------------------------------------------------ MinGRU (recurrent) path ----- */
+/* The network of Puffer/Net/MinGRU.lean:9-17 in the flattenMG layout (Puffer/RL/MinGRUTrain.lean:282-292):
+ * [wEnc(H*D) | bEnc(H) | L x layer(K*H x H) | wDec(A*H) | bDec(A) | wVal(H) | bVal(1)].
+ * K = 3: [hid | gate | proj] with the highway output (the reference); K = 2: [hid | gate], the output is
+ * the scan state. enc_act 0: linear encoder (the reference); 1: GELU after the encoder. */
+typedef struct {
+  size_t D, H, L, A, K;
+  int enc_act;
+} pl_mg_net;
+size_t pl_mg_param_count(const pl_mg_net* net);
+
+/* Host-buffer BPTT gradient: B sequences of T steps packed time-major (obs [(t*B+b)*D + j], scal =
+ * [act | adv | ret | old | term | ov] each [t*B + b]); zero initial state, state reset after a terminal.
+ * out = [summed ascent gradient (P); new log-prob (T*B); new value (T*B)].
+ * bf16 = 0: fp32 GEMMs and activations; 1: bf16 tensor-core GEMMs (fp32 accumulate), bf16 activations.
+ * Replaces the host mode of lean_cuda_mingru_ppo_grad (ffi/puffercuda.cu:5206-5622). */
+int pl_mingru_ppo_grad(const double* params, const double* obs, const double* scal, size_t B, size_t T,
+                       const pl_mg_net* net, double vfCoef, double entCoef, double clipEps, double vfClip,
+                       uint8_t bf16, double* out);
+
+/* Host bookkeeping twins, bit-exact: prioritised segment sampling (replaces lean_ffi_prio_sample,
+ * ffi/pufferffi.c:1094-1125) and the MinGRU minibatch scalar gather (replaces
+ * lean_ffi_gather_seq_minibatch, ffi/pufferffi.c:1137-1176; out = 6*T*Bmb, [act|adv|ret|old|term|ov]). */
+int pl_prio_sample(const double* advL1, size_t N, size_t mbSegs, double prioAlpha, double annealBeta, uint64_t rng,
+                   double* segIdx, double* mbPrio);
+int pl_gather_seq_minibatch(const double* actCol, const double* logpCol, const double* termCol,
+                            const double* advFlat, const double* valueBuf, const double* segIdx, const double* mbPrio,
+                            size_t T, size_t Bmb, double* out);
+
+/* Resident MinGRU state: the rollout's N x T columns (rows e*T + t) on the device, the live value and
+ * importance-ratio buffers the replay iterates, the device obs trajectory, the sampled minibatch, the
+ * BPTT workspace and the resident gradient. One object replaces the reference's process-global
+ * device columns and caches (ffi/puffercuda.cu:225-507, 5132-5622, 5727-5976). */
+typedef struct pl_mg pl_mg;
+int pl_mg_create(size_t N, size_t T, pl_mg** out);
+/* Replaces lean_cuda_mg_prep (ffi/puffercuda.cu:316-335): uploads rew, term, act, logp, val [N*T] and
+ * boot [N] (host f64); value := val, ratio := 1. The _dev form takes device f64 pointers. */
+int pl_mg_set_columns(pl_mg* s, const double* rew, const double* term, const double* act, const double* logp,
+                      const double* val, const double* boot);
+int pl_mg_set_columns_dev(pl_mg* s, const double* rew, const double* term, const double* act, const double* logp,
+                          const double* val, const double* boot, void* stream);
+/* The obs trajectory [(e*T + t)*D + j]: host f64 (copied to the device as fp32), or a device fp32
+ * buffer the caller owns and keeps alive (the rollout's resident trajectory, g_dMGObsTraj in the
+ * reference, ffi/puffercuda.cu:2130-2150). */
+int pl_mg_set_obs(pl_mg* s, const double* obs, size_t D);
+int pl_mg_set_obs_dev(pl_mg* s, const float* traj, size_t D);
+/* Replaces lean_cuda_mg_vtrace (ffi/puffercuda.cu:389-399): MinGRU-form V-trace of the columns with the
+ * live ratio/value buffers (f64, bit-exact), sum |adv| per segment copied to advL1 (host, N). */
+int pl_mg_vtrace(pl_mg* s, double gamma, double lam, double rhoClip, double cClip, double* advL1, void* stream);
+/* Replaces lean_cuda_mg_vtrace_prio (ffi/puffercuda.cu:443-470): the same V-trace, then prioritised
+ * sampling of mbSegs segments on the device; the sample stays resident for pl_mg_grad. */
+int pl_mg_vtrace_prio(pl_mg* s, double gamma, double lam, double rhoClip, double cClip, size_t mbSegs,
+                      double prioAlpha, double annealBeta, uint64_t rng, void* stream);
+/* Replaces the device-column mode of lean_cuda_mingru_ppo_grad: gathers the sampled minibatch (segIdx
+ * and mbPrio host arrays of Bmb entries, or both NULL for the sample pl_mg_vtrace_prio left), runs the
+ * BPTT gradient with the weights of `handle` (a pl_policy_load handle; 0 = the host `params` instead),
+ * leaves the summed gradient resident, and iterates value/ratio of the sampled segments (the last
+ * sampler of a segment writes). */
+int pl_mg_grad(pl_mg* s, const pl_mg_net* net, size_t handle, const double* params, const double* segIdx,
+               const double* mbPrio, size_t Bmb, double vfCoef, double entCoef, double clipEps, double vfClip,
+               uint8_t bf16, void* stream);
+/* Copies the last resident gradient (P) and, when non-NULL, the minibatch's new log-prob / value
+ * (T*Bmb each, time-major) to host f64. */
+int pl_mg_grad_download(pl_mg* s, double* grad, double* newlp, double* newval);
+/* Replaces lean_cuda_mingru_muon_resident (ffi/puffercuda.cu:5727-5976): clips the resident gradient
+ * (gClip == NULL; gnorm of g*gscale, Puffer/RL/MinGRUTrain.lean:640-648) or takes an already clipped
+ * host gradient gClip (P), then one Muon step of every matrix and bias of `handle` in place.
+ * coeffs: the Newton-Schulz table (iters rows of a, b, c; NULL = the reference's 5-row table). */
+int pl_mg_muon(pl_mg* s, const pl_mg_net* net, size_t handle, const double* gClip, double lr, double wd, double mu,
+               double eps, double maxGradNorm, double gscale, const double* coeffs, size_t iters, uint8_t bf16,
+               void* stream);
+/* Copies value, ratio and the last V-trace advantages (N*T each, may be NULL) to host f64. */
+int pl_mg_read_state(pl_mg* s, double* value, double* ratio, double* adv);
+typedef struct {
+  double gamma, lam, rhoClip, cClip, prioAlpha, annealBeta;
+  double wd, mu, eps, vfCoef, entCoef, clipEps, vfClip, maxGradNorm;
+  const double* ns_coeffs; /* NULL: the reference table */
+  size_t ns_iters;
+  uint8_t bf16;
+} pl_mg_hyper;
+/* One whole update (the minibatch loop of Puffer/RL/MinGRUTrain.lean:800-850): numMB x {V-trace +
+ * prioritised sampling of mbSegs segments, BPTT gradient, iterate, clip, Muon}; *rng advances by
+ * mbSegs * 0x9E3779B97F4A7C15 per minibatch. */
+int pl_mg_update(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hyper* h, size_t numMB, size_t mbSegs,
+                 uint64_t* rng, double lr, void* stream);
+uint64_t pl_mg_last_launches(const pl_mg* s);
+int pl_mg_destroy(pl_mg* s);
+
 /* ------------------------------------------------------------------ dashboard losses ----------- */
 /* The reference's 7-loss channel [policy, value, entropy, total, old_kl, kl, clipfrac]
  * (ffi/puffercuda.cu:251-262, 336-352). */

@@ -28,6 +28,18 @@ class PufferError(RuntimeError):
     """A library call returned a non-zero status."""
 
 
+class MgNet(C.Structure):
+    """pl_mg_net: the MinGRU network (K = 3 the reference layer, K = 2 gate + candidate only)."""
+    _fields_ = [("D", _sz), ("H", _sz), ("L", _sz), ("A", _sz), ("K", _sz), ("enc_act", C.c_int)]
+
+
+class MgHyper(C.Structure):
+    """pl_mg_hyper: the MinGRU update's hyperparameters."""
+    _fields_ = [(x, _d) for x in ("gamma", "lam", "rhoClip", "cClip", "prioAlpha", "annealBeta", "wd", "mu", "eps",
+                                  "vfCoef", "entCoef", "clipEps", "vfClip", "maxGradNorm")] + [
+        ("ns_coeffs", _dp), ("ns_iters", _sz), ("bf16", C.c_uint8)]
+
+
 def lib():
     """The loaded CUDA library (raises if it was not built: run `python -m pufferlean_b200.build`)."""
     global _lib
@@ -65,6 +77,25 @@ def _bind_optional(L):
         "pl_mlp_param_count": ([_sz] * 4, _sz),
         "pl_loss_enable": ([C.c_uint8], C.c_int),
         "pl_read_losses": ([_dp], C.c_int),
+        "pl_mg_param_count": ([C.POINTER(MgNet)], _sz),
+        "pl_mingru_ppo_grad": ([_dp] * 3 + [_sz, _sz, C.POINTER(MgNet)] + [_d] * 4 + [C.c_uint8, _dp], C.c_int),
+        "pl_prio_sample": ([_dp, _sz, _sz, _d, _d, C.c_uint64, _dp, _dp], C.c_int),
+        "pl_gather_seq_minibatch": ([_dp] * 7 + [_sz, _sz, _dp], C.c_int),
+        "pl_mg_create": ([_sz, _sz, C.POINTER(_vp)], C.c_int),
+        "pl_mg_destroy": ([_vp], C.c_int),
+        "pl_mg_set_columns": ([_vp] + [_dp] * 6, C.c_int),
+        "pl_mg_set_columns_dev": ([_vp] * 8, C.c_int),
+        "pl_mg_set_obs": ([_vp, _dp, _sz], C.c_int),
+        "pl_mg_set_obs_dev": ([_vp, _vp, _sz], C.c_int),
+        "pl_mg_vtrace": ([_vp] + [_d] * 4 + [_dp, _vp], C.c_int),
+        "pl_mg_vtrace_prio": ([_vp] + [_d] * 4 + [_sz, _d, _d, C.c_uint64, _vp], C.c_int),
+        "pl_mg_grad": ([_vp, C.POINTER(MgNet), _sz, _dp, _dp, _dp, _sz] + [_d] * 4 + [C.c_uint8, _vp], C.c_int),
+        "pl_mg_grad_download": ([_vp, _dp, _dp, _dp], C.c_int),
+        "pl_mg_muon": ([_vp, C.POINTER(MgNet), _sz, _dp] + [_d] * 6 + [_dp, _sz, C.c_uint8, _vp], C.c_int),
+        "pl_mg_read_state": ([_vp, _dp, _dp, _dp], C.c_int),
+        "pl_mg_update": ([_vp, C.POINTER(MgNet), _sz, C.POINTER(MgHyper), _sz, _sz, C.POINTER(C.c_uint64), _d, _vp],
+                         C.c_int),
+        "pl_mg_last_launches": ([_vp], C.c_uint64),
     }
     for name, (args, res) in specs.items():
         if hasattr(L, name):
@@ -210,3 +241,108 @@ def cuda_train_update_resident(handle, obs, acts, adv, ret, olp, old_val, perm, 
                                           epochs, num_mb, lr, wd, mu, eps, vf_coef, ent_coef, clip_eps, vf_clip,
                                           max_grad_norm, bf16, _p(out)), "pl_train_update_resident")
     return out
+
+
+# ------------------------------------------------------------------------------------------- MinGRU
+def mg_net(D, H, L, A, K=3, enc_act=0):
+    return MgNet(D, H, L, A, K, enc_act)
+
+
+def mg_param_count(D, H, L, A, K=3, enc_act=0):
+    return int(lib().pl_mg_param_count(C.byref(mg_net(D, H, L, A, K, enc_act))))
+
+
+def cuda_mingru_ppo_grad(params, obs, scal, B, T, H, D, L, A, vf_coef, ent_coef, clip_eps, vf_clip, bf16=0, K=3,
+                         enc_act=0):
+    """Host mode of lean_cuda_mingru_ppo_grad: [grad(P); new_logp(T*B); new_value(T*B)] (f64)."""
+    net = mg_net(D, H, L, A, K, enc_act)
+    P = int(lib().pl_mg_param_count(C.byref(net)))
+    out = np.zeros(P + 2 * T * B)
+    params, obs, scal = _f64(params), _f64(obs), _f64(scal)
+    _check(lib().pl_mingru_ppo_grad(_p(params), _p(obs), _p(scal), B, T, C.byref(net), vf_coef, ent_coef, clip_eps,
+                                    vf_clip, bf16, _p(out)), "pl_mingru_ppo_grad")
+    return out
+
+
+def prio_sample(adv_l1, N, T, mb_segs, prio_alpha, anneal_beta, rng):
+    """lean_ffi_prio_sample: (segment indices as f64, importance weights)."""
+    seg, mp = np.zeros(mb_segs), np.zeros(mb_segs)
+    adv_l1 = _f64(adv_l1)
+    _check(lib().pl_prio_sample(_p(adv_l1), N, mb_segs, prio_alpha, anneal_beta, rng & 0xFFFFFFFFFFFFFFFF, _p(seg),
+                                _p(mp)), "pl_prio_sample")
+    return seg, mp
+
+
+def gather_seq_minibatch(act_col, logp_col, term_col, adv_flat, value_buf, seg_idx, mb_prio, T, Bmb):
+    """lean_ffi_gather_seq_minibatch's packed [act|adv|ret|old|term|ov] (6*T*Bmb)."""
+    out = np.zeros(6 * T * Bmb)
+    arrs = [_f64(a) for a in (act_col, logp_col, term_col, adv_flat, value_buf, seg_idx, mb_prio)]
+    _check(lib().pl_gather_seq_minibatch(*[_p(a) for a in arrs], T, Bmb, _p(out)), "pl_gather_seq_minibatch")
+    return out
+
+
+class MgSession:
+    """The resident MinGRU state (pl_mg_*): columns, obs trajectory, sample, workspace, gradient."""
+
+    def __init__(self, N, T):
+        self.N, self.T = N, T
+        self.h = _vp()
+        _check(lib().pl_mg_create(N, T, C.byref(self.h)), "pl_mg_create")
+
+    def close(self):
+        if self.h:
+            lib().pl_mg_destroy(self.h)
+            self.h = _vp()
+
+    def set_columns(self, rew, term, act, logp, val, boot):
+        arrs = [_f64(a) for a in (rew, term, act, logp, val, boot)]
+        _check(lib().pl_mg_set_columns(self.h, *[_p(a) for a in arrs]), "pl_mg_set_columns")
+
+    def set_obs(self, obs, D):
+        obs = _f64(obs)
+        _check(lib().pl_mg_set_obs(self.h, _p(obs), D), "pl_mg_set_obs")
+
+    def vtrace(self, gamma, lam, rho, c):
+        l1 = np.zeros(self.N)
+        _check(lib().pl_mg_vtrace(self.h, gamma, lam, rho, c, _p(l1), None), "pl_mg_vtrace")
+        return l1
+
+    def vtrace_prio(self, gamma, lam, rho, c, mb_segs, alpha, beta, rng):
+        _check(lib().pl_mg_vtrace_prio(self.h, gamma, lam, rho, c, mb_segs, alpha, beta, rng & 0xFFFFFFFFFFFFFFFF,
+                                       None), "pl_mg_vtrace_prio")
+
+    def grad(self, net, handle=0, params=None, seg=None, mbp=None, Bmb=0, vf=0.5, ent=0.01, clip=0.2, vfclip=0.2,
+             bf16=0):
+        pr = _f64(params) if params is not None else None
+        sg = _f64(seg) if seg is not None else None
+        mp = _f64(mbp) if mbp is not None else None
+        _check(lib().pl_mg_grad(self.h, C.byref(net), handle, _p(pr) if pr is not None else None,
+                                _p(sg) if sg is not None else None, _p(mp) if mp is not None else None, Bmb, vf, ent,
+                                clip, vfclip, bf16, None), "pl_mg_grad")
+
+    def grad_download(self, P, R):
+        g, nl, nv = np.zeros(P), np.zeros(R), np.zeros(R)
+        _check(lib().pl_mg_grad_download(self.h, _p(g), _p(nl), _p(nv)), "pl_mg_grad_download")
+        return g, nl, nv
+
+    def muon(self, net, handle, lr, wd, mu, eps, max_grad_norm, gscale, gclip=None, coeffs=None, bf16=0):
+        gc = _f64(gclip) if gclip is not None else None
+        co = _f64(coeffs) if coeffs is not None else None
+        _check(lib().pl_mg_muon(self.h, C.byref(net), handle, _p(gc) if gc is not None else None, lr, wd, mu, eps,
+                                max_grad_norm, gscale, _p(co) if co is not None else None,
+                                (co.size // 3) if co is not None else 0, bf16, None), "pl_mg_muon")
+
+    def state(self):
+        n = self.N * self.T
+        v, r, a = np.zeros(n), np.zeros(n), np.zeros(n)
+        _check(lib().pl_mg_read_state(self.h, _p(v), _p(r), _p(a)), "pl_mg_read_state")
+        return v, r, a
+
+    def update(self, net, handle, hyper, num_mb, mb_segs, rng, lr):
+        r = C.c_uint64(rng & 0xFFFFFFFFFFFFFFFF)
+        _check(lib().pl_mg_update(self.h, C.byref(net), handle, C.byref(hyper), num_mb, mb_segs, C.byref(r), lr, None),
+               "pl_mg_update")
+        return r.value
+
+    def last_launches(self):
+        return int(lib().pl_mg_last_launches(self.h))

@@ -39,7 +39,7 @@ struct EpiArgs {
   long ldo2;
   float* colsum;  // [gridDim.y][ld_colsum] per-CTA column partial sums (fixed-order reduced later)
   long ld_colsum;
-  int act;        // 0 ReLU, 1 GELU (tanh form)
+  int act;        // 0 ReLU, 1 GELU (tanh form), 2 identity
   // PPO head (EPI_PPO): one row per thread, per-row columns of the minibatch
   const int* act_idx;
   const float* adv;
@@ -59,13 +59,16 @@ struct EpiArgs {
   float diag;        // EPI_F32 / EPI_BF16: added on the diagonal (row == column) of every matrix
 };
 
+// Activation codes: 0 ReLU, 1 GELU (tanh form), 2 identity (a linear layer with bias).
 __device__ __forceinline__ float act_fwd(float z, int act) {
   if (act == 0) return z > 0.f ? z : 0.f;
+  if (act == 2) return z;
   float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
   return 0.5f * z * (1.f + tanhf(u));
 }
 __device__ __forceinline__ float act_grad(float z, int act) {
   if (act == 0) return z > 0.f ? 1.f : 0.f;
+  if (act == 2) return 1.f;
   float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
   float t = tanhf(u);
   return 0.5f * (1.f + t) + 0.5f * z * (1.f - t * t) * 0.7978845608028654f * (1.f + 3.f * 0.044715f * z * z);
@@ -149,11 +152,13 @@ __device__ __forceinline__ float tanh_fast(float x) {
 }
 __device__ __forceinline__ float act_fwd_fast(float z, int act) {
   if (act == 0) return z > 0.f ? z : 0.f;
+  if (act == 2) return z;
   const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
   return 0.5f * z * (1.f + tanh_fast(u));
 }
 __device__ __forceinline__ float act_grad_fast(float z, int act) {
   if (act == 0) return z > 0.f ? 1.f : 0.f;
+  if (act == 2) return 1.f;
   const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
   const float t = tanh_fast(u);
   return 0.5f * (1.f + t) + 0.5f * z * (1.f - t * t) * 0.7978845608028654f * (1.f + 3.f * 0.044715f * z * z);

@@ -1,6 +1,8 @@
-// Host-side bookkeeping twins of the reference's C helpers: per-epoch shuffle and truncated GAE.
-// These stay on the host in the reference's update path as well (ffi/pufferffi.c:946-1041); they
-// are restated here so the library is a drop-in for the whole call sequence of one update.
+// Host-side bookkeeping twins of the reference's C helpers: per-epoch shuffle, truncated GAE,
+// prioritised segment sampling and the MinGRU minibatch scalar gather. These stay on the host in the
+// reference's update path as well (ffi/pufferffi.c:946-1041, 1094-1176); they are restated here so the
+// library is a drop-in for the whole call sequence of one update.
+#include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -64,6 +66,104 @@ int pl_gae_soa(const double* vals, const double* rews, const double* terms, size
     }
   }
   for (size_t t = 0; t < NT; t++) ret[t] = adv[t] + vals[t];
+  return PL_OK;
+}
+
+// Prioritised segment sampling: priorities |adv|^alpha summed in segment order, probabilities with
+// the 1e-6 floor, a sequential prefix sum, splitmix64 draws (state rng + (i+1)*GOLD), a lower-bound
+// search and the importance weight (N p)^-beta. Same operations in the same order as the reference
+// host sampler, so the result is bit-identical.
+int pl_prio_sample(const double* advL1, size_t N, size_t mbSegs, double prioAlpha, double annealBeta, uint64_t rng,
+                   double* segIdx, double* mbPrio) {
+  if (mbSegs == 0) return PL_OK;
+  if (!advL1 || !segIdx || !mbPrio || N == 0) return PL_ERR_INVALID;
+  double* w = (double*)malloc(sizeof(double) * N);
+  double* p = (double*)malloc(sizeof(double) * N);
+  double* cum = (double*)malloc(sizeof(double) * N);
+  if (!w || !p || !cum) {
+    free(w);
+    free(p);
+    free(cum);
+    return PL_ERR_NOMEM;
+  }
+  double sumW = 0.0;
+  for (size_t e = 0; e < N; e++) {
+    w[e] = exp(prioAlpha * log(advL1[e] + 1e-12));
+    sumW += w[e];
+  }
+  const double denom = sumW + 1e-6;
+  double acc = 0.0;
+  for (size_t e = 0; e < N; e++) {
+    p[e] = (w[e] + 1e-6) / denom;
+    acc += p[e];
+    cum[e] = acc;
+  }
+  const double total = acc;
+  for (size_t i = 0; i < mbSegs; i++) {
+    uint64_t z = rng + (uint64_t)(i + 1) * 0x9E3779B97F4A7C15ULL;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    z ^= z >> 31;
+    const double u = (double)(z >> 11) / 9007199254740992.0 * total;
+    size_t lo = 0, hi = N;
+    while (lo < hi) {
+      const size_t mid = (lo + hi) >> 1;
+      if (cum[mid] >= u)
+        hi = mid;
+      else
+        lo = mid + 1;
+    }
+    const size_t idx = lo < N ? lo : N - 1;
+    segIdx[i] = (double)idx;
+    mbPrio[i] = exp((-annealBeta) * log((double)N * p[idx] + 1e-12));
+  }
+  free(w);
+  free(p);
+  free(cum);
+  return PL_OK;
+}
+
+// MinGRU minibatch scalars, time-major (os = t*Bmb + b, si = seg[b]*T + t): the advantage mean and
+// population std over the sampled rows (b outer, t inner), then act, mbPrio-weighted normalised adv,
+// ret = adv + value, old log-prob, terminal flag, old value.
+int pl_gather_seq_minibatch(const double* actCol, const double* logpCol, const double* termCol,
+                            const double* advFlat, const double* valueBuf, const double* segIdx, const double* mbPrio,
+                            size_t T, size_t Bmb, double* out) {
+  const size_t nb = T * Bmb;
+  if (nb == 0) return PL_OK;
+  if (!actCol || !logpCol || !termCol || !advFlat || !valueBuf || !segIdx || !mbPrio || !out) return PL_ERR_INVALID;
+  const double navd = (double)nb;
+  double sum = 0.0;
+  for (size_t b = 0; b < Bmb; b++) {
+    const double* ab = advFlat + (size_t)segIdx[b] * T;
+    for (size_t t = 0; t < T; t++) sum += ab[t];
+  }
+  const double mean = sum / navd;
+  double sq = 0.0;
+  for (size_t b = 0; b < Bmb; b++) {
+    const double* ab = advFlat + (size_t)segIdx[b] * T;
+    for (size_t t = 0; t < T; t++) {
+      const double d = ab[t] - mean;
+      sq += d * d;
+    }
+  }
+  const double stde = sqrt(sq / navd) + 1e-8;
+  double *pact = out, *padv = out + nb, *pret = out + 2 * nb, *pold = out + 3 * nb, *pterm = out + 4 * nb,
+         *pov = out + 5 * nb;
+  for (size_t b = 0; b < Bmb; b++) {
+    const size_t e = (size_t)segIdx[b];
+    const double mp = mbPrio[b];
+    for (size_t t = 0; t < T; t++) {
+      const size_t si = e * T + t, os = t * Bmb + b;
+      const double a = advFlat[si], v = valueBuf[si];
+      pact[os] = (double)(unsigned long long)actCol[si];
+      padv[os] = mp * (a - mean) / stde;
+      pret[os] = a + v;
+      pold[os] = logpCol[si];
+      pov[os] = v;
+      pterm[os] = termCol[si] > 0.5 ? 1.0 : 0.0;
+    }
+  }
   return PL_OK;
 }
 

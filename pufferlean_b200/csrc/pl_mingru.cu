@@ -1,0 +1,1454 @@
+// MinGRU PPO+Muon update path: the recurrent policy of Puffer/Net/MinGRU.lean:9-17 trained by the
+// minibatch chain of Puffer/RL/MinGRUTrain.lean:800-850 (V-trace with live importance ratios and
+// values, prioritised segment sampling, BPTT PPO gradient, value/ratio iterate, clip, Muon).
+//
+// Layout of one minibatch (Bmb sampled segments x T steps): rows are time-major, r = t*Bmb + b, so
+// every GEMM of the network covers all T steps at once ([R x .] with R = T*Bmb), and the only
+// sequential work, the scan over t, is elementwise over (b, j):
+//
+//   forward   h0 = enc(X W_enc^T + b_enc)              GEMM (bias/activation in the epilogue)
+//             Y_l = h_l W_l^T                          GEMM, [R x K*H] = [hid | gate | (proj)]
+//             o_t = (1 - z_t) o_{t-1} + z_t g(hid_t)    scan over t, z = sigmoid(gate), state reset
+//             h_{l+1} = hg o + (1 - hg) h_l  (K = 3)    after a terminal; hg = sigmoid(proj)
+//             Out = h_L [W_dec; w_val]^T + b            GEMM, fp32 logits and value
+//   backward  dOut from the PPO objective per row; dh_L = dOut W_out; per layer the reverse scan
+//             gives dY (and the highway part of dh_l), dW_l = dY^T h_l, dh_l += dY W_l; the encoder
+//             takes dE = dh_0 * enc'(Z); dW_enc = dE^T X; bias gradients are column sums.
+//
+// Two tiers: tight (fp32 SIMT GEMMs, fp32 activations; the parity tier) and fast (bf16 tcgen05
+// GEMMs with fp32 accumulation, bf16 activations; the recurrent state itself is carried in fp32
+// registers through every scan).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/pufferlean_b200.h"
+#include "pl_common.cuh"
+#include "pl_gemm.cuh"
+#include "pl_mlp.cuh"
+#include "pl_muon.cuh"
+#include "pl_runtime.h"
+
+namespace pl {
+namespace {
+
+typedef __nv_bfloat16 bf16;
+
+template <typename S>
+__device__ __forceinline__ float ldv(const S* p, long i);
+template <>
+__device__ __forceinline__ float ldv<float>(const float* p, long i) {
+  return p[i];
+}
+template <>
+__device__ __forceinline__ float ldv<bf16>(const bf16* p, long i) {
+  return __bfloat162float(p[i]);
+}
+template <typename S>
+__device__ __forceinline__ void stv(S* p, long i, float v);
+template <>
+__device__ __forceinline__ void stv<float>(float* p, long i, float v) {
+  p[i] = v;
+}
+template <>
+__device__ __forceinline__ void stv<bf16>(bf16* p, long i, float v) {
+  p[i] = __float2bfloat16_rn(v);
+}
+
+__device__ __forceinline__ float sigf(float x) { return 1.f / (1.f + expf(-x)); }
+
+inline unsigned blocks_for(long n, int block = 256, long cap = 148 * 32) {
+  long g = (n + block - 1) / block;
+  return (unsigned)std::max<long>(1, std::min(g, cap));
+}
+inline long rup(long x, long m) { return (x + m - 1) / m * m; }
+
+// ---------------------------------------------------------------- minibatch gather
+// X[r][c] = traj[(seg[b]*T + t)*D + c] for c < D, 0 in the padding (r = t*Bmb + b)
+template <typename S>
+__global__ void mg_gather_obs_kernel(const float* __restrict__ traj, const double* __restrict__ seg, int Bmb, int T,
+                                     int D, int Dp, S* X) {
+  const long n = (long)T * Bmb * Dp;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / Dp;
+    const int c = (int)(i - r * Dp);
+    const int t = (int)(r / Bmb), b = (int)(r - (long)t * Bmb);
+    float v = 0.f;
+    if (c < D) v = traj[((long)seg[b] * T + t) * D + c];
+    stv(X, i, v);
+  }
+}
+// host-mode obs: src f64 [R x D] (already time-major) -> X [R x Dp]
+template <typename S>
+__global__ void mg_obs_rows_kernel(const double* __restrict__ src, long R, int D, int Dp, S* X) {
+  const long n = R * Dp;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / Dp;
+    const int c = (int)(i - r * Dp);
+    stv(X, i, c < D ? (float)src[r * D + c] : 0.f);
+  }
+}
+
+// Advantage mean and population std over the Bmb*T sampled entries (index q = b*T + t), one block
+// with a fixed-shape tree: ms = [mean, std + 1e-8].
+__global__ void __launch_bounds__(1024) mg_adv_ms_kernel(const double* __restrict__ adv,
+                                                         const double* __restrict__ seg, int Bmb, int T, double* ms) {
+  __shared__ double sh[1024];
+  const long n = (long)Bmb * T;
+  const int tid = threadIdx.x;
+  double s = 0.0;
+  for (long q = tid; q < n; q += 1024) {
+    const int b = (int)(q / T), t = (int)(q - (long)b * T);
+    s += adv[(long)seg[b] * T + t];
+  }
+  sh[tid] = s;
+  __syncthreads();
+  for (int k = 512; k > 0; k >>= 1) {
+    if (tid < k) sh[tid] += sh[tid + k];
+    __syncthreads();
+  }
+  const double mean = sh[0] / (double)(n > 0 ? n : 1);
+  __syncthreads();
+  double s2 = 0.0;
+  for (long q = tid; q < n; q += 1024) {
+    const int b = (int)(q / T), t = (int)(q - (long)b * T);
+    const double d = adv[(long)seg[b] * T + t] - mean;
+    s2 += d * d;
+  }
+  sh[tid] = s2;
+  __syncthreads();
+  for (int k = 512; k > 0; k >>= 1) {
+    if (tid < k) sh[tid] += sh[tid + k];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    ms[0] = mean;
+    ms[1] = sqrt(sh[0] / (double)(n > 0 ? n : 1)) + 1e-8;
+  }
+}
+// Per-row minibatch scalars from the resident columns (the layout of the host gather,
+// ffi/pufferffi.c:1137-1176): os = t*Bmb + b, si = seg[b]*T + t.
+__global__ void mg_gather_scal_kernel(const double* __restrict__ act, const double* __restrict__ logp,
+                                      const double* __restrict__ term, const double* __restrict__ adv,
+                                      const double* __restrict__ value, const double* __restrict__ seg,
+                                      const double* __restrict__ mbp, const double* __restrict__ ms, int Bmb, int T,
+                                      int* act_i, float* adv_f, float* ret_f, float* olp_f, float* ov_f,
+                                      float* term_f) {
+  const long n = (long)T * Bmb;
+  for (long os = (long)blockIdx.x * blockDim.x + threadIdx.x; os < n; os += (long)gridDim.x * blockDim.x) {
+    const int t = (int)(os / Bmb), b = (int)(os - (long)t * Bmb);
+    const long si = (long)seg[b] * T + t;
+    const double a = adv[si], v = value[si];
+    act_i[os] = (int)(unsigned long long)act[si];
+    adv_f[os] = (float)(mbp[b] * (a - ms[0]) / ms[1]);
+    ret_f[os] = (float)(a + v);
+    olp_f[os] = (float)logp[si];
+    ov_f[os] = (float)v;
+    term_f[os] = term[si] > 0.5 ? 1.f : 0.f;
+  }
+}
+// Host-mode scalars: scal = [act | adv | ret | old | term | ov], each R time-major entries.
+__global__ void mg_scal_rows_kernel(const double* __restrict__ scal, long R, int* act_i, float* adv_f, float* ret_f,
+                                    float* olp_f, float* ov_f, float* term_f) {
+  for (long r = (long)blockIdx.x * blockDim.x + threadIdx.x; r < R; r += (long)gridDim.x * blockDim.x) {
+    act_i[r] = (int)(unsigned long long)scal[r];
+    adv_f[r] = (float)scal[R + r];
+    ret_f[r] = (float)scal[2 * R + r];
+    olp_f[r] = (float)scal[3 * R + r];
+    term_f[r] = scal[4 * R + r] != 0.0 ? 1.f : 0.f;
+    ov_f[r] = (float)scal[5 * R + r];
+  }
+}
+
+// ---------------------------------------------------------------- scans
+// Forward scan of one layer: thread (b, j) walks t = 0..T-1 with the state in a register.
+// Y [R x K*H], hin/hout/Os [R x H], term [R] (1 = terminal at that step).
+template <typename S, int K>
+__global__ void __launch_bounds__(256) mg_scan_fwd_kernel(const S* __restrict__ Y, const S* __restrict__ hin, S* hout,
+                                                          S* Os, const float* __restrict__ term, int B, int H, int T) {
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)B * H) return;
+  const int b = (int)(idx / H), j = (int)(idx - (long)b * H);
+  const long KH = (long)K * H;
+  float state = 0.f;
+  for (int t = 0; t < T; t++) {
+    const long r = (long)t * B + b;
+    const float hid = ldv(Y, r * KH + j), gate = ldv(Y, r * KH + H + j);
+    const float z = sigf(gate), g = hid >= 0.f ? hid + 0.5f : sigf(hid);
+    const float o = (1.f - z) * state + z * g;
+    stv(Os, r * H + j, o);
+    if (K == 3) {
+      const float hg = sigf(ldv(Y, r * KH + 2 * H + j));
+      stv(hout, r * H + j, hg * o + (1.f - hg) * ldv(hin, r * H + j));
+    } else {
+      stv(hout, r * H + j, o);
+    }
+    state = term[r] != 0.f ? 0.f : o;
+  }
+}
+// Reverse scan of one layer (the per-element backward of ffi/pufferffi.c:840-868): dY [R x K*H],
+// dhn [R x H] = the highway part of the gradient reaching the layer input (K = 3).
+template <typename S, int K>
+__global__ void __launch_bounds__(256) mg_scan_bwd_kernel(const S* __restrict__ Y, const S* __restrict__ Os,
+                                                          const S* __restrict__ hin, const S* __restrict__ dh, S* dY,
+                                                          S* dhn, const float* __restrict__ term, int B, int H,
+                                                          int T) {
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)B * H) return;
+  const int b = (int)(idx / H), j = (int)(idx - (long)b * H);
+  const long KH = (long)K * H;
+  float dOnext = 0.f;
+  for (int t = T - 1; t >= 0; t--) {
+    const long r = (long)t * B + b;
+    const bool flow = t > 0 && term[r - B] == 0.f;  // no state (and no gradient) across a terminal
+    const float hid = ldv(Y, r * KH + j), gate = ldv(Y, r * KH + H + j);
+    const float o = ldv(Os, r * H + j);
+    const float prev = flow ? ldv(Os, (r - B) * H + j) : 0.f;
+    const float z = sigf(gate);
+    const float sh = sigf(hid);
+    const float g = hid >= 0.f ? hid + 0.5f : sh;
+    const float dhj = ldv(dh, r * H + j);
+    float dout;
+    if (K == 3) {
+      const float hg = sigf(ldv(Y, r * KH + 2 * H + j));
+      const float hi = ldv(hin, r * H + j);
+      const float dhg = dhj * (o - hi);
+      dout = dhj * hg + dOnext;
+      stv(dhn, r * H + j, dhj * (1.f - hg));
+      stv(dY, r * KH + 2 * H + j, dhg * hg * (1.f - hg));
+    } else {
+      dout = dhj + dOnext;
+    }
+    const float dz = dout * (g - prev);
+    const float dprev = dout * (1.f - z);
+    const float dg = dout * z;
+    const float sg = hid >= 0.f ? 1.f : sh * (1.f - sh);
+    stv(dY, r * KH + j, dg * sg);
+    stv(dY, r * KH + H + j, dz * z * (1.f - z));
+    dOnext = flow ? dprev : 0.f;
+  }
+}
+
+// ---------------------------------------------------------------- PPO head (per row)
+// The recurrent path's head math (ffi/puffercuda.cu:4910-4930): log-softmax with the max
+// subtracted, clipped surrogate, entropy bonus, clipped value loss. Out [R x ldo] fp32 without the
+// bias; bout [A+1]. dOut [R x Op] (zero past A+1). lossrow (optional) [R x 8]: pg, vloss, entropy,
+// old_kl, kl, clipped.
+template <typename S>
+__global__ void mg_ppo_rows_kernel(const float* __restrict__ Out, int ldo, const float* __restrict__ bout, long R,
+                                   int A, int Op, const int* __restrict__ act, const float* __restrict__ adv,
+                                   const float* __restrict__ ret, const float* __restrict__ olp,
+                                   const float* __restrict__ ov, float vf, float ent, float clip, float vfclip, S* dOut,
+                                   float* newlp, float* newval, float* lossrow) {
+  for (long r = (long)blockIdx.x * blockDim.x + threadIdx.x; r < R; r += (long)gridDim.x * blockDim.x) {
+    const float* o = Out + r * ldo;
+    float mx = o[0] + bout[0];
+    for (int k = 1; k < A; k++) mx = fmaxf(mx, o[k] + bout[k]);
+    float se = 0.f;
+    for (int k = 0; k < A; k++) se += expf(o[k] + bout[k] - mx);
+    const float lse = mx + logf(se);
+    float pout = 0.f;
+    for (int k = 0; k < A; k++) {
+      const float l = o[k] + bout[k];
+      pout += expf(l - lse) * l;
+    }
+    const int a = act[r];
+    const float logpA = o[a] + bout[a] - lse;
+    const float ratio = expf(logpA - olp[r]);
+    const float lo = 1.f - clip, hi = 1.f + clip;
+    const float rc = ratio < lo ? lo : (ratio > hi ? hi : ratio);
+    const float ad = adv[r];
+    const float s1 = ad * ratio, s2 = ad * rc;
+    const float dPol = s1 <= s2 ? ad * ratio : ad * ((lo < ratio && ratio < hi) ? 1.f : 0.f) * ratio;
+    const float vnew = o[A] + bout[A], rt = ret[r], vold = ov[r];
+    float dvl = vnew - rt;
+    float vcl = vnew;
+    if (vfclip > 0.f) {
+      const float dd = vnew - vold;
+      vcl = vold + (dd < -vfclip ? -vfclip : (dd > vfclip ? vfclip : dd));
+      const float du = (vnew - rt) * (vnew - rt), cc = (vcl - rt) * (vcl - rt);
+      if (!(du >= cc) && !(dd > -vfclip && dd < vfclip)) dvl = 0.f;
+    }
+    S* d = dOut + r * Op;
+    for (int k = 0; k < A; k++) {
+      const float l = o[k] + bout[k];
+      const float p = expf(l - lse);
+      stv(d, k, dPol * ((k == a ? 1.f : 0.f) - p) + ent * p * (pout - l));
+    }
+    stv(d, A, -vf * dvl);
+    for (int k = A + 1; k < Op; k++) stv(d, k, 0.f);
+    newlp[r] = logpA;
+    newval[r] = vnew;
+    if (lossrow) {
+      const float lgr = logpA - olp[r];
+      float* lr = lossrow + r * 8;
+      lr[0] = fmaxf(-ad * ratio, -ad * rc);
+      const float du = (vnew - rt) * (vnew - rt), cc = (vcl - rt) * (vcl - rt);
+      lr[1] = 0.5f * ((vfclip > 0.f && cc > du) ? cc : du);
+      lr[2] = lse - pout;  // entropy: -sum p (l - lse)
+      lr[3] = -lgr;
+      lr[4] = (ratio - 1.f) - lgr;
+      lr[5] = (ratio < lo || ratio > hi) ? 1.f : 0.f;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- reductions, elementwise
+// part[chunk][c] = sum of rows [chunk*rows_per, ...) of column c (sequential, coalesced across c)
+template <typename S>
+__global__ void mg_colsum_part_kernel(const S* __restrict__ M, long R, long ld, int N, int rows_per, float* part) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= N) return;
+  const long r0 = (long)blockIdx.y * rows_per, r1 = min(R, r0 + (long)rows_per);
+  float s = 0.f;
+  for (long r = r0; r < r1; r++) s += ldv(M, r * ld + c);
+  part[(long)blockIdx.y * N + c] = s;
+}
+__global__ void mg_colsum_final_kernel(const float* __restrict__ part, int chunks, int N, float* out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= N) return;
+  float s = 0.f;
+  for (int k = 0; k < chunks; k++) s += part[(long)k * N + c];
+  out[c] = s;
+}
+// dE = dh * enc'(Z) in place
+template <typename S>
+__global__ void mg_act_grad_kernel(S* dh, const S* __restrict__ Z, long n, int act) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    stv(dh, i, ldv(dh, i) * act_grad(ldv(Z, i), act));
+}
+__global__ void mg_axpy_kernel(float* y, const float* __restrict__ x, long n) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) y[i] += x[i];
+}
+// The head's [A+1 x H] weight gradient and [A+1] bias gradient into the flat layout
+// (wDec rows, bDec, wVal row, bVal).
+__global__ void mg_head_scatter_kernel(const float* __restrict__ gout, const float* __restrict__ gb, int A, int H,
+                                       float* gWdec, float* gBdec, float* gWval, float* gBval) {
+  const long n = (long)(A + 1) * H;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const int k = (int)(i / H);
+    const int j = (int)(i - (long)k * H);
+    if (k < A)
+      gWdec[i] = gout[i];
+    else
+      gWval[j] = gout[i];
+  }
+  if (blockIdx.x == 0)
+    for (int k = threadIdx.x; k <= A; k += blockDim.x) {
+      if (k < A)
+        gBdec[k] = gb[k];
+      else
+        gBval[0] = gb[k];
+    }
+}
+
+// ---------------------------------------------------------------- replay iterate
+__global__ void mg_lastw_kernel(int* lastw, const double* __restrict__ seg, int Bmb) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < Bmb) atomicMax(&lastw[(long)seg[b]], b);
+}
+// value/ratio of every sampled segment from the BPTT's new value / log-prob; when a segment was
+// drawn more than once, the largest b writes (the host loop's last write).
+__global__ void mg_iterate_kernel(double* value, double* ratio, const double* __restrict__ logp,
+                                  const float* __restrict__ newlp, const float* __restrict__ newval,
+                                  const double* __restrict__ seg, const int* __restrict__ lastw, int Bmb, int T) {
+  const long n = (long)T * Bmb;
+  for (long os = (long)blockIdx.x * blockDim.x + threadIdx.x; os < n; os += (long)gridDim.x * blockDim.x) {
+    const int t = (int)(os / Bmb), b = (int)(os - (long)t * Bmb);
+    const long e = (long)seg[b];
+    if (lastw[e] != b) continue;
+    const long si = e * T + t;
+    ratio[si] = exp((double)newlp[os] - logp[si]);
+    value[si] = (double)newval[os];
+  }
+}
+
+// ---------------------------------------------------------------- prioritised sampling
+// One block: priorities, their sum (fixed tree), probabilities, the prefix sum (per-thread runs
+// plus a sequential scan of the run totals), then the draws (splitmix64 state rng + (i+1)*GOLD,
+// lower-bound search, importance weight). Deterministic; the sums are ordered differently from the
+// host sampler's sequential loop, so a draw can differ from it only when u falls within rounding
+// of a cumulative boundary.
+__global__ void __launch_bounds__(1024) mg_prio_kernel(const double* __restrict__ l1, long N, long Bmb, double alpha,
+                                                       double beta, unsigned long long rng, double* p, double* cum,
+                                                       double* seg, double* mbp) {
+  __shared__ double sh[1024];
+  __shared__ double s_total;
+  const int tid = threadIdx.x;
+  const long per = (N + 1023) / 1024;
+  const long lo = min(N, (long)tid * per), hi = min(N, lo + per);
+  double s = 0.0;
+  for (long e = lo; e < hi; e++) {
+    const double w = exp(alpha * log(l1[e] + 1e-12));
+    p[e] = w;
+    s += w;
+  }
+  sh[tid] = s;
+  __syncthreads();
+  for (int k = 512; k > 0; k >>= 1) {
+    if (tid < k) sh[tid] += sh[tid + k];
+    __syncthreads();
+  }
+  const double denom = sh[0] + 1e-6;
+  __syncthreads();
+  double acc = 0.0;
+  for (long e = lo; e < hi; e++) {
+    const double q = (p[e] + 1e-6) / denom;
+    p[e] = q;
+    acc += q;
+    cum[e] = acc;
+  }
+  sh[tid] = acc;
+  __syncthreads();
+  if (tid == 0) {
+    double run = 0.0;
+    for (int i = 0; i < 1024; i++) {
+      const double v = sh[i];
+      sh[i] = run;
+      run += v;
+    }
+    s_total = run;
+  }
+  __syncthreads();
+  const double off = sh[tid];
+  for (long e = lo; e < hi; e++) cum[e] += off;
+  __syncthreads();
+  const double total = s_total;
+  for (long i = tid; i < Bmb; i += 1024) {
+    unsigned long long z = rng + (unsigned long long)(i + 1) * 0x9E3779B97F4A7C15ULL;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    z ^= z >> 31;
+    const double u = (double)(z >> 11) / 9007199254740992.0 * total;
+    long a = 0, b = N;
+    while (a < b) {
+      const long mid = (a + b) >> 1;
+      if (cum[mid] >= u)
+        b = mid;
+      else
+        a = mid + 1;
+    }
+    const long idx = a < N ? a : N - 1;
+    seg[i] = (double)idx;
+    mbp[i] = exp((-beta) * log((double)N * p[idx] + 1e-12));
+  }
+}
+
+__global__ void mg_fill_kernel(double* d, double v, long n) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) d[i] = v;
+}
+__global__ void mg_f64_to_f32_kernel(const double* __restrict__ s, long n, float* d) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    d[i] = (float)s[i];
+}
+
+}  // namespace
+
+// ================================================================= session
+struct MgShape {
+  long D = 0, H = 0, L = 0, A = 0, K = 0;
+  int enc_act = 0;
+  bool operator==(const MgShape& o) const {
+    return D == o.D && H == o.H && L == o.L && A == o.A && K == o.K && enc_act == o.enc_act;
+  }
+  long P() const { return H * D + H + L * K * H * H + A * H + A + H + 1; }
+  long oWenc() const { return 0; }
+  long oBenc() const { return H * D; }
+  long oLayer(long l) const { return H * D + H + l * K * H * H; }
+  long oWdec() const { return H * D + H + L * K * H * H; }
+  long oBdec() const { return oWdec() + A * H; }
+  long oWval() const { return oBdec() + A; }
+  long oBval() const { return oWval() + H; }
+};
+
+}  // namespace pl
+
+struct pl_mg {
+  int dev = 0;
+  long N = 0, T = 0;
+  std::vector<void*> allocs;  // columns and sampling (freed at destroy)
+  // resident columns, rows e*T + t (f64)
+  double *rew = nullptr, *term = nullptr, *act = nullptr, *logp = nullptr, *val0 = nullptr, *boot = nullptr;
+  double *value = nullptr, *ratio = nullptr, *adv = nullptr, *l1 = nullptr;
+  bool cols_valid = false;
+  // obs trajectory
+  const float* traj = nullptr;
+  float* traj_own = nullptr;
+  long trajD = 0;
+  // prioritised sample
+  double *prio_p = nullptr, *prio_cum = nullptr, *seg = nullptr, *mbp = nullptr;
+  long seg_cap = 0, prio_B = 0;
+  bool prio_fresh = false;
+  int* lastw = nullptr;
+  // BPTT / Muon workspace (reallocated when the shape, minibatch or tier changes)
+  struct Work {
+    std::vector<void*> allocs;
+    pl::MgShape sh;
+    long Bmb = 0, T = 0, R = 0, Dp = 0, Op = 0;
+    bool fast = false;
+    void* X = nullptr;
+    void* Z = nullptr;
+    std::vector<void*> h, Y, Os;
+    float* Out = nullptr;
+    void* dOut = nullptr;
+    void* dh[2] = {nullptr, nullptr};
+    void* dY = nullptr;
+    void* dhn = nullptr;
+    int* act_i = nullptr;
+    float *adv_f = nullptr, *ret_f = nullptr, *olp_f = nullptr, *ov_f = nullptr, *term_f = nullptr;
+    float *newlp = nullptr, *newval = nullptr, *lossrow = nullptr;
+    double* ms = nullptr;
+    double* obs_in = nullptr;   // host-mode obs upload
+    double* scal_in = nullptr;  // host-mode scalars upload
+    // weight shadows: fast = bf16 matrices [rows x ld] + fp32 biases; tight = fp32
+    void* Wenc = nullptr;
+    std::vector<void*> Wl;
+    void* Wout = nullptr;
+    float *benc = nullptr, *bout = nullptr;
+    // gradient and scratch
+    float* grad = nullptr;
+    float* gout = nullptr;
+    float* gbout = nullptr;
+    float* colpart = nullptr;
+    long colpart_elems = 0;
+    float* splitk = nullptr;
+    long splitk_elems = 0;
+    // Muon
+    double* cc = nullptr;
+    double* gn_part = nullptr;
+    double* g64 = nullptr;
+    double* params_in = nullptr;  // host params upload (pl_mg_grad with handle 0)
+    pl::NsWork ns;
+    double* exact_ws = nullptr;
+  } w;
+  bool have_work = false;
+  size_t shadow_src = 0;  // handle whose weights the shadows hold (0 = none / host params)
+  bool grad_fresh = false;
+  long grad_rows = 0;
+  uint64_t launches = 0;
+};
+
+namespace pl {
+namespace {
+
+template <typename T>
+T* mg_alloc(std::vector<void*>& list, size_t n, bool& failed, bool zero = false) {
+  void* p = nullptr;
+  if (n == 0) n = 1;
+  if (cudaMalloc(&p, n * sizeof(T)) != cudaSuccess) {
+    cudaGetLastError();
+    failed = true;
+    set_error(PL_ERR_NOMEM, "cudaMalloc of %zu bytes failed (MinGRU session)", n * sizeof(T));
+    return nullptr;
+  }
+  if (zero) cudaMemset(p, 0, n * sizeof(T));
+  list.push_back(p);
+  return (T*)p;
+}
+void free_list(std::vector<void*>& list) {
+  for (void* p : list) cudaFree(p);
+  list.clear();
+}
+
+int check_net(const pl_mg_net* net) {
+  PL_REQUIRE(net != nullptr, PL_ERR_INVALID, "MinGRU: NULL network description");
+  PL_REQUIRE(net->D > 0 && net->H > 0 && net->L > 0 && net->A > 0, PL_ERR_INVALID,
+             "MinGRU: D, H, L and A must be positive");
+  PL_REQUIRE(net->K == 2 || net->K == 3, PL_ERR_INVALID, "MinGRU: K must be 2 or 3 (got %zu)", net->K);
+  PL_REQUIRE(net->enc_act == 0 || net->enc_act == 1, PL_ERR_INVALID, "MinGRU: enc_act must be 0 or 1");
+  PL_REQUIRE(net->H < (1u << 20) && net->D < (1u << 20) && net->A < 4096 && net->L < 256, PL_ERR_INVALID,
+             "MinGRU: network extents out of range");
+  return PL_OK;
+}
+MgShape shape_of(const pl_mg_net* net) {
+  MgShape s;
+  s.D = (long)net->D;
+  s.H = (long)net->H;
+  s.L = (long)net->L;
+  s.A = (long)net->A;
+  s.K = (long)net->K;
+  s.enc_act = net->enc_act;
+  return s;
+}
+
+int ensure_work(pl_mg* s, const MgShape& sh, long Bmb, long T, bool fast) {
+  auto& w = s->w;
+  if (s->have_work && w.sh == sh && w.Bmb == Bmb && w.T == T && w.fast == fast) return PL_OK;
+  if (fast) PL_REQUIRE(sh.H % 8 == 0, PL_ERR_UNSUPPORTED, "MinGRU bf16 tier needs H %% 8 == 0 (H=%ld)", sh.H);
+  free_list(w.allocs);
+  s->have_work = false;
+  s->shadow_src = 0;
+  s->grad_fresh = false;
+  w = pl_mg::Work();
+  w.sh = sh;
+  w.Bmb = Bmb;
+  w.T = T;
+  w.fast = fast;
+  const long R = T * Bmb, H = sh.H, KH = sh.K * sh.H, L = sh.L, A = sh.A;
+  w.R = R;
+  w.Dp = fast ? rup(sh.D, 64) : sh.D;
+  w.Op = fast ? rup(A + 1, 64) : A + 1;
+  const size_t es = fast ? 2 : 4;
+  bool f = false;
+  auto act_buf = [&](long n) -> void* { return (void*)mg_alloc<char>(w.allocs, (size_t)n * es, f); };
+  w.X = act_buf(R * w.Dp);
+  if (sh.enc_act) w.Z = act_buf(R * H);
+  for (long l = 0; l <= L; l++) w.h.push_back(act_buf(R * H));
+  for (long l = 0; l < L; l++) {
+    w.Y.push_back(act_buf(R * KH));
+    w.Os.push_back(act_buf(R * H));
+  }
+  w.Out = mg_alloc<float>(w.allocs, (size_t)R * w.Op, f);
+  w.dOut = act_buf(R * w.Op);
+  w.dh[0] = act_buf(R * H);
+  w.dh[1] = act_buf(R * H);
+  w.dY = act_buf(R * KH);
+  if (sh.K == 3) w.dhn = act_buf(R * H);
+  w.act_i = mg_alloc<int>(w.allocs, R, f);
+  w.adv_f = mg_alloc<float>(w.allocs, R, f);
+  w.ret_f = mg_alloc<float>(w.allocs, R, f);
+  w.olp_f = mg_alloc<float>(w.allocs, R, f);
+  w.ov_f = mg_alloc<float>(w.allocs, R, f);
+  w.term_f = mg_alloc<float>(w.allocs, R, f);
+  w.newlp = mg_alloc<float>(w.allocs, R, f);
+  w.newval = mg_alloc<float>(w.allocs, R, f);
+  w.lossrow = mg_alloc<float>(w.allocs, (size_t)R * 8, f);
+  w.ms = mg_alloc<double>(w.allocs, 4, f);
+  // shadows (zeroed: the padding of the bf16 operands must read as zero)
+  w.Wenc = (void*)mg_alloc<char>(w.allocs, (size_t)H * w.Dp * es, f, true);
+  for (long l = 0; l < L; l++) w.Wl.push_back((void*)mg_alloc<char>(w.allocs, (size_t)KH * H * es, f, true));
+  w.Wout = (void*)mg_alloc<char>(w.allocs, (size_t)w.Op * H * es, f, true);
+  w.benc = mg_alloc<float>(w.allocs, H, f, true);
+  w.bout = mg_alloc<float>(w.allocs, w.Op, f, true);
+  const long P = sh.P();
+  w.grad = mg_alloc<float>(w.allocs, P, f);
+  w.gout = mg_alloc<float>(w.allocs, (size_t)(A + 1) * H, f);
+  w.gbout = mg_alloc<float>(w.allocs, w.Op, f);
+  const long chunks = (R + 255) / 256;
+  w.colpart_elems = chunks * std::max<long>(H, w.Op);
+  w.colpart = mg_alloc<float>(w.allocs, w.colpart_elems, f);
+  w.splitk_elems = std::max<long>(std::max<long>(8 * KH * H, 64 * (A + 1) * H), 64 * H * std::max<long>(sh.D, 64));
+  if (fast) w.splitk = mg_alloc<float>(w.allocs, w.splitk_elems, f);
+  w.cc = mg_alloc<double>(w.allocs, 2, f);
+  w.gn_part = mg_alloc<double>(w.allocs, 4096, f);
+  w.g64 = mg_alloc<double>(w.allocs, P, f);
+  w.params_in = mg_alloc<double>(w.allocs, P, f);
+  // Muon workspace: every matrix wide-side up (m = min, n = max)
+  long mmax = 1, nmax = 1, nprod = 1;
+  auto fit = [&](long r, long c) {
+    mmax = std::max(mmax, std::min(r, c));
+    nmax = std::max(nmax, std::max(r, c));
+    nprod = std::max(nprod, r * c);
+  };
+  fit(H, sh.D);
+  fit(KH, H);
+  fit(A, H);
+  fit(1, H);
+  if (fast) {
+    const long ldx = rup(nmax, 64), ldg = rup(mmax, 64);
+    w.ns.ldx = ldx;
+    w.ns.ldg = ldg;
+    w.ns.X0 = mg_alloc<bf16>(w.allocs, (size_t)rup(mmax, 128) * ldx, f, true);
+    w.ns.X1 = mg_alloc<bf16>(w.allocs, (size_t)rup(mmax, 128) * ldx, f, true);
+    w.ns.G = mg_alloc<bf16>(w.allocs, (size_t)rup(mmax, 128) * ldg, f, true);
+    w.ns.B = mg_alloc<bf16>(w.allocs, (size_t)rup(mmax, 128) * ldg, f, true);
+    w.ns.Xf = mg_alloc<float>(w.allocs, (size_t)mmax * ldx, f);
+    w.ns.U = mg_alloc<double>(w.allocs, nprod, f);
+    w.ns.part = mg_alloc<double>(w.allocs, 4096, f);
+  } else {
+    size_t ws = std::max(exact_ws_doubles((int)H, (int)sh.D), exact_ws_doubles((int)KH, (int)H));
+    ws = std::max(ws, exact_ws_doubles((int)A, (int)H));
+    ws = std::max(ws, exact_ws_doubles(1, (int)H));
+    w.exact_ws = mg_alloc<double>(w.allocs, ws, f);
+  }
+  if (f) {
+    free_list(w.allocs);
+    return PL_ERR_NOMEM;
+  }
+  PL_CUDA(cudaDeviceSynchronize());  // the zeroing memsets above ran on the legacy stream
+  s->have_work = true;
+  return PL_OK;
+}
+
+// Shadows from f64 params (device): fast = bf16 matrices + fp32 biases, tight = fp32 copies.
+int refresh_shadows(pl_mg* s, const double* par, cudaStream_t st) {
+  auto& w = s->w;
+  const MgShape& sh = w.sh;
+  const long H = sh.H, KH = sh.K * sh.H, A = sh.A;
+  int rc;
+  if (w.fast) {
+    rc = launch_w_to_bf16(par + sh.oWenc(), (int)H, (int)sh.D, (bf16*)w.Wenc, w.Dp, st);
+    for (long l = 0; !rc && l < sh.L; l++)
+      rc = launch_w_to_bf16(par + sh.oLayer(l), (int)KH, (int)H, (bf16*)w.Wl[l], H, st);
+    if (!rc) rc = launch_w_to_bf16(par + sh.oWdec(), (int)A, (int)H, (bf16*)w.Wout, H, st);
+    if (!rc) rc = launch_w_to_bf16(par + sh.oWval(), 1, (int)H, (bf16*)w.Wout + A * H, H, st);
+  } else {
+    rc = launch_f64_to_f32(par + sh.oWenc(), H * sh.D, (float*)w.Wenc, st);
+    for (long l = 0; !rc && l < sh.L; l++) rc = launch_f64_to_f32(par + sh.oLayer(l), KH * H, (float*)w.Wl[l], st);
+    if (!rc) rc = launch_f64_to_f32(par + sh.oWdec(), A * H, (float*)w.Wout, st);
+    if (!rc) rc = launch_f64_to_f32(par + sh.oWval(), H, (float*)w.Wout + A * H, st);
+  }
+  if (!rc) rc = launch_f64_to_f32(par + sh.oBenc(), H, w.benc, st);
+  if (!rc) rc = launch_f64_to_f32(par + sh.oBdec(), A, w.bout, st);
+  if (!rc) rc = launch_f64_to_f32(par + sh.oBval(), 1, w.bout + A, st);
+  return rc;
+}
+
+template <typename S>
+int colsum(pl_mg* s, const S* M, long R, long ld, int N, float* out, cudaStream_t st) {
+  auto& w = s->w;
+  const int rows_per = 256;
+  const int chunks = (int)((R + rows_per - 1) / rows_per);
+  PL_REQUIRE((long)chunks * N <= w.colpart_elems, PL_ERR_INVALID, "MinGRU colsum scratch too small");
+  dim3 g1((unsigned)((N + 127) / 128), (unsigned)chunks);
+  mg_colsum_part_kernel<S><<<g1, 128, 0, st>>>(M, R, ld, N, rows_per, w.colpart);
+  mg_colsum_final_kernel<<<(unsigned)((N + 127) / 128), 128, 0, st>>>(w.colpart, chunks, N, out);
+  count_launch(2);
+  PL_LAUNCH("mg_colsum_kernel");
+  return PL_OK;
+}
+
+// Weight gradient C[out x in] (fp32, ld in) = dZ^T Hin over R rows (both MN-major) with split-K
+// sized to fill the GPU.
+int wgrad_tc(pl_mg* s, const void* dZ, long ldz, int out, const void* Hin, long ldh, int in, long R, float* dst,
+             cudaStream_t st) {
+  auto& w = s->w;
+  Operand A{dZ, R, out, ldz, 1, 0};
+  Operand B{Hin, R, in, ldh, 1, 0};
+  const int bn = in <= 128 ? 128 : 256;
+  const long tiles = ceil_div(out, 128) * ceil_div(in, bn);
+  const long kb = ceil_div(R, 64);
+  int S = (int)std::min<long>(std::max<long>(1, (2 * 148 + tiles - 1) / tiles), 64);
+  while (S > 1 && kb / S < 4) S--;
+  while (S > 1 && (long)S * out * in > w.splitk_elems) S--;
+  EpiArgs e{};
+  e.ldo = in;
+  e.out_rows = out;
+  e.out_cols = in;
+  e.alpha = 1.f;
+  if (S == 1) {
+    e.out = dst;
+    return gemm_launch(bn, EPI_F32, true, true, A, B, out, in, (int)R, 1, e, st);
+  }
+  e.out = w.splitk;
+  e.out_bstride = (long)out * in;
+  e.k_splits = S;
+  int rc = gemm_launch(bn, EPI_F32, true, true, A, B, out, in, (int)R, 1, e, st);
+  if (rc) return rc;
+  return launch_splitk_reduce(w.splitk, S, (long)out * in, dst, st);
+}
+
+inline int pick_bn_n(long n) { return n <= 64 ? 64 : (n <= 128 ? 128 : 256); }
+
+// The BPTT gradient of the minibatch already gathered into the work buffers (X, act_i, adv_f,
+// ret_f, olp_f, ov_f, term_f): forward, PPO head, backward; summed gradient into w.grad.
+template <typename S>
+int bptt(pl_mg* s, double vf, double ent, double clip, double vfclip, bool losses, cudaStream_t st) {
+  auto& w = s->w;
+  const MgShape& sh = w.sh;
+  const long R = w.R, H = sh.H, KH = sh.K * sh.H, L = sh.L, A = sh.A, D = sh.D;
+  const int Bmb = (int)w.Bmb, T = (int)w.T;
+  const bool fast = w.fast;
+  const int enc_act = sh.enc_act ? 1 : 2;
+  float* grad = w.grad;
+  int rc;
+  // ---- encoder: h0 = enc(X W_enc^T + b_enc)
+  if (fast) {
+    Operand opA{w.X, R, w.Dp, w.Dp, 1, 0};
+    Operand opB{w.Wenc, H, w.Dp, w.Dp, 1, 0};
+    EpiArgs e{};
+    e.out = w.h[0];
+    e.ldo = H;
+    e.out_rows = (int)R;
+    e.out_cols = (int)H;
+    e.bias = w.benc;
+    e.act = enc_act;
+    e.out2 = sh.enc_act ? w.Z : nullptr;
+    e.ldo2 = H;
+    rc = gemm_launch(pick_bn_n(H), EPI_FWD, false, false, opA, opB, (int)R, (int)H, (int)w.Dp, 1, e, st);
+  } else {
+    float* Z = sh.enc_act ? (float*)w.Z : (float*)w.h[0];
+    rc = launch_sgemm((int)R, (int)H, (int)D, (const float*)w.X, D, 1, (const float*)w.Wenc, D, 1, Z, H, 1.f, st);
+    if (!rc) rc = launch_bias_act_f32(Z, sh.enc_act ? (float*)w.h[0] : nullptr, w.benc, R, (int)H, enc_act, st);
+  }
+  if (rc) return rc;
+  // ---- layers
+  for (long l = 0; l < L; l++) {
+    if (fast) {
+      Operand opA{w.h[l], R, H, H, 1, 0};
+      Operand opB{w.Wl[l], KH, H, H, 1, 0};
+      EpiArgs e{};
+      e.out = w.Y[l];
+      e.ldo = KH;
+      e.out_rows = (int)R;
+      e.out_cols = (int)KH;
+      e.alpha = 1.f;
+      rc = gemm_launch(256, EPI_BF16, false, false, opA, opB, (int)R, (int)KH, (int)H, 1, e, st);
+    } else {
+      rc = launch_sgemm((int)R, (int)KH, (int)H, (const float*)w.h[l], H, 1, (const float*)w.Wl[l], H, 1,
+                        (float*)w.Y[l], KH, 1.f, st);
+    }
+    if (rc) return rc;
+    const unsigned nb = (unsigned)((Bmb * H + 255) / 256);
+    if (sh.K == 3)
+      mg_scan_fwd_kernel<S, 3><<<nb, 256, 0, st>>>((const S*)w.Y[l], (const S*)w.h[l], (S*)w.h[l + 1], (S*)w.Os[l],
+                                                    w.term_f, Bmb, (int)H, T);
+    else
+      mg_scan_fwd_kernel<S, 2><<<nb, 256, 0, st>>>((const S*)w.Y[l], (const S*)w.h[l], (S*)w.h[l + 1], (S*)w.Os[l],
+                                                    w.term_f, Bmb, (int)H, T);
+    count_launch();
+    PL_LAUNCH("mg_scan_fwd_kernel");
+  }
+  // ---- heads: Out = h_L W_out^T (bias added by the row kernel)
+  if (fast) {
+    Operand opA{w.h[L], R, H, H, 1, 0};
+    Operand opB{w.Wout, w.Op, H, H, 1, 0};
+    EpiArgs e{};
+    e.out = w.Out;
+    e.ldo = w.Op;
+    e.out_rows = (int)R;
+    e.out_cols = (int)(A + 1);
+    e.alpha = 1.f;
+    rc = gemm_launch(128, EPI_F32, false, false, opA, opB, (int)R, (int)(A + 1), (int)H, 1, e, st);
+  } else {
+    rc = launch_sgemm((int)R, (int)(A + 1), (int)H, (const float*)w.h[L], H, 1, (const float*)w.Wout, H, 1, w.Out,
+                      w.Op, 1.f, st);
+  }
+  if (rc) return rc;
+  mg_ppo_rows_kernel<S><<<blocks_for(R, 128), 128, 0, st>>>(
+      w.Out, (int)w.Op, w.bout, R, (int)A, (int)w.Op, w.act_i, w.adv_f, w.ret_f, w.olp_f, w.ov_f, (float)vf,
+      (float)ent, (float)clip, (float)vfclip, (S*)w.dOut, w.newlp, w.newval, losses ? w.lossrow : nullptr);
+  count_launch();
+  PL_LAUNCH("mg_ppo_rows_kernel");
+  // ---- head gradients
+  rc = colsum<S>(s, (const S*)w.dOut, R, w.Op, (int)(A + 1), w.gbout, st);
+  if (rc) return rc;
+  if (fast)
+    rc = wgrad_tc(s, w.dOut, w.Op, (int)(A + 1), w.h[L], H, (int)H, R, w.gout, st);
+  else
+    rc = launch_sgemm((int)(A + 1), (int)H, (int)R, (const float*)w.dOut, 1, w.Op, (const float*)w.h[L], 1, H, w.gout,
+                      H, 1.f, st);
+  if (rc) return rc;
+  mg_head_scatter_kernel<<<blocks_for((A + 1) * H), 256, 0, st>>>(w.gout, w.gbout, (int)A, (int)H,
+                                                                   grad + sh.oWdec(), grad + sh.oBdec(),
+                                                                   grad + sh.oWval(), grad + sh.oBval());
+  count_launch();
+  PL_LAUNCH("mg_head_scatter_kernel");
+  // dh_L = dOut W_out
+  int cur = 0;
+  if (fast) {
+    Operand opA{w.dOut, R, w.Op, w.Op, 1, 0};
+    Operand opB{w.Wout, w.Op, H, H, 1, 0};  // MN-major: rows = K (outputs), cols = N (hidden)
+    EpiArgs e{};
+    e.out = w.dh[cur];
+    e.ldo = H;
+    e.out_rows = (int)R;
+    e.out_cols = (int)H;
+    e.alpha = 1.f;
+    rc = gemm_launch(256, EPI_BF16, false, true, opA, opB, (int)R, (int)H, (int)w.Op, 1, e, st);
+  } else {
+    rc = launch_sgemm((int)R, (int)H, (int)(A + 1), (const float*)w.dOut, w.Op, 1, (const float*)w.Wout, 1, H,
+                      (float*)w.dh[cur], H, 1.f, st);
+  }
+  if (rc) return rc;
+  // ---- layers, top down
+  for (long l = L - 1; l >= 0; l--) {
+    const unsigned nb = (unsigned)((Bmb * H + 255) / 256);
+    if (sh.K == 3)
+      mg_scan_bwd_kernel<S, 3><<<nb, 256, 0, st>>>((const S*)w.Y[l], (const S*)w.Os[l], (const S*)w.h[l],
+                                                    (const S*)w.dh[cur], (S*)w.dY, (S*)w.dhn, w.term_f, Bmb, (int)H,
+                                                    T);
+    else
+      mg_scan_bwd_kernel<S, 2><<<nb, 256, 0, st>>>((const S*)w.Y[l], (const S*)w.Os[l], (const S*)w.h[l],
+                                                    (const S*)w.dh[cur], (S*)w.dY, nullptr, w.term_f, Bmb, (int)H, T);
+    count_launch();
+    PL_LAUNCH("mg_scan_bwd_kernel");
+    // dW_l = dY^T h_l
+    if (fast)
+      rc = wgrad_tc(s, w.dY, KH, (int)KH, w.h[l], H, (int)H, R, grad + sh.oLayer(l), st);
+    else
+      rc = launch_sgemm((int)KH, (int)H, (int)R, (const float*)w.dY, 1, KH, (const float*)w.h[l], 1, H,
+                        grad + sh.oLayer(l), H, 1.f, st);
+    if (rc) return rc;
+    // dh_l = dY W_l (+ the highway part)
+    const int nxt = cur ^ 1;
+    if (fast) {
+      Operand opA{w.dY, R, KH, KH, 1, 0};
+      Operand opB{w.Wl[l], KH, H, H, 1, 0};  // MN-major: rows = K (= K*H), cols = N (= H)
+      EpiArgs e{};
+      e.out = w.dh[nxt];
+      e.ldo = H;
+      e.out_rows = (int)R;
+      e.out_cols = (int)H;
+      e.alpha = 1.f;
+      if (sh.K == 3) {
+        e.aux = (const bf16*)w.dhn;
+        e.ld_aux = H;
+        e.beta = 1.f;
+      }
+      rc = gemm_launch(256, EPI_BF16, false, true, opA, opB, (int)R, (int)H, (int)KH, 1, e, st);
+    } else {
+      rc = launch_sgemm((int)R, (int)H, (int)KH, (const float*)w.dY, KH, 1, (const float*)w.Wl[l], 1, H,
+                        (float*)w.dh[nxt], H, 1.f, st);
+      if (!rc && sh.K == 3) {
+        mg_axpy_kernel<<<blocks_for(R * H), 256, 0, st>>>((float*)w.dh[nxt], (const float*)w.dhn, R * H);
+        count_launch();
+        PL_LAUNCH("mg_axpy_kernel");
+      }
+    }
+    if (rc) return rc;
+    cur = nxt;
+  }
+  // ---- encoder gradients
+  if (sh.enc_act) {
+    mg_act_grad_kernel<S><<<blocks_for(R * H), 256, 0, st>>>((S*)w.dh[cur], (const S*)w.Z, R * H, 1);
+    count_launch();
+    PL_LAUNCH("mg_act_grad_kernel");
+  }
+  rc = colsum<S>(s, (const S*)w.dh[cur], R, H, (int)H, grad + sh.oBenc(), st);
+  if (rc) return rc;
+  if (fast) {
+    // dW_enc [H x D] = dE^T X (X padded to Dp; only D columns are written)
+    auto& ww = s->w;
+    Operand opA{ww.dh[cur], R, H, H, 1, 0};
+    Operand opB{ww.X, R, ww.Dp, ww.Dp, 1, 0};
+    const int bn = D <= 128 ? 128 : 256;
+    const long tiles = ceil_div(H, 128) * ceil_div(D, bn);
+    const long kb = ceil_div(R, 64);
+    int Sk = (int)std::min<long>(std::max<long>(1, (2 * 148 + tiles - 1) / tiles), 64);
+    while (Sk > 1 && kb / Sk < 4) Sk--;
+    while (Sk > 1 && (long)Sk * H * D > ww.splitk_elems) Sk--;
+    EpiArgs e{};
+    e.ldo = D;
+    e.out_rows = (int)H;
+    e.out_cols = (int)D;
+    e.alpha = 1.f;
+    if (Sk == 1) {
+      e.out = grad + sh.oWenc();
+      rc = gemm_launch(bn, EPI_F32, true, true, opA, opB, (int)H, (int)D, (int)R, 1, e, st);
+    } else {
+      e.out = ww.splitk;
+      e.out_bstride = H * D;
+      e.k_splits = Sk;
+      rc = gemm_launch(bn, EPI_F32, true, true, opA, opB, (int)H, (int)D, (int)R, 1, e, st);
+      if (!rc) rc = launch_splitk_reduce(ww.splitk, Sk, H * D, grad + sh.oWenc(), st);
+    }
+  } else {
+    rc = launch_sgemm((int)H, (int)D, (int)R, (const float*)w.dh[cur], 1, H, (const float*)w.X, 1, D,
+                      grad + sh.oWenc(), D, 1.f, st);
+  }
+  return rc;
+}
+
+int run_bptt(pl_mg* s, double vf, double ent, double clip, double vfclip, bool losses, cudaStream_t st) {
+  return s->w.fast ? bptt<bf16>(s, vf, ent, clip, vfclip, losses, st) : bptt<float>(s, vf, ent, clip, vfclip, losses, st);
+}
+
+// 7-loss channel reduction (the reference's host fold, ffi/puffercuda.cu:5446-5484)
+int reduce_losses(pl_mg* s, double vfCoef, double entCoef, double out[7], cudaStream_t st) {
+  auto& w = s->w;
+  std::vector<float> h((size_t)w.R * 8);
+  PL_CUDA(cudaMemcpyAsync(h.data(), w.lossrow, sizeof(float) * h.size(), cudaMemcpyDeviceToHost, st));
+  PL_CUDA(cudaStreamSynchronize(st));
+  double sPg = 0, sV = 0, sEnt = 0, sOld = 0, sKl = 0, nclip = 0;
+  for (long r = 0; r < w.R; r++) {
+    const float* q = h.data() + r * 8;
+    sPg += q[0];
+    sV += q[1];
+    sEnt += q[2];
+    sOld += q[3];
+    sKl += q[4];
+    nclip += q[5];
+  }
+  const double n = (double)w.R;
+  out[0] = sPg / n;
+  out[1] = sV / n;
+  out[2] = sEnt / n;
+  out[3] = out[0] + vfCoef * out[1] - entCoef * out[2];
+  out[4] = sOld / n;
+  out[5] = sKl / n;
+  out[6] = nclip / n;
+  return PL_OK;
+}
+
+int muon_step(pl_mg* s, size_t handle, const double* gClip, double lr, double wd, double mu, double eps,
+              double maxGradNorm, double gscale, const double* coeffs, int iters, cudaStream_t st) {
+  auto& w = s->w;
+  const MgShape& sh = w.sh;
+  const long P = sh.P(), H = sh.H, KH = sh.K * sh.H, A = sh.A;
+  double* pm = (double*)handle;
+  double* mom = pm + P;
+  int rc = PL_OK;
+  struct Mat {
+    long rows, cols, oW;
+    void* shadow;
+    long ldw;
+  };
+  struct Bias {
+    long n, oB;
+    float* shadow;
+  };
+  std::vector<Mat> mats;
+  mats.push_back({H, sh.D, sh.oWenc(), w.Wenc, w.Dp});
+  for (long l = 0; l < sh.L; l++) mats.push_back({KH, H, sh.oLayer(l), w.Wl[l], H});
+  mats.push_back({A, H, sh.oWdec(), w.Wout, H});
+  const size_t es = w.fast ? 2 : 4;
+  mats.push_back({1, H, sh.oWval(), (char*)w.Wout + (size_t)A * H * es, H});
+  const Bias biases[3] = {{H, sh.oBenc(), w.benc}, {A, sh.oBdec(), w.bout}, {1, sh.oBval(), w.bout + A}};
+  if (gClip) {
+    // an already clipped host gradient: cc = 1
+    if (w.fast) {
+      PL_CUDA(cudaMemcpyAsync(w.g64, gClip, sizeof(double) * P, cudaMemcpyHostToDevice, st));
+      mg_f64_to_f32_kernel<<<blocks_for(P), 256, 0, st>>>(w.g64, P, w.grad);
+      mg_fill_kernel<<<1, 32, 0, st>>>(w.cc, 1.0, 1);
+      count_launch(2);
+      PL_LAUNCH("mg_gclip_upload");
+    }
+  } else {
+    PL_REQUIRE(s->grad_fresh, PL_ERR_INVALID,
+               "MinGRU Muon: no resident gradient (call pl_mg_grad first, or pass a clipped host gradient)");
+    rc = launch_gradnorm(w.grad, P, gscale, maxGradNorm, w.gn_part, w.cc, st);
+    if (rc) return rc;
+  }
+  s->grad_fresh = false;
+  if (w.fast) {
+    for (const Mat& m : mats) {
+      const long n = m.rows * m.cols;
+      const int mm = (int)std::min(m.rows, m.cols), nn = (int)std::max(m.rows, m.cols);
+      int nparts = 0;
+      rc = launch_nesterov(w.grad + m.oW, w.cc, mom + m.oW, w.ns.U, mu, n, w.ns.part, &nparts, st);
+      if (!rc) rc = launch_ns_input(w.ns.U, w.ns.part, nparts, (int)m.rows, (int)m.cols, eps, w.ns.X0, w.ns.ldx, st);
+      if (!rc) rc = ns_run(mm, nn, coeffs, iters, w.ns, w.ns.X0, w.ns.ldx, w.ns.Xf, w.ns.ldx, st);
+      const double r = (double)m.rows / (double)m.cols;
+      if (!rc)
+        rc = launch_ns_finalize(w.ns.Xf, w.ns.ldx, (int)m.rows, (int)m.cols, 1.0 - lr * wd, lr * sqrt(r > 1.0 ? r : 1.0),
+                                pm + m.oW, (bf16*)m.shadow, m.ldw, st);
+      if (rc) return rc;
+    }
+    for (const Bias& b : biases) {
+      rc = launch_stepvec_fast(w.grad + b.oB, w.cc, pm + b.oB, mom + b.oB, b.shadow, lr, wd, mu, (int)b.n, st);
+      if (rc) return rc;
+    }
+  } else {
+    double cc = 1.0;
+    if (gClip) {
+      PL_CUDA(cudaMemcpyAsync(w.g64, gClip, sizeof(double) * P, cudaMemcpyHostToDevice, st));
+    } else {
+      PL_CUDA(cudaMemcpyAsync(&cc, w.cc, sizeof(double), cudaMemcpyDeviceToHost, st));
+      PL_CUDA(cudaStreamSynchronize(st));
+      rc = launch_f32_to_f64(w.grad, P, w.g64, st);
+      if (rc) return rc;
+    }
+    rc = set_ns_coeffs(coeffs, iters, st);
+    if (rc) return rc;
+    for (const Mat& m : mats) {
+      rc = muon_mat_exact((int)m.rows, (int)m.cols, pm + m.oW, mom + m.oW, w.g64 + m.oW, cc, lr, wd, mu, eps, iters,
+                          w.exact_ws, st);
+      if (rc) return rc;
+    }
+    for (const Bias& b : biases) {
+      rc = stepvec_launch(pm + b.oB, mom + b.oB, w.g64 + b.oB, lr, wd, mu, cc, b.n, st);
+      if (rc) return rc;
+    }
+    rc = refresh_shadows(s, pm, st);
+    if (rc) return rc;
+  }
+  s->shadow_src = handle;
+  return PL_OK;
+}
+
+int alloc_columns(pl_mg* s) {
+  bool f = false;
+  const size_t NT = (size_t)s->N * s->T;
+  s->rew = mg_alloc<double>(s->allocs, NT, f);
+  s->term = mg_alloc<double>(s->allocs, NT, f);
+  s->act = mg_alloc<double>(s->allocs, NT, f);
+  s->logp = mg_alloc<double>(s->allocs, NT, f);
+  s->val0 = mg_alloc<double>(s->allocs, NT, f);
+  s->boot = mg_alloc<double>(s->allocs, s->N, f);
+  s->value = mg_alloc<double>(s->allocs, NT, f);
+  s->ratio = mg_alloc<double>(s->allocs, NT, f);
+  s->adv = mg_alloc<double>(s->allocs, NT, f);
+  s->l1 = mg_alloc<double>(s->allocs, s->N, f);
+  s->prio_p = mg_alloc<double>(s->allocs, s->N, f);
+  s->prio_cum = mg_alloc<double>(s->allocs, s->N, f);
+  s->lastw = mg_alloc<int>(s->allocs, s->N, f);
+  return f ? PL_ERR_NOMEM : PL_OK;
+}
+
+int ensure_sample(pl_mg* s, long Bmb) {
+  if (Bmb <= s->seg_cap) return PL_OK;
+  bool f = false;
+  s->seg = mg_alloc<double>(s->allocs, Bmb, f);
+  s->mbp = mg_alloc<double>(s->allocs, Bmb, f);
+  if (f) return PL_ERR_NOMEM;
+  s->seg_cap = Bmb;
+  return PL_OK;
+}
+
+int mg_vtrace_dev(pl_mg* s, double gamma, double lam, double rho, double c, cudaStream_t st) {
+  PL_REQUIRE(s->cols_valid, PL_ERR_INVALID, "MinGRU: no columns (call pl_mg_set_columns first)");
+  return pl_vtrace_f64_dev(s->rew, s->value, s->term, s->ratio, s->boot, (size_t)s->N, (size_t)s->T, gamma, lam, rho,
+                           c, s->adv, s->l1, st);
+}
+
+}  // namespace
+}  // namespace pl
+
+// ================================================================= C API
+extern "C" {
+
+size_t pl_mg_param_count(const pl_mg_net* net) {
+  if (pl::check_net(net)) return 0;
+  return (size_t)pl::shape_of(net).P();
+}
+
+int pl_mg_create(size_t N, size_t T, pl_mg** out) {
+  using namespace pl;
+  PL_REQUIRE(out != nullptr, PL_ERR_INVALID, "pl_mg_create: NULL out");
+  *out = nullptr;
+  PL_REQUIRE(N > 0 && T > 0 && N < (1u << 30) && T < (1u << 20) && N * T < (1ull << 31), PL_ERR_INVALID,
+             "pl_mg_create: bad extents N=%zu T=%zu", N, T);
+  int rc = require_device();
+  if (rc) return rc;
+  pl_mg* s = new pl_mg();
+  PL_CUDA(cudaGetDevice(&s->dev));
+  s->N = (long)N;
+  s->T = (long)T;
+  rc = alloc_columns(s);
+  if (rc) {
+    free_list(s->allocs);
+    delete s;
+    return rc;
+  }
+  *out = s;
+  return PL_OK;
+}
+
+int pl_mg_destroy(pl_mg* s) {
+  if (!s) return PL_OK;
+  cudaDeviceSynchronize();
+  pl::free_list(s->w.allocs);
+  pl::free_list(s->allocs);
+  if (s->traj_own) cudaFree(s->traj_own);
+  delete s;
+  return PL_OK;
+}
+
+static int mg_set_columns_impl(pl_mg* s, const double* rew, const double* term, const double* act, const double* logp,
+                               const double* val, const double* boot, cudaMemcpyKind kind, cudaStream_t st) {
+  using namespace pl;
+  PL_REQUIRE(s && rew && term && act && logp && val && boot, PL_ERR_INVALID, "pl_mg_set_columns: NULL argument");
+  const size_t NT = (size_t)s->N * s->T;
+  PL_CUDA(cudaMemcpyAsync(s->rew, rew, NT * 8, kind, st));
+  PL_CUDA(cudaMemcpyAsync(s->term, term, NT * 8, kind, st));
+  PL_CUDA(cudaMemcpyAsync(s->act, act, NT * 8, kind, st));
+  PL_CUDA(cudaMemcpyAsync(s->logp, logp, NT * 8, kind, st));
+  PL_CUDA(cudaMemcpyAsync(s->val0, val, NT * 8, kind, st));
+  PL_CUDA(cudaMemcpyAsync(s->boot, boot, (size_t)s->N * 8, kind, st));
+  PL_CUDA(cudaMemcpyAsync(s->value, s->val0, NT * 8, cudaMemcpyDeviceToDevice, st));
+  mg_fill_kernel<<<blocks_for((long)NT), 256, 0, st>>>(s->ratio, 1.0, (long)NT);
+  count_launch();
+  PL_LAUNCH("mg_fill_kernel");
+  s->cols_valid = true;
+  s->prio_fresh = false;
+  return PL_OK;
+}
+
+int pl_mg_set_columns(pl_mg* s, const double* rew, const double* term, const double* act, const double* logp,
+                      const double* val, const double* boot) {
+  int rc = mg_set_columns_impl(s, rew, term, act, logp, val, boot, cudaMemcpyHostToDevice, 0);
+  if (rc) return rc;
+  PL_CUDA(cudaStreamSynchronize(0));
+  return PL_OK;
+}
+
+int pl_mg_set_columns_dev(pl_mg* s, const double* rew, const double* term, const double* act, const double* logp,
+                          const double* val, const double* boot, void* stream) {
+  return mg_set_columns_impl(s, rew, term, act, logp, val, boot, cudaMemcpyDeviceToDevice, (cudaStream_t)stream);
+}
+
+int pl_mg_set_obs(pl_mg* s, const double* obs, size_t D) {
+  using namespace pl;
+  PL_REQUIRE(s && obs && D > 0, PL_ERR_INVALID, "pl_mg_set_obs: bad argument");
+  const size_t n = (size_t)s->N * s->T * D;
+  if (s->traj_own && s->trajD != (long)D) {
+    cudaFree(s->traj_own);
+    s->traj_own = nullptr;
+  }
+  if (!s->traj_own) {
+    if (cudaMalloc(&s->traj_own, n * sizeof(float)) != cudaSuccess) {
+      cudaGetLastError();
+      s->traj_own = nullptr;
+      return set_error(PL_ERR_NOMEM, "pl_mg_set_obs: cudaMalloc of %zu bytes failed", n * sizeof(float));
+    }
+  }
+  double* tmp = (double*)scratch(20, n * sizeof(double));
+  if (!tmp) return PL_ERR_NOMEM;
+  PL_CUDA(cudaMemcpy(tmp, obs, n * sizeof(double), cudaMemcpyHostToDevice));
+  mg_f64_to_f32_kernel<<<blocks_for((long)n), 256>>>(tmp, (long)n, s->traj_own);
+  count_launch();
+  PL_LAUNCH("mg_f64_to_f32_kernel");
+  PL_CUDA(cudaDeviceSynchronize());
+  s->traj = s->traj_own;
+  s->trajD = (long)D;
+  return PL_OK;
+}
+
+int pl_mg_set_obs_dev(pl_mg* s, const float* traj, size_t D) {
+  using namespace pl;
+  PL_REQUIRE(s && traj && D > 0, PL_ERR_INVALID, "pl_mg_set_obs_dev: bad argument");
+  s->traj = traj;
+  s->trajD = (long)D;
+  return PL_OK;
+}
+
+int pl_mg_vtrace(pl_mg* s, double gamma, double lam, double rhoClip, double cClip, double* advL1, void* stream) {
+  using namespace pl;
+  PL_REQUIRE(s != nullptr, PL_ERR_INVALID, "pl_mg_vtrace: NULL session");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = mg_vtrace_dev(s, gamma, lam, rhoClip, cClip, st);
+  if (rc) return rc;
+  if (advL1) {
+    PL_CUDA(cudaMemcpyAsync(advL1, s->l1, sizeof(double) * s->N, cudaMemcpyDeviceToHost, st));
+    PL_CUDA(cudaStreamSynchronize(st));
+  }
+  return PL_OK;
+}
+
+int pl_mg_vtrace_prio(pl_mg* s, double gamma, double lam, double rhoClip, double cClip, size_t mbSegs,
+                      double prioAlpha, double annealBeta, uint64_t rng, void* stream) {
+  using namespace pl;
+  PL_REQUIRE(s != nullptr && mbSegs > 0 && mbSegs < (1u << 30), PL_ERR_INVALID, "pl_mg_vtrace_prio: bad argument");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = mg_vtrace_dev(s, gamma, lam, rhoClip, cClip, st);
+  if (rc) return rc;
+  rc = ensure_sample(s, (long)mbSegs);
+  if (rc) return rc;
+  mg_prio_kernel<<<1, 1024, 0, st>>>(s->l1, s->N, (long)mbSegs, prioAlpha, annealBeta, (unsigned long long)rng,
+                                     s->prio_p, s->prio_cum, s->seg, s->mbp);
+  count_launch();
+  PL_LAUNCH("mg_prio_kernel");
+  s->prio_B = (long)mbSegs;
+  s->prio_fresh = true;
+  return PL_OK;
+}
+
+int pl_mg_grad(pl_mg* s, const pl_mg_net* net, size_t handle, const double* params, const double* segIdx,
+               const double* mbPrio, size_t Bmb, double vfCoef, double entCoef, double clipEps, double vfClip,
+               uint8_t bf16f, void* stream) {
+  using namespace pl;
+  PL_REQUIRE(s != nullptr, PL_ERR_INVALID, "pl_mg_grad: NULL session");
+  int rc = check_net(net);
+  if (rc) return rc;
+  PL_REQUIRE((handle != 0) != (params != nullptr), PL_ERR_INVALID,
+             "pl_mg_grad: pass exactly one of a policy handle and host params");
+  PL_REQUIRE((segIdx == nullptr) == (mbPrio == nullptr), PL_ERR_INVALID,
+             "pl_mg_grad: segIdx and mbPrio are both host arrays or both NULL (the resident sample)");
+  PL_REQUIRE(Bmb > 0 && Bmb < (1u << 24), PL_ERR_INVALID, "pl_mg_grad: bad minibatch size %zu", Bmb);
+  PL_REQUIRE(s->cols_valid, PL_ERR_INVALID, "pl_mg_grad: no columns (call pl_mg_set_columns first)");
+  PL_REQUIRE(s->traj && s->trajD == (long)net->D, PL_ERR_INVALID,
+             "pl_mg_grad: no obs trajectory of width D=%zu (call pl_mg_set_obs first)", net->D);
+  if (!segIdx)
+    PL_REQUIRE(s->prio_fresh && s->prio_B == (long)Bmb, PL_ERR_INVALID,
+               "pl_mg_grad: no resident sample of %zu segments (call pl_mg_vtrace_prio first)", Bmb);
+  cudaStream_t st = (cudaStream_t)stream;
+  const MgShape sh = shape_of(net);
+  const uint64_t l0 = pl_kernel_launch_count();
+  rc = ensure_work(s, sh, (long)Bmb, s->T, bf16f != 0);
+  if (rc) return rc;
+  rc = ensure_sample(s, (long)Bmb);
+  if (rc) return rc;
+  auto& w = s->w;
+  if (segIdx) {
+    PL_CUDA(cudaMemcpyAsync(s->seg, segIdx, sizeof(double) * Bmb, cudaMemcpyHostToDevice, st));
+    PL_CUDA(cudaMemcpyAsync(s->mbp, mbPrio, sizeof(double) * Bmb, cudaMemcpyHostToDevice, st));
+  }
+  s->prio_fresh = false;
+  // weights
+  if (params) {
+    PL_CUDA(cudaMemcpyAsync(w.params_in, params, sizeof(double) * sh.P(), cudaMemcpyHostToDevice, st));
+    rc = refresh_shadows(s, w.params_in, st);
+    s->shadow_src = 0;
+  } else if (s->shadow_src != handle) {
+    rc = refresh_shadows(s, (const double*)handle, st);
+    s->shadow_src = handle;
+  }
+  if (rc) return rc;
+  // gather
+  const int Bi = (int)Bmb, T = (int)s->T;
+  mg_adv_ms_kernel<<<1, 1024, 0, st>>>(s->adv, s->seg, Bi, T, w.ms);
+  mg_gather_scal_kernel<<<blocks_for(w.R), 256, 0, st>>>(s->act, s->logp, s->term, s->adv, s->value, s->seg, s->mbp,
+                                                         w.ms, Bi, T, w.act_i, w.adv_f, w.ret_f, w.olp_f, w.ov_f,
+                                                         w.term_f);
+  if (w.fast)
+    mg_gather_obs_kernel<__nv_bfloat16><<<blocks_for(w.R * w.Dp), 256, 0, st>>>(s->traj, s->seg, Bi, T, (int)sh.D,
+                                                                               (int)w.Dp, (__nv_bfloat16*)w.X);
+  else
+    mg_gather_obs_kernel<float><<<blocks_for(w.R * w.Dp), 256, 0, st>>>(s->traj, s->seg, Bi, T, (int)sh.D, (int)w.Dp,
+                                                                        (float*)w.X);
+  count_launch(3);
+  PL_LAUNCH("mg_gather_kernels");
+  const bool losses = loss_channel_on();
+  rc = run_bptt(s, vfCoef, entCoef, clipEps, vfClip, losses, st);
+  if (rc) return rc;
+  // replay iterate
+  PL_CUDA(cudaMemsetAsync(s->lastw, 0xFF, sizeof(int) * s->N, st));
+  mg_lastw_kernel<<<(unsigned)((Bi + 255) / 256), 256, 0, st>>>(s->lastw, s->seg, Bi);
+  mg_iterate_kernel<<<blocks_for(w.R), 256, 0, st>>>(s->value, s->ratio, s->logp, w.newlp, w.newval, s->seg, s->lastw,
+                                                     Bi, T);
+  count_launch(2);
+  PL_LAUNCH("mg_iterate_kernel");
+  if (losses) {
+    double lo[7];
+    rc = reduce_losses(s, vfCoef, entCoef, lo, st);
+    if (rc) return rc;
+    loss_channel_store(lo);
+  }
+  s->grad_fresh = true;
+  s->grad_rows = w.R;
+  s->launches = pl_kernel_launch_count() - l0;
+  return PL_OK;
+}
+
+int pl_mg_grad_download(pl_mg* s, double* grad, double* newlp, double* newval) {
+  using namespace pl;
+  PL_REQUIRE(s && s->have_work, PL_ERR_INVALID, "pl_mg_grad_download: no gradient");
+  auto& w = s->w;
+  const long P = w.sh.P();
+  PL_CUDA(cudaDeviceSynchronize());
+  if (grad) {
+    std::vector<float> g((size_t)P);
+    PL_CUDA(cudaMemcpy(g.data(), w.grad, sizeof(float) * P, cudaMemcpyDeviceToHost));
+    for (long i = 0; i < P; i++) grad[i] = (double)g[i];
+  }
+  std::vector<float> t((size_t)w.R);
+  if (newlp) {
+    PL_CUDA(cudaMemcpy(t.data(), w.newlp, sizeof(float) * w.R, cudaMemcpyDeviceToHost));
+    for (long i = 0; i < w.R; i++) newlp[i] = (double)t[i];
+  }
+  if (newval) {
+    PL_CUDA(cudaMemcpy(t.data(), w.newval, sizeof(float) * w.R, cudaMemcpyDeviceToHost));
+    for (long i = 0; i < w.R; i++) newval[i] = (double)t[i];
+  }
+  return device_error_check();
+}
+
+int pl_mg_muon(pl_mg* s, const pl_mg_net* net, size_t handle, const double* gClip, double lr, double wd, double mu,
+               double eps, double maxGradNorm, double gscale, const double* coeffs, size_t iters, uint8_t bf16f,
+               void* stream) {
+  using namespace pl;
+  PL_REQUIRE(s != nullptr && handle != 0, PL_ERR_INVALID, "pl_mg_muon: NULL session or handle");
+  int rc = check_net(net);
+  if (rc) return rc;
+  if (!coeffs) {
+    coeffs = &kMuonCoeffs[0][0];
+    iters = 5;
+  }
+  PL_REQUIRE(iters > 0 && iters <= 64, PL_ERR_INVALID, "pl_mg_muon: 1..64 Newton-Schulz steps");
+  const MgShape sh = shape_of(net);
+  const long Bmb = s->have_work ? s->w.Bmb : 1;
+  if (!(s->have_work && s->w.sh == sh && s->w.fast == (bf16f != 0))) {
+    PL_REQUIRE(gClip != nullptr, PL_ERR_INVALID,
+               "pl_mg_muon: no resident gradient for this network and tier (call pl_mg_grad first)");
+    rc = ensure_work(s, sh, Bmb, s->T, bf16f != 0);
+    if (rc) return rc;
+  }
+  const uint64_t l0 = pl_kernel_launch_count();
+  rc = muon_step(s, handle, gClip, lr, wd, mu, eps, maxGradNorm, gscale, coeffs, (int)iters, (cudaStream_t)stream);
+  s->launches += pl_kernel_launch_count() - l0;
+  return rc;
+}
+
+int pl_mg_read_state(pl_mg* s, double* value, double* ratio, double* adv) {
+  using namespace pl;
+  PL_REQUIRE(s != nullptr, PL_ERR_INVALID, "pl_mg_read_state: NULL session");
+  const size_t NT = (size_t)s->N * s->T;
+  PL_CUDA(cudaDeviceSynchronize());
+  if (value) PL_CUDA(cudaMemcpy(value, s->value, NT * 8, cudaMemcpyDeviceToHost));
+  if (ratio) PL_CUDA(cudaMemcpy(ratio, s->ratio, NT * 8, cudaMemcpyDeviceToHost));
+  if (adv) PL_CUDA(cudaMemcpy(adv, s->adv, NT * 8, cudaMemcpyDeviceToHost));
+  return device_error_check();
+}
+
+int pl_mg_update(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hyper* h, size_t numMB, size_t mbSegs,
+                 uint64_t* rng, double lr, void* stream) {
+  using namespace pl;
+  PL_REQUIRE(s && net && h && rng && handle, PL_ERR_INVALID, "pl_mg_update: NULL argument");
+  const uint64_t l0 = pl_kernel_launch_count();
+  const double gscale = 1.0 / (double)(mbSegs * (size_t)s->T);
+  for (size_t mb = 0; mb < numMB; mb++) {
+    int rc = pl_mg_vtrace_prio(s, h->gamma, h->lam, h->rhoClip, h->cClip, mbSegs, h->prioAlpha, h->annealBeta, *rng,
+                               stream);
+    if (rc) return rc;
+    *rng += (uint64_t)mbSegs * 0x9E3779B97F4A7C15ULL;
+    rc = pl_mg_grad(s, net, handle, nullptr, nullptr, nullptr, mbSegs, h->vfCoef, h->entCoef, h->clipEps, h->vfClip,
+                    h->bf16, stream);
+    if (rc) return rc;
+    rc = pl_mg_muon(s, net, handle, nullptr, lr, h->wd, h->mu, h->eps, h->maxGradNorm, gscale, h->ns_coeffs,
+                    h->ns_coeffs ? h->ns_iters : 5, h->bf16, stream);
+    if (rc) return rc;
+  }
+  s->launches = pl_kernel_launch_count() - l0;
+  return PL_OK;
+}
+
+uint64_t pl_mg_last_launches(const pl_mg* s) { return s ? s->launches : 0; }
+
+// Host-mode gradient: one cached session per device carries the workspace between calls.
+int pl_mingru_ppo_grad(const double* params, const double* obs, const double* scal, size_t B, size_t T,
+                       const pl_mg_net* net, double vfCoef, double entCoef, double clipEps, double vfClip,
+                       uint8_t bf16f, double* out) {
+  using namespace pl;
+  int rc = check_net(net);
+  if (rc) return rc;
+  PL_REQUIRE(params && obs && scal && out, PL_ERR_INVALID, "pl_mingru_ppo_grad: NULL argument");
+  PL_REQUIRE(B > 0 && T > 0 && B * T < (1u << 28), PL_ERR_INVALID, "pl_mingru_ppo_grad: bad extents B=%zu T=%zu", B,
+             T);
+  rc = require_device();
+  if (rc) return rc;
+  static std::mutex mu;
+  static pl_mg* cache[64] = {nullptr};
+  std::lock_guard<std::mutex> g(mu);
+  int dev = 0;
+  PL_CUDA(cudaGetDevice(&dev));
+  PL_REQUIRE(dev >= 0 && dev < 64, PL_ERR_UNSUPPORTED, "device index out of range");
+  if (!cache[dev] || cache[dev]->T != (long)T || cache[dev]->N != (long)B) {
+    if (cache[dev]) pl_mg_destroy(cache[dev]);
+    cache[dev] = nullptr;
+    rc = pl_mg_create(B, T, &cache[dev]);
+    if (rc) return rc;
+  }
+  pl_mg* s = cache[dev];
+  const MgShape sh = shape_of(net);
+  rc = ensure_work(s, sh, (long)B, (long)T, bf16f != 0);
+  if (rc) return rc;
+  auto& w = s->w;
+  const long R = w.R, P = sh.P();
+  double* obs_d = (double*)scratch(21, sizeof(double) * R * sh.D);
+  double* scal_d = (double*)scratch(22, sizeof(double) * 6 * R);
+  if (!obs_d || !scal_d) return PL_ERR_NOMEM;
+  PL_CUDA(cudaMemcpy(obs_d, obs, sizeof(double) * R * sh.D, cudaMemcpyHostToDevice));
+  PL_CUDA(cudaMemcpy(scal_d, scal, sizeof(double) * 6 * R, cudaMemcpyHostToDevice));
+  PL_CUDA(cudaMemcpy(w.params_in, params, sizeof(double) * P, cudaMemcpyHostToDevice));
+  rc = refresh_shadows(s, w.params_in, 0);
+  if (rc) return rc;
+  s->shadow_src = 0;
+  if (w.fast)
+    mg_obs_rows_kernel<__nv_bfloat16><<<blocks_for(R * w.Dp), 256>>>(obs_d, R, (int)sh.D, (int)w.Dp,
+                                                                     (__nv_bfloat16*)w.X);
+  else
+    mg_obs_rows_kernel<float><<<blocks_for(R * w.Dp), 256>>>(obs_d, R, (int)sh.D, (int)w.Dp, (float*)w.X);
+  mg_scal_rows_kernel<<<blocks_for(R), 256>>>(scal_d, R, w.act_i, w.adv_f, w.ret_f, w.olp_f, w.ov_f, w.term_f);
+  count_launch(2);
+  PL_LAUNCH("mg_host_rows");
+  rc = run_bptt(s, vfCoef, entCoef, clipEps, vfClip, false, 0);
+  if (rc) return rc;
+  s->grad_fresh = true;
+  rc = pl_mg_grad_download(s, out, out + P, out + P + R);
+  return rc;
+}
+
+}  // extern "C"

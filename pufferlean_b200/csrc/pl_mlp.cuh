@@ -38,6 +38,10 @@ int launch_ns_prepare(const __nv_bfloat16* X, long batch, int rows, int cols, do
 int ns_run(int m, int n, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx, float* out_f32,
            long ld_out, cudaStream_t st);
 
+// The shared 7-loss dashboard channel (pl_mlp_update.cu).
+bool loss_channel_on();
+void loss_channel_store(const double v[7]);
+
 // launchers (pl_mlp_kernels.cu)
 int launch_obs_to_bf16_f64(const double* src, long NT, int D, int Dp, __nv_bfloat16* dst, cudaStream_t st);
 int launch_obs_to_bf16_f32(const float* src, long NT, int D, int Dp, __nv_bfloat16* dst, cudaStream_t st);

@@ -317,7 +317,7 @@ __global__ void bias_act_f32_kernel(float* Z, float* H, const float* __restrict_
 // dZ = dH * act'(Z)
 __global__ void act_grad_f32_kernel(float* dH, const float* __restrict__ Z, long n, int act) {
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
-    dH[i] = (act == 0) ? (Z[i] > 0.f ? dH[i] : 0.f) : dH[i] * act_grad(Z[i], act);
+    dH[i] = (act == 0) ? (Z[i] > 0.f ? dH[i] : 0.f) : (act == 2 ? dH[i] : dH[i] * act_grad(Z[i], act));
 }
 // Per-row PPO objective gradient on fp32 logits Out[M x O] (the reference's k_ppo_dout math,
 // ffi/puffercuda.cu:171-185, with the value clip of :133-141): dOut[M x O].

@@ -1127,6 +1127,22 @@ int pl_adv_normalize(const double* adv, size_t n, double* out) {
   return PL_OK;
 }
 
+}  // extern "C"
+
+namespace pl {
+// The one dashboard-loss channel every trainer writes (the MinGRU path included).
+bool loss_channel_on() {
+  std::lock_guard<std::mutex> g(g_mu);
+  return g_loss_on;
+}
+void loss_channel_store(const double v[7]) {
+  std::lock_guard<std::mutex> g(g_mu);
+  memcpy(g_losses, v, sizeof(g_losses));
+}
+}  // namespace pl
+
+extern "C" {
+
 int pl_loss_enable(uint8_t on) {
   std::lock_guard<std::mutex> g(g_mu);
   g_loss_on = on != 0;

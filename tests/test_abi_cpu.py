@@ -49,6 +49,54 @@ def test_host_bookkeeping_matches_oracle():
     assert np.array_equal(plb.gae_soa(vals, rews, terms, 10, 20, 0.995, 0.9), O.gae_soa(vals, rews, terms, 10, 20, 0.995, 0.9))
 
 
+def test_mingru_host_twins_bit_exact_against_golden():
+    """pl_prio_sample and pl_gather_seq_minibatch reproduce the reference's host C bit for bit."""
+    gp = np.load(os.path.join(ROOT, "tests", "golden", "prio.npz"))
+    m = gp["meta"]
+    seg, mp = plb.prio_sample(gp["L1"], int(m[0]), int(m[1]), int(m[2]), m[3], m[4], int(m[5]))
+    assert np.array_equal(seg, gp["idx"]) and np.array_equal(mp, gp["mbPrio"])
+    gs = np.load(os.path.join(ROOT, "tests", "golden", "gather_seq.npz"))
+    N, T, D, Bmb = (int(x) for x in gs["meta"])
+    out = plb.gather_seq_minibatch(gs["act"], gs["logp"], gs["term"], gs["adv"], gs["value"], gs["seg"], gs["mbPrio"], T,
+                                   Bmb)
+    assert np.array_equal(out, gs["out"])
+
+
+def test_mingru_host_twins_edge_cases():
+    from oracle import oracle as O
+
+    g = np.random.default_rng(3)
+    # a single segment; zero priorities everywhere (the 1e-6 floor); large N with many draws
+    for N, B in ((1, 5), (7, 7), (4000, 900)):
+        l1 = np.zeros(N) if N == 7 else g.uniform(0, 50, N)
+        seg, mp = plb.prio_sample(l1, N, 64, B, 0.6, 0.4, 0xDEADBEEF + N)
+        so, mo = O.prio_sample(l1, N, B, 0.6, 0.4, 0xDEADBEEF + N)
+        assert np.array_equal(seg, so) and np.array_equal(mp, mo)
+        assert seg.min() >= 0 and seg.max() <= N - 1
+    # a segment drawn several times, T = 1
+    adv = g.standard_normal(12)
+    out = plb.gather_seq_minibatch(np.arange(12.0) % 3, g.standard_normal(12), (g.random(12) < 0.3) * 1.0, adv,
+                                   g.standard_normal(12), np.array([3.0, 3.0, 0.0]), np.array([1.0, 0.5, 2.0]), 1, 3)
+    assert out.size == 18 and np.isfinite(out).all()
+
+
+def test_mingru_param_count_and_no_device():
+    assert plb.mg_param_count(118, 512, 1, 4) == 849925  # the Breakout net, 3H layers
+    assert plb.mg_param_count(118, 512, 1, 4, K=2) == 849925 - 512 * 512
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is visible")
+    except ImportError:
+        pass
+    with pytest.raises(plb.PufferError, match="no usable CUDA device|no CPU fallback"):
+        plb.MgSession(4, 8)
+    with pytest.raises(plb.PufferError, match="no usable CUDA device|no CPU fallback"):
+        plb.cuda_mingru_ppo_grad(np.zeros(plb.mg_param_count(2, 8, 1, 2)), np.zeros(8), np.zeros(24), 2, 2, 8, 2, 1, 2,
+                                 0.5, 0.01, 0.2, 0.2)
+
+
 # ---------------------------------------------------------------- Lean adapter (libpufferlean_lean.so)
 LEAN_LIB = os.path.join(os.path.dirname(plb.LIB_PATH), "libpufferlean_lean.so")
 
