@@ -484,6 +484,98 @@ def measure_ns_c3(reps=5):
             "frac": tf / (burst or peak_tf), "peak_kind": kind + " (bf16 burst)"}
 
 
+def mingru_init_pm(D, H, L, A, K, seed):
+    """[params; mom] in the flattenMG layout, Kaiming-uniform bounds of initMinGRU
+    (Puffer/RL/MinGRUTrain.lean:311-344: sqrt(2)/sqrt(D) encoder, 1/sqrt(H) elsewhere, biases zero),
+    drawn with numpy from `seed` (random-init weights of the named architecture)."""
+    g = np.random.default_rng(seed)
+    parts = [g.uniform(-1, 1, H * D) * np.sqrt(2.0 / D), np.zeros(H)]
+    parts += [g.uniform(-1, 1, K * H * H) / np.sqrt(H) for _ in range(L)]
+    parts += [g.uniform(-1, 1, A * H) / np.sqrt(H), np.zeros(A), g.uniform(-1, 1, H) / np.sqrt(H), np.zeros(1)]
+    p = np.concatenate(parts)
+    return p.size, np.concatenate([p, np.zeros(p.size)])
+
+
+MINGRU_C4 = dict(N=8192, T=64, D=118, H=512, L=1, A=4, mb_segs=512, num_mb=64, lr=0.02)
+
+
+def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None):
+    """the Breakout-shaped recurrent update, 8192 envs x 64, obs 118 ~U(0,1), 4 actions,
+    rewards U(-1,1), dones Bernoulli(.005); encoder 118->512 (+GELU), MinGRU hidden 512 with gate + candidate
+    512->1024 (K = 2; K = 3 adds the reference's highway projection), heads 512->4 and 512->1; minibatches of
+    32768 rows (512 segments x 64) x 64 per update (16 x 4 epochs), each: device V-trace over all 8192 segments,
+    prioritised sampling, BPTT gradient, value/ratio iterate, clip, Muon. samples/s = N*T / update time."""
+    import torch
+
+    import pufferlean_b200 as plb
+
+    c = MINGRU_C4
+    N, T, D, H, L_, A = c["N"], c["T"], c["D"], c["H"], c["L"], c["A"]
+    NT = N * T
+    L = plb.lib()
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    obs = torch.rand(NT * D, device="cuda", generator=gen)
+    rew = torch.rand(NT, device="cuda", generator=gen, dtype=torch.float64) * 2 - 1
+    term = (torch.rand(NT, device="cuda", generator=gen) < 0.005).double()
+    act = torch.randint(0, A, (NT,), device="cuda", generator=gen).double()
+    logp = torch.full((NT,), float(np.log(1.0 / A)), device="cuda", dtype=torch.float64) + \
+        0.05 * torch.randn(NT, device="cuda", generator=gen, dtype=torch.float64)
+    val = torch.randn(NT, device="cuda", generator=gen, dtype=torch.float64)
+    boot = torch.randn(N, device="cuda", generator=gen, dtype=torch.float64)
+    P, pm = mingru_init_pm(D, H, L_, A, K, 44)
+    handle = plb.policy_load(pm, P)
+    net = plb.mg_net(D, H, L_, A, K, enc_act)
+    co = np.ascontiguousarray(np.array(QUINTIC, dtype=np.float64))
+    hy = plb.MgHyper(gamma=0.995, lam=0.90, rhoClip=1.0, cClip=1.0, prioAlpha=0.8, annealBeta=0.2, wd=0.0, mu=0.95,
+                     eps=1e-12, vfCoef=0.5, entCoef=0.01, clipEps=0.2, vfClip=0.2, maxGradNorm=1.5,
+                     ns_coeffs=co.ctypes.data_as(C.POINTER(C.c_double)), ns_iters=5, bf16=1)
+    s = plb.MgSession(N, T)
+    st = torch.cuda.current_stream().cuda_stream
+    check(L.pl_mg_set_obs_dev(s.h, obs.data_ptr(), D), L)
+    rng = [0x5EED]
+
+    def step():
+        check(L.pl_mg_set_columns_dev(s.h, rew.data_ptr(), term.data_ptr(), act.data_ptr(), logp.data_ptr(),
+                                      val.data_ptr(), boot.data_ptr(), st), L)
+        r = C.c_uint64(rng[0])
+        check(L.pl_mg_update(s.h, C.byref(net), handle, C.byref(hy), c["num_mb"], c["mb_segs"], C.byref(r), c["lr"],
+                             st), L)
+        rng[0] = r.value
+
+    steps = steps or max(2, min(args.steps, 5))
+    warmup = warmup or max(3, args.warmup)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    l0 = L.pl_kernel_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    launches = (L.pl_kernel_launch_count() - l0) / steps
+    pm_out = plb.policy_download(handle, P)
+    plb.policy_free(handle)
+    s.close()
+    R = c["mb_segs"] * T
+    Op = A + 1
+    # algorithmic GEMM flops per minibatch: forward enc/layer/heads, backward dW of all + dX of layer/heads
+    fwd = 2 * R * (D * H + L_ * H * K * H + H * Op)
+    bwd = 2 * R * (D * H + L_ * 2 * H * K * H + 2 * H * Op)
+    flops = (fwd + bwd) * c["num_mb"]
+    m_ns = [(H, D)] + [(K * H, H)] * L_ + [(A, H), (1, H)]
+    ns_fl = sum(5 * (4 * min(r_, c_) ** 2 * max(r_, c_) + 2 * min(r_, c_) ** 3) for r_, c_ in m_ns) * c["num_mb"]
+    return {"config": "configs[3]: Breakout-shaped MinGRU update, 8192 envs x 64, obs 118, H 512, "
+                      f"{'gate+candidate 512->1024 (K=2)' if K == 2 else 'hid|gate|proj 512->1536 (K=3, reference)'}"
+                      f"{', GELU encoder' if enc_act else ''}, 4 actions, 64 minibatches of 512 segments x 64",
+            "K": K, "enc_act": "gelu" if enc_act else "none", "params": P,
+            "value": NT / (ms / 1e3), "unit": "samples/s", "ms_per_update": ms, "gpu_launches_per_update": launches,
+            "gemm_tflops_over_update": flops / (ms / 1e3) / 1e12, "ns_flops_per_update": ns_fl,
+            "finite": bool(np.isfinite(pm_out).all()), "data": "synthetic (seeded torch generator 4)"}
+
+
 def cudart_memcpy_d2h(dst, handle):
     """8-byte read-back of params[0] from the resident policy (the reference's divergence guard)."""
     import pufferlean_b200 as plb
@@ -528,10 +620,17 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the configs[1] / configs[2] kernel measurements")
-    ap.add_argument("--only", choices=["c2", "c3"], help="print only the configs[1] (c2) or configs[2] (c3) kernel line")
+    ap.add_argument("--only", choices=["c2", "c3", "c4", "c4r"],
+                    help="print only the configs[1] (c2), configs[2] (c3) or configs[3] (c4: K=2 + GELU encoder; "
+                         "c4r: the reference's K=3 linear-encoder net) measurement")
     args = ap.parse_args()
     if args.only:
-        res = measure_vtrace_c2() if args.only == "c2" else measure_ns_c3()
+        if args.only == "c4":
+            res = measure_mingru_c4(args)
+        elif args.only == "c4r":
+            res = measure_mingru_c4(args, K=3, enc_act=0)
+        else:
+            res = measure_vtrace_c2() if args.only == "c2" else measure_ns_c3()
         print(json.dumps(res), flush=True)
         return 0
     wl = WORKLOADS[args.workload]
@@ -571,6 +670,7 @@ def main():
     if rank == 0 and not args.no_extra:
         out["c2_vtrace"] = measure_vtrace_c2()
         out["c3_newton_schulz"] = measure_ns_c3()
+        out["c4_mingru"] = measure_mingru_c4(args)
     if rank == 0:
         if not args.no_cpu and world == 1:
             out["cpu_baseline"] = cpu_baseline(wl)

@@ -22,6 +22,7 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/pufferlean_b200.h"
@@ -57,8 +58,6 @@ __device__ __forceinline__ void stv<bf16>(bf16* p, long i, float v) {
   p[i] = __float2bfloat16_rn(v);
 }
 
-__device__ __forceinline__ float sigf(float x) { return 1.f / (1.f + expf(-x)); }
-
 inline unsigned blocks_for(long n, int block = 256, long cap = 148 * 32) {
   long g = (n + block - 1) / block;
   return (unsigned)std::max<long>(1, std::min(g, cap));
@@ -91,41 +90,47 @@ __global__ void mg_obs_rows_kernel(const double* __restrict__ src, long R, int D
   }
 }
 
-// Advantage mean and population std over the Bmb*T sampled entries (index q = b*T + t), one block
-// with a fixed-shape tree: ms = [mean, std + 1e-8].
-__global__ void __launch_bounds__(1024) mg_adv_ms_kernel(const double* __restrict__ adv,
-                                                         const double* __restrict__ seg, int Bmb, int T, double* ms) {
-  __shared__ double sh[1024];
+// Advantage mean and population std over the Bmb*T sampled entries (index q = b*T + t), in two
+// passes (sum, then squared deviations) over a fixed grid of kAdvBlocks blocks: each block writes
+// its partial, the last block to finish folds the partials in block order (the counter makes the
+// finish order irrelevant) and resets the counter. ms = [mean, std + 1e-8].
+constexpr int kAdvBlocks = 64;
+__global__ void __launch_bounds__(256) mg_adv_ms_kernel(const double* __restrict__ adv,
+                                                        const double* __restrict__ seg, int Bmb, int T, int sq,
+                                                        double* ms, double* part, unsigned* counter) {
+  __shared__ double sh[256];
+  __shared__ bool last;
   const long n = (long)Bmb * T;
   const int tid = threadIdx.x;
+  const double mean = sq ? ms[0] : 0.0;
   double s = 0.0;
-  for (long q = tid; q < n; q += 1024) {
+  for (long q = (long)blockIdx.x * 256 + tid; q < n; q += (long)gridDim.x * 256) {
     const int b = (int)(q / T), t = (int)(q - (long)b * T);
-    s += adv[(long)seg[b] * T + t];
+    const double a = adv[(long)seg[b] * T + t];
+    s += sq ? (a - mean) * (a - mean) : a;
   }
   sh[tid] = s;
   __syncthreads();
-  for (int k = 512; k > 0; k >>= 1) {
-    if (tid < k) sh[tid] += sh[tid + k];
-    __syncthreads();
-  }
-  const double mean = sh[0] / (double)(n > 0 ? n : 1);
-  __syncthreads();
-  double s2 = 0.0;
-  for (long q = tid; q < n; q += 1024) {
-    const int b = (int)(q / T), t = (int)(q - (long)b * T);
-    const double d = adv[(long)seg[b] * T + t] - mean;
-    s2 += d * d;
-  }
-  sh[tid] = s2;
-  __syncthreads();
-  for (int k = 512; k > 0; k >>= 1) {
+  for (int k = 128; k > 0; k >>= 1) {
     if (tid < k) sh[tid] += sh[tid + k];
     __syncthreads();
   }
   if (tid == 0) {
-    ms[0] = mean;
-    ms[1] = sqrt(sh[0] / (double)(n > 0 ? n : 1)) + 1e-8;
+    part[blockIdx.x] = sh[0];
+    __threadfence();
+    last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && tid == 0) {
+    __threadfence();
+    double tot = 0.0;
+    for (int i = 0; i < (int)gridDim.x; i++) tot += ((volatile double*)part)[i];
+    const double d = (double)(n > 0 ? n : 1);
+    if (sq)
+      ms[1] = sqrt(tot / d) + 1e-8;
+    else
+      ms[0] = tot / d;
+    *counter = 0;
   }
 }
 // Per-row minibatch scalars from the resident columns (the layout of the host gather,
@@ -163,71 +168,209 @@ __global__ void mg_scal_rows_kernel(const double* __restrict__ scal, long R, int
 }
 
 // ---------------------------------------------------------------- scans
-// Forward scan of one layer: thread (b, j) walks t = 0..T-1 with the state in a register.
-// Y [R x K*H], hin/hout/Os [R x H], term [R] (1 = terminal at that step).
-template <typename S, int K>
-__global__ void __launch_bounds__(256) mg_scan_fwd_kernel(const S* __restrict__ Y, const S* __restrict__ hin, S* hout,
-                                                          S* Os, const float* __restrict__ term, int B, int H, int T) {
+// Two adjacent columns per thread (VEC = 2) as one 4-byte (bf16) or 8-byte (fp32) access.
+template <int VEC>
+__device__ __forceinline__ void ldp(const float* p, float (&v)[VEC]) {
+  if constexpr (VEC == 2) {
+    const float2 q = *reinterpret_cast<const float2*>(p);
+    v[0] = q.x;
+    v[1] = q.y;
+  } else {
+    v[0] = p[0];
+  }
+}
+template <int VEC>
+__device__ __forceinline__ void ldp(const bf16* p, float (&v)[VEC]) {
+  if constexpr (VEC == 2) {
+    const float2 q = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+    v[0] = q.x;
+    v[1] = q.y;
+  } else {
+    v[0] = __bfloat162float(p[0]);
+  }
+}
+template <int VEC>
+__device__ __forceinline__ void stp(float* p, const float (&v)[VEC]) {
+  if constexpr (VEC == 2)
+    *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+  else
+    p[0] = v[0];
+}
+template <int VEC>
+__device__ __forceinline__ void stp(bf16* p, const float (&v)[VEC]) {
+  if constexpr (VEC == 2)
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v[0], v[1]);
+  else
+    p[0] = __float2bfloat16_rn(v[0]);
+}
+// Logistic function: the fast tier uses the hardware exponential and division approximations,
+// the tight tier the accurate library calls.
+template <bool FAST>
+__device__ __forceinline__ float sigm(float x) {
+  if constexpr (FAST)
+    return __fdividef(1.f, 1.f + __expf(-x));
+  else
+    return 1.f / (1.f + expf(-x));
+}
+
+// Forward scan of one layer: thread (b, columns j..j+VEC-1) walks t = 0..T-1 with the states in
+// registers. Y [R x K*H], hin/hout/Os [R x H], term [R] (1 = terminal at that step). The inputs of a
+// step do not depend on the state, so they are loaded kScanU steps at a time ahead of the
+// recurrence: the loads of a group are all in flight together and only the arithmetic is serial.
+constexpr int kScanU = 4;
+template <typename S, int K, int VEC, bool FAST>
+__global__ void __launch_bounds__(256) mg_scan_fwd_kernel(const S* __restrict__ Y, const S* __restrict__ hin,
+                                                          S* __restrict__ hout, S* __restrict__ Os,
+                                                          const float* __restrict__ term, int B, int H, int T) {
+  const int HV = H / VEC;
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (long)B * H) return;
-  const int b = (int)(idx / H), j = (int)(idx - (long)b * H);
-  const long KH = (long)K * H;
-  float state = 0.f;
-  for (int t = 0; t < T; t++) {
-    const long r = (long)t * B + b;
-    const float hid = ldv(Y, r * KH + j), gate = ldv(Y, r * KH + H + j);
-    const float z = sigf(gate), g = hid >= 0.f ? hid + 0.5f : sigf(hid);
-    const float o = (1.f - z) * state + z * g;
-    stv(Os, r * H + j, o);
-    if (K == 3) {
-      const float hg = sigf(ldv(Y, r * KH + 2 * H + j));
-      stv(hout, r * H + j, hg * o + (1.f - hg) * ldv(hin, r * H + j));
-    } else {
-      stv(hout, r * H + j, o);
+  if (idx >= (long)B * HV) return;
+  const int b = (int)(idx / HV), j = (int)(idx - (long)b * HV) * VEC;
+  const long KH = (long)K * H, sY = (long)B * KH, sH = (long)B * H;
+  const S* py = Y + (long)b * KH + j;
+  const S* ph = hin + (long)b * H + j;
+  S* po = Os + (long)b * H + j;
+  S* pout = hout + (long)b * H + j;
+  const float* pt = term + b;
+  float state[VEC];
+#pragma unroll
+  for (int v = 0; v < VEC; v++) state[v] = 0.f;
+  for (int t0 = 0; t0 < T; t0 += kScanU) {
+    float hid[kScanU][VEC], gate[kScanU][VEC], proj[kScanU][VEC], hi[kScanU][VEC], tm[kScanU];
+#pragma unroll
+    for (int u = 0; u < kScanU; u++) {
+      if (t0 + u < T) {
+        ldp<VEC>(py + u * sY, hid[u]);
+        ldp<VEC>(py + u * sY + H, gate[u]);
+        if (K == 3) {
+          ldp<VEC>(py + u * sY + 2 * H, proj[u]);
+          ldp<VEC>(ph + u * sH, hi[u]);
+        }
+        tm[u] = pt[(long)u * B];
+      }
     }
-    state = term[r] != 0.f ? 0.f : o;
+#pragma unroll
+    for (int u = 0; u < kScanU; u++) {
+      if (t0 + u < T) {
+        float o[VEC], hn[VEC];
+#pragma unroll
+        for (int v = 0; v < VEC; v++) {
+          const float z = sigm<FAST>(gate[u][v]);
+          const float g = hid[u][v] >= 0.f ? hid[u][v] + 0.5f : sigm<FAST>(hid[u][v]);
+          o[v] = (1.f - z) * state[v] + z * g;
+          if (K == 3) {
+            const float hg = sigm<FAST>(proj[u][v]);
+            hn[v] = hg * o[v] + (1.f - hg) * hi[u][v];
+          } else {
+            hn[v] = o[v];
+          }
+          state[v] = tm[u] != 0.f ? 0.f : o[v];
+        }
+        stp<VEC>(po + u * sH, o);
+        stp<VEC>(pout + u * sH, hn);
+      }
+    }
+    py += kScanU * sY;
+    ph += kScanU * sH;
+    po += kScanU * sH;
+    pout += kScanU * sH;
+    pt += (long)kScanU * B;
   }
 }
 // Reverse scan of one layer (the per-element backward of ffi/pufferffi.c:840-868): dY [R x K*H],
-// dhn [R x H] = the highway part of the gradient reaching the layer input (K = 3).
-template <typename S, int K>
+// dhn [R x H] = the highway part of the gradient reaching the layer input (K = 3). Loads run kScanU
+// steps ahead of the reverse recurrence, as in the forward scan.
+template <typename S, int K, int VEC, bool FAST>
 __global__ void __launch_bounds__(256) mg_scan_bwd_kernel(const S* __restrict__ Y, const S* __restrict__ Os,
-                                                          const S* __restrict__ hin, const S* __restrict__ dh, S* dY,
-                                                          S* dhn, const float* __restrict__ term, int B, int H,
-                                                          int T) {
+                                                          const S* __restrict__ hin, const S* __restrict__ dh,
+                                                          S* __restrict__ dY, S* __restrict__ dhn,
+                                                          const float* __restrict__ term, int B, int H, int T) {
+  const int HV = H / VEC;
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (long)B * H) return;
-  const int b = (int)(idx / H), j = (int)(idx - (long)b * H);
-  const long KH = (long)K * H;
-  float dOnext = 0.f;
-  for (int t = T - 1; t >= 0; t--) {
-    const long r = (long)t * B + b;
-    const bool flow = t > 0 && term[r - B] == 0.f;  // no state (and no gradient) across a terminal
-    const float hid = ldv(Y, r * KH + j), gate = ldv(Y, r * KH + H + j);
-    const float o = ldv(Os, r * H + j);
-    const float prev = flow ? ldv(Os, (r - B) * H + j) : 0.f;
-    const float z = sigf(gate);
-    const float sh = sigf(hid);
-    const float g = hid >= 0.f ? hid + 0.5f : sh;
-    const float dhj = ldv(dh, r * H + j);
-    float dout;
-    if (K == 3) {
-      const float hg = sigf(ldv(Y, r * KH + 2 * H + j));
-      const float hi = ldv(hin, r * H + j);
-      const float dhg = dhj * (o - hi);
-      dout = dhj * hg + dOnext;
-      stv(dhn, r * H + j, dhj * (1.f - hg));
-      stv(dY, r * KH + 2 * H + j, dhg * hg * (1.f - hg));
-    } else {
-      dout = dhj + dOnext;
+  if (idx >= (long)B * HV) return;
+  const int b = (int)(idx / HV), j = (int)(idx - (long)b * HV) * VEC;
+  const long KH = (long)K * H, sY = (long)B * KH, sH = (long)B * H;
+  const long last = (long)(T - 1);
+  const S* py = Y + last * sY + (long)b * KH + j;
+  S* pdy = dY + last * sY + (long)b * KH + j;
+  const long oH = last * sH + (long)b * H + j;
+  const S* po = Os + oH;
+  const S* ph = hin + oH;
+  const S* pd = dh + oH;
+  S* pdn = dhn ? dhn + oH : nullptr;
+  const float* pt = term + last * B + b;
+  float dOnext[VEC];
+#pragma unroll
+  for (int v = 0; v < VEC; v++) dOnext[v] = 0.f;
+  for (int t1 = T - 1; t1 >= 0; t1 -= kScanU) {
+    float hid[kScanU][VEC], gate[kScanU][VEC], proj[kScanU][VEC], hi[kScanU][VEC], o[kScanU][VEC],
+        prev[kScanU][VEC], dhv[kScanU][VEC];
+    bool flow[kScanU];
+#pragma unroll
+    for (int u = 0; u < kScanU; u++) {
+      const int t = t1 - u;
+      if (t >= 0) {
+        flow[u] = t > 0 && pt[-(long)(u + 1) * B] == 0.f;  // no state (and no gradient) across a terminal
+        ldp<VEC>(py - u * sY, hid[u]);
+        ldp<VEC>(py - u * sY + H, gate[u]);
+        if (K == 3) {
+          ldp<VEC>(py - u * sY + 2 * H, proj[u]);
+          ldp<VEC>(ph - u * sH, hi[u]);
+        }
+        ldp<VEC>(po - u * sH, o[u]);
+        if (t > 0)
+          ldp<VEC>(po - (u + 1) * sH, prev[u]);
+        else
+#pragma unroll
+          for (int v = 0; v < VEC; v++) prev[u][v] = 0.f;
+        ldp<VEC>(pd - u * sH, dhv[u]);
+      }
     }
-    const float dz = dout * (g - prev);
-    const float dprev = dout * (1.f - z);
-    const float dg = dout * z;
-    const float sg = hid >= 0.f ? 1.f : sh * (1.f - sh);
-    stv(dY, r * KH + j, dg * sg);
-    stv(dY, r * KH + H + j, dz * z * (1.f - z));
-    dOnext = flow ? dprev : 0.f;
+#pragma unroll
+    for (int u = 0; u < kScanU; u++) {
+      const int t = t1 - u;
+      if (t >= 0) {
+        float dyh[VEC], dyg[VEC], dyp[VEC], dhw[VEC];
+#pragma unroll
+        for (int v = 0; v < VEC; v++) {
+          const float pv = flow[u] ? prev[u][v] : 0.f;
+          const float z = sigm<FAST>(gate[u][v]);
+          const float sh = sigm<FAST>(hid[u][v]);
+          const float g = hid[u][v] >= 0.f ? hid[u][v] + 0.5f : sh;
+          const float dhj = dhv[u][v];
+          float dout;
+          if (K == 3) {
+            const float hg = sigm<FAST>(proj[u][v]);
+            const float dhg = dhj * (o[u][v] - hi[u][v]);
+            dout = dhj * hg + dOnext[v];
+            dhw[v] = dhj * (1.f - hg);
+            dyp[v] = dhg * hg * (1.f - hg);
+          } else {
+            dout = dhj + dOnext[v];
+          }
+          const float dz = dout * (g - pv);
+          const float dprev = dout * (1.f - z);
+          const float dg = dout * z;
+          const float sg = hid[u][v] >= 0.f ? 1.f : sh * (1.f - sh);
+          dyh[v] = dg * sg;
+          dyg[v] = dz * z * (1.f - z);
+          dOnext[v] = flow[u] ? dprev : 0.f;
+        }
+        stp<VEC>(pdy - u * sY, dyh);
+        stp<VEC>(pdy - u * sY + H, dyg);
+        if (K == 3) {
+          stp<VEC>(pdy - u * sY + 2 * H, dyp);
+          stp<VEC>(pdn - u * sH, dhw);
+        }
+      }
+    }
+    py -= kScanU * sY;
+    pdy -= kScanU * sY;
+    po -= kScanU * sH;
+    ph -= kScanU * sH;
+    pd -= kScanU * sH;
+    if (pdn) pdn -= kScanU * sH;
+    pt -= (long)kScanU * B;
   }
 }
 
@@ -371,12 +514,16 @@ __global__ void mg_iterate_kernel(double* value, double* ratio, const double* __
 // lower-bound search, importance weight). Deterministic; the sums are ordered differently from the
 // host sampler's sequential loop, so a draw can differ from it only when u falls within rounding
 // of a cumulative boundary.
+// rng_dev (optional): the generator state lives in device memory; it is read here and advanced by
+// Bmb * GOLD, so a captured minibatch graph draws a fresh sample on every replay.
 __global__ void __launch_bounds__(1024) mg_prio_kernel(const double* __restrict__ l1, long N, long Bmb, double alpha,
-                                                       double beta, unsigned long long rng, double* p, double* cum,
+                                                       double beta, unsigned long long rng,
+                                                       unsigned long long* rng_dev, double* p, double* cum,
                                                        double* seg, double* mbp) {
   __shared__ double sh[1024];
   __shared__ double s_total;
   const int tid = threadIdx.x;
+  if (rng_dev) rng = rng_dev[0];
   const long per = (N + 1023) / 1024;
   const long lo = min(N, (long)tid * per), hi = min(N, lo + per);
   double s = 0.0;
@@ -400,19 +547,29 @@ __global__ void __launch_bounds__(1024) mg_prio_kernel(const double* __restrict_
     acc += q;
     cum[e] = acc;
   }
-  sh[tid] = acc;
+  // exclusive scan of the 1024 run totals: within each warp, then over the 32 warp totals
+  const int lane = tid & 31, wid = tid >> 5;
+  double inc = acc;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) sh[wid] = inc;
   __syncthreads();
-  if (tid == 0) {
-    double run = 0.0;
-    for (int i = 0; i < 1024; i++) {
-      const double v = sh[i];
-      sh[i] = run;
-      run += v;
+  if (wid == 0) {
+    double w = sh[lane];
+    double winc = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double y = __shfl_up_sync(0xffffffffu, winc, o);
+      if (lane >= o) winc += y;
     }
-    s_total = run;
+    sh[32 + lane] = winc - w;  // exclusive offset of warp `lane`
+    if (lane == 31) s_total = winc;
   }
   __syncthreads();
-  const double off = sh[tid];
+  const double off = sh[32 + wid] + (inc - acc);
   for (long e = lo; e < hi; e++) cum[e] += off;
   __syncthreads();
   const double total = s_total;
@@ -434,6 +591,120 @@ __global__ void __launch_bounds__(1024) mg_prio_kernel(const double* __restrict_
     seg[i] = (double)idx;
     mbp[i] = exp((-beta) * log((double)N * p[idx] + 1e-12));
   }
+  if (rng_dev && tid == 0) rng_dev[0] = rng + (unsigned long long)Bmb * 0x9E3779B97F4A7C15ULL;
+}
+
+// ---------------------------------------------------------------- Muon of small matrices
+// One CTA does the whole Muon step of one matrix whose short side is at most kSmallSide: Nesterov
+// momentum in f64 (the fast tier's nesterov formula), the Frobenius normalisation, every Newton-Schulz
+// step in fp32 shared memory (G = X X^T, Pm = b G + c G G, X' = a X + Pm X), and the finalize into the
+// f64 master and its bf16 shadow. Replaces a chain of ~18 launches for the action and value heads.
+constexpr int kSmallSide = 32;
+constexpr int kSmallElems = 16384;  // m * n; two fp32 copies of X stay in shared memory
+constexpr int kSmallMaxIters = 16;
+struct SmallMat {
+  long oW;
+  int rows, cols;
+  void* Wb;
+  long ldw;
+  double scale;  // sqrt(max(1, rows/cols))
+};
+struct SmallMats {
+  SmallMat m[4];
+  float co[kSmallMaxIters][3];
+  int n, iters;
+};
+__global__ void __launch_bounds__(256) mg_small_muon_kernel(const SmallMats sm, const float* __restrict__ grad,
+                                                            const double* __restrict__ cc, double* W, double* mom,
+                                                            double mu, double eps, double c1, double lr) {
+  extern __shared__ float smf[];
+  __shared__ double shd[256];
+  const SmallMat& q = sm.m[blockIdx.x];
+  const int rows = q.rows, cols = q.cols;
+  const bool tr = rows > cols;
+  const int m = tr ? cols : rows, n = tr ? rows : cols;
+  float* X = smf;
+  float* X2 = smf + (long)m * n;
+  float* G = X2 + (long)m * n;
+  float* Pm = G + m * m;
+  const int tid = threadIdx.x;
+  const double c = cc[0];
+  double s = 0.0;
+  for (int i = tid; i < rows * cols; i += 256) {
+    const double gi = (double)grad[q.oW + i] * c;
+    const double mm = mu * mom[q.oW + i] + gi;
+    mom[q.oW + i] = mm;
+    const double ui = gi + mu * mm;
+    const int r = i / cols, cl = i - r * cols;
+    X[tr ? cl * n + r : r * n + cl] = (float)ui;
+    s += ui * ui;
+  }
+  shd[tid] = s;
+  __syncthreads();
+  for (int k = 128; k > 0; k >>= 1) {
+    if (tid < k) shd[tid] += shd[tid + k];
+    __syncthreads();
+  }
+  const float inv = (float)(1.0 / (sqrt(shd[0]) + eps));
+  for (int i = tid; i < m * n; i += 256) X[i] *= inv;
+  __syncthreads();
+  for (int it = 0; it < sm.iters; it++) {
+    const float a = sm.co[it][0], bb = sm.co[it][1], cf = sm.co[it][2];
+    for (int e = tid; e < m * m; e += 256) {
+      const int i = e / m, k = e - i * m;
+      float acc = 0.f;
+      for (int l = 0; l < n; l++) acc += X[i * n + l] * X[k * n + l];
+      G[e] = acc;
+    }
+    __syncthreads();
+    for (int e = tid; e < m * m; e += 256) {
+      const int i = e / m, k = e - i * m;
+      float acc = 0.f;
+      for (int l = 0; l < m; l++) acc += G[i * m + l] * G[l * m + k];
+      Pm[e] = bb * G[e] + cf * acc;
+    }
+    __syncthreads();
+    for (int e = tid; e < m * n; e += 256) {
+      const int i = e / n, l = e - i * n;
+      float acc = a * X[e];
+      for (int k = 0; k < m; k++) acc += Pm[i * m + k] * X[k * n + l];
+      X2[e] = acc;
+    }
+    __syncthreads();
+    float* t = X;
+    X = X2;
+    X2 = t;
+  }
+  const double c2 = lr * q.scale;
+  for (int i = tid; i < rows * cols; i += 256) {
+    const int r = i / cols, cl = i - r * cols;
+    const double x = (double)X[tr ? cl * n + r : r * n + cl];
+    const double w = c1 * W[q.oW + i] + c2 * x;
+    W[q.oW + i] = w;
+    if (q.Wb) ((__nv_bfloat16*)q.Wb)[r * q.ldw + cl] = __float2bfloat16_rn((float)w);
+  }
+}
+// stepVec of up to four biases in one launch, with their fp32 shadows.
+struct BiasList {
+  long oB[4];
+  int n[4];
+  float* shadow[4];
+  int count;
+};
+__global__ void mg_bias_step_kernel(const BiasList bl, const float* __restrict__ grad, const double* __restrict__ cc,
+                                    double* W, double* mom, double lr, double wd, double mu) {
+  const double c = cc[0];
+  for (int q = 0; q < bl.count; q++)
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < bl.n[q]; i += gridDim.x * blockDim.x) {
+      const long k = bl.oB[q] + i;
+      const double gi = (double)grad[k] * c;
+      const double newm = mu * mom[k] + gi;
+      const double upd = gi + mu * newm;
+      const double nb = W[k] * (1.0 - lr * wd) + lr * upd;
+      W[k] = nb;
+      mom[k] = newm;
+      if (bl.shadow[q]) bl.shadow[q][i] = (float)nb;
+    }
 }
 
 __global__ void mg_fill_kernel(double* d, double v, long n) {
@@ -500,6 +771,8 @@ struct pl_mg {
     float *adv_f = nullptr, *ret_f = nullptr, *olp_f = nullptr, *ov_f = nullptr, *term_f = nullptr;
     float *newlp = nullptr, *newval = nullptr, *lossrow = nullptr;
     double* ms = nullptr;
+    double* adv_part = nullptr;
+    unsigned* adv_counter = nullptr;
     double* obs_in = nullptr;   // host-mode obs upload
     double* scal_in = nullptr;  // host-mode scalars upload
     // weight shadows: fast = bf16 matrices [rows x ld] + fp32 biases; tight = fp32
@@ -520,9 +793,17 @@ struct pl_mg {
     double* gn_part = nullptr;
     double* g64 = nullptr;
     double* params_in = nullptr;  // host params upload (pl_mg_grad with handle 0)
-    pl::NsWork ns;
+    pl::NsWork ns, ns2;  // ns2: the Newton-Schulz chains that run on the side stream
     double* exact_ws = nullptr;
   } w;
+  cudaStream_t side = nullptr;  // second stream for concurrent Newton-Schulz chains
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  // one minibatch of pl_mg_update captured as a CUDA graph (fast tier), replayed numMB times
+  cudaStream_t cap = nullptr;
+  cudaGraphExec_t gexec = nullptr;
+  std::vector<double> gkey;
+  uint64_t gnodes = 0;
+  unsigned long long* rng_dev = nullptr;
   bool have_work = false;
   size_t shadow_src = 0;  // handle whose weights the shadows hold (0 = none / host params)
   bool grad_fresh = false;
@@ -616,6 +897,8 @@ int ensure_work(pl_mg* s, const MgShape& sh, long Bmb, long T, bool fast) {
   w.newval = mg_alloc<float>(w.allocs, R, f);
   w.lossrow = mg_alloc<float>(w.allocs, (size_t)R * 8, f);
   w.ms = mg_alloc<double>(w.allocs, 4, f);
+  w.adv_part = mg_alloc<double>(w.allocs, kAdvBlocks, f);
+  w.adv_counter = mg_alloc<unsigned>(w.allocs, 1, f, true);
   // shadows (zeroed: the padding of the bf16 operands must read as zero)
   w.Wenc = (void*)mg_alloc<char>(w.allocs, (size_t)H * w.Dp * es, f, true);
   for (long l = 0; l < L; l++) w.Wl.push_back((void*)mg_alloc<char>(w.allocs, (size_t)KH * H * es, f, true));
@@ -657,6 +940,15 @@ int ensure_work(pl_mg* s, const MgShape& sh, long Bmb, long T, bool fast) {
     w.ns.Xf = mg_alloc<float>(w.allocs, (size_t)mmax * ldx, f);
     w.ns.U = mg_alloc<double>(w.allocs, nprod, f);
     w.ns.part = mg_alloc<double>(w.allocs, 4096, f);
+    w.ns2 = w.ns;
+    w.ns2.X0 = mg_alloc<bf16>(w.allocs, (size_t)rup(mmax, 128) * ldx, f, true);
+    w.ns2.X1 = mg_alloc<bf16>(w.allocs, (size_t)rup(mmax, 128) * ldx, f, true);
+    w.ns2.G = mg_alloc<bf16>(w.allocs, (size_t)rup(mmax, 128) * ldg, f, true);
+    w.ns2.B = mg_alloc<bf16>(w.allocs, (size_t)rup(mmax, 128) * ldg, f, true);
+    w.ns2.Xf = mg_alloc<float>(w.allocs, (size_t)mmax * ldx, f);
+    w.ns2.U = mg_alloc<double>(w.allocs, nprod, f);
+    w.ns2.part = mg_alloc<double>(w.allocs, 4096, f);
+    w.ns2.err = nullptr;
   } else {
     size_t ws = std::max(exact_ws_doubles((int)H, (int)sh.D), exact_ws_doubles((int)KH, (int)H));
     ws = std::max(ws, exact_ws_doubles((int)A, (int)H));
@@ -742,6 +1034,39 @@ int wgrad_tc(pl_mg* s, const void* dZ, long ldz, int out, const void* Hin, long 
 
 inline int pick_bn_n(long n) { return n <= 64 ? 64 : (n <= 128 ? 128 : 256); }
 
+// Scan launches: the bf16 tier takes two columns per thread and the fast logistic; the fp32 tier
+// one column and the accurate one (it is the parity tier).
+template <typename S>
+int launch_scan_fwd(const void* Y, const void* hin, void* hout, void* Os, const float* term, int B, int H, int T, int K,
+                    cudaStream_t st) {
+  constexpr bool FAST = std::is_same<S, bf16>::value;
+  constexpr int VEC = FAST ? 2 : 1;
+  const unsigned nb = (unsigned)(((long)B * (H / VEC) + 255) / 256);
+  if (K == 3)
+    mg_scan_fwd_kernel<S, 3, VEC, FAST><<<nb, 256, 0, st>>>((const S*)Y, (const S*)hin, (S*)hout, (S*)Os, term, B, H, T);
+  else
+    mg_scan_fwd_kernel<S, 2, VEC, FAST><<<nb, 256, 0, st>>>((const S*)Y, (const S*)hin, (S*)hout, (S*)Os, term, B, H, T);
+  count_launch();
+  PL_LAUNCH("mg_scan_fwd_kernel");
+  return PL_OK;
+}
+template <typename S>
+int launch_scan_bwd(const void* Y, const void* Os, const void* hin, const void* dh, void* dY, void* dhn,
+                    const float* term, int B, int H, int T, int K, cudaStream_t st) {
+  constexpr bool FAST = std::is_same<S, bf16>::value;
+  constexpr int VEC = FAST ? 2 : 1;
+  const unsigned nb = (unsigned)(((long)B * (H / VEC) + 255) / 256);
+  if (K == 3)
+    mg_scan_bwd_kernel<S, 3, VEC, FAST><<<nb, 256, 0, st>>>((const S*)Y, (const S*)Os, (const S*)hin, (const S*)dh,
+                                                             (S*)dY, (S*)dhn, term, B, H, T);
+  else
+    mg_scan_bwd_kernel<S, 2, VEC, FAST><<<nb, 256, 0, st>>>((const S*)Y, (const S*)Os, (const S*)hin, (const S*)dh,
+                                                             (S*)dY, nullptr, term, B, H, T);
+  count_launch();
+  PL_LAUNCH("mg_scan_bwd_kernel");
+  return PL_OK;
+}
+
 // The BPTT gradient of the minibatch already gathered into the work buffers (X, act_i, adv_f,
 // ret_f, olp_f, ov_f, term_f): forward, PPO head, backward; summed gradient into w.grad.
 template <typename S>
@@ -791,15 +1116,8 @@ int bptt(pl_mg* s, double vf, double ent, double clip, double vfclip, bool losse
                         (float*)w.Y[l], KH, 1.f, st);
     }
     if (rc) return rc;
-    const unsigned nb = (unsigned)((Bmb * H + 255) / 256);
-    if (sh.K == 3)
-      mg_scan_fwd_kernel<S, 3><<<nb, 256, 0, st>>>((const S*)w.Y[l], (const S*)w.h[l], (S*)w.h[l + 1], (S*)w.Os[l],
-                                                    w.term_f, Bmb, (int)H, T);
-    else
-      mg_scan_fwd_kernel<S, 2><<<nb, 256, 0, st>>>((const S*)w.Y[l], (const S*)w.h[l], (S*)w.h[l + 1], (S*)w.Os[l],
-                                                    w.term_f, Bmb, (int)H, T);
-    count_launch();
-    PL_LAUNCH("mg_scan_fwd_kernel");
+    rc = launch_scan_fwd<S>(w.Y[l], w.h[l], w.h[l + 1], w.Os[l], w.term_f, Bmb, (int)H, T, (int)sh.K, st);
+    if (rc) return rc;
   }
   // ---- heads: Out = h_L W_out^T (bias added by the row kernel)
   if (fast) {
@@ -855,16 +1173,9 @@ int bptt(pl_mg* s, double vf, double ent, double clip, double vfclip, bool losse
   if (rc) return rc;
   // ---- layers, top down
   for (long l = L - 1; l >= 0; l--) {
-    const unsigned nb = (unsigned)((Bmb * H + 255) / 256);
-    if (sh.K == 3)
-      mg_scan_bwd_kernel<S, 3><<<nb, 256, 0, st>>>((const S*)w.Y[l], (const S*)w.Os[l], (const S*)w.h[l],
-                                                    (const S*)w.dh[cur], (S*)w.dY, (S*)w.dhn, w.term_f, Bmb, (int)H,
-                                                    T);
-    else
-      mg_scan_bwd_kernel<S, 2><<<nb, 256, 0, st>>>((const S*)w.Y[l], (const S*)w.Os[l], (const S*)w.h[l],
-                                                    (const S*)w.dh[cur], (S*)w.dY, nullptr, w.term_f, Bmb, (int)H, T);
-    count_launch();
-    PL_LAUNCH("mg_scan_bwd_kernel");
+    rc = launch_scan_bwd<S>(w.Y[l], w.Os[l], w.h[l], w.dh[cur], w.dY, sh.K == 3 ? w.dhn : nullptr, w.term_f, Bmb,
+                            (int)H, T, (int)sh.K, st);
+    if (rc) return rc;
     // dW_l = dY^T h_l
     if (fast)
       rc = wgrad_tc(s, w.dY, KH, (int)KH, w.h[l], H, (int)H, R, grad + sh.oLayer(l), st);
@@ -1014,22 +1325,73 @@ int muon_step(pl_mg* s, size_t handle, const double* gClip, double lr, double wd
   }
   s->grad_fresh = false;
   if (w.fast) {
+    // Matrices with a short side of at most kSmallSide take the one-launch fused step; the others run
+    // their tensor-core Newton-Schulz chains alternately on the caller's stream and the side stream.
+    SmallMats sm{};
+    sm.iters = iters;
+    const bool small_ok = iters <= kSmallMaxIters;
+    for (int i = 0; small_ok && i < iters; i++)
+      for (int k = 0; k < 3; k++) sm.co[i][k] = (float)coeffs[3 * i + k];
+    std::vector<const Mat*> big;
+    size_t small_smem = 0;
     for (const Mat& m : mats) {
+      const long mm = std::min(m.rows, m.cols);
+      if (small_ok && sm.n < 4 && mm <= kSmallSide && m.rows * m.cols <= kSmallElems) {
+        const double r = (double)m.rows / (double)m.cols;
+        sm.m[sm.n++] = SmallMat{m.oW, (int)m.rows, (int)m.cols, m.shadow, m.ldw, sqrt(r > 1.0 ? r : 1.0)};
+        small_smem = std::max(small_smem, (size_t)(2 * m.rows * m.cols + 2 * mm * mm) * sizeof(float));
+      } else {
+        big.push_back(&m);
+      }
+    }
+    const bool two = big.size() > 1;
+    if (two) {
+      if (!s->side) {
+        PL_CUDA(cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking));
+        PL_CUDA(cudaEventCreateWithFlags(&s->ev_fork, cudaEventDisableTiming));
+        PL_CUDA(cudaEventCreateWithFlags(&s->ev_join, cudaEventDisableTiming));
+      }
+      PL_CUDA(cudaEventRecord(s->ev_fork, st));
+      PL_CUDA(cudaStreamWaitEvent(s->side, s->ev_fork, 0));
+    }
+    for (size_t q = 0; q < big.size(); q++) {
+      const Mat& m = *big[q];
+      const bool on_side = two && (q % 2 == 1);
+      cudaStream_t ms = on_side ? s->side : st;
+      NsWork& ns = on_side ? w.ns2 : w.ns;
       const long n = m.rows * m.cols;
       const int mm = (int)std::min(m.rows, m.cols), nn = (int)std::max(m.rows, m.cols);
       int nparts = 0;
-      rc = launch_nesterov(w.grad + m.oW, w.cc, mom + m.oW, w.ns.U, mu, n, w.ns.part, &nparts, st);
-      if (!rc) rc = launch_ns_input(w.ns.U, w.ns.part, nparts, (int)m.rows, (int)m.cols, eps, w.ns.X0, w.ns.ldx, st);
-      if (!rc) rc = ns_run(mm, nn, coeffs, iters, w.ns, w.ns.X0, w.ns.ldx, w.ns.Xf, w.ns.ldx, st);
+      rc = launch_nesterov(w.grad + m.oW, w.cc, mom + m.oW, ns.U, mu, n, ns.part, &nparts, ms);
+      if (!rc) rc = launch_ns_input(ns.U, ns.part, nparts, (int)m.rows, (int)m.cols, eps, ns.X0, ns.ldx, ms);
+      if (!rc) rc = ns_run(mm, nn, coeffs, iters, ns, ns.X0, ns.ldx, ns.Xf, ns.ldx, ms);
       const double r = (double)m.rows / (double)m.cols;
       if (!rc)
-        rc = launch_ns_finalize(w.ns.Xf, w.ns.ldx, (int)m.rows, (int)m.cols, 1.0 - lr * wd, lr * sqrt(r > 1.0 ? r : 1.0),
-                                pm + m.oW, (bf16*)m.shadow, m.ldw, st);
+        rc = launch_ns_finalize(ns.Xf, ns.ldx, (int)m.rows, (int)m.cols, 1.0 - lr * wd, lr * sqrt(r > 1.0 ? r : 1.0),
+                                pm + m.oW, (bf16*)m.shadow, m.ldw, ms);
       if (rc) return rc;
     }
+    if (sm.n > 0) {
+      PL_CUDA(cudaFuncSetAttribute((const void*)mg_small_muon_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)((2 * kSmallElems + 2 * kSmallSide * kSmallSide) * sizeof(float))));
+      mg_small_muon_kernel<<<sm.n, 256, small_smem, st>>>(sm, w.grad, w.cc, pm, mom, mu, eps, 1.0 - lr * wd, lr);
+      count_launch();
+      PL_LAUNCH("mg_small_muon_kernel");
+    }
+    BiasList bl{};
     for (const Bias& b : biases) {
-      rc = launch_stepvec_fast(w.grad + b.oB, w.cc, pm + b.oB, mom + b.oB, b.shadow, lr, wd, mu, (int)b.n, st);
-      if (rc) return rc;
+      bl.oB[bl.count] = b.oB;
+      bl.n[bl.count] = (int)b.n;
+      bl.shadow[bl.count] = b.shadow;
+      bl.count++;
+    }
+    mg_bias_step_kernel<<<(unsigned)std::max<long>(1, (H + 255) / 256), 256, 0, st>>>(bl, w.grad, w.cc, pm, mom, lr, wd,
+                                                                                      mu);
+    count_launch();
+    PL_LAUNCH("mg_bias_step_kernel");
+    if (two) {
+      PL_CUDA(cudaEventRecord(s->ev_join, s->side));
+      PL_CUDA(cudaStreamWaitEvent(st, s->ev_join, 0));
     }
   } else {
     double cc = 1.0;
@@ -1075,6 +1437,7 @@ int alloc_columns(pl_mg* s) {
   s->prio_p = mg_alloc<double>(s->allocs, s->N, f);
   s->prio_cum = mg_alloc<double>(s->allocs, s->N, f);
   s->lastw = mg_alloc<int>(s->allocs, s->N, f);
+  s->rng_dev = mg_alloc<unsigned long long>(s->allocs, 1, f);
   return f ? PL_ERR_NOMEM : PL_OK;
 }
 
@@ -1133,6 +1496,11 @@ int pl_mg_destroy(pl_mg* s) {
   pl::free_list(s->w.allocs);
   pl::free_list(s->allocs);
   if (s->traj_own) cudaFree(s->traj_own);
+  if (s->gexec) cudaGraphExecDestroy(s->gexec);
+  if (s->cap) cudaStreamDestroy(s->cap);
+  if (s->side) cudaStreamDestroy(s->side);
+  if (s->ev_fork) cudaEventDestroy(s->ev_fork);
+  if (s->ev_join) cudaEventDestroy(s->ev_join);
   delete s;
   return PL_OK;
 }
@@ -1218,22 +1586,28 @@ int pl_mg_vtrace(pl_mg* s, double gamma, double lam, double rhoClip, double cCli
   return PL_OK;
 }
 
-int pl_mg_vtrace_prio(pl_mg* s, double gamma, double lam, double rhoClip, double cClip, size_t mbSegs,
-                      double prioAlpha, double annealBeta, uint64_t rng, void* stream) {
+static int mg_vtrace_prio_impl(pl_mg* s, double gamma, double lam, double rhoClip, double cClip, size_t mbSegs,
+                               double prioAlpha, double annealBeta, uint64_t rng, bool rng_on_device,
+                               cudaStream_t st) {
   using namespace pl;
   PL_REQUIRE(s != nullptr && mbSegs > 0 && mbSegs < (1u << 30), PL_ERR_INVALID, "pl_mg_vtrace_prio: bad argument");
-  cudaStream_t st = (cudaStream_t)stream;
   int rc = mg_vtrace_dev(s, gamma, lam, rhoClip, cClip, st);
   if (rc) return rc;
   rc = ensure_sample(s, (long)mbSegs);
   if (rc) return rc;
   mg_prio_kernel<<<1, 1024, 0, st>>>(s->l1, s->N, (long)mbSegs, prioAlpha, annealBeta, (unsigned long long)rng,
-                                     s->prio_p, s->prio_cum, s->seg, s->mbp);
+                                     rng_on_device ? s->rng_dev : nullptr, s->prio_p, s->prio_cum, s->seg, s->mbp);
   count_launch();
   PL_LAUNCH("mg_prio_kernel");
   s->prio_B = (long)mbSegs;
   s->prio_fresh = true;
   return PL_OK;
+}
+
+int pl_mg_vtrace_prio(pl_mg* s, double gamma, double lam, double rhoClip, double cClip, size_t mbSegs,
+                      double prioAlpha, double annealBeta, uint64_t rng, void* stream) {
+  return mg_vtrace_prio_impl(s, gamma, lam, rhoClip, cClip, mbSegs, prioAlpha, annealBeta, rng, false,
+                             (cudaStream_t)stream);
 }
 
 int pl_mg_grad(pl_mg* s, const pl_mg_net* net, size_t handle, const double* params, const double* segIdx,
@@ -1279,7 +1653,9 @@ int pl_mg_grad(pl_mg* s, const pl_mg_net* net, size_t handle, const double* para
   if (rc) return rc;
   // gather
   const int Bi = (int)Bmb, T = (int)s->T;
-  mg_adv_ms_kernel<<<1, 1024, 0, st>>>(s->adv, s->seg, Bi, T, w.ms);
+  mg_adv_ms_kernel<<<kAdvBlocks, 256, 0, st>>>(s->adv, s->seg, Bi, T, 0, w.ms, w.adv_part, w.adv_counter);
+  mg_adv_ms_kernel<<<kAdvBlocks, 256, 0, st>>>(s->adv, s->seg, Bi, T, 1, w.ms, w.adv_part, w.adv_counter);
+  count_launch();
   mg_gather_scal_kernel<<<blocks_for(w.R), 256, 0, st>>>(s->act, s->logp, s->term, s->adv, s->value, s->seg, s->mbp,
                                                          w.ms, Bi, T, w.act_i, w.adv_f, w.ret_f, w.olp_f, w.ov_f,
                                                          w.term_f);
@@ -1373,23 +1749,101 @@ int pl_mg_read_state(pl_mg* s, double* value, double* ratio, double* adv) {
   return device_error_check();
 }
 
+static int mg_minibatch(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hyper* h, size_t mbSegs,
+                        uint64_t rng, bool rng_on_device, double lr, cudaStream_t st) {
+  const double gscale = 1.0 / (double)(mbSegs * (size_t)s->T);
+  int rc = mg_vtrace_prio_impl(s, h->gamma, h->lam, h->rhoClip, h->cClip, mbSegs, h->prioAlpha, h->annealBeta, rng,
+                               rng_on_device, st);
+  if (rc) return rc;
+  rc = pl_mg_grad(s, net, handle, nullptr, nullptr, nullptr, mbSegs, h->vfCoef, h->entCoef, h->clipEps, h->vfClip,
+                  h->bf16, st);
+  if (rc) return rc;
+  return pl_mg_muon(s, net, handle, nullptr, lr, h->wd, h->mu, h->eps, h->maxGradNorm, gscale, h->ns_coeffs,
+                    h->ns_coeffs ? h->ns_iters : 5, h->bf16, st);
+}
+
+// The fast tier runs the first minibatch of the update eagerly (which also performs every one-time
+// set-up outside any capture) and replays a captured graph of the same minibatch for the other
+// numMB - 1: the sampler's generator state advances in device memory, every other argument of the
+// chain is fixed for the update. The graph is captured again when the network, handle,
+// hyperparameters, minibatch size or lr change.
+static int mg_update_graph(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hyper* h, size_t numMB,
+                           size_t mbSegs, uint64_t* rng, double lr, cudaStream_t st) {
+  using namespace pl;
+  std::vector<double> key = {(double)net->D, (double)net->H, (double)net->L, (double)net->A, (double)net->K,
+                             (double)net->enc_act, (double)handle, h->gamma, h->lam, h->rhoClip, h->cClip,
+                             h->prioAlpha, h->annealBeta, h->wd, h->mu, h->eps, h->vfCoef, h->entCoef, h->clipEps,
+                             h->vfClip, h->maxGradNorm, (double)mbSegs, lr, (double)h->ns_iters};
+  if (h->ns_coeffs)
+    for (size_t i = 0; i < 3 * h->ns_iters; i++) key.push_back(h->ns_coeffs[i]);
+  // everything that allocates or reads back happens before the capture
+  const MgShape sh = shape_of(net);
+  int rc = ensure_work(s, sh, (long)mbSegs, s->T, true);
+  if (!rc) rc = ensure_sample(s, (long)mbSegs);
+  if (rc) return rc;
+  if (s->shadow_src != handle) {
+    rc = refresh_shadows(s, (const double*)handle, st);
+    if (rc) return rc;
+    s->shadow_src = handle;
+  }
+  PL_CUDA(cudaMemcpyAsync(s->rng_dev, rng, sizeof(uint64_t), cudaMemcpyHostToDevice, st));
+  rc = mg_minibatch(s, net, handle, h, mbSegs, 0, true, lr, st);
+  if (rc) return rc;
+  if (!s->gexec || key != s->gkey) {
+    if (s->gexec) {
+      cudaGraphExecDestroy(s->gexec);
+      s->gexec = nullptr;
+    }
+    if (!s->cap) PL_CUDA(cudaStreamCreateWithFlags(&s->cap, cudaStreamNonBlocking));
+    const uint64_t c0 = pl_kernel_launch_count();
+    PL_CUDA(cudaStreamBeginCapture(s->cap, cudaStreamCaptureModeThreadLocal));
+    rc = mg_minibatch(s, net, handle, h, mbSegs, 0, true, lr, s->cap);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(s->cap, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return check_cuda(e, "cudaStreamEndCapture (MinGRU minibatch)");
+    const cudaError_t e2 = cudaGraphInstantiate(&s->gexec, g, 0);
+    cudaGraphDestroy(g);
+    if (e2 != cudaSuccess) {
+      s->gexec = nullptr;
+      return check_cuda(e2, "cudaGraphInstantiate (MinGRU minibatch)");
+    }
+    s->gkey = key;
+    s->gnodes = pl_kernel_launch_count() - c0;
+  }
+  for (size_t mb = 1; mb < numMB; mb++) {
+    PL_CUDA(cudaGraphLaunch(s->gexec, st));
+    count_launch(s->gnodes);
+  }
+  *rng += (uint64_t)numMB * (uint64_t)mbSegs * 0x9E3779B97F4A7C15ULL;
+  s->prio_fresh = false;
+  s->grad_fresh = false;
+  s->shadow_src = handle;
+  return PL_OK;
+}
+
 int pl_mg_update(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hyper* h, size_t numMB, size_t mbSegs,
                  uint64_t* rng, double lr, void* stream) {
   using namespace pl;
   PL_REQUIRE(s && net && h && rng && handle, PL_ERR_INVALID, "pl_mg_update: NULL argument");
+  int rc = check_net(net);
+  if (rc) return rc;
+  PL_REQUIRE(mbSegs > 0 && mbSegs < (1u << 24), PL_ERR_INVALID, "pl_mg_update: bad minibatch size %zu", mbSegs);
+  PL_REQUIRE(s->cols_valid && s->traj && s->trajD == (long)net->D, PL_ERR_INVALID,
+             "pl_mg_update: set the columns and the obs trajectory first");
   const uint64_t l0 = pl_kernel_launch_count();
-  const double gscale = 1.0 / (double)(mbSegs * (size_t)s->T);
+  if (h->bf16 && !loss_channel_on() && numMB > 1) {
+    rc = mg_update_graph(s, net, handle, h, numMB, mbSegs, rng, lr, (cudaStream_t)stream);
+    s->launches = pl_kernel_launch_count() - l0;
+    return rc;
+  }
   for (size_t mb = 0; mb < numMB; mb++) {
-    int rc = pl_mg_vtrace_prio(s, h->gamma, h->lam, h->rhoClip, h->cClip, mbSegs, h->prioAlpha, h->annealBeta, *rng,
-                               stream);
+    rc = mg_minibatch(s, net, handle, h, mbSegs, *rng, false, lr, (cudaStream_t)stream);
     if (rc) return rc;
     *rng += (uint64_t)mbSegs * 0x9E3779B97F4A7C15ULL;
-    rc = pl_mg_grad(s, net, handle, nullptr, nullptr, nullptr, mbSegs, h->vfCoef, h->entCoef, h->clipEps, h->vfClip,
-                    h->bf16, stream);
-    if (rc) return rc;
-    rc = pl_mg_muon(s, net, handle, nullptr, lr, h->wd, h->mu, h->eps, h->maxGradNorm, gscale, h->ns_coeffs,
-                    h->ns_coeffs ? h->ns_iters : 5, h->bf16, stream);
-    if (rc) return rc;
   }
   s->launches = pl_kernel_launch_count() - l0;
   return PL_OK;
