@@ -6,6 +6,8 @@
 #define PUFFERLEAN_LEAN_H
 #include <lean/lean.h>
 #include <stdint.h>
+
+#include "pufferlean_b200.h"
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -62,6 +64,39 @@ lean_obj_res lean_cuda_mg_read_losses(lean_obj_arg w);
 lean_obj_res lean_ffi_shuffle_perm(size_t NT, size_t epochs, uint64_t rng);
 lean_obj_res lean_ffi_gae_soa(lean_obj_arg vals, lean_obj_arg rews, lean_obj_arg terms, size_t N, size_t T,
                               double gamma, double lam);
+
+/* MinGRU path. cudaMgPrepFFI, CUDA.lean:154-155; replaces ffi/puffercuda.cu:316-335 */
+lean_obj_res lean_cuda_mg_prep(lean_obj_arg rew, lean_obj_arg term, lean_obj_arg act, lean_obj_arg logp,
+                               lean_obj_arg val, lean_obj_arg boot, size_t N, size_t T, size_t K, lean_obj_arg w);
+/* cudaMgColsReadyFFI, CUDA.lean:361-362; replaces ffi/puffercuda.cu:305-309 */
+lean_obj_res lean_cuda_mg_cols_ready(size_t N, size_t T, lean_obj_arg w);
+/* cudaMgVtraceFFI, CUDA.lean:159-160; replaces ffi/puffercuda.cu:389-399 */
+lean_obj_res lean_cuda_mg_vtrace(size_t N, size_t T, double gamma, double lam, double rhoClip, double cClip,
+                                 lean_obj_arg w);
+/* cudaMgVtracePrioFFI, CUDA.lean:369-371; replaces ffi/puffercuda.cu:443-470 */
+lean_obj_res lean_cuda_mg_vtrace_prio(size_t N, size_t T, double gamma, double lam, double rhoClip, double cClip,
+                                      size_t mbSegs, double prioAlpha, double annealBeta, uint64_t rng,
+                                      lean_obj_arg w);
+/* cudaMinGRUPpoGradFFI, CUDA.lean:126-129; replaces ffi/puffercuda.cu:5206-5622 */
+lean_obj_res lean_cuda_mingru_ppo_grad(lean_obj_arg params, lean_obj_arg obs, lean_obj_arg scal, size_t B, size_t T,
+                                       size_t H, size_t D, size_t L, size_t A, size_t K, lean_obj_arg hs,
+                                       double vfCoef, double entCoef, double clipEps, double vfClip,
+                                       lean_obj_arg segIdx, lean_obj_arg mbPrio, lean_obj_arg w);
+/* cudaMinGRUMuonResidentFFI, CUDA.lean:354-356; replaces ffi/puffercuda.cu:5727-5976 */
+lean_obj_res lean_cuda_mingru_muon_resident(size_t handle, lean_obj_arg gClip, size_t H, size_t D, size_t L,
+                                            size_t A, double lr, double wd, double mu, double eps,
+                                            double maxGradNorm, double gscale, lean_obj_arg w);
+/* No reference counterpart: the pl_mg session behind the MinGRU symbols (NULL before the first
+ * lean_cuda_mg_prep); the rollout passes its device obs trajectory to pl_mg_set_obs_dev on it. */
+pl_mg* pl_lean_mg_session(void);
+/* prioSampleFFI / gatherSeqMinibatchFFI, Puffer/Float/FFI.lean:113-125; replace ffi/pufferffi.c:1094-1125
+ * and :1137-1176 */
+lean_obj_res lean_ffi_prio_sample(lean_obj_arg advL1, size_t N, size_t T, size_t mbSegs, double prioAlpha,
+                                  double annealBeta, uint64_t rng);
+lean_obj_res lean_ffi_gather_seq_minibatch(lean_obj_arg obsCol, lean_obj_arg actCol, lean_obj_arg logpCol,
+                                           lean_obj_arg termCol, lean_obj_arg advFlat, lean_obj_arg valueBuf,
+                                           lean_obj_arg segIdx, lean_obj_arg mbPrio, size_t T, size_t Bmb, size_t D,
+                                           size_t N);
 
 #ifdef __cplusplus
 }

@@ -14,6 +14,7 @@
 #include <lean/lean.h>
 #include <math.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "pufferlean_b200.h"
@@ -224,6 +225,212 @@ LEAN_EXPORT lean_obj_res lean_cuda_mg_read_losses(lean_obj_arg w) {
   lean_obj_res out = new_fa(7);
   pl_read_losses(fa(out));
   return lean_io_result_mk_ok(out);
+}
+
+/* ---------------------------------------------------------------- MinGRU path (CUDA.lean:126-160, 354-371) */
+/* The reference keeps the MinGRU columns, sample and resident gradient in process globals; the adapter
+ * keeps one pl_mg session for them (recreated when N or T change) and remembers the policy handle of the
+ * last resident Muon step, whose weights a grad call with empty params then uses. The network is the
+ * reference's (K = 3, linear encoder). PUFFER_MG_BF16=0 selects the fp32 tier; the default is the bf16
+ * tensor-core tier (the reference's default is bf16 tensor-core compute as well). */
+static pl_mg* g_mg = NULL;
+static size_t g_mg_N = 0, g_mg_T = 0;
+static size_t g_mg_handle = 0;
+
+/* The session behind the MinGRU symbols (no reference counterpart): the rollout hands it the device obs
+ * trajectory with pl_mg_set_obs_dev, as the reference's rollout fills g_dMGObsTraj. NULL before the first
+ * lean_cuda_mg_prep. */
+LEAN_EXPORT pl_mg* pl_lean_mg_session(void) { return g_mg; }
+
+static uint8_t mg_bf16(void) {
+  const char* e = getenv("PUFFER_MG_BF16");
+  return (e && e[0] == '0') ? 0 : 1;
+}
+static int mg_session(size_t N, size_t T) {
+  if (g_mg && g_mg_N == N && g_mg_T == T) return 0;
+  if (g_mg) pl_mg_destroy(g_mg);
+  g_mg = NULL;
+  int rc = pl_mg_create(N, T, &g_mg);
+  if (rc) return rc;
+  g_mg_N = N;
+  g_mg_T = T;
+  return 0;
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_mg_prep(lean_obj_arg rew, lean_obj_arg term, lean_obj_arg act, lean_obj_arg logp,
+                                           lean_obj_arg val, lean_obj_arg boot, size_t N, size_t T, size_t K,
+                                           lean_obj_arg w) {
+  (void)w;
+  int rc = K > 1 ? -4 : mg_session(N, T);
+  if (!rc) rc = pl_mg_set_columns(g_mg, fa(rew), fa(term), fa(act), fa(logp), fa(val), fa(boot));
+  lean_dec(rew);
+  lean_dec(term);
+  lean_dec(act);
+  lean_dec(logp);
+  lean_dec(val);
+  lean_dec(boot);
+  if (K > 1) {
+    return lean_io_result_mk_error(lean_mk_io_user_error(
+        lean_mk_string("pufferlean_b200: lean_cuda_mg_prep: multi-discrete action columns (K > 1) are not supported")));
+  }
+  if (rc) return io_fail("lean_cuda_mg_prep");
+  return lean_io_result_mk_ok(lean_box(0));
+}
+
+/* No rollout of this library stamps the columns, so the trainer always takes the prep call. */
+LEAN_EXPORT lean_obj_res lean_cuda_mg_cols_ready(size_t N, size_t T, lean_obj_arg w) {
+  (void)N;
+  (void)T;
+  (void)w;
+  return lean_io_result_mk_ok(lean_box(0));
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_mg_vtrace(size_t N, size_t T, double gamma, double lam, double rhoClip,
+                                             double cClip, lean_obj_arg w) {
+  (void)w;
+  lean_obj_res out = new_fa(N);
+  int rc = (g_mg && g_mg_N == N && g_mg_T == T) ? pl_mg_vtrace(g_mg, gamma, lam, rhoClip, cClip, fa(out), NULL) : -1;
+  if (rc) {
+    lean_dec(out);
+    return io_fail("lean_cuda_mg_vtrace (no columns for this N x T: call lean_cuda_mg_prep first)");
+  }
+  return lean_io_result_mk_ok(out);
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_mg_vtrace_prio(size_t N, size_t T, double gamma, double lam, double rhoClip,
+                                                  double cClip, size_t mbSegs, double prioAlpha, double annealBeta,
+                                                  uint64_t rng, lean_obj_arg w) {
+  (void)w;
+  int rc = (g_mg && g_mg_N == N && g_mg_T == T)
+               ? pl_mg_vtrace_prio(g_mg, gamma, lam, rhoClip, cClip, mbSegs, prioAlpha, annealBeta, rng, NULL)
+               : -1;
+  if (rc) return io_fail("lean_cuda_mg_vtrace_prio (no columns for this N x T: call lean_cuda_mg_prep first)");
+  return lean_io_result_mk_ok(lean_box(1));
+}
+
+/* Host mode (obs and scal given): returns [grad(P); new_logp(T*B); new_value(T*B)]. Device-column mode
+ * (obs and scal empty): gathers the sample (segIdx/mbPrio, or the resident one of
+ * lean_cuda_mg_vtrace_prio when both are empty) from the session's columns and obs trajectory, leaves
+ * the gradient resident and returns an empty array. */
+LEAN_EXPORT lean_obj_res lean_cuda_mingru_ppo_grad(lean_obj_arg pa, lean_obj_arg obs, lean_obj_arg scal, size_t B,
+                                                   size_t T, size_t H, size_t D, size_t L, size_t A, size_t K,
+                                                   lean_obj_arg hs, double vfCoef, double entCoef, double clipEps,
+                                                   double vfClip, lean_obj_arg segIdx, lean_obj_arg mbPrio,
+                                                   lean_obj_arg w) {
+  (void)w;
+  pl_mg_net net = {D, H, L, A, 3, 0};
+  const size_t P = pl_mg_param_count(&net);
+  const int host = fan(obs) > 0 && fan(scal) > 0;
+  lean_obj_res out = NULL;
+  int rc = 0;
+  const char* why = "lean_cuda_mingru_ppo_grad";
+  if (K > 1) {
+    rc = -4;
+    why = "lean_cuda_mingru_ppo_grad (multi-discrete heads, K > 1, are not supported)";
+  } else if (host) {
+    out = new_fa(P + 2 * T * B);
+    if (fan(pa) < P || fan(obs) < T * B * D || fan(scal) < 6 * T * B) {
+      rc = -1;
+      why = "lean_cuda_mingru_ppo_grad (host mode: params, obs or scal shorter than P, T*B*D, 6*T*B)";
+    } else {
+      rc = pl_mingru_ppo_grad(fa(pa), fa(obs), fa(scal), B, T, &net, vfCoef, entCoef, clipEps, vfClip, mg_bf16(),
+                              fa(out));
+    }
+  } else {
+    const int resident_sample = fan(segIdx) == 0 && fan(mbPrio) == 0;
+    const size_t handle = fan(pa) >= P ? 0 : g_mg_handle;
+    if (!g_mg || g_mg_T != T) {
+      rc = -1;
+      why = "lean_cuda_mingru_ppo_grad (device-column mode without columns: call lean_cuda_mg_prep first)";
+    } else if (fan(pa) < P && !handle) {
+      rc = -1;
+      why = "lean_cuda_mingru_ppo_grad (empty params and no resident Muon step has run yet)";
+    } else {
+      rc = pl_mg_grad(g_mg, &net, handle, handle ? NULL : fa(pa), resident_sample ? NULL : fa(segIdx),
+                      resident_sample ? NULL : fa(mbPrio), B, vfCoef, entCoef, clipEps, vfClip, mg_bf16(), NULL);
+    }
+    out = new_fa(0);
+  }
+  lean_dec(pa);
+  lean_dec(obs);
+  lean_dec(scal);
+  lean_dec(hs);
+  lean_dec(segIdx);
+  lean_dec(mbPrio);
+  if (rc) {
+    lean_dec(out);
+    return io_fail(why);
+  }
+  return lean_io_result_mk_ok(out);
+}
+
+/* gClip empty: clip and consume the resident gradient, return an empty array; gClip of P entries: an
+ * already clipped host gradient, return the new weights (P). */
+LEAN_EXPORT lean_obj_res lean_cuda_mingru_muon_resident(size_t handle, lean_obj_arg gClip, size_t H, size_t D, size_t L,
+                                                        size_t A, double lr, double wd, double mu, double eps,
+                                                        double maxGradNorm, double gscale, lean_obj_arg w) {
+  (void)w;
+  pl_mg_net net = {D, H, L, A, 3, 0};
+  const size_t P = pl_mg_param_count(&net);
+  const int host = fan(gClip) > 0;
+  int rc;
+  const char* why = "lean_cuda_mingru_muon_resident";
+  if (!g_mg) {
+    rc = -1;
+    why = "lean_cuda_mingru_muon_resident (no MinGRU session: call lean_cuda_mg_prep first)";
+  } else if (host && fan(gClip) < P) {
+    rc = -1;
+    why = "lean_cuda_mingru_muon_resident (host gClip shorter than the parameter vector)";
+  } else {
+    rc = pl_mg_muon(g_mg, &net, handle, host ? fa(gClip) : NULL, lr, wd, mu, eps, maxGradNorm, gscale, NULL, 0,
+                    mg_bf16(), NULL);
+  }
+  lean_dec(gClip);
+  if (rc) return io_fail(why);
+  g_mg_handle = handle;
+  lean_obj_res out = new_fa(host ? P : 0);
+  if (host && pl_policy_download(handle, P, fa(out))) {
+    lean_dec(out);
+    return io_fail("lean_cuda_mingru_muon_resident (weights download)");
+  }
+  return lean_io_result_mk_ok(out);
+}
+
+/* ---------------------------------------------------------------- MinGRU host bookkeeping (FFI.lean:113-125) */
+LEAN_EXPORT lean_obj_res lean_ffi_prio_sample(lean_obj_arg advL1, size_t N, size_t T, size_t mbSegs, double prioAlpha,
+                                              double annealBeta, uint64_t rng) {
+  (void)T;
+  lean_obj_res idx = new_fa(mbSegs), mp = new_fa(mbSegs);
+  int rc = fan(advL1) < N ? -1 : pl_prio_sample(fa(advL1), N, mbSegs, prioAlpha, annealBeta, rng, fa(idx), fa(mp));
+  lean_dec(advL1);
+  if (rc) {
+    pure_fail(idx, "lean_ffi_prio_sample");
+    pure_fail(mp, "lean_ffi_prio_sample");
+  }
+  lean_obj_res pr = lean_alloc_ctor(0, 2, 0);
+  lean_ctor_set(pr, 0, idx);
+  lean_ctor_set(pr, 1, mp);
+  return pr;
+}
+
+LEAN_EXPORT lean_obj_res lean_ffi_gather_seq_minibatch(lean_obj_arg obsCol, lean_obj_arg actCol, lean_obj_arg logpCol,
+                                                       lean_obj_arg termCol, lean_obj_arg advFlat,
+                                                       lean_obj_arg valueBuf, lean_obj_arg segIdx,
+                                                       lean_obj_arg mbPrio, size_t T, size_t Bmb, size_t D, size_t N) {
+  (void)D;
+  (void)N;
+  lean_obj_res out = new_fa(6 * T * Bmb);
+  int rc = pl_gather_seq_minibatch(fa(actCol), fa(logpCol), fa(termCol), fa(advFlat), fa(valueBuf), fa(segIdx),
+                                   fa(mbPrio), T, Bmb, fa(out));
+  lean_dec(obsCol);
+  lean_dec(actCol);
+  lean_dec(logpCol);
+  lean_dec(termCol);
+  lean_dec(advFlat);
+  lean_dec(valueBuf);
+  lean_dec(segIdx);
+  lean_dec(mbPrio);
+  return rc ? pure_fail(out, "lean_ffi_gather_seq_minibatch") : out;
 }
 
 /* ---------------------------------------------------------------- host bookkeeping (FFI.lean) */

@@ -104,7 +104,7 @@ LEAN_LIB = os.path.join(os.path.dirname(plb.LIB_PATH), "libpufferlean_lean.so")
 def test_lean_adapter_exports_every_declared_symbol():
     lib = C.CDLL(LEAN_LIB)
     names = declared("pufferlean_lean.h")
-    assert len(names) >= 15
+    assert len(names) >= 23
     missing = [n for n in names if not hasattr(lib, n)]
     assert not missing, missing
 
@@ -123,6 +123,37 @@ def test_lean_adapter_host_bookkeeping_against_golden():
     out = O.ref_call(lib, "lean_ffi_gae_soa", C.c_void_p, O.FA(g["vals"]), O.FA(g["rews"]), O.FA(g["terms"]), int(N),
                      int(T), float(gm), float(lm))
     assert np.array_equal(O.read_float_array(out), g["out"])
+
+
+def test_lean_adapter_mingru_host_bookkeeping_against_golden():
+    from oracle import oracle as O
+
+    lib = C.CDLL(LEAN_LIB)
+    gp = np.load(os.path.join(ROOT, "tests", "golden", "prio.npz"))
+    m = gp["meta"]
+    pr = O.ref_call(lib, "lean_ffi_prio_sample", C.c_void_p, O.FA(gp["L1"]), int(m[0]), int(m[1]), int(m[2]),
+                    float(m[3]), float(m[4]), ("u64", int(m[5])))
+    assert np.array_equal(O.read_float_array(O.ctor_field(pr, 0)), gp["idx"])
+    assert np.array_equal(O.read_float_array(O.ctor_field(pr, 1)), gp["mbPrio"])
+    gs = np.load(os.path.join(ROOT, "tests", "golden", "gather_seq.npz"))
+    N, T, D, Bmb = (int(x) for x in gs["meta"])
+    out = O.ref_call(lib, "lean_ffi_gather_seq_minibatch", C.c_void_p, O.FA(np.zeros(N * T * D)), O.FA(gs["act"]),
+                     O.FA(gs["logp"]), O.FA(gs["term"]), O.FA(gs["adv"]), O.FA(gs["value"]), O.FA(gs["seg"]),
+                     O.FA(gs["mbPrio"]), T, Bmb, D, N)
+    assert np.array_equal(O.read_float_array(out), gs["out"])
+
+
+def test_lean_adapter_mingru_io_errors_without_state():
+    """Without columns, or asking for multi-discrete heads, the MinGRU IO symbols return IO errors."""
+    from oracle import oracle as O
+
+    lib = C.CDLL(LEAN_LIB)
+    r = O.ref_call(lib, "lean_cuda_mg_vtrace", C.c_void_p, 3, 4, 0.99, 0.95, 1.0, 1.0, ("obj", 1))
+    assert O.ctor_tag(r) == 1
+    r = O.ref_call(lib, "lean_cuda_mg_prep", C.c_void_p, *[O.FA(np.zeros(8)) for _ in range(6)], 2, 4, 2, ("obj", 1))
+    assert O.ctor_tag(r) == 1
+    r = O.ref_call(lib, "lean_cuda_mg_cols_ready", C.c_void_p, 2, 4, ("obj", 1))
+    assert O.ctor_tag(r) == 0
 
 
 def test_lean_adapter_pure_failure_is_nan_not_zero():

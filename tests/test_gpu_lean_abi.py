@@ -66,3 +66,72 @@ def test_lean_resident_policy_round_trip(lib):
     assert np.abs(pm - f["out"]).max() < 1e-3
     r = O.ref_call(lib, "lean_cuda_policy_free", VP, handle, ("obj", 1))
     assert O.ctor_tag(r) == 0
+
+
+def _mg_lean_inputs():
+    from oracle import kat
+
+    return kat.kat_mingru_update()
+
+
+def test_lean_mingru_host_grad_against_reference_c(lib, monkeypatch):
+    """lean_cuda_mingru_ppo_grad in host mode (obs and scal given) on the verify-mingru-grad-gpu inputs."""
+    from oracle import kat
+
+    monkeypatch.setenv("PUFFER_MG_BF16", "0")
+    k = kat.kat_mingru_grad()
+    g = np.load(os.path.join(GOLD, "mingru_grad.npz"))
+    P = O.mg_param_count(k["D"], k["H"], k["L"], k["A"])
+    r = O.ref_call(lib, "lean_cuda_mingru_ppo_grad", VP, FA(k["params"]), FA(k["obsTB"]), FA(k["scal"]), k["B"],
+                   k["T"], k["H"], k["D"], k["L"], k["A"], 1, FA(np.zeros(0)), k["vf"], k["ent"], k["clip"],
+                   k["vfClip"], FA(np.zeros(0)), FA(np.zeros(0)), ("obj", 1))
+    assert O.ctor_tag(r) == 0
+    out = O.read_float_array(O.ctor_field(r, 0))
+    ref = 0.0 + g["seq0"][:P] + g["seq1"][:P]
+    assert out.size == P + 2 * k["T"] * k["B"]
+    assert np.max(np.abs(out[:P] - ref) / (np.abs(ref) + 1e-4)) < 2e-3
+
+
+def test_lean_mingru_trainer_sequence_against_reference(lib, monkeypatch):
+    """The reference trainer's per-minibatch calls (Puffer/RL/MinGRUTrain.lean:800-850) through the Lean
+    symbols: mg_prep, then per minibatch mg_vtrace_prio, mingru_ppo_grad in device-column mode (params
+    on the first call, empty after), mingru_muon_resident with an empty gClip; fp32 tier against the
+    update composed from the reference's own C."""
+    monkeypatch.setenv("PUFFER_MG_BF16", "0")
+    k = _mg_lean_inputs()
+    N, T, D, H, L, A = (k[x] for x in ("N", "T", "D", "H", "L", "A"))
+    P = O.mg_param_count(D, H, L, A)
+    hh = plb.policy_load(k["pm0"], P)
+    try:
+        r = O.ref_call(lib, "lean_cuda_mg_prep", VP, FA(k["rew"]), FA(k["term"]), FA(k["act"]), FA(k["logp"]),
+                       FA(k["val0"]), FA(k["boot"]), N, T, 1, ("obj", 1))
+        assert O.ctor_tag(r) == 0
+        sess = lib.pl_lean_mg_session
+        sess.restype = C.c_void_p
+        s = sess()
+        assert s
+        obs = np.ascontiguousarray(k["obs"], dtype=np.float64)
+        plb.lib().pl_mg_set_obs.argtypes = [C.c_void_p, C.POINTER(C.c_double), C.c_size_t]
+        assert plb.lib().pl_mg_set_obs(s, obs.ctypes.data_as(C.POINTER(C.c_double)), D) == 0
+        rng = k["rng"]
+        Bmb = k["mbSegs"]
+        for mb in range(k["numMB"]):
+            r = O.ref_call(lib, "lean_cuda_mg_vtrace_prio", VP, N, T, k["gamma"], k["lam"], k["rho"], k["c"], Bmb,
+                           k["alpha"], k["beta"], ("u64", rng), ("obj", 1))
+            assert O.ctor_tag(r) == 0
+            rng = (rng + Bmb * 0x9E3779B97F4A7C15) & ((1 << 64) - 1)
+            pa = k["pm0"][:P] if mb == 0 else np.zeros(0)
+            r = O.ref_call(lib, "lean_cuda_mingru_ppo_grad", VP, FA(pa), FA(np.zeros(0)), FA(np.zeros(0)), Bmb, T, H, D,
+                           L, A, 1, FA(np.zeros(0)), k["vf"], k["ent"], k["clip"], k["vfClip"], FA(np.zeros(0)),
+                           FA(np.zeros(0)), ("obj", 1))
+            assert O.ctor_tag(r) == 0, "grad"
+            assert O.read_float_array(O.ctor_field(r, 0)).size == 0
+            r = O.ref_call(lib, "lean_cuda_mingru_muon_resident", VP, hh, FA(np.zeros(0)), H, D, L, A, k["lr"],
+                           k["wd"], k["mu"], k["eps"], k["maxGradNorm"], 1.0 / (Bmb * T), ("obj", 1))
+            assert O.ctor_tag(r) == 0, "muon"
+        out = plb.policy_download(hh, P)
+    finally:
+        plb.policy_free(hh)
+    ref = np.load(os.path.join(GOLD, "mingru_update.npz"))["out"]
+    d_ref, d_out = ref[:P] - k["pm0"][:P], out[:P] - k["pm0"][:P]
+    assert np.linalg.norm(d_out - d_ref) / np.linalg.norm(d_ref) < 1e-3
