@@ -499,7 +499,7 @@ def mingru_init_pm(D, H, L, A, K, seed):
 MINGRU_C4 = dict(N=8192, T=64, D=118, H=512, L=1, A=4, mb_segs=512, num_mb=64, lr=0.02)
 
 
-def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None):
+def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None, cpu=False):
     """the Breakout-shaped recurrent update, 8192 envs x 64, obs 118 ~U(0,1), 4 actions,
     rewards U(-1,1), dones Bernoulli(.005); encoder 118->512 (+GELU), MinGRU hidden 512 with gate + candidate
     512->1024 (K = 2; K = 3 adds the reference's highway projection), heads 512->4 and 512->1; minibatches of
@@ -567,7 +567,19 @@ def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None):
     flops = (fwd + bwd) * c["num_mb"]
     m_ns = [(H, D)] + [(K * H, H)] * L_ + [(A, H), (1, H)]
     ns_fl = sum(5 * (4 * min(r_, c_) ** 2 * max(r_, c_) + 2 * min(r_, c_) ** 3) for r_, c_ in m_ns) * c["num_mb"]
-    return {"config": "configs[3]: Breakout-shaped MinGRU update, 8192 envs x 64, obs 118, H 512, "
+    out_cpu = None
+    if cpu:
+        from oracle import cpu_port
+
+        per_update, det = cpu_port.mingru_timed_sample(D, H, L_, A, K, enc_act, T, c["mb_segs"], c["num_mb"], QUINTIC)
+        out_cpu = {"value": NT / per_update, "unit": "samples/s", "cores": det["threads"],
+                   "kind": "reference" if det["grad_source"] == "reference C" else "port",
+                   "sample": (f"BPTT gradient of {det['nseq']} sequences x {T} steps, one per host thread "
+                              f"({det['grad_source']}, ffi/pufferffi.c:763-876; {det['t_grad']:.2f} s) + one Muon "
+                              f"step of every matrix on numpy BLAS ({det['t_muon']:.2f} s), scaled to "
+                              f"{c['num_mb']} minibatches of {c['mb_segs']} sequences")}
+    return {"cpu_baseline": out_cpu,
+            "config": "configs[3]: Breakout-shaped MinGRU update, 8192 envs x 64, obs 118, H 512, "
                       f"{'gate+candidate 512->1024 (K=2)' if K == 2 else 'hid|gate|proj 512->1536 (K=3, reference)'}"
                       f"{', GELU encoder' if enc_act else ''}, 4 actions, 64 minibatches of 512 segments x 64",
             "K": K, "enc_act": "gelu" if enc_act else "none", "params": P,
@@ -626,9 +638,9 @@ def main():
     args = ap.parse_args()
     if args.only:
         if args.only == "c4":
-            res = measure_mingru_c4(args)
+            res = measure_mingru_c4(args, cpu=not args.no_cpu)
         elif args.only == "c4r":
-            res = measure_mingru_c4(args, K=3, enc_act=0)
+            res = measure_mingru_c4(args, K=3, enc_act=0, cpu=not args.no_cpu)
         else:
             res = measure_vtrace_c2() if args.only == "c2" else measure_ns_c3()
         print(json.dumps(res), flush=True)
@@ -670,7 +682,7 @@ def main():
     if rank == 0 and not args.no_extra:
         out["c2_vtrace"] = measure_vtrace_c2()
         out["c3_newton_schulz"] = measure_ns_c3()
-        out["c4_mingru"] = measure_mingru_c4(args)
+        out["c4_mingru"] = measure_mingru_c4(args, cpu=not args.no_cpu)
     if rank == 0:
         if not args.no_cpu and world == 1:
             out["cpu_baseline"] = cpu_baseline(wl)

@@ -145,3 +145,51 @@ def timed_update_sample(D, H, A, L, act, Nmb, epochs, num_mb, coeffs, rows=4096,
     t_rows, t_muon = t1 - t0, t2 - t1
     per_update = epochs * num_mb * (Nmb / rows * t_rows + t_muon)
     return per_update, dict(rows=rows, t_rows=t_rows, t_muon=t_muon)
+
+
+def mingru_timed_sample(D, H, L, A, K, enc_act, T, mb_segs, num_mb, coeffs, nseq=None, threads=None, seed=0):
+    """Host-core time of one MinGRU update, from a bounded sample: the BPTT gradient of `nseq` sequences
+    (the reference's scalar C lean_ffi_mingru_ppo_grad_seq, ffi/pufferffi.c:763-876, when K = 3 and the
+    encoder is linear, else our C restatement of it), one sequence per host thread, plus one Muon step
+    of every MinGRU matrix with the Newton-Schulz matmuls on numpy BLAS. Returns (seconds per update,
+    details). The reference's own trainer runs one sequence at a time on one core."""
+    import concurrent.futures as cf
+    import ctypes as C
+    import os
+
+    from oracle import oracle as O
+
+    threads = threads or os.cpu_count() or 1
+    nseq = nseq or max(threads, 16)
+    g = np.random.default_rng(seed)
+    params, _ = O.init_mingru(D, H, L, A, 0x51 + seed, K)
+    P = params.size
+    use_ref = K == 3 and enc_act == 0 and O.ref_available()
+    seqs = []
+    for _ in range(nseq):
+        seqs.append([g.uniform(0, 1, T * D), g.integers(0, A, T).astype(float), g.standard_normal(T),
+                     g.uniform(-1, 1, T), np.full(T, np.log(1.0 / A)), (g.random(T) < 0.005).astype(float),
+                     g.standard_normal(T)])
+
+    def one(s):
+        if use_ref:
+            r = O.ref_call(O.ref_cpu(), "lean_ffi_mingru_ppo_grad_seq", C.c_void_p, O.FA(params), *[O.FA(x) for x in s],
+                           T, H, D, L, A, 0.5, 0.01, 0.2, 0.2)
+            return O.read_float_array(r)[:P]
+        return O.mingru_grad_seq(params, *s, T, H, D, L, A, K, enc_act)[0]
+
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+        grads = list(ex.map(one, seqs))
+    t_grad = time.perf_counter() - t0
+    gsum = np.sum(grads, axis=0)
+    # one Muon step over the flattenMG matrices (wEnc H x D, layers K*H x H, wDec A x H, wVal 1 x H)
+    shapes = [(H, D)] + [(K * H, H)] * L + [(A, H), (1, H)]
+    t0 = time.perf_counter()
+    for r_, c_ in shapes:
+        newton_schulz(g.standard_normal((r_, c_)), coeffs, 1e-7)
+    t_muon = time.perf_counter() - t0
+    per_mb = t_grad * (mb_segs / nseq) + t_muon
+    return per_mb * num_mb, {"nseq": nseq, "threads": threads, "t_grad": t_grad, "t_muon": t_muon,
+                             "grad_source": "reference C" if use_ref else "restatement", "finite":
+                             bool(np.isfinite(gsum).all())}
