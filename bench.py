@@ -588,6 +588,103 @@ def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None, cpu=False):
             "finite": bool(np.isfinite(pm_out).all()), "data": "synthetic (seeded torch generator 4)"}
 
 
+def _mlp_loss(pm, obs, acts, adv, ret, olp, D, H, A, vf=0.5, ent=0.01, clip=0.2):
+    """PPO loss of the one-hidden-layer ReLU policy (the reference's MLP) on the whole buffer, f64:
+    -mean(min(adv r, adv clip(r))) + vf 0.5 mean((v - ret)^2) - ent mean(entropy)."""
+    W1 = pm[:H * D].reshape(H, D)
+    b1 = pm[H * D:H * D + H]
+    O = A + 1
+    W2 = pm[H * D + H:H * D + H + O * H].reshape(O, H)
+    b2 = pm[H * D + H + O * H:H * D + H + O * H + O]
+    h = np.maximum(obs @ W1.T + b1, 0.0)
+    out = h @ W2.T + b2
+    lg, v = out[:, :A], out[:, A]
+    m = lg.max(axis=1, keepdims=True)
+    lse = m[:, 0] + np.log(np.exp(lg - m).sum(axis=1))
+    p = np.exp(lg - lse[:, None])
+    logp = lg[np.arange(len(acts)), acts.astype(int)] - lse
+    r = np.exp(logp - olp)
+    pg = -np.mean(np.minimum(adv * r, adv * np.clip(r, 1 - clip, 1 + clip)))
+    entropy = np.mean(lse - (p * lg).sum(axis=1))
+    return float(pg + vf * 0.5 * np.mean((v - ret) ** 2) - ent * entropy)
+
+
+def measure_drift(updates=100):
+    """Loss-curve drift over `updates` consecutive updates: the reference's MLP (configs[0] shapes with
+    its own net: 4 -> 128 ReLU -> 2 + 1, Kaiming init, its Newton-Schulz table) trained on one fixed
+    seeded 64 x 64 buffer by this library (bf16 and fp32 tiers, the resident update through the C ABI)
+    and by the oracle (f64 restatement of the reference CPU update), identical inputs and shuffles.
+    Reports the PPO loss of both parameter trajectories on the whole buffer after every update."""
+    import pufferlean_b200 as plb
+    from oracle import oracle as O
+
+    N, T, D, H, A, E, MB = 64, 64, 4, 128, 2, 4, 4
+    NT = N * T
+    g = np.random.default_rng(11)
+    obs = g.standard_normal(NT * D)
+    acts = g.integers(0, A, NT).astype(np.float64)
+    rew = (g.random(NT) < 0.5).astype(np.float64)
+    term = (g.random(NT) < 0.01).astype(np.float64)
+    params, _ = O.init_mlp(D, H, A + 1, 0xD21F7)
+    P = params.size
+    pm0 = np.concatenate([params, np.zeros(P)])
+    _, olp, val = O.mlp_ppo_grad(params, obs, acts, np.zeros(NT), np.zeros(NT), np.zeros(NT), NT, D, H, A)
+    ga = O.gae_soa(val, rew, term, N, T, 0.995, 0.90)
+    adv, ret = ga[:NT], ga[NT:]
+    hyper = dict(lr=0.02, wd=0.0, mu=0.95, eps=1e-7, vf=0.5, ent=0.01, clip=0.2, vfClip=0.2, maxGradNorm=1.5)
+    ob2 = obs.reshape(NT, D)
+
+    def loss(pm):
+        return _mlp_loss(pm[:P], ob2, acts, adv, ret, olp, D, H, A)
+
+    cpu = pm0.copy()
+    # control: the same f64 oracle from weights perturbed by 1e-12 (relative), to separate the
+    # divergence the training dynamics amplify from any implementation difference
+    ctl = pm0.copy()
+    ctl[:P] *= 1.0 + 1e-12 * np.random.default_rng(12).standard_normal(P)
+    curves = {"oracle_f64": [loss(cpu)], "oracle_perturbed_1e-12": [loss(ctl)]}
+    handles = {"bf16": plb.policy_load(pm0, P), "fp32": plb.policy_load(pm0, P)}
+    for k in handles:
+        curves[k] = [curves["oracle_f64"][0]]
+    t0 = time.time()
+    for u in range(updates):
+        perm = plb.shuffle_perm(NT, E, 1000 + u)
+        cpu = O.train_update(cpu, obs, acts, adv, ret, olp, perm, NT, D, H, A, E, MB, hyper["lr"], hyper["wd"],
+                             hyper["mu"], hyper["eps"], hyper["vf"], hyper["ent"], hyper["clip"], ov=val,
+                             vfClip=hyper["vfClip"], maxGradNorm=hyper["maxGradNorm"])
+        curves["oracle_f64"].append(loss(cpu))
+        ctl = O.train_update(ctl, obs, acts, adv, ret, olp, perm, NT, D, H, A, E, MB, hyper["lr"], hyper["wd"],
+                             hyper["mu"], hyper["eps"], hyper["vf"], hyper["ent"], hyper["clip"], ov=val,
+                             vfClip=hyper["vfClip"], maxGradNorm=hyper["maxGradNorm"])
+        curves["oracle_perturbed_1e-12"].append(loss(ctl))
+        for k, h in handles.items():
+            plb.cuda_train_update_resident(h, obs, acts, adv, ret, olp, val, perm, NT, D, H, A, E, MB, hyper["lr"],
+                                           hyper["wd"], hyper["mu"], hyper["eps"], hyper["vf"], hyper["ent"],
+                                           hyper["clip"], hyper["vfClip"], hyper["maxGradNorm"], 1 if k == "bf16" else 0)
+            curves[k].append(loss(plb.policy_download(h, P)))
+    finals = {k: plb.policy_download(h, P)[:P] for k, h in handles.items()}
+    for h in handles.values():
+        plb.policy_free(h)
+    ref = np.array(curves["oracle_f64"])
+    res = {"config": "configs[0] shapes, the reference's MLP (4 -> 128 ReLU -> 2+1), one fixed seeded 64 x 64 buffer, "
+                     f"{E} epochs x {MB} minibatches per update, {updates} updates",
+           "loss_first": float(ref[0]), "loss_last_oracle": float(ref[-1]), "seconds": time.time() - t0}
+    scale = float(np.max(np.abs(ref - ref[0]))) or 1.0
+    res["oracle_mean_loss_updates_51_100"] = float(np.mean(ref[51:]))
+    for k in list(handles) + ["oracle_perturbed_1e-12"]:
+        c = np.array(curves[k])
+        d = np.abs(c - ref)
+        res[k] = {"loss_last": float(c[-1]), "max_abs_drift": float(d.max()),
+                  "max_drift_rel_to_loss_change": float(d.max() / scale),
+                  "drift_at": {str(u): float(d[u]) for u in sorted({1, 5, 10, 50, updates}) if u <= updates},
+                  "mean_loss_updates_51_100": float(np.mean(c[51:])) if updates > 51 else None,
+                  "param_rel_diff": float(np.linalg.norm((finals[k] if k in finals else ctl[:P]) - cpu[:P]) /
+                                          np.linalg.norm(cpu[:P] - pm0[:P]))}
+    res["curve_oracle_every10"] = [float(x) for x in ref[::10]]
+    res["curve_bf16_every10"] = [float(x) for x in np.array(curves["bf16"])[::10]]
+    return res
+
+
 def cudart_memcpy_d2h(dst, handle):
     """8-byte read-back of params[0] from the resident policy (the reference's divergence guard)."""
     import pufferlean_b200 as plb
@@ -632,10 +729,15 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the configs[1] / configs[2] kernel measurements")
+    ap.add_argument("--drift", type=int, default=0, metavar="U",
+                    help="print the loss-curve drift of U consecutive updates against the f64 oracle and exit")
     ap.add_argument("--only", choices=["c2", "c3", "c4", "c4r"],
                     help="print only the configs[1] (c2), configs[2] (c3) or configs[3] (c4: K=2 + GELU encoder; "
                          "c4r: the reference's K=3 linear-encoder net) measurement")
     args = ap.parse_args()
+    if args.drift:
+        print(json.dumps(measure_drift(args.drift)), flush=True)
+        return 0
     if args.only:
         if args.only == "c4":
             res = measure_mingru_c4(args, cpu=not args.no_cpu)
