@@ -164,6 +164,41 @@ __device__ __forceinline__ float act_grad_fast(float z, int act) {
   return 0.5f * (1.f + t) + 0.5f * z * (1.f - t * t) * 0.7978845608028654f * (1.f + 3.f * 0.044715f * z * z);
 }
 
+// Activation over a register row with the (warp-uniform) activation code tested once per row,
+// so the per-element code is branch-free: v = act(z), or v = acc * act'(z) for the gradient.
+__device__ __forceinline__ float gelu_fast(float z) {
+  const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
+  return 0.5f * z * (1.f + tanh_fast(u));
+}
+__device__ __forceinline__ float gelu_grad_fast(float z) {
+  const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
+  const float t = tanh_fast(u);
+  return 0.5f * (1.f + t) + 0.5f * z * (1.f - t * t) * 0.7978845608028654f * (1.f + 3.f * 0.044715f * z * z);
+}
+template <int N>
+__device__ __forceinline__ void act_fwd_row(const float (&z)[N], float (&v)[N], int act) {
+  if (act == 1) {
+#pragma unroll
+    for (int j = 0; j < N; j++) v[j] = gelu_fast(z[j]);
+  } else if (act == 0) {
+#pragma unroll
+    for (int j = 0; j < N; j++) v[j] = z[j] > 0.f ? z[j] : 0.f;
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; j++) v[j] = z[j];
+  }
+}
+template <int N>
+__device__ __forceinline__ void act_grad_row(float (&v)[N], const float (&z)[N], int act) {
+  if (act == 1) {
+#pragma unroll
+    for (int j = 0; j < N; j++) v[j] *= gelu_grad_fast(z[j]);
+  } else if (act == 0) {
+#pragma unroll
+    for (int j = 0; j < N; j++) v[j] = z[j] > 0.f ? v[j] : 0.f;
+  }
+}
+
 // Shared memory: 1 KB alignment slack, the TMA ring, barriers, then the epilogue area: bf16 staging
 // tiles for the TMA bulk stores (per epilogue warp, one 32 x 32 tile per output) and the column
 // reduction scratch [4][BN] (+ per-warp loss partials). The ring takes what is left of 227 KB.
@@ -410,13 +445,14 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
           const float acc = have_acc ? __uint_as_float(rr[j >> 4][j & 15]) : 0.f;
           if constexpr (EPI == EPI_FWD) {
             z[j] = acc + ((n0 + j) < ep.out_cols ? ep.bias[n0 + j] : 0.f);
-            v[j] = act_fwd_fast(z[j], ep.act);
           } else if constexpr (EPI == EPI_DGRAD) {
-            v[j] = (row_ok && n0 + j < ep.out_cols) ? acc * act_grad_fast(aux[j], ep.act) : 0.f;
+            v[j] = (row_ok && n0 + j < ep.out_cols) ? acc : 0.f;
           } else {
             v[j] = ep.alpha * acc + (ep.aux ? ep.beta * aux[j] : 0.f) + (row == n0 + j ? ep.diag : 0.f);
           }
         }
+        if constexpr (EPI == EPI_FWD) act_fwd_row(z, v, ep.act);
+        if constexpr (EPI == EPI_DGRAD) act_grad_row(v, aux, ep.act);
         if (lane == 0) tc::bulk_wait_read<0>();  // the previous tile's stores have read the staging area
         __syncwarp();
         stage_row32(stg, lane, v);

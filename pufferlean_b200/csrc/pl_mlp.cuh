@@ -54,6 +54,9 @@ int launch_gather(bool bf16, const int* idx, int Nmb, const void* obs, int rowEl
                   float* mb_adv, float* mb_ret, float* mb_olp, float* mb_ov, double* part, double* ms,
                   cudaStream_t st, double* sums = nullptr);
 int launch_adv_ms_from_sums(const double* sums, double* ms, cudaStream_t st);
+// Column sums of `tiles` rows of ld floats in `part`; part must have colsum_scratch_elems(tiles, ld)
+// floats (the second reduction level lives after the partials).
+long colsum_scratch_elems(int tiles, long ld);
 int launch_colsum_reduce(const float* part, int tiles, long ld, int ncols, float* out, cudaStream_t st);
 int launch_splitk_reduce(const float* part, int S, long n, float* out, cudaStream_t st);
 int launch_gradnorm(const float* g, long P, double sc, double maxNorm, double* part, double* cc, cudaStream_t st);

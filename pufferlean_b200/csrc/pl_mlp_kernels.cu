@@ -144,12 +144,24 @@ __global__ void adv_ms_from_sums_kernel(const double* __restrict__ sums, double*
 }
 
 // ---------------------------------------------------------------- fixed-order reductions
-// out[c] = sum_t part[t*ld + c], t ascending (bias gradients from per-CTA column partials)
-__global__ void colsum_reduce_kernel(const float* __restrict__ part, int tiles, long ld, int ncols, float* out) {
-  int c = blockIdx.x * blockDim.x + threadIdx.x;
+// out[c] = sum over t of part[t*ld + c] (bias gradients from per-CTA column partials), in two
+// fixed-order levels: blockIdx.y sums its run of kColChunk tiles (t ascending) into part2, then
+// colsum_final_kernel sums the runs in order. Spreading the tiles over blockIdx.y keeps every SM
+// streaming instead of leaving one thread per column to walk thousands of tiles.
+constexpr int kColChunk = 32;
+__global__ void colsum_reduce_kernel(const float* __restrict__ part, int tiles, long ld, int ncols, float* part2) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= ncols) return;
+  const int t0 = blockIdx.y * kColChunk, t1 = min(tiles, t0 + kColChunk);
+  float s = 0.f;
+  for (int t = t0; t < t1; t++) s += part[(long)t * ld + c];
+  part2[(long)blockIdx.y * ncols + c] = s;
+}
+__global__ void colsum_final_kernel(const float* __restrict__ part2, int runs, long ld, int ncols, float* out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= ncols) return;
   float s = 0.f;
-  for (int t = 0; t < tiles; t++) s += part[(long)t * ld + c];
+  for (int r = 0; r < runs; r++) s += part2[(long)r * ld + c];
   out[c] = s;
 }
 // out[i] = sum_s part[s*n + i], s ascending (split-K slices)
@@ -433,9 +445,21 @@ int launch_gather(bool bf16, const int* idx, int Nmb, const void* obs, int rowEl
   PL_LAUNCH("gather_kernel");
   return PL_OK;
 }
+// part holds `tiles` rows of ld floats followed by room for ceil(tiles / kColChunk) rows of ncols
+// (the second level of the reduction).
+long colsum_scratch_elems(int tiles, long ld) { return (long)tiles * ld + ceil_div(tiles, kColChunk) * ld; }
 int launch_colsum_reduce(const float* part, int tiles, long ld, int ncols, float* out, cudaStream_t st) {
-  colsum_reduce_kernel<<<(unsigned)ceil_div(ncols, 128), 128, 0, st>>>(part, tiles, ld, ncols, out);
-  count_launch();
+  const int runs = (int)ceil_div(tiles, kColChunk);
+  if (runs <= 1) {
+    colsum_final_kernel<<<(unsigned)ceil_div(ncols, 128), 128, 0, st>>>(part, tiles, ld, ncols, out);
+    count_launch();
+  } else {
+    float* part2 = const_cast<float*>(part) + (long)tiles * ld;
+    dim3 g1((unsigned)ceil_div(ncols, 128), (unsigned)runs);
+    colsum_reduce_kernel<<<g1, 128, 0, st>>>(part, tiles, ld, ncols, part2);
+    colsum_final_kernel<<<(unsigned)ceil_div(ncols, 128), 128, 0, st>>>(part2, runs, ncols, ncols, out);
+    count_launch(2);
+  }
   PL_LAUNCH("colsum_reduce_kernel");
   return PL_OK;
 }

@@ -80,6 +80,8 @@ struct pl_update {
   bool dp = false;             // world > 1 with a communicator
   double* adv_sums = nullptr;  // [sum, sum of squares, count] of the minibatch's raw advantages
   std::vector<int> owner;      // Newton-Schulz owner rank of each layer
+  std::vector<std::vector<int>> ns_groups;  // layers of equal shape, orthogonalised as one batch
+  long ns_batch = 1;                        // largest group
   std::vector<float*> xres;    // per-layer orthogonalised update (m x n wide layout, fp32)
   // profiling: CUDA events around each launch group, per class
   bool prof = false;
@@ -238,7 +240,7 @@ static int alloc_session(pl_update* u) {
   u->mb_ov = d.use_old_values ? dalloc<float>(u, M) : nullptr;
   u->adv_part = dalloc<double>(u, 2 * 4096);
   u->ms = dalloc<double>(u, 4);
-  u->colpart = dalloc<float>(u, (size_t)mt * std::max(u->Hp, u->Op));
+  u->colpart = dalloc<float>(u, (size_t)colsum_scratch_elems(mt, std::max(u->Hp, u->Op)));
   u->grad = dalloc<float>(u, u->P);
   u->gn_part = dalloc<double>(u, 4096);
   u->cc = dalloc<double>(u, 4);
@@ -268,14 +270,34 @@ static int alloc_session(pl_update* u) {
     nprod = std::max(nprod, (long)ly.out * ly.in);
   }
   const long ldx = round_up(nmax, 64), ldg = round_up(mmax, 64);
+  // equal-shaped layers (the hidden 2048 x 2048 matrices of configs[4]) share one batched
+  // Newton-Schulz: one launch per GEMM of the chain covers all of them, filling the GPU's SMs
+  u->ns_groups.clear();
+  for (size_t l = 0; l < u->layers.size(); l++) {
+    bool placed = false;
+    for (auto& g : u->ns_groups) {
+      const Layer& f = u->layers[g[0]];
+      if (f.out == u->layers[l].out && f.in == u->layers[l].in) {
+        g.push_back((int)l);
+        placed = true;
+        break;
+      }
+    }
+    if (!placed) u->ns_groups.push_back({(int)l});
+  }
+  u->ns_batch = 1;
+  if (!u->dp)
+    for (auto& g : u->ns_groups) u->ns_batch = std::max<long>(u->ns_batch, (long)g.size());
   if (fast) {
+    // one batch slot holds the largest matrix; a group's batch uses slots of its own (smaller) size
+    const long slotx = round_up(mmax, 128) * ldx, slotg = round_up(mmax, 128) * ldg;
     u->ns.ldx = ldx;
     u->ns.ldg = ldg;
-    u->ns.X0 = dalloc<__nv_bfloat16>(u, (size_t)round_up(mmax, 128) * ldx);
-    u->ns.X1 = dalloc<__nv_bfloat16>(u, (size_t)round_up(mmax, 128) * ldx);
-    u->ns.G = dalloc<__nv_bfloat16>(u, (size_t)round_up(mmax, 128) * ldg);
-    u->ns.B = dalloc<__nv_bfloat16>(u, (size_t)round_up(mmax, 128) * ldg);
-    u->ns.Xf = dalloc<float>(u, (size_t)mmax * ldx);
+    u->ns.X0 = dalloc<__nv_bfloat16>(u, (size_t)(slotx * u->ns_batch));
+    u->ns.X1 = dalloc<__nv_bfloat16>(u, (size_t)(slotx * u->ns_batch));
+    u->ns.G = dalloc<__nv_bfloat16>(u, (size_t)(slotg * u->ns_batch));
+    u->ns.B = dalloc<__nv_bfloat16>(u, (size_t)(slotg * u->ns_batch));
+    u->ns.Xf = dalloc<float>(u, (size_t)(mmax * ldx * u->ns_batch));
     u->ns.U = dalloc<double>(u, nprod);
     u->ns.part = dalloc<double>(u, 4096);
     for (void* p : {(void*)u->ns.X0, (void*)u->ns.X1, (void*)u->ns.G, (void*)u->ns.B})
@@ -535,34 +557,41 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
   }
   if (rc) return rc;
   if (u->dp) return muon_sharded(u, lr, st);
-  for (size_t l = 0; l < u->layers.size(); l++) {
-    const Layer& ly = u->layers[l];
-    const long n = (long)ly.out * ly.in;
-    int nparts = 0;
-    const int m = std::min(ly.out, ly.in), nn = std::max(ly.out, ly.in);
-    {
+  for (const auto& grp : u->ns_groups) {
+    const Layer& g0 = u->layers[grp[0]];
+    const int m = std::min(g0.out, g0.in), nn = std::max(g0.out, g0.in);
+    const int nb = (int)grp.size();
+    const long xstride = (long)m * u->ns.ldx;  // one wide m x ldx matrix per batch slot
+    for (int q = 0; q < nb; q++) {
+      const Layer& ly = u->layers[grp[q]];
+      const long n = (long)ly.out * ly.in;
+      int nparts = 0;
       Span sp(u, 6, st, 0);
       rc = launch_nesterov(u->grad + ly.oW, u->cc, u->pm + u->P + ly.oW, u->ns.U, d.mu, n, u->ns.part, &nparts, st);
-      if (!rc) rc = launch_ns_input(u->ns.U, u->ns.part, nparts, ly.out, ly.in, d.eps, u->ns.X0, u->ns.ldx, st);
+      if (!rc)
+        rc = launch_ns_input(u->ns.U, u->ns.part, nparts, ly.out, ly.in, d.eps, u->ns.X0 + q * xstride, u->ns.ldx, st);
+      if (rc) return rc;
+    }
+    {
+      // algorithmic Newton-Schulz flops per step and matrix: 4 m^2 n + 2 m^3
+      Span sp(u, 4, st, (double)nb * u->iters * (4.0 * m * (double)m * nn + 2.0 * m * (double)m * m));
+      rc = ns_run_batched(m, nn, nb, u->coeffs.data(), u->iters, u->ns, u->ns.X0, u->ns.ldx, xstride, u->ns.Xf,
+                          u->ns.ldx, xstride, st);
     }
     if (rc) return rc;
-    {
-      // algorithmic Newton-Schulz flops per step: 4 m^2 n + 2 m^3
-      Span sp(u, 4, st, (double)u->iters * (4.0 * m * (double)m * nn + 2.0 * m * (double)m * m));
-      rc = ns_run(m, nn, u->coeffs.data(), u->iters, u->ns, u->ns.X0, u->ns.ldx, u->ns.Xf, u->ns.ldx, st);
-    }
-    if (rc) return rc;
-    const double r = (double)ly.out / (double)ly.in;
-    const double scale = sqrt(r > 1.0 ? r : 1.0);
-    {
+    for (int q = 0; q < nb; q++) {
+      const int l = grp[q];
+      const Layer& ly = u->layers[l];
+      const double r = (double)ly.out / (double)ly.in;
+      const double scale = sqrt(r > 1.0 ? r : 1.0);
       Span sp(u, 6, st, 0);
-      rc = launch_ns_finalize(u->ns.Xf, u->ns.ldx, ly.out, ly.in, 1.0 - lr * d.wd, lr * scale, u->pm + ly.oW, u->Wb[l],
-                              ly.in_p, st);
+      rc = launch_ns_finalize(u->ns.Xf + q * xstride, u->ns.ldx, ly.out, ly.in, 1.0 - lr * d.wd, lr * scale,
+                              u->pm + ly.oW, u->Wb[l], ly.in_p, st);
       if (!rc)
         rc = launch_stepvec_fast(u->grad + ly.ob, u->cc, u->pm + ly.ob, u->pm + u->P + ly.ob, u->bf[l], lr, d.wd, d.mu,
                                  ly.out, st);
+      if (rc) return rc;
     }
-    if (rc) return rc;
   }
   return PL_OK;
 }
