@@ -63,6 +63,24 @@ class Desc(C.Structure):
                 ("world", C.c_int), ("comm", C.c_void_p)]
 
 
+# DRAM bytes per launch of the roofline kernel set (forward, PPO-head, data- and weight-gradient
+# tc_gemm launches), from one ncu capture of every GEMM launch of a 65,536-row update
+# (profiles/tc_gemm_dram_c5p.md: 11,464 MB over the 17 launches of one minibatch), scaled x4 to the
+# 262,144-row minibatch of configs[4] (every one of these launches moves bytes in proportion to rows).
+C5_GEMM_DRAM_BYTES_PER_LAUNCH = 4 * 11464e6 / 17
+
+
+def c5_gemm_algorithmic_bytes_per_launch(Nmb, D, H, L, A):
+    """Bytes each launch of one minibatch must move at least (bf16 activations read once, outputs written
+    once, weights read once), averaged over the 3L + 2 launches of the roofline kernel set."""
+    Op = 128 if A + 1 > 64 else 64
+    act = Nmb * H * 2
+    fwd = (Nmb * D * 2 + 2 * act) + (L - 1) * (act + 2 * act) + (act + Nmb * Op * 2)
+    dgrad = (L - 1) * 3 * act + (Nmb * Op * 2 + act + act)
+    wgrad = (Nmb * D * 2 + act) + (L - 1) * 2 * act + (Nmb * Op * 2 + act)
+    return (fwd + dgrad + wgrad) / (3 * L + 2)
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -264,7 +282,11 @@ def run_ours(args, wl, rank, world, local_rank):
                    "l2": "no flush: the obs column alone (fp32 %.1f GB) exceeds L2" % (NT * D * 4 / 1e9),
                    "parallelism": f"dp{world}"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
-                     "frac": achieved / peak_tf if peak_tf else None, "traffic": None,
+                     "frac": achieved / peak_tf if peak_tf else None,
+                     "traffic": C5_GEMM_DRAM_BYTES_PER_LAUNCH if wl is WORKLOADS["c5"] else None,
+                     "traffic_algorithmic": c5_gemm_algorithmic_bytes_per_launch(Nmb, D, H, Lh, A),
+                     "traffic_source": "ncu dram__bytes_read+write of every GEMM launch of a 65,536-row update, x4 "
+                                       "to 262,144 rows (profiles/tc_gemm_dram_c5p.md)",
                      "kernel": "tc_gemm_kernel (all forward/PPO-head/dgrad/wgrad launches of the step)",
                      "launches_per_step": gemm_n / args.steps, "peak_kind": peak_kind + " (bf16 sustained)"},
         "newton_schulz": {"tflops": ns_tf, "frac": ns_tf / peak_tf if peak_tf else None,

@@ -160,7 +160,7 @@ def mingru_timed_sample(D, H, L, A, K, enc_act, T, mb_segs, num_mb, coeffs, nseq
     from oracle import oracle as O
 
     threads = threads or os.cpu_count() or 1
-    nseq = nseq or max(threads, 16)
+    nseq = nseq or 8 * threads
     g = np.random.default_rng(seed)
     params, _ = O.init_mingru(D, H, L, A, 0x51 + seed, K)
     P = params.size
