@@ -521,12 +521,15 @@ def mingru_init_pm(D, H, L, A, K, seed):
 MINGRU_C4 = dict(N=8192, T=64, D=118, H=512, L=1, A=4, mb_segs=512, num_mb=64, lr=0.02)
 
 
-def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None, cpu=False):
+def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None, cpu=False, comm=None, rank=0, world=1):
     """the Breakout-shaped recurrent update, 8192 envs x 64, obs 118 ~U(0,1), 4 actions,
     rewards U(-1,1), dones Bernoulli(.005); encoder 118->512 (+GELU), MinGRU hidden 512 with gate + candidate
     512->1024 (K = 2; K = 3 adds the reference's highway projection), heads 512->4 and 512->1; minibatches of
     32768 rows (512 segments x 64) x 64 per update (16 x 4 epochs), each: device V-trace over all 8192 segments,
-    prioritised sampling, BPTT gradient, value/ratio iterate, clip, Muon. samples/s = N*T / update time."""
+    prioritised sampling, BPTT gradient, value/ratio iterate, clip, Muon. samples/s = N*T / update time.
+    With world > 1 every rank holds its own 8192-env rollout (weak scaling) and the ranks all-reduce the
+    advantage statistics and the gradient of every minibatch (pl_mg_set_comm); the time is the max over
+    ranks and the value world * N*T / time."""
     import torch
 
     import pufferlean_b200 as plb
@@ -535,7 +538,7 @@ def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None, cpu=False):
     N, T, D, H, L_, A = c["N"], c["T"], c["D"], c["H"], c["L"], c["A"]
     NT = N * T
     L = plb.lib()
-    gen = torch.Generator(device="cuda").manual_seed(4)
+    gen = torch.Generator(device="cuda").manual_seed(4 + 1000 * rank)
     obs = torch.rand(NT * D, device="cuda", generator=gen)
     rew = torch.rand(NT, device="cuda", generator=gen, dtype=torch.float64) * 2 - 1
     term = (torch.rand(NT, device="cuda", generator=gen) < 0.005).double()
@@ -552,6 +555,8 @@ def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None, cpu=False):
                      eps=1e-12, vfCoef=0.5, entCoef=0.01, clipEps=0.2, vfClip=0.2, maxGradNorm=1.5,
                      ns_coeffs=co.ctypes.data_as(C.POINTER(C.c_double)), ns_iters=5, bf16=1)
     s = plb.MgSession(N, T)
+    if world > 1:
+        s.set_comm(comm, rank, world)
     st = torch.cuda.current_stream().cuda_stream
     check(L.pl_mg_set_obs_dev(s.h, obs.data_ptr(), D), L)
     rng = [0x5EED]
@@ -569,6 +574,9 @@ def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None, cpu=False):
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
     l0 = L.pl_kernel_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -577,6 +585,10 @@ def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None, cpu=False):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
     launches = (L.pl_kernel_launch_count() - l0) / steps
     pm_out = plb.policy_download(handle, P)
     plb.policy_free(handle)
@@ -605,7 +617,9 @@ def measure_mingru_c4(args, K=2, enc_act=1, steps=None, warmup=None, cpu=False):
                       f"{'gate+candidate 512->1024 (K=2)' if K == 2 else 'hid|gate|proj 512->1536 (K=3, reference)'}"
                       f"{', GELU encoder' if enc_act else ''}, 4 actions, 64 minibatches of 512 segments x 64",
             "K": K, "enc_act": "gelu" if enc_act else "none", "params": P,
-            "value": NT / (ms / 1e3), "unit": "samples/s", "ms_per_update": ms, "gpu_launches_per_update": launches,
+            "n_gpus": world, "scaling": "weak",
+            "value": world * NT / (ms / 1e3), "unit": "samples/s", "ms_per_update": ms,
+            "gpu_launches_per_update": launches,
             "gemm_tflops_over_update": flops / (ms / 1e3) / 1e12, "ns_flops_per_update": ns_fl,
             "finite": bool(np.isfinite(pm_out).all()), "data": "synthetic (seeded torch generator 4)"}
 
@@ -800,13 +814,19 @@ def main():
     import pufferlean_b200 as plb
 
     plb.policy_free(state["handle"])
+    if world > 1 and not args.no_extra:
+        # configs[3] on every rank (its data-parallel form), before the communicator goes away
+        c4 = measure_mingru_c4(args, comm=state["comm"], rank=rank, world=world)
+        if rank == 0:
+            out["c4_mingru"] = c4
     if state.get("comm"):
         plb.lib().pl_comm_destroy.argtypes = [C.c_void_p]
         plb.lib().pl_comm_destroy(state["comm"])
     if rank == 0 and not args.no_extra:
         out["c2_vtrace"] = measure_vtrace_c2()
         out["c3_newton_schulz"] = measure_ns_c3()
-        out["c4_mingru"] = measure_mingru_c4(args, cpu=not args.no_cpu)
+        if world == 1:
+            out["c4_mingru"] = measure_mingru_c4(args, cpu=not args.no_cpu)
     if rank == 0:
         if not args.no_cpu and world == 1:
             out["cpu_baseline"] = cpu_baseline(wl)

@@ -279,6 +279,12 @@ int pl_mg_set_columns(pl_mg* s, const double* rew, const double* term, const dou
                       const double* val, const double* boot);
 int pl_mg_set_columns_dev(pl_mg* s, const double* rew, const double* term, const double* act, const double* logp,
                           const double* val, const double* boot, void* stream);
+/* Data parallelism (no reference counterpart; the reference trainer is single-GPU): one process and
+ * session per GPU, each with its own rollout columns (weak scaling). With world > 1, pl_mg_grad
+ * all-reduces the advantage sums (the normalisation uses the all-rank minibatch) and the summed
+ * gradient over `comm` (from pl_comm_create); pl_mg_update scales by the all-rank row count; every
+ * rank then takes the identical Muon step. */
+int pl_mg_set_comm(pl_mg* s, void* comm, int rank, int world);
 /* The obs trajectory [(e*T + t)*D + j]: host f64 (copied to the device as fp32), or a device fp32
  * buffer the caller owns and keeps alive (the rollout's resident trajectory, g_dMGObsTraj in the
  * reference, ffi/puffercuda.cu:2130-2150). */

@@ -96,6 +96,7 @@ def _bind_optional(L):
         "pl_mg_update": ([_vp, C.POINTER(MgNet), _sz, C.POINTER(MgHyper), _sz, _sz, C.POINTER(C.c_uint64), _d, _vp],
                          C.c_int),
         "pl_mg_last_launches": ([_vp], C.c_uint64),
+        "pl_mg_set_comm": ([_vp, _vp, C.c_int, C.c_int], C.c_int),
     }
     for name, (args, res) in specs.items():
         if hasattr(L, name):
@@ -297,6 +298,9 @@ class MgSession:
     def set_columns(self, rew, term, act, logp, val, boot):
         arrs = [_f64(a) for a in (rew, term, act, logp, val, boot)]
         _check(lib().pl_mg_set_columns(self.h, *[_p(a) for a in arrs]), "pl_mg_set_columns")
+
+    def set_comm(self, comm, rank, world):
+        _check(lib().pl_mg_set_comm(self.h, comm, rank, world), "pl_mg_set_comm")
 
     def set_obs(self, obs, D):
         obs = _f64(obs)

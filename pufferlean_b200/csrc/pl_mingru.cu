@@ -26,6 +26,7 @@
 #include <vector>
 
 #include "../../include/pufferlean_b200.h"
+#include "pl_comm.h"
 #include "pl_common.cuh"
 #include "pl_gemm.cuh"
 #include "pl_mlp.cuh"
@@ -95,9 +96,11 @@ __global__ void mg_obs_rows_kernel(const double* __restrict__ src, long R, int D
 // its partial, the last block to finish folds the partials in block order (the counter makes the
 // finish order irrelevant) and resets the counter. ms = [mean, std + 1e-8].
 constexpr int kAdvBlocks = 64;
+// With raw != 0 (data parallel), the last block stores the plain total in ms[2 + sq] for an
+// all-reduce over ranks, and mg_adv_final_kernel divides by the all-rank count.
 __global__ void __launch_bounds__(256) mg_adv_ms_kernel(const double* __restrict__ adv,
                                                         const double* __restrict__ seg, int Bmb, int T, int sq,
-                                                        double* ms, double* part, unsigned* counter) {
+                                                        double* ms, double* part, unsigned* counter, int raw) {
   __shared__ double sh[256];
   __shared__ bool last;
   const long n = (long)Bmb * T;
@@ -126,11 +129,21 @@ __global__ void __launch_bounds__(256) mg_adv_ms_kernel(const double* __restrict
     double tot = 0.0;
     for (int i = 0; i < (int)gridDim.x; i++) tot += ((volatile double*)part)[i];
     const double d = (double)(n > 0 ? n : 1);
-    if (sq)
+    if (raw)
+      ms[2 + sq] = tot;
+    else if (sq)
       ms[1] = sqrt(tot / d) + 1e-8;
     else
       ms[0] = tot / d;
     *counter = 0;
+  }
+}
+__global__ void mg_adv_final_kernel(double* ms, double n, int sq) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    if (sq)
+      ms[1] = sqrt(ms[3] / n) + 1e-8;
+    else
+      ms[0] = ms[2] / n;
   }
 }
 // Per-row minibatch scalars from the resident columns (the layout of the host gather,
@@ -805,6 +818,9 @@ struct pl_mg {
   uint64_t gnodes = 0;
   unsigned long long* rng_dev = nullptr;
   bool have_work = false;
+  // data parallelism: an ncclComm_t from pl_comm_create, this rank and the world size
+  void* comm = nullptr;
+  int rank = 0, world = 1;
   size_t shadow_src = 0;  // handle whose weights the shadows hold (0 = none / host params)
   bool grad_fresh = false;
   long grad_rows = 0;
@@ -1538,6 +1554,17 @@ int pl_mg_set_columns_dev(pl_mg* s, const double* rew, const double* term, const
   return mg_set_columns_impl(s, rew, term, act, logp, val, boot, cudaMemcpyDeviceToDevice, (cudaStream_t)stream);
 }
 
+int pl_mg_set_comm(pl_mg* s, void* comm, int rank, int world) {
+  using namespace pl;
+  PL_REQUIRE(s != nullptr && world >= 1 && rank >= 0 && rank < world, PL_ERR_INVALID,
+             "pl_mg_set_comm: bad rank %d / world %d", rank, world);
+  PL_REQUIRE(world == 1 || comm != nullptr, PL_ERR_INVALID, "pl_mg_set_comm: world %d needs a communicator", world);
+  s->comm = world > 1 ? comm : nullptr;
+  s->rank = rank;
+  s->world = world;
+  return PL_OK;
+}
+
 int pl_mg_set_obs(pl_mg* s, const double* obs, size_t D) {
   using namespace pl;
   PL_REQUIRE(s && obs && D > 0, PL_ERR_INVALID, "pl_mg_set_obs: bad argument");
@@ -1653,9 +1680,24 @@ int pl_mg_grad(pl_mg* s, const pl_mg_net* net, size_t handle, const double* para
   if (rc) return rc;
   // gather
   const int Bi = (int)Bmb, T = (int)s->T;
-  mg_adv_ms_kernel<<<kAdvBlocks, 256, 0, st>>>(s->adv, s->seg, Bi, T, 0, w.ms, w.adv_part, w.adv_counter);
-  mg_adv_ms_kernel<<<kAdvBlocks, 256, 0, st>>>(s->adv, s->seg, Bi, T, 1, w.ms, w.adv_part, w.adv_counter);
-  count_launch();
+  if (s->world > 1) {
+    // the advantage statistics are those of the all-rank minibatch
+    const double nall = (double)w.R * s->world;
+    for (int sq = 0; sq < 2; sq++) {
+      mg_adv_ms_kernel<<<kAdvBlocks, 256, 0, st>>>(s->adv, s->seg, Bi, T, sq, w.ms, w.adv_part, w.adv_counter, 1);
+      count_launch();
+      PL_LAUNCH("mg_adv_ms_kernel");
+      rc = comm_allreduce_f64(s->comm, w.ms + 2 + sq, 1, st);
+      if (rc) return rc;
+      mg_adv_final_kernel<<<1, 32, 0, st>>>(w.ms, nall, sq);
+      count_launch();
+      PL_LAUNCH("mg_adv_final_kernel");
+    }
+  } else {
+    mg_adv_ms_kernel<<<kAdvBlocks, 256, 0, st>>>(s->adv, s->seg, Bi, T, 0, w.ms, w.adv_part, w.adv_counter, 0);
+    mg_adv_ms_kernel<<<kAdvBlocks, 256, 0, st>>>(s->adv, s->seg, Bi, T, 1, w.ms, w.adv_part, w.adv_counter, 0);
+    count_launch();
+  }
   mg_gather_scal_kernel<<<blocks_for(w.R), 256, 0, st>>>(s->act, s->logp, s->term, s->adv, s->value, s->seg, s->mbp,
                                                          w.ms, Bi, T, w.act_i, w.adv_f, w.ret_f, w.olp_f, w.ov_f,
                                                          w.term_f);
@@ -1670,6 +1712,11 @@ int pl_mg_grad(pl_mg* s, const pl_mg_net* net, size_t handle, const double* para
   const bool losses = loss_channel_on();
   rc = run_bptt(s, vfCoef, entCoef, clipEps, vfClip, losses, st);
   if (rc) return rc;
+  // data parallel: the summed gradient of the all-rank minibatch on every rank
+  if (s->world > 1) {
+    rc = comm_allreduce_f32(s->comm, w.grad, (size_t)sh.P(), st);
+    if (rc) return rc;
+  }
   // replay iterate
   PL_CUDA(cudaMemsetAsync(s->lastw, 0xFF, sizeof(int) * s->N, st));
   mg_lastw_kernel<<<(unsigned)((Bi + 255) / 256), 256, 0, st>>>(s->lastw, s->seg, Bi);
@@ -1751,7 +1798,7 @@ int pl_mg_read_state(pl_mg* s, double* value, double* ratio, double* adv) {
 
 static int mg_minibatch(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hyper* h, size_t mbSegs,
                         uint64_t rng, bool rng_on_device, double lr, cudaStream_t st) {
-  const double gscale = 1.0 / (double)(mbSegs * (size_t)s->T);
+  const double gscale = 1.0 / ((double)mbSegs * (double)s->T * (double)s->world);
   int rc = mg_vtrace_prio_impl(s, h->gamma, h->lam, h->rhoClip, h->cClip, mbSegs, h->prioAlpha, h->annealBeta, rng,
                                rng_on_device, st);
   if (rc) return rc;
@@ -1835,7 +1882,7 @@ int pl_mg_update(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hype
   PL_REQUIRE(s->cols_valid && s->traj && s->trajD == (long)net->D, PL_ERR_INVALID,
              "pl_mg_update: set the columns and the obs trajectory first");
   const uint64_t l0 = pl_kernel_launch_count();
-  if (h->bf16 && !loss_channel_on() && numMB > 1) {
+  if (h->bf16 && !loss_channel_on() && numMB > 1 && s->world == 1) {
     rc = mg_update_graph(s, net, handle, h, numMB, mbSegs, rng, lr, (cudaStream_t)stream);
     s->launches = pl_kernel_launch_count() - l0;
     return rc;

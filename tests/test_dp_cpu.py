@@ -105,3 +105,78 @@ def test_data_parallel_decomposition_equals_full_minibatch_gloo():
         assert p.exitcode == 0
     assert err < 1e-10 * max(1.0, scale)
     assert plans[0] == plans[1]
+
+
+# ---------------------------------------------------------------------------------------- MinGRU
+def _mg_rank(rank, world, port, q):
+    """One rank of the MinGRU decomposition on the oracle: its own rollout and sample, the advantage
+    sum and squared-deviation sum all-reduced (two passes, as pl_mg_grad does), its own sequences'
+    summed gradient all-reduced."""
+    from oracle import oracle as O
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        N, T, D, H, L, A = 8, 5, 4, 8, 1, 3
+        g = np.random.default_rng(90 + rank)
+        adv = g.standard_normal(N * T)
+        val, logp = g.standard_normal(N * T), g.uniform(-2, -0.5, N * T)
+        act, term = g.integers(0, A, N * T).astype(float), (g.random(N * T) < 0.2) * 1.0
+        obs = g.uniform(0, 1, N * T * D)
+        seg = np.array([1.0, 6.0, 1.0]) if rank == 0 else np.array([0.0, 3.0, 7.0])
+        mbp = np.array([1.0, 0.5, 1.5]) if rank == 0 else np.array([0.9, 1.1, 1.2])
+        params, _ = O.init_mingru(D, H, L, A, 0x5151)
+        Bmb = seg.size
+        a_s = np.array([adv[int(e) * T + t] for e in seg for t in range(T)])
+        tot = torch.tensor([a_s.sum()], dtype=torch.float64)
+        dist.all_reduce(tot)
+        mean = float(tot[0]) / (Bmb * T * world)
+        sq = torch.tensor([((a_s - mean) ** 2).sum()], dtype=torch.float64)
+        dist.all_reduce(sq)
+        std = np.sqrt(float(sq[0]) / (Bmb * T * world))
+        sc = O.gather_seq_minibatch(act, logp, term, adv, val, seg, mbp, T, Bmb)
+        nb = T * Bmb
+        for b in range(Bmb):  # re-normalise the advantage rows with the all-rank statistics
+            e = int(seg[b])
+            for t in range(T):
+                sc[nb + t * Bmb + b] = mbp[b] * (adv[e * T + t] - mean) / (std + 1e-8)
+        obsTB = np.zeros(nb * D)
+        for t in range(T):
+            for b in range(Bmb):
+                e = int(seg[b])
+                obsTB[(t * Bmb + b) * D:(t * Bmb + b + 1) * D] = obs[(e * T + t) * D:(e * T + t + 1) * D]
+        P = params.size
+        gr = torch.tensor(O.mingru_grad_batch(params, obsTB, sc, Bmb, T, H, D, L, A)[:P])
+        dist.all_reduce(gr)
+        parts = [None] * world
+        dist.all_gather_object(parts, (adv, val, logp, act, term, obs, seg, mbp))
+        if rank == 0:
+            # single process: both rollouts side by side, rank 1's segments offset by N
+            cat = [np.concatenate([p[i] for p in parts]) for i in range(6)]
+            segu = np.concatenate([parts[0][6], parts[1][6] + N])
+            mbpu = np.concatenate([parts[0][7], parts[1][7]])
+            Bu = segu.size
+            scu = O.gather_seq_minibatch(cat[3], cat[2], cat[4], cat[0], cat[1], segu, mbpu, T, Bu)
+            obsu = np.zeros(T * Bu * D)
+            for t in range(T):
+                for b in range(Bu):
+                    e = int(segu[b])
+                    obsu[(t * Bu + b) * D:(t * Bu + b + 1) * D] = cat[5][(e * T + t) * D:(e * T + t + 1) * D]
+            ref = O.mingru_grad_batch(params, obsu, scu, Bu, T, H, D, L, A)[:P]
+            q.put(float(np.max(np.abs(gr.numpy() - ref) / (np.abs(ref) + 1e-9))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_mingru_dp_decomposition_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29900 + os.getpid() % 300
+    procs = [ctx.Process(target=_mg_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    rel = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert rel < 1e-9, rel

@@ -1,0 +1,116 @@
+"""MinGRU data parallelism on 2 GPUs (skipped with fewer): one process and session per GPU, each with
+its own rollout columns, the library's own NCCL communicator. Two ranks that each sample their own
+segments must take the same step as one GPU holding both rollouts and sampling the union (rank 1's
+segments offset by rank 0's count): the advantage statistics and the gradient are the all-rank
+minibatch's, and both ranks end with bit-identical weights."""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+N, T, D, H, L, A = 10, 6, 5, 16, 2, 3
+SEG = {0: [2.0, 7.0, 2.0, 4.0], 1: [0.0, 9.0, 5.0, 3.0]}
+MBP = {0: [1.0, 0.8, 1.2, 0.9], 1: [1.1, 0.7, 1.0, 1.3]}
+
+
+def rollout(rank):
+    g = np.random.default_rng(40 + rank)
+    NT = N * T
+    return dict(obs=g.uniform(0, 1, NT * D), rew=g.uniform(-1, 1, NT), term=(g.random(NT) < 0.15) * 1.0,
+                act=g.integers(0, A, NT).astype(float), logp=g.uniform(-2, -0.5, NT), val=g.uniform(-1, 1, NT),
+                boot=g.uniform(-1, 1, N))
+
+
+def init_pm():
+    from oracle import oracle as O
+
+    p, _ = O.init_mingru(D, H, L, A, 0x77AB)
+    return p.size, np.concatenate([p, np.zeros(p.size)])
+
+
+def step(plb, s, net, handle, seg, mbp, world, bf16):
+    s.vtrace(0.995, 0.90, 1.0, 1.0)
+    s.grad(net, handle=handle, seg=np.array(seg), mbp=np.array(mbp), Bmb=len(seg), bf16=bf16)
+    s.muon(net, handle, 0.02, 0.0, 0.95, 1e-7, 1.5, 1.0 / (len(seg) * T * world), bf16=bf16)
+
+
+def _rank(rank, port, bf16, q):
+    import torch.distributed as dist
+
+    import pufferlean_b200 as plb
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    L_ = plb.lib()
+    L_.pl_set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        ident = (C.c_uint8 * 128)()
+        if rank == 0:
+            assert L_.pl_comm_unique_id(ident) == 0
+        box = [bytes(ident)]
+        dist.broadcast_object_list(box, src=0)
+        ident = (C.c_uint8 * 128)(*box[0])
+        comm = C.c_void_p()
+        L_.pl_comm_create.argtypes = [C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]
+        assert L_.pl_comm_create(rank, WORLD, ident, C.byref(comm)) == 0, L_.pl_last_error()
+        P, pm = init_pm()
+        net = plb.mg_net(D, H, L, A)
+        r = rollout(rank)
+        s = plb.MgSession(N, T)
+        s.set_columns(r["rew"], r["term"], r["act"], r["logp"], r["val"], r["boot"])
+        s.set_obs(r["obs"], D)
+        s.set_comm(comm, rank, WORLD)
+        h = plb.policy_load(pm, P)
+        step(plb, s, net, h, SEG[rank], MBP[rank], WORLD, bf16)
+        out = plb.policy_download(h, P)
+        plb.policy_free(h)
+        s.close()
+        outs = [None] * WORLD
+        dist.all_gather_object(outs, out.tobytes())
+        if rank == 0:
+            r0, r1 = rollout(0), rollout(1)
+            u = {k: np.concatenate([r0[k], r1[k]]) for k in r0}
+            su = plb.MgSession(2 * N, T)
+            su.set_columns(u["rew"], u["term"], u["act"], u["logp"], u["val"], u["boot"])
+            su.set_obs(u["obs"], D)
+            hu = plb.policy_load(pm, P)
+            step(plb, su, net, hu, SEG[0] + [x + N for x in SEG[1]], MBP[0] + MBP[1], 1, bf16)
+            ref = plb.policy_download(hu, P)
+            plb.policy_free(hu)
+            su.close()
+            a = np.frombuffer(outs[0]), np.frombuffer(outs[1])
+            q.put((bool(np.array_equal(a[0], a[1])),
+                   float(np.linalg.norm(a[0][:P] - ref[:P]) / np.linalg.norm(ref[:P] - pm[:P]))))
+        L_.pl_comm_destroy.argtypes = [C.c_void_p]
+        L_.pl_comm_destroy(comm)
+    finally:
+        dist.destroy_process_group()
+
+
+# fp32 tier: gradients summed in another order (per rank, then all-reduced) -> 1e-4 on the step;
+# bf16 tier: those last-bit differences flip bf16 roundings inside Newton-Schulz -> 0.15
+@pytest.mark.parametrize("bf16,tol", [(0, 1e-4), (1, 0.15)])
+def test_two_rank_mingru_step_equals_union(bf16, tol):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + os.getpid() % 500 + bf16
+    procs = [ctx.Process(target=_rank, args=(r, port, bf16, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    same, rel = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert same, "ranks disagree"
+    assert rel < tol, rel
