@@ -332,6 +332,20 @@ int pl_mg_update(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hype
 uint64_t pl_mg_last_launches(const pl_mg* s);
 int pl_mg_destroy(pl_mg* s);
 
+/* ------------------------------------------------------------------ checkpoints --------------- */
+/* The reference's checkpoint file (Puffer/RL/FFITrain.lean:55-90, ckptToBytes / bytesToCkpt): a
+ * little-endian u64 parameter count P, then the P weights as little-endian IEEE f64 — byte-compatible,
+ * so runs resume across implementations. Host only: pl_ckpt_write writes w[0..P) to path;
+ * pl_ckpt_read reads at most cap weights into w and sets *P to the count it holds, bounded by the file
+ * size as the reference's parser is (a truncated file yields the doubles it contains). */
+int pl_ckpt_write(const char* path, const double* w, size_t P);
+int pl_ckpt_read(const char* path, double* w, size_t cap, size_t* P);
+/* The same through a policy handle: save writes the handle's first P values (the weights); restore
+ * creates a handle holding the file's weights and zero momentum (the reference re-zeros it on load,
+ * Puffer/RL/MinGRUTrain.lean:684-700). */
+int pl_policy_save(size_t handle, size_t P, const char* path);
+int pl_policy_restore(const char* path, size_t* P, size_t* handle);
+
 /* ------------------------------------------------------------------ dashboard losses ----------- */
 /* The reference's 7-loss channel [policy, value, entropy, total, old_kl, kl, clipfrac]
  * (ffi/puffercuda.cu:251-262, 336-352). */

@@ -97,6 +97,10 @@ def _bind_optional(L):
                          C.c_int),
         "pl_mg_last_launches": ([_vp], C.c_uint64),
         "pl_mg_set_comm": ([_vp, _vp, C.c_int, C.c_int], C.c_int),
+        "pl_ckpt_write": ([C.c_char_p, _dp, _sz], C.c_int),
+        "pl_ckpt_read": ([C.c_char_p, _dp, _sz, C.POINTER(_sz)], C.c_int),
+        "pl_policy_save": ([_sz, _sz, C.c_char_p], C.c_int),
+        "pl_policy_restore": ([C.c_char_p, C.POINTER(_sz), C.POINTER(_sz)], C.c_int),
     }
     for name, (args, res) in specs.items():
         if hasattr(L, name):
@@ -350,3 +354,29 @@ class MgSession:
 
     def last_launches(self):
         return int(lib().pl_mg_last_launches(self.h))
+
+
+# ------------------------------------------------------------------------------------------- checkpoints
+def ckpt_write(path, w):
+    """The reference's `<step>.bin` layout (Puffer/RL/FFITrain.lean:55-62): u64 P, then P f64, little-endian."""
+    w = _f64(w)
+    _check(lib().pl_ckpt_write(os.fsencode(path), _p(w), w.size), "pl_ckpt_write")
+
+
+def ckpt_read(path):
+    n = _sz(0)
+    _check(lib().pl_ckpt_read(os.fsencode(path), None, 0, C.byref(n)), "pl_ckpt_read")
+    w = np.zeros(n.value)
+    _check(lib().pl_ckpt_read(os.fsencode(path), _p(w), w.size, C.byref(n)), "pl_ckpt_read")
+    return w
+
+
+def policy_save(handle, P, path):
+    _check(lib().pl_policy_save(handle, P, os.fsencode(path)), "pl_policy_save")
+
+
+def policy_restore(path):
+    """(handle, P): a policy handle with the file's weights and zero momentum."""
+    P, h = _sz(0), _sz(0)
+    _check(lib().pl_policy_restore(os.fsencode(path), C.byref(P), C.byref(h)), "pl_policy_restore")
+    return h.value, P.value

@@ -3,6 +3,7 @@
 // reference's update path as well (ffi/pufferffi.c:946-1041, 1094-1176); they are restated here so the
 // library is a drop-in for the whole call sequence of one update.
 #include <math.h>
+#include <stdio.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -165,6 +166,93 @@ int pl_gather_seq_minibatch(const double* actCol, const double* logpCol, const d
     }
   }
   return PL_OK;
+}
+
+// Checkpoint file: u64 P (little-endian) then P f64 bit patterns (little-endian); written byte by
+// byte so the layout does not depend on the host's endianness.
+static void put_u64le(unsigned char* b, uint64_t v) {
+  for (int i = 0; i < 8; i++) b[i] = (unsigned char)(v >> (8 * i));
+}
+static uint64_t get_u64le(const unsigned char* b) {
+  uint64_t v = 0;
+  for (int i = 0; i < 8; i++) v |= (uint64_t)b[i] << (8 * i);
+  return v;
+}
+
+int pl_ckpt_write(const char* path, const double* w, size_t P) {
+  if (!path || (!w && P)) return PL_ERR_INVALID;
+  FILE* f = fopen(path, "wb");
+  if (!f) return PL_ERR_INVALID;
+  unsigned char b[8];
+  put_u64le(b, (uint64_t)P);
+  int ok = fwrite(b, 1, 8, f) == 8;
+  for (size_t i = 0; ok && i < P; i++) {
+    uint64_t bits;
+    memcpy(&bits, &w[i], 8);
+    put_u64le(b, bits);
+    ok = fwrite(b, 1, 8, f) == 8;
+  }
+  ok = (fclose(f) == 0) && ok;
+  return ok ? PL_OK : PL_ERR_INVALID;
+}
+
+int pl_ckpt_read(const char* path, double* w, size_t cap, size_t* P) {
+  if (!path || !P) return PL_ERR_INVALID;
+  FILE* f = fopen(path, "rb");
+  if (!f) return PL_ERR_INVALID;
+  fseek(f, 0, SEEK_END);
+  const long size = ftell(f);
+  fseek(f, 0, SEEK_SET);
+  unsigned char b[8];
+  if (size < 8 || fread(b, 1, 8, f) != 8) {
+    fclose(f);
+    *P = 0;
+    return size < 8 ? PL_OK : PL_ERR_INVALID;
+  }
+  const uint64_t hdr = get_u64le(b);
+  const uint64_t avail = (uint64_t)(size - 8) / 8;
+  const size_t n = (size_t)(hdr < avail ? hdr : avail);
+  *P = n;
+  if (!w) {
+    fclose(f);
+    return PL_OK;  // size query
+  }
+  if (n > cap) {
+    fclose(f);
+    return PL_ERR_INVALID;
+  }
+  int ok = 1;
+  for (size_t i = 0; ok && i < n; i++) {
+    ok = fread(b, 1, 8, f) == 8;
+    const uint64_t bits = get_u64le(b);
+    memcpy(&w[i], &bits, 8);
+  }
+  fclose(f);
+  return ok ? PL_OK : PL_ERR_INVALID;
+}
+
+int pl_policy_save(size_t handle, size_t P, const char* path) {
+  if (!handle || !path) return PL_ERR_INVALID;
+  double* w = (double*)malloc(sizeof(double) * 2 * (P ? P : 1));
+  if (!w) return PL_ERR_NOMEM;
+  int rc = pl_policy_download(handle, P, w);  // [params; mom]
+  if (!rc) rc = pl_ckpt_write(path, w, P);
+  free(w);
+  return rc;
+}
+
+int pl_policy_restore(const char* path, size_t* P, size_t* handle) {
+  if (!path || !P || !handle) return PL_ERR_INVALID;
+  size_t n = 0;
+  int rc = pl_ckpt_read(path, nullptr, 0, &n);
+  if (rc) return rc;
+  double* pm = (double*)calloc(2 * (n ? n : 1), sizeof(double));
+  if (!pm) return PL_ERR_NOMEM;
+  rc = pl_ckpt_read(path, pm, n, &n);
+  if (!rc) rc = pl_policy_load(pm, n, handle);
+  free(pm);
+  if (!rc) *P = n;
+  return rc;
 }
 
 }  // extern "C"

@@ -97,6 +97,30 @@ def test_mingru_param_count_and_no_device():
                                  0.5, 0.01, 0.2, 0.2)
 
 
+def test_checkpoint_bytes_match_the_reference_layout(tmp_path):
+    """ckptToBytes (Puffer/RL/FFITrain.lean:55-62): u64 P then P f64 bit patterns, little-endian; the
+    parser is bounded by the file size (bytesToCkpt, :66-69)."""
+    import struct
+
+    g = np.random.default_rng(4)
+    w = np.concatenate([g.standard_normal(37), [0.0, -0.0, np.inf, 1e-310]])
+    path = tmp_path / "123.bin"
+    plb.ckpt_write(str(path), w)
+    raw = path.read_bytes()
+    assert raw == struct.pack("<Q", w.size) + w.astype("<f8").tobytes()
+    back = plb.ckpt_read(str(path))
+    assert back.tobytes() == w.tobytes()
+    # a truncated file yields the doubles it holds; a header claiming fewer yields that many
+    path.write_bytes(raw[:8 + 8 * 5 + 3])
+    assert np.array_equal(plb.ckpt_read(str(path)), w[:5])
+    path.write_bytes(struct.pack("<Q", 2) + w.astype("<f8").tobytes())
+    assert np.array_equal(plb.ckpt_read(str(path)), w[:2])
+    path.write_bytes(b"\x01\x02")
+    assert plb.ckpt_read(str(path)).size == 0
+    with pytest.raises(plb.PufferError):
+        plb.ckpt_read(str(tmp_path / "missing.bin"))
+
+
 # ---------------------------------------------------------------- Lean adapter (libpufferlean_lean.so)
 LEAN_LIB = os.path.join(os.path.dirname(plb.LIB_PATH), "libpufferlean_lean.so")
 

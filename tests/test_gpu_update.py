@@ -213,3 +213,24 @@ def test_batched_newton_schulz(batch, rows, cols):
     for b in range(batch):
         ref = O.newton_schulz(Xin[b].ravel(), rows, cols, 1e-7, co).reshape(rows, cols)
         assert rel(got[b], ref) < 2e-2, (b, rel(got[b], ref))
+
+
+def test_policy_checkpoint_round_trip(tmp_path):
+    """Save a trained handle's weights in the reference's .bin layout and restore them into a new
+    handle: the weights come back bit for bit, the momentum as zeros (the reference re-zeros it)."""
+    g = np.random.default_rng(21)
+    P = 777
+    pm = g.standard_normal(2 * P)
+    h = plb.policy_load(pm, P)
+    path = tmp_path / "4096.bin"
+    try:
+        plb.policy_save(h, P, str(path))
+    finally:
+        plb.policy_free(h)
+    assert np.array_equal(plb.ckpt_read(str(path)), pm[:P])
+    h2, P2 = plb.policy_restore(str(path))
+    try:
+        out = plb.policy_download(h2, P2)
+    finally:
+        plb.policy_free(h2)
+    assert P2 == P and out[:P].tobytes() == pm[:P].tobytes() and not out[P:].any()
