@@ -332,6 +332,35 @@ int pl_mg_update(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hype
 uint64_t pl_mg_last_launches(const pl_mg* s);
 int pl_mg_destroy(pl_mg* s);
 
+/* ------------------------------------------------------------------ wide action heads --------- */
+/* The resident update of the multi-discrete and continuous plugin trainers (one hidden ReLU layer, O
+ * outputs): mode 1 = W categorical heads of sizes head_sizes[0..W) (O = sum + 1; joint log-prob, one
+ * clip on the joint ratio), mode 2 = W Gaussian dims (O = 2W + 1: means, raw log-stds clamped to
+ * [-20, 2], value). acts is NT x W row-major. Replaces lean_cuda_train_update_wide_resident
+ * (ffi/puffercuda.cu:1307-1409; heads k_ppo_dout_md :706-727 and k_ppo_dout_cont :1767-1790). */
+int pl_train_update_wide_resident(size_t handle, const double* obs, const double* acts, const double* adv,
+                                  const double* ret, const double* olp, const double* oldVal, size_t oldValN,
+                                  const double* perm, const double* head_sizes, size_t NT, size_t D, size_t H,
+                                  size_t O, size_t W, uint32_t mode, size_t epochs, size_t numMB, double lr, double wd,
+                                  double mu, double eps, double vfCoef, double entCoef, double clipEps, double vfClip,
+                                  double maxGradNorm, uint8_t bf16, double* params0_out);
+/* The summed objective gradient of those heads over N rows (no advantage normalisation), as the
+ * verify modes check it (the Gaussian form is the reference's lean_ffi_gauss_ppo_grad_batch_vclip,
+ * ffi/pufferffi.c:311-360, on the device; oldVal NULL = unclipped value loss). */
+int pl_mlp_ppo_grad_wide(const double* params, const double* obs, const double* acts, const double* advs,
+                         const double* rets, const double* oldlps, const double* oldVal, size_t N, size_t H, size_t D,
+                         size_t O, size_t W, uint32_t mode, const double* head_sizes, double vfCoef, double entCoef,
+                         double clipEps, double vfClip, uint8_t bf16, double* g);
+/* In-place Muon step of a resident one-hidden-layer policy [W1|b1|W2|b2] from a raw summed gradient
+ * (host, P values) scaled by gscale; f64, the reference's table. params_out (may be NULL) receives the
+ * new weights. Replaces lean_cuda_muon_step_mlp_resident (ffi/puffercuda.cu:5985-6020). */
+int pl_muon_step_mlp_resident(size_t handle, const double* gRaw, size_t H, size_t D, size_t O, double gscale,
+                              double lr, double wd, double mu, double eps, double* params_out);
+/* Session form: switch a pl_update session to wide heads before pl_update_set_columns (whose acts
+ * column is then NT x W; the _dev form takes it as f64 on the device). mode 0 restores one categorical
+ * head. */
+int pl_update_set_head(pl_update* u, int mode, size_t W, const double* head_sizes);
+
 /* ------------------------------------------------------------------ checkpoints --------------- */
 /* The reference's checkpoint file (Puffer/RL/FFITrain.lean:55-90, ckptToBytes / bytesToCkpt): a
  * little-endian u64 parameter count P, then the P weights as little-endian IEEE f64 — byte-compatible,

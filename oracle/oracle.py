@@ -82,6 +82,10 @@ def orc():
         lib.orc_mingru_update.restype = C.c_uint64
         lib.orc_mingru_update.argtypes = ([_dp] * 8 + [_sz] * 7 + [C.c_int] + [_sz] * 2 + [_d] * 6 + [C.c_uint64]
                                           + [_d] * 9 + [_dp, C.c_int])
+        lib.orc_mlp_ppo_grad_wide.argtypes = ([_dp] * 7 + [_sz] * 5 + [C.c_int, C.POINTER(C.c_int)] + [_d] * 5
+                                              + [_dp] * 3)
+        lib.orc_train_update_wide.argtypes = ([_dp] * 8 + [C.POINTER(C.c_int)] + [_sz] * 5 + [C.c_int] + [_sz] * 2
+                                              + [_d] * 10 + [_dp, C.c_int])
         lib.orc_init_mingru.restype = C.c_uint64
         lib.orc_init_mingru.argtypes = [_sz] * 5 + [C.c_uint64, _dp]
         _ORC = lib
@@ -284,6 +288,37 @@ def mingru_update(pm, obs, rew, term, act, logp, val0, boot, N, T, D, H, L, A, n
                                 lam, rho, c, alpha, beta, C.c_uint64(rng & 0xFFFFFFFFFFFFFFFF), lr, wd, mu, eps, vf,
                                 ent, clip, vfClip, maxGradNorm, _ptr(co), co.shape[0])
     return pm, int(r)
+
+
+# ---------------------------------------------------------------------------------------------
+# Wide action heads (mode 1 multi-discrete, mode 2 Gaussian) of the one-hidden-layer ReLU MLP
+def _hs(hs, W):
+    a = (C.c_int * max(W, 1))(*([int(x) for x in hs] if hs is not None else [0] * W))
+    return a
+
+
+def mlp_ppo_grad_wide(params, obs, acts, advs, rets, olps, N, D, H, O, W, mode, hs=None, ov=None, vf=0.5, ent=0.01,
+                      clip=0.2, vfClip=0.0, lsLo=-20.0):
+    P = H * D + H + O * H + O
+    g, nl, nv = np.zeros(P), np.zeros(N), np.zeros(N)
+    arrs = list(map(f64, (params, obs, acts, advs, rets, olps)))
+    ovp = _ptr(f64(ov)) if ov is not None else None
+    orc().orc_mlp_ppo_grad_wide(*[_ptr(a) for a in arrs], ovp, N, D, H, O, W, mode, _hs(hs, W), vf, ent, clip, vfClip,
+                                lsLo, _ptr(g), _ptr(nl), _ptr(nv))
+    return g, nl, nv
+
+
+def train_update_wide(pm, obs, acts, adv, ret, olp, perm, NT, D, H, O, W, mode, epochs, numMB, hs=None, ov=None,
+                      lr=0.02, wd=0.0, mu=0.95, eps=1e-7, vf=0.5, ent=0.01, clip=0.2, vfClip=0.0, maxGradNorm=0.0,
+                      lsLo=-20.0, coeffs=MUON_COEFFS):
+    pm = f64(pm).copy()
+    arrs = list(map(f64, (obs, acts, adv, ret, olp)))
+    ovp = _ptr(f64(ov)) if ov is not None else None
+    co = f64(coeffs)
+    orc().orc_train_update_wide(_ptr(pm), *[_ptr(a) for a in arrs], ovp, _ptr(f64(perm)), _hs(hs, W), NT, D, H, O, W,
+                                mode, epochs, numMB, lr, wd, mu, eps, vf, ent, clip, vfClip, maxGradNorm, lsLo, _ptr(co),
+                                co.shape[0])
+    return pm
 
 
 # ---------------------------------------------------------------------------------------------

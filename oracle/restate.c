@@ -1048,3 +1048,185 @@ uint64_t orc_init_mingru(size_t D, size_t H, size_t L, size_t A, size_t K, uint6
   p[0] = 0.0;
   return s;
 }
+
+/* ---------------------------------------------------------------- wide action heads --------- */
+/* Summed PPO-objective gradient of the one-hidden-layer ReLU MLP with a wide head (ascent convention):
+ * mode 1 = W categorical heads of sizes hs[0..W) (joint log-prob of log-softmax WITHOUT max subtraction,
+ * one clip on the joint ratio; ffi/puffercuda.cu:706-727, restated in f64), mode 2 = W Gaussian dims
+ * (out = [means | raw log-stds clamped to [lsLo, 2] | value]; ffi/pufferffi.c:311-360 op for op, whose
+ * forward accumulates the dot products from the last index down, gauss_forward :233-237). acts is
+ * N x W. ov == NULL or vfClip <= 0: unclipped value gradient. g[P] is zeroed; newlp/newval may be NULL. */
+void orc_mlp_ppo_grad_wide(const double* params, const double* obs, const double* acts, const double* advs,
+                           const double* rets, const double* olps, const double* ov, size_t N, size_t D, size_t H,
+                           size_t O, size_t W, int mode, const int* hs, double vfCoef, double entCoef, double clipEps,
+                           double vfClip, double lsLo, double* g, double* newlp, double* newval) {
+  const double lsHi = 2.0;
+  const size_t P = H * D + H + O * H + O;
+  const double* W1 = params;
+  const double* b1 = params + H * D;
+  const double* W2 = params + H * D + H;
+  const double* b2 = params + H * D + H + O * H;
+  for (size_t i = 0; i < P; i++) g[i] = 0.0;
+  double* gW1 = g;
+  double* gb1 = g + H * D;
+  double* gW2 = g + H * D + H;
+  double* gb2 = g + H * D + H + O * H;
+  double* z1 = (double*)malloc(sizeof(double) * H);
+  double* h = (double*)malloc(sizeof(double) * H);
+  double* out = (double*)malloc(sizeof(double) * O);
+  double* dout = (double*)malloc(sizeof(double) * O);
+  double* dh = (double*)malloc(sizeof(double) * H);
+  const double halfLog2pi = 0.5 * log(2.0 * 3.14159265358979323846);
+  for (size_t n = 0; n < N; n++) {
+    const double* x = obs + n * D;
+    const double* act = acts + n * W;
+    for (size_t j = 0; j < H; j++) {
+      const double* w = W1 + j * D;
+      double acc = 0.0;
+      for (size_t k = D; k-- > 0;) acc = w[k] * x[k] + acc;
+      double z = b1[j] + acc;
+      z1[j] = z;
+      h[j] = z > 0.0 ? z : 0.0;
+    }
+    for (size_t k = 0; k < O; k++) {
+      const double* w = W2 + k * H;
+      double acc = 0.0;
+      for (size_t j = H; j-- > 0;) acc = w[j] * h[j] + acc;
+      out[k] = b2[k] + acc;
+    }
+    double adv = advs[n], ret = rets[n], oldLogp = olps[n];
+    double logp = 0.0;
+    if (mode == 1) {
+      size_t off = 0;
+      for (size_t hh = 0; hh < W; hh++) {
+        double se = 0.0;
+        for (int k = 0; k < hs[hh]; k++) se += exp(out[off + k]);
+        logp += out[off + (size_t)act[hh]] - log(se);
+        off += hs[hh];
+      }
+    } else {
+      for (size_t i = 0; i < W; i++) {
+        double ls = out[W + i];
+        ls = ls < lsLo ? lsLo : (ls > lsHi ? lsHi : ls);
+        double invStd = exp(-ls);
+        double z = (act[i] - out[i]) * invStd;
+        logp += -0.5 * z * z - ls - halfLog2pi;
+      }
+    }
+    double ratio = exp(logp - oldLogp);
+    double lo = 1.0 - clipEps, hi = 1.0 + clipEps;
+    double ratioC = ratio < lo ? lo : (ratio > hi ? hi : ratio);
+    double surr1 = adv * ratio, surr2 = adv * ratioC;
+    double dPol;
+    if (surr1 <= surr2)
+      dPol = adv * ratio;
+    else {
+      double cg = (lo < ratio && ratio < hi) ? 1.0 : 0.0;
+      dPol = adv * cg * ratio;
+    }
+    if (mode == 1) {
+      size_t off = 0;
+      for (size_t hh = 0; hh < W; hh++) {
+        double se = 0.0;
+        for (int k = 0; k < hs[hh]; k++) se += exp(out[off + k]);
+        double lse = log(se), pout = 0.0;
+        for (int k = 0; k < hs[hh]; k++) pout += exp(out[off + k] - lse) * out[off + k];
+        for (int k = 0; k < hs[hh]; k++) {
+          double p = exp(out[off + k] - lse);
+          dout[off + k] = dPol * (((size_t)k == (size_t)act[hh] ? 1.0 : 0.0) - p) + entCoef * p * (pout - out[off + k]);
+        }
+        off += hs[hh];
+      }
+    } else {
+      for (size_t i = 0; i < W; i++) {
+        double lsr = out[W + i];
+        double ls = lsr < lsLo ? lsLo : (lsr > lsHi ? lsHi : lsr);
+        double lsGrad = (lsLo < lsr && lsr < lsHi) ? 1.0 : 0.0;
+        double invStd = exp(-ls);
+        double z = (act[i] - out[i]) * invStd;
+        dout[i] = dPol * (z * invStd);
+        dout[W + i] = lsGrad * (dPol * (z * z - 1.0) + entCoef);
+      }
+    }
+    double vnew = out[O - 1], dvloss_dv;
+    if (ov && vfClip > 0.0) {
+      double vold = ov[n], dd = vnew - vold;
+      double vclip = vold + (dd < -vfClip ? -vfClip : (dd > vfClip ? vfClip : dd));
+      double du = (vnew - ret) * (vnew - ret), dc = (vclip - ret) * (vclip - ret);
+      if (du >= dc)
+        dvloss_dv = (vnew - ret);
+      else if (dd > -vfClip && dd < vfClip)
+        dvloss_dv = (vnew - ret);
+      else
+        dvloss_dv = 0.0;
+    } else {
+      dvloss_dv = (vnew - ret);
+    }
+    dout[O - 1] = -vfCoef * dvloss_dv;
+    if (newlp) newlp[n] = logp;
+    if (newval) newval[n] = vnew;
+    for (size_t j = 0; j < H; j++) dh[j] = 0.0;
+    for (size_t k = 0; k < O; k++) {
+      double dk = dout[k];
+      double* gw = gW2 + k * H;
+      const double* w = W2 + k * H;
+      for (size_t j = 0; j < H; j++) {
+        gw[j] += dk * h[j];
+        dh[j] += dk * w[j];
+      }
+      gb2[k] += dk;
+    }
+    for (size_t j = 0; j < H; j++) {
+      double dz = (z1[j] > 0.0) ? dh[j] : 0.0;
+      double* gw = gW1 + j * D;
+      for (size_t d = 0; d < D; d++) gw[d] += dz * x[d];
+      gb1[j] += dz;
+    }
+  }
+  free(z1); free(h); free(out); free(dout); free(dh);
+}
+
+/* One wide resident update (lean_cuda_train_update_wide_resident, ffi/puffercuda.cu:1307-1409): per
+ * epoch and minibatch (mbSize = NT/numMB, the last takes the remainder) gather the rows, normalizeAdv,
+ * the summed gradient, mean + global-norm clip (gradClip with maxGradNorm), then stepMat on W1 and W2
+ * and stepVec on the biases. pm = [params; mom] updated in place. */
+void orc_train_update_wide(double* pm, const double* obs, const double* acts, const double* adv, const double* ret,
+                           const double* olp, const double* ov, const double* perm, const int* hs, size_t NT,
+                           size_t D, size_t H, size_t O, size_t W, int mode, size_t epochs, size_t numMB, double lr,
+                           double wd, double mu, double eps, double vfCoef, double entCoef, double clipEps,
+                           double vfClip, double maxGradNorm, double lsLo, const double* coeffs, int iters) {
+  const size_t P = H * D + H + O * H + O;
+  size_t mbSize = NT / numMB;
+  if (mbSize < 1) mbSize = 1;
+  double* mObs = (double*)malloc(sizeof(double) * NT * D);
+  double* mAct = (double*)malloc(sizeof(double) * NT * W);
+  double* mAdv = (double*)malloc(sizeof(double) * NT);
+  double* mAdvN = (double*)malloc(sizeof(double) * NT);
+  double* mRet = (double*)malloc(sizeof(double) * NT);
+  double* mOlp = (double*)malloc(sizeof(double) * NT);
+  double* mOv = (double*)malloc(sizeof(double) * NT);
+  double* g = (double*)malloc(sizeof(double) * P);
+  for (size_t e = 0; e < epochs; e++)
+    for (size_t m = 0; m < numMB; m++) {
+      size_t lo = m * mbSize, hi = (m + 1 == numMB) ? NT : (m + 1) * mbSize;
+      if (hi > NT) hi = NT;
+      if (hi <= lo) continue;
+      size_t Nmb = hi - lo;
+      const double* idx = perm + e * NT + lo;
+      for (size_t k = 0; k < Nmb; k++) {
+        size_t r = (size_t)idx[k];
+        memcpy(mObs + k * D, obs + r * D, sizeof(double) * D);
+        memcpy(mAct + k * W, acts + r * W, sizeof(double) * W);
+        mAdv[k] = adv[r];
+        mRet[k] = ret[r];
+        mOlp[k] = olp[r];
+        mOv[k] = ov ? ov[r] : 0.0;
+      }
+      orc_normalize_adv(mAdv, Nmb, mAdvN);
+      orc_mlp_ppo_grad_wide(pm, mObs, mAct, mAdvN, mRet, mOlp, ov ? mOv : NULL, Nmb, D, H, O, W, mode, hs, vfCoef,
+                            entCoef, clipEps, vfClip, lsLo, g, NULL, NULL);
+      orc_grad_clip(g, P, maxGradNorm, 1.0 / (double)Nmb);
+      orc_apply_muon(pm, g, D, H, O - 1, 1, lr, wd, mu, eps, coeffs, iters);
+    }
+  free(mObs); free(mAct); free(mAdv); free(mAdvN); free(mRet); free(mOlp); free(mOv); free(g);
+}

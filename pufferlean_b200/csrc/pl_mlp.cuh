@@ -79,5 +79,13 @@ int launch_ppo_rows_f32(const float* Out, int M, int A, const int* act, const fl
                         const float* ret, const float* olp, const float* ov, float vf, float ent, float clip,
                         float vfclip, float* dOut, float* newlp, float* newval, cudaStream_t st);
 int launch_colsum_f32(const float* Mx, long rows, int N, float* out, cudaStream_t st);
+// Wide action heads (multi-discrete mode 1, Gaussian mode 2): per-row PPO objective gradient,
+// per-128-row column sums (colpart) and loss sums (loss_part); see pl_mlp_kernels.cu.
+int launch_ppo_rows_wide(bool bf16_out, const float* Out, int ldo, const float* bias, int M, int O, int ldd, int mode,
+                        int W, const int* hs, const float* actw, const float* adv, const double* ms, const float* ret,
+                        const float* olp, const float* ov, float vf, float ent, float clip, float vfclip, float lslo,
+                        float lshi, void* dOut, float* colpart, float* loss_part, cudaStream_t st);
+int launch_gather_rows_f32(const int* idx, int Nmb, const float* src, int W, float* dst, cudaStream_t st);
+int launch_f64_to_f32_rows(const double* s, long n, float* d, cudaStream_t st);
 
 }  // namespace pl

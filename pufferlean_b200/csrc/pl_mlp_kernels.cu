@@ -372,6 +372,169 @@ __global__ void ppo_rows_f32_kernel(const float* __restrict__ Out, int M, int A,
   if (newlp) newlp[n] = logpA;
   if (newval) newval[n] = vnew;
 }
+// ---------------------------------------------------------------- wide action heads
+// Per-row PPO objective gradient of the multi-discrete (mode 1) and Gaussian (mode 2) heads, the
+// resident wide update's k_ppo_dout_md / k_ppo_dout_cont (ffi/puffercuda.cu:706-727, 1767-1790):
+//  mode 1: W categorical heads of sizes hs[0..W) over the first sum(hs) logits; the joint log-prob is
+//          the sum of the heads' (log-softmax without max subtraction, as the reference); one clip on
+//          the joint ratio; each head's logits get dPol (onehot - p) + ent p (sum p l - l);
+//  mode 2: W dims, out = [means (W) | raw log-stds (W) | value]; log-std clamped to [lslo, lshi];
+//          d/dmean = dPol z / std, d/draw-logstd = (dPol (z^2 - 1) + ent) inside the clamp, 0 outside;
+// value (column O-1) with the PufferLib value clip when ov != NULL and vfclip > 0. Out has ld `ldo`
+// and gets `bias` added when it is not NULL (the fast tier's GEMM writes no bias); the advantage is
+// normalised with ms = [mean, std + 1e-8] when ms != NULL. dOut [M x ldd] (zero past O). Each
+// 128-row block also writes its column sums of dOut (colpart[blockIdx.x][c], c < ldd) and its six
+// loss sums (loss_part[blockIdx.x][0..5]: pg, value, entropy, kl, old kl, clipped).
+template <typename S>
+__device__ __forceinline__ void st_elem(S* p, long i, float v);
+template <>
+__device__ __forceinline__ void st_elem<float>(float* p, long i, float v) {
+  p[i] = v;
+}
+template <>
+__device__ __forceinline__ void st_elem<__nv_bfloat16>(__nv_bfloat16* p, long i, float v) {
+  p[i] = __float2bfloat16_rn(v);
+}
+template <typename S>
+__global__ void __launch_bounds__(128) ppo_rows_wide_kernel(
+    const float* __restrict__ Out, int ldo, const float* __restrict__ bias, int M, int O, int ldd, int mode, int W,
+    const int* __restrict__ hs, const float* __restrict__ actw, const float* __restrict__ adv,
+    const double* __restrict__ ms, const float* __restrict__ ret, const float* __restrict__ olp,
+    const float* __restrict__ ov, float vf, float ent, float clip, float vfclip, float lslo, float lshi, S* dOut,
+    float* colpart, float* loss_part) {
+  __shared__ float red[4][128];
+  __shared__ float lred[4][8];
+  const int n = blockIdx.x * 128 + threadIdx.x;
+  const bool ok = n < M;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* out = Out + (long)(ok ? n : 0) * ldo;
+  auto lg = [&](int k) { return out[k] + (bias ? bias[k] : 0.f); };
+  float ad = ok ? adv[n] : 0.f;
+  if (ms && ok) ad = (float)(((double)ad - ms[0]) / ms[1]);
+  const float* a = actw + (long)(ok ? n : 0) * W;
+  // joint log-prob and the entropy of the row
+  float logp = 0.f, entr = 0.f;
+  if (mode == 1) {
+    int off = 0;
+    for (int h = 0; h < W; h++) {
+      const int sz = hs[h];
+      float se = 0.f;
+      for (int k = 0; k < sz; k++) se += expf(lg(off + k));
+      const float lse = logf(se);
+      logp += lg(off + (int)a[h]) - lse;
+      float pout = 0.f;
+      for (int k = 0; k < sz; k++) pout += expf(lg(off + k) - lse) * lg(off + k);
+      entr += lse - pout;
+      off += sz;
+    }
+  } else {
+    for (int i = 0; i < W; i++) {
+      const float lsr = lg(W + i);
+      const float ls = lsr < lslo ? lslo : (lsr > lshi ? lshi : lsr);
+      const float z = (a[i] - lg(i)) * expf(-ls);
+      logp += -0.5f * z * z - ls - 0.9189385332046727f;
+      entr += ls + 1.4189385332046727f;
+    }
+  }
+  const float lgr = logp - (ok ? olp[n] : 0.f);
+  const float ratio = expf(lgr);
+  const float lo = 1.f - clip, hi = 1.f + clip;
+  const float rc = ratio < lo ? lo : (ratio > hi ? hi : ratio);
+  const float s1 = ad * ratio, s2 = ad * rc;
+  const float dPol = s1 <= s2 ? ad * ratio : ad * ((lo < ratio && ratio < hi) ? 1.f : 0.f) * ratio;
+  const float vnew = lg(O - 1), rt = ok ? ret[n] : 0.f;
+  float dv = vnew - rt, vl = 0.5f * (vnew - rt) * (vnew - rt);
+  if (ov && vfclip > 0.f && ok) {
+    const float vold = ov[n], dd = vnew - vold;
+    const float vcl = vold + (dd < -vfclip ? -vfclip : (dd > vfclip ? vfclip : dd));
+    const float du = (vnew - rt) * (vnew - rt), cc = (vcl - rt) * (vcl - rt);
+    if (!(du >= cc) && !(dd > -vfclip && dd < vfclip)) dv = 0.f;
+    vl = 0.5f * (cc > du ? cc : du);
+  }
+  // per column: write dOut and fold the block's column sums
+  S* drow = dOut + (long)(ok ? n : 0) * ldd;
+  auto emit = [&](int k, float v) {
+    if (!ok) v = 0.f;
+    if (ok) st_elem(drow, k, v);
+    float w = v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+    if (lane == 0) red[warp][k & 127] = w;
+  };
+  int k0 = 0;  // columns are folded in chunks of 128 (ldd <= 128 keeps it to one)
+  for (int base = 0; base < ldd; base += 128) {
+    const int top = min(ldd, base + 128);
+    for (int k = base; k < top; k++) {
+      float v = 0.f;
+      if (k < O - 1) {
+        if (mode == 1) {
+          // head of column k
+          int off = 0, h = 0;
+          while (h < W && k >= off + hs[h]) off += hs[h++];
+          const int sz = hs[h];
+          float se = 0.f;
+          for (int j = 0; j < sz; j++) se += expf(lg(off + j));
+          const float lse = logf(se);
+          float pout = 0.f;
+          for (int j = 0; j < sz; j++) pout += expf(lg(off + j) - lse) * lg(off + j);
+          const float p = expf(lg(k) - lse);
+          v = dPol * ((k - off == (int)a[h] ? 1.f : 0.f) - p) + ent * p * (pout - lg(k));
+        } else if (k < W) {
+          const float lsr = lg(W + k);
+          const float ls = lsr < lslo ? lslo : (lsr > lshi ? lshi : lsr);
+          const float is = expf(-ls);
+          const float z = (a[k] - lg(k)) * is;
+          v = dPol * z * is;
+        } else {
+          const int i = k - W;
+          const float lsr = lg(k);
+          const float ls = lsr < lslo ? lslo : (lsr > lshi ? lshi : lsr);
+          const float z = (a[i] - lg(i)) * expf(-ls);
+          v = (lslo < lsr && lsr < lshi) ? dPol * (z * z - 1.f) + ent : 0.f;
+        }
+      } else if (k == O - 1) {
+        v = -vf * dv;
+      }
+      emit(k, v);
+    }
+    __syncthreads();
+    for (int k = base + threadIdx.x; k < top; k += 128)
+      colpart[(long)blockIdx.x * ldd + k] =
+          ((red[0][k & 127] + red[1][k & 127]) + red[2][k & 127]) + red[3][k & 127];
+    __syncthreads();
+    k0 = top;
+  }
+  (void)k0;
+  if (loss_part) {
+    float lt[6] = {ok ? fmaxf(-ad * ratio, -ad * rc) : 0.f, ok ? vl : 0.f, ok ? entr : 0.f,
+                   ok ? (ratio - 1.f) - lgr : 0.f, ok ? -lgr : 0.f,
+                   ok ? ((ratio < lo || ratio > hi) ? 1.f : 0.f) : 0.f};
+#pragma unroll
+    for (int q = 0; q < 6; q++) {
+      float w = lt[q];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+      if (lane == 0) lred[warp][q] = w;
+    }
+    __syncthreads();
+    if (threadIdx.x < 6)
+      loss_part[(long)blockIdx.x * 8 + threadIdx.x] =
+          ((lred[0][threadIdx.x] + lred[1][threadIdx.x]) + lred[2][threadIdx.x]) + lred[3][threadIdx.x];
+  }
+}
+// dst[k][0..W) = src[idx[k]][0..W)
+__global__ void gather_rows_f32_kernel(const int* __restrict__ idx, int Nmb, const float* __restrict__ src, int W,
+                                       float* dst) {
+  const long n = (long)Nmb * W;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long k = i / W;
+    dst[i] = src[(long)idx[k] * W + (i - k * W)];
+  }
+}
+__global__ void f64_to_f32_rows_kernel(const double* __restrict__ s, long n, float* d) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) d[i] = (float)s[i];
+}
+
 // gb[c] = sum_n M[n*N + c] (sequential per column, deterministic)
 __global__ void colsum_f32_kernel(const float* __restrict__ Mx, long rows, int N, float* out) {
   int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -542,6 +705,35 @@ int launch_act_grad_f32(float* dH, const float* Z, long n, int act, cudaStream_t
   act_grad_f32_kernel<<<grid_for(n), 256, 0, st>>>(dH, Z, n, act);
   count_launch();
   PL_LAUNCH("act_grad_f32_kernel");
+  return PL_OK;
+}
+int launch_ppo_rows_wide(bool bf16_out, const float* Out, int ldo, const float* bias, int M, int O, int ldd, int mode,
+                        int W, const int* hs, const float* actw, const float* adv, const double* ms, const float* ret,
+                        const float* olp, const float* ov, float vf, float ent, float clip, float vfclip, float lslo,
+                        float lshi, void* dOut, float* colpart, float* loss_part, cudaStream_t st) {
+  const unsigned nb = (unsigned)ceil_div(M, 128);
+  if (bf16_out)
+    ppo_rows_wide_kernel<__nv_bfloat16><<<nb, 128, 0, st>>>(Out, ldo, bias, M, O, ldd, mode, W, hs, actw, adv, ms, ret,
+                                                            olp, ov, vf, ent, clip, vfclip, lslo, lshi,
+                                                            (__nv_bfloat16*)dOut, colpart, loss_part);
+  else
+    ppo_rows_wide_kernel<float><<<nb, 128, 0, st>>>(Out, ldo, bias, M, O, ldd, mode, W, hs, actw, adv, ms, ret, olp, ov,
+                                                    vf, ent, clip, vfclip, lslo, lshi, (float*)dOut, colpart,
+                                                    loss_part);
+  count_launch();
+  PL_LAUNCH("ppo_rows_wide_kernel");
+  return PL_OK;
+}
+int launch_gather_rows_f32(const int* idx, int Nmb, const float* src, int W, float* dst, cudaStream_t st) {
+  gather_rows_f32_kernel<<<grid_for((long)Nmb * W), 256, 0, st>>>(idx, Nmb, src, W, dst);
+  count_launch();
+  PL_LAUNCH("gather_rows_f32_kernel");
+  return PL_OK;
+}
+int launch_f64_to_f32_rows(const double* s, long n, float* d, cudaStream_t st) {
+  f64_to_f32_rows_kernel<<<grid_for(n), 256, 0, st>>>(s, n, d);
+  count_launch();
+  PL_LAUNCH("f64_to_f32_rows_kernel");
   return PL_OK;
 }
 int launch_ppo_rows_f32(const float* Out, int M, int A, const int* act, const float* adv, const double* ms,

@@ -93,9 +93,19 @@ struct pl_update {
   double prof_ms[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   bool loss_on = false;
   double losses[7] = {0, 0, 0, 0, 0, 0, 0};
+  // wide action heads (pl_update_set_head): 0 categorical, 1 multi-discrete, 2 Gaussian
+  int head_mode = 0;
+  int W = 1;
+  int* hs_dev = nullptr;      // head sizes (mode 1)
+  float* actw_c = nullptr;    // action column [NT x W]
+  float* mb_actw = nullptr;   // its minibatch rows [mbMax x W]
+  float* Outw = nullptr;      // fast tier: fp32 head GEMM output [mbMax x Op]
 };
 
 namespace {
+
+// Log-std clamp of the Gaussian head (the resident device path's bounds, ffi/puffercuda.cu:1647-1648).
+constexpr float kContLogStdLo = -20.f, kContLogStdHi = 2.f;
 
 static std::mutex g_mu;
 static bool g_loss_on = false;
@@ -465,7 +475,36 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
   }
   // ---- PPO head: logits + value -> objective gradient dOut
   const Layer& hd = u->layers[L];
-  {
+  if (u->head_mode != 0) {
+    // wide heads: fp32 logits from a plain GEMM, then the row kernel (objective gradient, column
+    // partial sums for the bias gradient, loss sums)
+    rc = launch_gather_rows_f32(idx, Nmb, u->actw_c, u->W, u->mb_actw, st);
+    if (rc) return rc;
+    Operand A{hin, Nmb, hd.in, ldin, 1, 0};
+    Operand B{u->Wb[L], hd.out, hd.in, hd.in_p, 1, 0};
+    EpiArgs e{};
+    e.out = u->Outw;
+    e.ldo = u->Op;
+    e.out_rows = Nmb;
+    e.out_cols = hd.out;
+    e.alpha = 1.f;
+    {
+      Span sp(u, 1, st, gf(Nmb, hd.out, hd.in));
+      rc = gemm_launch(128, EPI_F32, false, false, A, B, Nmb, hd.out, hd.in, 1, e, st);
+      if (!rc)
+        rc = launch_ppo_rows_wide(true, u->Outw, u->Op, u->bf[L], Nmb, u->O, u->Op, u->head_mode, u->W, u->hs_dev,
+                                  u->mb_actw, u->mb_adv, u->grad_only ? nullptr : u->ms, u->mb_ret, u->mb_olp,
+                                  u->mb_ov, (float)d.vfCoef, (float)d.entCoef, (float)d.clipEps, (float)d.vfClip,
+                                  kContLogStdLo, kContLogStdHi, u->dOut, u->colpart,
+                                  last && u->loss_on ? u->loss_part : nullptr, st);
+    }
+    if (rc) return rc;
+    {
+      Span sp(u, 6, st, 0);
+      rc = launch_colsum_reduce(u->colpart, mt, u->Op, hd.out, u->grad + hd.ob, st);
+    }
+    if (rc) return rc;
+  } else {
     Operand A{hin, Nmb, hd.in, ldin, 1, 0};
     Operand B{u->Wb[L], hd.out, hd.in, hd.in_p, 1, 0};
     EpiArgs e{};
@@ -620,9 +659,18 @@ static int minibatch_tight(pl_update* u, const int* idx, int Nmb, double lr, boo
   if (rc) return rc;
   rc = launch_bias_act_f32(u->Out, nullptr, u->bf[L], Nmb, O, 0, st);
   if (rc) return rc;
-  rc = launch_ppo_rows_f32(u->Out, Nmb, (int)d.A, u->mb_act, u->mb_adv, u->grad_only ? nullptr : u->ms, u->mb_ret,
-                           u->mb_olp, u->mb_ov, (float)d.vfCoef, (float)d.entCoef, (float)d.clipEps, (float)d.vfClip,
-                           (float*)u->dOut, nullptr, nullptr, st);
+  if (u->head_mode != 0) {
+    rc = launch_gather_rows_f32(idx, Nmb, u->actw_c, u->W, u->mb_actw, st);
+    if (!rc)
+      rc = launch_ppo_rows_wide(false, u->Out, O, nullptr, Nmb, O, O, u->head_mode, u->W, u->hs_dev, u->mb_actw,
+                                u->mb_adv, u->grad_only ? nullptr : u->ms, u->mb_ret, u->mb_olp, u->mb_ov,
+                                (float)d.vfCoef, (float)d.entCoef, (float)d.clipEps, (float)d.vfClip, kContLogStdLo,
+                                kContLogStdHi, u->dOut, u->colpart, nullptr, st);
+  } else {
+    rc = launch_ppo_rows_f32(u->Out, Nmb, (int)d.A, u->mb_act, u->mb_adv, u->grad_only ? nullptr : u->ms, u->mb_ret,
+                             u->mb_olp, u->mb_ov, (float)d.vfCoef, (float)d.entCoef, (float)d.clipEps,
+                             (float)d.vfClip, (float*)u->dOut, nullptr, nullptr, st);
+  }
   if (rc) return rc;
   const float* dcur = (const float*)u->dOut;
   int nd = O;
@@ -791,6 +839,42 @@ static int staged(pl_update* u, const double* host, size_t n, cudaStream_t st, F
 
 extern "C" {
 
+int pl_update_set_head(pl_update* u, int mode, size_t W, const double* head_sizes) {
+  PL_REQUIRE(u != nullptr, PL_ERR_INVALID, "pl_update_set_head: NULL session");
+  PL_REQUIRE(mode >= 0 && mode <= 2, PL_ERR_INVALID, "pl_update_set_head: mode %d (0, 1 or 2)", mode);
+  if (mode == 0) {
+    u->head_mode = 0;
+    return PL_OK;
+  }
+  const long A = (long)u->d.A;
+  PL_REQUIRE(W >= 1 && W <= 4096, PL_ERR_INVALID, "pl_update_set_head: W = %zu", W);
+  PL_REQUIRE(u->O <= 128, PL_ERR_UNSUPPORTED, "wide heads need A + 1 <= 128 outputs (A = %ld)", A);
+  std::vector<int> hs((size_t)W, 0);
+  if (mode == 1) {
+    PL_REQUIRE(head_sizes != nullptr, PL_ERR_INVALID, "multi-discrete heads need their sizes");
+    long sum = 0;
+    for (size_t i = 0; i < W; i++) {
+      hs[i] = (int)head_sizes[i];
+      PL_REQUIRE(hs[i] >= 1, PL_ERR_INVALID, "head %zu has size %d", i, hs[i]);
+      sum += hs[i];
+    }
+    PL_REQUIRE(sum == A, PL_ERR_INVALID, "head sizes sum to %ld, the network has A = %ld logits", sum, A);
+  } else {
+    PL_REQUIRE((long)(2 * W) == A, PL_ERR_INVALID, "a Gaussian head of %zu dims needs A = %zu (got %ld)", W, 2 * W, A);
+  }
+  if (u->W != (int)W || !u->actw_c) {
+    u->actw_c = dalloc<float>(u, (size_t)u->d.NT * W);
+    u->mb_actw = dalloc<float>(u, (size_t)u->mbMax * W);
+    u->hs_dev = dalloc<int>(u, W);
+    if (u->fast && !u->Outw) u->Outw = dalloc<float>(u, (size_t)u->mbMax * u->Op);
+    if (u->alloc_failed) return PL_ERR_NOMEM;
+  }
+  PL_CUDA(cudaMemcpy(u->hs_dev, hs.data(), sizeof(int) * W, cudaMemcpyHostToDevice));
+  u->head_mode = mode;
+  u->W = (int)W;
+  return PL_OK;
+}
+
 int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, const double* adv, const double* ret,
                           const double* olp, const double* oldVal, const double* perm, void* stream) {
   PL_REQUIRE(u && obs && acts && adv && ret && olp && perm, PL_ERR_INVALID, "pl_update_set_columns: NULL column");
@@ -809,6 +893,17 @@ int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, c
     if (rc) return rc;
   }
   PL_CUDA(cudaMemcpyAsync(u->adv_c, adv, NT * sizeof(double), cudaMemcpyHostToDevice, st));
+  if (u->head_mode != 0) {
+    // wide action rows (NT x W) -> fp32 through staging; the categorical column is unused
+    const size_t n = (size_t)NT * u->W;
+    for (size_t off = 0; off < n; off += u->stage_elems) {
+      const size_t c = std::min(u->stage_elems, n - off);
+      PL_CUDA(cudaMemcpyAsync(u->stage, acts + off, c * 8, cudaMemcpyHostToDevice, st));
+      int rc = launch_f64_to_f32_rows(u->stage, (long)c, u->actw_c + off, st);
+      if (rc) return rc;
+    }
+    acts = ret;  // the column pass below then fills the unused integer column from ret
+  }
   // act/ret/olp/ov -> int32 / f32 through staging (4 columns)
   double* s = u->stage;
   const size_t per = u->stage_elems / 4;
@@ -844,6 +939,11 @@ int pl_update_set_columns_dev(pl_update* u, const float* obs, const double* acts
   }
   if (rc) return rc;
   if (adv) PL_CUDA(cudaMemcpyAsync(u->adv_c, adv, NT * sizeof(double), cudaMemcpyDeviceToDevice, st));
+  if (u->head_mode != 0) {
+    rc = launch_f64_to_f32_rows(acts, NT * u->W, u->actw_c, st);
+    if (rc) return rc;
+    acts = olp;  // the integer column is unused with wide heads
+  }
   rc = launch_columns(acts, ret, olp, (u->ov_c && oldVal) ? oldVal : nullptr, NT, u->act_c, ret ? u->ret_c : nullptr,
                       u->olp_c, (u->ov_c && oldVal) ? u->ov_c : nullptr, st);
   if (rc) return rc;
@@ -1014,7 +1114,7 @@ static int resident_update(size_t handle, const pl_mlp_arch* arch, const double*
                            size_t oldValN, const double* perm, size_t NT, size_t D, size_t H, size_t A, size_t epochs,
                            size_t numMB, double lr, double wd, double mu, double eps, double vfCoef, double entCoef,
                            double clipEps, double vfClip, double maxGradNorm, uint8_t bf16, bool grad_only,
-                           float* grad_out) {
+                           float* grad_out, int head_mode = 0, size_t W = 1, const double* head_sizes = nullptr) {
   int rc = require_device();
   if (rc) return rc;
   pl_update_desc d{};
@@ -1041,6 +1141,8 @@ static int resident_update(size_t handle, const pl_mlp_arch* arch, const double*
   rc = session_for(handle, d, &u);
   if (rc) return rc;
   u->grad_only = grad_only;
+  rc = pl_update_set_head(u, head_mode, W, head_sizes);
+  if (rc) return rc;
   rc = refresh_shadows(u, 0);
   if (rc) return rc;
   rc = pl_update_set_columns(u, obs, acts, adv, ret, olp, d.use_old_values ? oldVal : nullptr, perm, nullptr);
@@ -1064,6 +1166,75 @@ int pl_train_update_resident_deep(size_t handle, const pl_mlp_arch* arch, const 
   if (rc) return rc;
   if (params0_out) PL_CUDA(cudaMemcpy(params0_out, (const void*)handle, sizeof(double), cudaMemcpyDeviceToHost));
   return PL_OK;
+}
+
+int pl_train_update_wide_resident(size_t handle, const double* obs, const double* acts, const double* adv,
+                                  const double* ret, const double* olp, const double* oldVal, size_t oldValN,
+                                  const double* perm, const double* head_sizes, size_t NT, size_t D, size_t H,
+                                  size_t O, size_t W, uint32_t mode, size_t epochs, size_t numMB, double lr, double wd,
+                                  double mu, double eps, double vfCoef, double entCoef, double clipEps, double vfClip,
+                                  double maxGradNorm, uint8_t bf16, double* params0_out) {
+  PL_REQUIRE(handle && obs && acts && adv && ret && olp && perm, PL_ERR_INVALID, "wide update: NULL argument");
+  PL_REQUIRE(mode == 1 || mode == 2, PL_ERR_INVALID, "wide update: mode %u (1 multi-discrete, 2 Gaussian)", mode);
+  PL_REQUIRE(O >= 2, PL_ERR_INVALID, "wide update: O = %zu", O);
+  int rc = resident_update(handle, nullptr, obs, acts, adv, ret, olp, oldVal, oldValN, perm, NT, D, H, O - 1, epochs,
+                           numMB, lr, wd, mu, eps, vfCoef, entCoef, clipEps, vfClip, maxGradNorm, bf16, false,
+                           nullptr, (int)mode, W, head_sizes);
+  if (rc) return rc;
+  if (params0_out) PL_CUDA(cudaMemcpy(params0_out, (const void*)handle, sizeof(double), cudaMemcpyDeviceToHost));
+  return PL_OK;
+}
+
+int pl_mlp_ppo_grad_wide(const double* params, const double* obs, const double* acts, const double* advs,
+                         const double* rets, const double* oldlps, const double* oldVal, size_t N, size_t H, size_t D,
+                         size_t O, size_t W, uint32_t mode, const double* head_sizes, double vfCoef, double entCoef,
+                         double clipEps, double vfClip, uint8_t bf16, double* g) {
+  PL_REQUIRE(params && obs && acts && advs && rets && oldlps && g, PL_ERR_INVALID, "wide gradient: NULL argument");
+  PL_REQUIRE(mode == 1 || mode == 2, PL_ERR_INVALID, "wide gradient: mode %u (1 multi-discrete, 2 Gaussian)", mode);
+  const size_t P = pl_mlp_param_count(D, H, O - 1, 1);
+  std::vector<double> pm(2 * P, 0.0);
+  memcpy(pm.data(), params, sizeof(double) * P);
+  std::vector<double> perm(N);
+  for (size_t i = 0; i < N; i++) perm[i] = (double)i;
+  size_t h = 0;
+  int rc = pl_policy_load(pm.data(), P, &h);
+  if (rc) return rc;
+  std::vector<float> gf(P);
+  rc = resident_update(h, nullptr, obs, acts, advs, rets, oldlps, oldVal, oldVal ? N : 0, perm.data(), N, D, H, O - 1,
+                       1, 1, 0.0, 0.0, 0.0, 1e-7, vfCoef, entCoef, clipEps, vfClip, 0.0, bf16, true, gf.data(),
+                       (int)mode, W, head_sizes);
+  pl_policy_free(h);
+  if (rc) return rc;
+  for (size_t i = 0; i < P; i++) g[i] = (double)gf[i];
+  return PL_OK;
+}
+
+// One Muon step of the resident one-hidden-layer MLP from a raw summed gradient: the exact f64 tier
+// (the reference's muon_mat_dev / k_stepvec, the same folds as muon_mat_cpu / stepvec_cpu with the
+// gradient scale applied in the momentum update).
+int pl_muon_step_mlp_resident(size_t handle, const double* gRaw, size_t H, size_t D, size_t O, double gscale,
+                              double lr, double wd, double mu, double eps, double* params_out) {
+  PL_REQUIRE(handle && gRaw, PL_ERR_INVALID, "pl_muon_step_mlp_resident: NULL argument");
+  int rc = require_device();
+  if (rc) return rc;
+  const size_t P = H * D + H + O * H + O;
+  double* pm = (double*)handle;
+  double* g = (double*)scratch(23, sizeof(double) * P);
+  double* ws = (double*)scratch(24, sizeof(double) * std::max(exact_ws_doubles((int)H, (int)D),
+                                                               exact_ws_doubles((int)O, (int)H)));
+  if (!g || !ws) return PL_ERR_NOMEM;
+  PL_CUDA(cudaMemcpy(g, gRaw, sizeof(double) * P, cudaMemcpyHostToDevice));
+  rc = set_ns_coeffs(&kMuonCoeffs[0][0], 5, 0);
+  const size_t oW1 = 0, ob1 = H * D, oW2 = H * D + H, ob2 = H * D + H + O * H;
+  if (!rc) rc = muon_mat_exact((int)H, (int)D, pm + oW1, pm + P + oW1, g + oW1, gscale, lr, wd, mu, eps, 5, ws, 0);
+  if (!rc) rc = stepvec_launch(pm + ob1, pm + P + ob1, g + ob1, lr, wd, mu, gscale, (long)H, 0);
+  if (!rc) rc = muon_mat_exact((int)O, (int)H, pm + oW2, pm + P + oW2, g + oW2, gscale, lr, wd, mu, eps, 5, ws, 0);
+  if (!rc) rc = stepvec_launch(pm + ob2, pm + P + ob2, g + ob2, lr, wd, mu, gscale, (long)O, 0);
+  if (rc) return rc;
+  // sessions holding shadows of this handle refresh them at their next call (resident_update)
+  if (params_out) PL_CUDA(cudaMemcpy(params_out, pm, sizeof(double) * P, cudaMemcpyDeviceToHost));
+  PL_CUDA(cudaDeviceSynchronize());
+  return device_error_check();
 }
 
 int pl_train_update_resident(size_t handle, const double* obs, const double* acts, const double* adv,
