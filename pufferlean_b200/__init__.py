@@ -97,6 +97,10 @@ def _bind_optional(L):
                          C.c_int),
         "pl_mg_last_launches": ([_vp], C.c_uint64),
         "pl_mg_set_comm": ([_vp, _vp, C.c_int, C.c_int], C.c_int),
+        "pl_train_update_wide_resident": ([_sz] + [_dp] * 6 + [_sz, _dp, _dp] + [_sz] * 5 + [C.c_uint32, _sz, _sz]
+                                          + [_d] * 9 + [C.c_uint8, _dp], C.c_int),
+        "pl_mlp_ppo_grad_wide": ([_dp] * 7 + [_sz] * 5 + [C.c_uint32, _dp] + [_d] * 4 + [C.c_uint8, _dp], C.c_int),
+        "pl_muon_step_mlp_resident": ([_sz, _dp] + [_sz] * 3 + [_d] * 5 + [_dp], C.c_int),
         "pl_ckpt_write": ([C.c_char_p, _dp, _sz], C.c_int),
         "pl_ckpt_read": ([C.c_char_p, _dp, _sz, C.POINTER(_sz)], C.c_int),
         "pl_policy_save": ([_sz, _sz, C.c_char_p], C.c_int),
@@ -245,6 +249,48 @@ def cuda_train_update_resident(handle, obs, acts, adv, ret, olp, old_val, perm, 
     _check(lib().pl_train_update_resident(handle, *[_p(a) for a in arrs], _p(ov), ov.size, _p(pr), NT, D, H, A,
                                           epochs, num_mb, lr, wd, mu, eps, vf_coef, ent_coef, clip_eps, vf_clip,
                                           max_grad_norm, bf16, _p(out)), "pl_train_update_resident")
+    return out
+
+
+# ------------------------------------------------------------------------------------ wide action heads
+def _heads(head_sizes, W):
+    return _f64(head_sizes) if head_sizes is not None else np.zeros(max(int(W), 1))
+
+
+def cuda_train_update_wide_resident(handle, obs, acts, adv, ret, olp, old_val, perm, head_sizes, NT, D, H, O, W, mode,
+                                    epochs, num_mb, lr, wd, mu, eps, vf_coef, ent_coef, clip_eps, vf_clip,
+                                    max_grad_norm, bf16):
+    """cudaTrainUpdateWideResidentFFI: the resident update with W multi-discrete heads (mode 1, head_sizes
+    summing to O-1) or W Gaussian dims (mode 2, O = 2W+1); acts is NT x W. Returns [params[0]]."""
+    arrs = [_f64(x) for x in (obs, acts, adv, ret, olp)]
+    ov = _f64(old_val) if old_val is not None else np.empty(0)
+    pr, hs = _f64(perm), _heads(head_sizes, W)
+    out = np.empty(1)
+    _check(lib().pl_train_update_wide_resident(handle, *[_p(a) for a in arrs], _p(ov), ov.size, _p(pr), _p(hs), NT,
+                                               D, H, O, W, mode, epochs, num_mb, lr, wd, mu, eps, vf_coef, ent_coef,
+                                               clip_eps, vf_clip, max_grad_norm, bf16, _p(out)),
+           "pl_train_update_wide_resident")
+    return out
+
+
+def cuda_mlp_ppo_grad_wide(params, obs, acts, advs, rets, oldlps, old_val, N, H, D, O, W, mode, head_sizes, vf_coef,
+                           ent_coef, clip_eps, vf_clip, bf16):
+    """Summed wide-head objective gradient over N rows (P values, ascent convention)."""
+    arrs = [_f64(x) for x in (params, obs, acts, advs, rets, oldlps)]
+    ov = _f64(old_val) if old_val is not None else None
+    out = np.empty(H * D + H + O * H + O)
+    _check(lib().pl_mlp_ppo_grad_wide(*[_p(a) for a in arrs], _p(ov) if ov is not None else None, N, H, D, O, W, mode,
+                                      _p(_heads(head_sizes, W)), vf_coef, ent_coef, clip_eps, vf_clip, bf16, _p(out)),
+           "pl_mlp_ppo_grad_wide")
+    return out
+
+
+def cuda_muon_step_mlp_resident(handle, g_raw, H, D, O, gscale, lr, wd, mu, eps):
+    """cudaMuonStepMlpResidentFFI: in-place f64 Muon of the resident [W1|b1|W2|b2] from a raw summed gradient;
+    returns the new params."""
+    out = np.empty(H * D + H + O * H + O)
+    _check(lib().pl_muon_step_mlp_resident(handle, _p(_f64(g_raw)), H, D, O, gscale, lr, wd, mu, eps, _p(out)),
+           "pl_muon_step_mlp_resident")
     return out
 
 

@@ -395,6 +395,12 @@ template <>
 __device__ __forceinline__ void st_elem<__nv_bfloat16>(__nv_bfloat16* p, long i, float v) {
   p[i] = __float2bfloat16_rn(v);
 }
+// The action of one multi-discrete head as a logit index, held inside the head so that a malformed
+// action column cannot read past the row (valid actions are unchanged).
+__device__ __forceinline__ int head_action(float a, int sz) {
+  const int i = (int)a;
+  return i < 0 ? 0 : (i >= sz ? sz - 1 : i);
+}
 template <typename S>
 __global__ void __launch_bounds__(128) ppo_rows_wide_kernel(
     const float* __restrict__ Out, int ldo, const float* __restrict__ bias, int M, int O, int ldd, int mode, int W,
@@ -421,7 +427,7 @@ __global__ void __launch_bounds__(128) ppo_rows_wide_kernel(
       float se = 0.f;
       for (int k = 0; k < sz; k++) se += expf(lg(off + k));
       const float lse = logf(se);
-      logp += lg(off + (int)a[h]) - lse;
+      logp += lg(off + head_action(a[h], sz)) - lse;
       float pout = 0.f;
       for (int k = 0; k < sz; k++) pout += expf(lg(off + k) - lse) * lg(off + k);
       entr += lse - pout;
@@ -478,7 +484,7 @@ __global__ void __launch_bounds__(128) ppo_rows_wide_kernel(
           float pout = 0.f;
           for (int j = 0; j < sz; j++) pout += expf(lg(off + j) - lse) * lg(off + j);
           const float p = expf(lg(k) - lse);
-          v = dPol * ((k - off == (int)a[h] ? 1.f : 0.f) - p) + ent * p * (pout - lg(k));
+          v = dPol * ((k - off == head_action(a[h], sz) ? 1.f : 0.f) - p) + ent * p * (pout - lg(k));
         } else if (k < W) {
           const float lsr = lg(W + k);
           const float ls = lsr < lslo ? lslo : (lsr > lshi ? lshi : lsr);

@@ -222,6 +222,54 @@ def main():
                 pm[off:off + nbias], pm[P + off:P + off + nbias] = nb_, nm_
                 off += nbias
     np.savez(os.path.join(OUT, "mingru_update.npz"), out=pm, rng_out=np.array([r], dtype=np.uint64))
+
+    # Gaussian (continuous) head: out = [means | log-stds | value], O = 2W+1. The bias of the log-std rows
+    # puts some raw log-stds above the clamp's upper end 2 (their gradient is cut); none reaches the CPU
+    # form's lower end -5, below which the CPU (-5) and device (-20) clamps differ.
+    g = np.random.default_rng(0x6A055)
+    N, D, H, W = 37, 7, 24, 3
+    Og = 2 * W + 1
+    P = H * D + H + Og * H + Og
+    params = g.uniform(-0.25, 0.25, P)
+    params[H * D + H + Og * H + W:H * D + H + Og * H + 2 * W] = [-0.5, 0.3, 2.05]
+    obs, acts = g.uniform(-1, 1, N * D), g.standard_normal(N * W)
+    advs, rets, olps = g.standard_normal(N), g.standard_normal(N), g.uniform(-5.0, -1.0, N)
+    ov = rets + 0.3 * g.standard_normal(N)
+    ins = dict(params=params, obs=obs, acts=acts, advs=advs, rets=rets, olps=olps, ov=ov)
+    base = (FA(params), FA(obs), FA(acts), FA(advs), FA(rets), FA(olps))
+    g_plain = arr(ref_call(cpu, "lean_ffi_gauss_ppo_grad_batch", VP, *base, N, H, D, W, 0.5, 0.01, 0.2))
+    base = (FA(params), FA(obs), FA(acts), FA(advs), FA(rets), FA(olps), FA(ov))
+    g_vc = arr(ref_call(cpu, "lean_ffi_gauss_ppo_grad_batch_vclip", VP, *base, N, H, D, W, 0.5, 0.01, 0.2, 0.2))
+    np.savez(os.path.join(OUT, "gauss_grad.npz"), g_plain=g_plain, g_vclip=g_vc,
+             meta=np.array([N, D, H, W, 0.5, 0.01, 0.2, 0.2]), **ins)
+
+    # A whole Gaussian-head update (2 epochs x 4 minibatches, value clip on, no norm clip) composed from the
+    # reference's C: gather, adv normalisation, the Gaussian gradient, lean_ffi_muon_step_mlp with 1/n.
+    NT, E, MB = 64, 2, 4
+    pm0 = np.concatenate([params, g.uniform(-0.01, 0.01, P)])
+    obsT, actsT = g.uniform(-1, 1, NT * D), g.standard_normal(NT * W)
+    advT, retT, olpT = g.standard_normal(NT), g.standard_normal(NT), g.uniform(-5.0, -1.0, NT)
+    ovT = retT + 0.3 * g.standard_normal(NT)
+    perm = arr(ref_call(cpu, "lean_ffi_shuffle_perm", VP, NT, E, ("u64", 0x5EED)))
+    hyp = dict(lr=0.01, wd=0.001, mu=0.95, eps=1e-7, vf=0.5, ent=0.01, clip=0.2, vfClip=0.2)
+    pm = pm0.copy()
+    mb = NT // MB
+    for e in range(E):
+        for m in range(MB):
+            lo, hi = m * mb, (NT if m + 1 == MB else (m + 1) * mb)
+            idx = perm[e * NT + lo:e * NT + hi].astype(np.int64)
+            n = idx.size
+            mObs = obsT.reshape(NT, D)[idx].ravel()
+            mAct = actsT.reshape(NT, W)[idx].ravel()
+            advN = arr(ref_call(cfb, "lean_cuda_adv_normalize", VP, FA(advT[idx]), n))
+            gg = arr(ref_call(cpu, "lean_ffi_gauss_ppo_grad_batch_vclip", VP, FA(pm[:P]), FA(mObs), FA(mAct),
+                              FA(advN), FA(retT[idx]), FA(olpT[idx]), FA(ovT[idx]), n, H, D, W, hyp["vf"],
+                              hyp["ent"], hyp["clip"], hyp["vfClip"]))
+            pm = arr(ref_call(cpu, "lean_ffi_muon_step_mlp", VP, FA(pm), FA(gg[:P]), H, D, Og, 1.0 / n, hyp["lr"],
+                              hyp["wd"], hyp["mu"], hyp["eps"]))
+    np.savez(os.path.join(OUT, "gauss_update.npz"), pm0=pm0, out=pm, obs=obsT, acts=actsT, adv=advT, ret=retT,
+             olp=olpT, ov=ovT, perm=perm, meta=np.array([NT, D, H, W, E, MB]),
+             hyp=np.array([hyp[x] for x in ("lr", "wd", "mu", "eps", "vf", "ent", "clip", "vfClip")]))
     print("golden fixtures written to", OUT)
 
 

@@ -1,0 +1,177 @@
+"""GPU parity of the wide-action resident update (multi-discrete and Gaussian heads) and of the resident
+MLP Muon step, through the C-ABI, against the reference's own outputs and the pinned oracle.
+
+Bars as for the one-head update: the tight tier (fp32 GEMMs, f32 head arithmetic) within 1e-3 of the f64
+reference over a whole update; the bf16 tier within the reference's 0.2 absolute bar and 15% relative
+Frobenius on the parameter deltas (cosine > 0.99); the f64 Muon step bit for bit."""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import pufferlean_b200 as plb  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def rel(a, b):
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def rel_floor(a, ref, floor=1e-3):
+    return float(np.max(np.abs(a - ref) / (np.abs(ref) + floor)))
+
+
+def _problem(NT, D, H, W, mode, hs, seed, ls_bias=None):
+    g = np.random.default_rng(seed)
+    Oo = (sum(hs) if mode == 1 else 2 * W) + 1
+    P = H * D + H + Oo * H + Oo
+    fan_in = np.r_[np.full(H * D + H, D), np.full(Oo * H + Oo, H)]
+    pm = np.concatenate([g.uniform(-1.0, 1.0, P) / np.sqrt(fan_in), np.zeros(P)])
+    if ls_bias is not None:
+        pm[H * D + H + Oo * H + W:H * D + H + Oo * H + 2 * W] = ls_bias
+    obs = g.uniform(-1, 1, NT * D)
+    if mode == 1:
+        acts = np.stack([g.integers(0, s, NT) for s in hs], axis=1).astype(float).ravel()
+        olp = sum(np.log(np.full(NT, 1.0 / s)) for s in hs) + g.normal(0, 0.1, NT)
+    else:
+        acts = g.standard_normal(NT * W)
+        olp = g.uniform(-6.0, -2.0, NT)
+    adv, ret = g.standard_normal(NT), g.standard_normal(NT)
+    ov = ret + g.normal(0, 0.3, NT)
+    return Oo, P, pm, obs, acts, adv, ret, olp, ov
+
+
+CASES = [(1, [3, 4, 2, 6]), (2, None)]
+
+
+@pytest.mark.parametrize("mode,hs", CASES)
+def test_wide_gradient_tight_vs_oracle(mode, hs):
+    """Summed gradient (no normalisation) of the tight tier against the f64 oracle, value clip on. The
+    Gaussian case puts one log-std bias below the device clamp's lower end -20 (gradient cut there)."""
+    N, D, H = 700, 20, 64
+    W = len(hs) if hs else 3
+    Oo, P, pm, obs, acts, adv, ret, olp, ov = _problem(N, D, H, W, mode, hs, 3 + mode,
+                                                       ls_bias=[-0.3, 0.4, -25.0] if mode == 2 else None)
+    g = plb.cuda_mlp_ppo_grad_wide(pm[:P], obs, acts, adv, ret, olp, ov, N, H, D, Oo, W, mode, hs, 0.5, 0.01, 0.2,
+                                   0.2, 0)
+    ref, _, _ = O.mlp_ppo_grad_wide(pm[:P], obs, acts, adv, ret, olp, N, D, H, Oo, W, mode, hs=hs, ov=ov, vfClip=0.2,
+                                    lsLo=-20.0)
+    assert rel(g, ref) < 1e-5, rel(g, ref)
+    assert rel_floor(g, ref) < 2e-3, rel_floor(g, ref)
+
+
+@pytest.mark.parametrize("mode,hs", CASES)
+def test_wide_gradient_bf16_vs_oracle(mode, hs):
+    """The tcgen05 tier: each parameter block within 3e-2 relative Frobenius of the f64 oracle (a chain of
+    three bf16 GEMMs per block, as for the one-head gradient)."""
+    N, D, H = 3000, 50, 256
+    W = len(hs) if hs else 4
+    Oo, P, pm, obs, acts, adv, ret, olp, ov = _problem(N, D, H, W, mode, hs, 13 + mode)
+    g = plb.cuda_mlp_ppo_grad_wide(pm[:P], obs, acts, adv, ret, olp, None, N, H, D, Oo, W, mode, hs, 0.5, 0.01, 0.2,
+                                   0.0, 1)
+    ref, _, _ = O.mlp_ppo_grad_wide(pm[:P], obs, acts, adv, ret, olp, N, D, H, Oo, W, mode, hs=hs, lsLo=-20.0)
+    offs = [0, H * D, H * D + H, H * D + H + Oo * H, P]
+    for a, b in zip(offs[:-1], offs[1:]):
+        assert rel(g[a:b], ref[a:b]) < 3e-2, (a, b, rel(g[a:b], ref[a:b]))
+
+
+def _update(pm, P, obs, acts, adv, ret, olp, ov, perm, hs, NT, D, H, Oo, W, mode, E, MB, bf16, lr=0.02, maxgn=0.5):
+    h = plb.policy_load(pm, P)
+    try:
+        p0 = plb.cuda_train_update_wide_resident(h, obs, acts, adv, ret, olp, ov, perm, hs, NT, D, H, Oo, W, mode, E, MB,
+                                                 lr, 0.001, 0.95, 1e-7, 0.5, 0.01, 0.2, 0.2, maxgn, bf16)
+        out = plb.policy_download(h, P)
+    finally:
+        plb.policy_free(h)
+    assert p0[0] == out[0]
+    return out
+
+
+def test_gauss_update_against_reference_composition():
+    """The Gaussian golden update (composed from the reference's C: lean_ffi_gauss_ppo_grad_batch_vclip and
+    lean_ffi_muon_step_mlp over 2 epochs x 4 minibatches) through pl_train_update_wide_resident."""
+    f = np.load(os.path.join(GOLD, "gauss_update.npz"))
+    NT, D, H, W, E, MB = (int(x) for x in f["meta"])
+    lr, wd, mu, eps, vf, ent, clip, vfc = f["hyp"]
+    Oo = 2 * W + 1
+    P = H * D + H + Oo * H + Oo
+    h = plb.policy_load(f["pm0"], P)
+    try:
+        plb.cuda_train_update_wide_resident(h, f["obs"], f["acts"], f["adv"], f["ret"], f["olp"], f["ov"], f["perm"],
+                                            None, NT, D, H, Oo, W, 2, E, MB, lr, wd, mu, eps, vf, ent, clip, vfc, 0.0, 0)
+        out = plb.policy_download(h, P)
+    finally:
+        plb.policy_free(h)
+    ref = f["out"]
+    assert np.abs(out - ref).max() < 1e-3, np.abs(out - ref).max()
+    assert rel(out[:P] - f["pm0"][:P], ref[:P] - f["pm0"][:P]) < 1e-3
+
+
+@pytest.mark.parametrize("mode,hs", CASES)
+def test_wide_update_tight_vs_oracle(mode, hs):
+    NT, D, H, E, MB = 1024, 20, 96, 2, 4
+    W = len(hs) if hs else 3
+    Oo, P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, W, mode, hs, 23 + mode)
+    perm = O.shuffle_perm(NT, E, 91)
+    ref = O.train_update_wide(pm, obs, acts, adv, ret, olp, perm, NT, D, H, Oo, W, mode, E, MB, hs=hs, ov=ov, lr=0.02,
+                              wd=0.001, vfClip=0.2, maxGradNorm=0.5)
+    got = _update(pm, P, obs, acts, adv, ret, olp, ov, perm, hs, NT, D, H, Oo, W, mode, E, MB, 0)
+    assert np.abs(got - ref).max() < 1e-3, np.abs(got - ref).max()
+    assert rel(got[:P] - pm[:P], ref[:P] - pm[:P]) < 1e-3
+
+
+@pytest.mark.parametrize("mode,hs", CASES)
+def test_wide_update_bf16_vs_oracle(mode, hs):
+    NT, D, H, E, MB = 2048, 20, 192, 1, 2
+    W = len(hs) if hs else 3
+    Oo, P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, W, mode, hs, 33 + mode)
+    perm = O.shuffle_perm(NT, E, 92)
+    ref = O.train_update_wide(pm, obs, acts, adv, ret, olp, perm, NT, D, H, Oo, W, mode, E, MB, hs=hs, ov=ov, lr=0.02,
+                              wd=0.001, vfClip=0.2, maxGradNorm=0.5)
+    got = _update(pm, P, obs, acts, adv, ret, olp, ov, perm, hs, NT, D, H, Oo, W, mode, E, MB, 1)
+    assert np.abs(got - ref).max() < 0.2
+    dg, dr = got[:P] - pm[:P], ref[:P] - pm[:P]
+    assert rel(dg, dr) < 0.15, rel(dg, dr)
+    assert float(dg @ dr / (np.linalg.norm(dg) * np.linalg.norm(dr))) > 0.99
+
+
+def test_wide_bf16_update_is_deterministic():
+    NT, D, H, E, MB, hs = 4096, 33, 128, 2, 4, [5, 3, 7]
+    Oo, P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, 3, 1, hs, 7)
+    perm = O.shuffle_perm(NT, E, 93)
+    a = _update(pm, P, obs, acts, adv, ret, olp, ov, perm, hs, NT, D, H, Oo, 3, 1, E, MB, 1)
+    b = _update(pm, P, obs, acts, adv, ret, olp, ov, perm, hs, NT, D, H, Oo, 3, 1, E, MB, 1)
+    assert np.array_equal(a, b)
+
+
+def test_muon_step_mlp_resident_bit_exact():
+    """pl_muon_step_mlp_resident against lean_ffi_muon_step_mlp (the reference's muonStepMlpBlasFFI) on its
+    golden: new params and momentum, bit for bit; and a second step with weight decay against the oracle."""
+    f = np.load(os.path.join(GOLD, "muon_cpu.npz"))
+    H, D, Oo, gscale, lr, wd, mu, eps = f["meta"]
+    H, D, Oo = int(H), int(D), int(Oo)
+    P = f["params"].size
+    h = plb.policy_load(np.concatenate([f["params"], f["mom"]]), P)
+    try:
+        newp = plb.cuda_muon_step_mlp_resident(h, f["grad"], H, D, Oo, gscale, lr, wd, mu, eps)
+        pm = plb.policy_download(h, P)
+        assert np.array_equal(newp, f["out"][:P])
+        assert np.array_equal(pm, f["out"])
+        g2 = np.random.default_rng(4).standard_normal(P)
+        plb.cuda_muon_step_mlp_resident(h, g2, H, D, Oo, 0.25, 0.05, 0.01, 0.9, 1e-7)
+        pm2 = plb.policy_download(h, P)
+    finally:
+        plb.policy_free(h)
+    ref = O.apply_muon(f["out"], g2 * 0.25, D, H, Oo - 1, 1, 0.05, 0.01, 0.9, 1e-7)
+    assert np.array_equal(pm2, ref)
