@@ -506,6 +506,119 @@ def measure_ns_c3(reps=5):
             "frac": tf / (burst or peak_tf), "peak_kind": kind + " (bf16 burst)"}
 
 
+WIDE = dict(N=8192, T=64, D=128, H=512, Nmb=65536, epochs=4, lr=0.02)
+
+
+def measure_wide(args, mode, cpu=True):
+    """The wide-action resident update (ffi/puffercuda.cu:1307-1409): one hidden ReLU layer, 8 multi-discrete
+    heads of 6 (mode 1, O = 49) or 16 Gaussian dims (mode 2, O = 33); 8192 envs x 64 steps, 4 epochs of
+    65,536-row minibatches, value clip and grad-norm clip on. Device leg: the pl_update session with resident
+    columns; e2e leg: pl_train_update_wide_resident with host columns (uploads inside the timed region);
+    cpu leg: the f64 oracle on one 2,048-row minibatch."""
+    import torch
+
+    import pufferlean_b200 as plb
+
+    L = plb.lib()
+    dp, vp = C.POINTER(C.c_double), C.c_void_p
+    L.pl_update_create.argtypes = [C.c_size_t, C.POINTER(Desc), C.POINTER(vp)]
+    L.pl_update_set_head.argtypes = [vp, C.c_int, C.c_size_t, dp]
+    L.pl_update_set_columns_dev.argtypes = [vp] * 9
+    L.pl_update_run.argtypes = [vp, C.c_double, vp]
+    L.pl_update_profile.argtypes = [vp, C.c_int]
+    L.pl_update_profile_read.argtypes = [vp, dp, dp, dp]
+    L.pl_update_destroy.argtypes = [vp]
+    w = WIDE
+    NT, D, H, E, Nmb = w["N"] * w["T"], w["D"], w["H"], w["epochs"], w["Nmb"]
+    numMB = NT // Nmb
+    hs = [6] * 8 if mode == 1 else None
+    W = 8 if mode == 1 else 16
+    Oo = (sum(hs) if mode == 1 else 2 * W) + 1
+    P = H * D + H + Oo * H + Oo
+    rng = np.random.default_rng(0x1D + mode)
+    fan = np.r_[np.full(H * D + H, D), np.full(Oo * H + Oo, H)]
+    pm = np.concatenate([rng.uniform(-1, 1, P) / np.sqrt(fan), np.zeros(P)])
+    obs = rng.standard_normal(NT * D).astype(np.float32)
+    if mode == 1:
+        acts = rng.integers(0, 6, NT * W).astype(np.float64)
+        olp = np.full(NT, 8 * np.log(1 / 6)) + 0.05 * rng.standard_normal(NT)
+    else:
+        acts = rng.standard_normal(NT * W)
+        olp = -W * 0.5 * np.log(2 * np.pi * np.e) + 0.05 * rng.standard_normal(NT)
+    adv, ret = rng.standard_normal(NT), rng.standard_normal(NT)
+    ov = ret + 0.3 * rng.standard_normal(NT)
+    perm = plb.shuffle_perm(NT, E, 0x31DE)
+    hsa = np.ascontiguousarray(np.array(hs if hs else [0] * W, dtype=np.float64))
+    hyp = dict(wd=0.0, mu=0.95, eps=1e-7, vf=0.5, ent=0.01, clip=0.2, vfClip=0.2, maxgn=0.5)
+    handle = plb.policy_load(pm, P)
+    dev = {k: torch.from_numpy(np.ascontiguousarray(v)).cuda()
+           for k, v in dict(obs=obs, acts=acts, adv=adv, ret=ret, olp=olp, ov=ov, perm=perm).items()}
+    desc = Desc(NT=NT, D=D, H=H, A=Oo - 1, epochs=E, numMB=numMB, arch=Arch(1, 0, None, 0), wd=hyp["wd"],
+                mu=hyp["mu"], eps=hyp["eps"], vfCoef=hyp["vf"], entCoef=hyp["ent"], clipEps=hyp["clip"],
+                vfClip=hyp["vfClip"], maxGradNorm=hyp["maxgn"], bf16=1, use_old_values=1, rank=0, world=1, comm=None)
+    u = vp()
+    check(L.pl_update_create(handle, C.byref(desc), C.byref(u)), L)
+    check(L.pl_update_set_head(u, mode, W, hsa.ctypes.data_as(dp)), L)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step():
+        check(L.pl_update_set_columns_dev(u, dev["obs"].data_ptr(), dev["acts"].data_ptr(), dev["adv"].data_ptr(),
+                                          dev["ret"].data_ptr(), dev["olp"].data_ptr(), dev["ov"].data_ptr(),
+                                          dev["perm"].data_ptr(), stream), L)
+        check(L.pl_update_run(u, w["lr"], stream), L)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    check(L.pl_update_profile(u, 1), L)
+    l0 = L.pl_kernel_launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            step()
+        ev1.record()
+        torch.cuda.synchronize()
+    launches = L.pl_kernel_launch_count() - l0
+    ms = ev0.elapsed_time(ev1) / args.steps
+    pms, pfl, pln = (C.c_double * 8)(), (C.c_double * 8)(), (C.c_double * 8)()
+    check(L.pl_update_profile_read(u, pms, pfl, pln), L)
+    L.pl_update_destroy(u)
+    gemm_ms, gemm_fl = sum(pms[i] for i in range(4)), sum(pfl[i] for i in range(4))
+    peak_tf, _, kind = peaks()
+    achieved = gemm_fl / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
+    # e2e: the reference-shaped call with host columns (obs uploaded as f64, as that entry point takes it)
+    obs64 = obs.astype(np.float64)
+    args_h = (obs64, acts, adv, ret, olp, ov, perm, hs, NT, D, H, Oo, W, mode, E, numMB, w["lr"], hyp["wd"], hyp["mu"],
+              hyp["eps"], hyp["vf"], hyp["ent"], hyp["clip"], hyp["vfClip"], hyp["maxgn"], 1)
+    plb.cuda_train_update_wide_resident(handle, *args_h)
+    reps = max(1, min(args.steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        plb.cuda_train_update_wide_resident(handle, *args_h)
+    e2e_s = (time.perf_counter() - t0) / reps
+    plb.policy_free(handle)
+    out = {"workload": ("wide heads: 8 multi-discrete x 6" if mode == 1 else "wide heads: 16 Gaussian dims") +
+           f", MLP {D}->{H}->{Oo} ReLU, {w['N']} envs x {w['T']}, {E} epochs x {numMB} minibatches",
+           "unit": "samples/s", "value": NT * E / (ms / 1e3), "ms_per_update": ms,
+           "e2e": {"value": NT * E / e2e_s, "unit": "samples/s", "ms_per_update": e2e_s * 1e3,
+                   "h2d_bytes_per_step": 8 * (NT * (D + W + 4) + E * NT) + 8 * W},
+           "gemm_tflops": achieved, "gemm_frac": achieved / peak_tf if peak_tf else None,
+           "gemm_ms_per_update": gemm_ms / args.steps, "peak_kind": kind + " (bf16 sustained)",
+           "gpu_launches_per_update": launches / args.steps, "clocks": clk.summary()}
+    if cpu:
+        from oracle import oracle as O
+        n = 2048
+        idx = np.arange(n)
+        t0 = time.perf_counter()
+        O.train_update_wide(pm, obs64[:n * D], acts[:n * W], adv[:n], ret[:n], olp[:n], idx.astype(np.float64), n, D,
+                            H, Oo, W, mode, 1, 1, hs=hs, ov=ov[:n], lr=w["lr"], vfClip=0.2, maxGradNorm=0.5)
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": n / dt, "unit": "samples/s", "cores": 1, "kind": "port",
+                               "sample": f"one {n}-row minibatch (gradient + clip + Muon), f64 oracle"}
+    return out
+
+
 def mingru_init_pm(D, H, L, A, K, seed):
     """[params; mom] in the flattenMG layout, Kaiming-uniform bounds of initMinGRU
     (Puffer/RL/MinGRUTrain.lean:311-344: sqrt(2)/sqrt(D) encoder, 1/sqrt(H) elsewhere, biases zero),
@@ -767,9 +880,10 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the configs[1] / configs[2] kernel measurements")
     ap.add_argument("--drift", type=int, default=0, metavar="U",
                     help="print the loss-curve drift of U consecutive updates against the f64 oracle and exit")
-    ap.add_argument("--only", choices=["c2", "c3", "c4", "c4r"],
+    ap.add_argument("--only", choices=["c2", "c3", "c4", "c4r", "wide1", "wide2"],
                     help="print only the configs[1] (c2), configs[2] (c3) or configs[3] (c4: K=2 + GELU encoder; "
-                         "c4r: the reference's K=3 linear-encoder net) measurement")
+                         "c4r: the reference's K=3 linear-encoder net) measurement, or the wide-head update "
+                         "(wide1 multi-discrete, wide2 Gaussian)")
     args = ap.parse_args()
     if args.drift:
         print(json.dumps(measure_drift(args.drift)), flush=True)
@@ -779,6 +893,8 @@ def main():
             res = measure_mingru_c4(args, cpu=not args.no_cpu)
         elif args.only == "c4r":
             res = measure_mingru_c4(args, K=3, enc_act=0, cpu=not args.no_cpu)
+        elif args.only in ("wide1", "wide2"):
+            res = measure_wide(args, int(args.only[-1]), cpu=not args.no_cpu)
         else:
             res = measure_vtrace_c2() if args.only == "c2" else measure_ns_c3()
         print(json.dumps(res), flush=True)

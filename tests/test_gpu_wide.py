@@ -71,19 +71,80 @@ def test_wide_gradient_tight_vs_oracle(mode, hs):
     assert rel_floor(g, ref) < 2e-3, rel_floor(g, ref)
 
 
+def _bf(a):
+    return torch.tensor(a).to(torch.bfloat16).to(torch.float64).numpy()
+
+
+def _emulate_bf16_tier(p, obs, acts, adv, ret, olp, N, D, H, Oo, W, mode, hs, vf=0.5, ent=0.01, clip=0.2, lsLo=-20.0):
+    """The bf16 tier's rounding points on f64 arithmetic: observations and weights in bf16, hidden
+    activations stored in bf16, fp32 logits, the row gradient dOut stored in bf16, the masked hidden
+    gradient stored in bf16 (its column sum taken before rounding), f64 accumulation elsewhere."""
+    W1 = p[:H * D].reshape(H, D)
+    b1 = p[H * D:H * D + H]
+    W2 = p[H * D + H:H * D + H + Oo * H].reshape(Oo, H)
+    b2 = p[H * D + H + Oo * H:]
+    X = _bf(obs.reshape(N, D))
+    Z = X @ _bf(W1).T + b1
+    Hh = _bf(np.maximum(Z, 0.0))
+    out = Hh @ _bf(W2).T + b2
+    a = acts.reshape(N, W)
+    dout = np.zeros((N, Oo))
+    rows = np.arange(N)
+    if mode == 1:
+        logp, off, heads = np.zeros(N), 0, []
+        for h, sz in enumerate(hs):
+            z = out[:, off:off + sz]
+            lse = np.log(np.exp(z).sum(1))
+            logp += z[rows, a[:, h].astype(int)] - lse
+            heads.append((h, off, sz, z, lse))
+            off += sz
+    else:
+        ls = np.clip(out[:, W:2 * W], lsLo, 2.0)
+        zz = (a - out[:, :W]) * np.exp(-ls)
+        logp = (-0.5 * zz * zz - ls - 0.5 * np.log(2 * np.pi)).sum(1)
+    r = np.exp(logp - olp)
+    rc = np.clip(r, 1 - clip, 1 + clip)
+    dpol = np.where(adv * r <= adv * rc, adv * r, adv * ((1 - clip < r) & (r < 1 + clip)) * r)
+    if mode == 1:
+        for h, off, sz, z, lse in heads:
+            pk = np.exp(z - lse[:, None])
+            onehot = np.zeros_like(z)
+            onehot[rows, a[:, h].astype(int)] = 1.0
+            dout[:, off:off + sz] = dpol[:, None] * (onehot - pk) + ent * pk * ((pk * z).sum(1)[:, None] - z)
+    else:
+        raw = out[:, W:2 * W]
+        dout[:, :W] = dpol[:, None] * zz * np.exp(-ls)
+        dout[:, W:2 * W] = ((lsLo < raw) & (raw < 2.0)) * (dpol[:, None] * (zz * zz - 1.0) + ent)
+    dout[:, -1] = -vf * (out[:, -1] - ret)
+    dO = _bf(dout)
+    dH = (dO @ _bf(W2)) * (Z > 0)
+    dZ = _bf(dH)
+    return np.concatenate([(dZ.T @ X).ravel(), dH.sum(0), (dO.T @ Hh).ravel(), dout.sum(0)])
+
+
 @pytest.mark.parametrize("mode,hs", CASES)
 def test_wide_gradient_bf16_vs_oracle(mode, hs):
-    """The tcgen05 tier: each parameter block within 3e-2 relative Frobenius of the f64 oracle (a chain of
-    three bf16 GEMMs per block, as for the one-head gradient)."""
+    """The tcgen05 tier against (a) a bf16 emulation of its rounding points, within 1e-2 relative
+    Frobenius per parameter block, and (b) the f64 oracle: the rounding alone puts the first layer's
+    gradients (W1 and b1, sums over 3000 rows that largely cancel) 3-4% from f64 on these rows, a figure
+    the emulation reproduces, so their bar is 5e-2; the head layer keeps 3e-2. The old log-probs sit within 0.1 of
+    the new ones, so no ratio lies on a clip edge, where any rounding of the joint log-prob switches a
+    row between its gradient and zero (the whole-update tests keep such rows)."""
     N, D, H = 3000, 50, 256
     W = len(hs) if hs else 4
     Oo, P, pm, obs, acts, adv, ret, olp, ov = _problem(N, D, H, W, mode, hs, 13 + mode)
+    _, nl, _ = O.mlp_ppo_grad_wide(pm[:P], obs, acts, adv, ret, olp, N, D, H, Oo, W, mode, hs=hs, lsLo=-20.0)
+    olp = nl + np.random.default_rng(17).uniform(-0.1, 0.1, N)
     g = plb.cuda_mlp_ppo_grad_wide(pm[:P], obs, acts, adv, ret, olp, None, N, H, D, Oo, W, mode, hs, 0.5, 0.01, 0.2,
                                    0.0, 1)
     ref, _, _ = O.mlp_ppo_grad_wide(pm[:P], obs, acts, adv, ret, olp, N, D, H, Oo, W, mode, hs=hs, lsLo=-20.0)
+    emu = _emulate_bf16_tier(pm[:P], obs, acts, adv, ret, olp, N, D, H, Oo, W, mode, hs)
     offs = [0, H * D, H * D + H, H * D + H + Oo * H, P]
-    for a, b in zip(offs[:-1], offs[1:]):
-        assert rel(g[a:b], ref[a:b]) < 3e-2, (a, b, rel(g[a:b], ref[a:b]))
+    blocks = list(zip(offs[:-1], offs[1:]))
+    to_emu = [rel(g[a:b], emu[a:b]) for a, b in blocks]
+    to_ref = [rel(g[a:b], ref[a:b]) for a, b in blocks]
+    assert max(to_emu) < 1e-2, to_emu
+    assert to_ref[0] < 5e-2 and to_ref[1] < 5e-2 and max(to_ref[2:]) < 3e-2, to_ref
 
 
 def _update(pm, P, obs, acts, adv, ret, olp, ov, perm, hs, NT, D, H, Oo, W, mode, E, MB, bf16, lr=0.02, maxgn=0.5):
