@@ -57,6 +57,18 @@ lean_obj_res lean_cuda_train_update_resident_deep(size_t handle, lean_obj_arg ob
                                                   double lr, double wd, double mu, double eps, double vf, double ent,
                                                   double clip, double vfClip, double maxGradNorm, uint8_t bf16,
                                                   lean_obj_arg w);
+/* cudaTrainUpdateWideResidentFFI, CUDA.lean:259-262; replaces ffi/puffercuda.cu:1307-1409 (multi-discrete / Gaussian heads) */
+lean_obj_res lean_cuda_train_update_wide_resident(size_t handle, lean_obj_arg obs, lean_obj_arg acts, lean_obj_arg adv,
+                                                  lean_obj_arg ret, lean_obj_arg olp, lean_obj_arg ov,
+                                                  lean_obj_arg perm, lean_obj_arg hs, size_t NT, size_t D, size_t H,
+                                                  size_t O, size_t W, uint32_t mode, size_t epochs, size_t numMB,
+                                                  double lr, double wd, double mu, double eps, double vf, double ent,
+                                                  double clip, double vfClip, double maxGradNorm, uint8_t bf16,
+                                                  lean_obj_arg w);
+/* cudaMuonStepMlpResidentFFI, CUDA.lean:287-289; replaces ffi/puffercuda.cu:5985-6020 */
+lean_obj_res lean_cuda_muon_step_mlp_resident(size_t handle, lean_obj_arg gRaw, size_t H, size_t D, size_t O,
+                                              double gscale, double lr, double wd, double mu, double eps,
+                                              lean_obj_arg w);
 /* cudaMgLossEnableFFI / cudaMgReadLossesFFI, CUDA.lean:165-178; replace ffi/puffercuda.cu:336-352 */
 lean_obj_res lean_cuda_mg_loss_enable(uint8_t on, lean_obj_arg w);
 lean_obj_res lean_cuda_mg_read_losses(lean_obj_arg w);

@@ -390,6 +390,8 @@ def ref_call(lib, name, restype, *args):
             conv.append(C.c_double(a))
         elif isinstance(a, tuple) and a[0] == "u64":
             conv.append(C.c_uint64(a[1]))
+        elif isinstance(a, tuple) and a[0] == "u32":
+            conv.append(C.c_uint32(a[1]))
         elif isinstance(a, tuple) and a[0] == "u8":
             conv.append(C.c_uint8(a[1]))
         elif isinstance(a, tuple) and a[0] == "obj":

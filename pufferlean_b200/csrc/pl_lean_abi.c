@@ -213,6 +213,56 @@ LEAN_EXPORT lean_obj_res lean_cuda_train_update_resident_deep(size_t handle, lea
   return lean_io_result_mk_ok(out);
 }
 
+/* Wide action heads: W multi-discrete heads (mode 1, sizes in hs) or W Gaussian dims (mode 2) on the
+ * resident one-hidden-layer policy; O = sum(hs)+1 or 2W+1, acts NT x W. Returns [params[0]] like
+ * lean_cuda_train_update_resident. */
+LEAN_EXPORT lean_obj_res lean_cuda_train_update_wide_resident(size_t handle, lean_obj_arg obs, lean_obj_arg acts,
+                                                              lean_obj_arg adv, lean_obj_arg ret, lean_obj_arg olp,
+                                                              lean_obj_arg ov, lean_obj_arg perm, lean_obj_arg hs,
+                                                              size_t NT, size_t D, size_t H, size_t O, size_t W,
+                                                              uint32_t mode, size_t epochs, size_t numMB, double lr,
+                                                              double wd, double mu, double eps, double vf, double ent,
+                                                              double clip, double vfClip, double maxGradNorm,
+                                                              uint8_t bf16, lean_obj_arg w) {
+  (void)w;
+  lean_obj_res out = new_fa(1);
+  const double* hsp = fan(hs) >= W ? fa(hs) : NULL;
+  int rc = pl_train_update_wide_resident(handle, fa(obs), fa(acts), fa(adv), fa(ret), fa(olp), fa(ov), fan(ov),
+                                         fa(perm), hsp, NT, D, H, O, W, mode, epochs, numMB, lr, wd, mu, eps, vf, ent,
+                                         clip, vfClip, maxGradNorm, bf16, fa(out));
+  lean_dec(obs);
+  lean_dec(acts);
+  lean_dec(adv);
+  lean_dec(ret);
+  lean_dec(olp);
+  lean_dec(ov);
+  lean_dec(perm);
+  lean_dec(hs);
+  if (rc) {
+    lean_dec(out);
+    return io_fail("lean_cuda_train_update_wide_resident");
+  }
+  return lean_io_result_mk_ok(out);
+}
+
+/* In-place f64 Muon of the resident [W1|b1|W2|b2] from the raw summed gradient gRaw (scaled by gscale);
+ * returns the new params (P). */
+LEAN_EXPORT lean_obj_res lean_cuda_muon_step_mlp_resident(size_t handle, lean_obj_arg gRaw, size_t H, size_t D,
+                                                          size_t O, double gscale, double lr, double wd, double mu,
+                                                          double eps, lean_obj_arg w) {
+  (void)w;
+  const size_t P = H * D + H + O * H + O;
+  lean_obj_res out = new_fa(P);
+  int rc = fan(gRaw) >= P ? pl_muon_step_mlp_resident(handle, fa(gRaw), H, D, O, gscale, lr, wd, mu, eps, fa(out))
+                          : PL_ERR_INVALID;
+  lean_dec(gRaw);
+  if (rc) {
+    lean_dec(out);
+    return io_fail("lean_cuda_muon_step_mlp_resident");
+  }
+  return lean_io_result_mk_ok(out);
+}
+
 /* ---------------------------------------------------------------- dashboard losses (CUDA.lean:165-178) */
 LEAN_EXPORT lean_obj_res lean_cuda_mg_loss_enable(uint8_t on, lean_obj_arg w) {
   (void)w;

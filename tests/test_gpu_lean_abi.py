@@ -68,6 +68,45 @@ def test_lean_resident_policy_round_trip(lib):
     assert O.ctor_tag(r) == 0
 
 
+def _lean_handle(lib, pm, P):
+    r = O.ref_call(lib, "lean_cuda_policy_load", VP, FA(pm), P, ("obj", 1))
+    assert O.ctor_tag(r) == 0
+    return int.from_bytes(C.string_at(O.ctor_field(r, 0) + 8, 8), "little")
+
+
+def test_lean_wide_resident_gauss_golden(lib):
+    """lean_cuda_train_update_wide_resident (mode 2) on the Gaussian golden update composed from the
+    reference's C, then lean_cuda_muon_step_mlp_resident on the reference's muonStepMlpBlasFFI golden."""
+    f = np.load(os.path.join(GOLD, "gauss_update.npz"))
+    NT, D, H, W, E, MB = (int(x) for x in f["meta"])
+    lr, wd, mu, eps, vf, ent, clip, vfc = f["hyp"]
+    Oo = 2 * W + 1
+    P = H * D + H + Oo * H + Oo
+    handle = _lean_handle(lib, f["pm0"], P)
+    r = O.ref_call(lib, "lean_cuda_train_update_wide_resident", VP, handle, FA(f["obs"]), FA(f["acts"]), FA(f["adv"]),
+                   FA(f["ret"]), FA(f["olp"]), FA(f["ov"]), FA(f["perm"]), FA(np.zeros(0)), NT, D, H, Oo, W, ("u32", 2),
+                   E, MB, lr, wd, mu, eps, vf, ent, clip, vfc, 0.0, ("u8", 0), ("obj", 1))
+    assert O.ctor_tag(r) == 0
+    p0 = O.read_float_array(O.ctor_field(r, 0))
+    pm = O.read_float_array(O.ctor_field(O.ref_call(lib, "lean_cuda_policy_download", VP, handle, P, ("obj", 1)), 0))
+    assert p0[0] == pm[0]
+    assert np.abs(pm - f["out"]).max() < 1e-3
+    O.ref_call(lib, "lean_cuda_policy_free", VP, handle, ("obj", 1))
+
+    m = np.load(os.path.join(GOLD, "muon_cpu.npz"))
+    H, D, Oo, gscale, lr, wd, mu, eps = m["meta"]
+    H, D, Oo = int(H), int(D), int(Oo)
+    P = m["params"].size
+    handle = _lean_handle(lib, np.concatenate([m["params"], m["mom"]]), P)
+    r = O.ref_call(lib, "lean_cuda_muon_step_mlp_resident", VP, handle, FA(m["grad"]), H, D, Oo, gscale, lr, wd, mu, eps,
+                   ("obj", 1))
+    assert O.ctor_tag(r) == 0
+    assert np.array_equal(O.read_float_array(O.ctor_field(r, 0)), m["out"][:P])
+    pm = O.read_float_array(O.ctor_field(O.ref_call(lib, "lean_cuda_policy_download", VP, handle, P, ("obj", 1)), 0))
+    assert np.array_equal(pm, m["out"])
+    O.ref_call(lib, "lean_cuda_policy_free", VP, handle, ("obj", 1))
+
+
 def _mg_lean_inputs():
     from oracle import kat
 
