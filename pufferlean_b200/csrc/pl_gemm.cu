@@ -13,8 +13,17 @@ namespace pl {
 using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, int, int,
                            int, EpiArgs);
 
-// Instance tables live in the pl_gemm_inst_*.cu translation units.
+// Instance tables live in pl_gemm_inst.cu (single CTAs) and pl_gemm_pair_inst.cu (CTA pairs).
 GemmKernel gemm_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
+GemmKernel gemm_pair_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
+
+// 0: single CTAs only; 1: CTA pairs for 256-wide tiles of at least 256 rows (default).
+static int g_pair_mode = 1;
+int gemm_set_pair_mode(int mode) {
+  const int prev = g_pair_mode;
+  if (mode >= 0) g_pair_mode = mode ? 1 : 0;
+  return prev;
+}
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -77,14 +86,17 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
   PL_REQUIRE(b_mn ? (B.rows >= K && B.cols >= N) : (B.rows >= N && B.cols >= K), PL_ERR_INVALID,
              "GEMM B storage %ldx%ld too small for N=%d K=%d", B.rows, B.cols, N, K);
   uint32_t smem = 0;
-  GemmKernel k = gemm_instance(bn, epi, a_mn, b_mn, &smem);
+  GemmKernel k = nullptr;
+  const bool pair = g_pair_mode == 1 && bn == 256 && epi != EPI_PPO && M > 128 &&
+                    (k = gemm_pair_instance(bn, epi, a_mn, b_mn, &smem)) != nullptr;
+  if (!pair) k = gemm_instance(bn, epi, a_mn, b_mn, &smem);
   PL_REQUIRE(k != nullptr, PL_ERR_UNSUPPORTED, "no GEMM instance bn=%d epi=%d a_mn=%d b_mn=%d", bn, epi, (int)a_mn,
              (int)b_mn);
   if (epi == EPI_PPO) PL_REQUIRE(N <= bn, PL_ERR_INVALID, "PPO head needs all %d outputs in one tile (bn=%d)", N, bn);
   CUtensorMap ma, mb;
   int rc = make_map(&ma, A, a_mn ? 64 : 128);
   if (rc) return rc;
-  rc = make_map(&mb, B, b_mn ? 64 : (uint32_t)bn);
+  rc = make_map(&mb, B, b_mn ? 64 : (uint32_t)(pair ? bn / 2 : bn));  // a pair CTA loads half of B's rows
   if (rc) return rc;
   EpiArgs ep = ep_in;
   if (!ep.err) ep.err = device_error_word();
@@ -107,9 +119,17 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && num_sms[dev] == 0) cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-  const long tiles = ceil_div(N, bn) * ceil_div(M, 128) * (long)(splits > 1 ? splits : batch);
   const int sms = (dev >= 0 && dev < 64 && num_sms[dev] > 0) ? num_sms[dev] : 148;
-  dim3 grid((unsigned)(tiles < sms ? tiles : sms), 1, 1);
+  dim3 grid;
+  if (pair) {
+    // one cluster of two CTAs per pair tile of 256 rows, at most one CTA per SM
+    const long ptiles = ceil_div(N, bn) * ceil_div(M, 256) * (long)(splits > 1 ? splits : batch);
+    const long pairs = ptiles < sms / 2 ? ptiles : sms / 2;
+    grid = dim3((unsigned)(2 * pairs), 1, 1);
+  } else {
+    const long tiles = ceil_div(N, bn) * ceil_div(M, 128) * (long)(splits > 1 ? splits : batch);
+    grid = dim3((unsigned)(tiles < sms ? tiles : sms), 1, 1);
+  }
   static std::mutex mu;
   {
     std::lock_guard<std::mutex> g(mu);

@@ -740,6 +740,226 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
+// ---------------------------------------------------------------- CTA-pair variant
+// The same GEMM on clusters of two CTAs (the two SMs of a pair) with cta_group::2 MMAs: a pair tile is
+// 256 x BN, CTA r of the pair holds A rows [128 r, 128 r + 128) and B rows (the N side)
+// [BN/2 r, BN/2 r + BN/2) of every k-block, and receives accumulator rows [128 r, 128 r + 128) in its
+// own TMEM. Per SM that is BN/2 instead of BN B rows per k-block, so each SM moves a third fewer
+// operand bytes per flop and its shared-memory ring covers more k-blocks in flight.
+//   barriers: full[s] lives in the even CTA (armed there with both halves' bytes; both CTAs' loads
+//   report to it); empty[s] and acc_full[b] exist in both CTAs and are released by the even CTA's MMA
+//   thread, which commits to each; acc_empty[b] lives in the even CTA and counts the epilogue warps
+//   of both CTAs.
+template <int BN, int EPI>
+struct GemmPairSmem {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t FIXED = GemmSmem<BN, EPI>::FIXED;
+  static constexpr int FIT = (int)((232448 - FIXED) / STAGE_BYTES);
+  static constexpr int STAGES = FIT > 10 ? 10 : FIT;
+  static constexpr uint32_t TOTAL = FIXED + STAGES * STAGE_BYTES;
+  static_assert(STAGES >= 2, "shared memory budget");
+};
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, int M,
+                        int N, int K, EpiArgs ep) {
+  static_assert(EPI != EPI_PPO, "the PPO head runs on single CTAs");
+  static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+  using S = GemmPairSmem<BN, EPI>;
+  constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES, BNH = BN / 2;
+  constexpr uint32_t IDESC = tc::idesc_bf16(2 * BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* full = (uint64_t*)(sB + STAGES * S::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  uint8_t* stg_base = smem + STAGES * S::STAGE_BYTES + 256;
+  float* red = (float*)(stg_base + GemmSmem<BN, EPI>::STG_BYTES);
+  float* rowscr = red + 4 * BN;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = tc::cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_n = (N + BN - 1) / BN, num_m = (M + 2 * BM - 1) / (2 * BM);
+  const int num_z = ep.k_splits > 1 ? ep.k_splits : (ep.nbatch > 1 ? ep.nbatch : 1);
+  const int total_tiles = num_n * num_m * num_z;
+  const int total_kb = (K + BK - 1) / BK;
+  const int per_split = ep.k_splits > 1 ? (total_kb + ep.k_splits - 1) / ep.k_splits : total_kb;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      tc::mbar_init(&acc_full[b], 1);
+      tc::mbar_init(&acc_empty[b], 16);  // one arrival per epilogue warp of both CTAs
+    }
+    *abort_flag = 0;
+    tc::fence_mbar_init();
+    tc::tma_prefetch_desc(&tmA);
+    tc::tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tc::tmem_relinquish_pair();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  __syncwarp();
+  tc::cluster_sync();  // both CTAs' barriers are initialised before either signals the other
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto kb_range = [&](int z, int& b0, int& b1) {
+    if (ep.k_splits > 1) {
+      b0 = z * per_split;
+      b1 = min(total_kb, b0 + per_split);
+      if (b1 < b0) b1 = b0;
+    } else {
+      b0 = 0;
+      b1 = total_kb;
+    }
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer of this CTA's halves; the even CTA arms full[s] for both
+      long it = 0;
+      for (int t = pair; t < total_tiles && !*abort_flag; t += npairs) {
+        const TileIdx ti = tile_of(t, num_n, num_m);
+        const int batch = ep.k_splits > 1 ? 0 : ti.z;
+        const int arow = ti.m * 2 * BM + (int)rank * BM;
+        const int brow = ti.n * BN + (int)rank * BNH;
+        int b0, b1;
+        kb_range(ti.z, b0, b1);
+        for (int kb = b0; kb < b1; kb++, it++) {
+          const int s = (int)(it % STAGES);
+          if (it >= STAGES &&
+              !tc::mbar_wait(&empty[s], (uint32_t)(((it / STAGES) - 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          const int k0 = kb * BK;
+          if (rank == 0) tc::mbar_expect_tx(&full[s], 2 * S::STAGE_BYTES);
+          const uint32_t fb = tc::cluster_addr(tc::smem_u32(&full[s]), 0);
+          uint8_t* a = sA + s * S::A_BYTES;
+          uint8_t* b = sB + s * S::B_BYTES;
+          if (!A_MN) {
+            tc::tma_load_3d_pair(a, &tmA, fb, k0, arow, batch);
+          } else {
+            tc::tma_load_3d_pair(a, &tmA, fb, arow, k0, batch);
+            tc::tma_load_3d_pair(a + 8192, &tmA, fb, arow + 64, k0, batch);
+          }
+          if (!B_MN) {
+            tc::tma_load_3d_pair(b, &tmB, fb, k0, brow, batch);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BNH / 64; j++) tc::tma_load_3d_pair(b + j * 8192, &tmB, fb, brow + 64 * j, k0, batch);
+          }
+        }
+      }
+      // The even CTA's ring drains here: every phase it armed has received both CTAs' bytes.
+      if (rank == 0)
+        for (long i = it - STAGES > 0 ? it - STAGES : 0; i < it; i++)
+          tc::mbar_wait(&full[i % STAGES], (uint32_t)((i / STAGES) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 2);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer of the pair (even CTA, one thread)
+      long it = 0;
+      int j = 0;
+      for (int t = pair; t < total_tiles && !*abort_flag; t += npairs, j++) {
+        const TileIdx ti = tile_of(t, num_n, num_m);
+        int b0, b1;
+        kb_range(ti.z, b0, b1);
+        const int buf = j & 1;
+        if (j >= 2 &&
+            !tc::mbar_wait(&acc_empty[buf], (uint32_t)(((j >> 1) - 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 3)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+        for (int kb = b0; kb < b1; kb++, it++) {
+          const int s = (int)(it % STAGES);
+          if (!tc::mbar_wait(&full[s], (uint32_t)((it / STAGES) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 4)) {
+            *abort_flag = 1;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t a_addr = tc::smem_u32(sA + s * S::A_BYTES);
+          const uint32_t b_addr = tc::smem_u32(sB + s * S::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; kk++) {
+            const uint64_t ad = A_MN ? tc::sw128_desc(a_addr + kk * 2048, 8192, 1024)
+                                     : tc::sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? tc::sw128_desc(b_addr + kk * 2048, 8192, 1024)
+                                     : tc::sw128_desc(b_addr + kk * 32, 16, 1024);
+            tc::umma_bf16_pair(d_tmem, ad, bd, IDESC, (kb > b0 || kk > 0) ? 1u : 0u);
+          }
+          // stage s is free in both CTAs once these MMAs complete
+          const uint32_t e = tc::smem_u32(&empty[s]);
+          tc::umma_commit_pair(tc::cluster_addr(e, 0));
+          tc::umma_commit_pair(tc::cluster_addr(e, 1));
+        }
+        const uint32_t f = tc::smem_u32(&acc_full[buf]);
+        tc::umma_commit_pair(tc::cluster_addr(f, 0));
+        tc::umma_commit_pair(tc::cluster_addr(f, 1));
+      }
+      if (j > 0) tc::mbar_wait(&acc_full[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 5);
+    }
+  } else {
+    // ---------------- epilogue warps 2..9 of each CTA drain its 128 accumulator rows
+    const int sub = warp & 3;
+    const int half = (warp - 2) >> 2;
+    int j = 0;
+    for (int t = pair; t < total_tiles; t += npairs, j++) {
+      const TileIdx ti = tile_of(t, num_n, num_m);
+      int b0, b1;
+      kb_range(ti.z, b0, b1);
+      const int buf = j & 1;
+      const bool ok = tc::mbar_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 6);
+      if (!ok || *abort_flag) {
+        *abort_flag = 1;
+        break;
+      }
+      tc::tc_fence_after();
+      const uint32_t t_row = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(sub * 32) << 16);
+      // a 128-row block wholly past M (odd CTA, M not a multiple of 256) has nothing to write: its
+      // column partials would fall outside the ceil(M / 128) rows the caller provides
+      const int m_blk = ti.m * 2 + (int)rank;
+      if (m_blk * BM < M)
+        epilogue_tile<BN, EPI>(ep, t_row, m_blk, ti.n, ti.z, ep.k_splits > 1 ? 0 : ti.z, b1 > b0, sub, half, lane, red,
+                               rowscr, stg_base + (warp - 2) * GemmSmem<BN, EPI>::STG_WARP, &tmC, &tmC2);
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_remote(tc::cluster_addr(tc::smem_u32(&acc_empty[buf]), 0));
+    }
+    if (lane == 0) tc::bulk_wait<0>();
+    __syncwarp();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  __syncwarp();
+  tc::cluster_sync();  // no CTA leaves while the pair's MMAs or loads may still touch its memory
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 struct Operand {
   const void* ptr;  // bf16
@@ -753,5 +973,8 @@ struct Operand {
 // stored MN-major (storage rows = K) or K-major (storage rows = M or N).
 int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const Operand& B, int M, int N, int K,
                 int batch, const EpiArgs& ep, cudaStream_t st);
+// 0 = single-CTA tiles only, 1 = CTA pairs where eligible (default); a negative mode only queries.
+// Returns the previous mode.
+int gemm_set_pair_mode(int mode);
 
 }  // namespace pl

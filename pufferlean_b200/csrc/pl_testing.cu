@@ -41,6 +41,8 @@ extern "C" int pl_test_gemm(const pl_test_gemm_args* g, void* stream) {
                          g->batch > 1 ? g->batch : 1, ep, (cudaStream_t)stream);
 }
 
+extern "C" int pl_test_gemm_pair_mode(int mode) { return pl::gemm_set_pair_mode(mode); }
+
 extern "C" int pl_test_device_error(unsigned* code) {
   unsigned* w = pl::device_error_word();
   unsigned v = 0;
