@@ -29,9 +29,13 @@ typedef struct {
 
 int pl_test_gemm(const pl_test_gemm_args* g, void* stream);
 /* Selects the GEMM's tile mode for every later launch in this process: 0 = single-CTA tiles only,
- * 1 = CTA pairs (cta_group::2, 256-row tiles) where eligible, the default; a negative mode only
+ * the default, 1 = CTA pairs (cta_group::2, 256-row tiles) where eligible; a negative mode only
  * queries. Returns the previous mode. */
 int pl_test_gemm_pair_mode(int mode);
+/* Selects how the GEMM's staged bf16 epilogues write their tiles for every later launch: 1 = TMA
+ * bulk stores, 2 = coalesced global stores (the default); a non-positive mode only queries. Returns
+ * the previous mode. */
+int pl_test_gemm_store_mode(int mode);
 /* Reads and clears the device-side bounded-wait error word (0 = none). */
 int pl_test_device_error(unsigned* code);
 

@@ -17,11 +17,22 @@ using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensor
 GemmKernel gemm_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
 GemmKernel gemm_pair_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
 
-// 0: single CTAs only; 1: CTA pairs for 256-wide tiles of at least 256 rows (default).
-static int g_pair_mode = 1;
+// 0: single CTAs only (default: on B200 the single-CTA main loop already streams at the MMA rate these
+// shapes allow, and the pair's cluster set-up costs more than its halved B traffic saves); 1: CTA pairs
+// for 256-wide tiles of at least 256 rows.
+static int g_pair_mode = 0;
 int gemm_set_pair_mode(int mode) {
   const int prev = g_pair_mode;
   if (mode >= 0) g_pair_mode = mode ? 1 : 0;
+  return prev;
+}
+
+// Staged bf16 epilogues: 2 = coalesced global stores (default: TMA stores queue behind the main loop's
+// operand loads in the SM's one TMA unit), 1 = TMA bulk stores.
+static int g_store_mode = 2;
+int gemm_set_store_mode(int mode) {
+  const int prev = g_store_mode;
+  if (mode > 0) g_store_mode = mode == 1 ? 1 : 2;
   return prev;
 }
 
@@ -110,7 +121,7 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
     // the staged epilogue reads its aux tile with aligned 16-byte loads
     if (ok && ep.aux && (((uintptr_t)ep.aux & 15) || (ep.ld_aux % 8) || (batch > 1 && (ep.aux_bstride % 8))))
       ok = false;
-    ep.tma_out = ok ? 1 : 0;
+    ep.tma_out = ok ? g_store_mode : 0;
   }
   int splits = ep.k_splits > 1 ? ep.k_splits : 1;
   PL_REQUIRE(splits == 1 || batch == 1, PL_ERR_INVALID, "split-K and batching are exclusive");
