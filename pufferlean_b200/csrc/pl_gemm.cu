@@ -27,9 +27,10 @@ int gemm_set_pair_mode(int mode) {
   return prev;
 }
 
-// Staged bf16 epilogues: 2 = coalesced global stores (default: TMA stores queue behind the main loop's
-// operand loads in the SM's one TMA unit), 1 = TMA bulk stores.
-static int g_store_mode = 2;
+// Staged bf16 epilogues: 1 = TMA bulk stores (default), 2 = coalesced global stores (measured slower on
+// B200 for every shape of the update: the tile still passes through shared memory, whose bandwidth
+// the main loop's operand traffic already uses up, and the global stores add L1 traffic on top).
+static int g_store_mode = 1;
 int gemm_set_store_mode(int mode) {
   const int prev = g_store_mode;
   if (mode > 0) g_store_mode = mode == 1 ? 1 : 2;

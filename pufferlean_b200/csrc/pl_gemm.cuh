@@ -1068,8 +1068,8 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
 // 0 = single-CTA tiles only (default), 1 = CTA pairs where eligible; a negative mode only queries.
 // Returns the previous mode.
 int gemm_set_pair_mode(int mode);
-// How staged bf16 epilogues leave shared memory: 1 = TMA bulk stores, 2 = coalesced global stores
-// (default); a non-positive mode only queries. Returns the previous mode.
+// How staged bf16 epilogues leave shared memory: 1 = TMA bulk stores (default), 2 = coalesced global
+// stores; a non-positive mode only queries. Returns the previous mode.
 int gemm_set_store_mode(int mode);
 
 }  // namespace pl

@@ -25,6 +25,9 @@ struct NsWork {
   unsigned* err = nullptr;  // bounded-wait error word for the GEMMs (NULL = the per-device default)
 };
 
+// 0 = every batch takes the per-step GEMM chain, 1 = matrices with m, n <= 128 run fused in one CTA
+// each (default); a negative mode only queries. Returns the previous mode.
+int ns_set_small_mode(int mode);
 // final_bf16 (optional): the last step's bf16 output goes there (not an iterate buffer) instead of
 // back into X; result_at (optional): receives the iterate buffer that holds the bf16 result, and X
 // is then left as it is.

@@ -25,12 +25,206 @@ int ns_run(int m, int n, const double* coeffs, int iters, NsWork& w, __nv_bfloat
   return ns_run_batched(m, n, 1, coeffs, iters, w, X, ldx, 0, out_f32, ld_out, 0, st);
 }
 
+// ---------------------------------------------------------------- fused path for small matrices
+// Matrices with m, n <= 128 run every step inside one CTA: X (zero-padded to 128 x 128) stays in shared
+// memory in the 128-byte-swizzled K-major layout the tensor core reads, and each step is three chained
+// tcgen05.mma groups whose accumulators sit in TMEM columns [0,128) (G = X X^T), [128,256) (G G) and
+// [256,384) (X' = Pm X). Between them the four warps rewrite the next operand in shared memory: G in
+// bf16, then Pm = a I + b G + c G G from the fp32 accumulators, then X' over X. X serves as the second
+// operand of X' = Pm X read MN-major, where it lies. One launch replaces 3 x iters GEMM launches.
+struct NsSmallCoef {
+  float c[3 * 16];
+};
+constexpr int kNsSmallMaxIters = 16;
+
+// byte offset of the 16-byte chunk `ch` (8 bf16 columns) of row r in a 128 x 128 bf16 tile stored as
+// two 64-column SW128 atoms of 128 rows
+__device__ __forceinline__ uint32_t ns_sw_off(int r, int ch) {
+  return (uint32_t)((ch >> 3) * 16384 + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
+}
+// this thread's row (32 fp32 TMEM columns from tcol) as bf16 into chunks [c0/8, c0/8 + 4) of row r
+__device__ __forceinline__ void ns_put32(uint8_t* tile, int r, int c0, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    uint4 w;
+    uint32_t* u = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * q + 2 * j], v[8 * q + 2 * j + 1]);
+      u[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(tile + ns_sw_off(r, c0 / 8 + q)) = w;
+  }
+}
+__device__ __forceinline__ void ns_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t a[16], b[16];
+  tc::tmem_ld16(taddr, a);
+  tc::tmem_ld16(taddr + 16, b);
+  tc::tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    v[j] = __uint_as_float(a[j]);
+    v[16 + j] = __uint_as_float(b[j]);
+  }
+}
+
+__global__ void __launch_bounds__(128, 1)
+    ns_small_kernel(const __nv_bfloat16* __restrict__ X, long ldx, long xbs, int m, int n, NsSmallCoef coef,
+                    int iters, __nv_bfloat16* out_bf16, long ldo, long obs, float* out_f32, long ldf, long obsf,
+                    unsigned* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* Xs = smem;           // 32 KB: X, then each X'
+  uint8_t* Gs = smem + 32768;   // 32 KB: G, then Pm
+  uint64_t* bar = (uint64_t*)(smem + 65536);
+  uint32_t* tslot = (uint32_t*)(bar + 1);
+  volatile int* abort_flag = (volatile int*)(tslot + 1);
+  const int t = threadIdx.x, warp = t >> 5;
+  const int r = t;  // this thread's row: TMEM lane r, shared-memory row r
+  const long b = blockIdx.x;
+  if (t == 0) {
+    tc::mbar_init(bar, 1);
+    *abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tslot, 512);
+    tc::tmem_relinquish();
+  }
+  // X row r (zero past m rows / n columns) into the swizzled tile
+  {
+    const __nv_bfloat16* xr = X + b * xbs + (long)r * ldx;
+    const bool vec = ((ldx & 7) == 0) && ((((uintptr_t)X) & 15) == 0) && ((xbs & 7) == 0);
+#pragma unroll 4
+    for (int ch = 0; ch < 16; ch++) {
+      uint4 w = make_uint4(0, 0, 0, 0);
+      if (r < m) {
+        if (vec && ch * 8 + 8 <= n) {
+          w = *reinterpret_cast<const uint4*>(xr + ch * 8);
+        } else {
+          __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&w);
+          for (int e = 0; e < 8; e++) h[e] = (ch * 8 + e < n) ? xr[ch * 8 + e] : __float2bfloat16_rn(0.f);
+        }
+      }
+      *reinterpret_cast<uint4*>(Xs + ns_sw_off(r, ch)) = w;
+    }
+  }
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncwarp();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tslot;
+  const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);
+  constexpr uint32_t ID_KK = tc::idesc_bf16(128, 128, 0, 0);
+  constexpr uint32_t ID_KM = tc::idesc_bf16(128, 128, 0, 1);
+  const uint32_t xa = tc::smem_u32(Xs), ga = tc::smem_u32(Gs);
+  uint32_t phase = 0;
+  // D[tmem col dcol] = A B^T over K = 128 (8 slices of 16); B read MN-major when b_mn
+  auto mma = [&](uint32_t dcol, uint32_t a, uint32_t bb, bool b_mn) {
+    if (t == 0) {
+      tc::tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 8; kk++) {
+        const uint64_t ad = tc::sw128_desc(a + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+        const uint64_t bd = b_mn ? tc::sw128_desc(bb + kk * 2048, 16384, 1024)
+                                 : tc::sw128_desc(bb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+        tc::umma_bf16(tbase + dcol, ad, bd, b_mn ? ID_KM : ID_KK, kk > 0 ? 1u : 0u);
+      }
+      tc::umma_commit(bar);
+    }
+    if (!tc::mbar_wait(bar, phase, err, PL_ERR_MBAR_TIMEOUT | 8)) *abort_flag = 1;
+    phase ^= 1u;
+    tc::tc_fence_after();
+  };
+  // after the threads' shared-memory writes: visible to the tensor core before the next MMA
+  auto publish = [&]() {
+    tc::fence_proxy_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+  };
+  for (int it = 0; it < iters && !*abort_flag; it++) {
+    const float ca = coef.c[3 * it], cb = coef.c[3 * it + 1], cc = coef.c[3 * it + 2];
+    mma(0, xa, xa, false);  // G = X X^T
+    float v[32], g2[32];
+#pragma unroll 1
+    for (int c0 = 0; c0 < 128; c0 += 32) {
+      ns_ld32(trow + c0, v);
+      ns_put32(Gs, r, c0, v);
+    }
+    publish();
+    mma(128, ga, ga, false);  // G G (G symmetric: its rows serve as its columns)
+#pragma unroll 1
+    for (int c0 = 0; c0 < 128; c0 += 32) {
+      ns_ld32(trow + c0, v);
+      ns_ld32(trow + 128 + c0, g2);
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] = cc * g2[j] + cb * v[j] + (r == c0 + j ? ca : 0.f);
+      ns_put32(Gs, r, c0, v);
+    }
+    publish();
+    mma(256, ga, xa, true);  // X' = Pm X
+    const bool last = it + 1 == iters;
+#pragma unroll 1
+    for (int c0 = 0; c0 < 128; c0 += 32) {
+      ns_ld32(trow + 256 + c0, v);
+      if (!last) {
+        ns_put32(Xs, r, c0, v);
+      } else if (r < m) {
+        if (out_f32) {
+          float* o = out_f32 + b * obsf + (long)r * ldf;
+          for (int j = 0; j < 32; j++)
+            if (c0 + j < n) o[c0 + j] = v[j];
+        } else {
+          __nv_bfloat16* o = out_bf16 + b * obs + (long)r * ldo;
+          for (int j = 0; j < 32; j++)
+            if (c0 + j < n) o[c0 + j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+    if (!last) publish();
+  }
+  tc::tc_fence_before();
+  __syncwarp();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, 512);
+  }
+}
+constexpr uint32_t kNsSmallSmem = 1024 + 65536 + 64;
+static int g_ns_small = 1;  // 0: small matrices also take the per-step GEMM chain (tests compare the two)
+int ns_set_small_mode(int mode) {
+  const int prev = g_ns_small;
+  if (mode >= 0) g_ns_small = mode ? 1 : 0;
+  return prev;
+}
+
 int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
                    long xbs, float* out_f32, long ld_out, long obs, cudaStream_t st, __nv_bfloat16* final_bf16,
                    __nv_bfloat16** result_at) {
   PL_REQUIRE(!final_bf16 || (final_bf16 != w.X0 && final_bf16 != w.X1 && final_bf16 != X), PL_ERR_INVALID,
              "Newton-Schulz: the final output may not alias the iterates");
   PL_REQUIRE(m <= n, PL_ERR_INVALID, "Newton-Schulz expects the wide layout (m=%d > n=%d)", m, n);
+  if (g_ns_small && n <= 128 && iters <= kNsSmallMaxIters && batch <= 65535) {
+    NsSmallCoef cf{};
+    for (int i = 0; i < 3 * iters; i++) cf.c[i] = (float)coeffs[i];
+    const long xbs_eff = batch > 1 ? xbs : (long)ldx * m;
+    __nv_bfloat16* dst = final_bf16 ? final_bf16 : X;  // the result ends in place unless told otherwise
+    static bool configured = false;
+    if (!configured) {
+      PL_CUDA(cudaFuncSetAttribute((const void*)ns_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kNsSmallSmem));
+      configured = true;
+    }
+    ns_small_kernel<<<(unsigned)batch, 128, kNsSmallSmem, st>>>(
+        X, ldx, xbs_eff, m, n, cf, iters, out_f32 ? nullptr : dst, ldx, xbs_eff, out_f32, ld_out,
+        batch > 1 ? obs : (long)ld_out * m, w.err ? w.err : device_error_word());
+    count_launch();
+    PL_LAUNCH("ns_small_kernel");
+    if (result_at) *result_at = out_f32 ? nullptr : dst;
+    return PL_OK;
+  }
   const long gbs = (long)w.ldg * m;
   __nv_bfloat16* cur = X;
   __nv_bfloat16* nxt = (X == w.X0) ? w.X1 : w.X0;

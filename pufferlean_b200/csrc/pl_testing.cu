@@ -1,6 +1,7 @@
 // Test hooks (include/pufferlean_b200_testing.h): the GEMM and its epilogues on raw device pointers.
 #include "../../include/pufferlean_b200_testing.h"
 #include "pl_gemm.cuh"
+#include "pl_mlp.cuh"
 
 extern "C" int pl_test_gemm(const pl_test_gemm_args* g, void* stream) {
   PL_REQUIRE(g != nullptr, PL_ERR_INVALID, "pl_test_gemm: NULL args");
@@ -43,6 +44,7 @@ extern "C" int pl_test_gemm(const pl_test_gemm_args* g, void* stream) {
 
 extern "C" int pl_test_gemm_pair_mode(int mode) { return pl::gemm_set_pair_mode(mode); }
 extern "C" int pl_test_gemm_store_mode(int mode) { return pl::gemm_set_store_mode(mode); }
+extern "C" int pl_test_ns_small_mode(int mode) { return pl::ns_set_small_mode(mode); }
 
 extern "C" int pl_test_device_error(unsigned* code) {
   unsigned* w = pl::device_error_word();
