@@ -30,7 +30,7 @@ int ns_run(int m, int n, const double* coeffs, int iters, NsWork& w, __nv_bfloat
 // memory in the 128-byte-swizzled K-major layout the tensor core reads, and each step is three chained
 // tcgen05.mma groups whose accumulators sit in TMEM columns [0,128) (G = X X^T), [128,256) (G G) and
 // [256,384) (X' = Pm X). Between them the four warps rewrite the next operand in shared memory: G in
-// bf16, then Pm = a I + b G + c G G from the fp32 accumulators, then X' over X. X serves as the second
+// bf16, then Pm = a I + b G + c G G (G as rounded to bf16, G G from the accumulator), then X' over X. X serves as the second
 // operand of X' = Pm X read MN-major, where it lies. One launch replaces 3 x iters GEMM launches.
 struct NsSmallCoef {
   float c[3 * 16];
@@ -158,8 +158,11 @@ __global__ void __launch_bounds__(128, 1)
     for (int c0 = 0; c0 < 128; c0 += 32) {
       ns_ld32(trow + c0, v);
       ns_ld32(trow + 128 + c0, g2);
+      // G enters the polynomial rounded to bf16, as it entered G G: b G and c G G largely cancel, and
+      // an fp32 G beside a G G built from the rounded G doubles the step's error
 #pragma unroll
-      for (int j = 0; j < 32; j++) v[j] = cc * g2[j] + cb * v[j] + (r == c0 + j ? ca : 0.f);
+      for (int j = 0; j < 32; j++)
+        v[j] = cc * g2[j] + cb * __bfloat162float(__float2bfloat16_rn(v[j])) + (r == c0 + j ? ca : 0.f);
       ns_put32(Gs, r, c0, v);
     }
     publish();

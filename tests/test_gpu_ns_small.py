@@ -56,11 +56,14 @@ def test_small_ns_fused_vs_oracle_and_chain(batch, rows, cols):
         _small(prev)
     Xin = X0.double().cpu().numpy()
     f, c = Xf.double().cpu().numpy(), Xc.double().cpu().numpy()
+    worst = []
     for b in range(batch):
         ref = O.newton_schulz(Xin[b].ravel(), rows, cols, 1e-7, co).reshape(rows, cols)
-        assert rel(f[b], ref) < 2e-2, (b, rel(f[b], ref))
-        assert rel(c[b], ref) < 2e-2, (b, rel(c[b], ref))
-        assert rel(f[b], c[b]) < 2e-2, (b, rel(f[b], c[b]))
+        worst.append((rel(f[b], ref), rel(c[b], ref), rel(f[b], c[b])))
+    ef, ec, efc = (max(w[i] for w in worst) for i in range(3))
+    # both forms round the same operands to bf16 at the same points: equal to the chain's own accuracy
+    assert ef < 2e-2 and ec < 2e-2, (ef, ec)
+    assert efc < 5e-3, efc
 
 
 def test_small_ns_fp32_output_in_cartpole_update():
