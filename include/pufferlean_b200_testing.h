@@ -32,10 +32,6 @@ int pl_test_gemm(const pl_test_gemm_args* g, void* stream);
  * the default, 1 = CTA pairs (cta_group::2, 256-row tiles) where eligible; a negative mode only
  * queries. Returns the previous mode. */
 int pl_test_gemm_pair_mode(int mode);
-/* Selects how the GEMM's staged bf16 epilogues write their tiles for every later launch: 1 = TMA
- * bulk stores (the default), 2 = coalesced global stores; a non-positive mode only queries. Returns
- * the previous mode. */
-int pl_test_gemm_store_mode(int mode);
 /* Newton-Schulz for matrices with both sides <= 128: 1 = one fused CTA per matrix (the default),
  * 0 = the per-step GEMM chain; a negative mode only queries. Returns the previous mode. */
 int pl_test_ns_small_mode(int mode);

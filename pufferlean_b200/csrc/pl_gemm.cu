@@ -27,16 +27,6 @@ int gemm_set_pair_mode(int mode) {
   return prev;
 }
 
-// Staged bf16 epilogues: 1 = TMA bulk stores (default), 2 = coalesced global stores (measured slower on
-// B200 for every shape of the update: the tile still passes through shared memory, whose bandwidth
-// the main loop's operand traffic already uses up, and the global stores add L1 traffic on top).
-static int g_store_mode = 1;
-int gemm_set_store_mode(int mode) {
-  const int prev = g_store_mode;
-  if (mode > 0) g_store_mode = mode == 1 ? 1 : 2;
-  return prev;
-}
-
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -122,7 +112,7 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
     // the staged epilogue reads its aux tile with aligned 16-byte loads
     if (ok && ep.aux && (((uintptr_t)ep.aux & 15) || (ep.ld_aux % 8) || (batch > 1 && (ep.aux_bstride % 8))))
       ok = false;
-    ep.tma_out = ok ? g_store_mode : 0;
+    ep.tma_out = ok ? 1 : 0;
   }
   int splits = ep.k_splits > 1 ? ep.k_splits : 1;
   PL_REQUIRE(splits == 1 || batch == 1, PL_ERR_INVALID, "split-K and batching are exclusive");

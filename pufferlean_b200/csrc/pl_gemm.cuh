@@ -55,8 +55,7 @@ struct EpiArgs {
   unsigned* err;
   int k_splits;      // >1: the z index of a tile is its split-K slice; else its batch index
   int nbatch;        // number of stacked matrices (z extent when k_splits <= 1)
-  int tma_out;       // bf16 outputs leave through 32 x 32 shared-memory tiles (host-checked): 1 = TMA bulk
-                     // stores, 2 = coalesced global stores; 0 = straight from registers
+  int tma_out;       // bf16 outputs leave through shared memory and TMA bulk stores (host-checked)
   float diag;        // EPI_F32 / EPI_BF16: added on the diagonal (row == column) of every matrix
 };
 
@@ -210,15 +209,9 @@ struct GemmSmem {
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int NOUT = EPI == EPI_FWD ? 2 : ((EPI == EPI_DGRAD || EPI == EPI_BF16) ? 1 : 0);
-  static constexpr uint32_t STG_ONE = NOUT * 32 * 32 * 2;
-  static constexpr uint32_t RED_BYTES = (EPI == EPI_DGRAD || EPI == EPI_PPO) ? (4 * BN * 4 + 4 * 8 * 4) : 0;
-  // Two staging tiles per warp (a store may still read one while the next chunk fills the other)
-  // wherever that leaves the ring as deep as one tile would.
-  static constexpr int FIT_1 = (int)((232448 - (1024 + 256 + 8 * STG_ONE + RED_BYTES)) / STAGE_BYTES);
-  static constexpr int FIT_2 = (int)((232448 - (1024 + 256 + 16 * STG_ONE + RED_BYTES)) / STAGE_BYTES);
-  static constexpr int STG_BUFS = (NOUT == 1 && (FIT_2 >= 8 || FIT_2 == FIT_1)) ? 2 : 1;
-  static constexpr uint32_t STG_WARP = STG_BUFS * STG_ONE;
+  static constexpr uint32_t STG_WARP = NOUT * 32 * 32 * 2;
   static constexpr uint32_t STG_BYTES = 8 * STG_WARP;
+  static constexpr uint32_t RED_BYTES = (EPI == EPI_DGRAD || EPI == EPI_PPO) ? (4 * BN * 4 + 4 * 8 * 4) : 0;
   static constexpr uint32_t FIXED = 1024 + 256 + STG_BYTES + RED_BYTES;
   static constexpr int FIT = (int)((232448 - FIXED) / STAGE_BYTES);
   static constexpr int STAGES = FIT > 8 ? 8 : FIT;
@@ -260,31 +253,6 @@ __device__ __forceinline__ void stage_row32(uint8_t* tile, int lane, const float
   }
 }
 
-// Writes a staged 32 x 32 bf16 tile (row-major, 64 bytes a row) to out[row0.., n0..] with plain global
-// stores: lane l carries 16 bytes of row 8 it + l / 4, so each instruction covers 8 whole 64-byte row
-// pieces. Rows / columns past (rows, cols) are not written.
-__device__ __forceinline__ void write_tile32(const uint8_t* tile, __nv_bfloat16* out, long ldo, int row0, int n0,
-                                             int rows, int cols, int lane) {
-  const int rr = lane >> 2, cc = lane & 3;
-  const int gc = n0 + cc * 8;
-#pragma unroll
-  for (int it = 0; it < 4; it++) {
-    const int r = it * 8 + rr;
-    const int gr = row0 + r;
-    const uint4 val = *reinterpret_cast<const uint4*>(tile + r * 64 + cc * 16);
-    if (gr < rows) {
-      __nv_bfloat16* dst = out + (long)gr * ldo + gc;
-      if (gc + 8 <= cols) {
-        *reinterpret_cast<uint4*>(dst) = val;
-      } else {
-        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&val);
-        for (int e = 0; e < 8; e++)
-          if (gc + e < cols) dst[e] = h[e];
-      }
-    }
-  }
-}
-
 // The 32 bf16 aux values of one row at columns [nc, nc + 32) (zero past cols), as four 16-byte words.
 __device__ __forceinline__ void aux_load32(const __nv_bfloat16* aux_row, int nc, int cols, uint4 (&pre)[4]) {
   if (nc + 32 <= cols) {
@@ -298,28 +266,11 @@ __device__ __forceinline__ void aux_load32(const __nv_bfloat16* aux_row, int nc,
   }
 }
 
-// Issued by an epilogue warp before it waits for a tile's accumulator: the aux piece of its first
-// chunk, so that load's latency passes under the tile's main loop. Returns whether it loaded.
-template <int BN, int EPI>
-__device__ __forceinline__ bool epilogue_aux_first(const EpiArgs& ep, int m_tile, int n_tile, int batch, int sub,
-                                                   int half, int lane, uint4 (&pre)[4]) {
-  if constexpr (EPI == EPI_DGRAD || EPI == EPI_BF16) {
-    const int row = m_tile * 128 + sub * 32 + lane;
-    const int nc = n_tile * BN + half * (BN / 2);
-    if (ep.tma_out && ep.aux != nullptr && row < ep.out_rows && nc < ep.out_cols) {
-      aux_load32(ep.aux + (long)batch * ep.aux_bstride + (long)row * ep.ld_aux, nc, ep.out_cols, pre);
-      return true;
-    }
-  }
-  return false;
-}
-
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row, int m_tile, int n_tile, int bz,
                                               int batch, bool have_acc, int sub, int half, int lane, float* red,
-                                              float* rowscr, uint8_t* stg_warp, const CUtensorMap* tmC,
-                                              const CUtensorMap* tmC2, uint32_t& stg_seq, uint4 (&pre)[4],
-                                              bool pre_loaded) {
+                                              float* rowscr, uint8_t* stg, const CUtensorMap* tmC,
+                                              const CUtensorMap* tmC2) {
   constexpr int BM = 128;
   const int row = m_tile * BM + sub * 32 + lane;
   const bool row_ok = row < ep.out_rows;
@@ -468,8 +419,9 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
       const bool use_aux = HAS_AUX && ep.aux != nullptr && row_ok;
       const __nv_bfloat16* aux_row =
           use_aux ? ep.aux + (long)batch * ep.aux_bstride + (long)row * ep.ld_aux : nullptr;
+      uint4 pre[4];
       auto prefetch = [&](int nc) { aux_load32(aux_row, nc, ep.out_cols, pre); };
-      if (use_aux && !pre_loaded && n_base + cb < ep.out_cols) prefetch(n_base + cb);
+      if (use_aux && n_base + cb < ep.out_cols) prefetch(n_base + cb);
       for (int c32 = cb; c32 < ce; c32 += 32) {
         const int n0 = n_base + c32;
         if (n0 >= ep.out_cols) break;  // warp-uniform
@@ -504,43 +456,20 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
         }
         if constexpr (EPI == EPI_FWD) act_fwd_row(z, v, ep.act);
         if constexpr (EPI == EPI_DGRAD) act_grad_row(v, aux, ep.act);
-        // this chunk's staging tile: with two per warp, alternate and let one store stay in flight
-        constexpr int NBUF = GemmSmem<BN, EPI>::STG_BUFS;
-        uint8_t* stg = stg_warp + (NBUF == 2 ? (stg_seq & 1u) * GemmSmem<BN, EPI>::STG_ONE : 0u);
-        stg_seq++;
-        const bool via_tma = ep.tma_out == 1;
-        if (lane == 0 && via_tma) {
-          if constexpr (NBUF == 2)
-            tc::bulk_wait_read<1>();  // the store that last read this tile has finished reading it
-          else
-            tc::bulk_wait_read<0>();
-        }
+        if (lane == 0) tc::bulk_wait_read<0>();  // the previous tile's stores have read the staging area
         __syncwarp();
         stage_row32(stg, lane, v);
         if constexpr (EPI == EPI_FWD) {
           if (ep.out2) stage_row32(stg + 2048, lane, z);
         }
-        if (via_tma) {
-          tc::fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tc::tma_store_3d(tmC, stg, n0, row0, batch);
-            if constexpr (EPI == EPI_FWD) {
-              if (ep.out2) tc::tma_store_3d(tmC2, stg + 2048, n0, row0, batch);
-            }
-            tc::bulk_commit();
-          }
-        } else {
-          // plain coalesced stores: they leave through the load/store path, not the TMA unit that the
-          // main loop's operand loads keep busy
-          __syncwarp();
-          write_tile32(stg, (__nv_bfloat16*)ep.out + (long)batch * ep.out_bstride, ep.ldo, row0, n0, ep.out_rows,
-                       ep.out_cols, lane);
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tc::tma_store_3d(tmC, stg, n0, row0, batch);
           if constexpr (EPI == EPI_FWD) {
-            if (ep.out2)
-              write_tile32(stg + 2048, (__nv_bfloat16*)ep.out2, ep.ldo2, row0, n0, ep.out_rows, ep.out_cols, lane);
+            if (ep.out2) tc::tma_store_3d(tmC2, stg + 2048, n0, row0, batch);
           }
-          __syncwarp();  // the staging tile is read out before the next chunk overwrites it
+          tc::bulk_commit();
         }
         if constexpr (EPI == EPI_DGRAD) {
           if (do_colsum) {
@@ -786,16 +715,12 @@ __global__ void __launch_bounds__(320, 1)
     // warps w and w + 4 share those rows and split the tile's columns
     const int sub = warp & 3;
     const int half = (warp - 2) >> 2;
-    uint32_t stg_seq = 0;
     int j = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, j++) {
       const TileIdx ti = tile_of(t, num_n, num_m);
       int b0, b1;
       kb_range(ti.z, b0, b1);
       const int buf = j & 1;
-      uint4 pre[4];
-      const bool pre_loaded =
-          epilogue_aux_first<BN, EPI>(ep, ti.m, ti.n, ep.k_splits > 1 ? 0 : ti.z, sub, half, lane, pre);
       const bool ok = tc::mbar_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 6);
       if (!ok || *abort_flag) {
         *abort_flag = 1;
@@ -804,7 +729,7 @@ __global__ void __launch_bounds__(320, 1)
       tc::tc_fence_after();
       const uint32_t t_row = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(sub * 32) << 16);
       epilogue_tile<BN, EPI>(ep, t_row, ti.m, ti.n, ti.z, ep.k_splits > 1 ? 0 : ti.z, b1 > b0, sub, half, lane, red,
-                             rowscr, stg_base + (warp - 2) * S::STG_WARP, &tmC, &tmC2, stg_seq, pre, pre_loaded);
+                             rowscr, stg_base + (warp - 2) * S::STG_WARP, &tmC, &tmC2);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&acc_empty[buf])) : "memory");
@@ -1011,7 +936,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     // ---------------- epilogue warps 2..9 of each CTA drain its 128 accumulator rows
     const int sub = warp & 3;
     const int half = (warp - 2) >> 2;
-    uint32_t stg_seq = 0;
     int j = 0;
     for (int t = pair; t < total_tiles; t += npairs, j++) {
       const TileIdx ti = tile_of(t, num_n, num_m);
@@ -1019,9 +943,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       kb_range(ti.z, b0, b1);
       const int buf = j & 1;
       const int m_blk = ti.m * 2 + (int)rank;
-      uint4 pre[4];
-      const bool pre_loaded = m_blk * BM < M && epilogue_aux_first<BN, EPI>(ep, m_blk, ti.n, ep.k_splits > 1 ? 0 : ti.z,
-                                                                           sub, half, lane, pre);
       const bool ok = tc::mbar_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 6);
       if (!ok || *abort_flag) {
         *abort_flag = 1;
@@ -1033,8 +954,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       // column partials would fall outside the ceil(M / 128) rows the caller provides
       if (m_blk * BM < M)
         epilogue_tile<BN, EPI>(ep, t_row, m_blk, ti.n, ti.z, ep.k_splits > 1 ? 0 : ti.z, b1 > b0, sub, half, lane, red,
-                               rowscr, stg_base + (warp - 2) * GemmSmem<BN, EPI>::STG_WARP, &tmC, &tmC2, stg_seq, pre,
-                               pre_loaded);
+                               rowscr, stg_base + (warp - 2) * GemmSmem<BN, EPI>::STG_WARP, &tmC, &tmC2);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_remote(tc::cluster_addr(tc::smem_u32(&acc_empty[buf]), 0));
@@ -1068,8 +988,5 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
 // 0 = single-CTA tiles only (default), 1 = CTA pairs where eligible; a negative mode only queries.
 // Returns the previous mode.
 int gemm_set_pair_mode(int mode);
-// How staged bf16 epilogues leave shared memory: 1 = TMA bulk stores (default), 2 = coalesced global
-// stores; a non-positive mode only queries. Returns the previous mode.
-int gemm_set_store_mode(int mode);
 
 }  // namespace pl

@@ -185,49 +185,3 @@ def test_pair_mode_hook_round_trip():
     _mode(prev)
     assert _mode(-1) == prev
 
-
-def _store_mode(m):
-    L = plb.lib()
-    L.pl_test_gemm_store_mode.argtypes = [C.c_int]
-    return L.pl_test_gemm_store_mode(m)
-
-
-@pytest.mark.parametrize("pair", [0, 1])
-def test_store_modes_bit_identical(pair):
-    """The staged bf16 epilogues write the same bits through TMA bulk stores (mode 1) and through
-    coalesced global stores (mode 2): forward (two outputs), data gradient, bf16 axpby; ragged M and N."""
-    torch.manual_seed(31 + pair)
-    M, H, D = 300, 392, 128
-    X = _bf(torch.randn(M, D, device="cuda"))
-    W = _bf(torch.randn(H, D, device="cuda") / math.sqrt(D))
-    b = torch.randn(H, device="cuda")
-    dY = _bf(torch.randn(M, 192, device="cuda"))
-    W2 = _bf(torch.randn(192, H, device="cuda"))
-    aux = _bf(torch.randn(M, H, device="cuda"))
-
-    def run():
-        Hout = torch.zeros(M, H, dtype=torch.bfloat16, device="cuda")
-        Z = torch.zeros(M, H, dtype=torch.bfloat16, device="cuda")
-        G.gemm(X, W, M, H, D, False, False, 256, G.EPI_FWD, out=Hout, bias=b, out2=Z, ldo2=H, act=1)
-        dZ = torch.zeros(M, H, dtype=torch.bfloat16, device="cuda")
-        cs = torch.zeros((M + 127) // 128, H, device="cuda")
-        G.gemm(dY, W2, M, H, 192, False, True, 256, G.EPI_DGRAD, out=dZ, aux=aux, ld_aux=H, act=1, colsum=cs,
-               ld_colsum=H)
-        Y = torch.zeros(M, H, dtype=torch.bfloat16, device="cuda")
-        G.gemm(X, W, M, H, D, False, False, 256, G.EPI_BF16, out=Y, alpha=0.5, beta=2.0, aux=aux, ld_aux=H)
-        torch.cuda.synchronize()
-        return [t.clone() for t in (Hout, Z, dZ, cs, Y)]
-
-    prev_pair, prev_store = _mode(pair), _store_mode(1)
-    try:
-        a = run()
-        _store_mode(2)
-        c = run()
-    finally:
-        _mode(prev_pair)
-        _store_mode(prev_store)
-    assert G.device_error() == 0
-    for x, y in zip(a, c):
-        assert torch.equal(x, y)
-    z = X.float() @ W.float().t() + b
-    assert _rel(c[1], z) < 1e-2
