@@ -612,7 +612,6 @@ __global__ void __launch_bounds__(320, 1)
     tc::tmem_relinquish();
   }
   tc::tc_fence_before();
-  __syncwarp();  // warps 0 and 1 run lane-0-only roles: each warp reaches the CTA barrier converged
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
@@ -741,10 +740,10 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(epi_done)) : "memory");
   }
   tc::tc_fence_before();
-  __syncwarp();  // lane 0 of warps 0 and 1 arrives last; the whole warp meets the barrier together
   __syncthreads();
   if (warp == 1) {
     // TMEM is released only after every epilogue warp has signalled that its reads and stores are done
+    // (an explicit handshake: warps 0 and 1 reach the CTA barrier with lane 0 still in its role loop)
     if (lane == 0) tc::mbar_wait(epi_done, 0, ep.err, PL_ERR_MBAR_TIMEOUT | 7);
     __syncwarp();
     tc::tc_fence_after();
