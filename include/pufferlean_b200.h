@@ -258,6 +258,14 @@ int pl_mingru_ppo_grad(const double* params, const double* obs, const double* sc
                        const pl_mg_net* net, double vfCoef, double entCoef, double clipEps, double vfClip,
                        uint8_t bf16, double* out);
 
+/* The same with W multi-discrete heads of sizes head_sizes (summing to net->A): scal is
+ * [act (W per row, [(t*B + b)*W + h]) | adv | ret | old | term | ov], (W + 5)*T*B values; the head is
+ * k_mg_ppo_b_md's (joint log-prob in double). W = 1 is pl_mingru_ppo_grad. Replaces the K > 1 host mode
+ * of lean_cuda_mingru_ppo_grad (ffi/puffercuda.cu:5204-5221, 5428). */
+int pl_mingru_ppo_grad_md(const double* params, const double* obs, const double* scal, size_t B, size_t T,
+                          const pl_mg_net* net, size_t W, const double* head_sizes, double vfCoef, double entCoef,
+                          double clipEps, double vfClip, uint8_t bf16, double* out);
+
 /* Host bookkeeping twins, bit-exact: prioritised segment sampling (replaces lean_ffi_prio_sample,
  * ffi/pufferffi.c:1094-1125) and the MinGRU minibatch scalar gather (replaces
  * lean_ffi_gather_seq_minibatch, ffi/pufferffi.c:1137-1176; out = 6*T*Bmb, [act|adv|ret|old|term|ov]). */
@@ -279,6 +287,12 @@ int pl_mg_set_columns(pl_mg* s, const double* rew, const double* term, const dou
                       const double* val, const double* boot);
 int pl_mg_set_columns_dev(pl_mg* s, const double* rew, const double* term, const double* act, const double* logp,
                           const double* val, const double* boot, void* stream);
+/* Action heads of the session (the K of lean_cuda_mg_prep / lean_cuda_mingru_ppo_grad,
+ * ffi/puffercuda.cu:316-335, 5204-5221): W = 1 one categorical head (the default); W > 1 multi-discrete
+ * heads, the act column then holds W actions per row ([(e*T + t)*W + h]) and head_sizes (W values,
+ * summing to the network's A) select the heads' logits. Changing W drops the columns (set them again
+ * after); head_sizes may be NULL to fix the width first and give the sizes before the gradient. */
+int pl_mg_set_heads(pl_mg* s, size_t W, const double* head_sizes);
 /* Data parallelism (no reference counterpart; the reference trainer is single-GPU): one process and
  * session per GPU, each with its own rollout columns (weak scaling). With world > 1, pl_mg_grad
  * all-reduces the advantage sums (the normalisation uses the all-rank minibatch) and the summed

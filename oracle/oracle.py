@@ -79,6 +79,13 @@ def orc():
         lib.orc_prio_sample.argtypes = [_dp, _sz, _sz, _d, _d, C.c_uint64, _dp, _dp]
         lib.orc_gather_seq_minibatch.argtypes = [_dp] * 7 + [_sz, _sz, _dp]
         lib.orc_apply_muon_mg.argtypes = [_dp, _dp] + [_sz] * 5 + [_d] * 4 + [_dp, C.c_int]
+        _ip = C.POINTER(C.c_int)
+        lib.orc_mingru_grad_seq_md.argtypes = [_dp] * 8 + [_sz] * 6 + [C.c_int] + [_d] * 4 + [_sz, _ip] + [_dp] * 3
+        lib.orc_mingru_grad_batch_md.argtypes = [_dp] * 3 + [_sz] * 7 + [C.c_int] + [_d] * 4 + [_sz, _ip, _dp]
+        lib.orc_gather_seq_minibatch_md.argtypes = [_dp] * 7 + [_sz, _sz, _sz, _dp]
+        lib.orc_mingru_update_md.restype = C.c_uint64
+        lib.orc_mingru_update_md.argtypes = ([_dp] * 8 + [_sz] * 7 + [C.c_int] + [_sz] * 2 + [_d] * 6 + [C.c_uint64]
+                                             + [_d] * 9 + [_dp, C.c_int, _sz, _ip])
         lib.orc_mingru_update.restype = C.c_uint64
         lib.orc_mingru_update.argtypes = ([_dp] * 8 + [_sz] * 7 + [C.c_int] + [_sz] * 2 + [_d] * 6 + [C.c_uint64]
                                           + [_d] * 9 + [_dp, C.c_int])
@@ -235,23 +242,35 @@ def init_mingru(D, H, L, A, seed, K=3):
     return flat, int(s)
 
 
+def _heads(hs):
+    """(W, int array) for a head-size list; None = one categorical head (W = 1)."""
+    if hs is None:
+        return 1, None
+    return len(hs), (C.c_int * len(hs))(*[int(x) for x in hs])
+
+
 def mingru_grad_seq(params, obs, acts, advs, rets, olps, terms, ovs, T, H, D, L, A, K=3, enc_act=0, vf=0.5, ent=0.01,
-                    clip=0.2, vfClip=0.2):
+                    clip=0.2, vfClip=0.2, hs=None):
+    """hs: multi-discrete head sizes (sum A); acts then holds len(hs) actions per step."""
     P = mg_param_count(D, H, L, A, K)
     g, nl, nv = np.zeros(P), np.zeros(T), np.zeros(T)
     arrs = list(map(f64, (params, obs, acts, advs, rets, olps, terms, ovs)))
-    orc().orc_mingru_grad_seq(*[_ptr(a) for a in arrs], T, H, D, L, A, K, enc_act, vf, ent, clip, vfClip, _ptr(g),
-                              _ptr(nl), _ptr(nv))
+    W, hsa = _heads(hs)
+    orc().orc_mingru_grad_seq_md(*[_ptr(a) for a in arrs], T, H, D, L, A, K, enc_act, vf, ent, clip, vfClip, W, hsa,
+                                 _ptr(g), _ptr(nl), _ptr(nv))
     return g, nl, nv
 
 
-def mingru_grad_batch(params, obsTB, scal, B, T, H, D, L, A, K=3, enc_act=0, vf=0.5, ent=0.01, clip=0.2, vfClip=0.2):
-    """[g(P); newlp(T*B); newval(T*B)] for B time-major packed sequences (scal = [act|adv|ret|old|term|ov])."""
+def mingru_grad_batch(params, obsTB, scal, B, T, H, D, L, A, K=3, enc_act=0, vf=0.5, ent=0.01, clip=0.2, vfClip=0.2,
+                      hs=None):
+    """[g(P); newlp(T*B); newval(T*B)] for B time-major packed sequences (scal = [act|adv|ret|old|term|ov], the act
+    block len(hs) wide per row with multi-discrete heads)."""
     P = mg_param_count(D, H, L, A, K)
     out = np.zeros(P + 2 * T * B)
     params, obsTB, scal = map(f64, (params, obsTB, scal))
-    orc().orc_mingru_grad_batch(_ptr(params), _ptr(obsTB), _ptr(scal), B, T, H, D, L, A, K, enc_act, vf, ent, clip,
-                                vfClip, _ptr(out))
+    W, hsa = _heads(hs)
+    orc().orc_mingru_grad_batch_md(_ptr(params), _ptr(obsTB), _ptr(scal), B, T, H, D, L, A, K, enc_act, vf, ent, clip,
+                                   vfClip, W, hsa, _ptr(out))
     return out
 
 
@@ -263,10 +282,10 @@ def prio_sample(advL1, N, mbSegs, alpha, beta, rng):
     return seg, mp
 
 
-def gather_seq_minibatch(act, logp, term, adv, value, seg, mbPrio, T, Bmb):
-    out = np.zeros(6 * T * Bmb)
+def gather_seq_minibatch(act, logp, term, adv, value, seg, mbPrio, T, Bmb, W=1):
+    out = np.zeros((W + 5) * T * Bmb)
     arrs = list(map(f64, (act, logp, term, adv, value, seg, mbPrio)))
-    orc().orc_gather_seq_minibatch(*[_ptr(a) for a in arrs], T, Bmb, _ptr(out))
+    orc().orc_gather_seq_minibatch_md(*[_ptr(a) for a in arrs], T, Bmb, W, _ptr(out))
     return out
 
 
@@ -279,14 +298,15 @@ def apply_muon_mg(pm, g, D, H, L, A, lr, wd, mu, eps, K=3, coeffs=MUON_COEFFS):
 
 def mingru_update(pm, obs, rew, term, act, logp, val0, boot, N, T, D, H, L, A, numMB, mbSegs, rng, lr, K=3,
                   enc_act=0, gamma=0.995, lam=0.90, rho=1.0, c=1.0, alpha=0.8, beta=0.2, wd=0.0, mu=0.95, eps=1e-7,
-                  vf=0.5, ent=0.01, clip=0.2, vfClip=0.2, maxGradNorm=1.5, coeffs=MUON_COEFFS):
-    """One whole MinGRU update (orc_mingru_update); returns (pm', rng')."""
+                  vf=0.5, ent=0.01, clip=0.2, vfClip=0.2, maxGradNorm=1.5, coeffs=MUON_COEFFS, hs=None):
+    """One whole MinGRU update (orc_mingru_update_md); returns (pm', rng'). hs: multi-discrete head sizes."""
     pm = f64(pm).copy()
     arrs = list(map(f64, (obs, rew, term, act, logp, val0, boot)))
     co = f64(coeffs)
-    r = orc().orc_mingru_update(_ptr(pm), *[_ptr(a) for a in arrs], N, T, D, H, L, A, K, enc_act, numMB, mbSegs, gamma,
-                                lam, rho, c, alpha, beta, C.c_uint64(rng & 0xFFFFFFFFFFFFFFFF), lr, wd, mu, eps, vf,
-                                ent, clip, vfClip, maxGradNorm, _ptr(co), co.shape[0])
+    W, hsa = _heads(hs)
+    r = orc().orc_mingru_update_md(_ptr(pm), *[_ptr(a) for a in arrs], N, T, D, H, L, A, K, enc_act, numMB, mbSegs,
+                                   gamma, lam, rho, c, alpha, beta, C.c_uint64(rng & 0xFFFFFFFFFFFFFFFF), lr, wd, mu,
+                                   eps, vf, ent, clip, vfClip, maxGradNorm, _ptr(co), co.shape[0], W, hsa)
     return pm, int(r)
 
 

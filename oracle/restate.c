@@ -570,10 +570,15 @@ static double orc_sig(double x) { return 1.0 / (1.0 + exp(-x)); }
  * Zero initial state; the state resets to zero after a terminal step and no gradient flows back across
  * it. g[P] is zeroed and receives this sequence's summed ascent gradient; newlp/newval (T each, may be
  * NULL) receive the taken action's log-prob and the value at every step. */
-void orc_mingru_grad_seq(const double* params, const double* obsAll, const double* actA, const double* advA,
-                         const double* retA, const double* oldA, const double* termA, const double* ovA, size_t T,
-                         size_t H, size_t D, size_t L, size_t A, size_t K, int encAct, double vfCoef,
-                         double entCoef, double clipEps, double vfClip, double* g, double* newlp, double* newval) {
+/* W > 1: W multi-discrete heads of sizes hs (sum A) in place of the one categorical head, actA then
+ * holds W actions per step ([t*W + h]); the head follows k_mg_ppo_b_md (ffi/puffercuda.cu:4940-4980)
+ * restated in f64: per head the max-subtracted softmax, the joint log-prob sum_h log(exp(x_a - m)/se),
+ * one clipped ratio, per-logit gradient dPol (1[k = a_h] - p) + ent p (sum_j p_j x_j - x_k). */
+void orc_mingru_grad_seq_md(const double* params, const double* obsAll, const double* actA, const double* advA,
+                            const double* retA, const double* oldA, const double* termA, const double* ovA, size_t T,
+                            size_t H, size_t D, size_t L, size_t A, size_t K, int encAct, double vfCoef,
+                            double entCoef, double clipEps, double vfClip, size_t W, const int* hs, double* g,
+                            double* newlp, double* newval) {
   const size_t wEncSz = H * D, layerSz = K * H * H;
   const size_t P = orc_mg_param_count(D, H, L, A, K);
   const double* wEnc = params;
@@ -677,17 +682,32 @@ void orc_mingru_grad_seq(const double* params, const double* obsAll, const doubl
     size_t t = tt;
     const double* obs = obsAll + t * D;
     const double* logits = lg + t * A;
-    double sumexp = 0.0;
-    for (size_t k = 0; k < A; k++) sumexp += exp(logits[k]);
-    double lse = log(sumexp);
-    double pout = 0.0;
-    for (size_t k = 0; k < A; k++) {
-      pk[k] = exp(logits[k] - lse);
-      pout += pk[k] * logits[k];
-    }
-    size_t a = (size_t)actA[t];
     double adv = advA[t], ret = retA[t], oldLogp = oldA[t], vold = ovA[t];
-    double logpA = logits[a] - lse;
+    double logpA = 0.0, lse = 0.0, pout = 0.0;
+    size_t a = 0;
+    if (W <= 1) {
+      double sumexp = 0.0;
+      for (size_t k = 0; k < A; k++) sumexp += exp(logits[k]);
+      lse = log(sumexp);
+      for (size_t k = 0; k < A; k++) {
+        pk[k] = exp(logits[k] - lse);
+        pout += pk[k] * logits[k];
+      }
+      a = (size_t)actA[t];
+      logpA = logits[a] - lse;
+    } else {
+      size_t off = 0;
+      for (size_t h = 0; h < W; h++) {
+        const size_t sz = (size_t)hs[h], ah = (size_t)actA[t * W + h];
+        double m = logits[off];
+        for (size_t k = 1; k < sz; k++)
+          if (logits[off + k] > m) m = logits[off + k];
+        double se = 0.0;
+        for (size_t k = 0; k < sz; k++) se += exp(logits[off + k] - m);
+        logpA += log(exp(logits[off + ah] - m) / se);
+        off += sz;
+      }
+    }
     double ratio = exp(logpA - oldLogp);
     double lo = 1.0 - clipEps, hi = 1.0 + clipEps;
     double ratioC = ratio < lo ? lo : (ratio > hi ? hi : ratio);
@@ -718,8 +738,28 @@ void orc_mingru_grad_seq(const double* params, const double* obsAll, const doubl
     if (newval) newval[t] = vnew;
     const double* hf = hfin + t * H;
     for (size_t j = 0; j < H; j++) dhf[j] = 0.0;
+    if (W > 1) {
+      /* per head: p_k and sum_j p_j x_j of that head; pk then holds the logit gradient */
+      size_t off = 0;
+      for (size_t h = 0; h < W; h++) {
+        const size_t sz = (size_t)hs[h], ah = (size_t)actA[t * W + h];
+        double m = logits[off];
+        for (size_t k = 1; k < sz; k++)
+          if (logits[off + k] > m) m = logits[off + k];
+        double se = 0.0;
+        for (size_t k = 0; k < sz; k++) se += exp(logits[off + k] - m);
+        const double lh = m + log(se);
+        double po = 0.0;
+        for (size_t k = 0; k < sz; k++) po += exp(logits[off + k] - lh) * logits[off + k];
+        for (size_t k = 0; k < sz; k++) {
+          const double p = exp(logits[off + k] - lh);
+          pk[off + k] = dPol * (((k == ah) ? 1.0 : 0.0) - p) + entCoef * p * (po - logits[off + k]);
+        }
+        off += sz;
+      }
+    }
     for (size_t k = 0; k < A; k++) {
-      double dl = dPol * (((k == a) ? 1.0 : 0.0) - pk[k]) + entCoef * pk[k] * (pout - logits[k]);
+      double dl = W > 1 ? pk[k] : dPol * (((k == a) ? 1.0 : 0.0) - pk[k]) + entCoef * pk[k] * (pout - logits[k]);
       double* gw = gWDec + k * H;
       const double* w = wDec + k * H;
       for (size_t j = 0; j < H; j++) {
@@ -814,27 +854,39 @@ void orc_mingru_grad_seq(const double* params, const double* obsAll, const doubl
   free(dhf); free(dyh); free(dyg); free(dyp); free(pk);
 }
 
+void orc_mingru_grad_seq(const double* params, const double* obsAll, const double* actA, const double* advA,
+                         const double* retA, const double* oldA, const double* termA, const double* ovA, size_t T,
+                         size_t H, size_t D, size_t L, size_t A, size_t K, int encAct, double vfCoef,
+                         double entCoef, double clipEps, double vfClip, double* g, double* newlp, double* newval) {
+  orc_mingru_grad_seq_md(params, obsAll, actA, advA, retA, oldA, termA, ovA, T, H, D, L, A, K, encAct, vfCoef, entCoef,
+                         clipEps, vfClip, 1, NULL, g, newlp, newval);
+}
+
 /* The batched form the device kernel computes: B sequences packed time-major ([t*B + b] for the
  * scalars, [(t*B + b)*D + j] for obs; the layout of lean_cuda_mingru_ppo_grad, ffi/puffercuda.cu:5206),
  * summed over b in order 0..B-1 of the per-sequence gradients (the verify-mingru-grad-gpu check,
  * Exe/Puffer.lean:2398-2440). out = [g(P); newlp(T*B); newval(T*B)], the last two time-major. */
-void orc_mingru_grad_batch(const double* params, const double* obsTB, const double* scal, size_t B, size_t T,
-                           size_t H, size_t D, size_t L, size_t A, size_t K, int encAct, double vfCoef,
-                           double entCoef, double clipEps, double vfClip, double* out) {
-  const size_t P = orc_mg_param_count(D, H, L, A, K), nb = T * B;
+/* W > 1: scal = [act (W per row, [(t*B + b)*W + h]) | adv | ret | old | term | ov], (W + 5)*T*B values
+ * (the packed layout of ffi/puffercuda.cu:5216-5221). */
+void orc_mingru_grad_batch_md(const double* params, const double* obsTB, const double* scal, size_t B, size_t T,
+                              size_t H, size_t D, size_t L, size_t A, size_t K, int encAct, double vfCoef,
+                              double entCoef, double clipEps, double vfClip, size_t W, const int* hs, double* out) {
+  const size_t P = orc_mg_param_count(D, H, L, A, K), nb = T * B, Wa = W < 1 ? 1 : W;
   double* gb = (double*)malloc(sizeof(double) * P);
   double* so = (double*)malloc(sizeof(double) * T * D);
-  double* sc = (double*)malloc(sizeof(double) * 6 * T);
+  double* sc = (double*)malloc(sizeof(double) * (Wa + 5) * T);
   double* nl = (double*)malloc(sizeof(double) * T);
   double* nv = (double*)malloc(sizeof(double) * T);
   for (size_t i = 0; i < P; i++) out[i] = 0.0;
   for (size_t b = 0; b < B; b++) {
     for (size_t t = 0; t < T; t++) {
       for (size_t j = 0; j < D; j++) so[t * D + j] = obsTB[(t * B + b) * D + j];
-      for (size_t q = 0; q < 6; q++) sc[q * T + t] = scal[q * nb + t * B + b];
+      for (size_t h = 0; h < Wa; h++) sc[t * Wa + h] = scal[(t * B + b) * Wa + h];
+      for (size_t q = 1; q < 6; q++) sc[(Wa + q - 1) * T + t] = scal[(Wa + q - 1) * nb + t * B + b];
     }
-    orc_mingru_grad_seq(params, so, sc, sc + T, sc + 2 * T, sc + 3 * T, sc + 4 * T, sc + 5 * T, T, H, D, L, A, K,
-                        encAct, vfCoef, entCoef, clipEps, vfClip, gb, nl, nv);
+    const double* s1 = sc + Wa * T;
+    orc_mingru_grad_seq_md(params, so, sc, s1, s1 + T, s1 + 2 * T, s1 + 3 * T, s1 + 4 * T, T, H, D, L, A, K, encAct,
+                           vfCoef, entCoef, clipEps, vfClip, Wa, hs, gb, nl, nv);
     for (size_t i = 0; i < P; i++) out[i] = out[i] + gb[i];
     for (size_t t = 0; t < T; t++) {
       out[P + t * B + b] = nl[t];
@@ -842,6 +894,12 @@ void orc_mingru_grad_batch(const double* params, const double* obsTB, const doub
     }
   }
   free(gb); free(so); free(sc); free(nl); free(nv);
+}
+void orc_mingru_grad_batch(const double* params, const double* obsTB, const double* scal, size_t B, size_t T,
+                           size_t H, size_t D, size_t L, size_t A, size_t K, int encAct, double vfCoef,
+                           double entCoef, double clipEps, double vfClip, double* out) {
+  orc_mingru_grad_batch_md(params, obsTB, scal, B, T, H, D, L, A, K, encAct, vfCoef, entCoef, clipEps, vfClip, 1, NULL,
+                           out);
 }
 
 /* Prioritised segment sampling (ffi/pufferffi.c:1094-1125, lean_ffi_prio_sample):
@@ -894,10 +952,12 @@ void orc_prio_sample(const double* advL1, size_t N, size_t mbSegs, double prioAl
  * advMean / advStd over the Bmb*T sampled advantages (bi outer, t inner, population std), then for
  * os = t*Bmb + bi, si = seg[bi]*T + t: act = (double)(u64)act[si], adv = mbPrio[bi]*(a - mean)/(std + 1e-8),
  * ret = a + v, old = logp[si], term = term[si] > 0.5, ov = v. out = [act|adv|ret|old|term|ov] (6 * T * Bmb). */
-void orc_gather_seq_minibatch(const double* actCol, const double* logpCol, const double* termCol,
-                              const double* advFlat, const double* valueBuf, const double* segIdx,
-                              const double* mbPrio, size_t T, size_t Bmb, double* out) {
-  size_t nb = T * Bmb;
+/* W > 1: actCol holds W actions per row ([(e*T + t)*W + h]) and the act block of out is W wide
+ * ([os*W + h]); out = (W + 5)*T*Bmb values. */
+void orc_gather_seq_minibatch_md(const double* actCol, const double* logpCol, const double* termCol,
+                                 const double* advFlat, const double* valueBuf, const double* segIdx,
+                                 const double* mbPrio, size_t T, size_t Bmb, size_t W, double* out) {
+  size_t nb = T * Bmb, Wa = W < 1 ? 1 : W;
   double navd = (double)(nb > 0 ? nb : 1), sum = 0.0;
   for (size_t bi = 0; bi < Bmb; bi++) {
     size_t e = (size_t)segIdx[bi];
@@ -915,11 +975,11 @@ void orc_gather_seq_minibatch(const double* actCol, const double* logpCol, const
   }
   double advStd = sqrt(sq / navd);
   double* pact = out;
-  double* padv = out + nb;
-  double* pret = out + 2 * nb;
-  double* pold = out + 3 * nb;
-  double* pterm = out + 4 * nb;
-  double* pov = out + 5 * nb;
+  double* padv = out + Wa * nb;
+  double* pret = out + (Wa + 1) * nb;
+  double* pold = out + (Wa + 2) * nb;
+  double* pterm = out + (Wa + 3) * nb;
+  double* pov = out + (Wa + 4) * nb;
   double stde = advStd + 1e-8;
   for (size_t bi = 0; bi < Bmb; bi++) {
     size_t e = (size_t)segIdx[bi];
@@ -927,7 +987,7 @@ void orc_gather_seq_minibatch(const double* actCol, const double* logpCol, const
     for (size_t t = 0; t < T; t++) {
       size_t si = e * T + t, os = t * Bmb + bi;
       double a = advFlat[si], v = valueBuf[si];
-      pact[os] = (double)(unsigned long long)actCol[si];
+      for (size_t h = 0; h < Wa; h++) pact[os * Wa + h] = (double)(unsigned long long)actCol[si * Wa + h];
       padv[os] = mp * (a - advMean) / stde;
       pret[os] = a + v;
       pold[os] = logpCol[si];
@@ -935,6 +995,11 @@ void orc_gather_seq_minibatch(const double* actCol, const double* logpCol, const
       pterm[os] = termCol[si] > 0.5 ? 1.0 : 0.0;
     }
   }
+}
+void orc_gather_seq_minibatch(const double* actCol, const double* logpCol, const double* termCol,
+                              const double* advFlat, const double* valueBuf, const double* segIdx,
+                              const double* mbPrio, size_t T, size_t Bmb, double* out) {
+  orc_gather_seq_minibatch_md(actCol, logpCol, termCol, advFlat, valueBuf, segIdx, mbPrio, T, Bmb, 1, out);
 }
 
 /* applyMuonMG (Puffer/RL/MinGRUTrain.lean:265-279): stepMat on wEnc, every layer, wDec and wVal; stepVec
@@ -977,21 +1042,22 @@ void orc_apply_muon_mg(double* pm, const double* g, size_t D, size_t H, size_t L
  * summed BPTT gradient over the sampled segments -> value/ratio iterate (the last sampler of a segment
  * writes) -> gradClipMG with sc = 1/(Bmb*T) -> applyMuonMG. Columns are rows e*T + t; obs is
  * [(e*T + t)*D + j]. pm = [params; mom] updated in place. Returns the advanced rng. */
-uint64_t orc_mingru_update(double* pm, const double* obs, const double* rew, const double* term, const double* act,
-                           const double* logp, const double* val0, const double* boot, size_t N, size_t T,
-                           size_t D, size_t H, size_t L, size_t A, size_t K, int encAct, size_t numMB,
-                           size_t mbSegs, double gamma, double lam, double rhoClip, double cClip, double prioAlpha,
-                           double annealBeta, uint64_t rng, double lr, double wd, double mu, double eps,
-                           double vfCoef, double entCoef, double clipEps, double vfClip, double maxGradNorm,
-                           const double* coeffs, int iters) {
-  const size_t NT = N * T, P = orc_mg_param_count(D, H, L, A, K);
+/* W > 1: act holds W actions per row and the heads are the multi-discrete ones of sizes hs. */
+uint64_t orc_mingru_update_md(double* pm, const double* obs, const double* rew, const double* term, const double* act,
+                              const double* logp, const double* val0, const double* boot, size_t N, size_t T,
+                              size_t D, size_t H, size_t L, size_t A, size_t K, int encAct, size_t numMB,
+                              size_t mbSegs, double gamma, double lam, double rhoClip, double cClip, double prioAlpha,
+                              double annealBeta, uint64_t rng, double lr, double wd, double mu, double eps,
+                              double vfCoef, double entCoef, double clipEps, double vfClip, double maxGradNorm,
+                              const double* coeffs, int iters, size_t W, const int* hs) {
+  const size_t NT = N * T, P = orc_mg_param_count(D, H, L, A, K), Wa = W < 1 ? 1 : W;
   double* value = (double*)malloc(sizeof(double) * NT);
   double* ratio = (double*)malloc(sizeof(double) * NT);
   double* adv = (double*)malloc(sizeof(double) * NT);
   double* l1 = (double*)malloc(sizeof(double) * N);
   double* seg = (double*)malloc(sizeof(double) * mbSegs);
   double* mp = (double*)malloc(sizeof(double) * mbSegs);
-  double* sc = (double*)malloc(sizeof(double) * 6 * T * mbSegs);
+  double* sc = (double*)malloc(sizeof(double) * (Wa + 5) * T * mbSegs);
   double* obsTB = (double*)malloc(sizeof(double) * T * mbSegs * D);
   double* gout = (double*)malloc(sizeof(double) * (P + 2 * T * mbSegs));
   memcpy(value, val0, sizeof(double) * NT);
@@ -1001,13 +1067,14 @@ uint64_t orc_mingru_update(double* pm, const double* obs, const double* rew, con
     orc_adv_l1(adv, N, T, l1);
     orc_prio_sample(l1, N, mbSegs, prioAlpha, annealBeta, rng, seg, mp);
     rng += (uint64_t)mbSegs * ORC_GOLD;
-    orc_gather_seq_minibatch(act, logp, term, adv, value, seg, mp, T, mbSegs, sc);
+    orc_gather_seq_minibatch_md(act, logp, term, adv, value, seg, mp, T, mbSegs, Wa, sc);
     for (size_t t = 0; t < T; t++)
       for (size_t b = 0; b < mbSegs; b++) {
         size_t e = (size_t)seg[b];
         memcpy(obsTB + (t * mbSegs + b) * D, obs + (e * T + t) * D, sizeof(double) * D);
       }
-    orc_mingru_grad_batch(pm, obsTB, sc, mbSegs, T, H, D, L, A, K, encAct, vfCoef, entCoef, clipEps, vfClip, gout);
+    orc_mingru_grad_batch_md(pm, obsTB, sc, mbSegs, T, H, D, L, A, K, encAct, vfCoef, entCoef, clipEps, vfClip, Wa, hs,
+                             gout);
     for (size_t b = 0; b < mbSegs; b++) {
       size_t e = (size_t)seg[b];
       for (size_t t = 0; t < T; t++) {
@@ -1021,6 +1088,17 @@ uint64_t orc_mingru_update(double* pm, const double* obs, const double* rew, con
   }
   free(value); free(ratio); free(adv); free(l1); free(seg); free(mp); free(sc); free(obsTB); free(gout);
   return rng;
+}
+uint64_t orc_mingru_update(double* pm, const double* obs, const double* rew, const double* term, const double* act,
+                           const double* logp, const double* val0, const double* boot, size_t N, size_t T,
+                           size_t D, size_t H, size_t L, size_t A, size_t K, int encAct, size_t numMB,
+                           size_t mbSegs, double gamma, double lam, double rhoClip, double cClip, double prioAlpha,
+                           double annealBeta, uint64_t rng, double lr, double wd, double mu, double eps,
+                           double vfCoef, double entCoef, double clipEps, double vfClip, double maxGradNorm,
+                           const double* coeffs, int iters) {
+  return orc_mingru_update_md(pm, obs, rew, term, act, logp, val0, boot, N, T, D, H, L, A, K, encAct, numMB, mbSegs,
+                              gamma, lam, rhoClip, cClip, prioAlpha, annealBeta, rng, lr, wd, mu, eps, vfCoef, entCoef,
+                              clipEps, vfClip, maxGradNorm, coeffs, iters, 1, NULL);
 }
 
 /* initMinGRU (Puffer/RL/MinGRUTrain.lean:311-344) flattened: wEnc bound sqrt(2)/sqrt(D), layers

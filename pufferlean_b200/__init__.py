@@ -97,6 +97,9 @@ def _bind_optional(L):
                          C.c_int),
         "pl_mg_last_launches": ([_vp], C.c_uint64),
         "pl_mg_set_comm": ([_vp, _vp, C.c_int, C.c_int], C.c_int),
+        "pl_mg_set_heads": ([_vp, _sz, _dp], C.c_int),
+        "pl_mingru_ppo_grad_md": ([_dp] * 3 + [_sz, _sz, C.POINTER(MgNet), _sz, _dp] + [_d] * 4 + [C.c_uint8, _dp],
+                                  C.c_int),
         "pl_train_update_wide_resident": ([_sz] + [_dp] * 6 + [_sz, _dp, _dp] + [_sz] * 5 + [C.c_uint32, _sz, _sz]
                                           + [_d] * 9 + [C.c_uint8, _dp], C.c_int),
         "pl_mlp_ppo_grad_wide": ([_dp] * 7 + [_sz] * 5 + [C.c_uint32, _dp] + [_d] * 4 + [C.c_uint8, _dp], C.c_int),
@@ -304,14 +307,20 @@ def mg_param_count(D, H, L, A, K=3, enc_act=0):
 
 
 def cuda_mingru_ppo_grad(params, obs, scal, B, T, H, D, L, A, vf_coef, ent_coef, clip_eps, vf_clip, bf16=0, K=3,
-                         enc_act=0):
-    """Host mode of lean_cuda_mingru_ppo_grad: [grad(P); new_logp(T*B); new_value(T*B)] (f64)."""
+                         enc_act=0, hs=None):
+    """Host mode of lean_cuda_mingru_ppo_grad: [grad(P); new_logp(T*B); new_value(T*B)] (f64). hs: multi-discrete
+    head sizes (sum A); scal's act block then holds len(hs) actions per row."""
     net = mg_net(D, H, L, A, K, enc_act)
     P = int(lib().pl_mg_param_count(C.byref(net)))
     out = np.zeros(P + 2 * T * B)
     params, obs, scal = _f64(params), _f64(obs), _f64(scal)
-    _check(lib().pl_mingru_ppo_grad(_p(params), _p(obs), _p(scal), B, T, C.byref(net), vf_coef, ent_coef, clip_eps,
-                                    vf_clip, bf16, _p(out)), "pl_mingru_ppo_grad")
+    if hs is None:
+        _check(lib().pl_mingru_ppo_grad(_p(params), _p(obs), _p(scal), B, T, C.byref(net), vf_coef, ent_coef,
+                                        clip_eps, vf_clip, bf16, _p(out)), "pl_mingru_ppo_grad")
+    else:
+        h = _f64(hs)
+        _check(lib().pl_mingru_ppo_grad_md(_p(params), _p(obs), _p(scal), B, T, C.byref(net), h.size, _p(h), vf_coef,
+                                           ent_coef, clip_eps, vf_clip, bf16, _p(out)), "pl_mingru_ppo_grad_md")
     return out
 
 
@@ -344,6 +353,11 @@ class MgSession:
         if self.h:
             lib().pl_mg_destroy(self.h)
             self.h = _vp()
+
+    def set_heads(self, W, hs=None):
+        """W multi-discrete heads (act columns W wide per row); call before set_columns."""
+        h = _f64(hs) if hs is not None else None
+        _check(lib().pl_mg_set_heads(self.h, W, _p(h) if h is not None else None), "pl_mg_set_heads")
 
     def set_columns(self, rew, term, act, logp, val, boot):
         arrs = [_f64(a) for a in (rew, term, act, logp, val, boot)]

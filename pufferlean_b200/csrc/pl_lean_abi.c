@@ -311,7 +311,11 @@ LEAN_EXPORT lean_obj_res lean_cuda_mg_prep(lean_obj_arg rew, lean_obj_arg term, 
                                            lean_obj_arg val, lean_obj_arg boot, size_t N, size_t T, size_t K,
                                            lean_obj_arg w) {
   (void)w;
-  int rc = K > 1 ? -4 : mg_session(N, T);
+  /* K > 1: the act column holds K multi-discrete actions per row; their head sizes arrive with the
+   * gradient call (lean_cuda_mingru_ppo_grad's hs) */
+  int rc = mg_session(N, T);
+  if (!rc) rc = pl_mg_set_heads(g_mg, K < 1 ? 1 : K, NULL);
+  if (!rc && fan(act) < N * T * (K < 1 ? 1 : K)) rc = PL_ERR_INVALID;
   if (!rc) rc = pl_mg_set_columns(g_mg, fa(rew), fa(term), fa(act), fa(logp), fa(val), fa(boot));
   lean_dec(rew);
   lean_dec(term);
@@ -319,10 +323,6 @@ LEAN_EXPORT lean_obj_res lean_cuda_mg_prep(lean_obj_arg rew, lean_obj_arg term, 
   lean_dec(logp);
   lean_dec(val);
   lean_dec(boot);
-  if (K > 1) {
-    return lean_io_result_mk_error(lean_mk_io_user_error(
-        lean_mk_string("pufferlean_b200: lean_cuda_mg_prep: multi-discrete action columns (K > 1) are not supported")));
-  }
   if (rc) return io_fail("lean_cuda_mg_prep");
   return lean_io_result_mk_ok(lean_box(0));
 }
@@ -374,17 +374,18 @@ LEAN_EXPORT lean_obj_res lean_cuda_mingru_ppo_grad(lean_obj_arg pa, lean_obj_arg
   lean_obj_res out = NULL;
   int rc = 0;
   const char* why = "lean_cuda_mingru_ppo_grad";
-  if (K > 1) {
-    rc = -4;
-    why = "lean_cuda_mingru_ppo_grad (multi-discrete heads, K > 1, are not supported)";
+  const size_t W = K < 1 ? 1 : K; /* K > 1: multi-discrete heads of sizes hs (sum A) */
+  if (W > 1 && fan(hs) < W) {
+    rc = -1;
+    why = "lean_cuda_mingru_ppo_grad (K > 1 heads without their K sizes in hs)";
   } else if (host) {
     out = new_fa(P + 2 * T * B);
-    if (fan(pa) < P || fan(obs) < T * B * D || fan(scal) < 6 * T * B) {
+    if (fan(pa) < P || fan(obs) < T * B * D || fan(scal) < (W + 5) * T * B) {
       rc = -1;
-      why = "lean_cuda_mingru_ppo_grad (host mode: params, obs or scal shorter than P, T*B*D, 6*T*B)";
+      why = "lean_cuda_mingru_ppo_grad (host mode: params, obs or scal shorter than P, T*B*D, (K+5)*T*B)";
     } else {
-      rc = pl_mingru_ppo_grad(fa(pa), fa(obs), fa(scal), B, T, &net, vfCoef, entCoef, clipEps, vfClip, mg_bf16(),
-                              fa(out));
+      rc = pl_mingru_ppo_grad_md(fa(pa), fa(obs), fa(scal), B, T, &net, W, W > 1 ? fa(hs) : NULL, vfCoef, entCoef,
+                                 clipEps, vfClip, mg_bf16(), fa(out));
     }
   } else {
     const int resident_sample = fan(segIdx) == 0 && fan(mbPrio) == 0;
@@ -396,7 +397,9 @@ LEAN_EXPORT lean_obj_res lean_cuda_mingru_ppo_grad(lean_obj_arg pa, lean_obj_arg
       rc = -1;
       why = "lean_cuda_mingru_ppo_grad (empty params and no resident Muon step has run yet)";
     } else {
-      rc = pl_mg_grad(g_mg, &net, handle, handle ? NULL : fa(pa), resident_sample ? NULL : fa(segIdx),
+      rc = pl_mg_set_heads(g_mg, W, W > 1 ? fa(hs) : NULL);
+      if (!rc)
+        rc = pl_mg_grad(g_mg, &net, handle, handle ? NULL : fa(pa), resident_sample ? NULL : fa(segIdx),
                       resident_sample ? NULL : fa(mbPrio), B, vfCoef, entCoef, clipEps, vfClip, mg_bf16(), NULL);
     }
     out = new_fa(0);

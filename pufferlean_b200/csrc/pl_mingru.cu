@@ -152,14 +152,14 @@ __global__ void mg_gather_scal_kernel(const double* __restrict__ act, const doub
                                       const double* __restrict__ term, const double* __restrict__ adv,
                                       const double* __restrict__ value, const double* __restrict__ seg,
                                       const double* __restrict__ mbp, const double* __restrict__ ms, int Bmb, int T,
-                                      int* act_i, float* adv_f, float* ret_f, float* olp_f, float* ov_f,
+                                      int W, int* act_i, float* adv_f, float* ret_f, float* olp_f, float* ov_f,
                                       float* term_f) {
   const long n = (long)T * Bmb;
   for (long os = (long)blockIdx.x * blockDim.x + threadIdx.x; os < n; os += (long)gridDim.x * blockDim.x) {
     const int t = (int)(os / Bmb), b = (int)(os - (long)t * Bmb);
     const long si = (long)seg[b] * T + t;
     const double a = adv[si], v = value[si];
-    act_i[os] = (int)(unsigned long long)act[si];
+    for (int h = 0; h < W; h++) act_i[os * W + h] = (int)(unsigned long long)act[si * W + h];
     adv_f[os] = (float)(mbp[b] * (a - ms[0]) / ms[1]);
     ret_f[os] = (float)(a + v);
     olp_f[os] = (float)logp[si];
@@ -167,16 +167,18 @@ __global__ void mg_gather_scal_kernel(const double* __restrict__ act, const doub
     term_f[os] = term[si] > 0.5 ? 1.f : 0.f;
   }
 }
-// Host-mode scalars: scal = [act | adv | ret | old | term | ov], each R time-major entries.
-__global__ void mg_scal_rows_kernel(const double* __restrict__ scal, long R, int* act_i, float* adv_f, float* ret_f,
-                                    float* olp_f, float* ov_f, float* term_f) {
+// Host-mode scalars: scal = [act | adv | ret | old | term | ov], R time-major entries each, the act
+// block W per row ([r*W + h]) with multi-discrete heads (ffi/puffercuda.cu:5216-5221).
+__global__ void mg_scal_rows_kernel(const double* __restrict__ scal, long R, int W, int* act_i, float* adv_f,
+                                    float* ret_f, float* olp_f, float* ov_f, float* term_f) {
+  const double* s1 = scal + (long)W * R;
   for (long r = (long)blockIdx.x * blockDim.x + threadIdx.x; r < R; r += (long)gridDim.x * blockDim.x) {
-    act_i[r] = (int)(unsigned long long)scal[r];
-    adv_f[r] = (float)scal[R + r];
-    ret_f[r] = (float)scal[2 * R + r];
-    olp_f[r] = (float)scal[3 * R + r];
-    term_f[r] = scal[4 * R + r] != 0.0 ? 1.f : 0.f;
-    ov_f[r] = (float)scal[5 * R + r];
+    for (int h = 0; h < W; h++) act_i[r * W + h] = (int)(unsigned long long)scal[r * W + h];
+    adv_f[r] = (float)s1[r];
+    ret_f[r] = (float)s1[R + r];
+    olp_f[r] = (float)s1[2 * R + r];
+    term_f[r] = s1[3 * R + r] != 0.0 ? 1.f : 0.f;
+    ov_f[r] = (float)s1[4 * R + r];
   }
 }
 
@@ -444,6 +446,92 @@ __global__ void mg_ppo_rows_kernel(const float* __restrict__ Out, int ldo, const
       const float du = (vnew - rt) * (vnew - rt), cc = (vcl - rt) * (vcl - rt);
       lr[1] = 0.5f * ((vfclip > 0.f && cc > du) ? cc : du);
       lr[2] = lse - pout;  // entropy: -sum p (l - lse)
+      lr[3] = -lgr;
+      lr[4] = (ratio - 1.f) - lgr;
+      lr[5] = (ratio < lo || ratio > hi) ? 1.f : 0.f;
+    }
+  }
+}
+
+// Multi-discrete heads (ffi/puffercuda.cu:4940-4980, k_mg_ppo_b_md): W heads of sizes hs over the A
+// logits; per head the max-subtracted softmax; the joint log-prob accumulated in double as
+// sum_h log(exp(x_a - m) / se), the form of the sampler that produced the old log-prob; one clipped
+// ratio for the row. An action index outside its head is held inside it (valid columns never are).
+template <typename S>
+__global__ void mg_ppo_rows_md_kernel(const float* __restrict__ Out, int ldo, const float* __restrict__ bout, long R,
+                                      int A, int Op, int W, const int* __restrict__ hs, const int* __restrict__ act,
+                                      const float* __restrict__ adv, const float* __restrict__ ret,
+                                      const float* __restrict__ olp, const float* __restrict__ ov, float vf, float ent,
+                                      float clip, float vfclip, S* dOut, float* newlp, float* newval, float* lossrow) {
+  for (long r = (long)blockIdx.x * blockDim.x + threadIdx.x; r < R; r += (long)gridDim.x * blockDim.x) {
+    const float* o = Out + r * ldo;
+    const int* ar = act + r * W;
+    auto lg = [&](int k) { return o[k] + bout[k]; };
+    double joint = 0.0;
+    float entr = 0.f;
+    int off = 0;
+    for (int h = 0; h < W; h++) {
+      const int sz = hs[h];
+      int a = ar[h];
+      a = a < 0 ? 0 : (a >= sz ? sz - 1 : a);
+      float mx = lg(off);
+      for (int k = 1; k < sz; k++) mx = fmaxf(mx, lg(off + k));
+      float se = 0.f;
+      for (int k = 0; k < sz; k++) se += expf(lg(off + k) - mx);
+      joint += log(exp((double)lg(off + a) - (double)mx) / (double)se);
+      if (lossrow) {
+        const float lse = mx + logf(se);
+        float pout = 0.f;
+        for (int k = 0; k < sz; k++) pout += expf(lg(off + k) - lse) * lg(off + k);
+        entr += lse - pout;
+      }
+      off += sz;
+    }
+    const float ratio = (float)exp(joint - (double)olp[r]);
+    const float lo = 1.f - clip, hi = 1.f + clip;
+    const float rc = ratio < lo ? lo : (ratio > hi ? hi : ratio);
+    const float ad = adv[r];
+    const float s1 = ad * ratio, s2 = ad * rc;
+    const float dPol = s1 <= s2 ? ad * ratio : ad * ((lo < ratio && ratio < hi) ? 1.f : 0.f) * ratio;
+    const float vnew = lg(A), rt = ret[r], vold = ov[r];
+    float dvl = vnew - rt;
+    float vcl = vnew;
+    if (vfclip > 0.f) {
+      const float dd = vnew - vold;
+      vcl = vold + (dd < -vfclip ? -vfclip : (dd > vfclip ? vfclip : dd));
+      const float du = (vnew - rt) * (vnew - rt), cc = (vcl - rt) * (vcl - rt);
+      if (!(du >= cc) && !(dd > -vfclip && dd < vfclip)) dvl = 0.f;
+    }
+    S* d = dOut + r * Op;
+    off = 0;
+    for (int h = 0; h < W; h++) {
+      const int sz = hs[h];
+      int a = ar[h];
+      a = a < 0 ? 0 : (a >= sz ? sz - 1 : a);
+      float mx = lg(off);
+      for (int k = 1; k < sz; k++) mx = fmaxf(mx, lg(off + k));
+      float se = 0.f;
+      for (int k = 0; k < sz; k++) se += expf(lg(off + k) - mx);
+      const float lse = mx + logf(se);
+      float pout = 0.f;
+      for (int k = 0; k < sz; k++) pout += expf(lg(off + k) - lse) * lg(off + k);
+      for (int k = 0; k < sz; k++) {
+        const float l = lg(off + k), p = expf(l - lse);
+        stv(d, off + k, dPol * ((k == a ? 1.f : 0.f) - p) + ent * p * (pout - l));
+      }
+      off += sz;
+    }
+    stv(d, A, -vf * dvl);
+    for (int k = A + 1; k < Op; k++) stv(d, k, 0.f);
+    newlp[r] = (float)joint;
+    newval[r] = vnew;
+    if (lossrow) {
+      const float lgr = (float)joint - olp[r];
+      float* lr = lossrow + r * 8;
+      lr[0] = fmaxf(-ad * ratio, -ad * rc);
+      const float du = (vnew - rt) * (vnew - rt), cc = (vcl - rt) * (vcl - rt);
+      lr[1] = 0.5f * ((vfclip > 0.f && cc > du) ? cc : du);
+      lr[2] = entr;
       lr[3] = -lgr;
       lr[4] = (ratio - 1.f) - lgr;
       lr[5] = (ratio < lo || ratio > hi) ? 1.f : 0.f;
@@ -757,6 +845,10 @@ struct pl_mg {
   double *rew = nullptr, *term = nullptr, *act = nullptr, *logp = nullptr, *val0 = nullptr, *boot = nullptr;
   double *value = nullptr, *ratio = nullptr, *adv = nullptr, *l1 = nullptr;
   bool cols_valid = false;
+  // action heads: W = 1 one categorical head; W > 1 multi-discrete heads of sizes hs (act holds W per row)
+  int W = 1;
+  std::vector<int> hs;
+  int* hs_dev = nullptr;
   // obs trajectory
   const float* traj = nullptr;
   float* traj_own = nullptr;
@@ -780,7 +872,8 @@ struct pl_mg {
     void* dh[2] = {nullptr, nullptr};
     void* dY = nullptr;
     void* dhn = nullptr;
-    int* act_i = nullptr;
+    int* act_i = nullptr;  // [R x Wact]
+    int Wact = 1;
     float *adv_f = nullptr, *ret_f = nullptr, *olp_f = nullptr, *ov_f = nullptr, *term_f = nullptr;
     float *newlp = nullptr, *newval = nullptr, *lossrow = nullptr;
     double* ms = nullptr;
@@ -872,7 +965,7 @@ MgShape shape_of(const pl_mg_net* net) {
 
 int ensure_work(pl_mg* s, const MgShape& sh, long Bmb, long T, bool fast) {
   auto& w = s->w;
-  if (s->have_work && w.sh == sh && w.Bmb == Bmb && w.T == T && w.fast == fast) return PL_OK;
+  if (s->have_work && w.sh == sh && w.Bmb == Bmb && w.T == T && w.fast == fast && w.Wact == s->W) return PL_OK;
   if (fast) PL_REQUIRE(sh.H % 8 == 0, PL_ERR_UNSUPPORTED, "MinGRU bf16 tier needs H %% 8 == 0 (H=%ld)", sh.H);
   free_list(w.allocs);
   s->have_work = false;
@@ -903,7 +996,8 @@ int ensure_work(pl_mg* s, const MgShape& sh, long Bmb, long T, bool fast) {
   w.dh[1] = act_buf(R * H);
   w.dY = act_buf(R * KH);
   if (sh.K == 3) w.dhn = act_buf(R * H);
-  w.act_i = mg_alloc<int>(w.allocs, R, f);
+  w.Wact = s->W;
+  w.act_i = mg_alloc<int>(w.allocs, (size_t)R * s->W, f);
   w.adv_f = mg_alloc<float>(w.allocs, R, f);
   w.ret_f = mg_alloc<float>(w.allocs, R, f);
   w.olp_f = mg_alloc<float>(w.allocs, R, f);
@@ -1151,11 +1245,20 @@ int bptt(pl_mg* s, double vf, double ent, double clip, double vfclip, bool losse
                       w.Op, 1.f, st);
   }
   if (rc) return rc;
-  mg_ppo_rows_kernel<S><<<blocks_for(R, 128), 128, 0, st>>>(
-      w.Out, (int)w.Op, w.bout, R, (int)A, (int)w.Op, w.act_i, w.adv_f, w.ret_f, w.olp_f, w.ov_f, (float)vf,
-      (float)ent, (float)clip, (float)vfclip, (S*)w.dOut, w.newlp, w.newval, losses ? w.lossrow : nullptr);
-  count_launch();
-  PL_LAUNCH("mg_ppo_rows_kernel");
+  if (s->W > 1) {
+    mg_ppo_rows_md_kernel<S><<<blocks_for(R, 128), 128, 0, st>>>(
+        w.Out, (int)w.Op, w.bout, R, (int)A, (int)w.Op, s->W, s->hs_dev, w.act_i, w.adv_f, w.ret_f, w.olp_f, w.ov_f,
+        (float)vf, (float)ent, (float)clip, (float)vfclip, (S*)w.dOut, w.newlp, w.newval,
+        losses ? w.lossrow : nullptr);
+    count_launch();
+    PL_LAUNCH("mg_ppo_rows_md_kernel");
+  } else {
+    mg_ppo_rows_kernel<S><<<blocks_for(R, 128), 128, 0, st>>>(
+        w.Out, (int)w.Op, w.bout, R, (int)A, (int)w.Op, w.act_i, w.adv_f, w.ret_f, w.olp_f, w.ov_f, (float)vf,
+        (float)ent, (float)clip, (float)vfclip, (S*)w.dOut, w.newlp, w.newval, losses ? w.lossrow : nullptr);
+    count_launch();
+    PL_LAUNCH("mg_ppo_rows_kernel");
+  }
   // ---- head gradients
   rc = colsum<S>(s, (const S*)w.dOut, R, w.Op, (int)(A + 1), w.gbout, st);
   if (rc) return rc;
@@ -1437,6 +1540,18 @@ int muon_step(pl_mg* s, size_t handle, const double* gClip, double lr, double wd
   return PL_OK;
 }
 
+// Multi-discrete heads must cover the network's A logits exactly.
+int check_heads(const pl_mg* s, const pl_mg_net* net) {
+  if (s->W <= 1) return PL_OK;
+  PL_REQUIRE((int)s->hs.size() == s->W, PL_ERR_INVALID,
+             "MinGRU: %d-wide action column but no head sizes (pl_mg_set_heads with the sizes)", s->W);
+  long sum = 0;
+  for (int v : s->hs) sum += v;
+  PL_REQUIRE(sum == (long)net->A, PL_ERR_INVALID, "MinGRU: head sizes sum to %ld, the network has A = %zu logits", sum,
+             net->A);
+  return PL_OK;
+}
+
 int alloc_columns(pl_mg* s) {
   bool f = false;
   const size_t NT = (size_t)s->N * s->T;
@@ -1528,7 +1643,7 @@ static int mg_set_columns_impl(pl_mg* s, const double* rew, const double* term, 
   const size_t NT = (size_t)s->N * s->T;
   PL_CUDA(cudaMemcpyAsync(s->rew, rew, NT * 8, kind, st));
   PL_CUDA(cudaMemcpyAsync(s->term, term, NT * 8, kind, st));
-  PL_CUDA(cudaMemcpyAsync(s->act, act, NT * 8, kind, st));
+  PL_CUDA(cudaMemcpyAsync(s->act, act, NT * (size_t)s->W * 8, kind, st));
   PL_CUDA(cudaMemcpyAsync(s->logp, logp, NT * 8, kind, st));
   PL_CUDA(cudaMemcpyAsync(s->val0, val, NT * 8, kind, st));
   PL_CUDA(cudaMemcpyAsync(s->boot, boot, (size_t)s->N * 8, kind, st));
@@ -1552,6 +1667,35 @@ int pl_mg_set_columns(pl_mg* s, const double* rew, const double* term, const dou
 int pl_mg_set_columns_dev(pl_mg* s, const double* rew, const double* term, const double* act, const double* logp,
                           const double* val, const double* boot, void* stream) {
   return mg_set_columns_impl(s, rew, term, act, logp, val, boot, cudaMemcpyDeviceToDevice, (cudaStream_t)stream);
+}
+
+int pl_mg_set_heads(pl_mg* s, size_t W, const double* head_sizes) {
+  using namespace pl;
+  PL_REQUIRE(s != nullptr && W >= 1 && W <= 4096, PL_ERR_INVALID, "pl_mg_set_heads: bad width %zu", W);
+  if ((int)W != s->W) {
+    // the action column changes width: reallocate it; the columns must be set again
+    bool f = false;
+    s->act = mg_alloc<double>(s->allocs, (size_t)s->N * s->T * W, f);
+    if (f) return PL_ERR_NOMEM;
+    s->W = (int)W;
+    s->cols_valid = false;
+    s->prio_fresh = false;
+    s->hs.clear();
+    s->hs_dev = W > 1 ? mg_alloc<int>(s->allocs, W, f) : nullptr;
+    if (f) return PL_ERR_NOMEM;
+  }
+  if (W > 1 && head_sizes) {
+    std::vector<int> hv(W);
+    for (size_t i = 0; i < W; i++) {
+      hv[i] = (int)head_sizes[i];
+      PL_REQUIRE(hv[i] >= 1, PL_ERR_INVALID, "pl_mg_set_heads: head %zu has size %d", i, hv[i]);
+    }
+    if (hv != s->hs) {
+      PL_CUDA(cudaMemcpy(s->hs_dev, hv.data(), sizeof(int) * W, cudaMemcpyHostToDevice));
+      s->hs = hv;
+    }
+  }
+  return PL_OK;
 }
 
 int pl_mg_set_comm(pl_mg* s, void* comm, int rank, int world) {
@@ -1650,6 +1794,8 @@ int pl_mg_grad(pl_mg* s, const pl_mg_net* net, size_t handle, const double* para
              "pl_mg_grad: segIdx and mbPrio are both host arrays or both NULL (the resident sample)");
   PL_REQUIRE(Bmb > 0 && Bmb < (1u << 24), PL_ERR_INVALID, "pl_mg_grad: bad minibatch size %zu", Bmb);
   PL_REQUIRE(s->cols_valid, PL_ERR_INVALID, "pl_mg_grad: no columns (call pl_mg_set_columns first)");
+  rc = check_heads(s, net);
+  if (rc) return rc;
   PL_REQUIRE(s->traj && s->trajD == (long)net->D, PL_ERR_INVALID,
              "pl_mg_grad: no obs trajectory of width D=%zu (call pl_mg_set_obs first)", net->D);
   if (!segIdx)
@@ -1699,8 +1845,8 @@ int pl_mg_grad(pl_mg* s, const pl_mg_net* net, size_t handle, const double* para
     count_launch();
   }
   mg_gather_scal_kernel<<<blocks_for(w.R), 256, 0, st>>>(s->act, s->logp, s->term, s->adv, s->value, s->seg, s->mbp,
-                                                         w.ms, Bi, T, w.act_i, w.adv_f, w.ret_f, w.olp_f, w.ov_f,
-                                                         w.term_f);
+                                                         w.ms, Bi, T, s->W, w.act_i, w.adv_f, w.ret_f, w.olp_f,
+                                                         w.ov_f, w.term_f);
   if (w.fast)
     mg_gather_obs_kernel<__nv_bfloat16><<<blocks_for(w.R * w.Dp), 256, 0, st>>>(s->traj, s->seg, Bi, T, (int)sh.D,
                                                                                (int)w.Dp, (__nv_bfloat16*)w.X);
@@ -1820,7 +1966,8 @@ static int mg_update_graph(pl_mg* s, const pl_mg_net* net, size_t handle, const 
   std::vector<double> key = {(double)net->D, (double)net->H, (double)net->L, (double)net->A, (double)net->K,
                              (double)net->enc_act, (double)handle, h->gamma, h->lam, h->rhoClip, h->cClip,
                              h->prioAlpha, h->annealBeta, h->wd, h->mu, h->eps, h->vfCoef, h->entCoef, h->clipEps,
-                             h->vfClip, h->maxGradNorm, (double)mbSegs, lr, (double)h->ns_iters};
+                             h->vfClip, h->maxGradNorm, (double)mbSegs, lr, (double)h->ns_iters, (double)s->W};
+  for (int v : s->hs) key.push_back((double)v);
   if (h->ns_coeffs)
     for (size_t i = 0; i < 3 * h->ns_iters; i++) key.push_back(h->ns_coeffs[i]);
   // everything that allocates or reads back happens before the capture
@@ -1877,6 +2024,7 @@ int pl_mg_update(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hype
   using namespace pl;
   PL_REQUIRE(s && net && h && rng && handle, PL_ERR_INVALID, "pl_mg_update: NULL argument");
   int rc = check_net(net);
+  if (!rc) rc = check_heads(s, net);
   if (rc) return rc;
   PL_REQUIRE(mbSegs > 0 && mbSegs < (1u << 24), PL_ERR_INVALID, "pl_mg_update: bad minibatch size %zu", mbSegs);
   PL_REQUIRE(s->cols_valid && s->traj && s->trajD == (long)net->D, PL_ERR_INVALID,
@@ -1902,7 +2050,15 @@ uint64_t pl_mg_last_launches(const pl_mg* s) { return s ? s->launches : 0; }
 int pl_mingru_ppo_grad(const double* params, const double* obs, const double* scal, size_t B, size_t T,
                        const pl_mg_net* net, double vfCoef, double entCoef, double clipEps, double vfClip,
                        uint8_t bf16f, double* out) {
+  return pl_mingru_ppo_grad_md(params, obs, scal, B, T, net, 1, nullptr, vfCoef, entCoef, clipEps, vfClip, bf16f, out);
+}
+
+int pl_mingru_ppo_grad_md(const double* params, const double* obs, const double* scal, size_t B, size_t T,
+                          const pl_mg_net* net, size_t W, const double* head_sizes, double vfCoef, double entCoef,
+                          double clipEps, double vfClip, uint8_t bf16f, double* out) {
   using namespace pl;
+  PL_REQUIRE(W >= 1 && (W == 1 || head_sizes), PL_ERR_INVALID, "pl_mingru_ppo_grad_md: %zu heads need their sizes",
+             W);
   int rc = check_net(net);
   if (rc) return rc;
   PL_REQUIRE(params && obs && scal && out, PL_ERR_INVALID, "pl_mingru_ppo_grad: NULL argument");
@@ -1923,16 +2079,19 @@ int pl_mingru_ppo_grad(const double* params, const double* obs, const double* sc
     if (rc) return rc;
   }
   pl_mg* s = cache[dev];
+  rc = pl_mg_set_heads(s, W, W > 1 ? head_sizes : nullptr);
+  if (!rc) rc = check_heads(s, net);
+  if (rc) return rc;
   const MgShape sh = shape_of(net);
   rc = ensure_work(s, sh, (long)B, (long)T, bf16f != 0);
   if (rc) return rc;
   auto& w = s->w;
   const long R = w.R, P = sh.P();
   double* obs_d = (double*)scratch(21, sizeof(double) * R * sh.D);
-  double* scal_d = (double*)scratch(22, sizeof(double) * 6 * R);
+  double* scal_d = (double*)scratch(22, sizeof(double) * (W + 5) * R);
   if (!obs_d || !scal_d) return PL_ERR_NOMEM;
   PL_CUDA(cudaMemcpy(obs_d, obs, sizeof(double) * R * sh.D, cudaMemcpyHostToDevice));
-  PL_CUDA(cudaMemcpy(scal_d, scal, sizeof(double) * 6 * R, cudaMemcpyHostToDevice));
+  PL_CUDA(cudaMemcpy(scal_d, scal, sizeof(double) * (W + 5) * R, cudaMemcpyHostToDevice));
   PL_CUDA(cudaMemcpy(w.params_in, params, sizeof(double) * P, cudaMemcpyHostToDevice));
   rc = refresh_shadows(s, w.params_in, 0);
   if (rc) return rc;
@@ -1942,7 +2101,8 @@ int pl_mingru_ppo_grad(const double* params, const double* obs, const double* sc
                                                                      (__nv_bfloat16*)w.X);
   else
     mg_obs_rows_kernel<float><<<blocks_for(R * w.Dp), 256>>>(obs_d, R, (int)sh.D, (int)w.Dp, (float*)w.X);
-  mg_scal_rows_kernel<<<blocks_for(R), 256>>>(scal_d, R, w.act_i, w.adv_f, w.ret_f, w.olp_f, w.ov_f, w.term_f);
+  mg_scal_rows_kernel<<<blocks_for(R), 256>>>(scal_d, R, (int)W, w.act_i, w.adv_f, w.ret_f, w.olp_f, w.ov_f,
+                                              w.term_f);
   count_launch(2);
   PL_LAUNCH("mg_host_rows");
   rc = run_bptt(s, vfCoef, entCoef, clipEps, vfClip, false, 0);
