@@ -287,6 +287,26 @@ int pl_mg_set_columns(pl_mg* s, const double* rew, const double* term, const dou
                       const double* val, const double* boot);
 int pl_mg_set_columns_dev(pl_mg* s, const double* rew, const double* term, const double* act, const double* logp,
                           const double* val, const double* boot, void* stream);
+/* Rollout-side column producer (replaces the reference's device column stamping, ffi/puffercuda.cu:242-309,
+ * and its obs-trajectory scatter, :975-983): a rollout stamps each step's device outputs straight into
+ * the session's columns, so they never pass through the host. pl_mg_stamp_step writes step `step` of
+ * envs [e0, e0 + ne): act [ne x W] (the session's head width), logp and val [ne] (device f64; val also
+ * becomes the live value), obs [ne x D] (device f32, may be NULL) into the session's own trajectory.
+ * pl_mg_stamp_finish takes the whole update's reward and terminal planes, step-major [T x N] (row
+ * s*N + e, the rollout's staging order), and boot [N] (device f64); the columns are then complete.
+ * pl_mg_take_stamped reports (once) whether the current columns came from the stamps. */
+int pl_mg_stamp_step(pl_mg* s, size_t step, size_t e0, size_t ne, const double* act, const double* logp,
+                     const double* val, const float* obs, size_t D, void* stream);
+int pl_mg_stamp_finish(pl_mg* s, const double* rew, const double* term, const double* boot, void* stream);
+int pl_mg_take_stamped(pl_mg* s, int* stamped);
+/* The same scatters on caller-owned columns (the feed-forward path's obs trajectory and columns for
+ * pl_update_set_columns_dev): src holds ne rows of `width` values for step `step`, written to rows
+ * e*T + step of col [N*T x width]; a plane is step-major [T x N]. */
+int pl_stamp_rows_f64(double* col, size_t width, size_t N, size_t T, size_t step, size_t e0, size_t ne,
+                      const double* src, void* stream);
+int pl_stamp_rows_f32(float* col, size_t width, size_t N, size_t T, size_t step, size_t e0, size_t ne,
+                      const float* src, void* stream);
+int pl_stamp_plane_f64(double* col, size_t N, size_t T, const double* plane, void* stream);
 /* Action heads of the session (the K of lean_cuda_mg_prep / lean_cuda_mingru_ppo_grad,
  * ffi/puffercuda.cu:316-335, 5204-5221): W = 1 one categorical head (the default); W > 1 multi-discrete
  * heads, the act column then holds W actions per row ([(e*T + t)*W + h]) and head_sizes (W values,

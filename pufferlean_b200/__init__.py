@@ -98,6 +98,12 @@ def _bind_optional(L):
         "pl_mg_last_launches": ([_vp], C.c_uint64),
         "pl_mg_set_comm": ([_vp, _vp, C.c_int, C.c_int], C.c_int),
         "pl_mg_set_heads": ([_vp, _sz, _dp], C.c_int),
+        "pl_mg_stamp_step": ([_vp, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _sz, _vp], C.c_int),
+        "pl_mg_stamp_finish": ([_vp] * 5, C.c_int),
+        "pl_mg_take_stamped": ([_vp, C.POINTER(C.c_int)], C.c_int),
+        "pl_stamp_rows_f64": ([_vp, _sz, _sz, _sz, _sz, _sz, _sz, _vp, _vp], C.c_int),
+        "pl_stamp_rows_f32": ([_vp, _sz, _sz, _sz, _sz, _sz, _sz, _vp, _vp], C.c_int),
+        "pl_stamp_plane_f64": ([_vp, _sz, _sz, _vp, _vp], C.c_int),
         "pl_mingru_ppo_grad_md": ([_dp] * 3 + [_sz, _sz, C.POINTER(MgNet), _sz, _dp] + [_d] * 4 + [C.c_uint8, _dp],
                                   C.c_int),
         "pl_train_update_wide_resident": ([_sz] + [_dp] * 6 + [_sz, _dp, _dp] + [_sz] * 5 + [C.c_uint32, _sz, _sz]
@@ -358,6 +364,20 @@ class MgSession:
         """W multi-discrete heads (act columns W wide per row); call before set_columns."""
         h = _f64(hs) if hs is not None else None
         _check(lib().pl_mg_set_heads(self.h, W, _p(h) if h is not None else None), "pl_mg_set_heads")
+
+    def stamp_step(self, step, e0, ne, act, logp, val, obs=None, D=0, stream=None):
+        """Rollout step `step` of envs [e0, e0 + ne) from device arrays (addresses): act [ne x W], logp, val
+        [ne] f64; obs [ne x D] f32 or None."""
+        _check(lib().pl_mg_stamp_step(self.h, step, e0, ne, act, logp, val, obs, D, stream), "pl_mg_stamp_step")
+
+    def stamp_finish(self, rew, term, boot, stream=None):
+        """The update's reward / terminal planes, step-major [T x N] device f64, and boot [N]."""
+        _check(lib().pl_mg_stamp_finish(self.h, rew, term, boot, stream), "pl_mg_stamp_finish")
+
+    def take_stamped(self):
+        r = C.c_int(0)
+        _check(lib().pl_mg_take_stamped(self.h, C.byref(r)), "pl_mg_take_stamped")
+        return bool(r.value)
 
     def set_columns(self, rew, term, act, logp, val, boot):
         arrs = [_f64(a) for a in (rew, term, act, logp, val, boot)]

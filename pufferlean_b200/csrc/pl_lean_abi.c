@@ -327,12 +327,13 @@ LEAN_EXPORT lean_obj_res lean_cuda_mg_prep(lean_obj_arg rew, lean_obj_arg term, 
   return lean_io_result_mk_ok(lean_box(0));
 }
 
-/* No rollout of this library stamps the columns, so the trainer always takes the prep call. */
+/* 1 when a rollout stamped this update's columns into the session (pl_mg_stamp_step / _finish on
+ * pl_lean_mg_session()): the trainer then skips its prep call. Read once per update. */
 LEAN_EXPORT lean_obj_res lean_cuda_mg_cols_ready(size_t N, size_t T, lean_obj_arg w) {
-  (void)N;
-  (void)T;
   (void)w;
-  return lean_io_result_mk_ok(lean_box(0));
+  int r = 0;
+  if (g_mg && g_mg_N == N && g_mg_T == T && pl_mg_take_stamped(g_mg, &r)) r = 0;
+  return lean_io_result_mk_ok(lean_box(r ? 1 : 0));
 }
 
 LEAN_EXPORT lean_obj_res lean_cuda_mg_vtrace(size_t N, size_t T, double gamma, double lam, double rhoClip,

@@ -853,6 +853,7 @@ struct pl_mg {
   const float* traj = nullptr;
   float* traj_own = nullptr;
   long trajD = 0;
+  bool stamped = false;  // the columns of this update came from pl_mg_stamp_* (read once by pl_mg_take_stamped)
   // prioritised sample
   double *prio_p = nullptr, *prio_cum = nullptr, *seg = nullptr, *mbp = nullptr;
   long seg_cap = 0, prio_B = 0;
@@ -1653,6 +1654,7 @@ static int mg_set_columns_impl(pl_mg* s, const double* rew, const double* term, 
   PL_LAUNCH("mg_fill_kernel");
   s->cols_valid = true;
   s->prio_fresh = false;
+  s->stamped = false;
   return PL_OK;
 }
 
@@ -1733,6 +1735,73 @@ int pl_mg_set_obs(pl_mg* s, const double* obs, size_t D) {
   PL_CUDA(cudaDeviceSynchronize());
   s->traj = s->traj_own;
   s->trajD = (long)D;
+  return PL_OK;
+}
+
+// ---------------------------------------------------------------- rollout-side column producer
+static int mg_own_traj(pl_mg* s, size_t D) {
+  using namespace pl;
+  const size_t n = (size_t)s->N * s->T * D;
+  if (s->traj_own && s->trajD != (long)D) {
+    cudaFree(s->traj_own);
+    s->traj_own = nullptr;
+  }
+  if (!s->traj_own) {
+    if (cudaMalloc(&s->traj_own, n * sizeof(float)) != cudaSuccess) {
+      cudaGetLastError();
+      s->traj_own = nullptr;
+      return set_error(PL_ERR_NOMEM, "MinGRU obs trajectory: cudaMalloc of %zu bytes failed", n * sizeof(float));
+    }
+  }
+  s->traj = s->traj_own;
+  s->trajD = (long)D;
+  return PL_OK;
+}
+
+int pl_mg_stamp_step(pl_mg* s, size_t step, size_t e0, size_t ne, const double* act, const double* logp,
+                     const double* val, const float* obs, size_t D, void* stream) {
+  using namespace pl;
+  PL_REQUIRE(s && act && logp && val, PL_ERR_INVALID, "pl_mg_stamp_step: NULL argument");
+  PL_REQUIRE(step < (size_t)s->T && e0 + ne <= (size_t)s->N, PL_ERR_INVALID,
+             "pl_mg_stamp_step: step %zu / envs [%zu, %zu) outside %ld x %ld", step, e0, e0 + ne, s->N, s->T);
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = launch_stamp_rows_f64(s->act, s->W, s->T, (long)step, (long)e0, (long)ne, act, st);
+  if (!rc) rc = launch_stamp_rows_f64(s->logp, 1, s->T, (long)step, (long)e0, (long)ne, logp, st);
+  if (!rc) rc = launch_stamp_rows_f64(s->val0, 1, s->T, (long)step, (long)e0, (long)ne, val, st);
+  if (!rc) rc = launch_stamp_rows_f64(s->value, 1, s->T, (long)step, (long)e0, (long)ne, val, st);
+  if (!rc && obs) {
+    PL_REQUIRE(D > 0, PL_ERR_INVALID, "pl_mg_stamp_step: obs without its width D");
+    rc = mg_own_traj(s, D);
+    if (!rc) rc = launch_stamp_rows_f32(s->traj_own, (long)D, s->T, (long)step, (long)e0, (long)ne, obs, st);
+  }
+  s->cols_valid = false;  // complete once pl_mg_stamp_finish has the reward / terminal planes
+  s->prio_fresh = false;
+  return rc;
+}
+
+int pl_mg_stamp_finish(pl_mg* s, const double* rew, const double* term, const double* boot, void* stream) {
+  using namespace pl;
+  PL_REQUIRE(s && rew && term && boot, PL_ERR_INVALID, "pl_mg_stamp_finish: NULL argument");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = launch_stamp_plane(s->rew, s->N, s->T, rew, st);
+  if (!rc) rc = launch_stamp_plane(s->term, s->N, s->T, term, st);
+  if (rc) return rc;
+  PL_CUDA(cudaMemcpyAsync(s->boot, boot, (size_t)s->N * 8, cudaMemcpyDeviceToDevice, st));
+  const long NT = s->N * s->T;
+  mg_fill_kernel<<<blocks_for(NT), 256, 0, st>>>(s->ratio, 1.0, NT);
+  count_launch();
+  PL_LAUNCH("mg_fill_kernel");
+  s->cols_valid = true;
+  s->prio_fresh = false;
+  s->stamped = true;
+  return PL_OK;
+}
+
+int pl_mg_take_stamped(pl_mg* s, int* stamped) {
+  using namespace pl;
+  PL_REQUIRE(s && stamped, PL_ERR_INVALID, "pl_mg_take_stamped: NULL argument");
+  *stamped = (s->stamped && s->cols_valid) ? 1 : 0;
+  s->stamped = false;
   return PL_OK;
 }
 

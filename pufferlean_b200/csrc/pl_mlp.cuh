@@ -59,6 +59,12 @@ int launch_gather(bool bf16, const int* idx, int Nmb, const void* obs, int rowEl
 int launch_adv_ms_from_sums(const double* sums, double* ms, cudaStream_t st);
 // Column sums of `tiles` rows of ld floats in `part`; part must have colsum_scratch_elems(tiles, ld)
 // floats (the second reduction level lives after the partials).
+// rollout-side column producer (pl_columns.cu)
+int launch_stamp_rows_f64(double* col, long width, long T, long step, long e0, long ne, const double* src,
+                          cudaStream_t st);
+int launch_stamp_rows_f32(float* col, long width, long T, long step, long e0, long ne, const float* src,
+                          cudaStream_t st);
+int launch_stamp_plane(double* col, long N, long T, const double* plane, cudaStream_t st);
 long colsum_scratch_elems(int tiles, long ld);
 int launch_colsum_reduce(const float* part, int tiles, long ld, int ncols, float* out, cudaStream_t st);
 int launch_splitk_reduce(const float* part, int S, long n, float* out, cudaStream_t st);
