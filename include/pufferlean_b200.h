@@ -395,6 +395,27 @@ int pl_muon_step_mlp_resident(size_t handle, const double* gRaw, size_t H, size_
  * head. */
 int pl_update_set_head(pl_update* u, int mode, size_t W, const double* head_sizes);
 
+/* ------------------------------------------------------------------ LSTM (recurrent) path ------- */
+/* Batched LSTM + PPO truncated-BPTT gradient: B sequences packed time-major (obs [(t*B + b)*D + d],
+ * acts / advs / rets / oldlps / terms [t*B + b], h0s / c0s [b*H + j], the detached initial states);
+ * params [Wx(4H x D) | Wh(4H x H) | bih(4H) | Wo(O x H) | bo(O)], O = A + 1, gate rows i, f, g, o; a
+ * terminal at step t zeroes the state before step t + 1 and stops the gradient. g[P] = the summed ascent
+ * gradient; newlp / newval (may be NULL) the T*B new log-probs and values. tier 0: f64 arithmetic (the
+ * reference's f64 BLAS path), 1: f32 (its production tier), 2: its bf16 tier (computed as tier 1 here).
+ * H <= 1024. Replaces lean_ffi_lstm_ppo_grad_batch_blas / _f32 / _bf16 (ffi/pufferblas.c:897-1246, device
+ * twin ffi/puffercuda.cu:6794-7182). */
+int pl_lstm_ppo_grad_batch(const double* params, const double* obs, const double* acts, const double* advs,
+                           const double* rets, const double* oldlps, const double* terms, const double* h0s,
+                           const double* c0s, size_t B, size_t T, size_t H, size_t D, size_t A, double vfCoef,
+                           double entCoef, double clipEps, int tier, double* g, double* newlp, double* newval);
+/* on != 0: the next calls reuse the device copies of the previous call's inputs (all but params); the
+ * trainer's epochs > 0 of one update. Replaces lean_cuda_lstm_reuse_inputs (ffi/puffercuda.cu:344). */
+int pl_lstm_reuse_inputs(int on);
+/* Host: per-segment GAE with bootstrap, then advantages normalised over all N*T; time-major [t*N + n];
+ * out = [adv(N*T); ret(N*T)]. Bit-exact twin of lean_ffi_lstm_gae_boot_norm (ffi/pufferffi.c:975-1010). */
+int pl_lstm_gae_boot_norm(const double* vals, const double* rews, const double* terms, const double* bootV,
+                          size_t N, size_t T, double gamma, double lam, double* out);
+
 /* ------------------------------------------------------------------ checkpoints --------------- */
 /* The reference's checkpoint file (Puffer/RL/FFITrain.lean:55-90, ckptToBytes / bytesToCkpt): a
  * little-endian u64 parameter count P, then the P weights as little-endian IEEE f64 — byte-compatible,

@@ -69,6 +69,27 @@ lean_obj_res lean_cuda_train_update_wide_resident(size_t handle, lean_obj_arg ob
 lean_obj_res lean_cuda_muon_step_mlp_resident(size_t handle, lean_obj_arg gRaw, size_t H, size_t D, size_t O,
                                               double gscale, double lr, double wd, double mu, double eps,
                                               lean_obj_arg w);
+/* lstmPPOGradBatchBlasFFI / ...F32FFI / ...Bf16FFI, Puffer/Float/BLAS.lean:153-174; replace
+ * ffi/pufferblas.c:897-1246 (tiers f64 / f32 / bf16-as-f32) */
+lean_obj_res lean_ffi_lstm_ppo_grad_batch_blas(lean_obj_arg pa, lean_obj_arg obs, lean_obj_arg acts, lean_obj_arg advs,
+                                               lean_obj_arg rets, lean_obj_arg olps, lean_obj_arg terms,
+                                               lean_obj_arg h0s, lean_obj_arg c0s, size_t B, size_t T, size_t H,
+                                               size_t D, size_t A, double vf, double ent, double clip);
+lean_obj_res lean_ffi_lstm_ppo_grad_batch_blas_f32(lean_obj_arg pa, lean_obj_arg obs, lean_obj_arg acts,
+                                                   lean_obj_arg advs, lean_obj_arg rets, lean_obj_arg olps,
+                                                   lean_obj_arg terms, lean_obj_arg h0s, lean_obj_arg c0s, size_t B,
+                                                   size_t T, size_t H, size_t D, size_t A, double vf, double ent,
+                                                   double clip);
+lean_obj_res lean_ffi_lstm_ppo_grad_batch_blas_bf16(lean_obj_arg pa, lean_obj_arg obs, lean_obj_arg acts,
+                                                    lean_obj_arg advs, lean_obj_arg rets, lean_obj_arg olps,
+                                                    lean_obj_arg terms, lean_obj_arg h0s, lean_obj_arg c0s, size_t B,
+                                                    size_t T, size_t H, size_t D, size_t A, double vf, double ent,
+                                                    double clip);
+/* cudaLstmReuseInputsFFI, CUDA.lean:172; replaces ffi/puffercuda.cu:344 */
+lean_obj_res lean_cuda_lstm_reuse_inputs(uint8_t on, lean_obj_arg w);
+/* lstmGaeBootNormFFI, FFI.lean:91-92; replaces ffi/pufferffi.c:975-1010 */
+lean_obj_res lean_ffi_lstm_gae_boot_norm(lean_obj_arg vals, lean_obj_arg rews, lean_obj_arg terms, lean_obj_arg boot,
+                                         size_t N, size_t T, double gamma, double lam);
 /* cudaMgLossEnableFFI / cudaMgReadLossesFFI, CUDA.lean:165-178; replace ffi/puffercuda.cu:336-352 */
 lean_obj_res lean_cuda_mg_loss_enable(uint8_t on, lean_obj_arg w);
 lean_obj_res lean_cuda_mg_read_losses(lean_obj_arg w);

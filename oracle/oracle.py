@@ -86,6 +86,11 @@ def orc():
         lib.orc_mingru_update_md.restype = C.c_uint64
         lib.orc_mingru_update_md.argtypes = ([_dp] * 8 + [_sz] * 7 + [C.c_int] + [_sz] * 2 + [_d] * 6 + [C.c_uint64]
                                              + [_d] * 9 + [_dp, C.c_int, _sz, _ip])
+        lib.orc_lstm_param_count.restype = _sz
+        lib.orc_lstm_param_count.argtypes = [_sz] * 3
+        lib.orc_lstm_grad_seq.argtypes = [_dp] * 9 + [_sz] * 4 + [_d] * 3 + [_dp] * 3
+        lib.orc_lstm_grad_batch.argtypes = [_dp] * 9 + [_sz] * 5 + [_d] * 3 + [_dp]
+        lib.orc_lstm_gae_boot_norm.argtypes = [_dp] * 4 + [_sz, _sz, _d, _d, _dp]
         lib.orc_mingru_update.restype = C.c_uint64
         lib.orc_mingru_update.argtypes = ([_dp] * 8 + [_sz] * 7 + [C.c_int] + [_sz] * 2 + [_d] * 6 + [C.c_uint64]
                                           + [_d] * 9 + [_dp, C.c_int])
@@ -308,6 +313,36 @@ def mingru_update(pm, obs, rew, term, act, logp, val0, boot, N, T, D, H, L, A, n
                                    gamma, lam, rho, c, alpha, beta, C.c_uint64(rng & 0xFFFFFFFFFFFFFFFF), lr, wd, mu,
                                    eps, vf, ent, clip, vfClip, maxGradNorm, _ptr(co), co.shape[0], W, hsa)
     return pm, int(r)
+
+
+# ---------------------------------------------------------------------------------------------
+# LSTM (the third recurrent core)
+def lstm_param_count(D, H, A):
+    return int(orc().orc_lstm_param_count(D, H, A))
+
+
+def lstm_grad_seq(params, obs, acts, advs, rets, olps, terms, h0, c0, T, H, D, A, vf=0.5, ent=0.01, clip=0.2):
+    P = lstm_param_count(D, H, A)
+    g, nl, nv = np.zeros(P), np.zeros(T), np.zeros(T)
+    arrs = list(map(f64, (params, obs, acts, advs, rets, olps, terms, h0, c0)))
+    orc().orc_lstm_grad_seq(*[_ptr(a) for a in arrs], T, H, D, A, vf, ent, clip, _ptr(g), _ptr(nl), _ptr(nv))
+    return g, nl, nv
+
+
+def lstm_grad_batch(params, obsB, acts, advs, rets, olps, terms, h0s, c0s, B, T, H, D, A, vf=0.5, ent=0.01, clip=0.2):
+    """[g(P); newlp(T*B); newval(T*B)] of B time-major packed sequences."""
+    P = lstm_param_count(D, H, A)
+    out = np.zeros(P + 2 * T * B)
+    arrs = list(map(f64, (params, obsB, acts, advs, rets, olps, terms, h0s, c0s)))
+    orc().orc_lstm_grad_batch(*[_ptr(a) for a in arrs], B, T, H, D, A, vf, ent, clip, _ptr(out))
+    return out
+
+
+def lstm_gae_boot_norm(vals, rews, terms, boot, N, T, gamma, lam):
+    out = np.zeros(2 * N * T)
+    arrs = list(map(f64, (vals, rews, terms, boot)))
+    orc().orc_lstm_gae_boot_norm(*[_ptr(a) for a in arrs], N, T, gamma, lam, _ptr(out))
+    return out
 
 
 # ---------------------------------------------------------------------------------------------

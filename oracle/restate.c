@@ -1308,3 +1308,232 @@ void orc_train_update_wide(double* pm, const double* obs, const double* acts, co
     }
   free(mObs); free(mAct); free(mAdv); free(mAdvN); free(mRet); free(mOlp); free(mOv); free(g);
 }
+
+/* ---------------------------------------------------------------- LSTM (the third recurrent core) */
+/* One LSTM + categorical/value head sequence, truncated BPTT (ffi/pufferffi.c:556-630,
+ * lean_ffi_lstm_ppo_grad_seq): params [Wx(4H x D) | Wh(4H x H) | bih(4H) | Wo(O x H) | bo(O)], O = A + 1,
+ * gate rows i, f, g, o; h0/c0 the detached initial state; a terminal at step t zeroes the state before
+ * step t + 1 and stops the gradient there. Left-folded dots in the reference's order; the head's
+ * log-softmax without the max subtracted; no value clip. g[P] is overwritten. */
+static double orc_lstm_sig(double x) { return 1.0 / (1.0 + exp(-x)); }
+size_t orc_lstm_param_count(size_t D, size_t H, size_t A) {
+  return 4 * H * D + 4 * H * H + 4 * H + (A + 1) * H + (A + 1);
+}
+void orc_lstm_grad_seq(const double* params, const double* obs, const double* actA, const double* advA,
+                       const double* retA, const double* oldA, const double* termA, const double* h0,
+                       const double* c0, size_t T, size_t H, size_t D, size_t A, double vfCoef, double entCoef,
+                       double clipEps, double* g, double* newlp, double* newval) {
+  const size_t dout = A + 1, H4 = 4 * H, P = orc_lstm_param_count(D, H, A);
+  const double* Wx = params;
+  const double* Wh = Wx + H4 * D;
+  const double* bih = Wh + H4 * H;
+  const double* Wo = bih + H4;
+  const double* bo = Wo + dout * H;
+  for (size_t i = 0; i < P; i++) g[i] = 0.0;
+  double* gWx = g;
+  double* gWh = gWx + H4 * D;
+  double* gbih = gWh + H4 * H;
+  double* gWo = gbih + H4;
+  double* gbo = gWo + dout * H;
+  double* ii = (double*)malloc(sizeof(double) * T * H);
+  double* ff = (double*)malloc(sizeof(double) * T * H);
+  double* gga = (double*)malloc(sizeof(double) * T * H);
+  double* oo = (double*)malloc(sizeof(double) * T * H);
+  double* tc = (double*)malloc(sizeof(double) * T * H);
+  double* hp = (double*)malloc(sizeof(double) * T * H);
+  double* cp = (double*)malloc(sizeof(double) * T * H);
+  double* ht = (double*)malloc(sizeof(double) * T * H);
+  double* outs = (double*)malloc(sizeof(double) * T * dout);
+  double* h = (double*)malloc(sizeof(double) * H);
+  double* c = (double*)malloc(sizeof(double) * H);
+  double* gate = (double*)malloc(sizeof(double) * H4);
+  for (size_t j = 0; j < H; j++) {
+    h[j] = h0[j];
+    c[j] = c0[j];
+  }
+  for (size_t t = 0; t < T; t++) {
+    if (t > 0 && termA[t - 1] != 0.0)
+      for (size_t j = 0; j < H; j++) h[j] = c[j] = 0.0;
+    for (size_t j = 0; j < H; j++) {
+      hp[t * H + j] = h[j];
+      cp[t * H + j] = c[j];
+    }
+    const double* x = obs + t * D;
+    for (size_t k = 0; k < H4; k++) {
+      double gx = 0.0, gh = 0.0;
+      const double* wx = Wx + k * D;
+      const double* wh = Wh + k * H;
+      for (size_t d = 0; d < D; d++) gx += wx[d] * x[d];
+      for (size_t d = 0; d < H; d++) gh += wh[d] * h[d];
+      gate[k] = bih[k] + gx + gh;
+    }
+    for (size_t j = 0; j < H; j++) {
+      double ig = orc_lstm_sig(gate[j]), fg = orc_lstm_sig(gate[H + j]), gg = tanh(gate[2 * H + j]),
+             og = orc_lstm_sig(gate[3 * H + j]);
+      double cj = fg * c[j] + ig * gg, tcj = tanh(cj);
+      ii[t * H + j] = ig;
+      ff[t * H + j] = fg;
+      gga[t * H + j] = gg;
+      oo[t * H + j] = og;
+      tc[t * H + j] = tcj;
+      c[j] = cj;
+      h[j] = og * tcj;
+      ht[t * H + j] = h[j];
+    }
+    for (size_t m = 0; m < dout; m++) {
+      double acc = 0.0;
+      const double* w = Wo + m * H;
+      for (size_t j = 0; j < H; j++) acc += w[j] * h[j];
+      outs[t * dout + m] = bo[m] + acc;
+    }
+  }
+  double* dh_next = (double*)calloc(H, sizeof(double));
+  double* dc_next = (double*)calloc(H, sizeof(double));
+  double* dh = (double*)malloc(sizeof(double) * H);
+  double* dhprev = (double*)malloc(sizeof(double) * H);
+  double* dcprev = (double*)malloc(sizeof(double) * H);
+  double* dgate = (double*)malloc(sizeof(double) * H4);
+  double* dout_ = (double*)malloc(sizeof(double) * dout);
+  double* pk = (double*)malloc(sizeof(double) * (A ? A : 1));
+  for (size_t tt = T; tt-- > 0;) {
+    const size_t t = tt;
+    const double* out = outs + t * dout;
+    const size_t a = (size_t)actA[t];
+    const double adv = advA[t], ret = retA[t], oldLogp = oldA[t];
+    double sumexp = 0.0;
+    for (size_t k = 0; k < A; k++) sumexp += exp(out[k]);
+    const double lse = log(sumexp);
+    double pout = 0.0;
+    for (size_t k = 0; k < A; k++) {
+      pk[k] = exp(out[k] - lse);
+      pout += pk[k] * out[k];
+    }
+    const double logpA = out[a] - lse, ratio = exp(logpA - oldLogp), lo = 1.0 - clipEps, hi = 1.0 + clipEps;
+    const double ratioC = ratio < lo ? lo : (ratio > hi ? hi : ratio), surr1 = adv * ratio, surr2 = adv * ratioC;
+    double dPol;
+    if (surr1 <= surr2)
+      dPol = adv * ratio;
+    else
+      dPol = adv * ((lo < ratio && ratio < hi) ? 1.0 : 0.0) * ratio;
+    for (size_t k = 0; k < A; k++) {
+      double dp = dPol * (((k == a) ? 1.0 : 0.0) - pk[k]);
+      double de = entCoef * pk[k] * (pout - out[k]);
+      dout_[k] = dp + de;
+    }
+    dout_[A] = -vfCoef * (out[A] - ret);
+    if (newlp) newlp[t] = logpA;
+    if (newval) newval[t] = out[A];
+    for (size_t j = 0; j < H; j++) dh[j] = dh_next[j];
+    for (size_t m = 0; m < dout; m++) {
+      const double dm = dout_[m];
+      double* gw = gWo + m * H;
+      const double* w = Wo + m * H;
+      gbo[m] += dm;
+      for (size_t j = 0; j < H; j++) {
+        gw[j] += dm * ht[t * H + j];
+        dh[j] += dm * w[j];
+      }
+    }
+    for (size_t j = 0; j < H; j++) {
+      const double tcj = tc[t * H + j], og = oo[t * H + j];
+      const double dcj = dc_next[j] + dh[j] * og * (1.0 - tcj * tcj);
+      const double do_ = dh[j] * tcj, ig = ii[t * H + j], fg = ff[t * H + j], gg = gga[t * H + j],
+                   cprev = cp[t * H + j];
+      const double df_ = dcj * cprev, di_ = dcj * gg, dg_ = dcj * ig;
+      dcprev[j] = dcj * fg;
+      dgate[j] = di_ * ig * (1.0 - ig);
+      dgate[H + j] = df_ * fg * (1.0 - fg);
+      dgate[2 * H + j] = dg_ * (1.0 - gg * gg);
+      dgate[3 * H + j] = do_ * og * (1.0 - og);
+    }
+    for (size_t d = 0; d < H; d++) dhprev[d] = 0.0;
+    const double* x = obs + t * D;
+    const double* hprevk = hp + t * H;
+    for (size_t k = 0; k < H4; k++) {
+      const double da = dgate[k];
+      gbih[k] += da;
+      double* gwx = gWx + k * D;
+      for (size_t d = 0; d < D; d++) gwx[d] += da * x[d];
+      double* gwh = gWh + k * H;
+      const double* wh = Wh + k * H;
+      for (size_t d = 0; d < H; d++) {
+        gwh[d] += da * hprevk[d];
+        dhprev[d] += da * wh[d];
+      }
+    }
+    const int flow = (t > 0 && termA[t - 1] == 0.0);
+    for (size_t j = 0; j < H; j++) {
+      dh_next[j] = flow ? dhprev[j] : 0.0;
+      dc_next[j] = flow ? dcprev[j] : 0.0;
+    }
+  }
+  free(ii); free(ff); free(gga); free(oo); free(tc); free(hp); free(cp); free(ht); free(outs);
+  free(h); free(c); free(gate); free(dh_next); free(dc_next); free(dh); free(dhprev); free(dcprev); free(dgate);
+  free(dout_); free(pk);
+}
+
+/* The batched form (lean_ffi_lstm_ppo_grad_batch_blas, ffi/pufferblas.c:897-1018): B sequences packed
+ * time-major (obs [(t*B + b)*D + d], scalars [t*B + b], h0s/c0s [b*H + j]); the summed gradient over b in
+ * order 0..B-1 of the per-sequence ones. out = [g(P); newlp(T*B); newval(T*B)], the last two time-major. */
+void orc_lstm_grad_batch(const double* params, const double* obsB, const double* acts, const double* advs,
+                         const double* rets, const double* olps, const double* terms, const double* h0s,
+                         const double* c0s, size_t B, size_t T, size_t H, size_t D, size_t A, double vfCoef,
+                         double entCoef, double clipEps, double* out) {
+  const size_t P = orc_lstm_param_count(D, H, A), nb = T * B;
+  double* gb = (double*)malloc(sizeof(double) * P);
+  double* so = (double*)malloc(sizeof(double) * T * D);
+  double* sc = (double*)malloc(sizeof(double) * 5 * T);
+  double* nl = (double*)malloc(sizeof(double) * T);
+  double* nv = (double*)malloc(sizeof(double) * T);
+  for (size_t i = 0; i < P; i++) out[i] = 0.0;
+  for (size_t b = 0; b < B; b++) {
+    for (size_t t = 0; t < T; t++) {
+      for (size_t d = 0; d < D; d++) so[t * D + d] = obsB[(t * B + b) * D + d];
+      sc[t] = acts[t * B + b];
+      sc[T + t] = advs[t * B + b];
+      sc[2 * T + t] = rets[t * B + b];
+      sc[3 * T + t] = olps[t * B + b];
+      sc[4 * T + t] = terms[t * B + b];
+    }
+    orc_lstm_grad_seq(params, so, sc, sc + T, sc + 2 * T, sc + 3 * T, sc + 4 * T, h0s + b * H, c0s + b * H, T, H, D, A,
+                      vfCoef, entCoef, clipEps, gb, nl, nv);
+    for (size_t i = 0; i < P; i++) out[i] = out[i] + gb[i];
+    for (size_t t = 0; t < T; t++) {
+      out[P + t * B + b] = nl[t];
+      out[P + nb + t * B + b] = nv[t];
+    }
+  }
+  free(gb); free(so); free(sc); free(nl); free(nv);
+}
+
+/* Per-segment GAE with bootstrap, then the advantages normalised over all N*T (ffi/pufferffi.c:975-1010,
+ * lean_ffi_lstm_gae_boot_norm): time-major columns [t*N + n]; out = [adv(N*T); ret(N*T)]. */
+void orc_lstm_gae_boot_norm(const double* vals, const double* rews, const double* terms, const double* bootV,
+                            size_t N, size_t T, double gamma, double lam, double* out) {
+  const size_t NT = N * T;
+  double* adv = out;
+  double* ret = out + NT;
+  for (size_t n = 0; n < N; n++) {
+    double lastA = 0.0;
+    for (size_t i = 0; i < T; i++) {
+      const size_t t = T - 1 - i, idx = t * N + n;
+      const double nnt = (terms[idx] > 0.5) ? 0.0 : 1.0;
+      const double vNext = (t + 1 < T) ? vals[(t + 1) * N + n] : bootV[n];
+      const double delta = rews[idx] + gamma * vNext * nnt - vals[idx];
+      lastA = delta + gamma * lam * nnt * lastA;
+      adv[idx] = lastA;
+      ret[idx] = lastA + vals[idx];
+    }
+  }
+  const size_t den = NT > 0 ? NT : 1;
+  double sum = 0.0;
+  for (size_t i = 0; i < NT; i++) sum += adv[i];
+  const double mean = sum / (double)den;
+  double vsum = 0.0;
+  for (size_t i = 0; i < NT; i++) {
+    const double d = adv[i] - mean;
+    vsum += d * d;
+  }
+  const double inv = 1.0 / (sqrt(vsum / (double)den) + 1e-8);
+  for (size_t i = 0; i < NT; i++) adv[i] = (adv[i] - mean) * inv;
+}

@@ -110,6 +110,9 @@ def _bind_optional(L):
                                           + [_d] * 9 + [C.c_uint8, _dp], C.c_int),
         "pl_mlp_ppo_grad_wide": ([_dp] * 7 + [_sz] * 5 + [C.c_uint32, _dp] + [_d] * 4 + [C.c_uint8, _dp], C.c_int),
         "pl_muon_step_mlp_resident": ([_sz, _dp] + [_sz] * 3 + [_d] * 5 + [_dp], C.c_int),
+        "pl_lstm_ppo_grad_batch": ([_dp] * 9 + [_sz] * 5 + [_d] * 3 + [C.c_int, _dp, _dp, _dp], C.c_int),
+        "pl_lstm_reuse_inputs": ([C.c_int], C.c_int),
+        "pl_lstm_gae_boot_norm": ([_dp] * 4 + [_sz, _sz, _d, _d, _dp], C.c_int),
         "pl_ckpt_write": ([C.c_char_p, _dp, _sz], C.c_int),
         "pl_ckpt_read": ([C.c_char_p, _dp, _sz, C.POINTER(_sz)], C.c_int),
         "pl_policy_save": ([_sz, _sz, C.c_char_p], C.c_int),
@@ -300,6 +303,31 @@ def cuda_muon_step_mlp_resident(handle, g_raw, H, D, O, gscale, lr, wd, mu, eps)
     out = np.empty(H * D + H + O * H + O)
     _check(lib().pl_muon_step_mlp_resident(handle, _p(_f64(g_raw)), H, D, O, gscale, lr, wd, mu, eps, _p(out)),
            "pl_muon_step_mlp_resident")
+    return out
+
+
+# --------------------------------------------------------------------------------------------- LSTM
+def lstm_param_count(D, H, A):
+    return 4 * H * D + 4 * H * H + 4 * H + (A + 1) * H + (A + 1)
+
+
+def cuda_lstm_ppo_grad_batch(params, obsB, acts, advs, rets, oldlps, terms, h0s, c0s, B, T, H, D, A, vf_coef,
+                             ent_coef, clip_eps, tier=1, with_outputs=False):
+    """lstmPPOGradBatchBlas*FFI: the summed BPTT gradient (P values); tier 0 f64, 1 f32, 2 the bf16 tier.
+    with_outputs: also return the T*B new log-probs and values."""
+    arrs = [_f64(x) for x in (params, obsB, acts, advs, rets, oldlps, terms, h0s, c0s)]
+    g = np.empty(lstm_param_count(D, H, A))
+    nl, nv = (np.empty(T * B), np.empty(T * B)) if with_outputs else (None, None)
+    _check(lib().pl_lstm_ppo_grad_batch(*[_p(a) for a in arrs], B, T, H, D, A, vf_coef, ent_coef, clip_eps, tier,
+                                        _p(g), _p(nl) if nl is not None else None,
+                                        _p(nv) if nv is not None else None), "pl_lstm_ppo_grad_batch")
+    return (g, nl, nv) if with_outputs else g
+
+
+def lstm_gae_boot_norm(vals, rews, terms, boot, N, T, gamma, lam):
+    out = np.empty(2 * N * T)
+    arrs = [_f64(x) for x in (vals, rews, terms, boot)]
+    _check(lib().pl_lstm_gae_boot_norm(*[_p(a) for a in arrs], N, T, gamma, lam, _p(out)), "pl_lstm_gae_boot_norm")
     return out
 
 

@@ -256,3 +256,39 @@ int pl_policy_restore(const char* path, size_t* P, size_t* handle) {
 }
 
 }  // extern "C"
+
+// Per-segment GAE with bootstrap, then the advantages normalised over all N*T: the host C of the LSTM
+// trainer (ffi/pufferffi.c:975-1010, lean_ffi_lstm_gae_boot_norm), same recurrence and fold order.
+// Time-major columns [t*N + n]; out = [adv(N*T); ret(N*T)].
+extern "C" int pl_lstm_gae_boot_norm(const double* vals, const double* rews, const double* terms,
+                                     const double* bootV, size_t N, size_t T, double gamma, double lam,
+                                     double* out) {
+  if (!vals || !rews || !terms || !bootV || !out) return PL_ERR_INVALID;
+  const size_t NT = N * T;
+  double* adv = out;
+  double* ret = out + NT;
+  for (size_t n = 0; n < N; n++) {
+    double lastA = 0.0;
+    for (size_t i = 0; i < T; i++) {
+      const size_t t = T - 1 - i, idx = t * N + n;
+      const double nnt = (terms[idx] > 0.5) ? 0.0 : 1.0;
+      const double vNext = (t + 1 < T) ? vals[(t + 1) * N + n] : bootV[n];
+      const double delta = rews[idx] + gamma * vNext * nnt - vals[idx];
+      lastA = delta + gamma * lam * nnt * lastA;
+      adv[idx] = lastA;
+      ret[idx] = lastA + vals[idx];
+    }
+  }
+  const size_t den = NT > 0 ? NT : 1;
+  double sum = 0.0;
+  for (size_t i = 0; i < NT; i++) sum += adv[i];
+  const double mean = sum / (double)den;
+  double vsum = 0.0;
+  for (size_t i = 0; i < NT; i++) {
+    const double d = adv[i] - mean;
+    vsum += d * d;
+  }
+  const double inv = 1.0 / (sqrt(vsum / (double)den) + 1e-8);
+  for (size_t i = 0; i < NT; i++) adv[i] = (adv[i] - mean) * inv;
+  return PL_OK;
+}

@@ -263,6 +263,72 @@ LEAN_EXPORT lean_obj_res lean_cuda_muon_step_mlp_resident(size_t handle, lean_ob
   return lean_io_result_mk_ok(out);
 }
 
+/* ---------------------------------------------------------------- LSTM (Puffer/Float/BLAS.lean:153-173) */
+static lean_obj_res lstm_grad(lean_obj_arg pa, lean_obj_arg obs, lean_obj_arg acts, lean_obj_arg advs,
+                              lean_obj_arg rets, lean_obj_arg olps, lean_obj_arg terms, lean_obj_arg h0s,
+                              lean_obj_arg c0s, size_t B, size_t T, size_t H, size_t D, size_t A, double vf,
+                              double ent, double clip, int tier, const char* what) {
+  const size_t P = 4 * H * D + 4 * H * H + 4 * H + (A + 1) * H + (A + 1);
+  lean_obj_res out = new_fa(P);
+  int rc = (fan(pa) < P || fan(obs) < B * T * D || fan(acts) < B * T || fan(h0s) < B * H || fan(c0s) < B * H)
+               ? PL_ERR_INVALID
+               : pl_lstm_ppo_grad_batch(fa(pa), fa(obs), fa(acts), fa(advs), fa(rets), fa(olps), fa(terms), fa(h0s),
+                                        fa(c0s), B, T, H, D, A, vf, ent, clip, tier, fa(out), NULL, NULL);
+  lean_dec(pa);
+  lean_dec(obs);
+  lean_dec(acts);
+  lean_dec(advs);
+  lean_dec(rets);
+  lean_dec(olps);
+  lean_dec(terms);
+  lean_dec(h0s);
+  lean_dec(c0s);
+  if (rc) return pure_fail(out, what);
+  return out;
+}
+LEAN_EXPORT lean_obj_res lean_ffi_lstm_ppo_grad_batch_blas(lean_obj_arg pa, lean_obj_arg obs, lean_obj_arg acts,
+                                                          lean_obj_arg advs, lean_obj_arg rets, lean_obj_arg olps,
+                                                          lean_obj_arg terms, lean_obj_arg h0s, lean_obj_arg c0s,
+                                                          size_t B, size_t T, size_t H, size_t D, size_t A,
+                                                          double vf, double ent, double clip) {
+  return lstm_grad(pa, obs, acts, advs, rets, olps, terms, h0s, c0s, B, T, H, D, A, vf, ent, clip, 0,
+                   "lean_ffi_lstm_ppo_grad_batch_blas");
+}
+LEAN_EXPORT lean_obj_res lean_ffi_lstm_ppo_grad_batch_blas_f32(lean_obj_arg pa, lean_obj_arg obs, lean_obj_arg acts,
+                                                              lean_obj_arg advs, lean_obj_arg rets, lean_obj_arg olps,
+                                                              lean_obj_arg terms, lean_obj_arg h0s, lean_obj_arg c0s,
+                                                              size_t B, size_t T, size_t H, size_t D, size_t A,
+                                                              double vf, double ent, double clip) {
+  return lstm_grad(pa, obs, acts, advs, rets, olps, terms, h0s, c0s, B, T, H, D, A, vf, ent, clip, 1,
+                   "lean_ffi_lstm_ppo_grad_batch_blas_f32");
+}
+LEAN_EXPORT lean_obj_res lean_ffi_lstm_ppo_grad_batch_blas_bf16(lean_obj_arg pa, lean_obj_arg obs, lean_obj_arg acts,
+                                                               lean_obj_arg advs, lean_obj_arg rets,
+                                                               lean_obj_arg olps, lean_obj_arg terms,
+                                                               lean_obj_arg h0s, lean_obj_arg c0s, size_t B, size_t T,
+                                                               size_t H, size_t D, size_t A, double vf, double ent,
+                                                               double clip) {
+  return lstm_grad(pa, obs, acts, advs, rets, olps, terms, h0s, c0s, B, T, H, D, A, vf, ent, clip, 2,
+                   "lean_ffi_lstm_ppo_grad_batch_blas_bf16");
+}
+LEAN_EXPORT lean_obj_res lean_cuda_lstm_reuse_inputs(uint8_t on, lean_obj_arg w) {
+  (void)w;
+  pl_lstm_reuse_inputs(on);
+  return lean_io_result_mk_ok(lean_box(0));
+}
+LEAN_EXPORT lean_obj_res lean_ffi_lstm_gae_boot_norm(lean_obj_arg vals, lean_obj_arg rews, lean_obj_arg terms,
+                                                    lean_obj_arg boot, size_t N, size_t T, double gamma,
+                                                    double lam) {
+  lean_obj_res out = new_fa(2 * N * T);
+  int rc = pl_lstm_gae_boot_norm(fa(vals), fa(rews), fa(terms), fa(boot), N, T, gamma, lam, fa(out));
+  lean_dec(vals);
+  lean_dec(rews);
+  lean_dec(terms);
+  lean_dec(boot);
+  if (rc) return pure_fail(out, "lean_ffi_lstm_gae_boot_norm");
+  return out;
+}
+
 /* ---------------------------------------------------------------- dashboard losses (CUDA.lean:165-178) */
 LEAN_EXPORT lean_obj_res lean_cuda_mg_loss_enable(uint8_t on, lean_obj_arg w) {
   (void)w;

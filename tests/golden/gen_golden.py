@@ -270,6 +270,35 @@ def main():
     np.savez(os.path.join(OUT, "gauss_update.npz"), pm0=pm0, out=pm, obs=obsT, acts=actsT, adv=advT, ret=retT,
              olp=olpT, ov=ovT, perm=perm, meta=np.array([NT, D, H, W, E, MB]),
              hyp=np.array([hyp[x] for x in ("lr", "wd", "mu", "eps", "vf", "ent", "clip", "vfClip")]))
+
+    # LSTM: three sequences of the reference's scalar BPTT gradient (lean_ffi_lstm_ppo_grad_seq) from
+    # detached non-zero initial states, a terminal mid-sequence; and its GAE + normalisation
+    # (lean_ffi_lstm_gae_boot_norm) on time-major columns.
+    g = np.random.default_rng(0x157)
+    T, H, D, A, B = 9, 6, 5, 4, 3
+    P = 4 * H * D + 4 * H * H + 4 * H + (A + 1) * H + (A + 1)
+    lp = g.uniform(-0.4, 0.4, P)
+    obsB = g.standard_normal(T * B * D)
+    actB = g.integers(0, A, T * B).astype(float)
+    advB, retB, olpB = g.standard_normal(T * B), g.standard_normal(T * B), g.uniform(-3, -0.5, T * B)
+    termB = (g.random(T * B) < 0.15).astype(float)
+    h0s, c0s = g.uniform(-0.5, 0.5, B * H), g.uniform(-0.5, 0.5, B * H)
+    seqs = []
+    for b in range(B):
+        rows = [t * B + b for t in range(T)]
+        o = np.concatenate([obsB[r * D:(r + 1) * D] for r in rows])
+        seqs.append(arr(ref_call(cpu, "lean_ffi_lstm_ppo_grad_seq", VP, FA(lp), FA(o), FA(actB[rows]),
+                                 FA(advB[rows]), FA(retB[rows]), FA(olpB[rows]), FA(termB[rows]),
+                                 FA(h0s[b * H:(b + 1) * H]), FA(c0s[b * H:(b + 1) * H]), T, H, D, A, 0.5, 0.01,
+                                 0.2)))
+    N = 7
+    vals, rews = g.standard_normal(N * T), g.standard_normal(N * T)
+    terms, boot = (g.random(N * T) < 0.2).astype(float), g.standard_normal(N)
+    gae = arr(ref_call(cpu, "lean_ffi_lstm_gae_boot_norm", VP, FA(vals), FA(rews), FA(terms), FA(boot), N, T, 0.99,
+                       0.95))
+    np.savez(os.path.join(OUT, "lstm.npz"), params=lp, obsB=obsB, actB=actB, advB=advB, retB=retB, olpB=olpB,
+             termB=termB, h0s=h0s, c0s=c0s, seqs=np.stack(seqs), meta=np.array([T, H, D, A, B]), vals=vals, rews=rews,
+             terms=terms, boot=boot, gae=gae, gae_meta=np.array([N, T, 0.99, 0.95]))
     print("golden fixtures written to", OUT)
 
 
