@@ -619,6 +619,57 @@ def measure_wide(args, mode, cpu=True):
     return out
 
 
+def measure_lstm(args, cpu=True):
+    """The LSTM trainer's per-epoch BPTT gradient (lean_ffi_lstm_ppo_grad_batch_blas*, the reference's 256-env /
+    H 64 / T 64 configuration, Puffer/RL/FFITrain.lean:1010-1030) with D 32, A 4: one call = the summed gradient
+    over all B*T samples from host columns (the reference-facing call; inputs uploaded and the gradient read
+    back inside the timed region), and the same with the inputs reused on the device (epochs > 0). Tiers f32
+    (the trainer's production tier) and f64. cpu leg: the f64 oracle on 8 of the 256 sequences."""
+    import torch
+
+    import pufferlean_b200 as plb
+
+    B, T, H, D, A = 256, 64, 64, 32, 4
+    g = np.random.default_rng(0x15)
+    P = plb.lstm_param_count(D, H, A)
+    R = B * T
+    params = g.uniform(-1, 1, P) / np.sqrt(H)
+    cols = [g.standard_normal(R * D), g.integers(0, A, R).astype(float), g.standard_normal(R), g.standard_normal(R),
+            g.uniform(-3, -0.3, R), (g.random(R) < 0.01).astype(float), g.uniform(-0.5, 0.5, B * H),
+            g.uniform(-0.5, 0.5, B * H)]
+    L = plb.lib()
+    out = {"workload": f"LSTM BPTT gradient: {B} sequences x {T} steps, D {D} -> LSTM {H} -> {A} + 1", "unit": "samples/s"}
+    l0 = L.pl_kernel_launch_count()
+    for tier, name in ((1, "f32"), (0, "f64")):
+        for reuse in (0, 1):
+            plb.cuda_lstm_ppo_grad_batch(params, *cols, B, T, H, D, A, 0.5, 0.01, 0.2, tier=tier)
+            L.pl_lstm_reuse_inputs(reuse)
+            for _ in range(args.warmup):
+                plb.cuda_lstm_ppo_grad_batch(params, *cols, B, T, H, D, A, 0.5, 0.01, 0.2, tier=tier)
+            torch.cuda.synchronize()
+            reps = max(3, args.steps)
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                plb.cuda_lstm_ppo_grad_batch(params, *cols, B, T, H, D, A, 0.5, 0.01, 0.2, tier=tier)
+            dt = (time.perf_counter() - t0) / reps
+            L.pl_lstm_reuse_inputs(0)
+            key = f"{name}{'_reuse' if reuse else ''}"
+            out[key] = {"samples_per_s": R / dt, "ms_per_call": dt * 1e3}
+    out["value"] = out["f32"]["samples_per_s"]
+    out["gpu_launches_total"] = int(L.pl_kernel_launch_count() - l0)
+    if cpu:
+        from oracle import oracle as O
+        nb = 8
+        idx = [t * B + b for t in range(T) for b in range(nb)]
+        sub = ([cols[0].reshape(R, D)[idx].ravel()] + [c[idx] for c in cols[1:6]] + [c[:nb * H] for c in cols[6:]])
+        t0 = time.perf_counter()
+        O.lstm_grad_batch(params, *sub, nb, T, H, D, A)
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": nb * T / dt, "unit": "samples/s", "cores": 1, "kind": "port",
+                               "sample": f"{nb} of the {B} sequences, f64 oracle (the reference's scalar BPTT order)"}
+    return out
+
+
 def mingru_init_pm(D, H, L, A, K, seed):
     """[params; mom] in the flattenMG layout, Kaiming-uniform bounds of initMinGRU
     (Puffer/RL/MinGRUTrain.lean:311-344: sqrt(2)/sqrt(D) encoder, 1/sqrt(H) elsewhere, biases zero),
@@ -880,10 +931,10 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the configs[1] / configs[2] kernel measurements")
     ap.add_argument("--drift", type=int, default=0, metavar="U",
                     help="print the loss-curve drift of U consecutive updates against the f64 oracle and exit")
-    ap.add_argument("--only", choices=["c2", "c3", "c4", "c4r", "wide1", "wide2"],
+    ap.add_argument("--only", choices=["c2", "c3", "c4", "c4r", "wide1", "wide2", "lstm"],
                     help="print only the configs[1] (c2), configs[2] (c3) or configs[3] (c4: K=2 + GELU encoder; "
                          "c4r: the reference's K=3 linear-encoder net) measurement, or the wide-head update "
-                         "(wide1 multi-discrete, wide2 Gaussian)")
+                         "(wide1 multi-discrete, wide2 Gaussian), or the LSTM BPTT gradient (lstm)")
     args = ap.parse_args()
     if args.drift:
         print(json.dumps(measure_drift(args.drift)), flush=True)
@@ -895,6 +946,8 @@ def main():
             res = measure_mingru_c4(args, K=3, enc_act=0, cpu=not args.no_cpu)
         elif args.only in ("wide1", "wide2"):
             res = measure_wide(args, int(args.only[-1]), cpu=not args.no_cpu)
+        elif args.only == "lstm":
+            res = measure_lstm(args, cpu=not args.no_cpu)
         else:
             res = measure_vtrace_c2() if args.only == "c2" else measure_ns_c3()
         print(json.dumps(res), flush=True)
