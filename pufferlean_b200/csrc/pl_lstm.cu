@@ -304,7 +304,9 @@ int lstm_grad(const double* params, const double* obs, const double* acts, const
   const cudaStream_t st = 0;
   const int rows_per = 256;
   const long nch = ceil_div(NR, rows_per);
-  const int NZ = (int)std::min<long>(64, std::max<long>(1, NR / 1024));
+  // weight gradients: K = T*B rows split into slices of ~128 rows, so the small M x N products still
+  // spread over every SM; the slices are summed in order afterwards
+  const int NZ = (int)std::min<long>(256, std::max<long>(1, NR / 128));
   // scratch slots 40..63: inputs, activations, gradients
   auto buf = [&](int slot, size_t bytes) { return scratch(slot, bytes); };
   double* stage = (double*)buf(40, sizeof(double) * std::max<long>(P, NR * std::max<long>(D, 2)));
@@ -368,7 +370,9 @@ int lstm_grad(const double* params, const double* obs, const double* acts, const
   };
   rc = fwd_products();
   if (rc) return rc;
-  const int rows = (int)std::max<long>(1, std::min<long>(1024 / H, 8));
+  // sequences per CTA of the recurrence: one until there are more than ~2 per SM (each CTA reads Wh from
+  // shared memory once per sequence and step, so fewer sequences per CTA means more SMs share that work)
+  const int rows = (int)std::max<long>(1, std::min<long>(std::min<long>(1024 / H, 8), B / (2 * 148)));
   const size_t wsm = sizeof(R) * (size_t)H4 * (H + 1);
   const bool WS = wsm + sizeof(R) * (size_t)rows * H4 <= 200 * 1024;
   const size_t smem_f = (WS ? wsm : 0) + sizeof(R) * (size_t)rows * H;
