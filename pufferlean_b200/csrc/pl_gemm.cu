@@ -62,8 +62,8 @@ static int make_map(CUtensorMap* map, const Operand& op, uint32_t box_rows) {
   return PL_OK;
 }
 
-// Store map of a bf16 output for the staged epilogue: {cols, rows, batch} with a {32, 32, 1} box, no
-// swizzle (the staging tile is dense row-major). Returns false when the output cannot take TMA
+// Store map of a bf16 output for the staged epilogue: {cols, rows, batch} with a {32, 32, 1} box and
+// the 64-byte swizzle the staging tiles are written in. Returns false when the output cannot take TMA
 // stores (alignment), in which case the epilogue writes directly.
 static bool make_store_map(CUtensorMap* map, const void* ptr, long rows, long cols, long ld, long batch, long bstride) {
   auto enc = encode_fn();
@@ -75,7 +75,7 @@ static bool make_store_map(CUtensorMap* map, const void* ptr, long rows, long co
   cuuint32_t box[3] = {32, 32, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

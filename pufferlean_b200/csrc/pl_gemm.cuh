@@ -199,9 +199,11 @@ __device__ __forceinline__ void act_grad_row(float (&v)[N], const float (&z)[N],
   }
 }
 
-// Shared memory: 1 KB alignment slack, the TMA ring, barriers, then the epilogue area: bf16 staging
-// tiles for the TMA bulk stores (per epilogue warp, one 32 x 32 tile per output) and the column
-// reduction scratch [4][BN] (+ per-warp loss partials). The ring takes what is left of 227 KB.
+// Shared memory: 1 KB alignment slack, the TMA ring, the epilogue area (bf16 staging tiles for the
+// TMA bulk stores: per epilogue warp STG_BUFS sets of one 32 x 32 tile per output, 1 KB aligned for
+// the 64-byte swizzle; then the column reduction scratch [4][BN] + per-warp loss partials), then the
+// barriers. The ring takes what is left of 227 KB. The Newton-Schulz products (EPI_BF16) stage into
+// two alternating sets, so a chunk never waits for the previous chunk's store to finish reading.
 template <int BN, int EPI>
 struct GemmSmem {
   static constexpr int BM = 128, BK = 64;
@@ -209,7 +211,9 @@ struct GemmSmem {
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int NOUT = EPI == EPI_FWD ? 2 : ((EPI == EPI_DGRAD || EPI == EPI_BF16) ? 1 : 0);
-  static constexpr uint32_t STG_WARP = NOUT * 32 * 32 * 2;
+  static constexpr int STG_BUFS = EPI == EPI_BF16 ? 2 : 1;
+  static constexpr uint32_t STG_ONE = NOUT * 32 * 32 * 2;
+  static constexpr uint32_t STG_WARP = STG_BUFS * STG_ONE;
   static constexpr uint32_t STG_BYTES = 8 * STG_WARP;
   static constexpr uint32_t RED_BYTES = (EPI == EPI_DGRAD || EPI == EPI_PPO) ? (4 * BN * 4 + 4 * 8 * 4) : 0;
   static constexpr uint32_t FIXED = 1024 + 256 + STG_BYTES + RED_BYTES;
@@ -235,22 +239,30 @@ __device__ __forceinline__ TileIdx tile_of(int t, int num_n, int num_m) {
 
 // Epilogue of one 128 x BN accumulator tile held in TMEM columns [tcol, tcol + BN).
 // Runs on the 4 epilogue warps; warp `sub` owns TMEM lanes / tile rows [32 sub, 32 sub + 32).
-// Writes this lane's 32 bf16 values (its row of a 32 x 32 tile) into a dense staging tile; the
-// 16-byte pieces go in a lane-rotated order so the 8 lanes of each store phase hit distinct banks.
+// Writes this lane's 32 bf16 values (its row of a 32 x 32 tile) into a staging tile in the TMA
+// 64-byte swizzle (16-byte piece c of row r at position c ^ ((r >> 1) & 3); the store map reads it
+// back in order): the 8 lanes of each store phase then cover all 32 banks, and every register index
+// is static.
 __device__ __forceinline__ void stage_row32(uint8_t* tile, int lane, const float (&v)[32]) {
-  uint4 w[4];
-  uint32_t* u = reinterpret_cast<uint32_t*>(w);
+  uint8_t* row = tile + lane * 64;
+  const int x = (lane >> 1) & 3;
 #pragma unroll
-  for (int j = 0; j < 16; j++) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-    u[j] = *reinterpret_cast<uint32_t*>(&h);
-  }
-  uint4* row = reinterpret_cast<uint4*>(tile + lane * 64);
+  for (int c = 0; c < 4; c++) {
+    uint32_t u[4];
 #pragma unroll
-  for (int j = 0; j < 4; j++) {
-    const int c = (j + (lane >> 1)) & 3;
-    row[c] = w[c];
+    for (int k = 0; k < 4; k++) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * c + 2 * k], v[8 * c + 2 * k + 1]);
+      u[k] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(row + ((c ^ x) << 4)) = make_uint4(u[0], u[1], u[2], u[3]);
   }
+}
+
+// alpha * acc + beta * aux, one rounding per operation in this order. The Newton-Schulz polynomial
+// is formed with it in the GEMM epilogue and in the fused small-matrix kernel, so the two agree bit
+// for bit; the diagonal term is then one more rounded add on the diagonal only.
+__device__ __forceinline__ float axpb(float alpha, float acc, float beta, float aux) {
+  return __fmaf_rn(alpha, acc, __fmul_rn(beta, aux));
 }
 
 // The 32 bf16 aux values of one row at columns [nc, nc + 32) (zero past cols), as four 16-byte words.
@@ -270,7 +282,7 @@ template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row, int m_tile, int n_tile, int bz,
                                               int batch, bool have_acc, int sub, int half, int lane, float* red,
                                               float* rowscr, uint8_t* stg, const CUtensorMap* tmC,
-                                              const CUtensorMap* tmC2) {
+                                              const CUtensorMap* tmC2, uint32_t& seq) {
   constexpr int BM = 128;
   const int row = m_tile * BM + sub * 32 + lane;
   const bool row_ok = row < ep.out_rows;
@@ -411,63 +423,95 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
     constexpr bool STAGED_OK = (EPI == EPI_FWD || EPI == EPI_DGRAD || EPI == EPI_BF16);
     if (STAGED_OK && ep.tma_out) {
       // ---- staged path: 32 x 32 tiles through shared memory, TMA bulk stores (rows/cols past the
-      // logical extent are clipped by the tensor map). The bf16 aux row piece (Z for act', X for the
-      // Newton-Schulz axpby) is loaded one chunk ahead, so its latency hides under the current
-      // chunk's math and store.
+      // logical extent are clipped by the tensor map). Pipelined per warp: chunk c + 1's TMEM load is
+      // issued once chunk c is staged (its registers are free then) and overlaps chunk c's fence and
+      // store; chunk c + 1's bf16 aux piece (Z for act', X for the Newton-Schulz axpby) is loaded
+      // before chunk c's math, so its latency hides under a whole chunk.
       const int row0 = m_tile * 128 + sub * 32;
       constexpr bool HAS_AUX = (EPI == EPI_DGRAD || EPI == EPI_BF16);
+      constexpr int NCH = BN / 64;  // 32-column chunks in this warp's half of the tile
+      constexpr int NB = GemmSmem<BN, EPI>::STG_BUFS;
       const bool use_aux = HAS_AUX && ep.aux != nullptr && row_ok;
       const __nv_bfloat16* aux_row =
           use_aux ? ep.aux + (long)batch * ep.aux_bstride + (long)row * ep.ld_aux : nullptr;
+      const int left = ep.out_cols - (n_base + cb);
+      const int nch = left <= 0 ? 0 : min(NCH, (left + 31) >> 5);
       uint4 pre[4];
-      auto prefetch = [&](int nc) { aux_load32(aux_row, nc, ep.out_cols, pre); };
-      if (use_aux && n_base + cb < ep.out_cols) prefetch(n_base + cb);
-      for (int c32 = cb; c32 < ce; c32 += 32) {
+      if (nch > 0) {
+        tc::tmem_ld16(t_row + cb, rr[0]);
+        tc::tmem_ld16(t_row + cb + 16, rr[1]);
+        if (use_aux) aux_load32(aux_row, n_base + cb, ep.out_cols, pre);
+      }
+#pragma unroll 1
+      for (int ch = 0; ch < nch; ch++) {  // nch is warp-uniform
+        const int c32 = cb + 32 * ch;
         const int n0 = n_base + c32;
-        if (n0 >= ep.out_cols) break;  // warp-uniform
-        tc::tmem_ld16(t_row + c32, rr[0]);
-        tc::tmem_ld16(t_row + c32 + 16, rr[1]);
-        float aux[32];
-        if (use_aux) {
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(pre);
+        const bool full = n0 + 32 <= ep.out_cols;
+        uint4 cur[4];
 #pragma unroll
-          for (int j = 0; j < 16; j++) {
-            const float2 f = __bfloat1622float2(h[j]);
-            aux[2 * j] = f.x;
-            aux[2 * j + 1] = f.y;
+        for (int i = 0; i < 4; i++) cur[i] = use_aux ? pre[i] : make_uint4(0u, 0u, 0u, 0u);
+        if (use_aux && ch + 1 < nch) aux_load32(aux_row, n0 + 32, ep.out_cols, pre);
+        const __nv_bfloat16* auxh = reinterpret_cast<const __nv_bfloat16*>(cur);
+        float bz[32];
+        if constexpr (EPI == EPI_FWD) {
+          if (full && ((reinterpret_cast<uintptr_t>(ep.bias + n0) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              const float4 t = __ldg(reinterpret_cast<const float4*>(ep.bias + n0) + i);
+              bz[4 * i] = t.x;
+              bz[4 * i + 1] = t.y;
+              bz[4 * i + 2] = t.z;
+              bz[4 * i + 3] = t.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++) bz[j] = (n0 + j) < ep.out_cols ? ep.bias[n0 + j] : 0.f;
           }
-          if (c32 + 32 < ce && n0 + 32 < ep.out_cols) prefetch(n0 + 32);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; j++) aux[j] = 0.f;
         }
-        tc::tmem_wait_ld();
+        tc::tmem_wait_ld_tie(rr[0], rr[1]);
         float v[32], z[32];
 #pragma unroll
         for (int j = 0; j < 32; j++) {
           const float acc = have_acc ? __uint_as_float(rr[j >> 4][j & 15]) : 0.f;
           if constexpr (EPI == EPI_FWD) {
-            z[j] = acc + ((n0 + j) < ep.out_cols ? ep.bias[n0 + j] : 0.f);
+            z[j] = acc + bz[j];
           } else if constexpr (EPI == EPI_DGRAD) {
-            v[j] = (row_ok && n0 + j < ep.out_cols) ? acc : 0.f;
+            v[j] = (row_ok && (full || n0 + j < ep.out_cols)) ? acc : 0.f;
           } else {
-            v[j] = ep.alpha * acc + (ep.aux ? ep.beta * aux[j] : 0.f) + (row == n0 + j ? ep.diag : 0.f);
+            v[j] = use_aux ? axpb(ep.alpha, acc, ep.beta, __bfloat162float(auxh[j])) : __fmul_rn(ep.alpha, acc);
+          }
+        }
+        if constexpr (EPI == EPI_BF16) {
+          if (n0 == row0) {  // this chunk's columns are the warp's rows: the diagonal passes through it
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] = j == lane ? __fadd_rn(v[j], ep.diag) : v[j];
           }
         }
         if constexpr (EPI == EPI_FWD) act_fwd_row(z, v, ep.act);
-        if constexpr (EPI == EPI_DGRAD) act_grad_row(v, aux, ep.act);
-        if (lane == 0) tc::bulk_wait_read<0>();  // the previous tile's stores have read the staging area
+        if constexpr (EPI == EPI_DGRAD) {
+          float aux[32];
+#pragma unroll
+          for (int j = 0; j < 32; j++) aux[j] = __bfloat162float(auxh[j]);
+          act_grad_row(v, aux, ep.act);
+        }
+        uint8_t* st = stg + (NB == 2 ? (seq & 1u) * GemmSmem<BN, EPI>::STG_ONE : 0u);
+        seq++;
+        if (lane == 0) tc::bulk_wait_read<NB - 1>();  // the store that last read this tile is done with it
         __syncwarp();
-        stage_row32(stg, lane, v);
+        stage_row32(st, lane, v);
         if constexpr (EPI == EPI_FWD) {
-          if (ep.out2) stage_row32(stg + 2048, lane, z);
+          if (ep.out2) stage_row32(st + 2048, lane, z);
+        }
+        if (ch + 1 < nch) {  // the registers were consumed above: the next chunk's load reuses them
+          tc::tmem_ld16(t_row + c32 + 32, rr[0]);
+          tc::tmem_ld16(t_row + c32 + 48, rr[1]);
         }
         tc::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tc::tma_store_3d(tmC, stg, n0, row0, batch);
+          tc::tma_store_3d(tmC, st, n0, row0, batch);
           if constexpr (EPI == EPI_FWD) {
-            if (ep.out2) tc::tma_store_3d(tmC2, stg + 2048, n0, row0, batch);
+            if (ep.out2) tc::tma_store_3d(tmC2, st + 2048, n0, row0, batch);
           }
           tc::bulk_commit();
         }
@@ -507,8 +551,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
                             (ep.ld_aux % 8) == 0);
           }
 #pragma unroll
-          for (int j = 0; j < 16; j++)
-            v[j] = ep.alpha * v[j] + (ep.aux ? ep.beta * x[j] : 0.f) + (row == n0 + j ? ep.diag : 0.f);
+          for (int j = 0; j < 16; j++) {
+            const float t = ep.aux ? axpb(ep.alpha, v[j], ep.beta, x[j]) : __fmul_rn(ep.alpha, v[j]);
+            v[j] = row == n0 + j ? __fadd_rn(t, ep.diag) : t;
+          }
           const long off = (long)bz * ep.out_bstride + (long)row * ep.ldo + n0;
           if constexpr (EPI == EPI_F32)
             store_row16_f32((float*)ep.out + off, v, nvalid, (ep.ldo % 4) == 0);
@@ -574,16 +620,16 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
-  uint64_t* full = (uint64_t*)(sB + STAGES * S::B_BYTES);
+  uint8_t* stg_base = smem + STAGES * S::STAGE_BYTES;  // [8 warps][STG_WARP], 1 KB aligned
+  float* red = (float*)(stg_base + S::STG_BYTES);        // [4][BN]
+  float* rowscr = red + 4 * BN;                          // [4 warps][8]
+  uint64_t* full = (uint64_t*)(stg_base + S::STG_BYTES + S::RED_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint64_t* epi_done = acc_empty + 2;   // the 8 epilogue warps have finished with TMEM and their stores
   uint32_t* tmem_slot = (uint32_t*)(epi_done + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-  uint8_t* stg_base = smem + STAGES * S::STAGE_BYTES + 256;                     // [8 warps][STG_WARP]
-  float* red = (float*)(stg_base + S::STG_BYTES);                               // [4][BN]
-  float* rowscr = red + 4 * BN;                                                 // [4 warps][8]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_n = (N + BN - 1) / BN, num_m = (M + BM - 1) / BM;
@@ -714,6 +760,7 @@ __global__ void __launch_bounds__(320, 1)
     // warps w and w + 4 share those rows and split the tile's columns
     const int sub = warp & 3;
     const int half = (warp - 2) >> 2;
+    uint32_t stg_seq = 0;  // chunks this warp has staged: picks the staging tile
     int j = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, j++) {
       const TileIdx ti = tile_of(t, num_n, num_m);
@@ -728,7 +775,7 @@ __global__ void __launch_bounds__(320, 1)
       tc::tc_fence_after();
       const uint32_t t_row = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(sub * 32) << 16);
       epilogue_tile<BN, EPI>(ep, t_row, ti.m, ti.n, ti.z, ep.k_splits > 1 ? 0 : ti.z, b1 > b0, sub, half, lane, red,
-                             rowscr, stg_base + (warp - 2) * S::STG_WARP, &tmC, &tmC2);
+                             rowscr, stg_base + (warp - 2) * S::STG_WARP, &tmC, &tmC2, stg_seq);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&acc_empty[buf])) : "memory");
@@ -789,15 +836,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
-  uint64_t* full = (uint64_t*)(sB + STAGES * S::B_BYTES);
+  uint8_t* stg_base = smem + STAGES * S::STAGE_BYTES;  // 1 KB aligned
+  float* red = (float*)(stg_base + GemmSmem<BN, EPI>::STG_BYTES);
+  float* rowscr = red + 4 * BN;
+  uint64_t* full = (uint64_t*)(stg_base + GemmSmem<BN, EPI>::STG_BYTES + GemmSmem<BN, EPI>::RED_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-  uint8_t* stg_base = smem + STAGES * S::STAGE_BYTES + 256;
-  float* red = (float*)(stg_base + GemmSmem<BN, EPI>::STG_BYTES);
-  float* rowscr = red + 4 * BN;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_ctarank();
@@ -935,6 +982,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     // ---------------- epilogue warps 2..9 of each CTA drain its 128 accumulator rows
     const int sub = warp & 3;
     const int half = (warp - 2) >> 2;
+    uint32_t stg_seq = 0;  // chunks this warp has staged: picks the staging tile
     int j = 0;
     for (int t = pair; t < total_tiles; t += npairs, j++) {
       const TileIdx ti = tile_of(t, num_n, num_m);
@@ -953,7 +1001,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       // column partials would fall outside the ceil(M / 128) rows the caller provides
       if (m_blk * BM < M)
         epilogue_tile<BN, EPI>(ep, t_row, m_blk, ti.n, ti.z, ep.k_splits > 1 ? 0 : ti.z, b1 > b0, sub, half, lane, red,
-                               rowscr, stg_base + (warp - 2) * GemmSmem<BN, EPI>::STG_WARP, &tmC, &tmC2);
+                               rowscr, stg_base + (warp - 2) * GemmSmem<BN, EPI>::STG_WARP, &tmC, &tmC2, stg_seq);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_remote(tc::cluster_addr(tc::smem_u32(&acc_empty[buf]), 0));

@@ -162,7 +162,9 @@ __global__ void __launch_bounds__(128, 1)
       // an fp32 G beside a G G built from the rounded G doubles the step's error
 #pragma unroll
       for (int j = 0; j < 32; j++)
-        v[j] = cc * g2[j] + cb * __bfloat162float(__float2bfloat16_rn(v[j])) + (r == c0 + j ? ca : 0.f);
+        v[j] = axpb(cc, g2[j], cb, __bfloat162float(__float2bfloat16_rn(v[j])));
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] = r == c0 + j ? __fadd_rn(v[j], ca) : v[j];
       ns_put32(Gs, r, c0, v);
     }
     publish();
