@@ -35,6 +35,10 @@ int pl_test_gemm_pair_mode(int mode);
 /* Newton-Schulz for matrices with both sides <= 128: 1 = one fused CTA per matrix (the default),
  * 0 = the per-step GEMM chain; a negative mode only queries. Returns the previous mode. */
 int pl_test_ns_small_mode(int mode);
+/* Newton-Schulz for batches with m = min(rows, cols) > 128: 1 = all steps in one persistent
+ * cooperative launch (the default; not used while the stream is being captured), 0 = three GEMM
+ * launches per step; a negative mode only queries. Returns the previous mode. */
+int pl_test_ns_chain_mode(int mode);
 /* Reads and clears the device-side bounded-wait error word (0 = none). */
 int pl_test_device_error(unsigned* code);
 

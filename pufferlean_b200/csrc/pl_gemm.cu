@@ -42,7 +42,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 3-D bf16 tensor map over {cols (contiguous), rows, batch} with a {64, box_rows, 1} box and the
 // 128-byte swizzle the UMMA descriptors expect. Out-of-range elements read as zero.
-static int make_map(CUtensorMap* map, const Operand& op, uint32_t box_rows) {
+int gemm_operand_map(CUtensorMap* map, const Operand& op, uint32_t box_rows) {
   auto enc = encode_fn();
   PL_REQUIRE(enc != nullptr, PL_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
   PL_REQUIRE(((uintptr_t)op.ptr & 15) == 0, PL_ERR_INVALID, "GEMM operand base not 16-byte aligned");
@@ -65,7 +65,7 @@ static int make_map(CUtensorMap* map, const Operand& op, uint32_t box_rows) {
 // Store map of a bf16 output for the staged epilogue: {cols, rows, batch} with a {32, 32, 1} box and
 // the 64-byte swizzle the staging tiles are written in. Returns false when the output cannot take TMA
 // stores (alignment), in which case the epilogue writes directly.
-static bool make_store_map(CUtensorMap* map, const void* ptr, long rows, long cols, long ld, long batch, long bstride) {
+bool gemm_store_map(CUtensorMap* map, const void* ptr, long rows, long cols, long ld, long batch, long bstride) {
   auto enc = encode_fn();
   if (!enc || !ptr || ((uintptr_t)ptr & 15) || (ld * 2) % 16 || ld < cols) return false;
   if (batch > 1 && (bstride * 2) % 16) return false;
@@ -96,9 +96,9 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
              (int)b_mn);
   if (epi == EPI_PPO) PL_REQUIRE(N <= bn, PL_ERR_INVALID, "PPO head needs all %d outputs in one tile (bn=%d)", N, bn);
   CUtensorMap ma, mb;
-  int rc = make_map(&ma, A, a_mn ? 64 : 128);
+  int rc = gemm_operand_map(&ma, A, a_mn ? 64 : 128);
   if (rc) return rc;
-  rc = make_map(&mb, B, b_mn ? 64 : (uint32_t)(pair ? bn / 2 : bn));  // a pair CTA loads half of B's rows
+  rc = gemm_operand_map(&mb, B, b_mn ? 64 : (uint32_t)(pair ? bn / 2 : bn));  // a pair CTA loads half of B's rows
   if (rc) return rc;
   EpiArgs ep = ep_in;
   if (!ep.err) ep.err = device_error_word();
@@ -107,8 +107,8 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
   memset(&mc2, 0, sizeof(mc2));
   ep.tma_out = 0;
   if (epi == EPI_FWD || epi == EPI_DGRAD || epi == EPI_BF16) {
-    bool ok = make_store_map(&mc, ep.out, ep.out_rows, ep.out_cols, ep.ldo, batch, ep.out_bstride);
-    if (ok && epi == EPI_FWD && ep.out2) ok = make_store_map(&mc2, ep.out2, ep.out_rows, ep.out_cols, ep.ldo2, 1, 0);
+    bool ok = gemm_store_map(&mc, ep.out, ep.out_rows, ep.out_cols, ep.ldo, batch, ep.out_bstride);
+    if (ok && epi == EPI_FWD && ep.out2) ok = gemm_store_map(&mc2, ep.out2, ep.out_rows, ep.out_cols, ep.ldo2, 1, 0);
     // the staged epilogue reads its aux tile with aligned 16-byte loads
     if (ok && ep.aux && (((uintptr_t)ep.aux & 15) || (ep.ld_aux % 8) || (batch > 1 && (ep.aux_bstride % 8))))
       ok = false;

@@ -266,13 +266,15 @@ __device__ __forceinline__ float axpb(float alpha, float acc, float beta, float 
 }
 
 // The 32 bf16 aux values of one row at columns [nc, nc + 32) (zero past cols), as four 16-byte words.
+// Read through L2 only: in the persistent Newton-Schulz chain the aux matrix is rewritten by other
+// CTAs between the reads of one SM, so a line kept in L1 could be stale.
 __device__ __forceinline__ void aux_load32(const __nv_bfloat16* aux_row, int nc, int cols, uint4 (&pre)[4]) {
   if (nc + 32 <= cols) {
 #pragma unroll
-    for (int i = 0; i < 4; i++) pre[i] = reinterpret_cast<const uint4*>(aux_row + nc)[i];
+    for (int i = 0; i < 4; i++) pre[i] = __ldcg(reinterpret_cast<const uint4*>(aux_row + nc) + i);
   } else {
     __align__(16) __nv_bfloat16 t[32];
-    for (int q = 0; q < 32; q++) t[q] = (nc + q < cols) ? aux_row[nc + q] : __float2bfloat16_rn(0.f);
+    for (int q = 0; q < 32; q++) t[q] = (nc + q < cols) ? __ldcg(aux_row + nc + q) : __float2bfloat16_rn(0.f);
 #pragma unroll
     for (int i = 0; i < 4; i++) pre[i] = reinterpret_cast<const uint4*>(t)[i];
   }
@@ -470,16 +472,30 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
         }
         tc::tmem_wait_ld_tie(rr[0], rr[1]);
         float v[32], z[32];
+        if (!have_acc) {  // an empty split-K slice: the accumulator was never written
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-          const float acc = have_acc ? __uint_as_float(rr[j >> 4][j & 15]) : 0.f;
-          if constexpr (EPI == EPI_FWD) {
-            z[j] = acc + bz[j];
-          } else if constexpr (EPI == EPI_DGRAD) {
-            v[j] = (row_ok && (full || n0 + j < ep.out_cols)) ? acc : 0.f;
+          for (int j = 0; j < 16; j++) rr[0][j] = rr[1][j] = 0u;
+        }
+        // warp-uniform variants, each a branch-free loop
+        if constexpr (EPI == EPI_FWD) {
+#pragma unroll
+          for (int j = 0; j < 32; j++) z[j] = __uint_as_float(rr[j >> 4][j & 15]) + bz[j];
+        } else if constexpr (EPI == EPI_DGRAD) {
+          if (row_ok && full) {
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] = __uint_as_float(rr[j >> 4][j & 15]);
           } else {
-            v[j] = use_aux ? axpb(ep.alpha, acc, ep.beta, __bfloat162float(auxh[j])) : __fmul_rn(ep.alpha, acc);
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              v[j] = (row_ok && n0 + j < ep.out_cols) ? __uint_as_float(rr[j >> 4][j & 15]) : 0.f;
           }
+        } else if (use_aux) {
+#pragma unroll
+          for (int j = 0; j < 32; j++)
+            v[j] = axpb(ep.alpha, __uint_as_float(rr[j >> 4][j & 15]), ep.beta, __bfloat162float(auxh[j]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j++) v[j] = __fmul_rn(ep.alpha, __uint_as_float(rr[j >> 4][j & 15]));
         }
         if constexpr (EPI == EPI_BF16) {
           if (n0 == row0) {  // this chunk's columns are the warp's rows: the diagonal passes through it
@@ -1028,6 +1044,11 @@ struct Operand {
   long bstride;     // elements between stacked matrices
 };
 
+// 3-D bf16 operand map {cols, rows, batch} with a {64, box_rows, 1} box in the 128-byte swizzle.
+int gemm_operand_map(CUtensorMap* map, const Operand& op, uint32_t box_rows);
+// Store map of a bf16 output for the staged epilogue ({32, 32, 1} box, 64-byte swizzle); false when
+// the output's alignment rules TMA stores out.
+bool gemm_store_map(CUtensorMap* map, const void* ptr, long rows, long cols, long ld, long batch, long bstride);
 // C[M x N] = A * B^T with operands given by their storage; a_mn / b_mn say whether the operand is
 // stored MN-major (storage rows = K) or K-major (storage rows = M or N).
 int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const Operand& B, int M, int N, int K,

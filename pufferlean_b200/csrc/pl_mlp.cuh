@@ -23,11 +23,21 @@ struct NsWork {
   double* part = nullptr;
   long ldx = 0, ldg = 0;
   unsigned* err = nullptr;  // bounded-wait error word for the GEMMs (NULL = the per-device default)
+  unsigned* cnt = nullptr;  // ns_chain_counter_words(batch) words: enables the persistent chain kernel
 };
 
 // 0 = every batch takes the per-step GEMM chain, 1 = matrices with m, n <= 128 run fused in one CTA
 // each (default); a negative mode only queries. Returns the previous mode.
 int ns_set_small_mode(int mode);
+// 0 = every batch takes the per-step GEMM launches, 1 = batches with m > 128 run as one persistent
+// cooperative launch when the workspace has counters (default); a negative mode only queries.
+int ns_set_chain_mode(int mode);
+long ns_chain_counter_words(long batch);
+// Runs the whole chain as one persistent launch when eligible (sets *used); the result then lies in
+// *result (the final bf16 buffer, or the iterate buffer that holds it; NULL for fp32 output).
+int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
+                 long xbs, __nv_bfloat16* nxt, float* out_f32, long ld_out, long obs, __nv_bfloat16* final_bf16,
+                 cudaStream_t st, __nv_bfloat16** result, bool* used);
 // final_bf16 (optional): the last step's bf16 output goes there (not an iterate buffer) instead of
 // back into X; result_at (optional): receives the iterate buffer that holds the bf16 result, and X
 // is then left as it is.

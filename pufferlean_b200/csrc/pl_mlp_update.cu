@@ -310,6 +310,7 @@ static int alloc_session(pl_update* u) {
     u->ns.Xf = dalloc<float>(u, (size_t)(mmax * ldx * u->ns_batch));
     u->ns.U = dalloc<double>(u, nprod);
     u->ns.part = dalloc<double>(u, 4096);
+    u->ns.cnt = dalloc<unsigned>(u, (size_t)ns_chain_counter_words(u->ns_batch));
     for (void* p : {(void*)u->ns.X0, (void*)u->ns.X1, (void*)u->ns.G, (void*)u->ns.B})
       if (p) cudaMemset(p, 0, 1);  // touch
   } else {

@@ -234,6 +234,24 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
   __nv_bfloat16* cur = X;
   __nv_bfloat16* nxt = (X == w.X0) ? w.X1 : w.X0;
   const long xbs_eff = batch > 1 ? xbs : (long)ldx * m;
+  {
+    bool used = false;
+    __nv_bfloat16* res = nullptr;
+    const int rc = ns_chain_try(m, n, batch, coeffs, iters, w, X, ldx, xbs_eff, nxt, out_f32, ld_out,
+                                batch > 1 ? obs : (long)ld_out * m, final_bf16, st, &res, &used);
+    if (rc) return rc;
+    if (used) {
+      if (out_f32 || final_bf16) return PL_OK;
+      if (result_at) {
+        *result_at = res;
+        return PL_OK;
+      }
+      if (res != X)  // result must end where it started
+        PL_CUDA(cudaMemcpy2DAsync(X, ldx * 2, res, ldx * 2, (size_t)n * 2, (size_t)m * batch, cudaMemcpyDeviceToDevice,
+                                  st));
+      return PL_OK;
+    }
+  }
   for (int it = 0; it < iters; it++) {
     const float a = (float)coeffs[3 * it], b = (float)coeffs[3 * it + 1], c = (float)coeffs[3 * it + 2];
     Operand opX{cur, m, n, ldx, batch, xbs_eff};
@@ -469,7 +487,8 @@ extern "C" int pl_ns_batched_bf16_dev(void* Xv, size_t batch, size_t rows, size_
   w.G = (__nv_bfloat16*)scratch(12, gbytes);
   w.B = (__nv_bfloat16*)scratch(13, gbytes);
   double* part = (double*)scratch(14, (size_t)batch * ns_prepare_parts(per) * sizeof(double));
-  if (!w.X0 || !w.X1 || !w.G || !w.B || !part) return PL_ERR_NOMEM;
+  w.cnt = (unsigned*)scratch(15, sizeof(unsigned) * (size_t)ns_chain_counter_words((long)batch));
+  if (!w.X0 || !w.X1 || !w.G || !w.B || !part || !w.cnt) return PL_ERR_NOMEM;
   int rc = launch_ns_prepare(X, (long)batch, (int)rows, (int)cols, eps, part, w.X0, st);
   if (rc) return rc;
   // a wide batch ends in the caller's buffer; a tall one in the workspace, transposed back after

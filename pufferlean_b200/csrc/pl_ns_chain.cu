@@ -1,0 +1,438 @@
+// Persistent Newton-Schulz chain: every product of every quintic step of a batch of matrices in one
+// launch.
+//
+// The per-step form (ns_run_batched) launches three GEMMs per step -- G = X X^T, Pm = a I + b G + c G G,
+// X' = Pm X -- and each launch pays its ramp (barrier set-up, TMEM allocation, the first tile's main
+// loop before any epilogue) and its tail (the last, often partial, wave of tiles) on top of the launch
+// itself. Here one cooperative launch of one CTA per SM walks a single job list -- step by step,
+// product by product, matrix by matrix, tile by tile -- with the warp roles, shared-memory ring,
+// double-buffered TMEM accumulators and epilogue of tc_gemm_kernel. A job waits only for what it
+// reads: per matrix, three counters count the finished tile parts of G, Pm and X'. Each of a tile's
+// 8 epilogue warps waits for its own TMA stores to complete, fences them to the generic proxy and
+// bumps the counter behind a GPU-scope fence (8 parts make a tile; no barrier inside the CTA, so no
+// warp ever waits for another here). The producer warp polls the counter a job needs with acquire
+// loads, then fences to the async proxy before the job's TMA loads.
+// Matrix i's Pm tiles can therefore run while matrix j's G tiles are still in flight, and no SM idles
+// at a product boundary.
+//
+// Deadlock freedom: each CTA takes its jobs in increasing list order and every job depends only on
+// jobs earlier in the list, so the earliest unfinished job always has its inputs; the launch is
+// cooperative, so all CTAs are resident together. Every wait is bounded: a counter wait that runs out
+// sets the device error word and an abort word the other waiters watch, and the CTA drains and
+// returns like the GEMM does on a barrier timeout.
+//
+// Buffers: iterate s lives in xbuf[s & 1]; G and Pm have one buffer each. Overwrites are safe by the
+// chain itself: G(s, i) rewrites G only after X'(s-1, i) finished, which needed all of Pm(s-1, i), the
+// last reader of G(s-1, i); Pm(s, i) needs G(s, i), which needed X'(s-1, i), the last reader of Pm; and
+// X'(s, i) rewrites xbuf[(s+1) & 1] only after Pm(s, i), which transitively needed X'(s-1, i) and
+// G(s-1, i), the last readers of iterate s-1.
+#include "pl_gemm.cuh"
+#include "pl_mlp.cuh"
+#include "pl_runtime.h"
+
+namespace pl {
+
+namespace {
+
+constexpr int kChainBN = 256;
+constexpr int kChainMaxIters = 16;
+constexpr unsigned kParts = 8;  // epilogue warps per tile, each publishing its own part
+
+struct NsChainMaps {
+  CUtensorMap xk[2];  // iterates as K-major operands ({64, 128} boxes)
+  CUtensorMap xn[2];  // iterates as MN-major operands ({64, 64} boxes)
+  CUtensorMap xs[3];  // store maps of iterate 0, iterate 1 and the final bf16 output
+  CUtensorMap gk, gs;  // G: operand and store maps
+  CUtensorMap pk, ps;  // Pm
+};
+
+struct NsChainArgs {
+  int m, n, batch, iters;
+  int final_kind;  // 0: the last iterate into xbuf[iters & 1]; 1: into the final bf16 output; 2: fp32
+  const __nv_bfloat16* G;  // aux of the Pm epilogue
+  long ldg, gbs;
+  float* out_f32;
+  long ld_out, obs;
+  unsigned* cnt;  // [3][batch] finished tile parts (8 per tile) of G, Pm, X', then the abort word (zeroed)
+  unsigned* err;
+  float coef[3 * kChainMaxIters];
+};
+
+struct ChainJob {
+  int s, p, i, mt, nt;
+};
+
+// Job J of the list: step, product (0 G, 1 Pm, 2 X'), matrix, then tile (n fastest).
+__device__ __forceinline__ ChainJob chain_job(long J, int batch, int TG, int TX, int nG, int nX) {
+  const long JS = (long)batch * (2 * TG + TX);
+  ChainJob j;
+  j.s = (int)(J / JS);
+  long r = J - (long)j.s * JS;
+  int t, nn;
+  if (r < (long)batch * TG) {
+    j.p = 0;
+    nn = nG;
+  } else if (r < 2L * batch * TG) {
+    r -= (long)batch * TG;
+    j.p = 1;
+    nn = nG;
+  } else {
+    r -= 2L * batch * TG;
+    j.p = 2;
+    nn = nX;
+  }
+  const int per = j.p == 2 ? TX : TG;
+  j.i = (int)(r / per);
+  t = (int)(r - (long)j.i * per);
+  j.nt = t % nn;
+  j.mt = t / nn;
+  return j;
+}
+
+// Bounded acquire-poll of a tile counter. Gives up early when another CTA has raised the abort word.
+__device__ bool chain_wait(const unsigned* c, unsigned target, unsigned* abort_word, unsigned* err) {
+  for (uint32_t it = 0; it < (1u << 22); it++) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+    if (v >= target) return true;
+    if (*(volatile unsigned*)abort_word) return false;
+    __nanosleep(64);
+  }
+  atomicOr(err, PL_ERR_MBAR_TIMEOUT | 9);
+  atomicExch(abort_word, 1u);
+  return false;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(320, 1)
+    ns_chain_kernel(const __grid_constant__ NsChainMaps maps, const __grid_constant__ NsChainArgs a) {
+  using S = GemmSmem<BN, EPI_BF16>;
+  constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES;
+  constexpr uint32_t IDESC_KK = tc::idesc_bf16(BM, BN, 0, 0);
+  constexpr uint32_t IDESC_KN = tc::idesc_bf16(BM, BN, 0, 1);
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint8_t* stg_base = smem + STAGES * S::STAGE_BYTES;  // [8 warps][STG_WARP], 1 KB aligned
+  uint64_t* full = (uint64_t*)(stg_base + S::STG_BYTES + S::RED_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint64_t* epi_done = acc_empty + 2;
+  uint32_t* tmem_slot = (uint32_t*)(epi_done + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = a.m, n = a.n, B = a.batch;
+  const int nM = (m + BM - 1) / BM, nG = (m + BN - 1) / BN, nX = (n + BN - 1) / BN;
+  const int TG = nM * nG, TX = nM * nX;
+  const long total = (long)a.iters * B * (2 * TG + TX);
+  const int kbG = (n + BK - 1) / BK, kbM = (m + BK - 1) / BK;
+  unsigned* abort_word = a.cnt + 3L * B;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      tc::mbar_init(&acc_full[b], 1);
+      tc::mbar_init(&acc_empty[b], 8);
+    }
+    tc::mbar_init(epi_done, 8);
+    *abort_flag = 0;
+    tc::fence_mbar_init();
+    tc::tma_prefetch_desc(&maps.xk[0]);
+    tc::tma_prefetch_desc(&maps.gk);
+    tc::tma_prefetch_desc(&maps.pk);
+    tc::tma_prefetch_desc(&maps.xn[0]);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: waits for each job's inputs, then one ring across all jobs
+      long it = 0;
+      for (long J = blockIdx.x; J < total && !*abort_flag; J += gridDim.x) {
+        const ChainJob jb = chain_job(J, B, TG, TX, nG, nX);
+        const unsigned* c;
+        unsigned target;
+        if (jb.p == 0) {  // G(s) reads iterate s: all of X'(s-1)
+          c = a.cnt + 2L * B + jb.i;
+          target = kParts * (unsigned)(jb.s * TX);
+        } else if (jb.p == 1) {  // Pm(s) reads G(s)
+          c = a.cnt + jb.i;
+          target = kParts * (unsigned)((jb.s + 1) * TG);
+        } else {  // X'(s) reads Pm(s) (and iterate s, finished before G(s))
+          c = a.cnt + (long)B + jb.i;
+          target = kParts * (unsigned)((jb.s + 1) * TG);
+        }
+        if (target > 0 && !chain_wait(c, target, abort_word, a.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc::fence_proxy_async_global();
+        const CUtensorMap* mA = jb.p == 0 ? &maps.xk[jb.s & 1] : (jb.p == 1 ? &maps.gk : &maps.pk);
+        const CUtensorMap* mB = jb.p == 0 ? &maps.xk[jb.s & 1] : (jb.p == 1 ? &maps.gk : &maps.xn[jb.s & 1]);
+        const int nkb = jb.p == 0 ? kbG : kbM;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; kb++, it++) {
+          const int s = (int)(it % STAGES);
+          if (it >= STAGES &&
+              !tc::mbar_wait(&empty[s], (uint32_t)(((it / STAGES) - 1) & 1), a.err, PL_ERR_MBAR_TIMEOUT | 1)) {
+            ok = false;
+            break;
+          }
+          const int k0 = kb * BK;
+          tc::mbar_expect_tx(&full[s], S::STAGE_BYTES);
+          uint8_t* pa = sA + s * S::A_BYTES;
+          uint8_t* pb = sB + s * S::B_BYTES;
+          tc::tma_load_3d(pa, mA, &full[s], k0, jb.mt * BM, jb.i);
+          if (jb.p != 2) {  // B K-major: BN rows as 128-row boxes (the layout of one BN-row box)
+#pragma unroll
+            for (int h = 0; h < BN / 128; h++)
+              tc::tma_load_3d(pb + h * 16384, mB, &full[s], k0, jb.nt * BN + 128 * h, jb.i);
+          } else {  // B = the iterate read MN-major: 64-column chunks 8 KB apart
+#pragma unroll
+            for (int h = 0; h < BN / 64; h++)
+              tc::tma_load_3d(pb + h * 8192, mB, &full[s], jb.nt * BN + 64 * h, k0, jb.i);
+          }
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          atomicExch(abort_word, 1u);
+          break;
+        }
+      }
+      // every load issued must have landed before the CTA retires
+      for (long i = it - STAGES > 0 ? it - STAGES : 0; i < it; i++)
+        tc::mbar_wait(&full[i % STAGES], (uint32_t)((i / STAGES) & 1), a.err, PL_ERR_MBAR_TIMEOUT | 2);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer (one thread)
+      long it = 0;
+      int j = 0;
+      for (long J = blockIdx.x; J < total && !*abort_flag; J += gridDim.x, j++) {
+        const ChainJob jb = chain_job(J, B, TG, TX, nG, nX);
+        const int nkb = jb.p == 0 ? kbG : kbM;
+        const bool bmn = jb.p == 2;
+        const int buf = j & 1;
+        if (j >= 2 &&
+            !tc::mbar_wait(&acc_empty[buf], (uint32_t)(((j >> 1) - 1) & 1), a.err, PL_ERR_MBAR_TIMEOUT | 3)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < nkb; kb++, it++) {
+          const int s = (int)(it % STAGES);
+          if (!tc::mbar_wait(&full[s], (uint32_t)((it / STAGES) & 1), a.err, PL_ERR_MBAR_TIMEOUT | 4)) {
+            *abort_flag = 1;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t a_addr = tc::smem_u32(sA + s * S::A_BYTES);
+          const uint32_t b_addr = tc::smem_u32(sB + s * S::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; kk++) {
+            const uint64_t ad = tc::sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = bmn ? tc::sw128_desc(b_addr + kk * 2048, 8192, 1024)
+                                    : tc::sw128_desc(b_addr + kk * 32, 16, 1024);
+            tc::umma_bf16(d_tmem, ad, bd, bmn ? IDESC_KN : IDESC_KK, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc::umma_commit(&empty[s]);
+        }
+        tc::umma_commit(&acc_full[buf]);
+      }
+      if (j > 0) tc::mbar_wait(&acc_full[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), a.err, PL_ERR_MBAR_TIMEOUT | 5);
+    }
+  } else {
+    // ---------------- epilogue warps 2..9 (rows 32 (w % 4) .., columns split between w and w + 4)
+    const int sub = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* stg = stg_base + (warp - 2) * S::STG_WARP;
+    uint32_t seq = 0;
+    int j = 0;
+    for (long J = blockIdx.x; J < total; J += gridDim.x, j++) {
+      const ChainJob jb = chain_job(J, B, TG, TX, nG, nX);
+      const int buf = j & 1;
+      if (!tc::mbar_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), a.err, PL_ERR_MBAR_TIMEOUT | 6)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc::tc_fence_after();
+      const uint32_t t_row = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(sub * 32) << 16);
+      const bool last = jb.s + 1 == a.iters;
+      EpiArgs e{};
+      e.err = a.err;
+      e.k_splits = 1;
+      e.nbatch = B;
+      e.tma_out = 1;
+      e.out_rows = m;
+      e.alpha = 1.f;
+      const CUtensorMap* tmC;
+      if (jb.p == 0) {
+        e.out_cols = m;
+        tmC = &maps.gs;
+      } else if (jb.p == 1) {
+        e.out_cols = m;
+        e.alpha = a.coef[3 * jb.s + 2];
+        e.beta = a.coef[3 * jb.s + 1];
+        e.diag = a.coef[3 * jb.s];
+        e.aux = a.G;
+        e.ld_aux = a.ldg;
+        e.aux_bstride = a.gbs;
+        tmC = &maps.ps;
+      } else {
+        e.out_cols = n;
+        tmC = (last && a.final_kind == 1) ? &maps.xs[2] : &maps.xs[(jb.s + 1) & 1];
+      }
+      if (jb.p == 2 && last && a.final_kind == 2) {
+        e.out = a.out_f32;
+        e.ldo = a.ld_out;
+        e.out_bstride = a.obs;
+        e.tma_out = 0;
+        epilogue_tile<BN, EPI_F32>(e, t_row, jb.mt, jb.nt, jb.i, jb.i, true, sub, half, lane, nullptr, nullptr, stg,
+                                   tmC, tmC, seq);
+      } else {
+        epilogue_tile<BN, EPI_BF16>(e, t_row, jb.mt, jb.nt, jb.i, jb.i, true, sub, half, lane, nullptr, nullptr,
+                                    stg, tmC, tmC, seq);
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&acc_empty[buf])) : "memory");
+        // publish this warp's part: its stores have completed, are ordered before generic accesses,
+        // and the count is bumped after a GPU-scope fence (fp32 output is written by every lane: the
+        // warp's lanes were ordered before lane 0 by the epilogue's last __syncwarp)
+        tc::bulk_wait<0>();
+        tc::fence_proxy_async_global();
+        __threadfence();
+        atomicAdd(a.cnt + (long)jb.p * B + jb.i, 1u);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) tc::bulk_wait<0>();
+    tc::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(epi_done)) : "memory");
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (lane == 0) tc::mbar_wait(epi_done, 0, a.err, PL_ERR_MBAR_TIMEOUT | 7);
+    __syncwarp();
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace
+
+static int g_ns_chain = 1;  // 0: every batch takes the per-step launches (tests compare the two)
+int ns_set_chain_mode(int mode) {
+  const int prev = g_ns_chain;
+  if (mode >= 0) g_ns_chain = mode ? 1 : 0;
+  return prev;
+}
+
+long ns_chain_counter_words(long batch) { return 3 * batch + 1; }
+
+int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
+                 long xbs, __nv_bfloat16* nxt, float* out_f32, long ld_out, long obs, __nv_bfloat16* final_bf16,
+                 cudaStream_t st, __nv_bfloat16** result, bool* used) {
+  *used = false;
+  if (!g_ns_chain || !w.cnt || m <= 128 || iters > kChainMaxIters || iters < 1) return PL_OK;
+  if (ldx % 8 || xbs % 8 || w.ldg % 8 || !aligned16(X) || !aligned16(nxt) || !aligned16(w.G) || !aligned16(w.B) ||
+      (final_bf16 && !aligned16(final_bf16)))
+    return PL_OK;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  PL_CUDA(cudaStreamIsCapturing(st, &cap));
+  if (cap != cudaStreamCaptureStatusNone) return PL_OK;  // a cooperative launch is not captured here
+
+  using S = GemmSmem<kChainBN, EPI_BF16>;
+  NsChainMaps mp;
+  memset(&mp, 0, sizeof(mp));
+  __nv_bfloat16* xb[2] = {X, nxt};
+  const long gbs = (long)w.ldg * m;
+  for (int b = 0; b < 2; b++) {
+    Operand op{xb[b], m, n, ldx, batch, xbs};
+    int rc = gemm_operand_map(&mp.xk[b], op, 128);
+    if (rc) return rc;
+    rc = gemm_operand_map(&mp.xn[b], op, 64);
+    if (rc) return rc;
+    if (!gemm_store_map(&mp.xs[b], xb[b], m, n, ldx, batch, xbs)) return PL_OK;
+  }
+  mp.xs[2] = mp.xs[0];
+  if (final_bf16 && !gemm_store_map(&mp.xs[2], final_bf16, m, n, ldx, batch, xbs)) return PL_OK;
+  Operand og{w.G, m, m, w.ldg, batch, gbs}, opm{w.B, m, m, w.ldg, batch, gbs};
+  int rc = gemm_operand_map(&mp.gk, og, 128);
+  if (rc) return rc;
+  rc = gemm_operand_map(&mp.pk, opm, 128);
+  if (rc) return rc;
+  if (!gemm_store_map(&mp.gs, w.G, m, m, w.ldg, batch, gbs) || !gemm_store_map(&mp.ps, w.B, m, m, w.ldg, batch, gbs))
+    return PL_OK;
+
+  NsChainArgs a{};
+  a.m = m;
+  a.n = n;
+  a.batch = batch;
+  a.iters = iters;
+  a.final_kind = out_f32 ? 2 : (final_bf16 ? 1 : 0);
+  a.G = w.G;
+  a.ldg = w.ldg;
+  a.gbs = gbs;
+  a.out_f32 = out_f32;
+  a.ld_out = ld_out;
+  a.obs = obs;
+  a.cnt = w.cnt;
+  a.err = w.err ? w.err : device_error_word();
+  for (int i = 0; i < 3 * iters; i++) a.coef[i] = (float)coeffs[i];
+
+  static int num_sms[64] = {0};
+  static bool configured[64] = {false};
+  int dev = 0;
+  PL_CUDA(cudaGetDevice(&dev));
+  PL_REQUIRE(dev >= 0 && dev < 64, PL_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  if (!configured[dev]) {
+    PL_CUDA(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    PL_CUDA(cudaFuncSetAttribute((const void*)ns_chain_kernel<kChainBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)S::TOTAL));
+    configured[dev] = true;
+  }
+  const long nM = ceil_div(m, 128), TG = nM * ceil_div(m, kChainBN), TX = nM * ceil_div(n, kChainBN);
+  const long total = (long)iters * batch * (2 * TG + TX);
+  const int grid = (int)(total < num_sms[dev] ? total : num_sms[dev]);
+
+  PL_CUDA(cudaMemsetAsync(w.cnt, 0, sizeof(unsigned) * (size_t)ns_chain_counter_words(batch), st));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(320, 1, 1);
+  cfg.dynamicSmemBytes = S::TOTAL;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PL_CUDA(cudaLaunchKernelEx(&cfg, ns_chain_kernel<kChainBN>, mp, a));
+  count_launch();
+  PL_LAUNCH("ns_chain_kernel");
+  *used = true;
+  if (result) *result = out_f32 ? nullptr : (final_bf16 ? final_bf16 : xb[iters & 1]);
+  return PL_OK;
+}
+
+}  // namespace pl

@@ -9,7 +9,8 @@
 //
 // Limit: kNoAllocBytes (32 MiB) per device, which every GPU that loads the library holds until the
 // process exits. The workspace needs 2*batch*m*n + 2*batch*m*m bf16 values (m = min(rows, cols),
-// n = max(rows, cols)), one double per 16384 elements of every matrix for the norm, and 256 bytes;
+// n = max(rows, cols)), one double per 16384 elements of every matrix for the norm, 3 * batch + 1
+// words of tile counters for the persistent chain, and 256 bytes;
 // larger requests are rejected with PL_ERR_INVALID.
 //
 // Sharing: every call on a device uses the same array and leaves its contents behind, so two calls
@@ -66,7 +67,8 @@ extern "C" int pl_ns_batched_bf16_dev_noalloc(void* Xv, size_t batch, size_t row
   const long per = (long)m * n;
   const size_t xbytes = align256((size_t)per * batch * 2), gbytes = align256((size_t)m * m * batch * 2);
   const size_t pbytes = align256((size_t)batch * ns_prepare_parts(per) * sizeof(double));
-  const size_t need = 256 + 2 * xbytes + 2 * gbytes + pbytes;
+  const size_t cbytes = align256(sizeof(unsigned) * (size_t)ns_chain_counter_words((long)batch));
+  const size_t need = 256 + 2 * xbytes + 2 * gbytes + pbytes + cbytes;
   PL_REQUIRE(need <= kNoAllocBytes, PL_ERR_INVALID,
              "no-alloc Newton-Schulz: %zu matrices of %zux%zu need %zu bytes of workspace, above the fixed %zu-byte "
              "limit (use pl_ns_batched_bf16_dev, which allocates)",
@@ -83,6 +85,7 @@ extern "C" int pl_ns_batched_bf16_dev_noalloc(void* Xv, size_t batch, size_t row
   w.G = (__nv_bfloat16*)(b + 256 + 2 * xbytes);
   w.B = (__nv_bfloat16*)(b + 256 + 2 * xbytes + gbytes);
   double* part = (double*)(b + 256 + 2 * xbytes + 2 * gbytes);
+  w.cnt = (unsigned*)(b + 256 + 2 * xbytes + 2 * gbytes + pbytes);
   w.ldx = n;
   w.ldg = m;
   PL_CUDA(cudaMemsetAsync(w.err, 0, sizeof(unsigned), st));

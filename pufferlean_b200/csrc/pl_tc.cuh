@@ -74,6 +74,12 @@ __device__ __forceinline__ void bulk_wait() {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Orders this thread's generic-proxy accesses to global memory with its async-proxy (TMA) accesses:
+// after TMA stores have completed, before a release that publishes them; after an acquire, before
+// TMA loads of what it published.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)map) : "memory");
 }

@@ -1,0 +1,120 @@
+"""The persistent Newton-Schulz chain (every step of a batch in one cooperative launch, with per-matrix
+tile counters as the only synchronisation) against the per-step GEMM launches on the same inputs -- bit
+for bit, since both run the same 128 x 256 tiles through the same epilogue -- and against the f64 oracle:
+square, wide, tall (transposed on the way in and out), sides that are not multiples of the tile, even and
+odd step counts, repeated calls, the allocation-free entry point, and the fp32-output form inside a bf16
+MLP update."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import pufferlean_b200 as plb  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+DP = C.POINTER(C.c_double)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.set_device(0)
+
+
+def _chain(mode):
+    L = plb.lib()
+    L.pl_test_ns_chain_mode.argtypes = [C.c_int]
+    return L.pl_test_ns_chain_mode(mode)
+
+
+def _ns(X, batch, rows, cols, co, entry="pl_ns_batched_bf16_dev"):
+    L = plb.lib()
+    fn = getattr(L, entry)
+    fn.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_double, DP, C.c_size_t, C.c_void_p]
+    rc = fn(X.data_ptr(), batch, rows, cols, 1e-7, co.ctypes.data_as(DP), co.shape[0], None)
+    assert rc == 0, L.pl_last_error()
+    torch.cuda.synchronize()
+    code = C.c_uint(0)
+    assert L.pl_test_device_error(C.byref(code)) == 0 and code.value == 0, hex(code.value)
+
+
+def _both(X0, batch, rows, cols, co, entry="pl_ns_batched_bf16_dev"):
+    prev = _chain(1)
+    try:
+        Xc = X0.clone()
+        _ns(Xc, batch, rows, cols, co, entry)
+        _chain(0)
+        Xs = X0.clone()
+        _ns(Xs, batch, rows, cols, co, entry)
+    finally:
+        _chain(prev)
+    return Xc, Xs
+
+
+def rel(a, b):
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.mark.parametrize("batch,rows,cols", [(8, 512, 512), (5, 384, 768), (3, 256, 1024), (4, 1024, 512),
+                                             (2, 200, 328), (16, 512, 2048), (1, 136, 2048)])
+@pytest.mark.parametrize("steps", [5, 4])
+def test_chain_is_bit_identical_to_per_step_launches(batch, rows, cols, steps):
+    torch.manual_seed(rows + 3 * cols + steps)
+    X0 = torch.randn(batch, rows, cols, device="cuda").to(torch.bfloat16)
+    co = np.ascontiguousarray(O.QUINTIC_COEFFS[:steps])
+    Xc, Xs = _both(X0, batch, rows, cols, co)
+    assert torch.equal(Xc, Xs)
+    assert not torch.equal(Xc, X0)
+
+
+def test_chain_vs_oracle_and_repeatable():
+    batch, rows, cols = 3, 200, 328
+    torch.manual_seed(5)
+    X0 = torch.randn(batch, rows, cols, device="cuda").to(torch.bfloat16)
+    co = np.ascontiguousarray(O.QUINTIC_COEFFS)
+    prev = _chain(1)
+    try:
+        a = X0.clone()
+        _ns(a, batch, rows, cols, co)
+        b = X0.clone()
+        _ns(b, batch, rows, cols, co)
+    finally:
+        _chain(prev)
+    assert torch.equal(a, b)
+    Xin, got = X0.double().cpu().numpy(), a.double().cpu().numpy()
+    for i in range(batch):
+        ref = O.newton_schulz(Xin[i].ravel(), rows, cols, 1e-7, co).reshape(rows, cols)
+        assert rel(got[i], ref) < 2e-2, (i, rel(got[i], ref))
+
+
+def test_chain_noalloc_entry():
+    batch, rows, cols = 6, 512, 768
+    torch.manual_seed(9)
+    X0 = torch.randn(batch, rows, cols, device="cuda").to(torch.bfloat16)
+    co = np.ascontiguousarray(O.QUINTIC_COEFFS)
+    Xc, Xs = _both(X0, batch, rows, cols, co, "pl_ns_batched_bf16_dev_noalloc")
+    assert torch.equal(Xc, Xs)
+    Xr = X0.clone()
+    _ns(Xr, batch, rows, cols, co)  # the allocating entry: same kernels, same result
+    assert torch.equal(Xc, Xr)
+
+
+def test_chain_fp32_output_in_deep_update():
+    """bf16-tier deep MLP update whose two hidden 192 x 192 matrices take the chain (batched, fp32 output
+    for the finalise): the same parameters bit for bit as with per-step launches."""
+    from tests.test_gpu_update import _problem, _run_resident
+    NT, D, H, A, L, E, MB = 2048, 20, 192, 7, 3, 1, 2
+    P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, A, L, 41, 1)
+    perm = O.shuffle_perm(NT, E, 79)
+    prev = _chain(1)
+    try:
+        got_c, _ = _run_resident(pm, P, (L, 1), obs, acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, 0.02, 0.2, 0.5, 1)
+        _chain(0)
+        got_s, _ = _run_resident(pm, P, (L, 1), obs, acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, 0.02, 0.2, 0.5, 1)
+    finally:
+        _chain(prev)
+    assert np.array_equal(got_c, got_s)
