@@ -57,6 +57,7 @@ struct EpiArgs {
   int nbatch;        // number of stacked matrices (z extent when k_splits <= 1)
   int tma_out;       // bf16 outputs leave through shared memory and TMA bulk stores (host-checked)
   float diag;        // EPI_F32 / EPI_BF16: added on the diagonal (row == column) of every matrix
+  const float* alpha_b;  // EPI_F32 / EPI_BF16, optional: per-matrix factor on alpha (indexed by batch)
 };
 
 // Activation codes: 0 ReLU, 1 GELU (tanh form), 2 identity (a linear layer with bias).
@@ -288,6 +289,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
   constexpr int BM = 128;
   const int row = m_tile * BM + sub * 32 + lane;
   const bool row_ok = row < ep.out_rows;
+  const float alpha = ep.alpha_b ? ep.alpha * ep.alpha_b[batch] : ep.alpha;
   if constexpr (EPI == EPI_PPO) {
     // one thread = one minibatch row; BN covers every logit + the value column. The second group of
     // epilogue warps has no columns of its own here and only joins the barriers.
@@ -492,10 +494,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
         } else if (use_aux) {
 #pragma unroll
           for (int j = 0; j < 32; j++)
-            v[j] = axpb(ep.alpha, __uint_as_float(rr[j >> 4][j & 15]), ep.beta, __bfloat162float(auxh[j]));
+            v[j] = axpb(alpha, __uint_as_float(rr[j >> 4][j & 15]), ep.beta, __bfloat162float(auxh[j]));
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; j++) v[j] = __fmul_rn(ep.alpha, __uint_as_float(rr[j >> 4][j & 15]));
+          for (int j = 0; j < 32; j++) v[j] = __fmul_rn(alpha, __uint_as_float(rr[j >> 4][j & 15]));
         }
         if constexpr (EPI == EPI_BF16) {
           if (n0 == row0) {  // this chunk's columns are the warp's rows: the diagonal passes through it
@@ -568,7 +570,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
           }
 #pragma unroll
           for (int j = 0; j < 16; j++) {
-            const float t = ep.aux ? axpb(ep.alpha, v[j], ep.beta, x[j]) : __fmul_rn(ep.alpha, v[j]);
+            const float t = ep.aux ? axpb(alpha, v[j], ep.beta, x[j]) : __fmul_rn(alpha, v[j]);
             v[j] = row == n0 + j ? __fadd_rn(t, ep.diag) : t;
           }
           const long off = (long)bz * ep.out_bstride + (long)row * ep.ldo + n0;

@@ -36,14 +36,22 @@ long ns_chain_counter_words(long batch);
 // Runs the whole chain as one persistent launch when eligible (sets *used); the result then lies in
 // *result (the final bf16 buffer, or the iterate buffer that holds it; NULL for fp32 output).
 int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
-                 long xbs, __nv_bfloat16* nxt, float* out_f32, long ld_out, long obs, __nv_bfloat16* final_bf16,
-                 cudaStream_t st, __nv_bfloat16** result, bool* used);
+                 long xbs, __nv_bfloat16* const xbuf[2], float* out_f32, long ld_out, long obs,
+                 __nv_bfloat16* final_bf16, const float* scale0, cudaStream_t st, __nv_bfloat16** result, bool* used);
 // final_bf16 (optional): the last step's bf16 output goes there (not an iterate buffer) instead of
 // back into X; result_at (optional): receives the iterate buffer that holds the bf16 result, and X
-// is then left as it is.
+// is then left as it is. Iterate 0 is X; iterate s >= 1 lives in w.X0 / w.X1 (X itself when X is one
+// of them). scale0 (optional, m > 128): X is not yet normalised, and scale0[b] (with scale0[b]^2 at
+// scale0[batch + b]) is the per-matrix factor the first step's G and X' epilogues apply; final_bf16
+// may then be X itself (X is read by the first step only; iters >= 2).
 int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
                    long xbs, float* out_f32, long ld_out, long obs, cudaStream_t st,
-                   __nv_bfloat16* final_bf16 = nullptr, __nv_bfloat16** result_at = nullptr);
+                   __nv_bfloat16* final_bf16 = nullptr, __nv_bfloat16** result_at = nullptr,
+                   const float* scale0 = nullptr);
+// Per-matrix 1 / (||X||_F + eps) and its square into scale[0, batch) and scale[batch, 2 batch): the
+// sum-of-squares pass of launch_ns_prepare without the scaled copy.
+int launch_ns_scale_factors(const __nv_bfloat16* X, long batch, int rows, int cols, double eps, double* part,
+                            float* scale, cudaStream_t st);
 // Normalised wide-layout copy of a batch of row-major bf16 matrices (pl_ns.cu).
 long ns_prepare_parts(long per);
 int launch_ns_prepare(const __nv_bfloat16* X, long batch, int rows, int cols, double eps, double* part,

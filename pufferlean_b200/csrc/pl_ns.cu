@@ -207,10 +207,12 @@ int ns_set_small_mode(int mode) {
 
 int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
                    long xbs, float* out_f32, long ld_out, long obs, cudaStream_t st, __nv_bfloat16* final_bf16,
-                   __nv_bfloat16** result_at) {
-  PL_REQUIRE(!final_bf16 || (final_bf16 != w.X0 && final_bf16 != w.X1 && final_bf16 != X), PL_ERR_INVALID,
-             "Newton-Schulz: the final output may not alias the iterates");
+                   __nv_bfloat16** result_at, const float* scale0) {
+  PL_REQUIRE(!final_bf16 || (final_bf16 != w.X0 && final_bf16 != w.X1 && (final_bf16 != X || (scale0 && iters >= 2))),
+             PL_ERR_INVALID, "Newton-Schulz: the final output may not alias the iterates");
   PL_REQUIRE(m <= n, PL_ERR_INVALID, "Newton-Schulz expects the wide layout (m=%d > n=%d)", m, n);
+  PL_REQUIRE(!scale0 || (m > 128 && iters >= 2), PL_ERR_INVALID,
+             "Newton-Schulz: an unnormalised input needs m > 128 and at least two steps");
   if (g_ns_small && n <= 128 && iters <= kNsSmallMaxIters && batch <= 65535) {
     NsSmallCoef cf{};
     for (int i = 0; i < 3 * iters; i++) cf.c[i] = (float)coeffs[i];
@@ -231,14 +233,22 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
     return PL_OK;
   }
   const long gbs = (long)w.ldg * m;
-  __nv_bfloat16* cur = X;
-  __nv_bfloat16* nxt = (X == w.X0) ? w.X1 : w.X0;
   const long xbs_eff = batch > 1 ? xbs : (long)ldx * m;
+  // iterate 0 is X, iterate s >= 1 is xbuf[s & 1]: with X one of the workspace buffers, the other
+  // takes odd iterates and X itself even ones; an outside X is read by the first step only
+  __nv_bfloat16* xbuf[2];
+  if (X == w.X0 || X == w.X1) {
+    xbuf[0] = X;
+    xbuf[1] = X == w.X0 ? w.X1 : w.X0;
+  } else {
+    xbuf[0] = w.X0;
+    xbuf[1] = w.X1;
+  }
   {
     bool used = false;
     __nv_bfloat16* res = nullptr;
-    const int rc = ns_chain_try(m, n, batch, coeffs, iters, w, X, ldx, xbs_eff, nxt, out_f32, ld_out,
-                                batch > 1 ? obs : (long)ld_out * m, final_bf16, st, &res, &used);
+    const int rc = ns_chain_try(m, n, batch, coeffs, iters, w, X, ldx, xbs_eff, xbuf, out_f32, ld_out,
+                                batch > 1 ? obs : (long)ld_out * m, final_bf16, scale0, st, &res, &used);
     if (rc) return rc;
     if (used) {
       if (out_f32 || final_bf16) return PL_OK;
@@ -252,25 +262,30 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
       return PL_OK;
     }
   }
+  __nv_bfloat16* cur = X;
   for (int it = 0; it < iters; it++) {
     const float a = (float)coeffs[3 * it], b = (float)coeffs[3 * it + 1], c = (float)coeffs[3 * it + 2];
+    const bool first = it == 0, last = it + 1 == iters;
+    __nv_bfloat16* nxt = xbuf[(it + 1) & 1];
     Operand opX{cur, m, n, ldx, batch, xbs_eff};
     Operand opG{w.G, m, m, w.ldg, batch, gbs};
     Operand opB{w.B, m, m, w.ldg, batch, gbs};
     EpiArgs e{};
     e.err = w.err;
-    // G = X X^T
+    // G = X X^T (times scale0^2 on an unnormalised input)
     e.out = w.G;
     e.ldo = w.ldg;
     e.out_bstride = gbs;
     e.out_rows = m;
     e.out_cols = m;
     e.alpha = 1.f;
+    e.alpha_b = (first && scale0) ? scale0 + batch : nullptr;
     int rc = gemm_launch(pick_bn(m), EPI_BF16, false, false, opX, opX, m, m, n, batch, e, st);
     if (rc) return rc;
     // Pm = a I + b G + c G G
     e.out = w.B;
     e.alpha = c;
+    e.alpha_b = nullptr;
     e.beta = b;
     e.diag = a;
     e.aux = w.G;
@@ -278,7 +293,7 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
     e.aux_bstride = gbs;
     rc = gemm_launch(pick_bn(m), EPI_BF16, false, false, opG, opG, m, m, m, batch, e, st);
     if (rc) return rc;
-    // X' = Pm X
+    // X' = Pm X (times scale0 on an unnormalised input)
     EpiArgs u{};
     u.err = w.err;
     u.ldo = ldx;
@@ -286,7 +301,7 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
     u.out_rows = m;
     u.out_cols = n;
     u.alpha = 1.f;
-    const bool last = (it + 1 == iters);
+    u.alpha_b = (first && scale0) ? scale0 : nullptr;
     if (last && out_f32) {
       u.out = out_f32;
       u.ldo = ld_out;
@@ -298,7 +313,7 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
       rc = gemm_launch(pick_bn(n), EPI_BF16, false, true, opB, opX, m, n, m, batch, u, st);
       if (rc) return rc;
       if (last && final_bf16) return PL_OK;
-      std::swap(cur, nxt);
+      cur = nxt;
     }
   }
   if (result_at) {
@@ -456,6 +471,32 @@ int launch_ns_prepare(const __nv_bfloat16* X, long batch, int rows, int cols, do
   }
   return PL_OK;
 }
+__global__ void ns_scale_factor_kernel(const double* __restrict__ part, long chunks, long batch, double eps,
+                                       float* __restrict__ scale) {
+  const long b = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  double t = 0.0;
+  for (long c = 0; c < chunks; c++) t += part[b * chunks + c];
+  const double inv = 1.0 / (sqrt(t) + eps);
+  scale[b] = (float)inv;
+  scale[batch + b] = (float)(inv * inv);
+}
+int launch_ns_scale_factors(const __nv_bfloat16* X, long batch, int rows, int cols, double eps, double* part,
+                            float* scale, cudaStream_t st) {
+  const long per = (long)rows * cols, chunks = ns_chunks(per);
+  PL_REQUIRE(batch <= 65535, PL_ERR_UNSUPPORTED, "batched Newton-Schulz: at most 65535 matrices per call");
+  dim3 grid((unsigned)chunks, (unsigned)batch);
+  if ((per % 8) == 0 && ((uintptr_t)X % 16) == 0)
+    ns_sumsq_kernel<true><<<grid, 256, 0, st>>>(X, per, part);
+  else
+    ns_sumsq_kernel<false><<<grid, 256, 0, st>>>(X, per, part);
+  count_launch();
+  PL_LAUNCH("ns_sumsq_kernel");
+  ns_scale_factor_kernel<<<(unsigned)ceil_div(batch, 128), 128, 0, st>>>(part, chunks, batch, eps, scale);
+  count_launch();
+  PL_LAUNCH("ns_scale_factor_kernel");
+  return PL_OK;
+}
 int launch_transpose_bf16(const __nv_bfloat16* src, long batch, int rows, int cols, __nv_bfloat16* dst,
                           cudaStream_t st) {
   dim3 grid((unsigned)ceil_div(cols, 32), (unsigned)ceil_div(rows, 32), (unsigned)batch);
@@ -489,10 +530,20 @@ extern "C" int pl_ns_batched_bf16_dev(void* Xv, size_t batch, size_t rows, size_
   double* part = (double*)scratch(14, (size_t)batch * ns_prepare_parts(per) * sizeof(double));
   w.cnt = (unsigned*)scratch(15, sizeof(unsigned) * (size_t)ns_chain_counter_words((long)batch));
   if (!w.X0 || !w.X1 || !w.G || !w.B || !part || !w.cnt) return PL_ERR_NOMEM;
-  int rc = launch_ns_prepare(X, (long)batch, (int)rows, (int)cols, eps, part, w.X0, st);
+  __nv_bfloat16* res = nullptr;
+  int rc;
+  if (!tall && m > 128 && iters >= 2) {
+    // the normalisation folds into the first step: its G and X' epilogues scale by 1/||X|| squared and
+    // once, and the iterates start from the caller's X without a scaled copy
+    float* scale = (float*)scratch(16, sizeof(float) * 2 * batch);
+    if (!scale) return PL_ERR_NOMEM;
+    rc = launch_ns_scale_factors(X, (long)batch, (int)rows, (int)cols, eps, part, scale, st);
+    if (rc) return rc;
+    return ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, X, n, per, nullptr, 0, 0, st, X, &res, scale);
+  }
+  rc = launch_ns_prepare(X, (long)batch, (int)rows, (int)cols, eps, part, w.X0, st);
   if (rc) return rc;
   // a wide batch ends in the caller's buffer; a tall one in the workspace, transposed back after
-  __nv_bfloat16* res = nullptr;
   rc = ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, w.X0, n, per, nullptr, 0, 0, st, tall ? nullptr : X,
                       &res);
   if (rc) return rc;

@@ -21,7 +21,7 @@
 // sets the device error word and an abort word the other waiters watch, and the CTA drains and
 // returns like the GEMM does on a barrier timeout.
 //
-// Buffers: iterate s lives in xbuf[s & 1]; G and Pm have one buffer each. Overwrites are safe by the
+// Buffers: iterate 0 is the input, iterate s >= 1 lives in buffer s & 1; G and Pm have one buffer each. Overwrites are safe by the
 // chain itself: G(s, i) rewrites G only after X'(s-1, i) finished, which needed all of Pm(s-1, i), the
 // last reader of G(s-1, i); Pm(s, i) needs G(s, i), which needed X'(s-1, i), the last reader of Pm; and
 // X'(s, i) rewrites xbuf[(s+1) & 1] only after Pm(s, i), which transitively needed X'(s-1, i) and
@@ -39,16 +39,17 @@ constexpr int kChainMaxIters = 16;
 constexpr unsigned kParts = 8;  // epilogue warps per tile, each publishing its own part
 
 struct NsChainMaps {
-  CUtensorMap xk[2];  // iterates as K-major operands ({64, 128} boxes)
-  CUtensorMap xn[2];  // iterates as MN-major operands ({64, 64} boxes)
-  CUtensorMap xs[3];  // store maps of iterate 0, iterate 1 and the final bf16 output
+  CUtensorMap xk[3];  // iterate buffers 0, 1 and the input as K-major operands ({64, 128} boxes)
+  CUtensorMap xn[3];  // the same as MN-major operands ({64, 64} boxes)
+  CUtensorMap xs[3];  // store maps of iterate buffers 0, 1 and of the final bf16 output
   CUtensorMap gk, gs;  // G: operand and store maps
   CUtensorMap pk, ps;  // Pm
 };
 
 struct NsChainArgs {
   int m, n, batch, iters;
-  int final_kind;  // 0: the last iterate into xbuf[iters & 1]; 1: into the final bf16 output; 2: fp32
+  int final_kind;  // 0: the last iterate into buffer iters & 1; 1: into the final bf16 output; 2: fp32
+  const float* scale0;  // optional per-matrix factor of an unnormalised input: [batch] s, [batch] s^2
   const __nv_bfloat16* G;  // aux of the Pm epilogue
   long ldg, gbs;
   float* out_f32;
@@ -87,6 +88,21 @@ __device__ __forceinline__ ChainJob chain_job(long J, int batch, int TG, int TX,
   j.nt = t % nn;
   j.mt = t / nn;
   return j;
+}
+
+// Target of the counter job `jb` waits on (0 = none), and the counter itself.
+__device__ __forceinline__ unsigned chain_dep(const ChainJob& jb, const unsigned* cnt, int B, int TG, int TX,
+                                              const unsigned** c) {
+  if (jb.p == 0) {  // G(s) reads iterate s: all of X'(s-1)
+    *c = cnt + 2L * B + jb.i;
+    return kParts * (unsigned)(jb.s * TX);
+  }
+  if (jb.p == 1) {  // Pm(s) reads G(s)
+    *c = cnt + jb.i;
+    return kParts * (unsigned)((jb.s + 1) * TG);
+  }
+  *c = cnt + (long)B + jb.i;  // X'(s) reads Pm(s) (and iterate s, finished before G(s))
+  return kParts * (unsigned)((jb.s + 1) * TG);
 }
 
 // Bounded acquire-poll of a tile counter. Gives up early when another CTA has raised the abort word.
@@ -144,10 +160,10 @@ __global__ void __launch_bounds__(320, 1)
     tc::mbar_init(epi_done, 8);
     *abort_flag = 0;
     tc::fence_mbar_init();
-    tc::tma_prefetch_desc(&maps.xk[0]);
+    tc::tma_prefetch_desc(&maps.xk[2]);
     tc::tma_prefetch_desc(&maps.gk);
     tc::tma_prefetch_desc(&maps.pk);
-    tc::tma_prefetch_desc(&maps.xn[0]);
+    tc::tma_prefetch_desc(&maps.xn[2]);
   }
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, TMEM_COLS);
@@ -165,24 +181,15 @@ __global__ void __launch_bounds__(320, 1)
       for (long J = blockIdx.x; J < total && !*abort_flag; J += gridDim.x) {
         const ChainJob jb = chain_job(J, B, TG, TX, nG, nX);
         const unsigned* c;
-        unsigned target;
-        if (jb.p == 0) {  // G(s) reads iterate s: all of X'(s-1)
-          c = a.cnt + 2L * B + jb.i;
-          target = kParts * (unsigned)(jb.s * TX);
-        } else if (jb.p == 1) {  // Pm(s) reads G(s)
-          c = a.cnt + jb.i;
-          target = kParts * (unsigned)((jb.s + 1) * TG);
-        } else {  // X'(s) reads Pm(s) (and iterate s, finished before G(s))
-          c = a.cnt + (long)B + jb.i;
-          target = kParts * (unsigned)((jb.s + 1) * TG);
-        }
+        const unsigned target = chain_dep(jb, a.cnt, B, TG, TX, &c);
         if (target > 0 && !chain_wait(c, target, abort_word, a.err)) {
           *abort_flag = 1;
           break;
         }
         tc::fence_proxy_async_global();
-        const CUtensorMap* mA = jb.p == 0 ? &maps.xk[jb.s & 1] : (jb.p == 1 ? &maps.gk : &maps.pk);
-        const CUtensorMap* mB = jb.p == 0 ? &maps.xk[jb.s & 1] : (jb.p == 1 ? &maps.gk : &maps.xn[jb.s & 1]);
+        const int xi = jb.s == 0 ? 2 : (jb.s & 1);  // where iterate s lives
+        const CUtensorMap* mA = jb.p == 0 ? &maps.xk[xi] : (jb.p == 1 ? &maps.gk : &maps.pk);
+        const CUtensorMap* mB = jb.p == 0 ? &maps.xk[xi] : (jb.p == 1 ? &maps.gk : &maps.xn[xi]);
         const int nkb = jb.p == 0 ? kbG : kbM;
         bool ok = true;
         for (int kb = 0; kb < nkb; kb++, it++) {
@@ -283,6 +290,7 @@ __global__ void __launch_bounds__(320, 1)
       const CUtensorMap* tmC;
       if (jb.p == 0) {
         e.out_cols = m;
+        if (jb.s == 0 && a.scale0) e.alpha_b = a.scale0 + B;
         tmC = &maps.gs;
       } else if (jb.p == 1) {
         e.out_cols = m;
@@ -295,6 +303,7 @@ __global__ void __launch_bounds__(320, 1)
         tmC = &maps.ps;
       } else {
         e.out_cols = n;
+        if (jb.s == 0 && a.scale0) e.alpha_b = a.scale0;
         tmC = (last && a.final_kind == 1) ? &maps.xs[2] : &maps.xs[(jb.s + 1) & 1];
       }
       if (jb.p == 2 && last && a.final_kind == 2) {
@@ -351,11 +360,12 @@ int ns_set_chain_mode(int mode) {
 long ns_chain_counter_words(long batch) { return 3 * batch + 1; }
 
 int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
-                 long xbs, __nv_bfloat16* nxt, float* out_f32, long ld_out, long obs, __nv_bfloat16* final_bf16,
-                 cudaStream_t st, __nv_bfloat16** result, bool* used) {
+                 long xbs, __nv_bfloat16* const xbuf[2], float* out_f32, long ld_out, long obs,
+                 __nv_bfloat16* final_bf16, const float* scale0, cudaStream_t st, __nv_bfloat16** result, bool* used) {
   *used = false;
   if (!g_ns_chain || !w.cnt || m <= 128 || iters > kChainMaxIters || iters < 1) return PL_OK;
-  if (ldx % 8 || xbs % 8 || w.ldg % 8 || !aligned16(X) || !aligned16(nxt) || !aligned16(w.G) || !aligned16(w.B) ||
+  if (ldx % 8 || xbs % 8 || w.ldg % 8 || !aligned16(X) || !aligned16(xbuf[0]) || !aligned16(xbuf[1]) ||
+      !aligned16(w.G) || !aligned16(w.B) ||
       (final_bf16 && !aligned16(final_bf16)))
     return PL_OK;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
@@ -365,15 +375,15 @@ int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWor
   using S = GemmSmem<kChainBN, EPI_BF16>;
   NsChainMaps mp;
   memset(&mp, 0, sizeof(mp));
-  __nv_bfloat16* xb[2] = {X, nxt};
+  __nv_bfloat16* xb[3] = {xbuf[0], xbuf[1], X};
   const long gbs = (long)w.ldg * m;
-  for (int b = 0; b < 2; b++) {
+  for (int b = 0; b < 3; b++) {
     Operand op{xb[b], m, n, ldx, batch, xbs};
     int rc = gemm_operand_map(&mp.xk[b], op, 128);
     if (rc) return rc;
     rc = gemm_operand_map(&mp.xn[b], op, 64);
     if (rc) return rc;
-    if (!gemm_store_map(&mp.xs[b], xb[b], m, n, ldx, batch, xbs)) return PL_OK;
+    if (b < 2 && !gemm_store_map(&mp.xs[b], xb[b], m, n, ldx, batch, xbs)) return PL_OK;
   }
   mp.xs[2] = mp.xs[0];
   if (final_bf16 && !gemm_store_map(&mp.xs[2], final_bf16, m, n, ldx, batch, xbs)) return PL_OK;
@@ -391,6 +401,7 @@ int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWor
   a.batch = batch;
   a.iters = iters;
   a.final_kind = out_f32 ? 2 : (final_bf16 ? 1 : 0);
+  a.scale0 = scale0;
   a.G = w.G;
   a.ldg = w.ldg;
   a.gbs = gbs;

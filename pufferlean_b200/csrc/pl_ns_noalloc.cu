@@ -10,7 +10,7 @@
 // Limit: kNoAllocBytes (32 MiB) per device, which every GPU that loads the library holds until the
 // process exits. The workspace needs 2*batch*m*n + 2*batch*m*m bf16 values (m = min(rows, cols),
 // n = max(rows, cols)), one double per 16384 elements of every matrix for the norm, 3 * batch + 1
-// words of tile counters for the persistent chain, and 256 bytes;
+// words of tile counters for the persistent chain, 2 * batch floats of per-matrix scale, and 256 bytes;
 // larger requests are rejected with PL_ERR_INVALID.
 //
 // Sharing: every call on a device uses the same array and leaves its contents behind, so two calls
@@ -68,7 +68,8 @@ extern "C" int pl_ns_batched_bf16_dev_noalloc(void* Xv, size_t batch, size_t row
   const size_t xbytes = align256((size_t)per * batch * 2), gbytes = align256((size_t)m * m * batch * 2);
   const size_t pbytes = align256((size_t)batch * ns_prepare_parts(per) * sizeof(double));
   const size_t cbytes = align256(sizeof(unsigned) * (size_t)ns_chain_counter_words((long)batch));
-  const size_t need = 256 + 2 * xbytes + 2 * gbytes + pbytes + cbytes;
+  const size_t sbytes = align256(sizeof(float) * 2 * batch);
+  const size_t need = 256 + 2 * xbytes + 2 * gbytes + pbytes + cbytes + sbytes;
   PL_REQUIRE(need <= kNoAllocBytes, PL_ERR_INVALID,
              "no-alloc Newton-Schulz: %zu matrices of %zux%zu need %zu bytes of workspace, above the fixed %zu-byte "
              "limit (use pl_ns_batched_bf16_dev, which allocates)",
@@ -86,14 +87,20 @@ extern "C" int pl_ns_batched_bf16_dev_noalloc(void* Xv, size_t batch, size_t row
   w.B = (__nv_bfloat16*)(b + 256 + 2 * xbytes + gbytes);
   double* part = (double*)(b + 256 + 2 * xbytes + 2 * gbytes);
   w.cnt = (unsigned*)(b + 256 + 2 * xbytes + 2 * gbytes + pbytes);
+  float* scale = (float*)(b + 256 + 2 * xbytes + 2 * gbytes + pbytes + cbytes);
   w.ldx = n;
   w.ldg = m;
   PL_CUDA(cudaMemsetAsync(w.err, 0, sizeof(unsigned), st));
   __nv_bfloat16* X = (__nv_bfloat16*)Xv;
   const bool tall = rows > cols;
+  __nv_bfloat16* res = nullptr;
+  if (!tall && m > 128 && iters >= 2) {  // normalisation folded into the first step, as in the allocating entry
+    rc = launch_ns_scale_factors(X, (long)batch, (int)rows, (int)cols, eps, part, scale, st);
+    if (rc) return rc;
+    return ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, X, n, per, nullptr, 0, 0, st, X, &res, scale);
+  }
   rc = launch_ns_prepare(X, (long)batch, (int)rows, (int)cols, eps, part, w.X0, st);
   if (rc) return rc;
-  __nv_bfloat16* res = nullptr;
   rc = ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, w.X0, n, per, nullptr, 0, 0, st, tall ? nullptr : X,
                       &res);
   if (rc) return rc;
