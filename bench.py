@@ -381,7 +381,9 @@ def run_e2e(args, wl, state, rank, world, local_rank):
         dt = float(t.item())
     if world > 1:
         L.pl_update_destroy(sess)
-    h2d = 8 * (NT * D + 5 * NT + E * NT)
+    # observations cross the host link as bf16 rows padded to 64 columns (rounded on the host threads,
+    # pl_host_stage.cpp); the other columns and the shuffle as f64
+    h2d = 2 * NT * (-(-D // 64) * 64) + 8 * (5 * NT + E * NT)
     return {"value": world * NT / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": 8 if world == 1 else 16,
             "steps": k, "s_per_step": dt,

@@ -39,6 +39,12 @@ int pl_test_ns_small_mode(int mode);
  * cooperative launch (the default; not used while the stream is being captured), 0 = three GEMM
  * launches per step; a negative mode only queries. Returns the previous mode. */
 int pl_test_ns_chain_mode(int mode);
+/* Host observations in the bf16 tier: 1 = rounded to bf16 on the host threads, a quarter of the bytes
+ * copied (the default), 0 = f64 rows copied and converted on the device; a negative mode only
+ * queries. Returns the previous mode. */
+int pl_test_host_bf16(int mode);
+/* The host rounding itself: rows x D f64 values -> Dp-wide bf16 rows (bits), zero padded. */
+int pl_test_round_rows_bf16(const double* src, long rows, int D, int Dp, uint16_t* dst);
 /* Reads and clears the device-side bounded-wait error word (0 = none). */
 int pl_test_device_error(unsigned* code);
 

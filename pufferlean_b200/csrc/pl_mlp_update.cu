@@ -26,6 +26,7 @@
 #include "pl_mlp.cuh"
 #include "pl_muon.cuh"
 #include "pl_runtime.h"
+#include "pl_host_stage.h"
 
 using namespace pl;
 
@@ -93,6 +94,7 @@ struct pl_update {
   double prof_ms[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   bool loss_on = false;
   double losses[7] = {0, 0, 0, 0, 0, 0, 0};
+  HostStage hstage;  // pinned staging of host observations rounded to bf16 on the host
   // wide action heads (pl_update_set_head): 0 categorical, 1 multi-discrete, 2 Gaussian
   int head_mode = 0;
   int W = 1;
@@ -109,6 +111,7 @@ constexpr float kContLogStdLo = -20.f, kContLogStdHi = 2.f;
 
 static std::mutex g_mu;
 static bool g_loss_on = false;
+static bool g_host_bf16 = true;  // bf16 tier: host observations rounded to bf16 on the host threads
 static double g_losses[7] = {0, 0, 0, 0, 0, 0, 0};
 
 template <typename T>
@@ -817,6 +820,7 @@ int pl_update_destroy(pl_update* u) {
   if (!u) return PL_OK;
   cudaDeviceSynchronize();
   for (cudaEvent_t e : u->ev) cudaEventDestroy(e);
+  u->hstage.release();
   free_all(u);
   delete u;
   return PL_OK;
@@ -884,9 +888,17 @@ int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, c
   const pl_update_desc& d = u->d;
   const long NT = (long)d.NT;
   const int D = (int)d.D;
-  // obs: whole rows per chunk
+  // obs: in the bf16 tier the host threads round the rows to bf16 and a quarter of the f64 bytes
+  // cross the host link (pinned double buffering, conversion of chunk k + 1 overlapping the copy of
+  // chunk k); otherwise whole rows per chunk through the device staging buffer, converted there
+  bool host_done = false;
+  if (u->fast && g_host_bf16 && (size_t)NT * d.D >= ((size_t)1 << 20) && u->hstage.init((size_t)16 << 20) == 0) {
+    if (upload_rows_bf16(u->hstage, obs, NT, D, u->Dp, u->obs, st) != 0)
+      return check_cuda(cudaGetLastError(), "host bf16 observation upload");
+    host_done = true;
+  }
   const size_t rows_per = std::max<size_t>(1, u->stage_elems / d.D);
-  for (size_t r0 = 0; r0 < (size_t)NT; r0 += rows_per) {
+  for (size_t r0 = 0; r0 < (size_t)NT && !host_done; r0 += rows_per) {
     const size_t nr = std::min(rows_per, (size_t)NT - r0);
     PL_CUDA(cudaMemcpyAsync(u->stage, obs + r0 * D, nr * D * sizeof(double), cudaMemcpyHostToDevice, st));
     int rc = u->fast ? launch_obs_to_bf16_f64(u->stage, (long)nr, D, u->Dp, (__nv_bfloat16*)u->obs + r0 * u->Dp, st)
@@ -1358,3 +1370,12 @@ int pl_read_losses(double out[7]) {
 }
 
 }  // extern "C"
+
+// Test hook: 1 = in the bf16 tier, host observations are rounded to bf16 on the host threads before
+// the copy (the default), 0 = f64 rows copied and converted on the device; a negative mode only
+// queries. Returns the previous mode.
+extern "C" int pl_test_host_bf16(int mode) {
+  const int prev = g_host_bf16 ? 1 : 0;
+  if (mode >= 0) g_host_bf16 = mode != 0;
+  return prev;
+}

@@ -1,0 +1,80 @@
+"""Host observations in the bf16 tier are rounded to bf16 on the host threads (f64 -> f32 to nearest,
+f32 -> bf16 to nearest even) and copied as bf16, a quarter of the f64 bytes: the device copy and the
+whole update are bit-identical to copying the f64 rows and converting them on the device, including
+rounding ties, subnormals, signed zeros, infinities after the f32 step and values beyond the bf16
+range, for row widths with and without padding."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import pufferlean_b200 as plb  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def _mode(m):
+    L = plb.lib()
+    L.pl_test_host_bf16.argtypes = [C.c_int]
+    return L.pl_test_host_bf16(m)
+
+
+def _edge_values(n, rng):
+    f32 = np.float32
+    ties = (np.arange(n) % 512 + 256).astype(np.float64) * 2.0 ** -8 + 2.0 ** -17  # halfway between bf16s
+    ties = ties * np.where(rng.random(n) < 0.5, -1.0, 1.0)
+    special = np.array([0.0, -0.0, 1e-40, -1e-40, 3.4e38, -3.4e38, 1e39, -1e39, 6.1e-5, 65504.0, 1.0 + 2 ** -30,
+                        float(f32(1.0) + f32(2 ** -8)), 2.0 ** -126, 2.0 ** -149])
+    out = rng.standard_normal(n) * np.exp(rng.uniform(-20, 20, n))
+    out[: n // 4] = ties[: n // 4]
+    out[n // 4: n // 4 + special.size] = special
+    return out
+
+
+@pytest.mark.parametrize("D", [64, 20])
+def test_host_rounding_bit_identical(D):
+    from tests.test_gpu_update import _problem, _run_resident
+    NT, H, A, L, E, MB = 16384, 128, 5, 1, 2, 4
+    P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, A, L, 61 + D, 1)
+    rng = np.random.default_rng(D)
+    obs = obs.copy()
+    # rounding ties, subnormals and signed zeros among ordinary values (the extremes, which would
+    # overflow the network, are covered elementwise below)
+    x = _edge_values(NT * D // 8, rng)
+    obs[: NT * D // 8] = np.where(np.abs(x) < 8.0, x, np.sign(x) * 2.0 ** -130)
+    perm = O.shuffle_perm(NT, E, 82)
+    args = (acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, 0.02, 0.2, 0.5, 1)
+    prev = _mode(1)
+    try:
+        host, _ = _run_resident(pm, P, (L, 1), obs, *args)
+        _mode(0)
+        dev, _ = _run_resident(pm, P, (L, 1), obs, *args)
+    finally:
+        _mode(prev)
+    assert np.isfinite(host).all()
+    assert np.array_equal(host, dev)
+    assert not np.array_equal(host[:P], pm[:P])
+
+
+def test_host_rounding_matches_device_conversion_elementwise():
+    """The conversion itself over special values (no network in between): torch's f32 -> bf16 on the
+    GPU is the reference for the rounding of the f32 values."""
+    rng = np.random.default_rng(5)
+    x = _edge_values(1 << 16, rng)
+    want = torch.from_numpy(x).to(torch.float32).cuda().to(torch.bfloat16).view(torch.int16).cpu().numpy()
+    L = plb.lib()
+    L.pl_test_round_rows_bf16.argtypes = [C.POINTER(C.c_double), C.c_long, C.c_int, C.c_int,
+                                          C.POINTER(C.c_uint16)]
+    out = np.zeros(x.size, dtype=np.uint16)
+    assert L.pl_test_round_rows_bf16(x.ctypes.data_as(C.POINTER(C.c_double)), x.size // 64, 64, 64,
+                                     out.ctypes.data_as(C.POINTER(C.c_uint16))) == 0
+    assert np.array_equal(out.view(np.int16), want)
