@@ -381,9 +381,10 @@ def run_e2e(args, wl, state, rank, world, local_rank):
         dt = float(t.item())
     if world > 1:
         L.pl_update_destroy(sess)
-    # observations cross the host link as bf16 rows padded to 64 columns (rounded on the host threads,
-    # pl_host_stage.cpp); the other columns and the shuffle as f64
-    h2d = 2 * NT * (-(-D // 64) * 64) + 8 * (5 * NT + E * NT)
+    # the bytes the library copied in the last update: observations partly as bf16 rows rounded on the
+    # host threads, partly as f64 rows converted on the device; the other columns and the shuffle
+    L.pl_update_last_upload_bytes.restype = C.c_uint64
+    h2d = int(L.pl_update_last_upload_bytes())
     return {"value": world * NT / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": 8 if world == 1 else 16,
             "steps": k, "s_per_step": dt,

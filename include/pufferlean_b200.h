@@ -213,6 +213,10 @@ int pl_update_set_advantages_dev(pl_update* u, const float* rew, const float* va
 int pl_update_run(pl_update* u, double lr, void* stream);
 /* Kernels launched by the last pl_update_run (this library's own kernels). */
 uint64_t pl_update_last_launches(const pl_update* u);
+/* Host-to-device bytes the last pl_update_set_columns call (of any session in the process; the
+ * reference-shaped update entries call it once per update) copied: observations as bf16 rows where
+ * the host threads rounded them and as f64 rows otherwise, plus the scalar columns and the shuffle. */
+uint64_t pl_update_last_upload_bytes(void);
 /* Per-class kernel timing with CUDA events on the launch stream while `on` (classes: 0 forward GEMM,
  * 1 PPO-head GEMM, 2 data-gradient GEMM, 3 weight-gradient GEMM incl. split-K sum, 4 Newton-Schulz
  * GEMMs, 5 gather/statistics, 6 optimizer elementwise and reductions, 7 data-parallel collectives).

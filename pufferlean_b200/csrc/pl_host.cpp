@@ -9,12 +9,61 @@
 #include <string.h>
 
 #include "../../include/pufferlean_b200.h"
+#include "pl_host_stage.h"
 
 extern "C" {
 
 // Fisher-Yates per epoch, splitmix64 state chained across epochs (Puffer/RL/VecTrain.lean:240-252).
+// The generator is counter-based (step i of the whole sequence draws splitmix64(seed + (i + 1) * gamma)),
+// so for large inputs the draws of every epoch are computed on all host threads at once and each
+// epoch's swap pass, the only sequential part, runs on its own thread; the output is the same.
+static inline uint64_t sm64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+static const uint64_t kGolden = 0x9E3779B97F4A7C15ULL;
+
 int pl_shuffle_perm(size_t NT, size_t epochs, uint64_t rng, double* out) {
   if (!out && NT * epochs) return PL_ERR_INVALID;
+  if (NT >= ((size_t)1 << 18) && NT < ((size_t)1 << 32)) {
+    uint32_t* k = (uint32_t*)malloc(sizeof(uint32_t) * NT * epochs);
+    uint32_t* a = (uint32_t*)malloc(sizeof(uint32_t) * NT * epochs);
+    if (!k || !a) {
+      free(k);
+      free(a);
+      return PL_ERR_NOMEM;
+    }
+    const size_t total = NT * epochs;
+    pl::host_parallel([&](int t, int T) {  // the draws: step i of epoch e is step e NT + i of the stream
+      const size_t lo = total * t / T, hi = total * (t + 1) / T;
+      for (size_t q = lo; q < hi; q++) {
+        const size_t i = q % NT, j = NT - 1 - i;
+        k[q] = (uint32_t)(sm64(rng + (uint64_t)(q + 1) * kGolden) % (uint64_t)(j + 1));
+      }
+    });
+    pl::host_parallel([&](int t, int T) {  // the swaps, one epoch per thread
+      for (size_t e = (size_t)t; e < epochs; e += (size_t)T) {
+        uint32_t* ae = a + e * NT;
+        const uint32_t* ke = k + e * NT;
+        for (size_t i = 0; i < NT; i++) ae[i] = (uint32_t)i;
+        for (size_t i = 0; i < NT; i++) {
+          if (i + 32 < NT) __builtin_prefetch(ae + ke[i + 32], 1);  // the draws are known ahead
+          const size_t j = NT - 1 - i, kk = ke[i];
+          const uint32_t tmp = ae[j];
+          ae[j] = ae[kk];
+          ae[kk] = tmp;
+        }
+      }
+    });
+    pl::host_parallel([&](int t, int T) {
+      const size_t lo = total * t / T, hi = total * (t + 1) / T;
+      for (size_t q = lo; q < hi; q++) out[q] = (double)a[q];
+    });
+    free(k);
+    free(a);
+    return PL_OK;
+  }
   uint32_t* a = (uint32_t*)malloc(sizeof(uint32_t) * (NT ? NT : 1));
   if (!a) return PL_ERR_NOMEM;
   uint64_t s = rng;
@@ -22,12 +71,8 @@ int pl_shuffle_perm(size_t NT, size_t epochs, uint64_t rng, double* out) {
     for (size_t i = 0; i < NT; i++) a[i] = (uint32_t)i;
     for (size_t i = 0; i < NT; i++) {
       const size_t j = NT - 1 - i;
-      s += 0x9E3779B97F4A7C15ULL;
-      uint64_t z = s;
-      z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
-      z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
-      z ^= z >> 31;
-      const size_t k = (size_t)(z % (uint64_t)(j + 1));
+      s += kGolden;
+      const size_t k = (size_t)(sm64(s) % (uint64_t)(j + 1));
       const uint32_t t = a[j];
       a[j] = a[k];
       a[k] = t;
@@ -39,15 +84,13 @@ int pl_shuffle_perm(size_t NT, size_t epochs, uint64_t rng, double* out) {
   return PL_OK;
 }
 
-// Truncated GAE, rho = c = 1, reward clamp, adv[T-1] = 0, ret = adv + val (row e*T + t).
-int pl_gae_soa(const double* vals, const double* rews, const double* terms, size_t N, size_t T, double gamma,
-               double lam, double* out) {
-  if ((!vals || !rews || !terms || !out) && N * T) return PL_ERR_INVALID;
-  const size_t NT = N * T;
-  double* adv = out;
-  double* ret = out + NT;
+// Truncated GAE, rho = c = 1, reward clamp, adv[T-1] = 0, ret = adv + val (row e*T + t). Every
+// environment's backward scan is independent: large inputs split the environments over the host
+// threads (each scan keeps its own operation order, so the output is the same).
+static void gae_envs(const double* vals, const double* rews, const double* terms, size_t e0, size_t e1, size_t T,
+                     double gamma, double lam, double* adv, double* ret) {
   const volatile double gl = gamma * lam;
-  for (size_t e = 0; e < N; e++) {
+  for (size_t e = e0; e < e1; e++) {
     const size_t base = e * T;
     if (T >= 1) adv[base + T - 1] = 0.0;
     double last = 0.0;
@@ -65,8 +108,23 @@ int pl_gae_soa(const double* vals, const double* rews, const double* terms, size
       last = delta + kn;
       adv[t] = last;
     }
+    for (size_t t = base; t < base + T; t++) ret[t] = adv[t] + vals[t];
   }
-  for (size_t t = 0; t < NT; t++) ret[t] = adv[t] + vals[t];
+}
+
+int pl_gae_soa(const double* vals, const double* rews, const double* terms, size_t N, size_t T, double gamma,
+               double lam, double* out) {
+  if ((!vals || !rews || !terms || !out) && N * T) return PL_ERR_INVALID;
+  const size_t NT = N * T;
+  double* adv = out;
+  double* ret = out + NT;
+  if (NT >= ((size_t)1 << 18) && N >= 64) {
+    pl::host_parallel([&](int t, int Tn) {
+      gae_envs(vals, rews, terms, N * t / Tn, N * (t + 1) / Tn, T, gamma, lam, adv, ret);
+    });
+    return PL_OK;
+  }
+  gae_envs(vals, rews, terms, 0, N, T, gamma, lam, adv, ret);
   return PL_OK;
 }
 

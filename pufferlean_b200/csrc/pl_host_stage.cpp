@@ -99,7 +99,9 @@ inline uint16_t bf16_bits(float f) {
   return (uint16_t)(nan ? 0x7FFFu : r);
 }
 
-void rows_to_bf16(const double* src, long r0, long r1, int D, int Dp, uint16_t* dst) {
+// Cloned for AVX-512 and AVX2 with run-time dispatch (the library is built for baseline x86-64).
+__attribute__((target_clones("avx512f", "avx2", "default"))) void rows_to_bf16(const double* src, long r0, long r1,
+                                                                               int D, int Dp, uint16_t* dst) {
   for (long r = r0; r < r1; r++) {
     const double* s = src + r * D;
     uint16_t* o = dst + r * Dp;
@@ -111,6 +113,7 @@ void rows_to_bf16(const double* src, long r0, long r1, int D, int Dp, uint16_t* 
 }  // namespace
 
 int host_threads() { return pool().size(); }
+void host_parallel(const std::function<void(int, int)>& fn) { pool().run(fn); }
 
 int HostStage::init(size_t bytes) {
   if (buf[0] && cap >= bytes) return 0;
@@ -143,14 +146,24 @@ void HostStage::release() {
   cap = 0;
 }
 
-int upload_rows_bf16(HostStage& hs, const double* obs, long NT, int D, int Dp, void* dst_dev, cudaStream_t st) {
+int upload_rows_bf16(HostStage& hs, const double* obs, long NT, int D, int Dp, void* dst_dev, cudaStream_t st,
+                     const std::function<int(long, long)>& dev_rows) {
   const size_t row_bytes = (size_t)Dp * 2;
   const long rows = std::max<long>(1, (long)(hs.cap / row_bytes));
   uint16_t* dst = (uint16_t*)dst_dev;
   Pool& P = pool();
+  // Host share: with H the host threads' f64 read rate (about 6 GB/s per thread, at most ~90 GB/s)
+  // and L the link rate (~50 GB/s), rounding a share a on the host takes a S / H and the link moves
+  // (a / 4 + 1 - a) S, so both end together at a = H / (L + 0.75 H).
+  long NH = NT;
+  if (dev_rows) {
+    const double H = std::min(6.0 * P.size(), 90.0), L = 50.0;
+    NH = std::min(NT, std::max(0L, (long)(NT * (H / (L + 0.75 * H)))));
+  }
+  long dnext = NH;  // next row handed to the device
   int k = 0;
-  for (long r0 = 0; r0 < NT; r0 += rows, k ^= 1) {
-    const long nr = std::min(rows, NT - r0);
+  for (long r0 = 0; r0 < NH; r0 += rows, k ^= 1) {
+    const long nr = std::min(rows, NH - r0);
     if (hs.used[k] && cudaEventSynchronize(hs.done[k]) != cudaSuccess) return -1;  // its last copy has left
     uint16_t* b = (uint16_t*)hs.buf[k];
     const double* s = obs + r0 * D;
@@ -161,7 +174,16 @@ int upload_rows_bf16(HostStage& hs, const double* obs, long NT, int D, int Dp, v
     if (cudaMemcpyAsync(dst + r0 * Dp, b, (size_t)nr * row_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) return -1;
     if (cudaEventRecord(hs.done[k], st) != cudaSuccess) return -1;
     hs.used[k] = true;
+    if (dev_rows && dnext < NT) {  // the device's rows in proportion, queued behind this chunk's copy
+      const long want = NH > 0 ? (long)((double)(NT - NH) * (double)(r0 + nr) / (double)NH) + NH : NT;
+      const long upto = (r0 + nr >= NH) ? NT : std::min(NT, want);
+      if (upto > dnext) {
+        if (dev_rows(dnext, upto - dnext) != 0) return -1;
+        dnext = upto;
+      }
+    }
   }
+  if (dev_rows && dnext < NT && dev_rows(dnext, NT - dnext) != 0) return -1;
   return 0;
 }
 

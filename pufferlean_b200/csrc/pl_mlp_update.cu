@@ -18,6 +18,8 @@
 #include <math.h>
 #include <string.h>
 
+#include <atomic>
+#include <functional>
 #include <mutex>
 #include <vector>
 
@@ -111,7 +113,8 @@ constexpr float kContLogStdLo = -20.f, kContLogStdHi = 2.f;
 
 static std::mutex g_mu;
 static bool g_loss_on = false;
-static bool g_host_bf16 = true;  // bf16 tier: host observations rounded to bf16 on the host threads
+static bool g_host_bf16 = true;
+static std::atomic<uint64_t> g_upload_bytes{0};  // host-to-device bytes of the last set_columns call  // bf16 tier: host observations rounded to bf16 on the host threads
 static double g_losses[7] = {0, 0, 0, 0, 0, 0, 0};
 
 template <typename T>
@@ -827,6 +830,7 @@ int pl_update_destroy(pl_update* u) {
 }
 
 uint64_t pl_update_last_launches(const pl_update* u) { return u ? u->launches : 0; }
+uint64_t pl_update_last_upload_bytes(void) { return g_upload_bytes.load(); }
 
 }  // extern "C"
 
@@ -892,26 +896,52 @@ int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, c
   // cross the host link (pinned double buffering, conversion of chunk k + 1 overlapping the copy of
   // chunk k); otherwise whole rows per chunk through the device staging buffer, converted there
   bool host_done = false;
+  uint64_t bytes = 0;
+  long dev_rows_n = 0;
   if (u->fast && g_host_bf16 && (size_t)NT * d.D >= ((size_t)1 << 20) && u->hstage.init((size_t)16 << 20) == 0) {
-    if (upload_rows_bf16(u->hstage, obs, NT, D, u->Dp, u->obs, st) != 0)
+    // from pinned memory a share of the rows also goes as f64 through the device staging buffer
+    cudaPointerAttributes at{};
+    const bool pinned = cudaPointerGetAttributes(&at, obs) == cudaSuccess && at.type == cudaMemoryTypeHost;
+    cudaGetLastError();
+    std::function<int(long, long)> dev;
+    if (pinned)
+      dev = [&](long r0, long nr) -> int {
+        const long per = std::max<long>(1, (long)(u->stage_elems / d.D));
+        for (long r = r0; r < r0 + nr; r += per) {
+          const long n = std::min(per, r0 + nr - r);
+          if (cudaMemcpyAsync(u->stage, obs + r * D, (size_t)n * D * sizeof(double), cudaMemcpyHostToDevice, st) !=
+              cudaSuccess)
+            return -1;
+          bytes += (uint64_t)n * D * sizeof(double);
+          dev_rows_n += n;
+          if (launch_obs_to_bf16_f64(u->stage, n, D, u->Dp, (__nv_bfloat16*)u->obs + r * u->Dp, st) != PL_OK)
+            return -1;
+        }
+        return 0;
+      };
+    if (upload_rows_bf16(u->hstage, obs, NT, D, u->Dp, u->obs, st, dev) != 0)
       return check_cuda(cudaGetLastError(), "host bf16 observation upload");
+    bytes += (uint64_t)(NT - dev_rows_n) * u->Dp * 2;
     host_done = true;
   }
   const size_t rows_per = std::max<size_t>(1, u->stage_elems / d.D);
   for (size_t r0 = 0; r0 < (size_t)NT && !host_done; r0 += rows_per) {
     const size_t nr = std::min(rows_per, (size_t)NT - r0);
     PL_CUDA(cudaMemcpyAsync(u->stage, obs + r0 * D, nr * D * sizeof(double), cudaMemcpyHostToDevice, st));
+    bytes += (uint64_t)nr * D * sizeof(double);
     int rc = u->fast ? launch_obs_to_bf16_f64(u->stage, (long)nr, D, u->Dp, (__nv_bfloat16*)u->obs + r0 * u->Dp, st)
                      : launch_obs_to_f32_f64(u->stage, (long)nr * D, (float*)u->obs + r0 * D, st);
     if (rc) return rc;
   }
   PL_CUDA(cudaMemcpyAsync(u->adv_c, adv, NT * sizeof(double), cudaMemcpyHostToDevice, st));
+  bytes += (uint64_t)NT * sizeof(double);
   if (u->head_mode != 0) {
     // wide action rows (NT x W) -> fp32 through staging; the categorical column is unused
     const size_t n = (size_t)NT * u->W;
     for (size_t off = 0; off < n; off += u->stage_elems) {
       const size_t c = std::min(u->stage_elems, n - off);
       PL_CUDA(cudaMemcpyAsync(u->stage, acts + off, c * 8, cudaMemcpyHostToDevice, st));
+      bytes += c * 8;
       int rc = launch_f64_to_f32_rows(u->stage, (long)c, u->actw_c + off, st);
       if (rc) return rc;
     }
@@ -926,10 +956,13 @@ int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, c
     PL_CUDA(cudaMemcpyAsync(s + per, ret + off, c * 8, cudaMemcpyHostToDevice, st));
     PL_CUDA(cudaMemcpyAsync(s + 2 * per, olp + off, c * 8, cudaMemcpyHostToDevice, st));
     if (u->ov_c) PL_CUDA(cudaMemcpyAsync(s + 3 * per, oldVal + off, c * 8, cudaMemcpyHostToDevice, st));
+    bytes += c * 8 * (u->ov_c ? 4 : 3);
     int rc = launch_columns(s, s + per, s + 2 * per, u->ov_c ? s + 3 * per : nullptr, (long)c, u->act_c + off,
                             u->ret_c + off, u->olp_c + off, u->ov_c ? u->ov_c + off : nullptr, st);
     if (rc) return rc;
   }
+  bytes += (uint64_t)d.epochs * d.NT * sizeof(double);
+  g_upload_bytes.store(bytes);
   return staged(u, perm, d.epochs * d.NT, st, [&](double* sp, size_t c, size_t off) {
     return launch_perm(sp, (long)c, u->perm + off, st);
   });

@@ -2,7 +2,8 @@
 f32 -> bf16 to nearest even) and copied as bf16, a quarter of the f64 bytes: the device copy and the
 whole update are bit-identical to copying the f64 rows and converting them on the device, including
 rounding ties, subnormals, signed zeros, infinities after the f32 step and values beyond the bf16
-range, for row widths with and without padding."""
+range, for row widths with and without padding, from pageable and from pinned memory (where a share of
+the rows goes as f64 and is converted on the device)."""
 import ctypes as C
 
 import numpy as np
@@ -40,8 +41,10 @@ def _edge_values(n, rng):
     return out
 
 
-@pytest.mark.parametrize("D", [64, 20])
-def test_host_rounding_bit_identical(D):
+@pytest.mark.parametrize("D,pinned", [(64, False), (20, False), (64, True), (72, True)])
+def test_host_rounding_bit_identical(D, pinned):
+    """Pageable rows are all rounded on the host; pinned rows are split between the host rounding and
+    f64 copies converted on the device."""
     from tests.test_gpu_update import _problem, _run_resident
     NT, H, A, L, E, MB = 16384, 128, 5, 1, 2, 4
     P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, A, L, 61 + D, 1)
@@ -52,6 +55,10 @@ def test_host_rounding_bit_identical(D):
     x = _edge_values(NT * D // 8, rng)
     obs[: NT * D // 8] = np.where(np.abs(x) < 8.0, x, np.sign(x) * 2.0 ** -130)
     perm = O.shuffle_perm(NT, E, 82)
+    keep = None
+    if pinned:
+        keep = torch.from_numpy(obs).pin_memory()
+        obs = keep.numpy()
     args = (acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, 0.02, 0.2, 0.5, 1)
     prev = _mode(1)
     try:
