@@ -44,6 +44,7 @@ struct NsChainMaps {
   CUtensorMap xs[3];  // store maps of iterate buffers 0, 1 and of the final bf16 output
   CUtensorMap gk, gs;  // G: operand and store maps
   CUtensorMap pk, ps;  // Pm
+  CUtensorMap xk256[3], gk256;  // K-major B views with 256-row boxes
 };
 
 struct NsChainArgs {
@@ -189,7 +190,7 @@ __global__ void __launch_bounds__(320, 1)
         tc::fence_proxy_async_global();
         const int xi = jb.s == 0 ? 2 : (jb.s & 1);  // where iterate s lives
         const CUtensorMap* mA = jb.p == 0 ? &maps.xk[xi] : (jb.p == 1 ? &maps.gk : &maps.pk);
-        const CUtensorMap* mB = jb.p == 0 ? &maps.xk[xi] : (jb.p == 1 ? &maps.gk : &maps.xn[xi]);
+        const CUtensorMap* mB = jb.p == 0 ? &maps.xk256[xi] : (jb.p == 1 ? &maps.gk256 : &maps.xn[xi]);
         const int nkb = jb.p == 0 ? kbG : kbM;
         bool ok = true;
         for (int kb = 0; kb < nkb; kb++, it++) {
@@ -204,10 +205,8 @@ __global__ void __launch_bounds__(320, 1)
           uint8_t* pa = sA + s * S::A_BYTES;
           uint8_t* pb = sB + s * S::B_BYTES;
           tc::tma_load_3d(pa, mA, &full[s], k0, jb.mt * BM, jb.i);
-          if (jb.p != 2) {  // B K-major: BN rows as 128-row boxes (the layout of one BN-row box)
-#pragma unroll
-            for (int h = 0; h < BN / 128; h++)
-              tc::tma_load_3d(pb + h * 16384, mB, &full[s], k0, jb.nt * BN + 128 * h, jb.i);
+          if (jb.p != 2) {  // B K-major: one BN-row box
+            tc::tma_load_3d(pb, mB, &full[s], k0, jb.nt * BN, jb.i);
           } else {  // B = the iterate read MN-major: 64-column chunks 8 KB apart
 #pragma unroll
             for (int h = 0; h < BN / 64; h++)
@@ -381,6 +380,8 @@ int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWor
     Operand op{xb[b], m, n, ldx, batch, xbs};
     int rc = gemm_operand_map(&mp.xk[b], op, 128);
     if (rc) return rc;
+    rc = gemm_operand_map(&mp.xk256[b], op, 256);
+    if (rc) return rc;
     rc = gemm_operand_map(&mp.xn[b], op, 64);
     if (rc) return rc;
     if (b < 2 && !gemm_store_map(&mp.xs[b], xb[b], m, n, ldx, batch, xbs)) return PL_OK;
@@ -389,6 +390,8 @@ int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWor
   if (final_bf16 && !gemm_store_map(&mp.xs[2], final_bf16, m, n, ldx, batch, xbs)) return PL_OK;
   Operand og{w.G, m, m, w.ldg, batch, gbs}, opm{w.B, m, m, w.ldg, batch, gbs};
   int rc = gemm_operand_map(&mp.gk, og, 128);
+  if (rc) return rc;
+  rc = gemm_operand_map(&mp.gk256, og, 256);
   if (rc) return rc;
   rc = gemm_operand_map(&mp.pk, opm, 128);
   if (rc) return rc;
