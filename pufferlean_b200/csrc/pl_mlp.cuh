@@ -33,6 +33,27 @@ int ns_set_small_mode(int mode);
 // cooperative launch when the workspace has counters (default); a negative mode only queries.
 int ns_set_chain_mode(int mode);
 long ns_chain_counter_words(long batch);
+// One group of same-shape wide matrices for the persistent chain: iterate 0 is X, later iterates
+// alternate between xbuf[1] and xbuf[0]; G / B the m x m workspaces; the last step writes out_f32,
+// final_bf16 or xbuf[iters & 1]; scale0 (optional) is the first step's per-matrix factor; cnt holds
+// 3 * batch zeroed counters.
+struct NsChainGroupHost {
+  int m, n, batch;
+  __nv_bfloat16 *X, *xbuf[2];
+  long ldx, xbs;
+  __nv_bfloat16 *G, *B;
+  long ldg;
+  float* out_f32;
+  long ld_out, obs;
+  __nv_bfloat16* final_bf16;
+  const float* scale0;
+  unsigned* cnt;
+};
+// Up to 4 groups in one persistent cooperative launch (sets *used; nothing is launched when a group
+// cannot take the chain, the stream is being captured or the chain is switched off). abort_word: one
+// zeroed word.
+int ns_chain_launch(int ngroups, const NsChainGroupHost* groups, const double* coeffs, int iters,
+                    unsigned* abort_word, unsigned* err, cudaStream_t st, bool* used);
 // Runs the whole chain as one persistent launch when eligible (sets *used); the result then lies in
 // *result (the final bf16 buffer, or the iterate buffer that holds it; NULL for fp32 output).
 int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,

@@ -38,6 +38,9 @@ constexpr int kChainBN = 256;
 constexpr int kChainMaxIters = 16;
 constexpr unsigned kParts = 8;  // epilogue warps per tile, each publishing its own part
 
+constexpr int kChainMaxGroups = 4;
+
+// Tensor maps of one group (a batch of same-shape matrices).
 struct NsChainMaps {
   CUtensorMap xk[3];  // iterate buffers 0, 1 and the input as K-major operands ({64, 128} boxes)
   CUtensorMap xn[3];  // the same as MN-major operands ({64, 64} boxes)
@@ -46,64 +49,70 @@ struct NsChainMaps {
   CUtensorMap pk, ps;  // Pm
   CUtensorMap xk256[3], gk256;  // K-major B views with 256-row boxes
 };
+struct NsChainMapSet {
+  NsChainMaps g[kChainMaxGroups];
+};
 
-struct NsChainArgs {
-  int m, n, batch, iters;
+// Shape, buffers and counters of one group.
+struct NsChainGroup {
+  int m, n, batch;
+  int nG, nX, TG, TX, kbG, kbM;  // tile columns of G / X', tiles per matrix, k-blocks of G / the rest
   int final_kind;  // 0: the last iterate into buffer iters & 1; 1: into the final bf16 output; 2: fp32
   const float* scale0;  // optional per-matrix factor of an unnormalised input: [batch] s, [batch] s^2
   const __nv_bfloat16* G;  // aux of the Pm epilogue
   long ldg, gbs;
   float* out_f32;
   long ld_out, obs;
-  unsigned* cnt;  // [3][batch] finished tile parts (8 per tile) of G, Pm, X', then the abort word (zeroed)
+  unsigned* cnt;  // [3][batch] finished tile parts (8 per tile) of G, Pm, X' (zeroed before launch)
+};
+
+struct NsChainArgs {
+  int ngroups, iters;
+  long pjobs[3];   // jobs of each product over all groups, per step
+  long step_jobs;  // their sum
+  unsigned* abort_word;  // zeroed before launch
   unsigned* err;
   float coef[3 * kChainMaxIters];
+  NsChainGroup g[kChainMaxGroups];
 };
 
 struct ChainJob {
-  int s, p, i, mt, nt;
+  int s, p, g, i, mt, nt;
 };
 
-// Job J of the list: step, product (0 G, 1 Pm, 2 X'), matrix, then tile (n fastest).
-__device__ __forceinline__ ChainJob chain_job(long J, int batch, int TG, int TX, int nG, int nX) {
-  const long JS = (long)batch * (2 * TG + TX);
+// Job J of the list: step, product (0 G, 1 Pm, 2 X'), group, matrix, then tile (n fastest).
+__device__ __forceinline__ ChainJob chain_job(long J, const NsChainArgs& a) {
   ChainJob j;
-  j.s = (int)(J / JS);
-  long r = J - (long)j.s * JS;
-  int t, nn;
-  if (r < (long)batch * TG) {
-    j.p = 0;
-    nn = nG;
-  } else if (r < 2L * batch * TG) {
-    r -= (long)batch * TG;
-    j.p = 1;
-    nn = nG;
-  } else {
-    r -= 2L * batch * TG;
-    j.p = 2;
-    nn = nX;
+  j.s = (int)(J / a.step_jobs);
+  long r = J - (long)j.s * a.step_jobs;
+  j.p = 0;
+  while (j.p < 2 && r >= a.pjobs[j.p]) r -= a.pjobs[j.p++];
+  j.g = 0;
+  int per = j.p == 2 ? a.g[0].TX : a.g[0].TG;
+  while (j.g + 1 < a.ngroups && r >= (long)a.g[j.g].batch * per) {
+    r -= (long)a.g[j.g].batch * per;
+    j.g++;
+    per = j.p == 2 ? a.g[j.g].TX : a.g[j.g].TG;
   }
-  const int per = j.p == 2 ? TX : TG;
   j.i = (int)(r / per);
-  t = (int)(r - (long)j.i * per);
+  const int t = (int)(r - (long)j.i * per), nn = j.p == 2 ? a.g[j.g].nX : a.g[j.g].nG;
   j.nt = t % nn;
   j.mt = t / nn;
   return j;
 }
 
 // Target of the counter job `jb` waits on (0 = none), and the counter itself.
-__device__ __forceinline__ unsigned chain_dep(const ChainJob& jb, const unsigned* cnt, int B, int TG, int TX,
-                                              const unsigned** c) {
+__device__ __forceinline__ unsigned chain_dep(const ChainJob& jb, const NsChainGroup& gp, const unsigned** c) {
   if (jb.p == 0) {  // G(s) reads iterate s: all of X'(s-1)
-    *c = cnt + 2L * B + jb.i;
-    return kParts * (unsigned)(jb.s * TX);
+    *c = gp.cnt + 2L * gp.batch + jb.i;
+    return kParts * (unsigned)(jb.s * gp.TX);
   }
   if (jb.p == 1) {  // Pm(s) reads G(s)
-    *c = cnt + jb.i;
-    return kParts * (unsigned)((jb.s + 1) * TG);
+    *c = gp.cnt + jb.i;
+    return kParts * (unsigned)((jb.s + 1) * gp.TG);
   }
-  *c = cnt + (long)B + jb.i;  // X'(s) reads Pm(s) (and iterate s, finished before G(s))
-  return kParts * (unsigned)((jb.s + 1) * TG);
+  *c = gp.cnt + (long)gp.batch + jb.i;  // X'(s) reads Pm(s) (and iterate s, finished before G(s))
+  return kParts * (unsigned)((jb.s + 1) * gp.TG);
 }
 
 // Bounded acquire-poll of a tile counter. Gives up early when another CTA has raised the abort word.
@@ -122,7 +131,7 @@ __device__ bool chain_wait(const unsigned* c, unsigned target, unsigned* abort_w
 
 template <int BN>
 __global__ void __launch_bounds__(320, 1)
-    ns_chain_kernel(const __grid_constant__ NsChainMaps maps, const __grid_constant__ NsChainArgs a) {
+    ns_chain_kernel(const __grid_constant__ NsChainMapSet ms, const __grid_constant__ NsChainArgs a) {
   using S = GemmSmem<BN, EPI_BF16>;
   constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES;
   constexpr uint32_t IDESC_KK = tc::idesc_bf16(BM, BN, 0, 0);
@@ -142,12 +151,8 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = a.m, n = a.n, B = a.batch;
-  const int nM = (m + BM - 1) / BM, nG = (m + BN - 1) / BN, nX = (n + BN - 1) / BN;
-  const int TG = nM * nG, TX = nM * nX;
-  const long total = (long)a.iters * B * (2 * TG + TX);
-  const int kbG = (n + BK - 1) / BK, kbM = (m + BK - 1) / BK;
-  unsigned* abort_word = a.cnt + 3L * B;
+  const long total = (long)a.iters * a.step_jobs;
+  unsigned* abort_word = a.abort_word;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -161,10 +166,10 @@ __global__ void __launch_bounds__(320, 1)
     tc::mbar_init(epi_done, 8);
     *abort_flag = 0;
     tc::fence_mbar_init();
-    tc::tma_prefetch_desc(&maps.xk[2]);
-    tc::tma_prefetch_desc(&maps.gk);
-    tc::tma_prefetch_desc(&maps.pk);
-    tc::tma_prefetch_desc(&maps.xn[2]);
+    tc::tma_prefetch_desc(&ms.g[0].xk[2]);
+    tc::tma_prefetch_desc(&ms.g[0].gk);
+    tc::tma_prefetch_desc(&ms.g[0].pk);
+    tc::tma_prefetch_desc(&ms.g[0].xn[2]);
   }
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, TMEM_COLS);
@@ -180,9 +185,11 @@ __global__ void __launch_bounds__(320, 1)
       // ---------------- TMA producer: waits for each job's inputs, then one ring across all jobs
       long it = 0;
       for (long J = blockIdx.x; J < total && !*abort_flag; J += gridDim.x) {
-        const ChainJob jb = chain_job(J, B, TG, TX, nG, nX);
+        const ChainJob jb = chain_job(J, a);
+        const NsChainGroup& gp = a.g[jb.g];
+        const NsChainMaps& maps = ms.g[jb.g];
         const unsigned* c;
-        const unsigned target = chain_dep(jb, a.cnt, B, TG, TX, &c);
+        const unsigned target = chain_dep(jb, gp, &c);
         if (target > 0 && !chain_wait(c, target, abort_word, a.err)) {
           *abort_flag = 1;
           break;
@@ -191,7 +198,7 @@ __global__ void __launch_bounds__(320, 1)
         const int xi = jb.s == 0 ? 2 : (jb.s & 1);  // where iterate s lives
         const CUtensorMap* mA = jb.p == 0 ? &maps.xk[xi] : (jb.p == 1 ? &maps.gk : &maps.pk);
         const CUtensorMap* mB = jb.p == 0 ? &maps.xk256[xi] : (jb.p == 1 ? &maps.gk256 : &maps.xn[xi]);
-        const int nkb = jb.p == 0 ? kbG : kbM;
+        const int nkb = jb.p == 0 ? gp.kbG : gp.kbM;
         bool ok = true;
         for (int kb = 0; kb < nkb; kb++, it++) {
           const int s = (int)(it % STAGES);
@@ -229,8 +236,8 @@ __global__ void __launch_bounds__(320, 1)
       long it = 0;
       int j = 0;
       for (long J = blockIdx.x; J < total && !*abort_flag; J += gridDim.x, j++) {
-        const ChainJob jb = chain_job(J, B, TG, TX, nG, nX);
-        const int nkb = jb.p == 0 ? kbG : kbM;
+        const ChainJob jb = chain_job(J, a);
+        const int nkb = jb.p == 0 ? a.g[jb.g].kbG : a.g[jb.g].kbM;
         const bool bmn = jb.p == 2;
         const int buf = j & 1;
         if (j >= 2 &&
@@ -270,7 +277,10 @@ __global__ void __launch_bounds__(320, 1)
     uint32_t seq = 0;
     int j = 0;
     for (long J = blockIdx.x; J < total; J += gridDim.x, j++) {
-      const ChainJob jb = chain_job(J, B, TG, TX, nG, nX);
+      const ChainJob jb = chain_job(J, a);
+      const NsChainGroup& gp = a.g[jb.g];
+      const NsChainMaps& maps = ms.g[jb.g];
+      const int m = gp.m, n = gp.n, B = gp.batch;
       const int buf = j & 1;
       if (!tc::mbar_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), a.err, PL_ERR_MBAR_TIMEOUT | 6)) {
         *abort_flag = 1;
@@ -289,26 +299,26 @@ __global__ void __launch_bounds__(320, 1)
       const CUtensorMap* tmC;
       if (jb.p == 0) {
         e.out_cols = m;
-        if (jb.s == 0 && a.scale0) e.alpha_b = a.scale0 + B;
+        if (jb.s == 0 && gp.scale0) e.alpha_b = gp.scale0 + B;
         tmC = &maps.gs;
       } else if (jb.p == 1) {
         e.out_cols = m;
         e.alpha = a.coef[3 * jb.s + 2];
         e.beta = a.coef[3 * jb.s + 1];
         e.diag = a.coef[3 * jb.s];
-        e.aux = a.G;
-        e.ld_aux = a.ldg;
-        e.aux_bstride = a.gbs;
+        e.aux = gp.G;
+        e.ld_aux = gp.ldg;
+        e.aux_bstride = gp.gbs;
         tmC = &maps.ps;
       } else {
         e.out_cols = n;
-        if (jb.s == 0 && a.scale0) e.alpha_b = a.scale0;
-        tmC = (last && a.final_kind == 1) ? &maps.xs[2] : &maps.xs[(jb.s + 1) & 1];
+        if (jb.s == 0 && gp.scale0) e.alpha_b = gp.scale0;
+        tmC = (last && gp.final_kind == 1) ? &maps.xs[2] : &maps.xs[(jb.s + 1) & 1];
       }
-      if (jb.p == 2 && last && a.final_kind == 2) {
-        e.out = a.out_f32;
-        e.ldo = a.ld_out;
-        e.out_bstride = a.obs;
+      if (jb.p == 2 && last && gp.final_kind == 2) {
+        e.out = gp.out_f32;
+        e.ldo = gp.ld_out;
+        e.out_bstride = gp.obs;
         e.tma_out = 0;
         epilogue_tile<BN, EPI_F32>(e, t_row, jb.mt, jb.nt, jb.i, jb.i, true, sub, half, lane, nullptr, nullptr, stg,
                                    tmC, tmC, seq);
@@ -326,7 +336,7 @@ __global__ void __launch_bounds__(320, 1)
         tc::bulk_wait<0>();
         tc::fence_proxy_async_global();
         __threadfence();
-        atomicAdd(a.cnt + (long)jb.p * B + jb.i, 1u);
+        atomicAdd(gp.cnt + (long)jb.p * B + jb.i, 1u);
       }
       __syncwarp();
     }
@@ -358,79 +368,93 @@ int ns_set_chain_mode(int mode) {
 
 long ns_chain_counter_words(long batch) { return 3 * batch + 1; }
 
-int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
-                 long xbs, __nv_bfloat16* const xbuf[2], float* out_f32, long ld_out, long obs,
-                 __nv_bfloat16* final_bf16, const float* scale0, cudaStream_t st, __nv_bfloat16** result, bool* used) {
+// Maps and kernel-side description of one group; returns 1 (nothing launched) when its buffers
+// cannot take the chain's TMA maps.
+static int chain_group(const NsChainGroupHost& h, int iters, NsChainMaps& mp, NsChainGroup& g) {
+  const int m = h.m, n = h.n;
+  if (h.ldx % 8 || h.xbs % 8 || h.ldg % 8 || !aligned16(h.X) || !aligned16(h.xbuf[0]) || !aligned16(h.xbuf[1]) ||
+      !aligned16(h.G) || !aligned16(h.B) || (h.final_bf16 && !aligned16(h.final_bf16)))
+    return 1;
+  memset(&mp, 0, sizeof(mp));
+  __nv_bfloat16* xb[3] = {h.xbuf[0], h.xbuf[1], h.X};
+  const long gbs = (long)h.ldg * m;
+  for (int b = 0; b < 3; b++) {
+    Operand op{xb[b], m, n, h.ldx, h.batch, h.xbs};
+    int rc = gemm_operand_map(&mp.xk[b], op, 128);
+    if (!rc) rc = gemm_operand_map(&mp.xk256[b], op, 256);
+    if (!rc) rc = gemm_operand_map(&mp.xn[b], op, 64);
+    if (rc) return rc;
+    if (b < 2 && !gemm_store_map(&mp.xs[b], xb[b], m, n, h.ldx, h.batch, h.xbs)) return 1;
+  }
+  mp.xs[2] = mp.xs[0];
+  if (h.final_bf16 && !gemm_store_map(&mp.xs[2], h.final_bf16, m, n, h.ldx, h.batch, h.xbs)) return 1;
+  Operand og{h.G, m, m, h.ldg, h.batch, gbs}, opm{h.B, m, m, h.ldg, h.batch, gbs};
+  int rc = gemm_operand_map(&mp.gk, og, 128);
+  if (!rc) rc = gemm_operand_map(&mp.gk256, og, 256);
+  if (!rc) rc = gemm_operand_map(&mp.pk, opm, 128);
+  if (rc) return rc;
+  if (!gemm_store_map(&mp.gs, h.G, m, m, h.ldg, h.batch, gbs) || !gemm_store_map(&mp.ps, h.B, m, m, h.ldg, h.batch, gbs))
+    return 1;
+  const int nM = (int)ceil_div(m, 128);
+  g = NsChainGroup{};
+  g.m = m;
+  g.n = n;
+  g.batch = h.batch;
+  g.nG = (int)ceil_div(m, kChainBN);
+  g.nX = (int)ceil_div(n, kChainBN);
+  g.TG = nM * g.nG;
+  g.TX = nM * g.nX;
+  g.kbG = (int)ceil_div(n, 64);
+  g.kbM = (int)ceil_div(m, 64);
+  g.final_kind = h.out_f32 ? 2 : (h.final_bf16 ? 1 : 0);
+  g.scale0 = h.scale0;
+  g.G = h.G;
+  g.ldg = h.ldg;
+  g.gbs = gbs;
+  g.out_f32 = h.out_f32;
+  g.ld_out = h.ld_out;
+  g.obs = h.obs;
+  g.cnt = h.cnt;
+  (void)iters;
+  return PL_OK;
+}
+
+int ns_chain_launch(int ngroups, const NsChainGroupHost* hs, const double* coeffs, int iters, unsigned* abort_word,
+                    unsigned* err, cudaStream_t st, bool* used) {
   *used = false;
-  if (!g_ns_chain || !w.cnt || m <= 128 || iters > kChainMaxIters || iters < 1) return PL_OK;
-  if (ldx % 8 || xbs % 8 || w.ldg % 8 || !aligned16(X) || !aligned16(xbuf[0]) || !aligned16(xbuf[1]) ||
-      !aligned16(w.G) || !aligned16(w.B) ||
-      (final_bf16 && !aligned16(final_bf16)))
-    return PL_OK;
+  if (!g_ns_chain || ngroups < 1 || ngroups > kChainMaxGroups || iters > kChainMaxIters || iters < 1) return PL_OK;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   PL_CUDA(cudaStreamIsCapturing(st, &cap));
   if (cap != cudaStreamCaptureStatusNone) return PL_OK;  // a cooperative launch is not captured here
-
   using S = GemmSmem<kChainBN, EPI_BF16>;
-  NsChainMaps mp;
-  memset(&mp, 0, sizeof(mp));
-  __nv_bfloat16* xb[3] = {xbuf[0], xbuf[1], X};
-  const long gbs = (long)w.ldg * m;
-  for (int b = 0; b < 3; b++) {
-    Operand op{xb[b], m, n, ldx, batch, xbs};
-    int rc = gemm_operand_map(&mp.xk[b], op, 128);
-    if (rc) return rc;
-    rc = gemm_operand_map(&mp.xk256[b], op, 256);
-    if (rc) return rc;
-    rc = gemm_operand_map(&mp.xn[b], op, 64);
-    if (rc) return rc;
-    if (b < 2 && !gemm_store_map(&mp.xs[b], xb[b], m, n, ldx, batch, xbs)) return PL_OK;
-  }
-  mp.xs[2] = mp.xs[0];
-  if (final_bf16 && !gemm_store_map(&mp.xs[2], final_bf16, m, n, ldx, batch, xbs)) return PL_OK;
-  Operand og{w.G, m, m, w.ldg, batch, gbs}, opm{w.B, m, m, w.ldg, batch, gbs};
-  int rc = gemm_operand_map(&mp.gk, og, 128);
-  if (rc) return rc;
-  rc = gemm_operand_map(&mp.gk256, og, 256);
-  if (rc) return rc;
-  rc = gemm_operand_map(&mp.pk, opm, 128);
-  if (rc) return rc;
-  if (!gemm_store_map(&mp.gs, w.G, m, m, w.ldg, batch, gbs) || !gemm_store_map(&mp.ps, w.B, m, m, w.ldg, batch, gbs))
-    return PL_OK;
-
+  NsChainMapSet mset;
   NsChainArgs a{};
-  a.m = m;
-  a.n = n;
-  a.batch = batch;
+  a.ngroups = ngroups;
   a.iters = iters;
-  a.final_kind = out_f32 ? 2 : (final_bf16 ? 1 : 0);
-  a.scale0 = scale0;
-  a.G = w.G;
-  a.ldg = w.ldg;
-  a.gbs = gbs;
-  a.out_f32 = out_f32;
-  a.ld_out = ld_out;
-  a.obs = obs;
-  a.cnt = w.cnt;
-  a.err = w.err ? w.err : device_error_word();
+  for (int k = 0; k < ngroups; k++) {
+    const int rc = chain_group(hs[k], iters, mset.g[k], a.g[k]);
+    if (rc == 1) return PL_OK;
+    if (rc) return rc;
+    a.pjobs[0] += (long)a.g[k].batch * a.g[k].TG;
+    a.pjobs[1] += (long)a.g[k].batch * a.g[k].TG;
+    a.pjobs[2] += (long)a.g[k].batch * a.g[k].TX;
+  }
+  a.step_jobs = a.pjobs[0] + a.pjobs[1] + a.pjobs[2];
+  a.abort_word = abort_word;
+  a.err = err ? err : device_error_word();
   for (int i = 0; i < 3 * iters; i++) a.coef[i] = (float)coeffs[i];
 
   static int num_sms[64] = {0};
-  static bool configured[64] = {false};
   int dev = 0;
   PL_CUDA(cudaGetDevice(&dev));
   PL_REQUIRE(dev >= 0 && dev < 64, PL_ERR_UNSUPPORTED, "device index %d out of range", dev);
-  if (!configured[dev]) {
-    PL_CUDA(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev));
+  if (!num_sms[dev]) {
     PL_CUDA(cudaFuncSetAttribute((const void*)ns_chain_kernel<kChainBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)S::TOTAL));
-    configured[dev] = true;
+    PL_CUDA(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev));
   }
-  const long nM = ceil_div(m, 128), TG = nM * ceil_div(m, kChainBN), TX = nM * ceil_div(n, kChainBN);
-  const long total = (long)iters * batch * (2 * TG + TX);
+  const long total = (long)iters * a.step_jobs;
   const int grid = (int)(total < num_sms[dev] ? total : num_sms[dev]);
-
-  PL_CUDA(cudaMemsetAsync(w.cnt, 0, sizeof(unsigned) * (size_t)ns_chain_counter_words(batch), st));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
   cfg.blockDim = dim3(320, 1, 1);
@@ -441,11 +465,40 @@ int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWor
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  PL_CUDA(cudaLaunchKernelEx(&cfg, ns_chain_kernel<kChainBN>, mp, a));
+  PL_CUDA(cudaLaunchKernelEx(&cfg, ns_chain_kernel<kChainBN>, mset, a));
   count_launch();
   PL_LAUNCH("ns_chain_kernel");
   *used = true;
-  if (result) *result = out_f32 ? nullptr : (final_bf16 ? final_bf16 : xb[iters & 1]);
+  return PL_OK;
+}
+
+int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
+                 long xbs, __nv_bfloat16* const xbuf[2], float* out_f32, long ld_out, long obs,
+                 __nv_bfloat16* final_bf16, const float* scale0, cudaStream_t st, __nv_bfloat16** result, bool* used) {
+  *used = false;
+  if (!w.cnt || m <= 128) return PL_OK;
+  NsChainGroupHost h{};
+  h.m = m;
+  h.n = n;
+  h.batch = batch;
+  h.X = X;
+  h.xbuf[0] = xbuf[0];
+  h.xbuf[1] = xbuf[1];
+  h.ldx = ldx;
+  h.xbs = xbs;
+  h.G = w.G;
+  h.B = w.B;
+  h.ldg = w.ldg;
+  h.out_f32 = out_f32;
+  h.ld_out = ld_out;
+  h.obs = obs;
+  h.final_bf16 = final_bf16;
+  h.scale0 = scale0;
+  h.cnt = w.cnt;
+  PL_CUDA(cudaMemsetAsync(w.cnt, 0, sizeof(unsigned) * (size_t)ns_chain_counter_words(batch), st));
+  const int rc = ns_chain_launch(1, &h, coeffs, iters, w.cnt + 3L * batch, w.err, st, used);
+  if (rc || !*used) return rc;
+  if (result) *result = out_f32 ? nullptr : (final_bf16 ? final_bf16 : xbuf[iters & 1]);
   return PL_OK;
 }
 
