@@ -233,6 +233,9 @@ __device__ __forceinline__ float sigm(float x) {
 // step do not depend on the state, so they are loaded kScanU steps at a time ahead of the
 // recurrence: the loads of a group are all in flight together and only the arithmetic is serial.
 constexpr int kScanU = 4;
+// The reverse scan holds more live values per step; two steps ahead keep it at 4 blocks of 256 per
+// SM (<= 64 registers), so its 512-block grids (512 segments x 512 columns) finish in one wave.
+constexpr int kScanUB = 2;
 template <typename S, int K, int VEC, bool FAST>
 __global__ void __launch_bounds__(256) mg_scan_fwd_kernel(const S* __restrict__ Y, const S* __restrict__ hin,
                                                           S* __restrict__ hout, S* __restrict__ Os,
@@ -296,7 +299,7 @@ __global__ void __launch_bounds__(256) mg_scan_fwd_kernel(const S* __restrict__ 
 // dhn [R x H] = the highway part of the gradient reaching the layer input (K = 3). Loads run kScanU
 // steps ahead of the reverse recurrence, as in the forward scan.
 template <typename S, int K, int VEC, bool FAST>
-__global__ void __launch_bounds__(256) mg_scan_bwd_kernel(const S* __restrict__ Y, const S* __restrict__ Os,
+__global__ void __launch_bounds__(256, 4) mg_scan_bwd_kernel(const S* __restrict__ Y, const S* __restrict__ Os,
                                                           const S* __restrict__ hin, const S* __restrict__ dh,
                                                           S* __restrict__ dY, S* __restrict__ dhn,
                                                           const float* __restrict__ term, int B, int H, int T) {
@@ -317,12 +320,12 @@ __global__ void __launch_bounds__(256) mg_scan_bwd_kernel(const S* __restrict__ 
   float dOnext[VEC];
 #pragma unroll
   for (int v = 0; v < VEC; v++) dOnext[v] = 0.f;
-  for (int t1 = T - 1; t1 >= 0; t1 -= kScanU) {
-    float hid[kScanU][VEC], gate[kScanU][VEC], proj[kScanU][VEC], hi[kScanU][VEC], o[kScanU][VEC],
-        prev[kScanU][VEC], dhv[kScanU][VEC];
-    bool flow[kScanU];
+  for (int t1 = T - 1; t1 >= 0; t1 -= kScanUB) {
+    float hid[kScanUB][VEC], gate[kScanUB][VEC], proj[kScanUB][VEC], hi[kScanUB][VEC], o[kScanUB][VEC],
+        prev[kScanUB][VEC], dhv[kScanUB][VEC];
+    bool flow[kScanUB];
 #pragma unroll
-    for (int u = 0; u < kScanU; u++) {
+    for (int u = 0; u < kScanUB; u++) {
       const int t = t1 - u;
       if (t >= 0) {
         flow[u] = t > 0 && pt[-(long)(u + 1) * B] == 0.f;  // no state (and no gradient) across a terminal
@@ -342,7 +345,7 @@ __global__ void __launch_bounds__(256) mg_scan_bwd_kernel(const S* __restrict__ 
       }
     }
 #pragma unroll
-    for (int u = 0; u < kScanU; u++) {
+    for (int u = 0; u < kScanUB; u++) {
       const int t = t1 - u;
       if (t >= 0) {
         float dyh[VEC], dyg[VEC], dyp[VEC], dhw[VEC];
@@ -379,13 +382,13 @@ __global__ void __launch_bounds__(256) mg_scan_bwd_kernel(const S* __restrict__ 
         }
       }
     }
-    py -= kScanU * sY;
-    pdy -= kScanU * sY;
-    po -= kScanU * sH;
-    ph -= kScanU * sH;
-    pd -= kScanU * sH;
-    if (pdn) pdn -= kScanU * sH;
-    pt -= (long)kScanU * B;
+    py -= kScanUB * sY;
+    pdy -= kScanUB * sY;
+    po -= kScanUB * sH;
+    ph -= kScanUB * sH;
+    pd -= kScanUB * sH;
+    if (pdn) pdn -= kScanUB * sH;
+    pt -= (long)kScanUB * B;
   }
 }
 
