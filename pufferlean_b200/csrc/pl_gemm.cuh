@@ -309,6 +309,103 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
       olp = ep.olp[row];
       if (ep.ov) vold = ep.ov[row];
     }
+    if constexpr (BN >= 80) {
+      if (A + 1 <= 80) {
+        // ---- fast path for heads of up to 79 actions + the value: the row's logits and value in
+        // registers after one wait for five TMEM loads, two passes (max, then exp sum and the
+        // probability-weighted logit sum), the gradient from the registers; padding columns get zeros
+        uint32_t r5[5][16];
+#pragma unroll
+        for (int q = 0; q < 5; q++) tc::tmem_ld16(t_row + 16 * q, r5[q]);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 5; q++) tc::tmem_tie16(r5[q]);
+        float x[80];
+#pragma unroll
+        for (int k = 0; k < 80; k++)
+          x[k] = (have_acc ? __uint_as_float(r5[k >> 4][k & 15]) : 0.f) + (k <= A ? __ldg(ep.bias + k) : 0.f);
+        float mx = -INFINITY, xa = 0.f, vnew = 0.f;
+#pragma unroll
+        for (int k = 0; k < 80; k++) {
+          if (k < A) mx = fmaxf(mx, x[k]);
+          if (k == a) xa = x[k];
+          if (k == A) vnew = x[k];
+        }
+        float se = 0.f, sx = 0.f;
+#pragma unroll
+        for (int k = 0; k < 80; k++) {
+          if (k < A) {
+            const float e = __expf(x[k] - mx);
+            se += e;
+            sx += e * x[k];
+          }
+        }
+        const float lse = mx + logf(se), pout = sx / se;
+        const float logpA = xa - lse;
+        const float ratio = expf(logpA - olp);
+        const float lo = 1.f - ep.clip, hi = 1.f + ep.clip;
+        const float ratioC = ratio < lo ? lo : (ratio > hi ? hi : ratio);
+        const float surr1 = adv * ratio, surr2 = adv * ratioC;
+        const float dPol = surr1 <= surr2 ? adv * ratio : adv * ((lo < ratio && ratio < hi) ? 1.f : 0.f) * ratio;
+        float dv = vnew - ret;
+        if (ep.ov && ep.vfclip > 0.f) {
+          const float dd = vnew - vold;
+          const float vc = vold + (dd < -ep.vfclip ? -ep.vfclip : (dd > ep.vfclip ? ep.vfclip : dd));
+          const float du = (vnew - ret) * (vnew - ret), cc = (vc - ret) * (vc - ret);
+          if (!(du >= cc) && !(dd > -ep.vfclip && dd < ep.vfclip)) dv = 0.f;
+        }
+        const float dval = -ep.vf * dv;
+        if (row_ok) {
+          if (ep.newlp) ep.newlp[row] = logpA;
+          if (ep.newval) ep.newval[row] = vnew;
+        }
+        if (ep.loss_part) {
+          const float ent_row = lse - pout;
+          float lt[6] = {row_ok ? -fminf(surr1, surr2) : 0.f, row_ok ? 0.5f * (vnew - ret) * (vnew - ret) : 0.f,
+                         row_ok ? ent_row : 0.f, row_ok ? (ratio - 1.f) - logf(ratio) : 0.f,
+                         row_ok ? -logf(ratio) : 0.f, row_ok ? (fabsf(ratio - 1.f) > ep.clip ? 1.f : 0.f) : 0.f};
+#pragma unroll
+          for (int q = 0; q < 6; q++) {
+            float v = lt[q];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) rowscr[sub * 8 + q] = v;
+          }
+        }
+        __nv_bfloat16* outp = (__nv_bfloat16*)ep.out + (long)row * ep.ldo;
+        const bool vec = (ep.ldo % 8) == 0;
+#pragma unroll
+        for (int q = 0; q < 5; q++) {
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            const int k = 16 * q + j;
+            const float pk = __expf(x[k] - lse);
+            const float d = k < A ? dPol * ((k == a ? 1.f : 0.f) - pk) + ep.ent * pk * (pout - x[k]) : (k == A ? dval : 0.f);
+            v[j] = row_ok ? d : 0.f;
+          }
+          if (row_ok && 16 * q < ep.ldo) store_row16_bf16(outp + 16 * q, v, min(16, (int)(ep.ldo - 16 * q)), vec);
+          const float cs = warp_colsum16(v, lane);
+          if ((lane & 1) == 0) red[sub * BN + 16 * q + (lane >> 1)] = cs;
+        }
+        if (row_ok) {
+          float z[16];
+#pragma unroll
+          for (int j = 0; j < 16; j++) z[j] = 0.f;
+          for (int c0 = 80; c0 < BN && c0 < ep.ldo; c0 += 16) store_row16_bf16(outp + c0, z, min(16, (int)(ep.ldo - c0)), vec);
+        }
+        tc::named_bar_sync(1, 256);
+        const int t = threadIdx.x - 64;
+        for (int c = t; c < BN; c += 128) {
+          if (c < ep.out_cols)
+            ep.colsum[(long)m_tile * ep.ld_colsum + c] = ((red[c] + red[BN + c]) + red[2 * BN + c]) + red[3 * BN + c];
+        }
+        if (ep.loss_part && t < 6)
+          ep.loss_part[(long)m_tile * 8 + t] = ((rowscr[t] + rowscr[8 + t]) + rowscr[16 + t]) + rowscr[24 + t];
+        tc::named_bar_sync(1, 256);  // scratch is reused by the next tile
+        return;
+      }
+    }
     float mx = -INFINITY, se = 0.f, xa = 0.f, vnew = 0.f;
     for (int c0 = 0; c0 < BN; c0 += 16) {
       uint32_t r[16];

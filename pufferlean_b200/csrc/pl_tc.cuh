@@ -128,6 +128,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Marks the 16 registers of an x16 load as produced here (after a tcgen05.wait::ld), so that their
+// uses cannot be scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_tie16(uint32_t (&a)[16]) {
+  asm volatile(""
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]),
+                 "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15])
+               :
+               : "memory");
+}
 // The same wait, with the 32 registers of two x16 loads passed through it: their uses then depend on
 // the wait, so the compiler cannot schedule them ahead of it (later loads may be in flight meanwhile).
 __device__ __forceinline__ void tmem_wait_ld_tie(uint32_t (&a)[16], uint32_t (&b)[16]) {

@@ -215,10 +215,11 @@ def test_gemm_forward_and_dgrad_epilogues(act):
     assert _rel(cs.sum(0), dz.sum(0)) < 1e-4
 
 
-def test_gemm_ppo_head_epilogue():
-    torch.manual_seed(3)
-    M, H, A = 333, 128, 5
-    Op = 64
+@pytest.mark.parametrize("A,Op", [(5, 64), (64, 128), (79, 128), (100, 128)])
+def test_gemm_ppo_head_epilogue(A, Op):
+    """A + 1 <= 80 with a 128-wide tile takes the register-resident epilogue, the others the general one."""
+    torch.manual_seed(3 + A)
+    M, H = 333, 128
     Hid = _bf(torch.randn(M, H, device="cuda"))
     Wo = torch.zeros(Op, H, device="cuda")
     Wo[:A + 1] = torch.randn(A + 1, H, device="cuda") / math.sqrt(H)
@@ -235,7 +236,7 @@ def test_gemm_ppo_head_epilogue():
     cs = torch.zeros(mt, Op, device="cuda")
     nlp = torch.empty(M, device="cuda")
     nv = torch.empty(M, device="cuda")
-    G.gemm(Hid, Wo, M, A + 1, H, False, False, 64, G.EPI_PPO, out=dOut, ldo=Op, out_cols=A + 1, bias=bias,
+    G.gemm(Hid, Wo, M, A + 1, H, False, False, Op, G.EPI_PPO, out=dOut, ldo=Op, out_cols=A + 1, bias=bias,
            colsum=cs, ld_colsum=Op, act_idx=act, adv=adv, ret=ret, olp=olp, ov=ov, A=A, vf=0.5, ent=0.01, clip=0.2,
            vfclip=0.2, newlp=nlp, newval=nv)
     torch.cuda.synchronize()
