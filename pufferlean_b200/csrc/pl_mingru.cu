@@ -543,15 +543,27 @@ __global__ void mg_ppo_rows_md_kernel(const float* __restrict__ Out, int ldo, co
 }
 
 // ---------------------------------------------------------------- reductions, elementwise
-// part[chunk][c] = sum of rows [chunk*rows_per, ...) of column c (sequential, coalesced across c)
+// part[chunk][c] = sum of rows [chunk*rows_per, ...) of column c.
+// Column sums of one chunk of rows: a 32 x 8 block, thread (x, y) sums column 32 blockIdx.x + x over
+// the chunk's rows y, y + 8, ..., and row 0 adds the 8 partials in order (deterministic). Eight threads
+// per column keep narrow sums (the head's A + 1 columns) from running one thread per column.
 template <typename S>
-__global__ void mg_colsum_part_kernel(const S* __restrict__ M, long R, long ld, int N, int rows_per, float* part) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= N) return;
+__global__ void __launch_bounds__(256) mg_colsum_part_kernel(const S* __restrict__ M, long R, long ld, int N,
+                                                             int rows_per, float* part) {
+  __shared__ float sh[8][33];
+  const int c = blockIdx.x * 32 + threadIdx.x;
   const long r0 = (long)blockIdx.y * rows_per, r1 = min(R, r0 + (long)rows_per);
   float s = 0.f;
-  for (long r = r0; r < r1; r++) s += ldv(M, r * ld + c);
-  part[(long)blockIdx.y * N + c] = s;
+  if (c < N)
+    for (long r = r0 + threadIdx.y; r < r1; r += 8) s += ldv(M, r * ld + c);
+  sh[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) t += sh[k][threadIdx.x];
+    part[(long)blockIdx.y * N + c] = t;
+  }
 }
 __global__ void mg_colsum_final_kernel(const float* __restrict__ part, int chunks, int N, float* out) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1108,8 +1120,8 @@ int colsum(pl_mg* s, const S* M, long R, long ld, int N, float* out, cudaStream_
   const int rows_per = 256;
   const int chunks = (int)((R + rows_per - 1) / rows_per);
   PL_REQUIRE((long)chunks * N <= w.colpart_elems, PL_ERR_INVALID, "MinGRU colsum scratch too small");
-  dim3 g1((unsigned)((N + 127) / 128), (unsigned)chunks);
-  mg_colsum_part_kernel<S><<<g1, 128, 0, st>>>(M, R, ld, N, rows_per, w.colpart);
+  dim3 g1((unsigned)((N + 31) / 32), (unsigned)chunks);
+  mg_colsum_part_kernel<S><<<g1, dim3(32, 8), 0, st>>>(M, R, ld, N, rows_per, w.colpart);
   mg_colsum_final_kernel<<<(unsigned)((N + 127) / 128), 128, 0, st>>>(w.colpart, chunks, N, out);
   count_launch(2);
   PL_LAUNCH("mg_colsum_kernel");
