@@ -565,12 +565,17 @@ __global__ void __launch_bounds__(256) mg_colsum_part_kernel(const S* __restrict
     part[(long)blockIdx.y * N + c] = t;
   }
 }
-__global__ void mg_colsum_final_kernel(const float* __restrict__ part, int chunks, int N, float* out) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= N) return;
+// out[c] = sum over chunks of part[chunk][c]: one warp per column, lane l takes chunks l, l + 32, ...,
+// then a fixed shuffle tree (deterministic).
+__global__ void __launch_bounds__(256) mg_colsum_final_kernel(const float* __restrict__ part, int chunks, int N,
+                                                              float* out) {
+  const int c = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (c >= N) return;  // warp-uniform
   float s = 0.f;
-  for (int k = 0; k < chunks; k++) s += part[(long)k * N + c];
-  out[c] = s;
+  for (int k = lane; k < chunks; k += 32) s += part[(long)k * N + c];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) out[c] = s;
 }
 // dE = dh * enc'(Z) in place
 template <typename S>
@@ -1122,7 +1127,7 @@ int colsum(pl_mg* s, const S* M, long R, long ld, int N, float* out, cudaStream_
   PL_REQUIRE((long)chunks * N <= w.colpart_elems, PL_ERR_INVALID, "MinGRU colsum scratch too small");
   dim3 g1((unsigned)((N + 31) / 32), (unsigned)chunks);
   mg_colsum_part_kernel<S><<<g1, dim3(32, 8), 0, st>>>(M, R, ld, N, rows_per, w.colpart);
-  mg_colsum_final_kernel<<<(unsigned)((N + 127) / 128), 128, 0, st>>>(w.colpart, chunks, N, out);
+  mg_colsum_final_kernel<<<(unsigned)((N + 7) / 8), 256, 0, st>>>(w.colpart, chunks, N, out);
   count_launch(2);
   PL_LAUNCH("mg_colsum_kernel");
   return PL_OK;
