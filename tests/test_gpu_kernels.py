@@ -58,7 +58,7 @@ def _rollout(B, T, seed, done_p=0.05):
     return rew, val, term, imp, boot
 
 
-@pytest.mark.parametrize("B,T", [(1, 1), (3, 2), (64, 64), (257, 33), (100, 256)])
+@pytest.mark.parametrize("B,T", [(1, 1), (3, 2), (64, 64), (257, 33), (100, 256), (8192, 64), (45, 17)])
 def test_vtrace_f64_dev_bit_exact_vs_oracle(B, T):
     rew, val, term, imp, boot = _rollout(B, T, B * 1000 + T)
     for mingru in (False, True):
