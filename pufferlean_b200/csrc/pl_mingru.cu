@@ -771,11 +771,15 @@ __global__ void __launch_bounds__(256) mg_small_muon_kernel(const SmallMats sm, 
   __syncthreads();
   for (int it = 0; it < sm.iters; it++) {
     const float a = sm.co[it][0], bb = sm.co[it][1], cf = sm.co[it][2];
-    for (int e = tid; e < m * m; e += 256) {
-      const int i = e / m, k = e - i * m;
+    // G = X X^T: one warp per entry (lanes take every 32nd column, then a fixed shuffle tree), so
+    // the long side is not one thread's dependent chain
+    for (int e = tid >> 5; e < m * m; e += 8) {
+      const int i = e / m, k = e - i * m, ln = tid & 31;
       float acc = 0.f;
-      for (int l = 0; l < n; l++) acc += X[i * n + l] * X[k * n + l];
-      G[e] = acc;
+      for (int l = ln; l < n; l += 32) acc += X[i * n + l] * X[k * n + l];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (ln == 0) G[e] = acc;
     }
     __syncthreads();
     for (int e = tid; e < m * m; e += 256) {
