@@ -11,7 +11,9 @@
 // in registers, Wh sits in shared memory with a padded row stride (H + 1, so the forward's row reads
 // and the reverse's column reads both hit distinct banks), and a terminal at step t zeroes the state
 // before step t + 1 and stops the gradient there. Tiers: 0 = f64 arithmetic throughout, 1 = f32; tier 2
-// (the reference's bf16 tier) currently runs the f32 computation.
+// (the reference's bf16 tier) is the f32 computation with every product's operands rounded to bf16 before
+// the multiply-add and f32 accumulation, as cuBLAS's CUBLAS_COMPUTE_32F_FAST_16BF does for the
+// reference's GEMMs; the gate, cell and head arithmetic stays f32.
 #include <mutex>
 
 #include "../../include/pufferlean_b200.h"
@@ -34,9 +36,16 @@ __device__ __forceinline__ R lsig(R x) {
   return R(1) / (R(1) + lexp(-x));
 }
 
+// An operand of a product: as is, or (RB, the bf16 tier) rounded to bf16 to nearest even.
+template <bool RB, typename R>
+__device__ __forceinline__ R lop(R x) {
+  if constexpr (RB) return (R)__bfloat162float(__float2bfloat16_rn((float)x));
+  return x;
+}
+
 // C[z][m, n] = sum_{k in slice z} A[m*ars + k*acs] * B[n*brs + k*bcs], k ascending; 64 x 64 tiles,
 // 16-deep k steps through shared memory, 4 x 4 outputs per thread. gridDim.z slices of kc rows of K.
-template <typename R>
+template <typename R, bool RB>
 __global__ void __launch_bounds__(256) lstm_gemm_kernel(int M, int N, int K, int kc, const R* __restrict__ A,
                                                         long ars, long acs, const R* __restrict__ B, long brs,
                                                         long bcs, R* C, long ldc, long zs) {
@@ -54,8 +63,8 @@ __global__ void __launch_bounds__(256) lstm_gemm_kernel(int M, int N, int K, int
     for (int e = threadIdx.x; e < 16 * 64; e += 256) {
       const int kk = e / 64, mm = e - kk * 64;
       const int k = kb + kk;
-      sA[kk][mm] = (k < k1 && m0 + mm < M) ? A[(long)(m0 + mm) * ars + (long)k * acs] : R(0);
-      sB[kk][mm] = (k < k1 && n0 + mm < N) ? B[(long)(n0 + mm) * brs + (long)k * bcs] : R(0);
+      sA[kk][mm] = (k < k1 && m0 + mm < M) ? lop<RB>(A[(long)(m0 + mm) * ars + (long)k * acs]) : R(0);
+      sB[kk][mm] = (k < k1 && n0 + mm < N) ? lop<RB>(B[(long)(n0 + mm) * brs + (long)k * bcs]) : R(0);
     }
     __syncthreads();
 #pragma unroll
@@ -113,7 +122,7 @@ __global__ void lstm_act_kernel(const double* __restrict__ s, long n, int A, int
 
 // Forward recurrence. Gin [R x 4H] = X Wx^T (no bias); per step g = (bih + Gin) + h_prev Wh^T. WS: Wh
 // staged in shared memory (it fits up to H ~ 64 in f32); otherwise it is read through L1 / L2.
-template <typename R, bool WS>
+template <typename R, bool WS, bool RB>
 __global__ void lstm_fwd_kernel(const R* __restrict__ Gin, const R* __restrict__ Wh, const R* __restrict__ bih,
                                 const double* __restrict__ term, const R* __restrict__ h0,
                                 const R* __restrict__ c0, R* II, R* FF, R* GG, R* OO, R* TC, R* HT, R* HP, R* CP,
@@ -128,7 +137,7 @@ __global__ void lstm_fwd_kernel(const R* __restrict__ Gin, const R* __restrict__
   if (WS)
     for (int i = tid; i < H4 * H; i += blockDim.x) {
       const int m = i / H, k = i - m * H;
-      sWh[(long)m * SW + k] = Wh[i];
+      sWh[(long)m * SW + k] = lop<RB>(Wh[i]);
     }
   const R* Wm = WS ? sWh : Wh;
   const int ws = WS ? SW : H;
@@ -150,11 +159,18 @@ __global__ void lstm_fwd_kernel(const R* __restrict__ Gin, const R* __restrict__
       const R* w2 = Wm + (long)(2 * H + j) * ws;
       const R* w3 = Wm + (long)(3 * H + j) * ws;
       for (int k = 0; k < H; k++) {
-        const R hv = hr[k];
-        a0 += w0[k] * hv;
-        a1 += w1[k] * hv;
-        a2 += w2[k] * hv;
-        a3 += w3[k] * hv;
+        const R hv = lop<RB>(hr[k]);
+        if (WS) {  // staged already rounded
+          a0 += w0[k] * hv;
+          a1 += w1[k] * hv;
+          a2 += w2[k] * hv;
+          a3 += w3[k] * hv;
+        } else {
+          a0 += lop<RB>(w0[k]) * hv;
+          a1 += lop<RB>(w1[k]) * hv;
+          a2 += lop<RB>(w2[k]) * hv;
+          a3 += lop<RB>(w3[k]) * hv;
+        }
       }
       hold = hr[j];
     }
@@ -181,7 +197,7 @@ __global__ void lstm_fwd_kernel(const R* __restrict__ Gin, const R* __restrict__
 }
 
 // Reverse recurrence. dHo [R x H] = dOut Wo (the head's share of dh); writes dG [R x 4H].
-template <typename R, bool WS>
+template <typename R, bool WS, bool RB>
 __global__ void lstm_bwd_kernel(const R* __restrict__ II, const R* __restrict__ FF, const R* __restrict__ GG,
                                 const R* __restrict__ OO, const R* __restrict__ TC, const R* __restrict__ CP,
                                 const R* __restrict__ dHo, const R* __restrict__ Wh, const double* __restrict__ term,
@@ -196,7 +212,7 @@ __global__ void lstm_bwd_kernel(const R* __restrict__ II, const R* __restrict__ 
   if (WS)
     for (int i = tid; i < H4 * H; i += blockDim.x) {
       const int m = i / H, k = i - m * H;
-      sWh[(long)m * SW + k] = Wh[i];
+      sWh[(long)m * SW + k] = lop<RB>(Wh[i]);
     }
   const R* Wm = WS ? sWh : Wh;
   const int ws = WS ? SW : H;
@@ -218,17 +234,20 @@ __global__ void lstm_bwd_kernel(const R* __restrict__ II, const R* __restrict__ 
       dgr[H + j] = q1;
       dgr[2 * H + j] = q2;
       dgr[3 * H + j] = q3;
-      R* s = sdg + r * H4;
-      s[j] = q0;
-      s[H + j] = q1;
-      s[2 * H + j] = q2;
-      s[3 * H + j] = q3;
+      R* s = sdg + r * H4;  // the product's operand copy (rounded in the bf16 tier)
+      s[j] = lop<RB>(q0);
+      s[H + j] = lop<RB>(q1);
+      s[2 * H + j] = lop<RB>(q2);
+      s[3 * H + j] = lop<RB>(q3);
     }
     __syncthreads();
     R dhp = R(0);
     if (ok) {
       const R* s = sdg + r * H4;
-      for (int k = 0; k < H4; k++) dhp += s[k] * Wm[(long)k * ws + j];
+      if (WS)
+        for (int k = 0; k < H4; k++) dhp += s[k] * Wm[(long)k * ws + j];
+      else
+        for (int k = 0; k < H4; k++) dhp += s[k] * lop<RB>(Wm[(long)k * ws + j]);
       const bool flow = t > 0 && term[(long)(t - 1) * B + b] == 0.0;
       dhn = flow ? dhp : R(0);
       dcn = flow ? dcp : R(0);
@@ -283,10 +302,13 @@ inline unsigned nblk(long n) {
 // into the f64 output when out64 is given, else written (nz = 1) to C.
 template <typename R>
 int lstm_gemm(int M, int N, int K, const R* A, long ars, long acs, const R* B, long brs, long bcs, R* C, long ldc,
-              int nz, cudaStream_t st) {
+              int nz, cudaStream_t st, bool rb = false) {
   const int kc = (int)ceil_div(ceil_div(K, nz), 16) * 16;
   dim3 grid((unsigned)ceil_div(N, 64), (unsigned)ceil_div(M, 64), (unsigned)nz);
-  lstm_gemm_kernel<R><<<grid, 256, 0, st>>>(M, N, K, kc, A, ars, acs, B, brs, bcs, C, ldc, (long)M * ldc);
+  if (rb)
+    lstm_gemm_kernel<R, true><<<grid, 256, 0, st>>>(M, N, K, kc, A, ars, acs, B, brs, bcs, C, ldc, (long)M * ldc);
+  else
+    lstm_gemm_kernel<R, false><<<grid, 256, 0, st>>>(M, N, K, kc, A, ars, acs, B, brs, bcs, C, ldc, (long)M * ldc);
   count_launch();
   PL_LAUNCH("lstm_gemm_kernel");
   return PL_OK;
@@ -366,7 +388,7 @@ int lstm_grad(const double* params, const double* obs, const double* acts, const
   R* CP = HP + NR * H;
   // ---- products over all rows that do not depend on the recurrence, and the recurrence itself
   auto fwd_products = [&]() -> int {
-    return lstm_gemm<R>((int)NR, (int)H4, (int)D, X, D, 1, Wx, D, 1, Gin, H4, 1, st);  // Gin = X Wx^T
+    return lstm_gemm<R>((int)NR, (int)H4, (int)D, X, D, 1, Wx, D, 1, Gin, H4, 1, st, tc);  // Gin = X Wx^T
   };
   rc = fwd_products();
   if (rc) return rc;
@@ -377,8 +399,10 @@ int lstm_grad(const double* params, const double* obs, const double* acts, const
   const bool WS = wsm + sizeof(R) * (size_t)rows * H4 <= 200 * 1024;
   const size_t smem_f = (WS ? wsm : 0) + sizeof(R) * (size_t)rows * H;
   const size_t smem_b = (WS ? wsm : 0) + sizeof(R) * (size_t)rows * H4;
-  auto kf = WS ? lstm_fwd_kernel<R, true> : lstm_fwd_kernel<R, false>;
-  auto kb = WS ? lstm_bwd_kernel<R, true> : lstm_bwd_kernel<R, false>;
+  auto kf = WS ? (tc ? lstm_fwd_kernel<R, true, true> : lstm_fwd_kernel<R, true, false>)
+                : (tc ? lstm_fwd_kernel<R, false, true> : lstm_fwd_kernel<R, false, false>);
+  auto kb = WS ? (tc ? lstm_bwd_kernel<R, true, true> : lstm_bwd_kernel<R, true, false>)
+                : (tc ? lstm_bwd_kernel<R, false, true> : lstm_bwd_kernel<R, false, false>);
   static std::mutex mu;
   {
     std::lock_guard<std::mutex> lk(mu);
@@ -391,13 +415,13 @@ int lstm_grad(const double* params, const double* obs, const double* acts, const
   count_launch();
   PL_LAUNCH("lstm_fwd_kernel");
   // head: Out = HT Wo^T; row gradient; dHo = dOut Wo
-  rc = lstm_gemm<R>((int)NR, (int)O, (int)H, HT, H, 1, Wo, H, 1, Out, O, 1, st);
+  rc = lstm_gemm<R>((int)NR, (int)O, (int)H, HT, H, 1, Wo, H, 1, Out, O, 1, st, tc);
   if (rc) return rc;
   lstm_head_kernel<R><<<nblk(NR), 256, 0, st>>>(Out, bo, NR, (int)A, act, col, col + NR, col + 2 * NR, (R)vf, (R)ent,
                                                 (R)clip, dOut, lpv, lpv + NR);
   count_launch();
   PL_LAUNCH("lstm_head_kernel");
-  rc = lstm_gemm<R>((int)NR, (int)H, (int)O, dOut, O, 1, Wo, 1, H, dHo, H, 1, st);
+  rc = lstm_gemm<R>((int)NR, (int)H, (int)O, dOut, O, 1, Wo, 1, H, dHo, H, 1, st, tc);
   if (rc) return rc;
   kb<<<nb, rows * (int)H, smem_b, st>>>(II, FF, GG, OO, TC, CP, dHo, Wh, term, dG, (int)B, (int)T, (int)H, rows);
   count_launch();
@@ -409,7 +433,7 @@ int lstm_grad(const double* params, const double* obs, const double* acts, const
   double* gWo = gbih + H4;
   double* gbo = gWo + O * H;
   auto wgrad = [&](int M, int N, const R* Am, long acs_, const R* Bm, long bcs_, double* dst) -> int {
-    int r2 = lstm_gemm<R>(M, N, (int)NR, Am, 1, acs_, Bm, 1, bcs_, part, N, NZ, st);
+    int r2 = lstm_gemm<R>(M, N, (int)NR, Am, 1, acs_, Bm, 1, bcs_, part, N, NZ, st, tc);
     if (r2) return r2;
     lstm_slice_sum_kernel<R><<<nblk((long)M * N), 256, 0, st>>>(part, NZ, (long)M * N, dst);
     count_launch();
@@ -435,7 +459,7 @@ int lstm_grad(const double* params, const double* obs, const double* acts, const
   if (newlp) PL_CUDA(cudaMemcpyAsync(newlp, lpv, sizeof(double) * NR, cudaMemcpyDeviceToHost, st));
   if (newval) PL_CUDA(cudaMemcpyAsync(newval, lpv + NR, sizeof(double) * NR, cudaMemcpyDeviceToHost, st));
   PL_CUDA(cudaStreamSynchronize(st));
-  (void)tc;
+
   return device_error_check();
 }
 
