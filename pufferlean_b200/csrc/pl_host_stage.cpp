@@ -110,6 +110,34 @@ __attribute__((target_clones("avx512f", "avx2", "default"))) void rows_to_bf16(c
   }
 }
 
+// Rows k in [k0, k1) of the order: src row order[k] (an f64 row index, as the reference's shuffles are
+// stored) -> dst row k - k0. An entry that is not an integer in [0, nrows) leaves a zero row and sets
+// *bad. The next row's first lines are prefetched while this one is rounded (rows are visited in the
+// shuffle's random order).
+__attribute__((target_clones("avx512f", "avx2", "default"))) void rows_to_bf16_order(
+    const double* src, const double* order, long nrows, long k0, long k1, int D, int Dp, uint16_t* dst, int* bad) {
+  for (long k = k0; k < k1; k++) {
+    const double f = order[k];
+    const long r = (long)f;
+    uint16_t* o = dst + (k - k0) * Dp;
+    if (!(f >= 0.0 && f < (double)nrows) || (double)r != f) {
+      for (int c = 0; c < Dp; c++) o[c] = 0;
+      *bad = 1;
+      continue;
+    }
+    if (k + 1 < k1) {
+      const double fn = order[k + 1];
+      if (fn >= 0.0 && fn < (double)nrows) {
+        const char* nx = (const char*)(src + (long)fn * D);
+        for (int b = 0; b < 4 && b * 64 < D * 8; b++) __builtin_prefetch(nx + b * 64);
+      }
+    }
+    const double* s = src + r * D;
+    for (int c = 0; c < D; c++) o[c] = bf16_bits((float)s[c]);
+    for (int c = D; c < Dp; c++) o[c] = 0;
+  }
+}
+
 }  // namespace
 
 int host_threads() { return pool().size(); }
@@ -185,6 +213,31 @@ int upload_rows_bf16(HostStage& hs, const double* obs, long NT, int D, int Dp, v
   }
   if (dev_rows && dnext < NT && dev_rows(dnext, NT - dnext) != 0) return -1;
   return 0;
+}
+
+int upload_rows_bf16_order(HostStage& hs, const double* obs, const double* order, long nrows, long k0, long k1, int D,
+                           int Dp, void* dst_dev, cudaStream_t st) {
+  const size_t row_bytes = (size_t)Dp * 2;
+  const long rows = std::max<long>(1, (long)(hs.cap / row_bytes));
+  uint16_t* dst = (uint16_t*)dst_dev;
+  Pool& P = pool();
+  int bad = 0;
+  int k = hs.next;
+  for (long r0 = k0; r0 < k1; r0 += rows, k ^= 1) {
+    const long nr = std::min(rows, k1 - r0);
+    if (hs.used[k] && cudaEventSynchronize(hs.done[k]) != cudaSuccess) return -1;  // its last copy has left
+    uint16_t* b = (uint16_t*)hs.buf[k];
+    P.run([&](int t, int T) {
+      int tb = 0;
+      rows_to_bf16_order(obs, order, nrows, r0 + nr * t / T, r0 + nr * (t + 1) / T, D, Dp, b + (nr * t / T) * Dp, &tb);
+      if (tb) __atomic_store_n(&bad, 1, __ATOMIC_RELAXED);
+    });
+    if (cudaMemcpyAsync(dst + r0 * Dp, b, (size_t)nr * row_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) return -1;
+    if (cudaEventRecord(hs.done[k], st) != cudaSuccess) return -1;
+    hs.used[k] = true;
+  }
+  hs.next = k;
+  return bad ? -2 : 0;
 }
 
 }  // namespace pl

@@ -91,10 +91,13 @@ int launch_obs_to_f32_f64(const double* src, long n, float* dst, cudaStream_t st
 int launch_columns(const double* act, const double* ret, const double* olp, const double* ov, long NT, int* act_i,
                    float* ret_f, float* olp_f, float* ov_f, cudaStream_t st);
 int launch_perm(const double* perm, long n, int* out, cudaStream_t st);
+// For observations stored in the first epoch's order: pos = inverse of perm[0, NT) (scratch, NT ints)
+// and out[i] = pos[perm[i]] for i < n, each row id translated into its first-epoch position.
+int launch_perm_positions(const int* perm, long NT, long n, int* pos, int* out, cudaStream_t st);
 int launch_gather(bool bf16, const int* idx, int Nmb, const void* obs, int rowElems, void* X, const int* act_c,
                   const double* adv_c, const float* ret_c, const float* olp_c, const float* ov_c, int* mb_act,
                   float* mb_adv, float* mb_ret, float* mb_olp, float* mb_ov, double* part, double* ms,
-                  cudaStream_t st, double* sums = nullptr);
+                  cudaStream_t st, double* sums = nullptr, const int* oidx = nullptr);
 int launch_adv_ms_from_sums(const double* sums, double* ms, cudaStream_t st);
 // Column sums of `tiles` rows of ld floats in `part`; part must have colsum_scratch_elems(tiles, ld)
 // floats (the second reduction level lives after the partials).

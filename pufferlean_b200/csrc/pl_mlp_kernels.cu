@@ -59,17 +59,35 @@ __global__ void perm_kernel(const double* __restrict__ perm, long n, int* out) {
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
     out[i] = (int)perm[i];
 }
+// pos[perm[k]] = k over the first NT entries (the first epoch's order); entries outside [0, NT) are
+// skipped, so pos (zeroed before) stays in range.
+__global__ void perm_inverse_kernel(const int* __restrict__ perm, long NT, int* pos) {
+  for (long k = (long)blockIdx.x * blockDim.x + threadIdx.x; k < NT; k += (long)gridDim.x * blockDim.x) {
+    const int p = perm[k];
+    if (p >= 0 && p < NT) pos[p] = (int)k;
+  }
+}
+// out[i] = pos[perm[i]]: row ids of later epochs' orders translated into first-epoch positions.
+__global__ void perm_compose_kernel(const int* __restrict__ perm, const int* __restrict__ pos, long NT, long n,
+                                    int* out) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const int p = perm[i];
+    out[i] = (p >= 0 && p < NT) ? pos[p] : 0;
+  }
+}
 
 // ---------------------------------------------------------------- gather + advantage statistics
-// Row k of the minibatch = column row idx[k]. One warp per row for the obs copy (16-byte vectors);
-// scalars by lane 0. Each block folds sum(adv), sum(adv^2) of its rows into part[blockIdx.x].
+// Row k of the minibatch = column row idx[k]; its observation row is oidx[k] when the observations
+// are stored in another order (oidx null: idx[k]; obs null: no observation copy). One warp per row for
+// the obs copy (16-byte vectors); scalars by lane 0. Each block folds sum(adv), sum(adv^2) of its rows
+// into part[blockIdx.x].
 template <bool BF16>
 __global__ void __launch_bounds__(256) gather_kernel(const int* __restrict__ idx, int Nmb, const void* __restrict__ obs,
                                                      int rowElems, void* X, const int* __restrict__ act_c,
                                                      const double* __restrict__ adv_c, const float* __restrict__ ret_c,
                                                      const float* __restrict__ olp_c, const float* __restrict__ ov_c,
                                                      int* mb_act, float* mb_adv, float* mb_ret, float* mb_olp,
-                                                     float* mb_ov, double* part) {
+                                                     float* mb_ov, double* part, const int* __restrict__ oidx) {
   __shared__ double sh[256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows_per_block = (Nmb + gridDim.x - 1) / gridDim.x;
@@ -80,13 +98,16 @@ __global__ void __launch_bounds__(256) gather_kernel(const int* __restrict__ idx
     const int vec_elems = BF16 ? 8 : 4;  // 16 bytes
     // 16-byte vectors only when every row starts 16-byte aligned (always for the padded bf16 rows)
     const int nvec = (rowElems % vec_elems == 0) ? rowElems / vec_elems : 0;
-    const uint4* s = reinterpret_cast<const uint4*>((const char*)obs + src * rowElems * (BF16 ? 2 : 4));
-    uint4* d = reinterpret_cast<uint4*>((char*)X + (long)k * rowElems * (BF16 ? 2 : 4));
-    for (int v = lane; v < nvec; v += 32) d[v] = s[v];
-    if (!BF16) {
-      const float* sf = (const float*)obs + src * rowElems;
-      float* df = (float*)X + (long)k * rowElems;
-      for (int c = nvec * 4 + lane; c < rowElems; c += 32) df[c] = sf[c];
+    if (obs) {
+      const long orow = oidx ? (long)oidx[k] : src;
+      const uint4* s = reinterpret_cast<const uint4*>((const char*)obs + orow * rowElems * (BF16 ? 2 : 4));
+      uint4* d = reinterpret_cast<uint4*>((char*)X + (long)k * rowElems * (BF16 ? 2 : 4));
+      for (int v = lane; v < nvec; v += 32) d[v] = s[v];
+      if (!BF16) {
+        const float* sf = (const float*)obs + orow * rowElems;
+        float* df = (float*)X + (long)k * rowElems;
+        for (int c = nvec * 4 + lane; c < rowElems; c += 32) df[c] = sf[c];
+      }
     }
     if (lane == 0) {
       const double a = adv_c[src];
@@ -583,6 +604,14 @@ int launch_columns(const double* act, const double* ret, const double* olp, cons
   PL_LAUNCH("columns_kernel");
   return PL_OK;
 }
+int launch_perm_positions(const int* perm, long NT, long n, int* pos, int* out, cudaStream_t st) {
+  PL_CUDA(cudaMemsetAsync(pos, 0, sizeof(int) * NT, st));
+  perm_inverse_kernel<<<grid_for(NT), 256, 0, st>>>(perm, NT, pos);
+  perm_compose_kernel<<<grid_for(n), 256, 0, st>>>(perm, pos, NT, n, out);
+  count_launch(2);
+  PL_LAUNCH("perm_compose_kernel");
+  return PL_OK;
+}
 int launch_perm(const double* perm, long n, int* out, cudaStream_t st) {
   perm_kernel<<<grid_for(n), 256, 0, st>>>(perm, n, out);
   count_launch();
@@ -598,14 +627,14 @@ int launch_adv_ms_from_sums(const double* sums, double* ms, cudaStream_t st) {
 int launch_gather(bool bf16, const int* idx, int Nmb, const void* obs, int rowElems, void* X, const int* act_c,
                   const double* adv_c, const float* ret_c, const float* olp_c, const float* ov_c, int* mb_act,
                   float* mb_adv, float* mb_ret, float* mb_olp, float* mb_ov, double* part, double* ms,
-                  cudaStream_t st, double* sums) {
+                  cudaStream_t st, double* sums, const int* oidx) {
   const int nb = (int)(Nmb < kRedBlocks * 8 ? (Nmb + 7) / 8 : kRedBlocks);
   if (bf16)
     gather_kernel<true><<<nb, 256, 0, st>>>(idx, Nmb, obs, rowElems, X, act_c, adv_c, ret_c, olp_c, ov_c, mb_act,
-                                            mb_adv, mb_ret, mb_olp, mb_ov, part);
+                                            mb_adv, mb_ret, mb_olp, mb_ov, part, oidx);
   else
     gather_kernel<false><<<nb, 256, 0, st>>>(idx, Nmb, obs, rowElems, X, act_c, adv_c, ret_c, olp_c, ov_c, mb_act,
-                                             mb_adv, mb_ret, mb_olp, mb_ov, part);
+                                             mb_adv, mb_ret, mb_olp, mb_ov, part, oidx);
   if (sums)
     adv_sums_kernel<<<1, 32, 0, st>>>(part, nb, Nmb, sums);
   else

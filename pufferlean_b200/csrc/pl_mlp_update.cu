@@ -97,6 +97,16 @@ struct pl_update {
   bool loss_on = false;
   double losses[7] = {0, 0, 0, 0, 0, 0, 0};
   HostStage hstage;  // pinned staging of host observations rounded to bf16 on the host
+  // Observations kept in the first epoch's shuffle order (reference-shaped call, bf16 tier): the host
+  // rounds and copies the rows of each first-epoch minibatch on a copy stream just ahead of it, so the
+  // upload runs under the compute; later epochs read rows through perm translated into those positions.
+  const double* pend_obs = nullptr;   // host rows not yet uploaded (until the first epoch has run)
+  const double* pend_perm = nullptr;  // the host shuffle whose first epoch orders them
+  bool obs_epoch0 = false;            // obs holds rows in the first epoch's order
+  int* pos0 = nullptr;                // NT ints, scratch of the translation
+  int* operm = nullptr;               // epochs x NT first-epoch positions
+  cudaStream_t cst = nullptr;
+  cudaEvent_t cev = nullptr, sev = nullptr;
   // wide action heads (pl_update_set_head): 0 categorical, 1 multi-discrete, 2 Gaussian
   int head_mode = 0;
   int W = 1;
@@ -441,7 +451,10 @@ static int muon_sharded(pl_update* u, double lr, cudaStream_t st) {
   return PL_OK;
 }
 
-static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool last, cudaStream_t st) {
+// oidx: observation rows when obs is not in column order; xdirect: the minibatch's rows already
+// contiguous in obs (no observation gather).
+static int minibatch_fast(pl_update* u, const int* idx, const int* oidx, const void* xdirect, int Nmb, double lr,
+                          bool last, cudaStream_t st) {
   const pl_update_desc& d = u->d;
   const int L = u->L;
   const int act = d.arch.act;
@@ -449,15 +462,17 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
   int rc;
   {
     Span sp(u, 5, st, 0);
-    rc = launch_gather(true, idx, Nmb, u->obs, u->Dp, u->X, u->act_c, u->adv_c, u->ret_c, u->olp_c, u->ov_c, u->mb_act,
-                       u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st, u->dp ? u->adv_sums : nullptr);
+    rc = launch_gather(true, idx, Nmb, xdirect ? nullptr : u->obs, u->Dp, u->X, u->act_c, u->adv_c, u->ret_c, u->olp_c,
+                       u->ov_c, u->mb_act, u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st,
+                       u->dp ? u->adv_sums : nullptr, oidx);
     // data parallel: the normalisation statistics are those of the whole (all-rank) minibatch
     if (!rc && u->dp) rc = comm_allreduce_f64(d.comm, u->adv_sums, 3, st);
     if (!rc && u->dp) rc = launch_adv_ms_from_sums(u->adv_sums, u->ms, st);
   }
   if (rc) return rc;
   // ---- forward
-  const void* hin = u->X;
+  const void* xin = xdirect ? xdirect : u->X;
+  const void* hin = xin;
   long ldin = u->Dp;
   for (int l = 0; l < L; l++) {
     const Layer& ly = u->layers[l];
@@ -551,7 +566,7 @@ static int minibatch_fast(pl_update* u, const int* idx, int Nmb, double lr, bool
   int dsel = 0;
   for (int l = L; l >= 0; l--) {
     const Layer& ly = u->layers[l];
-    const void* hprev = l == 0 ? u->X : u->Hs[l - 1];
+    const void* hprev = l == 0 ? xin : u->Hs[l - 1];
     const long ldprev = l == 0 ? u->Dp : u->Hp;
     {
       Span sp(u, 3, st, gf(ly.out, ly.in, Nmb));
@@ -823,6 +838,9 @@ int pl_update_destroy(pl_update* u) {
   if (!u) return PL_OK;
   cudaDeviceSynchronize();
   for (cudaEvent_t e : u->ev) cudaEventDestroy(e);
+  if (u->cev) cudaEventDestroy(u->cev);
+  if (u->sev) cudaEventDestroy(u->sev);
+  if (u->cst) cudaStreamDestroy(u->cst);
   u->hstage.release();
   free_all(u);
   delete u;
@@ -884,9 +902,15 @@ int pl_update_set_head(pl_update* u, int mode, size_t W, const double* head_size
   return PL_OK;
 }
 
-int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, const double* adv, const double* ret,
-                          const double* olp, const double* oldVal, const double* perm, void* stream) {
+}  // extern "C"
+
+// defer: the observation rows are left on the host for pl_update_run to upload in the first epoch's
+// order (the caller runs the update before touching them again).
+static int set_columns(pl_update* u, const double* obs, const double* acts, const double* adv, const double* ret,
+                       const double* olp, const double* oldVal, const double* perm, void* stream, bool defer) {
   PL_REQUIRE(u && obs && acts && adv && ret && olp && perm, PL_ERR_INVALID, "pl_update_set_columns: NULL column");
+  u->pend_obs = u->pend_perm = nullptr;
+  u->obs_epoch0 = false;
   PL_REQUIRE(!u->d.use_old_values || oldVal, PL_ERR_INVALID, "value clip needs the old-value column");
   cudaStream_t st = (cudaStream_t)stream;
   const pl_update_desc& d = u->d;
@@ -898,7 +922,21 @@ int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, c
   bool host_done = false;
   uint64_t bytes = 0;
   long dev_rows_n = 0;
-  if (u->fast && g_host_bf16 && (size_t)NT * d.D >= ((size_t)1 << 20) && u->hstage.init((size_t)16 << 20) == 0) {
+  if (defer && u->fast && g_host_bf16 && d.D >= 64 && d.epochs > 0 && (size_t)NT * d.D >= ((size_t)1 << 20) &&
+      u->hstage.init((size_t)16 << 20) == 0) {
+    if (!u->operm) {
+      u->pos0 = dalloc<int>(u, (size_t)NT);
+      u->operm = dalloc<int>(u, (size_t)d.epochs * NT);
+      if (!u->pos0 || !u->operm) return PL_ERR_NOMEM;
+    }
+    u->pend_obs = obs;
+    u->pend_perm = perm;
+    u->obs_epoch0 = true;
+    bytes += (uint64_t)NT * u->Dp * 2;
+    host_done = true;
+  }
+  if (!host_done && u->fast && g_host_bf16 && (size_t)NT * d.D >= ((size_t)1 << 20) &&
+      u->hstage.init((size_t)16 << 20) == 0) {
     // from pinned memory a share of the rows also goes as f64 through the device staging buffer
     cudaPointerAttributes at{};
     const bool pinned = cudaPointerGetAttributes(&at, obs) == cudaSuccess && at.type == cudaMemoryTypeHost;
@@ -963,9 +1001,18 @@ int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, c
   }
   bytes += (uint64_t)d.epochs * d.NT * sizeof(double);
   g_upload_bytes.store(bytes);
-  return staged(u, perm, d.epochs * d.NT, st, [&](double* sp, size_t c, size_t off) {
+  int rc = staged(u, perm, d.epochs * d.NT, st, [&](double* sp, size_t c, size_t off) {
     return launch_perm(sp, (long)c, u->perm + off, st);
   });
+  if (!rc && u->obs_epoch0) rc = launch_perm_positions(u->perm, NT, (long)(d.epochs * NT), u->pos0, u->operm, st);
+  return rc;
+}
+
+extern "C" {
+
+int pl_update_set_columns(pl_update* u, const double* obs, const double* acts, const double* adv, const double* ret,
+                          const double* olp, const double* oldVal, const double* perm, void* stream) {
+  return set_columns(u, obs, acts, adv, ret, olp, oldVal, perm, stream, false);
 }
 
 int pl_update_set_columns_dev(pl_update* u, const float* obs, const double* acts, const double* adv,
@@ -973,6 +1020,8 @@ int pl_update_set_columns_dev(pl_update* u, const float* obs, const double* acts
                               void* stream) {
   // adv / ret / oldVal may be NULL when pl_update_set_advantages_dev provides them
   PL_REQUIRE(u && obs && acts && olp && perm, PL_ERR_INVALID, "pl_update_set_columns_dev: NULL column");
+  u->pend_obs = u->pend_perm = nullptr;
+  u->obs_epoch0 = false;
   cudaStream_t st = (cudaStream_t)stream;
   const pl_update_desc& d = u->d;
   const long NT = (long)d.NT;
@@ -1055,6 +1104,20 @@ int pl_update_run(pl_update* u, double lr, void* stream) {
   const uint64_t l0 = pl_kernel_launch_count();
   u->loss_on = g_loss_on;
   int lastNmb = 0;
+  // pending host observations: each first-epoch minibatch's rows are rounded and copied on the copy
+  // stream just before its kernels are queued, and the compute stream waits for exactly those rows
+  const bool upl = u->pend_obs != nullptr;
+  struct Done {
+    pl_update* u;
+    ~Done() { u->pend_obs = u->pend_perm = nullptr; }
+  } done{u};
+  if (upl) {
+    if (!u->cst) PL_CUDA(cudaStreamCreateWithFlags(&u->cst, cudaStreamNonBlocking));
+    if (!u->cev) PL_CUDA(cudaEventCreateWithFlags(&u->cev, cudaEventDisableTiming));
+    if (!u->sev) PL_CUDA(cudaEventCreateWithFlags(&u->sev, cudaEventDisableTiming));
+    PL_CUDA(cudaEventRecord(u->sev, st));  // earlier work on obs is done before it is overwritten
+    PL_CUDA(cudaStreamWaitEvent(u->cst, u->sev, 0));
+  }
   for (size_t e = 0; e < d.epochs; e++)
     for (size_t m = 0; m < d.numMB; m++) {
       const long lo = (long)m * u->mbSize;
@@ -1064,7 +1127,24 @@ int pl_update_run(pl_update* u, double lr, void* stream) {
       const int Nmb = (int)(hi - lo);
       const int* idx = u->perm + e * d.NT + lo;
       const bool last = (e + 1 == d.epochs) && (m + 1 == d.numMB);
-      int rc = u->fast ? minibatch_fast(u, idx, Nmb, lr, last, st) : minibatch_tight(u, idx, Nmb, lr, last, st);
+      if (upl && e == 0) {
+        const int r = upload_rows_bf16_order(u->hstage, u->pend_obs, u->pend_perm, (long)d.NT, lo, hi, (int)d.D, u->Dp,
+                                             u->obs, u->cst);
+        PL_REQUIRE(r != -2, PL_ERR_INVALID, "shuffle entry is not a row index in [0, %zu)", d.NT);
+        if (r) return check_cuda(cudaGetLastError(), "host bf16 observation upload");
+        PL_CUDA(cudaEventRecord(u->cev, u->cst));
+        PL_CUDA(cudaStreamWaitEvent(st, u->cev, 0));
+      }
+      const int* oidx = nullptr;
+      const void* xdirect = nullptr;
+      if (u->obs_epoch0) {
+        if (e == 0)
+          xdirect = (const __nv_bfloat16*)u->obs + lo * u->Dp;
+        else
+          oidx = u->operm + e * d.NT + lo;
+      }
+      int rc = u->fast ? minibatch_fast(u, idx, oidx, xdirect, Nmb, lr, last, st)
+                       : minibatch_tight(u, idx, Nmb, lr, last, st);
       if (rc) return rc;
       lastNmb = Nmb;
     }
@@ -1191,7 +1271,7 @@ static int resident_update(size_t handle, const pl_mlp_arch* arch, const double*
   if (rc) return rc;
   rc = refresh_shadows(u, 0);
   if (rc) return rc;
-  rc = pl_update_set_columns(u, obs, acts, adv, ret, olp, d.use_old_values ? oldVal : nullptr, perm, nullptr);
+  rc = set_columns(u, obs, acts, adv, ret, olp, d.use_old_values ? oldVal : nullptr, perm, nullptr, true);
   if (rc) return rc;
   rc = pl_update_run(u, lr, nullptr);
   if (rc) return rc;

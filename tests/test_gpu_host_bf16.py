@@ -2,8 +2,10 @@
 f32 -> bf16 to nearest even) and copied as bf16, a quarter of the f64 bytes: the device copy and the
 whole update are bit-identical to copying the f64 rows and converting them on the device, including
 rounding ties, subnormals, signed zeros, infinities after the f32 step and values beyond the bf16
-range, for row widths with and without padding, from pageable and from pinned memory (where a share of
-the rows goes as f64 and is converted on the device)."""
+range, for row widths with and without padding, from pageable and from pinned memory. Rows of 64 or
+more values are uploaded by the reference-shaped call in the first epoch's shuffle order, one
+minibatch's rows ahead of its kernels, and later epochs read them through the translated shuffle;
+narrower pinned rows are split between the host rounding and f64 copies converted on the device."""
 import ctypes as C
 
 import numpy as np
@@ -41,12 +43,14 @@ def _edge_values(n, rng):
     return out
 
 
-@pytest.mark.parametrize("D,pinned", [(64, False), (20, False), (64, True), (72, True)])
-def test_host_rounding_bit_identical(D, pinned):
-    """Pageable rows are all rounded on the host; pinned rows are split between the host rounding and
-    f64 copies converted on the device."""
+@pytest.mark.parametrize("D,pinned,MB", [(64, False, 4), (20, False, 4), (64, True, 4), (72, True, 3),
+                                         (20, True, 4), (128, False, 1)])
+def test_host_rounding_bit_identical(D, pinned, MB):
+    """Against f64 copies converted on the device in column order: rows of >= 64 values go in the first
+    epoch's order, minibatch by minibatch (3 minibatches: a ragged last one); narrower pinned rows are
+    split between the host rounding and device conversion."""
     from tests.test_gpu_update import _problem, _run_resident
-    NT, H, A, L, E, MB = 16384, 128, 5, 1, 2, 4
+    NT, H, A, L, E = (65536 if D < 64 else 16384), 128, 5, 1, 2
     P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, A, L, 61 + D, 1)
     rng = np.random.default_rng(D)
     obs = obs.copy()
@@ -70,6 +74,19 @@ def test_host_rounding_bit_identical(D, pinned):
     assert np.isfinite(host).all()
     assert np.array_equal(host, dev)
     assert not np.array_equal(host[:P], pm[:P])
+
+
+def test_invalid_shuffle_entry_is_an_error():
+    """A first-epoch shuffle entry outside [0, NT) (or not an integer) fails the call with an error
+    instead of reading outside the host rows."""
+    from tests.test_gpu_update import _problem, _run_resident
+    NT, D, H, A, L, E, MB = 16384, 64, 128, 5, 1, 2, 4
+    P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, A, L, 5, 1)
+    for bad in (float(NT), -1.0, 2.5):
+        perm = O.shuffle_perm(NT, E, 3).copy()
+        perm[NT // 2 + 7] = bad
+        with pytest.raises(AssertionError, match="shuffle entry"):
+            _run_resident(pm, P, (L, 1), obs, acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, 0.02, 0.2, 0.5, 1)
 
 
 def test_host_rounding_matches_device_conversion_elementwise():
