@@ -353,8 +353,7 @@ def run_e2e(args, wl, state, rank, world, local_rank):
         # API fed from the same pinned host columns
         vp = C.c_void_p
         L.pl_update_create.argtypes = [C.c_size_t, C.POINTER(Desc), C.POINTER(vp)]
-        L.pl_update_set_columns.argtypes = [vp] * 9
-        L.pl_update_run.argtypes = [vp, C.c_double, vp]
+        L.pl_update_run_columns.argtypes = [vp] * 8 + [C.c_double, vp]
         L.pl_update_destroy.argtypes = [vp]
         sess = vp()
         check(L.pl_update_create(state["handle"], C.byref(state["desc"]), C.byref(sess)), L)
@@ -362,10 +361,9 @@ def run_e2e(args, wl, state, rank, world, local_rank):
         def step(i):  # noqa: F811
             check(L.pl_gae_soa(P_(cols["val"]), P_(cols["rew"]), P_(cols["term"]), N, T, 0.995, 0.90, P_(gae)), L)
             check(L.pl_shuffle_perm(NT, E, 0xE2E + 1000 * rank + i, P_(perm)), L)
-            check(L.pl_update_set_columns(sess, obs_h.data_ptr(), cols["acts"].data_ptr(), gae.data_ptr(),
+            check(L.pl_update_run_columns(sess, obs_h.data_ptr(), cols["acts"].data_ptr(), gae.data_ptr(),
                                           gae.data_ptr() + 8 * NT, cols["olp"].data_ptr(), cols["val"].data_ptr(),
-                                          perm.data_ptr(), None), L)
-            check(L.pl_update_run(sess, wl["lr"], None), L)
+                                          perm.data_ptr(), wl["lr"], None), L)
             cudart_memcpy_d2h(out0, state["handle"])  # synchronizes, then reads params[0]
     step(0)
     if world > 1:
@@ -389,7 +387,7 @@ def run_e2e(args, wl, state, rank, world, local_rank):
             "d2h_bytes_per_step": 8 if world == 1 else 16,
             "steps": k, "s_per_step": dt,
             "path": ("pl_train_update_resident_deep (the reference-facing C-ABI call)" if world == 1 else
-                     "pl_update_set_columns + pl_update_run on a data-parallel session (the C-ABI's DP form)") +
+                     "pl_update_run_columns on a data-parallel session (the C-ABI's DP form)") +
                     ", pinned host f64 columns, host GAE + shuffle in the timed region"}
 
 

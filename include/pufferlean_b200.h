@@ -211,6 +211,14 @@ int pl_update_set_advantages_dev(pl_update* u, const float* rew, const float* va
                                  void* stream);
 /* Runs every epoch x minibatch of one update at learning rate lr on `stream`. */
 int pl_update_run(pl_update* u, double lr, void* stream);
+/* pl_update_set_columns + pl_update_run in one call, with the upload of the reference-shaped update
+ * entries (ffi/puffercuda.cu:1187, lean_cuda_train_update_resident): in the bf16 tier, rows of 64 or
+ * more observations are read from the host during the call in the first epoch's shuffle order, one
+ * minibatch ahead of the kernels that use them, so the upload runs under the compute. The host columns
+ * must stay unchanged until the call returns; a first-epoch shuffle entry that is not a row index in
+ * [0, NT) fails the call. Results are identical to the two calls. */
+int pl_update_run_columns(pl_update* u, const double* obs, const double* acts, const double* adv, const double* ret,
+                          const double* olp, const double* oldVal, const double* perm, double lr, void* stream);
 /* Kernels launched by the last pl_update_run (this library's own kernels). */
 uint64_t pl_update_last_launches(const pl_update* u);
 /* Host-to-device bytes the last pl_update_set_columns call (of any session in the process; the

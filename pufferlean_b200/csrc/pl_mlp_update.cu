@@ -1154,6 +1154,13 @@ int pl_update_run(pl_update* u, double lr, void* stream) {
   return PL_OK;
 }
 
+extern "C" int pl_update_run_columns(pl_update* u, const double* obs, const double* acts, const double* adv,
+                                     const double* ret, const double* olp, const double* oldVal, const double* perm,
+                                     double lr, void* stream) {
+  int rc = set_columns(u, obs, acts, adv, ret, olp, oldVal, perm, stream, true);
+  return rc ? rc : pl_update_run(u, lr, stream);
+}
+
 // ---------------------------------------------------------------- policy handle
 int pl_policy_load(const double* pm, size_t P, size_t* handle) {
   int rc = require_device();

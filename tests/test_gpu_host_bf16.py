@@ -102,3 +102,47 @@ def test_host_rounding_matches_device_conversion_elementwise():
     assert L.pl_test_round_rows_bf16(x.ctypes.data_as(C.POINTER(C.c_double)), x.size // 64, 64, 64,
                                      out.ctypes.data_as(C.POINTER(C.c_uint16))) == 0
     assert np.array_equal(out.view(np.int16), want)
+
+
+def test_session_run_columns_equals_set_columns_and_run():
+    """pl_update_run_columns (rows uploaded in the first epoch's order during the run) against
+    pl_update_set_columns + pl_update_run on a session: bit-identical parameters, twice in a row on the
+    same session (the second call's upload waits for nothing stale)."""
+    from tests.test_gpu_dp import Arch, Desc
+    from tests.test_gpu_update import _problem
+    NT, D, H, A, L, E, MB = 16384, 96, 128, 5, 2, 2, 3
+    P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, A, L, 77, 1)
+    L_ = plb.lib()
+    vp = C.c_void_p
+    L_.pl_update_create.argtypes = [C.c_size_t, C.POINTER(Desc), C.POINTER(vp)]
+    L_.pl_update_set_columns.argtypes = [vp] * 9
+    L_.pl_update_run.argtypes = [vp, C.c_double, vp]
+    L_.pl_update_run_columns.argtypes = [vp] * 8 + [C.c_double, vp]
+    L_.pl_update_destroy.argtypes = [vp]
+    outs = []
+    for combined in (False, True):
+        h = plb.policy_load(pm, P)
+        d = Desc(NT=NT, D=D, H=H, A=A, epochs=E, numMB=MB, arch=Arch(L, 1, None, 0), wd=0.0, mu=0.95, eps=1e-7,
+                 vfCoef=0.5, entCoef=0.01, clipEps=0.2, vfClip=0.2, maxGradNorm=0.5, bf16=1, use_old_values=1,
+                 rank=0, world=1, comm=None)
+        u = vp()
+        assert L_.pl_update_create(h, C.byref(d), C.byref(u)) == 0, L_.pl_last_error()
+        try:
+            for i in range(2):
+                perm = np.ascontiguousarray(O.shuffle_perm(NT, E, 90 + i), dtype=np.float64)
+                cols = [np.ascontiguousarray(x, dtype=np.float64) for x in (obs, acts, adv, ret, olp, ov)]
+                ptrs = [x.ctypes.data for x in cols] + [perm.ctypes.data]
+                if combined:
+                    rc = L_.pl_update_run_columns(u, *ptrs, 0.02, None)
+                else:
+                    rc = L_.pl_update_set_columns(u, *ptrs, None)
+                    rc = rc or L_.pl_update_run(u, 0.02, None)
+                assert rc == 0, L_.pl_last_error()
+            torch.cuda.synchronize()
+        finally:
+            L_.pl_update_destroy(u)
+        outs.append(plb.policy_download(h, P))
+        plb.policy_free(h)
+    assert np.isfinite(outs[0]).all()
+    assert np.array_equal(outs[0], outs[1])
+    assert not np.array_equal(outs[0][:P], pm[:P])
