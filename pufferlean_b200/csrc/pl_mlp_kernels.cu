@@ -222,7 +222,28 @@ __global__ void __launch_bounds__(256) nesterov_kernel(const float* __restrict__
   __shared__ double sh[256];
   const double c = cc[0];
   double s = 0.0;
-  for (long i = (long)blockIdx.x * 256 + threadIdx.x; i < n; i += (long)gridDim.x * 256) {
+  const long S = (long)gridDim.x * 256;
+  long i = (long)blockIdx.x * 256 + threadIdx.x;
+  // four grid strides' loads in flight at once; the sum still takes them in stride order
+  for (; i + 3 * S < n; i += 4 * S) {
+    float gv[4];
+    double mv[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      gv[q] = g[i + q * S];
+      mv[q] = mom[i + q * S];
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const double gi = (double)gv[q] * c;
+      const double m = mu * mv[q] + gi;
+      mom[i + q * S] = m;
+      const double ui = gi + mu * m;
+      u[i + q * S] = ui;
+      s += ui * ui;
+    }
+  }
+  for (; i < n; i += S) {
     const double gi = (double)g[i] * c;
     const double m = mu * mom[i] + gi;
     mom[i] = m;
@@ -233,11 +254,16 @@ __global__ void __launch_bounds__(256) nesterov_kernel(const float* __restrict__
   s = block_sum_f64(s, sh);
   if (threadIdx.x == 0) part[blockIdx.x] = s;
 }
-// X = u / (||u||_F + eps) as bf16, stored wide: for rows > cols the matrix is transposed so that
-// X is min(rows,cols) x max(rows,cols) with the long side contiguous (ld = ldx).
-__global__ void ns_input_kernel(const double* __restrict__ u, const double* __restrict__ part, int nparts,
-                                int rows, int cols, double eps, __nv_bfloat16* X, long ldx) {
+// X = u / (||u||_F + eps) as bf16, stored wide: for rows > cols (TR) the matrix is transposed so
+// that X is min(rows,cols) x max(rows,cols) with the long side contiguous (ld = ldx). Blocks walk
+// rows (no per-element index division); the transposed form goes through 32 x 32 shared-memory tiles
+// so that both the reads of u and the writes of X are coalesced. 256 threads per block.
+template <bool TR>
+__global__ void __launch_bounds__(256) ns_input_kernel(const double* __restrict__ u, const double* __restrict__ part,
+                                                       int nparts, int rows, int cols, double eps, __nv_bfloat16* X,
+                                                       long ldx) {
   __shared__ double inv_s;
+  __shared__ __nv_bfloat16 tile[32][34];
   if (threadIdx.x == 0) {
     double s = 0.0;
     for (int b = 0; b < nparts; b++) s += part[b];
@@ -245,29 +271,65 @@ __global__ void ns_input_kernel(const double* __restrict__ u, const double* __re
   }
   __syncthreads();
   const double inv = inv_s;
-  const long n = (long)rows * cols;
-  const bool tr = rows > cols;
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const long r = i / cols, c = i - r * cols;
-    const __nv_bfloat16 v = __float2bfloat16_rn((float)(inv * u[i]));
-    if (tr)
-      X[c * ldx + r] = v;
-    else
-      X[r * ldx + c] = v;
+  if (!TR) {
+    for (int r = blockIdx.x; r < rows; r += gridDim.x)
+      for (int c = threadIdx.x; c < cols; c += blockDim.x)
+        X[(long)r * ldx + c] = __float2bfloat16_rn((float)(inv * u[(long)r * cols + c]));
+    return;
+  }
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int tcols = (cols + 31) >> 5, ntiles = ((rows + 31) >> 5) * tcols;
+  for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {  // block-uniform trip count
+    const int r0 = (t / tcols) * 32, c0 = (t % tcols) * 32;
+    for (int j = ty; j < 32; j += 8) {
+      const int r = r0 + j, c = c0 + tx;
+      if (r < rows && c < cols) tile[j][tx] = __float2bfloat16_rn((float)(inv * u[(long)r * cols + c]));
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += 8) {
+      const int c = c0 + j, r = r0 + tx;
+      if (r < rows && c < cols) X[(long)c * ldx + r] = tile[tx][j];
+    }
+    __syncthreads();
   }
 }
 // W <- c1*W + c2*X (f64 master, rows x cols row-major) and the bf16 shadow Wb (ldw), from the
-// fp32 Newton-Schulz result Xf (wide layout, ldx; transposed back when rows > cols).
-__global__ void ns_finalize_kernel(const float* __restrict__ Xf, long ldx, int rows, int cols, double c1, double c2,
-                                   double* W, __nv_bfloat16* Wb, long ldw) {
-  const long n = (long)rows * cols;
-  const bool tr = rows > cols;
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const long r = i / cols, c = i - r * cols;
-    const double x = (double)(tr ? Xf[c * ldx + r] : Xf[r * ldx + c]);
-    const double w = c1 * W[i] + c2 * x;
-    W[i] = w;
-    if (Wb) Wb[r * ldw + c] = __float2bfloat16_rn((float)w);
+// fp32 Newton-Schulz result Xf (wide layout, ldx; transposed back when rows > cols: TR, through
+// 32 x 32 shared-memory tiles). 256 threads per block.
+template <bool TR>
+__global__ void __launch_bounds__(256) ns_finalize_kernel(const float* __restrict__ Xf, long ldx, int rows, int cols,
+                                                          double c1, double c2, double* W, __nv_bfloat16* Wb,
+                                                          long ldw) {
+  if (!TR) {
+    for (int r = blockIdx.x; r < rows; r += gridDim.x)
+      for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        const long i = (long)r * cols + c;
+        const double w = c1 * W[i] + c2 * (double)Xf[(long)r * ldx + c];
+        W[i] = w;
+        if (Wb) Wb[(long)r * ldw + c] = __float2bfloat16_rn((float)w);
+      }
+    return;
+  }
+  __shared__ float tile[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int tcols = (cols + 31) >> 5, ntiles = ((rows + 31) >> 5) * tcols;
+  for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {  // block-uniform trip count
+    const int r0 = (t / tcols) * 32, c0 = (t % tcols) * 32;
+    for (int j = ty; j < 32; j += 8) {
+      const int c = c0 + j, r = r0 + tx;
+      if (r < rows && c < cols) tile[j][tx] = Xf[(long)c * ldx + r];
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += 8) {
+      const int r = r0 + j, c = c0 + tx;
+      if (r < rows && c < cols) {
+        const long i = (long)r * cols + c;
+        const double w = c1 * W[i] + c2 * (double)tile[tx][j];
+        W[i] = w;
+        if (Wb) Wb[(long)r * ldw + c] = __float2bfloat16_rn((float)w);
+      }
+    }
+    __syncthreads();
   }
 }
 // stepVec on a bias with the scaled gradient g*cc, plus its fp32 shadow.
@@ -285,11 +347,9 @@ __global__ void stepvec_fast_kernel(const float* __restrict__ g, const double* _
 }
 // f64 master weights -> bf16 shadow (padded, ld) / fp32 copies
 __global__ void w_to_bf16_kernel(const double* __restrict__ W, int rows, int cols, __nv_bfloat16* Wb, long ldw) {
-  const long n = (long)rows * cols;
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const long r = i / cols, c = i - r * cols;
-    Wb[r * ldw + c] = __float2bfloat16_rn((float)W[i]);
-  }
+  for (int r = blockIdx.x; r < rows; r += gridDim.x)
+    for (int c = threadIdx.x; c < cols; c += blockDim.x)
+      Wb[(long)r * ldw + c] = __float2bfloat16_rn((float)W[(long)r * cols + c]);
 }
 __global__ void f64_to_f32_kernel(const double* __restrict__ s, long n, float* d) {
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) d[i] = (float)s[i];
@@ -572,6 +632,8 @@ __global__ void colsum_f32_kernel(const float* __restrict__ Mx, long rows, int N
 }
 
 // ---------------------------------------------------------------- host launchers
+// One block per row (or tile) up to 148 x 16 blocks, at least one.
+static inline unsigned rowwise_grid(long units) { return (unsigned)std::max(1L, std::min(units, 148L * 16)); }
 static inline unsigned grid_for(long n, int block = 256, long cap = 148 * 16) {
   long g = (n + block - 1) / block;
   if (g < 1) g = 1;
@@ -685,14 +747,23 @@ int launch_nesterov(const float* g, const double* cc, double* mom, double* u, do
 }
 int launch_ns_input(const double* u, const double* part, int nparts, int rows, int cols, double eps,
                     __nv_bfloat16* X, long ldx, cudaStream_t st) {
-  ns_input_kernel<<<grid_for((long)rows * cols), 256, 0, st>>>(u, part, nparts, rows, cols, eps, X, ldx);
+  if (rows > cols)
+    ns_input_kernel<true><<<rowwise_grid(ceil_div(rows, 32) * ceil_div(cols, 32)), 256, 0, st>>>(u, part, nparts, rows,
+                                                                                               cols, eps, X, ldx);
+  else
+    ns_input_kernel<false><<<rowwise_grid(rows), 256, 0, st>>>(u, part, nparts, rows, cols, eps, X, ldx);
   count_launch();
   PL_LAUNCH("ns_input_kernel");
   return PL_OK;
 }
 int launch_ns_finalize(const float* Xf, long ldx, int rows, int cols, double c1, double c2, double* W,
                        __nv_bfloat16* Wb, long ldw, cudaStream_t st) {
-  ns_finalize_kernel<<<grid_for((long)rows * cols), 256, 0, st>>>(Xf, ldx, rows, cols, c1, c2, W, Wb, ldw);
+  if (rows > cols)
+    ns_finalize_kernel<true><<<rowwise_grid(ceil_div(rows, 32) * ceil_div(cols, 32)), 256, 0, st>>>(Xf, ldx, rows,
+                                                                                                   cols, c1, c2, W, Wb,
+                                                                                                   ldw);
+  else
+    ns_finalize_kernel<false><<<rowwise_grid(rows), 256, 0, st>>>(Xf, ldx, rows, cols, c1, c2, W, Wb, ldw);
   count_launch();
   PL_LAUNCH("ns_finalize_kernel");
   return PL_OK;
@@ -705,7 +776,7 @@ int launch_stepvec_fast(const float* g, const double* cc, double* b, double* m, 
   return PL_OK;
 }
 int launch_w_to_bf16(const double* W, int rows, int cols, __nv_bfloat16* Wb, long ldw, cudaStream_t st) {
-  w_to_bf16_kernel<<<grid_for((long)rows * cols), 256, 0, st>>>(W, rows, cols, Wb, ldw);
+  w_to_bf16_kernel<<<rowwise_grid(rows), 256, 0, st>>>(W, rows, cols, Wb, ldw);
   count_launch();
   PL_LAUNCH("w_to_bf16_kernel");
   return PL_OK;
