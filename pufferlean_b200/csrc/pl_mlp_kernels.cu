@@ -30,13 +30,34 @@ __device__ __forceinline__ double block_sum_f64(double v, double* sh) {
 // ---------------------------------------------------------------- columns
 // obs rows (f64 or f32, D wide) -> bf16 rows Dp wide, zero padded.
 template <typename T>
-__global__ void obs_to_bf16_kernel(const T* __restrict__ src, long NT, int D, int Dp, __nv_bfloat16* dst) {
-  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  long n = NT * Dp;
-  for (; i < n; i += (long)gridDim.x * blockDim.x) {
-    long r = i / Dp;
-    int c = (int)(i - r * Dp);
-    dst[i] = __float2bfloat16_rn(c < D ? (float)src[r * D + c] : 0.f);
+__global__ void __launch_bounds__(256) obs_to_bf16_kernel(const T* __restrict__ src, long NT, int D, int Dp,
+                                                          __nv_bfloat16* dst) {
+  // one warp per row; four values per lane and step (16- or 32-byte loads, an 8-byte store) when every
+  // row starts aligned, else one value per lane
+  const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+  const bool vec = (D % 4) == 0 && (Dp % 4) == 0 && ((uintptr_t)src & 15) == 0 && ((uintptr_t)dst & 7) == 0;
+  for (long r = (long)blockIdx.x * wpb + (threadIdx.x >> 5); r < NT; r += (long)gridDim.x * wpb) {
+    const T* s = src + r * D;
+    __nv_bfloat16* d = dst + r * Dp;
+    if (vec) {
+      for (int c = lane * 4; c < Dp; c += 128) {
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (c < D) {
+          if constexpr (sizeof(T) == 4) {
+            const float4 q = *reinterpret_cast<const float4*>(s + c);
+            v[0] = q.x, v[1] = q.y, v[2] = q.z, v[3] = q.w;
+          } else {
+            const double2 a = *reinterpret_cast<const double2*>(s + c);
+            const double2 b = *reinterpret_cast<const double2*>(s + c + 2);
+            v[0] = (float)a.x, v[1] = (float)a.y, v[2] = (float)b.x, v[3] = (float)b.y;
+          }
+        }
+        __nv_bfloat162 o[2] = {__floats2bfloat162_rn(v[0], v[1]), __floats2bfloat162_rn(v[2], v[3])};
+        *reinterpret_cast<uint2*>(d + c) = *reinterpret_cast<const uint2*>(o);
+      }
+    } else {
+      for (int c = lane; c < Dp; c += 32) d[c] = __float2bfloat16_rn(c < D ? (float)s[c] : 0.f);
+    }
   }
 }
 template <typename T>
@@ -642,13 +663,13 @@ static inline unsigned grid_for(long n, int block = 256, long cap = 148 * 16) {
 }
 
 int launch_obs_to_bf16_f64(const double* src, long NT, int D, int Dp, __nv_bfloat16* dst, cudaStream_t st) {
-  obs_to_bf16_kernel<double><<<grid_for(NT * Dp), 256, 0, st>>>(src, NT, D, Dp, dst);
+  obs_to_bf16_kernel<double><<<rowwise_grid(ceil_div(NT, 8)), 256, 0, st>>>(src, NT, D, Dp, dst);
   count_launch();
   PL_LAUNCH("obs_to_bf16_kernel");
   return PL_OK;
 }
 int launch_obs_to_bf16_f32(const float* src, long NT, int D, int Dp, __nv_bfloat16* dst, cudaStream_t st) {
-  obs_to_bf16_kernel<float><<<grid_for(NT * Dp), 256, 0, st>>>(src, NT, D, Dp, dst);
+  obs_to_bf16_kernel<float><<<rowwise_grid(ceil_div(NT, 8)), 256, 0, st>>>(src, NT, D, Dp, dst);
   count_launch();
   PL_LAUNCH("obs_to_bf16_kernel");
   return PL_OK;
