@@ -123,7 +123,15 @@ __global__ void __launch_bounds__(256) gather_kernel(const int* __restrict__ idx
       const long orow = oidx ? (long)oidx[k] : src;
       const uint4* s = reinterpret_cast<const uint4*>((const char*)obs + orow * rowElems * (BF16 ? 2 : 4));
       uint4* d = reinterpret_cast<uint4*>((char*)X + (long)k * rowElems * (BF16 ? 2 : 4));
-      for (int v = lane; v < nvec; v += 32) d[v] = s[v];
+      int v = lane;
+      for (; v + 96 < nvec; v += 128) {  // four vectors per lane in flight: the loads before the stores
+        const uint4 a0 = s[v], a1 = s[v + 32], a2 = s[v + 64], a3 = s[v + 96];
+        d[v] = a0;
+        d[v + 32] = a1;
+        d[v + 64] = a2;
+        d[v + 96] = a3;
+      }
+      for (; v < nvec; v += 32) d[v] = s[v];
       if (!BF16) {
         const float* sf = (const float*)obs + orow * rowElems;
         float* df = (float*)X + (long)k * rowElems;
