@@ -216,7 +216,23 @@ __global__ void colsum_final_kernel(const float* __restrict__ part2, int runs, l
 }
 // out[i] = sum_s part[s*n + i], s ascending (split-K slices)
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int S, long n, float* out) {
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+  // four adjacent outputs per thread and step (16-byte loads and store) where the slices allow it;
+  // every output still sums its slices in order z = 0, 1, ...
+  const long stride = (long)gridDim.x * blockDim.x, t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long n4 = ((n & 3) == 0 && ((uintptr_t)part & 15) == 0 && ((uintptr_t)out & 15) == 0) ? n / 4 : 0;
+  for (long i = t; i < n4; i += stride) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int z = 0; z < S; z++) {
+      const float4 p = reinterpret_cast<const float4*>(part + (long)z * n)[i];
+      s.x += p.x;
+      s.y += p.y;
+      s.z += p.z;
+      s.w += p.w;
+    }
+    reinterpret_cast<float4*>(out)[i] = s;
+  }
+  for (long i = n4 * 4 + t; i < n; i += stride) {
     float s = 0.f;
     for (int z = 0; z < S; z++) s += part[(long)z * n + i];
     out[i] = s;
