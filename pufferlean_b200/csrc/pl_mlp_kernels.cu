@@ -243,7 +243,17 @@ __global__ void __launch_bounds__(256) gradnorm_part_kernel(const float* __restr
                                                             double* part) {
   __shared__ double sh[256];
   double s = 0.0;
-  for (long i = (long)blockIdx.x * 256 + threadIdx.x; i < P; i += (long)gridDim.x * 256) {
+  const long S = (long)gridDim.x * 256;
+  long i = (long)blockIdx.x * 256 + threadIdx.x;
+  for (; i + 3 * S < P; i += 4 * S) {  // four strides' loads in flight, summed in stride order
+    const float a[4] = {g[i], g[i + S], g[i + 2 * S], g[i + 3 * S]};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const double x = (double)a[q] * sc;
+      s += x * x;
+    }
+  }
+  for (; i < P; i += S) {
     const double x = (double)g[i] * sc;
     s += x * x;
   }
@@ -317,9 +327,18 @@ __global__ void __launch_bounds__(256) ns_input_kernel(const double* __restrict_
   __syncthreads();
   const double inv = inv_s;
   if (!TR) {
-    for (int r = blockIdx.x; r < rows; r += gridDim.x)
-      for (int c = threadIdx.x; c < cols; c += blockDim.x)
-        X[(long)r * ldx + c] = __float2bfloat16_rn((float)(inv * u[(long)r * cols + c]));
+    const int B = blockDim.x;
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+      const double* ur = u + (long)r * cols;
+      __nv_bfloat16* xr = X + (long)r * ldx;
+      int c = threadIdx.x;
+      for (; c + 3 * B < cols; c += 4 * B) {  // four loads in flight per thread
+        const double a[4] = {ur[c], ur[c + B], ur[c + 2 * B], ur[c + 3 * B]};
+#pragma unroll
+        for (int q = 0; q < 4; q++) xr[c + q * B] = __float2bfloat16_rn((float)(inv * a[q]));
+      }
+      for (; c < cols; c += B) xr[c] = __float2bfloat16_rn((float)(inv * ur[c]));
+    }
     return;
   }
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
