@@ -96,13 +96,17 @@ int pl_ns_batched_bf16_dev(void* X, size_t batch, size_t rows, size_t cols, doub
                            size_t iters, void* stream);
 
 /* The same batched Newton-Schulz without allocating device memory, for callers that cannot call
- * cudaMalloc: code running while a CUDA graph is captured, hosts whose device memory belongs to
- * another allocator or a fixed budget, loops that must stay off the driver's allocator. No
- * counterpart in the reference. The workspace is a fixed 32 MiB array inside the library (held on
- * every GPU that loads it until exit); requests needing more (2*batch*m*n + 2*batch*m*m bf16 values,
- * m = min(rows,cols), n = max(rows,cols), plus 256 bytes) fail with PL_ERR_INVALID. All calls on a
- * device share that array, so calls that overlap on the GPU race: serialise them. The first call on
- * a device looks the array up (cudaGetSymbolAddress); make it before any stream capture. */
+ * cudaMalloc: hosts whose device memory belongs to another allocator or to a budget fixed at
+ * start-up, and loops that must stay off the driver's allocator (whose calls can block and
+ * synchronise the device). No counterpart in the reference. The workspace is a fixed 32 MiB array
+ * inside the library, held on every GPU that loads it until exit. A request needs, each region
+ * rounded up to 256 bytes: 2*batch*m*n bf16 + 2*batch*m*m bf16 + batch*ceil(m*n/16384) doubles +
+ * (3*batch + 1) 32-bit words + 2*batch floats + 256 bytes, with m = min(rows,cols) and
+ * n = max(rows,cols); larger requests fail with PL_ERR_INVALID before anything runs. All calls on a
+ * device share that array and it keeps the last call's contents, so calls that overlap on the GPU
+ * race: serialise them. The call waits for its work on `stream` and returns PL_ERR_DEVICE_TIMEOUT
+ * if a device-side bounded wait ran out. The first call on a device looks the array up
+ * (cudaGetSymbolAddress) and clears its error word. */
 int pl_ns_batched_bf16_dev_noalloc(void* X, size_t batch, size_t rows, size_t cols, double eps,
                                    const double* coeffs, size_t iters, void* stream);
 

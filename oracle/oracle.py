@@ -37,8 +37,16 @@ def build():
     import subprocess
 
     subprocess.check_call(["make", "-s", "-C", HERE, "all"])
-    if os.path.isdir(os.environ.get("PL_REFERENCE_DIR", "/root/reference")):
-        subprocess.check_call(["make", "-s", "-C", HERE, "ref"])
+    ref = reference_dir()
+    if ref:
+        subprocess.check_call(["make", "-s", "-C", HERE, "ref", "REF=" + ref])
+
+
+def reference_dir():
+    """The reference checkout: $PL_REFERENCE_DIR, else a directory named `reference` beside this
+    repository; None when neither exists (the GPU box, which uses the prebuilt oracle/_ref files)."""
+    cand = os.environ.get("PL_REFERENCE_DIR") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isdir(cand) else None
 
 
 def orc():

@@ -20,50 +20,51 @@ __global__ void vtrace_f64_kernel(const double* __restrict__ rew, const double* 
                                   const double* __restrict__ bootv, double* __restrict__ adv,
                                   double* __restrict__ adv_l1, int B, int T, double gamma, double lam,
                                   double rhoClip, double cClip) {
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= B) return;
-  const long base = (long)row * T;
-  const double* rw = rew + base;
-  const double* vv = val + base;
-  const double* tm = term + base;
-  const double* im = imp + base;
-  double* ad = adv + base;
-  const double gl = __dmul_rn(gamma, lam);
-  double last = 0.0;
+  const int seg = blockIdx.x * blockDim.x + threadIdx.x;
+  if (seg >= B) return;
+  const long off = (long)seg * T;
+  const double* reward = rew + off;
+  const double* value = val + off;
+  const double* done = term + off;
+  const double* ratio = imp + off;
+  double* out = adv + off;
+  const double gamma_lambda = __dmul_rn(gamma, lam);
+  double carry = 0.0;  // A[t+1] of the backward recurrence
   if (!MINGRU) {
-    if (T > 0) ad[T - 1] = 0.0;
+    if (T > 0) out[T - 1] = 0.0;
     for (int t = T - 2; t >= 0; t--) {
-      const double nnt = (tm[t] != 0.0) ? 0.0 : 1.0;
-      const double iv = im[t];
-      const double rho = iv < rhoClip ? iv : rhoClip;
-      const double c = iv < cClip ? iv : cClip;
-      const double rr = rw[t];
-      const double r = rr > 1.0 ? 1.0 : (rr < -1.0 ? -1.0 : rr);
-      // rho * (r + gamma*V[t+1]*nnt - V[t])
-      const double delta = __dmul_rn(rho, __dsub_rn(__dadd_rn(r, __dmul_rn(__dmul_rn(gamma, vv[t + 1]), nnt)), vv[t]));
-      // delta + gamma*lam*c*last*nnt
-      last = __dadd_rn(delta, __dmul_rn(__dmul_rn(__dmul_rn(gl, c), last), nnt));
-      ad[t] = last;
+      const double alive = (done[t] != 0.0) ? 0.0 : 1.0;
+      const double w = ratio[t];
+      const double rho_t = w < rhoClip ? w : rhoClip;
+      const double c_t = w < cClip ? w : cClip;
+      const double r_raw = reward[t];
+      const double r_t = r_raw > 1.0 ? 1.0 : (r_raw < -1.0 ? -1.0 : r_raw);  // NaN passes through
+      // rho * (r + gamma*V[t+1]*alive - V[t])
+      const double td =
+          __dmul_rn(rho_t, __dsub_rn(__dadd_rn(r_t, __dmul_rn(__dmul_rn(gamma, value[t + 1]), alive)), value[t]));
+      // td + gamma*lambda*c*A[t+1]*alive
+      carry = __dadd_rn(td, __dmul_rn(__dmul_rn(__dmul_rn(gamma_lambda, c_t), carry), alive));
+      out[t] = carry;
     }
   } else {
     for (int t = T - 1; t >= 0; t--) {
-      const double nnt = (tm[t] > 0.5) ? 0.0 : 1.0;
-      const double vNext = (t + 1 < T) ? vv[t + 1] : bootv[row];
-      const double iv = im[t];
-      const double rho = iv < rhoClip ? iv : rhoClip;
-      const double c = iv < cClip ? iv : cClip;
-      const double rr = rw[t];
-      const double r = rr > 1.0 ? 1.0 : (rr < -1.0 ? -1.0 : rr);
-      // rho*r + gamma*vNext*nnt - V[t]
-      const double delta = __dsub_rn(__dadd_rn(__dmul_rn(rho, r), __dmul_rn(__dmul_rn(gamma, vNext), nnt)), vv[t]);
-      last = __dadd_rn(delta, __dmul_rn(__dmul_rn(__dmul_rn(gl, c), last), nnt));
-      ad[t] = last;
+      const double alive = (done[t] > 0.5) ? 0.0 : 1.0;
+      const double v_next = (t + 1 < T) ? value[t + 1] : bootv[seg];
+      const double w = ratio[t];
+      const double rho_t = w < rhoClip ? w : rhoClip;
+      const double c_t = w < cClip ? w : cClip;
+      const double r_raw = reward[t];
+      const double r_t = r_raw > 1.0 ? 1.0 : (r_raw < -1.0 ? -1.0 : r_raw);  // NaN passes through
+      // rho*r + gamma*v_next*alive - V[t]
+      const double td = __dsub_rn(__dadd_rn(__dmul_rn(rho_t, r_t), __dmul_rn(__dmul_rn(gamma, v_next), alive)), value[t]);
+      carry = __dadd_rn(td, __dmul_rn(__dmul_rn(__dmul_rn(gamma_lambda, c_t), carry), alive));
+      out[t] = carry;
     }
   }
   if (adv_l1) {
     double s = 0.0;
-    for (int t = 0; t < T; t++) s = __dadd_rn(s, fabs(ad[t]));
-    adv_l1[row] = s;
+    for (int t = 0; t < T; t++) s = __dadd_rn(s, fabs(out[t]));
+    adv_l1[seg] = s;
   }
 }
 
