@@ -72,6 +72,17 @@ int pl_vtrace_f64_dev(const double* rew, const double* val, const double* term, 
 
 /* ------------------------------------------------------------------ host bookkeeping ---------- */
 
+/* out = arr[off, off + len) of an n-element array; the range must lie inside it (PL_ERR_INVALID
+ * otherwise). Replaces lean_ffi_slice (ffi/pufferffi.c:13-20; Puffer/Float/FFI.lean:76-77). */
+int pl_slice(const double* arr, size_t n, size_t off, size_t len, double* out);
+/* Minibatch gather from the SoA columns of NT rows: row k takes column row (size_t)idxs[k] (f64-encoded
+ * index, truncated like the reference's cast): mbObs[k*D + j] = obsCol[i*D + j], mbAct/mbAdv/mbRet/
+ * mbOlp[k] = the scalar columns at i. Bit-exact; an index that is NaN, negative or >= NT fails with
+ * PL_ERR_INVALID before anything is written. Replaces lean_ffi_gather_minibatch
+ * (ffi/pufferffi.c:1046-1081; Puffer/Float/FFI.lean:105-107). */
+int pl_gather_minibatch(const double* obsCol, const double* actions, const double* advs, const double* rets,
+                        const double* olps, size_t NT, const double* idxs, size_t Nmb, size_t D, double* mbObs,
+                        double* mbAct, double* mbAdv, double* mbRet, double* mbOlp);
 /* Per-epoch Fisher-Yates with splitmix64, f64-encoded, bit-exact.
  * Replaces lean_ffi_shuffle_perm (ffi/pufferffi.c:1017-1041). out has epochs*NT entries. */
 int pl_shuffle_perm(size_t NT, size_t epochs, uint64_t rng, double* out);

@@ -45,6 +45,16 @@ int pl_test_ns_chain_mode(int mode);
 int pl_test_host_bf16(int mode);
 /* The host rounding itself: rows x D f64 values -> Dp-wide bf16 rows (bits), zero padded. */
 int pl_test_round_rows_bf16(const double* src, long rows, int D, int Dp, uint16_t* dst);
+/* The gather of minibatch (epoch, mb) of an update session, exactly as pl_update_run runs it before
+ * that minibatch's forward pass (same row range, same shuffle translation, same kernel), with its
+ * outputs copied to the host: rows = Nmb x row_elems observation values (f32 in the tight tier; bf16
+ * bits in the bf16 tier, row_elems = D rounded up to 64, zero padded), act (int32), adv, ret, olp and
+ * ov (f32; ov only when the session clips values). *nmb receives Nmb (0 for an empty minibatch). Any
+ * output pointer may be NULL. Under data parallelism every rank must call it (it all-reduces the
+ * advantage statistics as the update does). */
+struct pl_update;
+int pl_test_update_gather(struct pl_update* u, size_t epoch, size_t mb, void* rows, size_t* row_elems, int* act,
+                          float* adv, float* ret, float* olp, float* ov, size_t* nmb, void* stream);
 /* Reads and clears the device-side bounded-wait error word (0 = none). */
 int pl_test_device_error(unsigned* code);
 

@@ -97,6 +97,13 @@ lean_obj_res lean_cuda_mg_read_losses(lean_obj_arg w);
 lean_obj_res lean_ffi_shuffle_perm(size_t NT, size_t epochs, uint64_t rng);
 lean_obj_res lean_ffi_gae_soa(lean_obj_arg vals, lean_obj_arg rews, lean_obj_arg terms, size_t N, size_t T,
                               double gamma, double lam);
+/* sliceFFI, FFI.lean:76-77; replaces ffi/pufferffi.c:13-20. A range outside the array gives NaNs. */
+lean_obj_res lean_ffi_slice(lean_obj_arg arr, size_t off, size_t len);
+/* gatherMinibatchFFI, FFI.lean:105-107; replaces ffi/pufferffi.c:1046-1081. Returns
+ * (mbObs, (mbAct, (mbAdv, (mbRet, mbOlp)))); NT is the length of the action column, and an index that
+ * is not a row of it gives NaN-filled arrays. */
+lean_obj_res lean_ffi_gather_minibatch(lean_obj_arg obsCol, lean_obj_arg actions, lean_obj_arg advs, lean_obj_arg rets,
+                                       lean_obj_arg olps, lean_obj_arg idxs, size_t Nmb, size_t D);
 
 /* MinGRU path. cudaMgPrepFFI, CUDA.lean:154-155; replaces ffi/puffercuda.cu:316-335 */
 lean_obj_res lean_cuda_mg_prep(lean_obj_arg rew, lean_obj_arg term, lean_obj_arg act, lean_obj_arg logp,

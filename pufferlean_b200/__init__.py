@@ -81,6 +81,8 @@ def _bind_optional(L):
         "pl_mingru_ppo_grad": ([_dp] * 3 + [_sz, _sz, C.POINTER(MgNet)] + [_d] * 4 + [C.c_uint8, _dp], C.c_int),
         "pl_prio_sample": ([_dp, _sz, _sz, _d, _d, C.c_uint64, _dp, _dp], C.c_int),
         "pl_gather_seq_minibatch": ([_dp] * 7 + [_sz, _sz, _dp], C.c_int),
+        "pl_slice": ([_dp, _sz, _sz, _sz, _dp], C.c_int),
+        "pl_gather_minibatch": ([_dp] * 5 + [_sz, _dp, _sz, _sz] + [_dp] * 5, C.c_int),
         "pl_mg_create": ([_sz, _sz, C.POINTER(_vp)], C.c_int),
         "pl_mg_destroy": ([_vp], C.c_int),
         "pl_mg_set_columns": ([_vp] + [_dp] * 6, C.c_int),
@@ -173,6 +175,27 @@ def shuffle_perm(NT, epochs, rng):
     out = np.empty(NT * epochs)
     _check(lib().pl_shuffle_perm(NT, epochs, C.c_uint64(rng & (2**64 - 1)), _p(out)), "pl_shuffle_perm")
     return out
+
+
+def slice(arr, off, length):  # noqa: A001 - the reference's name (sliceFFI)
+    """sliceFFI: arr[off : off + length] (the range must lie inside arr)."""
+    a = _f64(arr)
+    out = np.empty(length)
+    _check(lib().pl_slice(_p(a), a.size, off, length, _p(out)), "pl_slice")
+    return out
+
+
+def gather_minibatch(obs_col, actions, advs, rets, olps, idxs, Nmb, D):
+    """gatherMinibatchFFI: rows idxs[0:Nmb] (f64-encoded) of the SoA columns ->
+    (mbObs[Nmb*D], mbAct, mbAdv, mbRet, mbOlp); NT is the length of the action column."""
+    o, a, ad, r, ol, ix = (_f64(x) for x in (obs_col, actions, advs, rets, olps, idxs))
+    NT = min(a.size, ad.size, r.size, ol.size, o.size // D if D else a.size)
+    if ix.size < Nmb:
+        raise PufferError(f"gather_minibatch: {ix.size} indices for {Nmb} rows")
+    outs = [np.empty(Nmb * D)] + [np.empty(Nmb) for _ in range(4)]
+    _check(lib().pl_gather_minibatch(_p(o), _p(a), _p(ad), _p(r), _p(ol), NT, _p(ix), Nmb, D, *[_p(x) for x in outs]),
+           "pl_gather_minibatch")
+    return tuple(outs)
 
 
 def gae_soa(vals, rews, terms, N, T, gamma, lam):

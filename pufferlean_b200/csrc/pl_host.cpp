@@ -1,17 +1,74 @@
-// Host-side bookkeeping twins of the reference's C helpers: per-epoch shuffle, truncated GAE,
-// prioritised segment sampling and the MinGRU minibatch scalar gather. These stay on the host in the
-// reference's update path as well (ffi/pufferffi.c:946-1041, 1094-1176); they are restated here so the
-// library is a drop-in for the whole call sequence of one update.
+// Host-side bookkeeping twins of the reference's C helpers: column slice, per-epoch shuffle, truncated
+// GAE, the feed-forward minibatch row gather, prioritised segment sampling and the MinGRU minibatch
+// scalar gather. These stay on the host in the reference's update path as well (ffi/pufferffi.c:13-20,
+// 946-1081, 1094-1176); they are restated here so the library is a drop-in for the whole call sequence
+// of one update.
 #include <math.h>
 #include <stdio.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
 
+#include <thread>
+#include <vector>
+
 #include "../../include/pufferlean_b200.h"
 #include "pl_host_stage.h"
+#include "pl_runtime.h"
 
 extern "C" {
+
+// out = arr[off, off + len): one contiguous copy (ffi/pufferffi.c:13-20). The range must lie inside the
+// n-element array (the reference leaves that to the caller; here it fails with PL_ERR_INVALID).
+int pl_slice(const double* arr, size_t n, size_t off, size_t len, double* out) {
+  if (len == 0) return PL_OK;
+  if (!arr || !out || off > n || len > n - off)
+    return pl::set_error(PL_ERR_INVALID, "pl_slice: range [%zu, %zu + %zu) outside an array of %zu", off, off, len, n);
+  memcpy(out, arr + off, len * sizeof(double));
+  return PL_OK;
+}
+
+// Minibatch row gather (ffi/pufferffi.c:1046-1081): row k of the minibatch is column row
+// (size_t)idxs[k] (truncation of the f64-encoded index, as the reference's cast): its D observation
+// values and its action, advantage, return and old log-prob. Plain copies, so bit-exact. Every index
+// is checked against the NT rows first (NaN, negative or >= NT fails with PL_ERR_INVALID and nothing
+// is written); large minibatches split their rows over the host threads.
+int pl_gather_minibatch(const double* obsCol, const double* actions, const double* advs, const double* rets,
+                        const double* olps, size_t NT, const double* idxs, size_t Nmb, size_t D, double* mbObs,
+                        double* mbAct, double* mbAdv, double* mbRet, double* mbOlp) {
+  if (Nmb == 0) return PL_OK;
+  if (!actions || !advs || !rets || !olps || !idxs || !mbAct || !mbAdv || !mbRet || !mbOlp || (D && (!obsCol || !mbObs)))
+    return pl::set_error(PL_ERR_INVALID, "pl_gather_minibatch: NULL column");
+  for (size_t k = 0; k < Nmb; k++)
+    if (!(idxs[k] >= 0.0 && idxs[k] < (double)NT))
+      return pl::set_error(PL_ERR_INVALID, "pl_gather_minibatch: index %zu (%g) is not a row in [0, %zu)", k, idxs[k],
+                           NT);
+  auto rows = [&](size_t k0, size_t k1) {
+    for (size_t k = k0; k < k1; k++) {
+      const size_t i = (size_t)idxs[k];
+      if (D) memcpy(mbObs + k * D, obsCol + i * D, D * sizeof(double));
+      mbAct[k] = actions[i];
+      mbAdv[k] = advs[i];
+      mbRet[k] = rets[i];
+      mbOlp[k] = olps[i];
+    }
+  };
+  const size_t work = Nmb * (D + 4);
+  unsigned nt = std::thread::hardware_concurrency();
+  if (nt > 16) nt = 16;
+  if (work < ((size_t)1 << 20) || nt < 2) {
+    rows(0, Nmb);
+    return PL_OK;
+  }
+  std::vector<std::thread> th;
+  const size_t per = (Nmb + nt - 1) / nt;
+  for (unsigned t = 0; t < nt; t++) {
+    const size_t k0 = t * per, k1 = k0 + per < Nmb ? k0 + per : Nmb;
+    if (k0 < k1) th.emplace_back(rows, k0, k1);
+  }
+  for (auto& t : th) t.join();
+  return PL_OK;
+}
 
 // Fisher-Yates per epoch, splitmix64 state chained across epochs (Puffer/RL/VecTrain.lean:240-252).
 // The generator is counter-based (step i of the whole sequence draws splitmix64(seed + (i + 1) * gamma)),

@@ -560,6 +560,45 @@ LEAN_EXPORT lean_obj_res lean_ffi_shuffle_perm(size_t NT, size_t epochs, uint64_
   return out;
 }
 
+LEAN_EXPORT lean_obj_res lean_ffi_slice(lean_obj_arg arr, size_t off, size_t len) {
+  lean_obj_res out = new_fa(len);
+  int rc = pl_slice(fa(arr), fan(arr), off, len, fa(out));
+  lean_dec(arr);
+  return rc ? pure_fail(out, "lean_ffi_slice") : out;
+}
+
+LEAN_EXPORT lean_obj_res lean_ffi_gather_minibatch(lean_obj_arg obsCol, lean_obj_arg actions, lean_obj_arg advs,
+                                                   lean_obj_arg rets, lean_obj_arg olps, lean_obj_arg idxs, size_t Nmb,
+                                                   size_t D) {
+  lean_obj_res o[5] = {new_fa(Nmb * D), new_fa(Nmb), new_fa(Nmb), new_fa(Nmb), new_fa(Nmb)};
+  /* rows that exist in every column */
+  size_t NT = fan(actions);
+  if (fan(advs) < NT) NT = fan(advs);
+  if (fan(rets) < NT) NT = fan(rets);
+  if (fan(olps) < NT) NT = fan(olps);
+  if (D && fan(obsCol) / D < NT) NT = fan(obsCol) / D;
+  int rc = fan(idxs) < Nmb ? -1
+                           : pl_gather_minibatch(fa(obsCol), fa(actions), fa(advs), fa(rets), fa(olps), NT, fa(idxs),
+                                                 Nmb, D, fa(o[0]), fa(o[1]), fa(o[2]), fa(o[3]), fa(o[4]));
+  lean_dec(obsCol);
+  lean_dec(actions);
+  lean_dec(advs);
+  lean_dec(rets);
+  lean_dec(olps);
+  lean_dec(idxs);
+  if (rc)
+    for (int i = 0; i < 5; i++) pure_fail(o[i], "lean_ffi_gather_minibatch");
+  /* (mbObs, (mbAct, (mbAdv, (mbRet, mbOlp)))): Prod.mk, constructor 0 with 2 fields */
+  lean_obj_res t = o[4];
+  for (int i = 3; i >= 0; i--) {
+    lean_obj_res p = lean_alloc_ctor(0, 2, 0);
+    lean_ctor_set(p, 0, o[i]);
+    lean_ctor_set(p, 1, t);
+    t = p;
+  }
+  return t;
+}
+
 LEAN_EXPORT lean_obj_res lean_ffi_gae_soa(lean_obj_arg vals, lean_obj_arg rews, lean_obj_arg terms, size_t N, size_t T,
                                           double gamma, double lam) {
   lean_obj_res out = new_fa(2 * N * T);

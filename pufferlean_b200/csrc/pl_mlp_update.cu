@@ -451,6 +451,51 @@ static int muon_sharded(pl_update* u, double lr, cudaStream_t st) {
   return PL_OK;
 }
 
+// The minibatch's rows of the resident columns (row k = column row idx[k]; its observation row is
+// oidx[k] when obs is not in column order; xdirect: the observation rows are already contiguous and
+// only the scalars are gathered), with the advantage statistics of the minibatch (all ranks' rows
+// under data parallelism).
+static int gather_step(pl_update* u, const int* idx, const int* oidx, const void* xdirect, int Nmb, cudaStream_t st) {
+  const bool fast = u->fast;
+  int rc = launch_gather(fast, idx, Nmb, xdirect ? nullptr : u->obs, fast ? u->Dp : (int)u->d.D, u->X, u->act_c,
+                         u->adv_c, u->ret_c, u->olp_c, u->ov_c, u->mb_act, u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov,
+                         u->adv_part, u->ms, st, u->dp ? u->adv_sums : nullptr, fast ? oidx : nullptr);
+  // data parallel: the normalisation statistics are those of the whole (all-rank) minibatch
+  if (!rc && u->dp) rc = comm_allreduce_f64(u->d.comm, u->adv_sums, 3, st);
+  if (!rc && u->dp) rc = launch_adv_ms_from_sums(u->adv_sums, u->ms, st);
+  return rc;
+}
+
+// Minibatch m of epoch e: rows [lo, lo + Nmb) of that epoch's shuffle, mbSize = NT / numMB and the
+// last minibatch taking the remainder (ffi/puffercuda.cu:1236-1241); false when it is empty. idx, oidx
+// and xdirect are what gather_step reads for it.
+struct MbRows {
+  long lo = 0;
+  int Nmb = 0;
+  const int* idx = nullptr;
+  const int* oidx = nullptr;
+  const void* xdirect = nullptr;
+};
+static bool minibatch_rows(const pl_update* u, size_t e, size_t m, MbRows* r) {
+  const pl_update_desc& d = u->d;
+  const long lo = (long)m * u->mbSize;
+  long hi = (m + 1 == d.numMB) ? (long)d.NT : (long)(m + 1) * u->mbSize;
+  if (hi > (long)d.NT) hi = (long)d.NT;
+  if (hi <= lo) return false;
+  r->lo = lo;
+  r->Nmb = (int)(hi - lo);
+  r->idx = u->perm + e * d.NT + lo;
+  r->oidx = nullptr;
+  r->xdirect = nullptr;
+  if (u->obs_epoch0) {
+    if (e == 0)
+      r->xdirect = (const __nv_bfloat16*)u->obs + lo * u->Dp;
+    else
+      r->oidx = u->operm + e * d.NT + lo;
+  }
+  return true;
+}
+
 // oidx: observation rows when obs is not in column order; xdirect: the minibatch's rows already
 // contiguous in obs (no observation gather).
 static int minibatch_fast(pl_update* u, const int* idx, const int* oidx, const void* xdirect, int Nmb, double lr,
@@ -462,12 +507,7 @@ static int minibatch_fast(pl_update* u, const int* idx, const int* oidx, const v
   int rc;
   {
     Span sp(u, 5, st, 0);
-    rc = launch_gather(true, idx, Nmb, xdirect ? nullptr : u->obs, u->Dp, u->X, u->act_c, u->adv_c, u->ret_c, u->olp_c,
-                       u->ov_c, u->mb_act, u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st,
-                       u->dp ? u->adv_sums : nullptr, oidx);
-    // data parallel: the normalisation statistics are those of the whole (all-rank) minibatch
-    if (!rc && u->dp) rc = comm_allreduce_f64(d.comm, u->adv_sums, 3, st);
-    if (!rc && u->dp) rc = launch_adv_ms_from_sums(u->adv_sums, u->ms, st);
+    rc = gather_step(u, idx, oidx, xdirect, Nmb, st);
   }
   if (rc) return rc;
   // ---- forward
@@ -661,11 +701,7 @@ static int minibatch_tight(pl_update* u, const int* idx, int Nmb, double lr, boo
   (void)last;
   const pl_update_desc& d = u->d;
   const int L = u->L, act = d.arch.act, D = (int)d.D, H = (int)d.H, O = u->O;
-  int rc = launch_gather(false, idx, Nmb, u->obs, D, u->X, u->act_c, u->adv_c, u->ret_c, u->olp_c, u->ov_c, u->mb_act,
-                         u->mb_adv, u->mb_ret, u->mb_olp, u->mb_ov, u->adv_part, u->ms, st,
-                         u->dp ? u->adv_sums : nullptr);
-  if (!rc && u->dp) rc = comm_allreduce_f64(d.comm, u->adv_sums, 3, st);
-  if (!rc && u->dp) rc = launch_adv_ms_from_sums(u->adv_sums, u->ms, st);
+  int rc = gather_step(u, idx, nullptr, nullptr, Nmb, st);
   if (rc) return rc;
   const float* hin = (const float*)u->X;
   int nin = D;
@@ -1120,12 +1156,10 @@ int pl_update_run(pl_update* u, double lr, void* stream) {
   }
   for (size_t e = 0; e < d.epochs; e++)
     for (size_t m = 0; m < d.numMB; m++) {
-      const long lo = (long)m * u->mbSize;
-      long hi = (m + 1 == d.numMB) ? (long)d.NT : (long)(m + 1) * u->mbSize;
-      if (hi > (long)d.NT) hi = (long)d.NT;
-      if (hi <= lo) continue;
-      const int Nmb = (int)(hi - lo);
-      const int* idx = u->perm + e * d.NT + lo;
+      MbRows mr;
+      if (!minibatch_rows(u, e, m, &mr)) continue;
+      const long lo = mr.lo, hi = mr.lo + mr.Nmb;
+      const int Nmb = mr.Nmb;
       const bool last = (e + 1 == d.epochs) && (m + 1 == d.numMB);
       if (upl && e == 0) {
         const int r = upload_rows_bf16_order(u->hstage, u->pend_obs, u->pend_perm, (long)d.NT, lo, hi, (int)d.D, u->Dp,
@@ -1135,16 +1169,8 @@ int pl_update_run(pl_update* u, double lr, void* stream) {
         PL_CUDA(cudaEventRecord(u->cev, u->cst));
         PL_CUDA(cudaStreamWaitEvent(st, u->cev, 0));
       }
-      const int* oidx = nullptr;
-      const void* xdirect = nullptr;
-      if (u->obs_epoch0) {
-        if (e == 0)
-          xdirect = (const __nv_bfloat16*)u->obs + lo * u->Dp;
-        else
-          oidx = u->operm + e * d.NT + lo;
-      }
-      int rc = u->fast ? minibatch_fast(u, idx, oidx, xdirect, Nmb, lr, last, st)
-                       : minibatch_tight(u, idx, Nmb, lr, last, st);
+      int rc = u->fast ? minibatch_fast(u, mr.idx, mr.oidx, mr.xdirect, Nmb, lr, last, st)
+                       : minibatch_tight(u, mr.idx, Nmb, lr, last, st);
       if (rc) return rc;
       lastNmb = Nmb;
     }
@@ -1498,4 +1524,32 @@ extern "C" int pl_test_host_bf16(int mode) {
   const int prev = g_host_bf16 ? 1 : 0;
   if (mode >= 0) g_host_bf16 = mode != 0;
   return prev;
+}
+
+// Test hook: the gather of minibatch (epoch, mb) exactly as pl_update_run runs it before that
+// minibatch's forward pass, with its outputs copied to the host.
+extern "C" int pl_test_update_gather(pl_update* u, size_t epoch, size_t mb, void* rows, size_t* row_elems, int* act,
+                                     float* adv, float* ret, float* olp, float* ov, size_t* nmb, void* stream) {
+  PL_REQUIRE(u && nmb, PL_ERR_INVALID, "pl_test_update_gather: NULL argument");
+  PL_REQUIRE(epoch < u->d.epochs && mb < u->d.numMB, PL_ERR_INVALID, "pl_test_update_gather: no minibatch (%zu, %zu)",
+             epoch, mb);
+  PL_REQUIRE(u->pend_obs == nullptr, PL_ERR_INVALID, "pl_test_update_gather: observations not uploaded yet");
+  cudaStream_t st = (cudaStream_t)stream;
+  MbRows mr;
+  *nmb = 0;
+  if (!minibatch_rows(u, epoch, mb, &mr)) return PL_OK;
+  int rc = gather_step(u, mr.idx, mr.oidx, mr.xdirect, mr.Nmb, st);
+  if (rc) return rc;
+  PL_CUDA(cudaStreamSynchronize(st));
+  const size_t re = u->fast ? (size_t)u->Dp : (size_t)u->d.D, es = u->fast ? 2 : 4;
+  *nmb = (size_t)mr.Nmb;
+  if (row_elems) *row_elems = re;
+  const size_t n = (size_t)mr.Nmb;
+  if (rows) PL_CUDA(cudaMemcpy(rows, mr.xdirect ? mr.xdirect : u->X, n * re * es, cudaMemcpyDeviceToHost));
+  if (act) PL_CUDA(cudaMemcpy(act, u->mb_act, n * sizeof(int), cudaMemcpyDeviceToHost));
+  if (adv) PL_CUDA(cudaMemcpy(adv, u->mb_adv, n * sizeof(float), cudaMemcpyDeviceToHost));
+  if (ret) PL_CUDA(cudaMemcpy(ret, u->mb_ret, n * sizeof(float), cudaMemcpyDeviceToHost));
+  if (olp) PL_CUDA(cudaMemcpy(olp, u->mb_olp, n * sizeof(float), cudaMemcpyDeviceToHost));
+  if (ov && u->mb_ov) PL_CUDA(cudaMemcpy(ov, u->mb_ov, n * sizeof(float), cudaMemcpyDeviceToHost));
+  return PL_OK;
 }

@@ -5,6 +5,8 @@
 #include <stdint.h>
 
 namespace pl {
+// Records the message pl_last_error returns on this thread and returns code.
+int set_error(int code, const char* fmt, ...);
 void count_launch(uint64_t n = 1);
 int require_device();
 // Grow-only device buffer `slot` (0..63) of at least `bytes` on the current device; NULL on failure

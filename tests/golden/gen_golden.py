@@ -2,7 +2,7 @@
 
 Run in the build container (the reference tree must be present and no GPU visible):
 
-    make -C oracle all ref && python tests/golden/gen_golden.py
+    make -C oracle all ref && python tests/golden/gen_golden.py [--only gather]
 
 Inputs are the seeded known-answer inputs of the reference's verify-* modes (oracle/kat.py).
 Outputs come from the reference's C compiled from its sources by oracle/Makefile:
@@ -31,10 +31,53 @@ def arr(p):
     return O.read_float_array(p)
 
 
+def unpack5(tup):
+    """(a, (b, (c, (d, e)))) of the reference's Prod constructors -> five arrays."""
+    out = []
+    for _ in range(4):
+        out.append(arr(O.ctor_field(tup, 0)))
+        tup = O.ctor_field(tup, 1)
+    out.append(arr(tup))
+    return out
+
+
+def gather_fixture(cpu):
+    """lean_ffi_gather_minibatch over every minibatch of three shuffled epochs (ragged last minibatch,
+    a row width that is not a multiple of the vector width), and lean_ffi_slice on a few ranges."""
+    rng = kat.Rng(0x6A7E)
+    NT, D, E, MB = 203, 9, 3, 4
+    obs = np.array([rng.randF(-3.0, 3.0) for _ in range(NT * D)])
+    acts = np.array([float(rng.next() % 7) for _ in range(NT)])
+    advs = np.array([rng.randF(-2.0, 2.0) for _ in range(NT)])
+    rets = np.array([rng.randF(-2.0, 2.0) for _ in range(NT)])
+    olps = np.array([rng.randF(-4.0, -0.1) for _ in range(NT)])
+    perm = arr(ref_call(cpu, "lean_ffi_shuffle_perm", VP, NT, E, ("u64", 0x6A7E)))
+    mb = NT // MB
+    outs = [[] for _ in range(5)]
+    for e in range(E):
+        for m in range(MB):
+            lo, hi = m * mb, (NT if m + 1 == MB else (m + 1) * mb)
+            idx = perm[e * NT + lo:e * NT + hi]
+            got = unpack5(ref_call(cpu, "lean_ffi_gather_minibatch", VP, FA(obs), FA(acts), FA(advs), FA(rets),
+                                   FA(olps), FA(idx), hi - lo, D))
+            for i in range(5):
+                outs[i].append(got[i])
+    slices = [(0, 5), (17, 100), (NT * D - 3, 3), (40, 0)]
+    sl = {f"slice{i}": arr(ref_call(cpu, "lean_ffi_slice", VP, FA(obs), off, ln)) for i, (off, ln) in enumerate(slices)}
+    np.savez(os.path.join(OUT, "gather_minibatch.npz"), obs=obs, acts=acts, advs=advs, rets=rets, olps=olps, perm=perm,
+             mbObs=np.concatenate(outs[0]), mbAct=np.concatenate(outs[1]), mbAdv=np.concatenate(outs[2]),
+             mbRet=np.concatenate(outs[3]), mbOlp=np.concatenate(outs[4]), slices=np.array(slices),
+             meta=np.array([NT, D, E, MB]), **sl)
+
+
 def main():
     cpu = O.ref_cpu()
+    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "gather":
+        gather_fixture(cpu)
+        return
     cfb = O.ref_cudafb()
     out = {}
+    gather_fixture(cpu)
 
     k = kat.kat_vtrace()
     a = arr(ref_call(cfb, "lean_cuda_vtrace", VP, FA(k["rew"]), FA(k["val"]), FA(k["term"]), FA(k["imp"]), k["B"],

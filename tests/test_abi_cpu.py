@@ -49,6 +49,49 @@ def test_host_bookkeeping_matches_oracle():
     assert np.array_equal(plb.gae_soa(vals, rews, terms, 10, 20, 0.995, 0.9), O.gae_soa(vals, rews, terms, 10, 20, 0.995, 0.9))
 
 
+def _gather_golden():
+    return np.load(os.path.join(ROOT, "tests", "golden", "gather_minibatch.npz"))
+
+
+def test_gather_minibatch_and_slice_bit_exact_against_golden():
+    """The reference's lean_ffi_gather_minibatch over every minibatch of three shuffled epochs (ragged
+    last minibatch) and lean_ffi_slice, against the plain-ABI twins."""
+    g = _gather_golden()
+    NT, D, E, MB = (int(x) for x in g["meta"])
+    mb = NT // MB
+    cols = [g[x] for x in ("mbObs", "mbAct", "mbAdv", "mbRet", "mbOlp")]
+    pos = [0] * 5
+    for e in range(E):
+        for m in range(MB):
+            lo, hi = m * mb, (NT if m + 1 == MB else (m + 1) * mb)
+            n = hi - lo
+            got = plb.gather_minibatch(g["obs"], g["acts"], g["advs"], g["rets"], g["olps"],
+                                       g["perm"][e * NT + lo:e * NT + hi], n, D)
+            for i, (x, w) in enumerate(zip(got, (D, 1, 1, 1, 1))):
+                assert np.array_equal(x, cols[i][pos[i]:pos[i] + n * w]), (e, m, i)
+                pos[i] += n * w
+    for i, (off, ln) in enumerate(g["slices"]):
+        assert np.array_equal(plb.slice(g["obs"], int(off), int(ln)), g[f"slice{i}"])
+
+
+def test_gather_minibatch_edge_cases():
+    g = np.random.default_rng(3)
+    obs, a, ad, r, ol = g.standard_normal(40), g.standard_normal(10), g.standard_normal(10), g.standard_normal(10), \
+        g.standard_normal(10)
+    # empty minibatch, fractional indices truncated like the reference's cast, D = 0
+    assert all(x.size == 0 for x in plb.gather_minibatch(obs, a, ad, r, ol, np.zeros(0), 0, 4))
+    got = plb.gather_minibatch(obs, a, ad, r, ol, np.array([2.9, 0.0]), 2, 4)
+    assert np.array_equal(got[0], np.concatenate([obs[8:12], obs[0:4]])) and np.array_equal(got[1], a[[2, 0]])
+    assert np.array_equal(plb.gather_minibatch(obs, a, ad, r, ol, np.array([9.0]), 1, 0)[2], ad[[9]])
+    # an index that is not a row fails before anything is written
+    for bad in (10.0, -1.0, np.nan):
+        with pytest.raises(plb.PufferError, match="not a row"):
+            plb.gather_minibatch(obs, a, ad, r, ol, np.array([1.0, bad]), 2, 4)
+    with pytest.raises(plb.PufferError, match="outside"):
+        plb.slice(obs, 38, 3)
+    assert plb.slice(obs, 40, 0).size == 0
+
+
 def test_mingru_host_twins_bit_exact_against_golden():
     """pl_prio_sample and pl_gather_seq_minibatch reproduce the reference's host C bit for bit."""
     gp = np.load(os.path.join(ROOT, "tests", "golden", "prio.npz"))
@@ -147,6 +190,36 @@ def test_lean_adapter_host_bookkeeping_against_golden():
     out = O.ref_call(lib, "lean_ffi_gae_soa", C.c_void_p, O.FA(g["vals"]), O.FA(g["rews"]), O.FA(g["terms"]), int(N),
                      int(T), float(gm), float(lm))
     assert np.array_equal(O.read_float_array(out), g["out"])
+
+
+def test_lean_adapter_gather_minibatch_and_slice_against_golden():
+    from oracle import oracle as O
+
+    lib = C.CDLL(LEAN_LIB)
+    g = _gather_golden()
+    NT, D, E, MB = (int(x) for x in g["meta"])
+    n = NT - (MB - 1) * (NT // MB)  # the ragged last minibatch of the last epoch
+    lo = (E - 1) * NT + (MB - 1) * (NT // MB)
+    t = O.ref_call(lib, "lean_ffi_gather_minibatch", C.c_void_p, O.FA(g["obs"]), O.FA(g["acts"]), O.FA(g["advs"]),
+                   O.FA(g["rets"]), O.FA(g["olps"]), O.FA(g["perm"][lo:lo + n]), n, D)
+    got = []
+    for _ in range(4):
+        got.append(O.read_float_array(O.ctor_field(t, 0)))
+        t = O.ctor_field(t, 1)
+    got.append(O.read_float_array(t))
+    k0 = (E - 1) * NT + (MB - 1) * (NT // MB)
+    assert np.array_equal(got[0], g["mbObs"][k0 * D:(k0 + n) * D])
+    for x, name in zip(got[1:], ("mbAct", "mbAdv", "mbRet", "mbOlp")):
+        assert np.array_equal(x, g[name][k0:k0 + n])
+    for i, (off, ln) in enumerate(g["slices"]):
+        out = O.ref_call(lib, "lean_ffi_slice", C.c_void_p, O.FA(g["obs"]), int(off), int(ln))
+        assert np.array_equal(O.read_float_array(out), g[f"slice{i}"])
+    # out of range: NaNs, never zeros
+    out = O.ref_call(lib, "lean_ffi_slice", C.c_void_p, O.FA(np.ones(4)), 3, 2)
+    assert np.all(np.isnan(O.read_float_array(out)))
+    t = O.ref_call(lib, "lean_ffi_gather_minibatch", C.c_void_p, O.FA(np.ones(8)), O.FA(np.ones(2)),
+                   O.FA(np.ones(2)), O.FA(np.ones(2)), O.FA(np.ones(2)), O.FA(np.array([5.0])), 1, 4)
+    assert np.all(np.isnan(O.read_float_array(O.ctor_field(t, 0))))
 
 
 def test_lean_adapter_mingru_host_bookkeeping_against_golden():
