@@ -45,9 +45,12 @@ WORKLOADS = {
     # profiling case of C5: the same per-row shapes, 1024 envs, one minibatch of 65,536 rows
     "c5p": dict(name="C5 per-row shapes, 1024 envs (profiling case)", N=1024, T=64, D=1024, H=2048, L=5, A=64,
                 act=1, Nmb=65536, epochs=1, obs="normal", rew="normal", done=0.01, lr=0.02),
-    # CartPole-shaped, 1024 envs x 64, obs 4, hidden 128, 2 actions
-    "c1": dict(name="C1 CartPole-shaped PPO+Muon update (configs[0])", N=1024, T=64, D=4, H=128, L=1, A=2, act=1,
-               Nmb=16384, epochs=4, obs="normal", rew="bern", done=0.01, lr=0.02),
+    # CartPole-shaped, 1024 envs x 64, obs 4, hidden 128, 2 actions, fp32. The network
+    # is the reference's own (ReLU; its CPU path has no GELU) so the reference arm runs the same work through its
+    # compiled C; no value clip (lean_ffi_mlp_ppo_grad_batch_blas has none)
+    "c1": dict(name="C1 CartPole-shaped PPO+Muon update (configs[0], the reference's ReLU network, fp32)", N=1024,
+               T=64, D=4, H=128, L=1, A=2, act=0, Nmb=16384, epochs=4, obs="normal", rew="bern", done=0.01, lr=0.02,
+               bf16=0, vfclip=0.0, maxgn=1.5),
 }
 
 
@@ -219,8 +222,9 @@ def run_ours(args, wl, rank, world, local_rank):
     co = np.ascontiguousarray(np.array(QUINTIC, dtype=np.float64))
     comm = make_comm(L, rank, world)
     desc = Desc(NT=NT, D=D, H=H, A=A, epochs=E, numMB=numMB, arch=Arch(Lh, wl["act"], co.ctypes.data_as(dp), 5),
-                wd=0.0, mu=0.95, eps=1e-12, vfCoef=0.5, entCoef=0.01, clipEps=0.2, vfClip=0.2, maxGradNorm=1.5,
-                bf16=1, use_old_values=1, rank=rank, world=world, comm=comm)
+                wd=0.0, mu=0.95, eps=1e-12, vfCoef=0.5, entCoef=0.01, clipEps=0.2, vfClip=wl.get("vfclip", 0.2),
+                maxGradNorm=wl.get("maxgn", 1.5), bf16=wl.get("bf16", 1), use_old_values=int(wl.get("vfclip", 0.2) > 0),
+                rank=rank, world=world, comm=comm)
     u = vp()
     check(L.pl_update_create(handle, C.byref(desc), C.byref(u)), L)
     stream = torch.cuda.current_stream().cuda_stream
@@ -240,15 +244,27 @@ def run_ours(args, wl, rank, world, local_rank):
     torch.cuda.synchronize()
     check(L.pl_update_profile(u, 1), L)
     l0 = L.pl_kernel_launch_count()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # inputs smaller than L2 are timed step by step with a 256 MB write between steps, so
+    # every step starts with a cold L2; larger ones (configs[4]: 17 GB of observations) need no flush
+    in_bytes = NT * (D + 8) * 4
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda") if in_bytes < (256 << 20) else None
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps if flush is not None else 1)]
     with ClockSampler(local_rank) as clk:
-        ev0.record()
-        for _ in range(args.steps):
-            step()
-        ev1.record()
+        if flush is None:
+            evs[0][0].record()
+            for _ in range(args.steps):
+                step()
+            evs[0][1].record()
+        else:
+            for e0, e1 in evs:
+                flush.fill_(1.0)
+                e0.record()
+                step()
+                e1.record()
         torch.cuda.synchronize()
     launches = L.pl_kernel_launch_count() - l0
-    ms = ev0.elapsed_time(ev1) / args.steps
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / args.steps
     pms, pfl, pln = (C.c_double * 8)(), (C.c_double * 8)(), (C.c_double * 8)()
     check(L.pl_update_profile_read(u, pms, pfl, pln), L)
     check(L.pl_update_profile(u, 0), L)
@@ -274,12 +290,15 @@ def run_ours(args, wl, rank, world, local_rank):
     out = {
         "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; obs/rewards N(0,1), dones Bern(0.01))",
+        "vs_baseline": None, "dtype": "bf16" if wl.get("bf16", 1) else "f32",
+        "data": "synthetic (seeded; obs N(0,1), rewards %s, dones Bern(%g))" % (
+            "N(0,1)" if wl["rew"] == "normal" else "Bern(0.5)", wl["done"]),
         "config": {"workload": wl["name"], "N_envs_per_gpu": N, "horizon": T, "obs_dim": D, "hidden": H,
                    "hidden_layers": Lh, "actions": A, "activation": "gelu" if wl["act"] else "relu",
                    "minibatch_rows_per_gpu": Nmb, "epochs": E, "minibatches_per_epoch": numMB,
                    "ns_coeffs": "quintic (3.4445,-4.7750,2.0315) x5", "params": P,
-                   "l2": "no flush: the obs column alone (fp32 %.1f GB) exceeds L2" % (NT * D * 4 / 1e9),
+                   "l2": ("no flush: the obs column alone (fp32 %.1f GB) exceeds L2" % (NT * D * 4 / 1e9)
+                          if flush is None else "L2 flushed (256 MB write) before each timed step"),
                    "parallelism": f"dp{world}"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": achieved / peak_tf if peak_tf else None,
@@ -345,8 +364,8 @@ def run_e2e(args, wl, state, rank, world, local_rank):
         ret = C.cast(gae.data_ptr() + 8 * NT, dp)
         check(L.pl_train_update_resident_deep(state["handle"], C.byref(arch), P_(obs_h), P_(cols["acts"]), adv, ret,
                                               P_(cols["olp"]), P_(cols["val"]), NT, P_(perm), NT, D, H, A, E, numMB,
-                                              wl["lr"], 0.0, 0.95, 1e-12, 0.5, 0.01, 0.2, 0.2, 1.5, 1,
-                                              out0.ctypes.data_as(dp)), L)
+                                              wl["lr"], 0.0, 0.95, 1e-12, 0.5, 0.01, 0.2, wl.get("vfclip", 0.2),
+                                              wl.get("maxgn", 1.5), wl.get("bf16", 1), out0.ctypes.data_as(dp)), L)
 
     if world > 1:
         # the reference's C-ABI is single-GPU; the data-parallel form of the same call is the session
@@ -920,6 +939,65 @@ def cpu_baseline(wl, steps=1):
                        f"{wl['N'] * wl['T'] // wl['Nmb']} minibatches of {wl['Nmb']} rows")}
 
 
+def reference_c1(wl, steps, warmup):
+    """configs[0] through the reference's own compiled C (oracle/_ref/libref_cpu.so, composed as its CPU
+    trainer calls it: oracle/ref_update.py) on every host core: whole updates, same shapes, init and
+    hyperparameters as this library's C1 line."""
+    from oracle import ref_update as R
+
+    N, T, D, H, A = wl["N"], wl["T"], wl["D"], wl["H"], wl["A"]
+    NT, E = N * T, wl["epochs"]
+    g = np.random.default_rng(7)
+    _, pm = xavier_pm(D, H, A, 1, 42)
+    cols = (g.standard_normal(NT * D), g.integers(0, A, NT).astype(float),
+            np.log(1.0 / A) + 0.05 * g.standard_normal(NT), g.standard_normal(NT),
+            (g.random(NT) < 0.5).astype(float), (g.random(NT) < wl["done"]).astype(float))
+    dt, pm, threads = R.timed_updates(pm, cols, N, T, D, H, A, E, NT // wl["Nmb"], steps, warmup, lr=wl["lr"],
+                                      eps=1e-12, max_grad_norm=wl["maxgn"])
+    return {"value": NT / dt, "unit": "samples/s", "cores": int(threads), "kind": "reference",
+            "sample": (f"{steps} whole updates ({dt:.3f} s each) through the reference's compiled C: lean_ffi_gae_soa, "
+                       "lean_ffi_shuffle_perm, per minibatch lean_ffi_gather_minibatch, normalizeAdv (restatement), "
+                       "lean_ffi_mlp_ppo_grad_batch_blas, the mean-gradient clip, lean_ffi_muon_step_mlp; BLAS "
+                       f"threads {threads} (lean_ffi_blas_set_threads)"),
+            "finite": bool(np.isfinite(pm).all())}
+
+
+def measure_c1(args):
+    """configs[0] on this library (device-resident update and the reference-facing call from host
+    columns) beside the reference's own compiled C on the host cores."""
+    import pufferlean_b200 as plb
+
+    wl = WORKLOADS["c1"]
+    a = argparse.Namespace(**vars(args))
+    a.steps, a.warmup = 20, 3
+    out, state = run_ours(a, wl, 0, 1, 0)
+    e2e = run_e2e(a, wl, state, 0, 1, 0)
+    plb.policy_free(state["handle"])
+    res = {"config": wl["name"], "dtype": "f32 (tight tier: fp32 GEMMs, f64 Muon)", "value": out["value"],
+           "ms_per_step": out["ms_per_step"], "gpu_launches_per_update": out["gpu_launches"] / a.steps,
+           "l2": out["config"]["l2"], "e2e": e2e}
+    if not args.no_cpu and os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libref_cpu.so")):
+        ref = reference_c1(wl, 3, 1)
+        res["reference_c"] = ref
+        res["device_over_reference"] = out["value"] / ref["value"]
+        res["e2e_over_reference"] = e2e["value"] / ref["value"]
+    return res
+
+
+def _all_cores_blas():
+    """Every host core for numpy's BLAS, whatever OMP_NUM_THREADS the launcher set."""
+    try:
+        from threadpoolctl import threadpool_limits
+
+        from oracle.ref_update import host_cores
+
+        return threadpool_limits(limits=host_cores(), user_api="blas")
+    except Exception:
+        import contextlib
+
+        return contextlib.nullcontext()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -961,11 +1039,15 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
-        base = cpu_baseline(wl, steps=max(1, min(args.steps, 2)))
+        if args.workload == "c1":
+            base = reference_c1(wl, max(1, args.steps), min(args.warmup, 1))
+        else:
+            with _all_cores_blas():
+                base = cpu_baseline(wl, steps=max(1, min(args.steps, 2)))
         line = {"metric": METRIC, "value": base["value"], "unit": "samples/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f64", "data": "synthetic (seeded)", "impl": "reference",
-                "config": {"workload": wl["name"], "parallelism": "host cores"},
+                "config": {"workload": wl["name"], "parallelism": "host cores (%d)" % base["cores"]},
                 "cpu_baseline": base,
                 "e2e": {"value": base["value"], "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -997,9 +1079,15 @@ def main():
         out["c3_newton_schulz"] = measure_ns_c3()
         if world == 1:
             out["c4_mingru"] = measure_mingru_c4(args, cpu=not args.no_cpu)
+            if args.workload != "c1":
+                out["c1_cartpole"] = measure_c1(args)
     if rank == 0:
         if not args.no_cpu and world == 1:
-            out["cpu_baseline"] = cpu_baseline(wl)
+            if args.workload == "c1":
+                out["cpu_baseline"] = reference_c1(wl, 3, 1)
+            else:
+                with _all_cores_blas():
+                    out["cpu_baseline"] = cpu_baseline(wl)
         print(json.dumps(out), flush=True)
     if world > 1:
         import torch

@@ -124,12 +124,14 @@ int launch_f64_to_f32(const double* s, long n, float* d, cudaStream_t st);
 int launch_f32_to_f64(const float* s, long n, double* d, cudaStream_t st);
 int launch_sgemm(int M, int N, int K, const float* A, long ars, long acs, const float* B, long brs, long bcs, float* C,
                  long ldc, float alpha, cudaStream_t st);
+int launch_sgemm_splitk(int M, int N, int K, const float* A, long ars, long acs, const float* B, long brs, long bcs,
+                        float* C, long ldc, float* ws, long ws_elems, cudaStream_t st);
 int launch_bias_act_f32(float* Z, float* H, const float* b, long M, int N, int act, cudaStream_t st);
 int launch_act_grad_f32(float* dH, const float* Z, long n, int act, cudaStream_t st);
 int launch_ppo_rows_f32(const float* Out, int M, int A, const int* act, const float* adv, const double* ms,
                         const float* ret, const float* olp, const float* ov, float vf, float ent, float clip,
                         float vfclip, float* dOut, float* newlp, float* newval, cudaStream_t st);
-int launch_colsum_f32(const float* Mx, long rows, int N, float* out, cudaStream_t st);
+int launch_colsum_f32(const float* Mx, long rows, int N, float* out, float* ws, long ws_elems, cudaStream_t st);
 // Wide action heads (multi-discrete mode 1, Gaussian mode 2): per-row PPO objective gradient,
 // per-128-row column sums (colpart) and loss sums (loss_part); see pl_mlp_kernels.cu.
 int launch_ppo_rows_wide(bool bf16_out, const float* Out, int ldo, const float* bias, int M, int O, int ldd, int mode,

@@ -423,20 +423,23 @@ __global__ void f32_to_f64_kernel(const float* __restrict__ s, long n, double* d
 }
 
 // ---------------------------------------------------------------- tight tier (fp32 SIMT)
-// C[m,n] = alpha * sum_k A(m,k) B(n,k), A(m,k) = A[m*ars + k*acs], B(n,k) = B[n*brs + k*bcs]
+// C[m,n] = alpha * sum_k A(m,k) B(n,k), A(m,k) = A[m*ars + k*acs], B(n,k) = B[n*brs + k*bcs]. Split K:
+// blockIdx.z sums k in [z*kc, (z+1)*kc) into C + z*cz (kc = K and cz = 0 without a split).
 __global__ void __launch_bounds__(256) sgemm_kernel(int M, int N, int K, const float* __restrict__ A, long ars, long acs,
                                                     const float* __restrict__ B, long brs, long bcs, float* C, long ldc,
-                                                    float alpha) {
+                                                    float alpha, int kc, long cz) {
   __shared__ float As[16][65], Bs[16][65];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  const int kb = blockIdx.z * kc, ke = min(K, kb + kc);
+  C += blockIdx.z * cz;
   float acc[4][4] = {};
-  for (int k0 = 0; k0 < K; k0 += 16) {
+  for (int k0 = kb; k0 < ke; k0 += 16) {
     for (int i = threadIdx.x; i < 16 * 64; i += 256) {
       const int kk = i / 64, mm = i % 64;
       const int m = m0 + mm, n = n0 + mm, k = k0 + kk;
-      As[kk][mm] = (m < M && k < K) ? A[(long)m * ars + (long)k * acs] : 0.f;
-      Bs[kk][mm] = (n < N && k < K) ? B[(long)n * brs + (long)k * bcs] : 0.f;
+      As[kk][mm] = (m < M && k < ke) ? A[(long)m * ars + (long)k * acs] : 0.f;
+      Bs[kk][mm] = (n < N && k < ke) ? B[(long)n * brs + (long)k * bcs] : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -687,11 +690,33 @@ __global__ void f64_to_f32_rows_kernel(const double* __restrict__ s, long n, flo
 }
 
 // gb[c] = sum_n M[n*N + c] (sequential per column, deterministic)
-__global__ void colsum_f32_kernel(const float* __restrict__ Mx, long rows, int N, float* out) {
-  int c = blockIdx.x * blockDim.x + threadIdx.x;
+// Column sums of a row-major rows x N matrix in a fixed order, two levels: block (x, y) takes 32
+// columns of the row chunk [y*chunk, (y+1)*chunk); its 8 row lanes each sum every 8th row of the chunk
+// in order and are combined in lane order, giving part[y*N + c]; colsum_parts_kernel then sums the
+// chunks in order. (One thread per column walking all rows left the GPU idle on long minibatches.)
+__global__ void __launch_bounds__(256) colsum_chunk_f32_kernel(const float* __restrict__ Mx, long rows, int N,
+                                                               long chunk, float* part) {
+  __shared__ float sh[8][33];
+  const int cl = threadIdx.x & 31, rl = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + cl;
+  const long r0 = (long)blockIdx.y * chunk, r1 = min(rows, r0 + chunk);
+  float s = 0.f;
+  if (c < N)
+    for (long r = r0 + rl; r < r1; r += 8) s += Mx[r * N + c];
+  sh[rl][cl] = s;
+  __syncthreads();
+  if (rl == 0 && c < N) {
+    float t = sh[0][cl];
+#pragma unroll
+    for (int q = 1; q < 8; q++) t += sh[q][cl];
+    part[(long)blockIdx.y * N + c] = t;
+  }
+}
+__global__ void colsum_parts_kernel(const float* __restrict__ part, int chunks, int N, float* out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= N) return;
   float s = 0.f;
-  for (long n = 0; n < rows; n++) s += Mx[n * N + c];
+  for (int y = 0; y < chunks; y++) s += part[(long)y * N + c];
   out[c] = s;
 }
 
@@ -860,10 +885,27 @@ int launch_f32_to_f64(const float* s, long n, double* d, cudaStream_t st) {
 int launch_sgemm(int M, int N, int K, const float* A, long ars, long acs, const float* B, long brs, long bcs, float* C,
                  long ldc, float alpha, cudaStream_t st) {
   dim3 grid((unsigned)ceil_div(N, 64), (unsigned)ceil_div(M, 64));
-  sgemm_kernel<<<grid, 256, 0, st>>>(M, N, K, A, ars, acs, B, brs, bcs, C, ldc, alpha);
+  sgemm_kernel<<<grid, 256, 0, st>>>(M, N, K, A, ars, acs, B, brs, bcs, C, ldc, alpha, K, 0);
   count_launch();
   PL_LAUNCH("sgemm_kernel");
   return PL_OK;
+}
+// A long-K product with few output tiles (the weight gradients, K = the minibatch rows) would leave
+// all but a few SMs idle walking K: split K over blockIdx.z into slices of the workspace (S * M * N
+// floats, C dense: ldc = N), then sum the slices in order (deterministic).
+int launch_sgemm_splitk(int M, int N, int K, const float* A, long ars, long acs, const float* B, long brs, long bcs,
+                        float* C, long ldc, float* ws, long ws_elems, cudaStream_t st) {
+  const long tiles = ceil_div(N, 64) * ceil_div(M, 64), mn = (long)M * N;
+  long S = std::min<long>(ceil_div(K, 256), ceil_div(2 * 148, tiles));
+  if (ws && mn > 0) S = std::min<long>(S, ws_elems / mn);
+  if (S < 2 || !ws || ldc != N) return launch_sgemm(M, N, K, A, ars, acs, B, brs, bcs, C, ldc, 1.f, st);
+  const int kc = (int)round_up(ceil_div(K, S), 16);
+  S = ceil_div(K, kc);
+  dim3 grid((unsigned)ceil_div(N, 64), (unsigned)ceil_div(M, 64), (unsigned)S);
+  sgemm_kernel<<<grid, 256, 0, st>>>(M, N, K, A, ars, acs, B, brs, bcs, ws, N, 1.f, kc, mn);
+  count_launch();
+  PL_LAUNCH("sgemm_kernel");
+  return launch_splitk_reduce(ws, (int)S, mn, C, st);
 }
 int launch_bias_act_f32(float* Z, float* H, const float* b, long M, int N, int act, cudaStream_t st) {
   bias_act_f32_kernel<<<grid_for(M * N), 256, 0, st>>>(Z, H, b, M, N, act);
@@ -915,10 +957,17 @@ int launch_ppo_rows_f32(const float* Out, int M, int A, const int* act, const fl
   PL_LAUNCH("ppo_rows_f32_kernel");
   return PL_OK;
 }
-int launch_colsum_f32(const float* Mx, long rows, int N, float* out, cudaStream_t st) {
-  colsum_f32_kernel<<<(unsigned)ceil_div(N, 128), 128, 0, st>>>(Mx, rows, N, out);
-  count_launch();
-  PL_LAUNCH("colsum_f32_kernel");
+int launch_colsum_f32(const float* Mx, long rows, int N, float* out, float* ws, long ws_elems, cudaStream_t st) {
+  PL_REQUIRE(N > 0 && ws && ws_elems >= N, PL_ERR_INVALID, "colsum: workspace of %ld floats for %d columns", ws_elems,
+             N);
+  long chunks = std::min<long>(std::max<long>(1, ceil_div(rows, 128)), ws_elems / N);
+  chunks = std::min<long>(chunks, 65535);
+  const long chunk = std::max<long>(1, ceil_div(rows, chunks));
+  chunks = std::max<long>(1, ceil_div(rows, chunk));
+  colsum_chunk_f32_kernel<<<dim3((unsigned)ceil_div(N, 32), (unsigned)chunks), 256, 0, st>>>(Mx, rows, N, chunk, ws);
+  colsum_parts_kernel<<<(unsigned)ceil_div(N, 128), 128, 0, st>>>(ws, (int)chunks, N, out);
+  count_launch(2);
+  PL_LAUNCH("colsum_chunk_f32_kernel");
   return PL_OK;
 }
 

@@ -275,7 +275,7 @@ static int alloc_session(pl_update* u) {
   size_t maxw = 0;
   for (auto& ly : u->layers) maxw = std::max(maxw, (size_t)ly.out * ly.in);
   u->splitk_elems = maxw * 8;
-  u->splitk = fast ? dalloc<float>(u, u->splitk_elems) : nullptr;
+  u->splitk = dalloc<float>(u, u->splitk_elems);  // tight tier: the split-K weight gradients
   // parameters in compute precision
   for (auto& ly : u->layers) {
     if (fast) {
@@ -737,10 +737,12 @@ static int minibatch_tight(pl_update* u, const int* idx, int Nmb, double lr, boo
     const Layer& ly = u->layers[l];
     const float* hprev = l == 0 ? (const float*)u->X : (const float*)u->Hs[l - 1];
     // bias grad
-    rc = launch_colsum_f32(dcur, Nmb, nd, u->grad + ly.ob, st);
+    rc = launch_colsum_f32(dcur, Nmb, nd, u->grad + ly.ob, u->colpart,
+                           (long)colsum_scratch_elems((int)ceil_div(u->mbMax, 128), std::max(u->Hp, u->Op)), st);
     if (rc) return rc;
     // dW[o, i] = sum_n dcur[n, o] hprev[n, i]
-    rc = launch_sgemm(ly.out, ly.in, Nmb, dcur, 1, nd, hprev, 1, ly.in, u->grad + ly.oW, ly.in, 1.f, st);
+    rc = launch_sgemm_splitk(ly.out, ly.in, Nmb, dcur, 1, nd, hprev, 1, ly.in, u->grad + ly.oW, ly.in, u->splitk,
+                             (long)u->splitk_elems, st);
     if (rc) return rc;
     if (l == 0) break;
     // dH[n, i] = sum_o dcur[n, o] W[o, i]

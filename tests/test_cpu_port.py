@@ -85,3 +85,29 @@ def test_port_newton_schulz_equals_restatement(rows, cols):
     want = O.newton_schulz(X.ravel(), rows, cols, 1e-7, O.QUINTIC_COEFFS).reshape(rows, cols)
     got = cpu_port.newton_schulz(X, O.QUINTIC_COEFFS, 1e-7)
     assert rel(got, want) < 1e-11
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("maxgn,NT,MB", [(0.0, 256, 4), (0.5, 301, 3)])
+def test_reference_c_update_composition_equals_restatement(maxgn, NT, MB):
+    """oracle/ref_update.py (the configs[0] CPU baseline: the reference's compiled C called in its CPU
+    trainer's order) against the restatement's whole update with the same GAE and shuffle."""
+    from oracle import ref_update as R
+
+    g = np.random.default_rng(NT)
+    T = 16 if NT % 16 == 0 else 7
+    N = NT // T
+    NT = N * T
+    D, H, A, E = 4, 32, 2, 2
+    P = O.param_count(D, H, A, 1)
+    pm = np.concatenate([g.uniform(-0.3, 0.3, P), np.zeros(P)])
+    obs, acts = g.standard_normal(NT * D), g.integers(0, A, NT).astype(float)
+    olps = np.log(0.5) + 0.05 * g.standard_normal(NT)
+    vals, rews, terms = g.standard_normal(NT), (g.random(NT) < 0.5).astype(float), (g.random(NT) < 0.05).astype(float)
+    got = R.update(pm.copy(), obs, acts, olps, vals, rews, terms, N, T, D, H, A, E, MB, 77, eps=1e-12,
+                   max_grad_norm=maxgn)
+    ga = O.gae_soa(vals, rews, terms, N, T, 0.995, 0.90)
+    perm = O.shuffle_perm(NT, E, 77)
+    want = O.train_update(pm, obs, acts, ga[:NT], ga[NT:], olps, perm, NT, D, H, A, E, MB, 0.02, 0.0, 0.95, 1e-12,
+                          0.5, 0.01, 0.2, maxGradNorm=maxgn)
+    assert rel(got, want) < 1e-11
