@@ -182,7 +182,7 @@ def make_comm(L, rank, world):
     return comm
 
 
-def run_ours(args, wl, rank, world, local_rank):
+def run_ours(args, wl, rank, world, local_rank, comm=None):
     import torch
 
     import pufferlean_b200 as plb
@@ -204,7 +204,8 @@ def run_ours(args, wl, rank, world, local_rank):
     NT = N * T
     Nmb, E = wl["Nmb"], wl["epochs"]
     numMB = NT // Nmb
-    seed = 1234 + rank
+    strong = getattr(args, "scaling", "weak") == "strong"
+    seed = 1234 + (0 if strong else rank)  # strong scaling: every rank holds the same rollout
     gen = torch.Generator(device="cuda").manual_seed(seed)
     obs = torch.randn(NT, D, device="cuda", generator=gen) if wl["obs"] == "normal" else \
         torch.rand(NT, D, device="cuda", generator=gen)
@@ -215,18 +216,22 @@ def run_ours(args, wl, rank, world, local_rank):
     term = (torch.rand(NT, device="cuda", generator=gen) < wl["done"]).float()
     olp = (torch.full((NT,), float(np.log(1.0 / A)), device="cuda", dtype=torch.float64) +
            0.05 * torch.randn(NT, device="cuda", generator=gen, dtype=torch.float64))
-    perm_h = plb.shuffle_perm(NT, E, 0xC5 + rank)
+    perm_h = plb.shuffle_perm(NT, E, 0xC5 + (0 if strong else rank))
     perm = torch.from_numpy(perm_h).cuda()
     P, pm = xavier_pm(D, H, A, Lh, 42)
     handle = plb.policy_load(pm, P)
     co = np.ascontiguousarray(np.array(QUINTIC, dtype=np.float64))
-    comm = make_comm(L, rank, world)
+    if comm is None:
+        comm = make_comm(L, rank, world)
     desc = Desc(NT=NT, D=D, H=H, A=A, epochs=E, numMB=numMB, arch=Arch(Lh, wl["act"], co.ctypes.data_as(dp), 5),
                 wd=0.0, mu=0.95, eps=1e-12, vfCoef=0.5, entCoef=0.01, clipEps=0.2, vfClip=wl.get("vfclip", 0.2),
                 maxGradNorm=wl.get("maxgn", 1.5), bf16=wl.get("bf16", 1), use_old_values=int(wl.get("vfclip", 0.2) > 0),
                 rank=rank, world=world, comm=comm)
     u = vp()
     check(L.pl_update_create(handle, C.byref(desc), C.byref(u)), L)
+    if strong and world > 1:
+        L.pl_update_split_minibatch.argtypes = [vp, C.c_int]
+        check(L.pl_update_split_minibatch(u, 1), L)
     stream = torch.cuda.current_stream().cuda_stream
 
     def step():
@@ -267,12 +272,15 @@ def run_ours(args, wl, rank, world, local_rank):
     ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / args.steps
     pms, pfl, pln = (C.c_double * 8)(), (C.c_double * 8)(), (C.c_double * 8)()
     check(L.pl_update_profile_read(u, pms, pfl, pln), L)
+    cms, cbytes, cn = C.c_double(), C.c_double(), C.c_double()
+    L.pl_update_comm_profile_read.argtypes = [vp, dp, dp, dp]
+    check(L.pl_update_comm_profile_read(u, C.byref(cms), C.byref(cbytes), C.byref(cn)), L)
     check(L.pl_update_profile(u, 0), L)
     if world > 1:
         t = torch.tensor([ms], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
-    value = world * NT / (ms / 1e3)
+    value = (1 if strong else world) * NT / (ms / 1e3)
     peak_tf, peak_hbm, peak_kind = peaks()
     gemm_ms = sum(pms[i] for i in range(4))
     gemm_fl = sum(pfl[i] for i in range(4))
@@ -289,17 +297,20 @@ def run_ours(args, wl, rank, world, local_rank):
 
     out = {
         "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if strong and world > 1 else "weak",
         "vs_baseline": None, "dtype": "bf16" if wl.get("bf16", 1) else "f32",
         "data": "synthetic (seeded; obs N(0,1), rewards %s, dones Bern(%g))" % (
             "N(0,1)" if wl["rew"] == "normal" else "Bern(0.5)", wl["done"]),
         "config": {"workload": wl["name"], "N_envs_per_gpu": N, "horizon": T, "obs_dim": D, "hidden": H,
                    "hidden_layers": Lh, "actions": A, "activation": "gelu" if wl["act"] else "relu",
-                   "minibatch_rows_per_gpu": Nmb, "epochs": E, "minibatches_per_epoch": numMB,
+                   "minibatch_rows_per_gpu": Nmb // world if strong else Nmb, "epochs": E,
+                   "minibatches_per_epoch": numMB,
                    "ns_coeffs": "quintic (3.4445,-4.7750,2.0315) x5", "params": P,
                    "l2": ("no flush: the obs column alone (fp32 %.1f GB) exceeds L2" % (NT * D * 4 / 1e9)
                           if flush is None else "L2 flushed (256 MB write) before each timed step"),
-                   "parallelism": f"dp{world}"},
+                   "parallelism": f"dp{world}" + (" (one rollout, each minibatch split over the ranks)"
+                                                   if strong and world > 1 else "")},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": achieved / peak_tf if peak_tf else None,
                      "traffic": C5_GEMM_DRAM_BYTES_PER_LAUNCH if wl is WORKLOADS["c5"] else None,
@@ -312,6 +323,14 @@ def run_ours(args, wl, rank, world, local_rank):
                           "ms_per_step": pms[4] / args.steps},
         "profile": prof,
         "gpu_launches": int(launches),
+        "dp_allreduce": None if world == 1 else {
+            "ms_per_step_on_comm_stream": cms.value / args.steps,
+            "ms_per_step_exposed": pms[7] / args.steps,
+            "bytes_per_rank_per_step": cbytes.value / args.steps,
+            "launches_per_step": cn.value / args.steps,
+            "bus_gbs": (cbytes.value * 2 * (world - 1) / world / (cms.value / 1e3) / 1e9) if cms.value > 0 else None,
+            "how": "per-layer fp32 ncclAllReduce on a second stream, each started when its layer's gradient is "
+                   "complete; bus GB/s = bytes x 2(N-1)/N / time on that stream"},
         "clocks": clk.summary(),
     }
     return out, dict(handle=handle, P=P, pm=pm, comm=comm, desc=desc, co=co)
@@ -329,13 +348,14 @@ def run_e2e(args, wl, state, rank, world, local_rank):
     NT = N * T
     E, Nmb = wl["epochs"], wl["Nmb"]
     numMB = NT // Nmb
-    gen = torch.Generator(device="cuda").manual_seed(99 + rank)
+    strong = getattr(args, "scaling", "weak") == "strong"
+    gen = torch.Generator(device="cuda").manual_seed(99 + (0 if strong else rank))
     obs_h = torch.empty(NT * D, dtype=torch.float64, pin_memory=True)
     chunk = 1 << 27
     for o in range(0, NT * D, chunk):
         n = min(chunk, NT * D - o)
         obs_h[o:o + n].copy_(torch.randn(n, device="cuda", generator=gen, dtype=torch.float64))
-    g = np.random.default_rng(7 + rank)
+    g = np.random.default_rng(7 + (0 if strong else rank))
     cols = {k: torch.empty(NT, dtype=torch.float64, pin_memory=True) for k in ("acts", "olp", "val", "rew", "term")}
     cols["acts"].copy_(torch.from_numpy(g.integers(0, A, NT).astype(np.float64)))
     cols["olp"].copy_(torch.from_numpy(np.log(1.0 / A) + 0.05 * g.standard_normal(NT)))
@@ -376,10 +396,14 @@ def run_e2e(args, wl, state, rank, world, local_rank):
         L.pl_update_destroy.argtypes = [vp]
         sess = vp()
         check(L.pl_update_create(state["handle"], C.byref(state["desc"]), C.byref(sess)), L)
+        strong = getattr(args, "scaling", "weak") == "strong"
+        if strong:
+            L.pl_update_split_minibatch.argtypes = [vp, C.c_int]
+            check(L.pl_update_split_minibatch(sess, 1), L)
 
         def step(i):  # noqa: F811
             check(L.pl_gae_soa(P_(cols["val"]), P_(cols["rew"]), P_(cols["term"]), N, T, 0.995, 0.90, P_(gae)), L)
-            check(L.pl_shuffle_perm(NT, E, 0xE2E + 1000 * rank + i, P_(perm)), L)
+            check(L.pl_shuffle_perm(NT, E, 0xE2E + (0 if strong else 1000 * rank) + i, P_(perm)), L)
             check(L.pl_update_run_columns(sess, obs_h.data_ptr(), cols["acts"].data_ptr(), gae.data_ptr(),
                                           gae.data_ptr() + 8 * NT, cols["olp"].data_ptr(), cols["val"].data_ptr(),
                                           perm.data_ptr(), wl["lr"], None), L)
@@ -402,7 +426,7 @@ def run_e2e(args, wl, state, rank, world, local_rank):
     # host threads, partly as f64 rows converted on the device; the other columns and the shuffle
     L.pl_update_last_upload_bytes.restype = C.c_uint64
     h2d = int(L.pl_update_last_upload_bytes())
-    return {"value": world * NT / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d,
+    return {"value": (1 if strong else world) * NT / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": 8 if world == 1 else 16,
             "steps": k, "s_per_step": dt,
             "path": ("pl_train_update_resident_deep (the reference-facing C-ABI call)" if world == 1 else
@@ -1005,6 +1029,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c5")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="N > 1: weak = every rank its own rollout of the workload's size; strong = one rollout of "
+                         "that size, each minibatch split over the ranks (value = that rollout's samples / time)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the configs[1] / configs[2] kernel measurements")
@@ -1066,6 +1093,18 @@ def main():
     import pufferlean_b200 as plb
 
     plb.policy_free(state["handle"])
+    if world > 1 and args.scaling == "weak":
+        # the same workload as ONE rollout with each minibatch split over the ranks (strong scaling),
+        # device-resident, on the same communicator
+        a2 = argparse.Namespace(**vars(args))
+        a2.scaling = "strong"
+        s_out, s_state = run_ours(a2, wl, rank, world, local_rank, comm=state["comm"])
+        plb.policy_free(s_state["handle"])
+        if rank == 0:
+            out["strong_scaling"] = {k: s_out[k] for k in ("value", "unit", "ms_per_step", "scaling", "dp_allreduce",
+                                                           "gpu_launches")}
+            out["strong_scaling"]["config"] = s_out["config"]
+            out["strong_scaling"]["profile"] = s_out["profile"]
     if world > 1 and not args.no_extra:
         # configs[3] on every rank (its data-parallel form), before the communicator goes away
         c4 = measure_mingru_c4(args, comm=state["comm"], rank=rank, world=world)

@@ -248,6 +248,16 @@ uint64_t pl_update_last_upload_bytes(void);
  * profiling was switched on. */
 int pl_update_profile(pl_update* u, int on);
 int pl_update_profile_read(pl_update* u, double ms[8], double flops[8], double launches[8]);
+/* Data parallel: the gradient all-reduces on the session's communication stream since profiling was
+ * switched on: their total milliseconds on that stream (class 7 above is the part of it the compute
+ * stream had to wait for), bytes reduced per rank and launches. */
+int pl_update_comm_profile_read(pl_update* u, double* ms, double* bytes, double* launches);
+/* Strong-scaling form of a data-parallel session (no reference counterpart): every rank holds the
+ * same columns and the same shuffle, and rank r of R takes rows [lo + n*r/R, lo + n*(r+1)/R) of each
+ * minibatch [lo, lo + n), so the R ranks together run exactly the single-GPU update's minibatches
+ * (the advantage statistics and the gradient mean are over the whole minibatch). Without it (the
+ * default) every rank brings its own rollout. Needs at least R rows per minibatch. */
+int pl_update_split_minibatch(pl_update* u, int on);
 int pl_update_destroy(pl_update* u);
 
 /* ------------------------------------------------------------------ data parallelism ----------- */
@@ -256,7 +266,8 @@ int pl_update_destroy(pl_update* u);
  * channel, each rank creates its communicator on its current device and passes it to
  * pl_update_create through pl_update_desc {rank, world, comm}. In a data-parallel update every rank
  * gathers its own rows of each minibatch; the advantage statistics and the summed gradient are
- * all-reduced; each weight matrix is orthogonalised by one owner rank (pl_muon_shard_plan) and the
+ * all-reduced (the gradient layer by layer on a second stream, each block as soon as the backward pass
+ * has finished it); each weight matrix is orthogonalised by one owner rank (pl_muon_shard_plan) and the
  * results are broadcast; every rank then applies the identical step. */
 int pl_comm_unique_id(uint8_t id[128]);
 int pl_comm_create(int rank, int world, const uint8_t id[128], void** comm);

@@ -55,6 +55,10 @@ int pl_test_round_rows_bf16(const double* src, long rows, int D, int Dp, uint16_
 struct pl_update;
 int pl_test_update_gather(struct pl_update* u, size_t epoch, size_t mb, void* rows, size_t* row_elems, int* act,
                           float* adv, float* ret, float* olp, float* ov, size_t* nmb, void* stream);
+/* Data-parallel sessions created afterwards: 1 = the gradient all-reduced per layer on a second stream
+ * while the backward pass continues (the default), 0 = one all-reduce of the whole gradient after the
+ * backward pass; a negative mode only queries. Returns the previous mode. */
+int pl_test_dp_overlap(int mode);
 /* Reads and clears the device-side bounded-wait error word (0 = none). */
 int pl_test_device_error(unsigned* code);
 

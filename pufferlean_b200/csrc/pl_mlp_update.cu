@@ -81,6 +81,19 @@ struct pl_update {
   float* adv_f = nullptr;  // fp32 scan output of pl_update_set_advantages_dev
   // data parallelism
   bool dp = false;             // world > 1 with a communicator
+  // strong-scaling split (pl_update_split_minibatch): every rank holds the same columns and takes rows
+  // [lo + n*r/R, lo + n*(r+1)/R) of each minibatch [lo, lo + n)
+  bool split = false;
+  long nglob = 0;  // rows of the current minibatch over all ranks: the gradient mean's divisor
+  // the gradient all-reduce in per-layer buckets on a second stream, each started as soon as that
+  // layer's gradient block is complete, so it runs under the rest of the backward pass
+  bool overlap = true;
+  cudaStream_t ast = nullptr;
+  std::vector<cudaEvent_t> aev;  // [layers] block complete, [layers] all-reduces done
+  double comm_ms = 0, comm_bytes = 0, comm_launches = 0;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> comm_ev;
+  std::vector<double> comm_ev_bytes;
+  size_t comm_ev_used = 0;
   double* adv_sums = nullptr;  // [sum, sum of squares, count] of the minibatch's raw advantages
   std::vector<int> owner;      // Newton-Schulz owner rank of each layer
   std::vector<std::vector<int>> ns_groups;  // layers of equal shape, orthogonalised as one batch
@@ -124,6 +137,7 @@ constexpr float kContLogStdLo = -20.f, kContLogStdHi = 2.f;
 static std::mutex g_mu;
 static bool g_loss_on = false;
 static bool g_host_bf16 = true;
+static bool g_dp_overlap = true;  // sessions created afterwards overlap the gradient all-reduce
 static std::atomic<uint64_t> g_upload_bytes{0};  // host-to-device bytes of the last set_columns call  // bf16 tier: host observations rounded to bf16 on the host threads
 static double g_losses[7] = {0, 0, 0, 0, 0, 0, 0};
 
@@ -172,6 +186,17 @@ struct Span {
 };
 
 static void prof_collect(pl_update* u) {
+  if (u->comm_ev_used) {
+    cudaDeviceSynchronize();
+    for (size_t i = 0; i < u->comm_ev_used; i++) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, u->comm_ev[i].first, u->comm_ev[i].second);
+      u->comm_ms += ms;
+      u->comm_bytes += u->comm_ev_bytes[i];
+      u->comm_launches += 1;
+    }
+    u->comm_ev_used = 0;
+  }
   if (u->ev_used == 0) return;
   cudaDeviceSynchronize();
   for (size_t i = 0; i < u->ev_cls.size(); i++) {
@@ -451,6 +476,41 @@ static int muon_sharded(pl_update* u, double lr, cudaStream_t st) {
   return PL_OK;
 }
 
+// Data parallel: the summed gradient of layer l's block [W_l | b_l] (contiguous in the flat layout) is
+// all-reduced on the comm stream once the compute stream has finished it. b_l is complete before
+// W_l: the head's bias in the PPO epilogue, every other bias in the data-gradient epilogue of the layer
+// above. The compute stream only waits for the all-reduces before the gradient norm (comm_wait).
+static int comm_block(pl_update* u, int l, cudaStream_t st) {
+  const Layer& ly = u->layers[l];
+  const size_t n = (size_t)ly.out * ly.in + (size_t)ly.out;
+  PL_CUDA(cudaEventRecord(u->aev[l], st));
+  PL_CUDA(cudaStreamWaitEvent(u->ast, u->aev[l], 0));
+  if (u->prof) {
+    while (u->comm_ev.size() <= u->comm_ev_used) {
+      cudaEvent_t a, b;
+      cudaEventCreate(&a);
+      cudaEventCreate(&b);
+      u->comm_ev.push_back({a, b});
+      u->comm_ev_bytes.push_back(0);
+    }
+    cudaEventRecord(u->comm_ev[u->comm_ev_used].first, u->ast);
+  }
+  int rc = comm_allreduce_f32(u->d.comm, u->grad + ly.oW, n, u->ast);
+  if (u->prof) {
+    cudaEventRecord(u->comm_ev[u->comm_ev_used].second, u->ast);
+    u->comm_ev_bytes[u->comm_ev_used] = (double)n * sizeof(float);
+    u->comm_ev_used++;
+  }
+  return rc;
+}
+static int comm_wait(pl_update* u, cudaStream_t st) {
+  const int nl = (int)u->layers.size();
+  PL_CUDA(cudaEventRecord(u->aev[nl], u->ast));
+  Span sp(u, 7, st, 0);  // time the compute stream is held by the collectives it could not hide
+  PL_CUDA(cudaStreamWaitEvent(st, u->aev[nl], 0));
+  return PL_OK;
+}
+
 // The minibatch's rows of the resident columns (row k = column row idx[k]; its observation row is
 // oidx[k] when obs is not in column order; xdirect: the observation rows are already contiguous and
 // only the scalars are gathered), with the advantage statistics of the minibatch (all ranks' rows
@@ -472,6 +532,7 @@ static int gather_step(pl_update* u, const int* idx, const int* oidx, const void
 struct MbRows {
   long lo = 0;
   int Nmb = 0;
+  long nglob = 0;  // rows of the minibatch over all ranks
   const int* idx = nullptr;
   const int* oidx = nullptr;
   const void* xdirect = nullptr;
@@ -482,16 +543,24 @@ static bool minibatch_rows(const pl_update* u, size_t e, size_t m, MbRows* r) {
   long hi = (m + 1 == d.numMB) ? (long)d.NT : (long)(m + 1) * u->mbSize;
   if (hi > (long)d.NT) hi = (long)d.NT;
   if (hi <= lo) return false;
-  r->lo = lo;
-  r->Nmb = (int)(hi - lo);
-  r->idx = u->perm + e * d.NT + lo;
+  long a = lo, b = hi;
+  r->nglob = hi - lo;
+  if (u->dp && u->split) {  // this rank's share of the one global minibatch
+    a = lo + (hi - lo) * d.rank / d.world;
+    b = lo + (hi - lo) * (d.rank + 1) / d.world;
+  } else if (u->dp) {  // every rank its own rollout: the all-rank minibatch is world equal parts
+    r->nglob = (hi - lo) * d.world;
+  }
+  r->lo = a;
+  r->Nmb = (int)(b - a);
+  r->idx = u->perm + e * d.NT + a;
   r->oidx = nullptr;
   r->xdirect = nullptr;
   if (u->obs_epoch0) {
     if (e == 0)
-      r->xdirect = (const __nv_bfloat16*)u->obs + lo * u->Dp;
+      r->xdirect = (const __nv_bfloat16*)u->obs + a * u->Dp;
     else
-      r->oidx = u->operm + e * d.NT + lo;
+      r->oidx = u->operm + e * d.NT + a;
   }
   return true;
 }
@@ -612,6 +681,7 @@ static int minibatch_fast(pl_update* u, const int* idx, const int* oidx, const v
       Span sp(u, 3, st, gf(ly.out, ly.in, Nmb));
       rc = wgrad_fast(u, dcur, ldd, ly.out, hprev, ldprev, ly.in, Nmb, u->grad + ly.oW, st);
     }
+    if (!rc && u->dp && u->overlap && !u->grad_only) rc = comm_block(u, l, st);
     if (rc) return rc;
     if (l == 0) break;
     // dZ_{l-1} = (dcur W_l) * act'(Z_{l-1})
@@ -643,13 +713,16 @@ static int minibatch_fast(pl_update* u, const int* idx, const int* oidx, const v
     dsel ^= 1;
   }
   if (u->grad_only) return PL_OK;
-  long Nglob = Nmb;
+  const long Nglob = u->dp ? u->nglob : Nmb;
   if (u->dp) {
-    // ---- data parallel: sum the gradient over ranks (the mean is over the all-rank minibatch)
-    Span sp(u, 7, st, 0);
-    rc = comm_allreduce_f32(d.comm, u->grad, u->P, st);
+    // ---- data parallel: the gradient summed over ranks (the mean is over the all-rank minibatch)
+    if (u->overlap) {
+      rc = comm_wait(u, st);
+    } else {
+      Span sp(u, 7, st, 0);
+      rc = comm_allreduce_f32(d.comm, u->grad, u->P, st);
+    }
     if (rc) return rc;
-    Nglob = (long)Nmb * d.world;
   }
   // ---- clip to the mean gradient, then Muon on every layer
   {
@@ -756,11 +829,10 @@ static int minibatch_tight(pl_update* u, const int* idx, int Nmb, double lr, boo
     dsel ^= 1;
   }
   if (u->grad_only) return PL_OK;
-  long Nglob = Nmb;
+  const long Nglob = u->dp ? u->nglob : Nmb;
   if (u->dp) {
     rc = comm_allreduce_f32(d.comm, u->grad, u->P, st);
     if (rc) return rc;
-    Nglob = (long)Nmb * d.world;
   }
   rc = launch_gradnorm(u->grad, (long)u->P, 1.0 / (double)Nglob, d.maxGradNorm, u->gn_part, u->cc, st);
   if (rc) return rc;
@@ -856,6 +928,10 @@ int pl_update_create(size_t handle, const pl_update_desc* desc, pl_update** out)
     }
     u->owner.assign(u->layers.size(), 0);
     pl_muon_shard_plan(rows.data(), cols.data(), rows.size(), d.world, u->owner.data());
+    u->overlap = g_dp_overlap;
+    cudaStreamCreateWithFlags(&u->ast, cudaStreamNonBlocking);
+    u->aev.resize(u->layers.size() + 1);
+    for (auto& e : u->aev) cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
   } else {
     u->owner.assign(u->layers.size(), 0);
   }
@@ -876,6 +952,12 @@ int pl_update_destroy(pl_update* u) {
   if (!u) return PL_OK;
   cudaDeviceSynchronize();
   for (cudaEvent_t e : u->ev) cudaEventDestroy(e);
+  for (cudaEvent_t e : u->aev) cudaEventDestroy(e);
+  for (auto& p : u->comm_ev) {
+    cudaEventDestroy(p.first);
+    cudaEventDestroy(p.second);
+  }
+  if (u->ast) cudaStreamDestroy(u->ast);
   if (u->cev) cudaEventDestroy(u->cev);
   if (u->sev) cudaEventDestroy(u->sev);
   if (u->cst) cudaStreamDestroy(u->cst);
@@ -1119,6 +1201,8 @@ int pl_update_profile(pl_update* u, int on) {
     for (int i = 0; i < 8; i++) u->prof_ms[i] = u->prof_flops[i] = u->prof_launch[i] = 0;
     u->ev_used = 0;
     u->ev_cls.clear();
+    u->comm_ms = u->comm_bytes = u->comm_launches = 0;
+    u->comm_ev_used = 0;
   }
   u->prof = on != 0;
   return PL_OK;
@@ -1132,6 +1216,24 @@ int pl_update_profile_read(pl_update* u, double ms[8], double flops[8], double l
     if (flops) flops[i] = u->prof_flops[i];
     if (launches) launches[i] = u->prof_launch[i];
   }
+  return PL_OK;
+}
+
+int pl_update_comm_profile_read(pl_update* u, double* ms, double* bytes, double* launches) {
+  PL_REQUIRE(u != nullptr, PL_ERR_INVALID, "pl_update_comm_profile_read: NULL session");
+  prof_collect(u);
+  if (ms) *ms = u->comm_ms;
+  if (bytes) *bytes = u->comm_bytes;
+  if (launches) *launches = u->comm_launches;
+  return PL_OK;
+}
+
+int pl_update_split_minibatch(pl_update* u, int on) {
+  PL_REQUIRE(u != nullptr, PL_ERR_INVALID, "pl_update_split_minibatch: NULL session");
+  if (on && u->dp)
+    PL_REQUIRE(u->mbSize >= u->d.world, PL_ERR_INVALID,
+               "split minibatch: %ld rows per minibatch for %d ranks", u->mbSize, u->d.world);
+  u->split = on != 0;
   return PL_OK;
 }
 
@@ -1160,7 +1262,9 @@ int pl_update_run(pl_update* u, double lr, void* stream) {
     for (size_t m = 0; m < d.numMB; m++) {
       MbRows mr;
       if (!minibatch_rows(u, e, m, &mr)) continue;
-      const long lo = mr.lo, hi = mr.lo + mr.Nmb;
+      u->nglob = mr.nglob;
+      // the first-epoch upload brings every row of the minibatch (later epochs read them all)
+      const long lo = (long)m * u->mbSize, hi = (m + 1 == d.numMB) ? (long)d.NT : (long)(m + 1) * u->mbSize;
       const int Nmb = mr.Nmb;
       const bool last = (e + 1 == d.epochs) && (m + 1 == d.numMB);
       if (upl && e == 0) {
@@ -1540,6 +1644,7 @@ extern "C" int pl_test_update_gather(pl_update* u, size_t epoch, size_t mb, void
   MbRows mr;
   *nmb = 0;
   if (!minibatch_rows(u, epoch, mb, &mr)) return PL_OK;
+  u->nglob = mr.nglob;
   int rc = gather_step(u, mr.idx, mr.oidx, mr.xdirect, mr.Nmb, st);
   if (rc) return rc;
   PL_CUDA(cudaStreamSynchronize(st));
@@ -1554,4 +1659,12 @@ extern "C" int pl_test_update_gather(pl_update* u, size_t epoch, size_t mb, void
   if (olp) PL_CUDA(cudaMemcpy(olp, u->mb_olp, n * sizeof(float), cudaMemcpyDeviceToHost));
   if (ov && u->mb_ov) PL_CUDA(cudaMemcpy(ov, u->mb_ov, n * sizeof(float), cudaMemcpyDeviceToHost));
   return PL_OK;
+}
+
+// Test hook: 1 = sessions created afterwards all-reduce the gradient per layer on a second stream under
+// the backward pass (the default), 0 = one all-reduce of the whole gradient after it; < 0 queries.
+extern "C" int pl_test_dp_overlap(int mode) {
+  const int prev = g_dp_overlap ? 1 : 0;
+  if (mode >= 0) g_dp_overlap = mode != 0;
+  return prev;
 }

@@ -1,10 +1,10 @@
 """Host-side logic of the data-parallel update, on CPU.
 
 * pl_muon_shard_plan: which rank orthogonalises which matrix (every rank must derive the same plan).
-* The decomposition the library implements with NCCL, run here as world_size-2 gloo ranks on the
-  oracle: each rank gathers its own rows of the minibatch, the advantage (sum, sum of squares,
-  count) and the summed gradients are all-reduced, and the result equals the single-process
-  minibatch of all rows.
+* The decomposition the library implements with NCCL, run here as gloo ranks on the oracle (2 and 3
+  ranks, uneven shares): each rank takes rows [n*r/R, n*(r+1)/R) of the one minibatch (the
+  strong-scaling split), the advantage (sum, sum of squares, count) and the summed gradients are
+  all-reduced, and the result equals the single-process minibatch of all rows.
 """
 import ctypes as C
 import os
@@ -91,9 +91,9 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_data_parallel_decomposition_equals_full_minibatch_gloo():
-    world = 2
-    port = 29500 + os.getpid() % 1000
+@pytest.mark.parametrize("world", [2, 3])
+def test_data_parallel_decomposition_equals_full_minibatch_gloo(world):
+    port = 29500 + os.getpid() % 1000 + 7 * world
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]

@@ -49,7 +49,7 @@ def init_pm():
     return P, pm
 
 
-def run_update(L_, handle, NT, world, rank, comm, cols, perm, bf16):
+def run_update(L_, handle, NT, world, rank, comm, cols, perm, bf16, split=False):
     dp = C.POINTER(C.c_double)
     vp = C.c_void_p
     L_.pl_update_create.argtypes = [C.c_size_t, C.POINTER(Desc), C.POINTER(vp)]
@@ -61,6 +61,9 @@ def run_update(L_, handle, NT, world, rank, comm, cols, perm, bf16):
              rank=rank, world=world, comm=comm)
     u = vp()
     assert L_.pl_update_create(handle, C.byref(d), C.byref(u)) == 0, L_.pl_last_error()
+    if split:
+        L_.pl_update_split_minibatch.argtypes = [vp, C.c_int]
+        assert L_.pl_update_split_minibatch(u, 1) == 0, L_.pl_last_error()
     arrs = [np.ascontiguousarray(x, dtype=np.float64) for x in list(cols) + [perm]]
     obs, acts, adv, ret, olp, ov, pr = arrs
     rc = L_.pl_update_set_columns(u, obs.ctypes.data, acts.ctypes.data, adv.ctypes.data, ret.ctypes.data,
@@ -146,3 +149,77 @@ def test_two_rank_update_equals_union_minibatch(bf16, tol):
         assert p.exitcode == 0
     assert same, "ranks disagree"
     assert reldelta < tol, (maxabs, reldelta)
+
+
+def _rank_split(rank, port, bf16, q):
+    """Strong-scaling form: both ranks hold the same rollout and split every minibatch; the gradient is
+    all-reduced per layer under the backward pass (and, for comparison, in one piece after it)."""
+    import torch.distributed as dist
+
+    import pufferlean_b200 as plb
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    L_ = plb.lib()
+    L_.pl_set_device(rank)
+    L_.pl_test_dp_overlap.argtypes = [C.c_int]
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        ident = (C.c_uint8 * 128)()
+        if rank == 0:
+            assert L_.pl_comm_unique_id(ident) == 0
+        box = [bytes(ident)]
+        dist.broadcast_object_list(box, src=0)
+        ident = (C.c_uint8 * 128)(*box[0])
+        comm = C.c_void_p()
+        L_.pl_comm_create.argtypes = [C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]
+        assert L_.pl_comm_create(rank, WORLD, ident, C.byref(comm)) == 0, L_.pl_last_error()
+        P, pm = init_pm()
+        cols = columns(0)
+        perm = plb.shuffle_perm(NT_R, E, 700)
+        outs = []
+        for overlap in (1, 0):
+            prev = L_.pl_test_dp_overlap(overlap)
+            h = plb.policy_load(pm, P)
+            run_update(L_, h, NT_R, WORLD, rank, comm, cols, perm, bf16, split=True)
+            outs.append(plb.policy_download(h, P))
+            plb.policy_free(h)
+            L_.pl_test_dp_overlap(prev)
+        both = [None] * WORLD
+        dist.all_gather_object(both, outs[0].tobytes())
+        if rank == 0:
+            h = plb.policy_load(pm, P)
+            run_update(L_, h, NT_R, 1, 0, None, cols, perm, bf16)
+            ref = plb.policy_download(h, P)
+            plb.policy_free(h)
+            a = np.frombuffer(both[0]), np.frombuffer(both[1])
+            q.put((bool(np.array_equal(a[0], a[1])), bool(np.array_equal(outs[0], outs[1])),
+                   float(np.linalg.norm(a[0][:P] - ref[:P]) / max(np.linalg.norm(ref[:P] - pm[:P]), 1e-30))))
+        L_.pl_comm_destroy.argtypes = [C.c_void_p]
+        L_.pl_comm_destroy(comm)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("bf16,tol", [(0, 1e-4), (1, 0.15)])
+def test_two_rank_split_minibatch_equals_single_gpu_update(bf16, tol):
+    """Two ranks splitting each minibatch of one rollout run the single-GPU update: same result up to
+    the order of the gradient sum (same tolerances as above); ranks bit-identical; the overlapped
+    per-layer all-reduce gives the same bits as one all-reduce after the backward pass."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29650 + os.getpid() % 300 + bf16
+    procs = [ctx.Process(target=_rank_split, args=(r, port, bf16, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    same, overlap_same, reldelta = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert same, "ranks disagree"
+    assert overlap_same, "overlapped all-reduce changed the result"
+    assert reldelta < tol, reldelta
