@@ -200,7 +200,7 @@ typedef struct {
   double wd, mu, eps, vfCoef, entCoef, clipEps, vfClip, maxGradNorm;
   uint8_t bf16;
   uint8_t use_old_values; /* value clip needs the old-value column */
-  /* data-parallel group: rank/world; comm = an ncclComm_t created by the caller, or NULL at world 1 */
+  /* data-parallel group: rank/world; comm = a communicator from pl_comm_create, or NULL at world 1 */
   int rank, world;
   void* comm;
 } pl_update_desc;
@@ -270,8 +270,23 @@ int pl_update_destroy(pl_update* u);
  * has finished it); each weight matrix is orthogonalised by one owner rank (pl_muon_shard_plan) and the
  * results are broadcast; every rank then applies the identical step. */
 int pl_comm_unique_id(uint8_t id[128]);
+/* Creates this rank's communicator non-blocking and polls it with the deadline of pl_comm_set_timeout:
+ * a peer that never joins makes it fail with PL_ERR_COMM (the half-made communicator is aborted). */
 int pl_comm_create(int rank, int world, const uint8_t id[128], void** comm);
 int pl_comm_destroy(void* comm);
+/* Deadline of every blocking step of the communicator (creation, an enqueue that answers "in
+ * progress", pl_comm_wait), in seconds; 600 by default. Applies to later calls in the process. */
+int pl_comm_set_timeout(double seconds);
+/* Watchdog of enqueued work: waits until `stream` has finished while polling the communicator's
+ * asynchronous error state. An error (a peer that died, a network error) or the deadline aborts the
+ * communicator (ncclCommAbort, which also releases NCCL kernels still waiting for a peer) and returns
+ * PL_ERR_COMM. Every later call on an aborted communicator, and every update session or MinGRU state
+ * that uses it, fails with PL_ERR_COMM before enqueuing anything. */
+int pl_comm_wait(void* comm, void* stream);
+/* Aborts the communicator (e.g. after the host learned that a peer left); idempotent. */
+int pl_comm_abort(void* comm);
+/* 1 if the communicator was aborted, 0 if not, -1 if it is not a communicator of this library. */
+int pl_comm_aborted(void* comm);
 /* Owner rank of each of nmat matrices (rows[i] x cols[i]) for the sharded Newton-Schulz: greedy
  * longest-processing-time by 4 m^2 n + 2 m^3 flops. Deterministic. */
 int pl_muon_shard_plan(const size_t* rows, const size_t* cols, size_t nmat, int world, int* owner);

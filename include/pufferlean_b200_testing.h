@@ -59,6 +59,13 @@ int pl_test_update_gather(struct pl_update* u, size_t epoch, size_t mb, void* ro
  * while the backward pass continues (the default), 0 = one all-reduce of the whole gradient after the
  * backward pass; a negative mode only queries. Returns the previous mode. */
 int pl_test_dp_overlap(int mode);
+/* Replaces NCCL and the stream query used by pl_comm_* with host-side fakes, for failure tests without a
+ * GPU: 1 = creation never completes (a peer that never joins), 2 = a peer fails once the communicator
+ * is up (asynchronous-error queries report it), 3 = enqueued work never completes, 4 = a healthy
+ * communicator; 0 = the real library. A negative mode only queries. Returns the previous mode. */
+int pl_test_comm_fake(int mode);
+/* Number of communicator aborts the fakes have received. */
+int pl_test_comm_fake_aborts(void);
 /* Reads and clears the device-side bounded-wait error word (0 = none). */
 int pl_test_device_error(unsigned* code);
 

@@ -936,7 +936,7 @@ struct pl_mg {
   uint64_t gnodes = 0;
   unsigned long long* rng_dev = nullptr;
   bool have_work = false;
-  // data parallelism: an ncclComm_t from pl_comm_create, this rank and the world size
+  // data parallelism: a communicator from pl_comm_create, this rank and the world size
   void* comm = nullptr;
   int rank = 0, world = 1;
   size_t shadow_src = 0;  // handle whose weights the shadows hold (0 = none / host params)
@@ -1729,6 +1729,8 @@ int pl_mg_set_comm(pl_mg* s, void* comm, int rank, int world) {
   PL_REQUIRE(s != nullptr && world >= 1 && rank >= 0 && rank < world, PL_ERR_INVALID,
              "pl_mg_set_comm: bad rank %d / world %d", rank, world);
   PL_REQUIRE(world == 1 || comm != nullptr, PL_ERR_INVALID, "pl_mg_set_comm: world %d needs a communicator", world);
+  PL_REQUIRE(world == 1 || pl_comm_aborted(comm) == 0, PL_ERR_INVALID,
+             "pl_mg_set_comm: not a live communicator from pl_comm_create");
   s->comm = world > 1 ? comm : nullptr;
   s->rank = rank;
   s->world = world;
@@ -2116,6 +2118,8 @@ int pl_mg_update(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hype
                  uint64_t* rng, double lr, void* stream) {
   using namespace pl;
   PL_REQUIRE(s && net && h && rng && handle, PL_ERR_INVALID, "pl_mg_update: NULL argument");
+  PL_REQUIRE(!s->comm || pl_comm_aborted(s->comm) == 0, PL_ERR_COMM,
+             "pl_mg_update: the communicator was aborted (or is not one of this library)");
   int rc = check_net(net);
   if (!rc) rc = check_heads(s, net);
   if (rc) return rc;

@@ -917,9 +917,10 @@ int pl_update_create(size_t handle, const pl_update_desc* desc, pl_update** out)
   build_layout(u);
   u->dp = d.world > 1;
   if (u->dp) {
-    if (!d.comm || d.rank < 0 || d.rank >= d.world) {
+    if (!d.comm || d.rank < 0 || d.rank >= d.world || pl_comm_aborted(d.comm) != 0) {
       delete u;
-      return set_error(PL_ERR_INVALID, "data-parallel session needs a communicator and 0 <= rank < world");
+      return set_error(PL_ERR_INVALID, "data-parallel session needs a live communicator from pl_comm_create and "
+                                       "0 <= rank < world");
     }
     std::vector<size_t> rows, cols;
     for (auto& ly : u->layers) {
@@ -1239,6 +1240,8 @@ int pl_update_split_minibatch(pl_update* u, int on) {
 
 int pl_update_run(pl_update* u, double lr, void* stream) {
   PL_REQUIRE(u != nullptr, PL_ERR_INVALID, "pl_update_run: NULL session");
+  PL_REQUIRE(!u->dp || pl_comm_aborted(u->d.comm) == 0, PL_ERR_COMM,
+             "pl_update_run: the session's communicator was aborted (or is not one of this library)");
   cudaStream_t st = (cudaStream_t)stream;
   const pl_update_desc& d = u->d;
   const uint64_t l0 = pl_kernel_launch_count();
