@@ -352,6 +352,12 @@ int pl_mg_stamp_step(pl_mg* s, size_t step, size_t e0, size_t ne, const double* 
                      const double* val, const float* obs, size_t D, void* stream);
 int pl_mg_stamp_finish(pl_mg* s, const double* rew, const double* term, const double* boot, void* stream);
 int pl_mg_take_stamped(pl_mg* s, int* stamped);
+/* Resident chaining (the reference's g_mgchain protocol, ffi/puffercuda.cu:255-289): a rollout that keeps
+ * its observations and recurrent state resident across updates stamps (N envs, obs D, L*H state);
+ * N = 0 clears the stamp. pl_mg_chain_ready reports whether the stamp matches a query (the trainer then
+ * passes empty obs0 / state0 to that rollout). */
+int pl_mg_chain_stamp(pl_mg* s, size_t N, size_t D, size_t LH);
+int pl_mg_chain_ready(pl_mg* s, size_t N, size_t D, size_t LH, int* ready);
 /* The same scatters on caller-owned columns (the feed-forward path's obs trajectory and columns for
  * pl_update_set_columns_dev): src holds ne rows of `width` values for step `step`, written to rows
  * e*T + step of col [N*T x width]; a plane is step-major [T x N]. */

@@ -26,6 +26,15 @@ lean_obj_res lean_cuda_muon_stepmat(lean_obj_arg W, lean_obj_arg G, lean_obj_arg
 lean_obj_res lean_cuda_mlp_ppo_grad(lean_obj_arg params, lean_obj_arg obs, lean_obj_arg acts, lean_obj_arg advs,
                                     lean_obj_arg rets, lean_obj_arg olps, size_t N, size_t H, size_t D, size_t A,
                                     double vf, double ent, double clip, uint8_t bf16);
+/* cudaMlpPpoGradMDFFI / cudaMlpPpoGradContFFI, CUDA.lean:93-106; replace ffi/puffercuda.cu:1570, 1873.
+ * Summed gradient g[P]: O = sum(headSizes) + 1 (acts N x K) or O = 2d + 1 (acts N x d). */
+lean_obj_res lean_cuda_mlp_ppo_grad_md(lean_obj_arg params, lean_obj_arg obsB, lean_obj_arg acts, lean_obj_arg advs,
+                                       lean_obj_arg rets, lean_obj_arg oldlps, lean_obj_arg headSizes, size_t N,
+                                       size_t H, size_t D, size_t K, double vfCoef, double entCoef, double clipEps,
+                                       uint8_t bf16);
+lean_obj_res lean_cuda_mlp_ppo_grad_cont(lean_obj_arg params, lean_obj_arg obsB, lean_obj_arg acts, lean_obj_arg advs,
+                                         lean_obj_arg rets, lean_obj_arg oldlps, size_t N, size_t H, size_t D, size_t d,
+                                         double vfCoef, double entCoef, double clipEps, uint8_t bf16);
 /* cudaAdvNormalizeFFI, CUDA.lean:50-52; replaces ffi/puffercuda.cu:836-855 */
 lean_obj_res lean_cuda_adv_normalize(lean_obj_arg adv, size_t n);
 /* cudaTrainStepFFI, CUDA.lean:61-63; replaces ffi/puffercuda.cu:988-1080 */
@@ -111,6 +120,8 @@ lean_obj_res lean_cuda_mg_prep(lean_obj_arg rew, lean_obj_arg term, lean_obj_arg
 /* cudaMgColsReadyFFI, CUDA.lean:361-362; replaces ffi/puffercuda.cu:305-309 */
 lean_obj_res lean_cuda_mg_cols_ready(size_t N, size_t T, lean_obj_arg w);
 /* cudaMgVtraceFFI, CUDA.lean:159-160; replaces ffi/puffercuda.cu:389-399 */
+/* cudaMgChainReadyFFI, CUDA.lean:338; replaces ffi/puffercuda.cu:284-289 (IO Bool). */
+lean_obj_res lean_cuda_mg_chain_ready(size_t N, size_t D, size_t LH, lean_obj_arg w);
 lean_obj_res lean_cuda_mg_vtrace(size_t N, size_t T, double gamma, double lam, double rhoClip, double cClip,
                                  lean_obj_arg w);
 /* cudaMgVtracePrioFFI, CUDA.lean:369-371; replaces ffi/puffercuda.cu:443-470 */

@@ -90,6 +90,51 @@ LEAN_EXPORT lean_obj_res lean_cuda_mlp_ppo_grad(lean_obj_arg pa, lean_obj_arg ob
   return rc ? pure_fail(out, "lean_cuda_mlp_ppo_grad") : out;
 }
 
+/* Multi-discrete and Gaussian twins of lean_cuda_mlp_ppo_grad (CUDA.lean:93-106): the summed gradient
+ * g[P] of the one-hidden-layer network with O = sum(headSizes) + 1 or O = 2d + 1 outputs. */
+LEAN_EXPORT lean_obj_res lean_cuda_mlp_ppo_grad_md(lean_obj_arg pa, lean_obj_arg obs, lean_obj_arg acts,
+                                                   lean_obj_arg advs, lean_obj_arg rets, lean_obj_arg olps,
+                                                   lean_obj_arg hs, size_t N, size_t H, size_t D, size_t K, double vf,
+                                                   double ent, double clip, uint8_t bf16) {
+  size_t A = 0;
+  int bad = fan(hs) < K;
+  for (size_t i = 0; !bad && i < K; i++) {
+    const double h = fa(hs)[i];
+    if (!(h >= 1.0)) bad = 1;
+    else A += (size_t)h;
+  }
+  const size_t O = A + 1;
+  lean_obj_res out = new_fa(H * D + H + O * H + O);
+  int rc = bad ? -1
+               : pl_mlp_ppo_grad_wide(fa(pa), fa(obs), fa(acts), fa(advs), fa(rets), fa(olps), NULL, N, H, D, O, K, 1,
+                                      fa(hs), vf, ent, clip, 0.0, bf16, fa(out));
+  lean_dec(pa);
+  lean_dec(obs);
+  lean_dec(acts);
+  lean_dec(advs);
+  lean_dec(rets);
+  lean_dec(olps);
+  lean_dec(hs);
+  return rc ? pure_fail(out, "lean_cuda_mlp_ppo_grad_md") : out;
+}
+
+LEAN_EXPORT lean_obj_res lean_cuda_mlp_ppo_grad_cont(lean_obj_arg pa, lean_obj_arg obs, lean_obj_arg acts,
+                                                     lean_obj_arg advs, lean_obj_arg rets, lean_obj_arg olps, size_t N,
+                                                     size_t H, size_t D, size_t d, double vf, double ent, double clip,
+                                                     uint8_t bf16) {
+  const size_t O = 2 * d + 1;
+  lean_obj_res out = new_fa(H * D + H + O * H + O);
+  int rc = pl_mlp_ppo_grad_wide(fa(pa), fa(obs), fa(acts), fa(advs), fa(rets), fa(olps), NULL, N, H, D, O, d, 2, NULL,
+                                vf, ent, clip, 0.0, bf16, fa(out));
+  lean_dec(pa);
+  lean_dec(obs);
+  lean_dec(acts);
+  lean_dec(advs);
+  lean_dec(rets);
+  lean_dec(olps);
+  return rc ? pure_fail(out, "lean_cuda_mlp_ppo_grad_cont") : out;
+}
+
 LEAN_EXPORT lean_obj_res lean_cuda_adv_normalize(lean_obj_arg adv, size_t n) {
   lean_obj_res out = new_fa(n);
   int rc = pl_adv_normalize(fa(adv), n, fa(out));
@@ -399,6 +444,16 @@ LEAN_EXPORT lean_obj_res lean_cuda_mg_cols_ready(size_t N, size_t T, lean_obj_ar
   (void)w;
   int r = 0;
   if (g_mg && g_mg_N == N && g_mg_T == T && pl_mg_take_stamped(g_mg, &r)) r = 0;
+  return lean_io_result_mk_ok(lean_box(r ? 1 : 0));
+}
+
+/* Resident chaining (CUDA.lean:338, ffi/puffercuda.cu:255-289): true when the rollout that fed this
+ * session stamped that it keeps its observations and recurrent state resident for (N, D, L*H)
+ * (pl_mg_chain_stamp), so the trainer may pass empty obs0 / state0 to the next rollout. */
+LEAN_EXPORT lean_obj_res lean_cuda_mg_chain_ready(size_t N, size_t D, size_t LH, lean_obj_arg w) {
+  (void)w;
+  int r = 0;
+  if (g_mg && pl_mg_chain_ready(g_mg, N, D, LH, &r)) r = 0;
   return lean_io_result_mk_ok(lean_box(r ? 1 : 0));
 }
 

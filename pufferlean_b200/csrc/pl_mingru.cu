@@ -864,6 +864,7 @@ struct MgShape {
 struct pl_mg {
   int dev = 0;
   long N = 0, T = 0;
+  long chain_N = 0, chain_D = 0, chain_LH = 0;  // resident-chaining stamp of the rollout (N = 0: none)
   std::vector<void*> allocs;  // columns and sampling (freed at destroy)
   // resident columns, rows e*T + t (f64)
   double *rew = nullptr, *term = nullptr, *act = nullptr, *logp = nullptr, *val0 = nullptr, *boot = nullptr;
@@ -1828,6 +1829,22 @@ int pl_mg_take_stamped(pl_mg* s, int* stamped) {
   PL_REQUIRE(s && stamped, PL_ERR_INVALID, "pl_mg_take_stamped: NULL argument");
   *stamped = (s->stamped && s->cols_valid) ? 1 : 0;
   s->stamped = false;
+  return PL_OK;
+}
+
+int pl_mg_chain_stamp(pl_mg* s, size_t N, size_t D, size_t LH) {
+  using namespace pl;
+  PL_REQUIRE(s != nullptr, PL_ERR_INVALID, "pl_mg_chain_stamp: NULL session");
+  s->chain_N = (long)N;
+  s->chain_D = N ? (long)D : 0;
+  s->chain_LH = N ? (long)LH : 0;
+  return PL_OK;
+}
+
+int pl_mg_chain_ready(pl_mg* s, size_t N, size_t D, size_t LH, int* ready) {
+  using namespace pl;
+  PL_REQUIRE(s && ready, PL_ERR_INVALID, "pl_mg_chain_ready: NULL argument");
+  *ready = (s->chain_N > 0 && s->chain_N == (long)N && s->chain_D == (long)D && s->chain_LH == (long)LH) ? 1 : 0;
   return PL_OK;
 }
 

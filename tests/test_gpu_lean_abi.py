@@ -174,3 +174,56 @@ def test_lean_mingru_trainer_sequence_against_reference(lib, monkeypatch):
     ref = np.load(os.path.join(GOLD, "mingru_update.npz"))["out"]
     d_ref, d_out = ref[:P] - k["pm0"][:P], out[:P] - k["pm0"][:P]
     assert np.linalg.norm(d_out - d_ref) / np.linalg.norm(d_ref) < 1e-3
+
+
+@pytest.mark.parametrize("bf16", [0, 1])
+def test_lean_wide_gradients_md_and_cont(lib, bf16):
+    """lean_cuda_mlp_ppo_grad_md / _cont (the verify modes' wide-head gradients) against the plain ABI
+    (same kernels: bit-identical) and, in the tight tier, the oracle."""
+    g = np.random.default_rng(31 + bf16)
+    N, D, H = 700, 12, 64
+    for mode in (1, 2):
+        hs = np.array([3.0, 5.0, 2.0]) if mode == 1 else None
+        W = 3 if mode == 1 else 4
+        O_ = int(hs.sum()) + 1 if mode == 1 else 2 * W + 1
+        P = H * D + H + O_ * H + O_
+        params = g.uniform(-0.2, 0.2, P)
+        obs = g.standard_normal(N * D)
+        if mode == 1:
+            acts = np.stack([g.integers(0, int(h), N) for h in hs], 1).astype(float).ravel()
+        else:
+            acts = g.standard_normal(N * W)
+        adv, ret = g.standard_normal(N), g.standard_normal(N)
+        olp = g.normal(-2.0, 0.3, N)
+        if mode == 1:
+            out = O.ref_call(lib, "lean_cuda_mlp_ppo_grad_md", VP, FA(params), FA(obs), FA(acts), FA(adv), FA(ret),
+                             FA(olp), FA(hs), N, H, D, W, 0.5, 0.01, 0.2, ("u8", bf16))
+        else:
+            out = O.ref_call(lib, "lean_cuda_mlp_ppo_grad_cont", VP, FA(params), FA(obs), FA(acts), FA(adv), FA(ret),
+                             FA(olp), N, H, D, W, 0.5, 0.01, 0.2, ("u8", bf16))
+        got = O.read_float_array(out)
+        want = plb.cuda_mlp_ppo_grad_wide(params, obs, acts, adv, ret, olp, None, N, H, D, O_, W, mode, hs, 0.5, 0.01,
+                                          0.2, 0.0, bf16)
+        assert got.size == P and np.array_equal(got, want)
+        if not bf16:
+            ref, _, _ = O.mlp_ppo_grad_wide(params, obs, acts, adv, ret, olp, N, D, H, O_, W, mode, hs=hs)
+            assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-5
+
+
+def test_lean_mg_chain_ready_follows_the_rollout_stamp(lib):
+    N, T, D, LH = 4, 8, 6, 32
+    r = O.ref_call(lib, "lean_cuda_mg_prep", VP, *[FA(np.zeros(N * T)) for _ in range(5)], FA(np.zeros(N)), N, T, 1,
+                   ("obj", 1))
+    assert O.ctor_tag(r) == 0
+    ready = lambda n, d, lh: O.ctor_field(O.ref_call(lib, "lean_cuda_mg_chain_ready", VP, n, d, lh, ("obj", 1)), 0)
+    box = lambda b: (b << 1) | 1  # lean_box
+    assert ready(N, D, LH) == box(0)
+    L = plb.lib()
+    lib.pl_lean_mg_session.restype = VP
+    L.pl_mg_chain_stamp.argtypes = [VP, C.c_size_t, C.c_size_t, C.c_size_t]
+    sess = lib.pl_lean_mg_session()
+    assert L.pl_mg_chain_stamp(sess, N, D, LH) == 0
+    assert ready(N, D, LH) == box(1)
+    assert ready(N, D + 1, LH) == box(0)
+    assert L.pl_mg_chain_stamp(sess, 0, 0, 0) == 0
+    assert ready(N, D, LH) == box(0)
