@@ -69,6 +69,12 @@ int pl_vtrace_f32_dev(const float* rew, const float* val, const float* term, con
 int pl_vtrace_f64_dev(const double* rew, const double* val, const double* term, const double* imp,
                       const double* bootv, size_t B, size_t T, double gamma, double lam, double rhoClip,
                       double cClip, double* adv, double* adv_l1, void* stream);
+/* The f64 scan in the fp32 form's warp-parallel order (one warp per segment, coalesced loads, affine
+ * maps composed by shuffles): not bit-identical to the sequential order, about 1e-15 relative. The
+ * recurrent update's bf16 tier uses it. No separate reference symbol (same semantics as above). */
+int pl_vtrace_f64_scan_dev(const double* rew, const double* val, const double* term, const double* imp,
+                           const double* bootv, size_t B, size_t T, double gamma, double lam, double rhoClip,
+                           double cClip, double* adv, double* adv_l1, void* stream);
 
 /* ------------------------------------------------------------------ host bookkeeping ---------- */
 

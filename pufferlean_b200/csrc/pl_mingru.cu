@@ -1608,8 +1608,13 @@ int ensure_sample(pl_mg* s, long Bmb) {
   return PL_OK;
 }
 
-int mg_vtrace_dev(pl_mg* s, double gamma, double lam, double rho, double c, cudaStream_t st) {
+// exact: the reference's sequential f64 order (bit-identical, one thread per segment); otherwise the
+// warp-parallel f64 scan (coalesced, about 1e-15 relative), which the bf16 tier's update uses.
+int mg_vtrace_dev(pl_mg* s, double gamma, double lam, double rho, double c, cudaStream_t st, bool exact = true) {
   PL_REQUIRE(s->cols_valid, PL_ERR_INVALID, "MinGRU: no columns (call pl_mg_set_columns first)");
+  if (!exact)
+    return pl_vtrace_f64_scan_dev(s->rew, s->value, s->term, s->ratio, s->boot, (size_t)s->N, (size_t)s->T, gamma,
+                                  lam, rho, c, s->adv, s->l1, st);
   return pl_vtrace_f64_dev(s->rew, s->value, s->term, s->ratio, s->boot, (size_t)s->N, (size_t)s->T, gamma, lam, rho,
                            c, s->adv, s->l1, st);
 }
@@ -1871,10 +1876,10 @@ int pl_mg_vtrace(pl_mg* s, double gamma, double lam, double rhoClip, double cCli
 
 static int mg_vtrace_prio_impl(pl_mg* s, double gamma, double lam, double rhoClip, double cClip, size_t mbSegs,
                                double prioAlpha, double annealBeta, uint64_t rng, bool rng_on_device,
-                               cudaStream_t st) {
+                               cudaStream_t st, bool exact = true) {
   using namespace pl;
   PL_REQUIRE(s != nullptr && mbSegs > 0 && mbSegs < (1u << 30), PL_ERR_INVALID, "pl_mg_vtrace_prio: bad argument");
-  int rc = mg_vtrace_dev(s, gamma, lam, rhoClip, cClip, st);
+  int rc = mg_vtrace_dev(s, gamma, lam, rhoClip, cClip, st, exact);
   if (rc) return rc;
   rc = ensure_sample(s, (long)mbSegs);
   if (rc) return rc;
@@ -2058,7 +2063,7 @@ static int mg_minibatch(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_
                         uint64_t rng, bool rng_on_device, double lr, cudaStream_t st) {
   const double gscale = 1.0 / ((double)mbSegs * (double)s->T * (double)s->world);
   int rc = mg_vtrace_prio_impl(s, h->gamma, h->lam, h->rhoClip, h->cClip, mbSegs, h->prioAlpha, h->annealBeta, rng,
-                               rng_on_device, st);
+                               rng_on_device, st, /*exact=*/h->bf16 == 0);
   if (rc) return rc;
   rc = pl_mg_grad(s, net, handle, nullptr, nullptr, nullptr, mbSegs, h->vfCoef, h->entCoef, h->clipEps, h->vfClip,
                   h->bf16, st);

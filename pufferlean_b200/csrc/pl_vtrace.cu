@@ -3,11 +3,12 @@
 //  * exact tier (f64): the reference's sequential backward scan with its IEEE op order, every
 //    product and sum rounded on its own (__dmul_rn / __dadd_rn, no fused multiply-add), so the
 //    result is bit-identical to ffi/puffercuda.cu:69-90 (vector form) and :146-167 (MinGRU form).
-//  * fast tier (fp32): one warp per segment. Each lane owns a contiguous run of T/32 steps, loaded
-//    with vector loads; the recurrence A_t = delta_t + k_t * A_{t+1} is a composition of affine
-//    maps, so each lane folds its run into one map (k, delta), a 5-step shuffle suffix scan
-//    composes the maps of the lanes to its right, and the lane then replays its run backwards
-//    from the scanned boundary value. sum_t |A_t| per segment falls out of the same registers.
+//  * fast tier (fp32, and an f64 form for the recurrent update's bf16 tier): one warp per segment.
+//    Each lane owns a contiguous run of T/32 steps, loaded with vector loads; the recurrence
+//    A_t = delta_t + k_t * A_{t+1} is a composition of affine maps, so each lane folds its run into
+//    one map (k, delta), a 5-step shuffle suffix scan composes the maps of the lanes to its right,
+//    and the lane then replays its run backwards from the scanned boundary value. sum_t |A_t| per
+//    segment falls out of the same registers.
 #include "pl_common.cuh"
 #include "pl_runtime.h"
 
@@ -68,90 +69,136 @@ __global__ void vtrace_f64_kernel(const double* __restrict__ rew, const double* 
   }
 }
 
-// ---------------------------------------------------------------- fast fp32
-template <int EPL>
-__device__ __forceinline__ void load_run(const float* __restrict__ p, int t0, int T, bool vec, float (&x)[EPL],
-                                         float fill) {
+// ---------------------------------------------------------------- warp-per-segment scan (fp32 / f64)
+template <int EPL, typename F>
+__device__ __forceinline__ void load_run(const F* __restrict__ p, int t0, int T, bool vec, F (&x)[EPL], F fill) {
   if (vec && t0 + EPL <= T) {
-    if constexpr (EPL == 4) {
-      float4 q = *reinterpret_cast<const float4*>(p + t0);
-      x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
+    if constexpr (sizeof(F) == 4 && EPL == 2) {
+      const float2 q = *reinterpret_cast<const float2*>(p + t0);
+      x[0] = q.x;
+      x[1] = q.y;
       return;
-    } else if constexpr (EPL == 2) {
-      float2 q = *reinterpret_cast<const float2*>(p + t0);
-      x[0] = q.x; x[1] = q.y;
+    } else if constexpr (sizeof(F) == 4 && EPL % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < EPL; i += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(p + t0 + i);
+        x[i] = q.x;
+        x[i + 1] = q.y;
+        x[i + 2] = q.z;
+        x[i + 3] = q.w;
+      }
       return;
-    } else if constexpr (EPL == 8) {
-      float4 q0 = *reinterpret_cast<const float4*>(p + t0);
-      float4 q1 = *reinterpret_cast<const float4*>(p + t0 + 4);
-      x[0] = q0.x; x[1] = q0.y; x[2] = q0.z; x[3] = q0.w;
-      x[4] = q1.x; x[5] = q1.y; x[6] = q1.z; x[7] = q1.w;
+    } else if constexpr (sizeof(F) == 8 && EPL % 2 == 0) {
+#pragma unroll
+      for (int i = 0; i < EPL; i += 2) {
+        const double2 q = *reinterpret_cast<const double2*>(p + t0 + i);
+        x[i] = q.x;
+        x[i + 1] = q.y;
+      }
       return;
     }
   }
 #pragma unroll
   for (int e = 0; e < EPL; e++) x[e] = (t0 + e < T) ? p[t0 + e] : fill;
 }
+template <int EPL, typename F>
+__device__ __forceinline__ void store_run(F* __restrict__ p, int t0, int T, bool vec, const F (&x)[EPL]) {
+  if (vec && t0 + EPL <= T) {
+    if constexpr (sizeof(F) == 4 && EPL == 2) {
+      *reinterpret_cast<float2*>(p + t0) = make_float2(x[0], x[1]);
+      return;
+    } else if constexpr (sizeof(F) == 4 && EPL % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < EPL; i += 4)
+        *reinterpret_cast<float4*>(p + t0 + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+      return;
+    } else if constexpr (sizeof(F) == 8 && EPL % 2 == 0) {
+#pragma unroll
+      for (int i = 0; i < EPL; i += 2) *reinterpret_cast<double2*>(p + t0 + i) = make_double2(x[i], x[i + 1]);
+      return;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < EPL; e++)
+    if (t0 + e < T) p[t0 + e] = x[e];
+}
 
-template <int EPL, bool MINGRU>
-__global__ void __launch_bounds__(256) vtrace_f32_kernel(const float* __restrict__ rew, const float* __restrict__ val,
-                                                         const float* __restrict__ term, const float* __restrict__ imp,
-                                                         const float* __restrict__ bootv, float* __restrict__ adv,
-                                                         float* __restrict__ adv_l1, int B, int T, float gamma,
-                                                         float lam, float rhoClip, float cClip) {
+// Programmatic dependent launch: a scan may be launched before the kernel ahead of it in the stream has
+// finished (its launch and set-up overlap that kernel's tail); it waits for that kernel's results
+// before its first load and lets the next one start once its loads are done. Both are no-ops for a
+// plain launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// One warp per segment; lane l owns steps [l EPL, (l + 1) EPL) of the horizon. The backward recurrence
+// A_t = delta_t + k_t A_{t+1} is a chain of affine maps: each lane folds its run into one map, a 5-step
+// shuffle suffix scan composes the maps to its right, and the lane replays its run from the scanned
+// boundary value. Not the reference's sequential operation order (the f64 form agrees with it to
+// rounding, about 1e-15 relative; the exact tier is vtrace_f64_kernel).
+template <typename F, int EPL, bool MINGRU>
+__global__ void __launch_bounds__(256) vtrace_warp_kernel(const F* __restrict__ rew, const F* __restrict__ val,
+                                                          const F* __restrict__ term, const F* __restrict__ imp,
+                                                          const F* __restrict__ bootv, F* __restrict__ adv,
+                                                          F* __restrict__ adv_l1, int B, int T, F gamma, F lam,
+                                                          F rhoClip, F cClip) {
   const int lane = threadIdx.x & 31;
   const long seg = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (seg >= B) return;  // warp-uniform
+  pdl_wait();
+  if (seg >= B) {  // warp-uniform
+    pdl_release();
+    return;
+  }
   const long base = seg * T;
   const int t0 = lane * EPL;
   // vector loads need every row start aligned to the run width
-  constexpr uintptr_t ALIGN = EPL >= 4 ? 16 : EPL * 4;
+  constexpr uintptr_t ALIGN = EPL * sizeof(F) >= 16 ? 16 : EPL * sizeof(F);
   const uintptr_t orp = (uintptr_t)(rew + base) | (uintptr_t)(val + base) | (uintptr_t)(term + base) |
                         (imp ? (uintptr_t)(imp + base) : 0) | (uintptr_t)(adv + base);
   const bool vec = EPL > 1 && (T % EPL) == 0 && (orp % ALIGN) == 0;
-  float r[EPL], v[EPL], d[EPL], im[EPL];
-  load_run<EPL>(rew + base, t0, T, vec, r, 0.f);
-  load_run<EPL>(val + base, t0, T, vec, v, 0.f);
-  load_run<EPL>(term + base, t0, T, vec, d, 0.f);
+  F r[EPL], v[EPL], d[EPL], im[EPL];
+  load_run<EPL, F>(rew + base, t0, T, vec, r, F(0));
+  load_run<EPL, F>(val + base, t0, T, vec, v, F(0));
+  load_run<EPL, F>(term + base, t0, T, vec, d, F(0));
   if (imp)
-    load_run<EPL>(imp + base, t0, T, vec, im, 1.f);
+    load_run<EPL, F>(imp + base, t0, T, vec, im, F(1));
   else {
 #pragma unroll
-    for (int e = 0; e < EPL; e++) im[e] = 1.f;  // no importance ratios: rho = c = min(1, clip)
+    for (int e = 0; e < EPL; e++) im[e] = F(1);  // no importance ratios: rho = c = min(1, clip)
   }
+  const F boot = MINGRU ? bootv[seg] : F(0);
+  pdl_release();
   // value one step past this lane's run: the first value of the next lane (or the bootstrap)
-  float v_after = __shfl_down_sync(0xffffffffu, v[0], 1);
-  const float boot = MINGRU ? bootv[seg] : 0.f;
-  const float gl = gamma * lam;
-  float k[EPL], dl[EPL];
+  const F v_after = __shfl_down_sync(0xffffffffu, v[0], 1);
+  const F gl = gamma * lam;
+  F k[EPL], dl[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; e++) {
     const int t = t0 + e;
-    const float vn = (e + 1 < EPL) ? v[e + 1] : v_after;
-    const float rc = fminf(fmaxf(r[e], -1.f), 1.f);
-    const float rho = im[e] < rhoClip ? im[e] : rhoClip;
-    const float c = im[e] < cClip ? im[e] : cClip;
+    const F vn = (e + 1 < EPL) ? v[e + 1] : v_after;
+    const F rc = r[e] > F(1) ? F(1) : (r[e] < F(-1) ? F(-1) : r[e]);
+    const F rho = im[e] < rhoClip ? im[e] : rhoClip;
+    const F c = im[e] < cClip ? im[e] : cClip;
     if (t >= T) {  // past the horizon: identity map
-      k[e] = 1.f;
-      dl[e] = 0.f;
+      k[e] = F(1);
+      dl[e] = F(0);
     } else if (!MINGRU) {
-      const float nnt = (d[e] != 0.f) ? 0.f : 1.f;
+      const F nnt = (d[e] != F(0)) ? F(0) : F(1);
       if (t == T - 1) {  // A[T-1] = 0
-        k[e] = 0.f;
-        dl[e] = 0.f;
+        k[e] = F(0);
+        dl[e] = F(0);
       } else {
         dl[e] = rho * (rc + gamma * vn * nnt - v[e]);
         k[e] = gl * c * nnt;
       }
     } else {
-      const float nnt = (d[e] > 0.5f) ? 0.f : 1.f;
-      const float vnx = (t == T - 1) ? boot : vn;
+      const F nnt = (d[e] > F(0.5)) ? F(0) : F(1);
+      const F vnx = (t == T - 1) ? boot : vn;
       dl[e] = rho * rc + gamma * vnx * nnt - v[e];
-      k[e] = (t == T - 1) ? 0.f : gl * c * nnt;  // A_T enters as 0
+      k[e] = (t == T - 1) ? F(0) : gl * c * nnt;  // A_T enters as 0
     }
   }
   // fold this lane's run into one affine map F(x) = KK*x + DD (applied to A at the run's end)
-  float KK = 1.f, DD = 0.f;
+  F KK = F(1), DD = F(0);
 #pragma unroll
   for (int e = EPL - 1; e >= 0; e--) {
     DD = dl[e] + k[e] * DD;
@@ -160,40 +207,24 @@ __global__ void __launch_bounds__(256) vtrace_f32_kernel(const float* __restrict
   // inclusive suffix scan of maps over lanes: lane l -> F_l o F_{l+1} o ... o F_31
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
-    const float K2 = __shfl_down_sync(0xffffffffu, KK, off);
-    const float D2 = __shfl_down_sync(0xffffffffu, DD, off);
+    const F K2 = __shfl_down_sync(0xffffffffu, KK, off);
+    const F D2 = __shfl_down_sync(0xffffffffu, DD, off);
     if (lane + off < 32) {
       DD = DD + KK * D2;
       KK = KK * K2;
     }
   }
-  float A = __shfl_down_sync(0xffffffffu, DD, 1);  // value entering this run from the right
-  if (lane == 31) A = 0.f;
-  float out[EPL];
-  float l1 = 0.f;
+  F A = __shfl_down_sync(0xffffffffu, DD, 1);  // value entering this run from the right
+  if (lane == 31) A = F(0);
+  F out[EPL];
+  F l1 = F(0);
 #pragma unroll
   for (int e = EPL - 1; e >= 0; e--) {
     A = dl[e] + k[e] * A;
     out[e] = A;
-    if (t0 + e < T) l1 += fabsf(A);
+    if (t0 + e < T) l1 += A < F(0) ? -A : A;
   }
-  float* ad = adv + base;
-  if (vec && t0 + EPL <= T) {
-    if constexpr (EPL == 4) {
-      *reinterpret_cast<float4*>(ad + t0) = make_float4(out[0], out[1], out[2], out[3]);
-    } else if constexpr (EPL == 2) {
-      *reinterpret_cast<float2*>(ad + t0) = make_float2(out[0], out[1]);
-    } else if constexpr (EPL == 8) {
-      *reinterpret_cast<float4*>(ad + t0) = make_float4(out[0], out[1], out[2], out[3]);
-      *reinterpret_cast<float4*>(ad + t0 + 4) = make_float4(out[4], out[5], out[6], out[7]);
-    } else {
-      ad[t0] = out[0];
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < EPL; e++)
-      if (t0 + e < T) ad[t0 + e] = out[e];
-  }
+  store_run<EPL, F>(adv + base, t0, T, vec, out);
   if (adv_l1) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
@@ -201,23 +232,43 @@ __global__ void __launch_bounds__(256) vtrace_f32_kernel(const float* __restrict
   }
 }
 
-template <bool MINGRU>
-static int launch_f32(const float* rew, const float* val, const float* term, const float* imp, const float* bootv,
-                      int B, int T, float g, float l, float rho, float c, float* adv, float* l1, cudaStream_t st) {
+// Launch of the warp scan with programmatic stream serialisation allowed (see pdl_wait).
+template <typename F, int EPL, bool MINGRU>
+static cudaError_t launch_warp(dim3 grid, dim3 block, cudaStream_t st, const F* rew, const F* val, const F* term,
+                               const F* imp, const F* bootv, F* adv, F* l1, int B, int T, F g, F l, F rho, F c) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, vtrace_warp_kernel<F, EPL, MINGRU>, rew, val, term, imp, bootv, adv, l1, B, T, g, l,
+                            rho, c);
+}
+
+template <typename F, bool MINGRU>
+static int launch_scan(const F* rew, const F* val, const F* term, const F* imp, const F* bootv, int B, int T, F g,
+                       F l, F rho, F c, F* adv, F* l1, cudaStream_t st) {
   const int warps = 8;
   dim3 grid((unsigned)ceil_div(B, warps)), block(32 * warps);
+  cudaError_t e;
   if (T <= 32)
-    vtrace_f32_kernel<1, MINGRU><<<grid, block, 0, st>>>(rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
+    e = launch_warp<F, 1, MINGRU>(grid, block, st, rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
   else if (T <= 64)
-    vtrace_f32_kernel<2, MINGRU><<<grid, block, 0, st>>>(rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
+    e = launch_warp<F, 2, MINGRU>(grid, block, st, rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
   else if (T <= 128)
-    vtrace_f32_kernel<4, MINGRU><<<grid, block, 0, st>>>(rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
+    e = launch_warp<F, 4, MINGRU>(grid, block, st, rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
   else if (T <= 256)
-    vtrace_f32_kernel<8, MINGRU><<<grid, block, 0, st>>>(rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
+    e = launch_warp<F, 8, MINGRU>(grid, block, st, rew, val, term, imp, bootv, adv, l1, B, T, g, l, rho, c);
   else
-    return set_error(PL_ERR_UNSUPPORTED, "fp32 V-trace supports horizons up to 256 (T=%d)", T);
+    return set_error(PL_ERR_UNSUPPORTED, "the V-trace scan supports horizons up to 256 (T=%d)", T);
+  if (e != cudaSuccess) return check_cuda(e, "vtrace_warp_kernel launch");
   count_launch();
-  PL_LAUNCH("vtrace_f32_kernel");
+  PL_LAUNCH("vtrace_warp_kernel");
   return PL_OK;
 }
 
@@ -237,8 +288,18 @@ int vtrace_f64_launch(const double* rew, const double* val, const double* term, 
 int vtrace_f32_launch(const float* rew, const float* val, const float* term, const float* imp, const float* bootv,
                       int B, int T, double g, double l, double rho, double c, float* adv, float* l1,
                       cudaStream_t st) {
-  if (bootv) return launch_f32<true>(rew, val, term, imp, bootv, B, T, (float)g, (float)l, (float)rho, (float)c, adv, l1, st);
-  return launch_f32<false>(rew, val, term, imp, bootv, B, T, (float)g, (float)l, (float)rho, (float)c, adv, l1, st);
+  if (bootv)
+    return launch_scan<float, true>(rew, val, term, imp, bootv, B, T, (float)g, (float)l, (float)rho, (float)c, adv,
+                                    l1, st);
+  return launch_scan<float, false>(rew, val, term, imp, bootv, B, T, (float)g, (float)l, (float)rho, (float)c, adv,
+                                   l1, st);
+}
+
+int vtrace_f64_scan_launch(const double* rew, const double* val, const double* term, const double* imp,
+                           const double* bootv, int B, int T, double g, double l, double rho, double c, double* adv,
+                           double* l1, cudaStream_t st) {
+  if (bootv) return launch_scan<double, true>(rew, val, term, imp, bootv, B, T, g, l, rho, c, adv, l1, st);
+  return launch_scan<double, false>(rew, val, term, imp, bootv, B, T, g, l, rho, c, adv, l1, st);
 }
 
 static int vtrace_host(const double* rew, const double* val, const double* term, const double* imp,
@@ -286,6 +347,15 @@ int pl_vtrace_f32_dev(const float* rew, const float* val, const float* term, con
   PL_REQUIRE(B < (1u << 31) && T < (1u << 31), PL_ERR_INVALID, "V-trace extents too large");
   return pl::vtrace_f32_launch(rew, val, term, imp, bootv, (int)B, (int)T, gamma, lam, rhoClip, cClip, adv, adv_l1,
                                (cudaStream_t)stream);
+}
+
+int pl_vtrace_f64_scan_dev(const double* rew, const double* val, const double* term, const double* imp,
+                           const double* bootv, size_t B, size_t T, double gamma, double lam, double rhoClip,
+                           double cClip, double* adv, double* adv_l1, void* stream) {
+  if (B * T == 0) return PL_OK;
+  PL_REQUIRE(B < (1u << 31) && T < (1u << 31), PL_ERR_INVALID, "V-trace extents too large");
+  return pl::vtrace_f64_scan_launch(rew, val, term, imp, bootv, (int)B, (int)T, gamma, lam, rhoClip, cClip, adv,
+                                    adv_l1, (cudaStream_t)stream);
 }
 
 int pl_vtrace_f64_dev(const double* rew, const double* val, const double* term, const double* imp,

@@ -98,6 +98,29 @@ def test_vtrace_f32_fast_matches_oracle(B, T):
         np.testing.assert_allclose(l1.cpu().numpy(), O.adv_l1(ref, B, T), rtol=1e-5, atol=1e-4)
 
 
+@pytest.mark.parametrize("B,T", [(1, 1), (5, 7), (64, 12), (8192, 64), (300, 100), (33, 256), (17, 200), (9, 33)])
+def test_vtrace_f64_scan_matches_oracle(B, T):
+    """The warp-parallel f64 scan (the recurrent update's bf16 tier) against the sequential oracle:
+    a different summation order, so rounding-level agreement (1e-13 relative to the row scale)."""
+    rew, val, term, imp, boot = _rollout(B, T, B * 11 + T, done_p=0.02)
+    L = plb.lib()
+    L.pl_vtrace_f64_scan_dev.argtypes = L.pl_vtrace_f64_dev.argtypes
+    for mingru in (False, True):
+        ref = (O.vtrace_mingru(rew, val, term, imp, boot, B, T, 0.995, 0.9, 1.0, 1.0) if mingru else
+               O.vtrace(rew, val, term, imp, B, T, 0.995, 0.9, 1.0, 1.0))
+        d = {k: torch.tensor(v, device="cuda") for k, v in dict(rew=rew, val=val, term=term, imp=imp, boot=boot).items()}
+        adv = torch.full((B * T,), float("nan"), dtype=torch.float64, device="cuda")
+        l1 = torch.empty(B, dtype=torch.float64, device="cuda")
+        rc = L.pl_vtrace_f64_scan_dev(d["rew"].data_ptr(), d["val"].data_ptr(), d["term"].data_ptr(),
+                                      d["imp"].data_ptr(), d["boot"].data_ptr() if mingru else None, B, T, 0.995, 0.9,
+                                      1.0, 1.0, adv.data_ptr(), l1.data_ptr(), None)
+        assert rc == 0, L.pl_last_error()
+        got = adv.cpu().numpy()
+        scale = np.maximum(np.abs(ref), 1.0)
+        assert np.max(np.abs(got - ref) / scale) < 1e-13
+        np.testing.assert_allclose(l1.cpu().numpy(), O.adv_l1(ref, B, T), rtol=1e-13, atol=1e-12)
+
+
 # ------------------------------------------------------------------------------------------------ Muon f64
 def test_muon_stepmat_kat_bit_exact():
     f = load("muon_stepmat")
