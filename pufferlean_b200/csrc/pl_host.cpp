@@ -9,7 +9,6 @@
 #include <stdlib.h>
 #include <string.h>
 
-#include <thread>
 #include <vector>
 
 #include "../../include/pufferlean_b200.h"
@@ -54,19 +53,15 @@ int pl_gather_minibatch(const double* obsCol, const double* actions, const doubl
     }
   };
   const size_t work = Nmb * (D + 4);
-  unsigned nt = std::thread::hardware_concurrency();
-  if (nt > 16) nt = 16;
-  if (work < ((size_t)1 << 20) || nt < 2) {
+  if (work < ((size_t)1 << 20) || pl::host_threads() < 2) {
     rows(0, Nmb);
     return PL_OK;
   }
-  std::vector<std::thread> th;
-  const size_t per = (Nmb + nt - 1) / nt;
-  for (unsigned t = 0; t < nt; t++) {
-    const size_t k0 = t * per, k1 = k0 + per < Nmb ? k0 + per : Nmb;
-    if (k0 < k1) th.emplace_back(rows, k0, k1);
-  }
-  for (auto& t : th) t.join();
+  pl::host_parallel([&](int t, int T) {
+    const size_t per = (Nmb + (size_t)T - 1) / (size_t)T;
+    const size_t k0 = (size_t)t * per, k1 = k0 + per < Nmb ? k0 + per : Nmb;
+    if (k0 < k1) rows(k0, k1);
+  });
   return PL_OK;
 }
 

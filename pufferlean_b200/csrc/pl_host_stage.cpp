@@ -13,6 +13,9 @@
 #include <condition_variable>
 #include <functional>
 #include <mutex>
+#include <sched.h>
+#include <stdlib.h>
+
 #include <thread>
 #include <vector>
 
@@ -22,13 +25,30 @@ namespace pl {
 
 namespace {
 
+// Threads of the pool: the cores this process may run on, shared with the other processes of the node
+// that upload at the same time (one per GPU: LOCAL_WORLD_SIZE, as torch.distributed launchers set it),
+// at most 16; PL_HOST_THREADS overrides. Eight ranks on one host then split its cores instead of each
+// starting 16 threads that compete for them.
+static int pool_threads() {
+  if (const char* e = getenv("PL_HOST_THREADS")) {
+    const int v = atoi(e);
+    if (v >= 1) return std::min(v, 64);
+  }
+  int cores = 0;
+  cpu_set_t set;
+  if (sched_getaffinity(0, sizeof(set), &set) == 0) cores = CPU_COUNT(&set);
+  if (cores <= 0) cores = (int)std::thread::hardware_concurrency();
+  int local = 1;
+  if (const char* e = getenv("LOCAL_WORLD_SIZE")) local = std::max(1, atoi(e));
+  return std::max(1, std::min(16, std::max(1, cores) / local));
+}
+
 // Fork-join pool: run(fn) calls fn(t, T) on T threads (the caller is thread 0) and returns when all
 // have returned.
 class Pool {
  public:
   Pool() {
-    const unsigned hc = std::thread::hardware_concurrency();
-    n_ = (int)std::max(1u, std::min(16u, hc ? hc : 1u));
+    n_ = pool_threads();
     for (int t = 1; t < n_; t++) th_.emplace_back([this, t] { loop(t); });
   }
   ~Pool() {

@@ -21,6 +21,13 @@
 // sets the device error word and an abort word the other waiters watch, and the CTA drains and
 // returns like the GEMM does on a barrier timeout.
 //
+// Symmetry: G = X X^T and Pm = a I + b G + c G G are symmetric, so only their tiles (mt, nt) with
+// 128 mt < 256 (nt + 1) -- on or above the diagonal band of 128 x 256 tiles -- are computed (a quarter
+// fewer G and Pm jobs at m = 512). A product that reads G or Pm takes each 64-wide k-block of its
+// operand rows from where it lies: K-major from the stored tile when that tile exists, otherwise the
+// transposed block of the stored upper tile read MN-major (the instruction descriptor's major bit is
+// chosen per k-block). Nothing is mirrored and nothing reads the lower band, which is never written.
+//
 // Buffers: iterate 0 is the input, iterate s >= 1 lives in buffer s & 1; G and Pm have one buffer each. Overwrites are safe by the
 // chain itself: G(s, i) rewrites G only after X'(s-1, i) finished, which needed all of Pm(s-1, i), the
 // last reader of G(s-1, i); Pm(s, i) needs G(s, i), which needed X'(s-1, i), the last reader of Pm; and
@@ -45,8 +52,8 @@ struct NsChainMaps {
   CUtensorMap xk[3];  // iterate buffers 0, 1 and the input as K-major operands ({64, 128} boxes)
   CUtensorMap xn[3];  // the same as MN-major operands ({64, 64} boxes)
   CUtensorMap xs[3];  // store maps of iterate buffers 0, 1 and of the final bf16 output
-  CUtensorMap gk, gs;  // G: operand and store maps
-  CUtensorMap pk, ps;  // Pm
+  CUtensorMap gk, gs, gn;  // G: K-major operand, store, MN-major operand ({64, 64} boxes) maps
+  CUtensorMap pk, ps, pn;  // Pm
   CUtensorMap xk256[3], gk256;  // K-major B views with 256-row boxes
 };
 struct NsChainMapSet {
@@ -57,6 +64,7 @@ struct NsChainMapSet {
 struct NsChainGroup {
   int m, n, batch;
   int nG, nX, TG, TX, kbG, kbM;  // tile columns of G / X', tiles per matrix, k-blocks of G / the rest
+  int TS;  // G / Pm tiles computed per matrix (the upper band: (mt, nt) with mt < 2 nt + 2)
   int final_kind;  // 0: the last iterate into buffer iters & 1; 1: into the final bf16 output; 2: fp32
   const float* scale0;  // optional per-matrix factor of an unnormalised input: [batch] s, [batch] s^2
   const __nv_bfloat16* G;  // aux of the Pm epilogue
@@ -80,7 +88,14 @@ struct ChainJob {
   int s, p, g, i, mt, nt;
 };
 
-// Job J of the list: step, product (0 G, 1 Pm, 2 X'), group, matrix, then tile (n fastest).
+// Whether the 64-wide k-block at column k0 of the operand rows starting at row0 (a multiple of 128)
+// lies in a computed tile of a symmetric product: tile (row0 / 128, k0 / 256) exists when
+// row0 / 128 < 2 (k0 / 256) + 2. For a 256-row B block (row0 = 256 nt) both of its 128-row halves give
+// the same answer.
+__device__ __forceinline__ bool sym_stored(int row0, int k0) { return (row0 >> 7) < 2 * (k0 >> 8) + 2; }
+
+// Job J of the list: step, product (0 G, 1 Pm, 2 X'), group, matrix, then tile (n fastest; for G and
+// Pm only the upper band, row by row from nt = mt / 2).
 __device__ __forceinline__ ChainJob chain_job(long J, const NsChainArgs& a) {
   ChainJob j;
   j.s = (int)(J / a.step_jobs);
@@ -88,16 +103,25 @@ __device__ __forceinline__ ChainJob chain_job(long J, const NsChainArgs& a) {
   j.p = 0;
   while (j.p < 2 && r >= a.pjobs[j.p]) r -= a.pjobs[j.p++];
   j.g = 0;
-  int per = j.p == 2 ? a.g[0].TX : a.g[0].TG;
+  int per = j.p == 2 ? a.g[0].TX : a.g[0].TS;
   while (j.g + 1 < a.ngroups && r >= (long)a.g[j.g].batch * per) {
     r -= (long)a.g[j.g].batch * per;
     j.g++;
-    per = j.p == 2 ? a.g[j.g].TX : a.g[j.g].TG;
+    per = j.p == 2 ? a.g[j.g].TX : a.g[j.g].TS;
   }
   j.i = (int)(r / per);
-  const int t = (int)(r - (long)j.i * per), nn = j.p == 2 ? a.g[j.g].nX : a.g[j.g].nG;
-  j.nt = t % nn;
-  j.mt = t / nn;
+  int t = (int)(r - (long)j.i * per);
+  if (j.p == 2) {
+    const int nn = a.g[j.g].nX;
+    j.nt = t % nn;
+    j.mt = t / nn;
+  } else {
+    const int nn = a.g[j.g].nG;
+    int mt = 0;
+    while (t >= nn - (mt >> 1)) t -= nn - (mt >> 1), mt++;
+    j.mt = mt;
+    j.nt = (mt >> 1) + t;
+  }
   return j;
 }
 
@@ -109,10 +133,10 @@ __device__ __forceinline__ unsigned chain_dep(const ChainJob& jb, const NsChainG
   }
   if (jb.p == 1) {  // Pm(s) reads G(s)
     *c = gp.cnt + jb.i;
-    return kParts * (unsigned)((jb.s + 1) * gp.TG);
+    return kParts * (unsigned)((jb.s + 1) * gp.TS);
   }
   *c = gp.cnt + (long)gp.batch + jb.i;  // X'(s) reads Pm(s) (and iterate s, finished before G(s))
-  return kParts * (unsigned)((jb.s + 1) * gp.TG);
+  return kParts * (unsigned)((jb.s + 1) * gp.TS);
 }
 
 // Bounded acquire-poll of a tile counter. Gives up early when another CTA has raised the abort word.
@@ -136,6 +160,8 @@ __global__ void __launch_bounds__(320, 1)
   constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES;
   constexpr uint32_t IDESC_KK = tc::idesc_bf16(BM, BN, 0, 0);
   constexpr uint32_t IDESC_KN = tc::idesc_bf16(BM, BN, 0, 1);
+  constexpr uint32_t IDESC_NK = tc::idesc_bf16(BM, BN, 1, 0);
+  constexpr uint32_t IDESC_NN = tc::idesc_bf16(BM, BN, 1, 1);
   constexpr uint32_t TMEM_COLS = 2 * BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -197,6 +223,7 @@ __global__ void __launch_bounds__(320, 1)
         tc::fence_proxy_async_global();
         const int xi = jb.s == 0 ? 2 : (jb.s & 1);  // where iterate s lives
         const CUtensorMap* mA = jb.p == 0 ? &maps.xk[xi] : (jb.p == 1 ? &maps.gk : &maps.pk);
+        const CUtensorMap* mAn = jb.p == 1 ? &maps.gn : &maps.pn;  // A's transposed blocks (G or Pm)
         const CUtensorMap* mB = jb.p == 0 ? &maps.xk256[xi] : (jb.p == 1 ? &maps.gk256 : &maps.xn[xi]);
         const int nkb = jb.p == 0 ? gp.kbG : gp.kbM;
         bool ok = true;
@@ -211,13 +238,19 @@ __global__ void __launch_bounds__(320, 1)
           tc::mbar_expect_tx(&full[s], S::STAGE_BYTES);
           uint8_t* pa = sA + s * S::A_BYTES;
           uint8_t* pb = sB + s * S::B_BYTES;
-          tc::tma_load_3d(pa, mA, &full[s], k0, jb.mt * BM, jb.i);
-          if (jb.p != 2) {  // B K-major: one BN-row box
+          if (jb.p == 0 || sym_stored(jb.mt * BM, k0)) {  // A K-major: one 128-row box
+            tc::tma_load_3d(pa, mA, &full[s], k0, jb.mt * BM, jb.i);
+          } else {  // the transposed block of the stored upper tile, MN-major: two 64-row chunks
+            tc::tma_load_3d(pa, mAn, &full[s], jb.mt * BM, k0, jb.i);
+            tc::tma_load_3d(pa + 8192, mAn, &full[s], jb.mt * BM + 64, k0, jb.i);
+          }
+          if (jb.p == 0 || (jb.p == 1 && sym_stored(jb.nt * BN, k0))) {  // B K-major: one BN-row box
             tc::tma_load_3d(pb, mB, &full[s], k0, jb.nt * BN, jb.i);
-          } else {  // B = the iterate read MN-major: 64-column chunks 8 KB apart
+          } else {  // B read MN-major (the iterate, or G's transposed block): 64-column chunks 8 KB apart
+            const CUtensorMap* mBn = jb.p == 1 ? &maps.gn : mB;
 #pragma unroll
             for (int h = 0; h < BN / 64; h++)
-              tc::tma_load_3d(pb + h * 8192, mB, &full[s], jb.nt * BN + 64 * h, k0, jb.i);
+              tc::tma_load_3d(pb + h * 8192, mBn, &full[s], jb.nt * BN + 64 * h, k0, jb.i);
           }
         }
         if (!ok) {
@@ -238,7 +271,6 @@ __global__ void __launch_bounds__(320, 1)
       for (long J = blockIdx.x; J < total && !*abort_flag; J += gridDim.x, j++) {
         const ChainJob jb = chain_job(J, a);
         const int nkb = jb.p == 0 ? a.g[jb.g].kbG : a.g[jb.g].kbM;
-        const bool bmn = jb.p == 2;
         const int buf = j & 1;
         if (j >= 2 &&
             !tc::mbar_wait(&acc_empty[buf], (uint32_t)(((j >> 1) - 1) & 1), a.err, PL_ERR_MBAR_TIMEOUT | 3)) {
@@ -256,12 +288,18 @@ __global__ void __launch_bounds__(320, 1)
           tc::tc_fence_after();
           const uint32_t a_addr = tc::smem_u32(sA + s * S::A_BYTES);
           const uint32_t b_addr = tc::smem_u32(sB + s * S::B_BYTES);
+          // operand majors of this k-block, as the producer loaded it
+          const int k0 = kb * BK;
+          const bool amn = jb.p != 0 && !sym_stored(jb.mt * BM, k0);
+          const bool bmn = jb.p == 2 || (jb.p == 1 && !sym_stored(jb.nt * BN, k0));
+          const uint32_t idesc = amn ? (bmn ? IDESC_NN : IDESC_NK) : (bmn ? IDESC_KN : IDESC_KK);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; kk++) {
-            const uint64_t ad = tc::sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t ad = amn ? tc::sw128_desc(a_addr + kk * 2048, 8192, 1024)
+                                    : tc::sw128_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = bmn ? tc::sw128_desc(b_addr + kk * 2048, 8192, 1024)
                                     : tc::sw128_desc(b_addr + kk * 32, 16, 1024);
-            tc::umma_bf16(d_tmem, ad, bd, bmn ? IDESC_KN : IDESC_KK, (kb > 0 || kk > 0) ? 1u : 0u);
+            tc::umma_bf16(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           }
           tc::umma_commit(&empty[s]);
         }
@@ -391,7 +429,9 @@ static int chain_group(const NsChainGroupHost& h, int iters, NsChainMaps& mp, Ns
   Operand og{h.G, m, m, h.ldg, h.batch, gbs}, opm{h.B, m, m, h.ldg, h.batch, gbs};
   int rc = gemm_operand_map(&mp.gk, og, 128);
   if (!rc) rc = gemm_operand_map(&mp.gk256, og, 256);
+  if (!rc) rc = gemm_operand_map(&mp.gn, og, 64);
   if (!rc) rc = gemm_operand_map(&mp.pk, opm, 128);
+  if (!rc) rc = gemm_operand_map(&mp.pn, opm, 64);
   if (rc) return rc;
   if (!gemm_store_map(&mp.gs, h.G, m, m, h.ldg, h.batch, gbs) || !gemm_store_map(&mp.ps, h.B, m, m, h.ldg, h.batch, gbs))
     return 1;
@@ -404,6 +444,8 @@ static int chain_group(const NsChainGroupHost& h, int iters, NsChainMaps& mp, Ns
   g.nX = (int)ceil_div(n, kChainBN);
   g.TG = nM * g.nG;
   g.TX = nM * g.nX;
+  g.TS = 0;
+  for (int mt = 0; mt < nM; mt++) g.TS += g.nG - (mt >> 1);
   g.kbG = (int)ceil_div(n, 64);
   g.kbM = (int)ceil_div(m, 64);
   g.final_kind = h.out_f32 ? 2 : (h.final_bf16 ? 1 : 0);
@@ -435,8 +477,8 @@ int ns_chain_launch(int ngroups, const NsChainGroupHost* hs, const double* coeff
     const int rc = chain_group(hs[k], iters, mset.g[k], a.g[k]);
     if (rc == 1) return PL_OK;
     if (rc) return rc;
-    a.pjobs[0] += (long)a.g[k].batch * a.g[k].TG;
-    a.pjobs[1] += (long)a.g[k].batch * a.g[k].TG;
+    a.pjobs[0] += (long)a.g[k].batch * a.g[k].TS;
+    a.pjobs[1] += (long)a.g[k].batch * a.g[k].TS;
     a.pjobs[2] += (long)a.g[k].batch * a.g[k].TX;
   }
   a.step_jobs = a.pjobs[0] + a.pjobs[1] + a.pjobs[2];
