@@ -2149,7 +2149,7 @@ int pl_mg_update(pl_mg* s, const pl_mg_net* net, size_t handle, const pl_mg_hype
   PL_REQUIRE(s->cols_valid && s->traj && s->trajD == (long)net->D, PL_ERR_INVALID,
              "pl_mg_update: set the columns and the obs trajectory first");
   const uint64_t l0 = pl_kernel_launch_count();
-  if (h->bf16 && !loss_channel_on() && numMB > 1 && s->world == 1) {
+  if (h->bf16 && !loss_channel_on() && numMB > 1) {  // data parallel too: the collectives are captured
     rc = mg_update_graph(s, net, handle, h, numMB, mbSegs, rng, lr, (cudaStream_t)stream);
     s->launches = pl_kernel_launch_count() - l0;
     return rc;

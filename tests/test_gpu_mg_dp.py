@@ -114,3 +114,79 @@ def test_two_rank_mingru_step_equals_union(bf16, tol):
         assert p.exitcode == 0
     assert same, "ranks disagree"
     assert rel < tol, rel
+
+
+def _rank_graph(rank, port, q):
+    """pl_mg_update on 2 ranks: the bf16 tier replays one captured minibatch graph that holds the
+    collectives; the same update run eagerly (the loss channel on keeps it out of the graph) must give
+    the same bits, on both ranks."""
+    import torch.distributed as dist
+
+    import pufferlean_b200 as plb
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    L_ = plb.lib()
+    L_.pl_set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        ident = (C.c_uint8 * 128)()
+        if rank == 0:
+            assert L_.pl_comm_unique_id(ident) == 0
+        box = [bytes(ident)]
+        dist.broadcast_object_list(box, src=0)
+        ident = (C.c_uint8 * 128)(*box[0])
+        comm = C.c_void_p()
+        L_.pl_comm_create.argtypes = [C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]
+        assert L_.pl_comm_create(rank, WORLD, ident, C.byref(comm)) == 0, L_.pl_last_error()
+        P, pm = init_pm()
+        net = plb.mg_net(D, H, L, A)
+        r = rollout(rank)
+        hy = plb.MgHyper(gamma=0.995, lam=0.90, rhoClip=1.0, cClip=1.0, prioAlpha=0.8, annealBeta=0.2, wd=0.0,
+                         mu=0.95, eps=1e-7, vfCoef=0.5, entCoef=0.01, clipEps=0.2, vfClip=0.2, maxGradNorm=1.5,
+                         ns_coeffs=None, ns_iters=5, bf16=1)
+        outs = []
+        for losses in (0, 1):
+            L_.pl_loss_enable(losses)
+            s = plb.MgSession(N, T)
+            s.set_columns(r["rew"], r["term"], r["act"], r["logp"], r["val"], r["boot"])
+            s.set_obs(r["obs"], D)
+            s.set_comm(comm, rank, WORLD)
+            h = plb.policy_load(pm, P)
+            rng = 0x1234 + 7 * rank
+            for _ in range(2):  # the second update replays the graph captured by the first
+                rng = s.update(net, h, hy, 3, 4, rng, 0.02)
+            outs.append(plb.policy_download(h, P))
+            plb.policy_free(h)
+            s.close()
+        L_.pl_loss_enable(0)
+        both = [None] * WORLD
+        dist.all_gather_object(both, outs[0].tobytes())
+        if rank == 0:
+            a = np.frombuffer(both[0]), np.frombuffer(both[1])
+            q.put((bool(np.array_equal(a[0], a[1])), bool(np.array_equal(outs[0], outs[1])),
+                   bool(np.isfinite(outs[0]).all()), bool(not np.array_equal(outs[0][:P], pm[:P]))))
+        L_.pl_comm_destroy.argtypes = [C.c_void_p]
+        L_.pl_comm_destroy(comm)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_mingru_update_graph_with_collectives_equals_eager():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29850 + os.getpid() % 100
+    procs = [ctx.Process(target=_rank_graph, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    ranks_same, graph_same, finite, moved = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert finite and moved
+    assert ranks_same, "ranks disagree"
+    assert graph_same, "the replayed graph differs from the eager update"
