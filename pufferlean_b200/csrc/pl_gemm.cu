@@ -15,6 +15,7 @@ using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensor
 
 // Instance tables live in pl_gemm_inst.cu (single CTAs) and pl_gemm_pair_inst.cu (CTA pairs).
 GemmKernel gemm_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
+GemmKernel gemm_instance_at(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
 GemmKernel gemm_pair_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
 
 // 0: single CTAs only (default: on B200 the single-CTA main loop already streams at the MMA rate these
@@ -81,6 +82,7 @@ bool gemm_store_map(CUtensorMap* map, const void* ptr, long rows, long cols, lon
 
 int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const Operand& B, int M, int N, int K,
                 int batch, const EpiArgs& ep_in, cudaStream_t st) {
+  const int bn_in = bn;
   PL_REQUIRE(M > 0 && N > 0 && K > 0, PL_ERR_INVALID, "GEMM with empty extent M=%d N=%d K=%d", M, N, K);
   // Operand storage must cover the logical extents the tiles index.
   PL_REQUIRE(a_mn ? (A.rows >= K && A.cols >= M) : (A.rows >= M && A.cols >= K), PL_ERR_INVALID,
@@ -91,7 +93,20 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
   GemmKernel k = nullptr;
   const bool pair = g_pair_mode == 1 && bn == 256 && epi != EPI_PPO && M > 128 &&
                     (k = gemm_pair_instance(bn, epi, a_mn, b_mn, &smem)) != nullptr;
-  if (!pair) k = gemm_instance(bn, epi, a_mn, b_mn, &smem);
+  // the data gradient of a short-K product (the head's, K <= 128) is a memory-bound epilogue: 128-wide
+  // tiles whose aux comes through TMA into shared memory (needs the staged stores, checked below)
+  bool at = false;
+  if (!pair && epi == EPI_DGRAD && K <= 128 && ep_in.aux && batch == 1 && ep_in.k_splits <= 1) {
+    uint32_t smem_at = 0;
+    GemmKernel ka = gemm_instance_at(128, epi, a_mn, b_mn, &smem_at);
+    if (ka) {
+      at = true;
+      k = ka;
+      smem = smem_at;
+      bn = 128;
+    }
+  }
+  if (!pair && !at) k = gemm_instance(bn, epi, a_mn, b_mn, &smem);
   PL_REQUIRE(k != nullptr, PL_ERR_UNSUPPORTED, "no GEMM instance bn=%d epi=%d a_mn=%d b_mn=%d", bn, epi, (int)a_mn,
              (int)b_mn);
   if (epi == EPI_PPO) PL_REQUIRE(N <= bn, PL_ERR_INVALID, "PPO head needs all %d outputs in one tile (bn=%d)", N, bn);
@@ -113,6 +128,17 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
     if (ok && ep.aux && (((uintptr_t)ep.aux & 15) || (ep.ld_aux % 8) || (batch > 1 && (ep.aux_bstride % 8))))
       ok = false;
     ep.tma_out = ok ? 1 : 0;
+  }
+  if (at) {
+    // the aux operand map ({64, 128} boxes, 128-byte swizzle) rides in the second store map's slot
+    Operand aux{ep.aux, ep.out_rows, ep.out_cols, ep.ld_aux, 1, 0};
+    if (!ep.tma_out || gemm_operand_map(&mc2, aux, 128) != PL_OK) {
+      clear_error();
+      at = false;
+      bn = bn_in;
+      k = gemm_instance(bn, epi, a_mn, b_mn, &smem);
+      PL_REQUIRE(k != nullptr, PL_ERR_UNSUPPORTED, "no GEMM instance bn=%d epi=%d", bn, epi);
+    }
   }
   int splits = ep.k_splits > 1 ? ep.k_splits : 1;
   PL_REQUIRE(splits == 1 || batch == 1, PL_ERR_INVALID, "split-K and batching are exclusive");

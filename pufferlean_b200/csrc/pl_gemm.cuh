@@ -205,23 +205,30 @@ __device__ __forceinline__ void act_grad_row(float (&v)[N], const float (&z)[N],
 // the 64-byte swizzle; then the column reduction scratch [4][BN] + per-warp loss partials), then the
 // barriers. The ring takes what is left of 227 KB. The Newton-Schulz products (EPI_BF16) stage into
 // two alternating sets, so a chunk never waits for the previous chunk's store to finish reading.
-template <int BN, int EPI>
+//
+// AT (aux through TMA, the data gradient of a short-K product such as the head's, K <= 128): the ring
+// keeps 2 stages and the space goes to two aux tiles (128 x BN bf16, 128-byte swizzle) that the
+// producer loads with each tile's operands, so the epilogue reads its aux from shared memory instead of
+// waiting on DRAM chunk by chunk.
+template <int BN, int EPI, bool AT = false>
 struct GemmSmem {
   static constexpr int BM = 128, BK = 64;
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int NOUT = EPI == EPI_FWD ? 2 : ((EPI == EPI_DGRAD || EPI == EPI_BF16) ? 1 : 0);
-  static constexpr int STG_BUFS = EPI == EPI_BF16 ? 2 : 1;
+  static constexpr int STG_BUFS = (EPI == EPI_BF16 || AT) ? 2 : 1;
   static constexpr uint32_t STG_ONE = NOUT * 32 * 32 * 2;
   static constexpr uint32_t STG_WARP = STG_BUFS * STG_ONE;
   static constexpr uint32_t STG_BYTES = 8 * STG_WARP;
   static constexpr uint32_t RED_BYTES = (EPI == EPI_DGRAD || EPI == EPI_PPO) ? (4 * BN * 4 + 4 * 8 * 4) : 0;
-  static constexpr uint32_t FIXED = 1024 + 256 + STG_BYTES + RED_BYTES;
+  static constexpr uint32_t AUX_TILE = AT ? 128u * BN * 2u : 0u;
+  static constexpr uint32_t AUX_BYTES = 2 * AUX_TILE;
+  static constexpr uint32_t FIXED = 1024 + 256 + STG_BYTES + RED_BYTES + AUX_BYTES;
   static constexpr int FIT = (int)((232448 - FIXED) / STAGE_BYTES);
-  static constexpr int STAGES = FIT > 8 ? 8 : FIT;
+  static constexpr int STAGES = AT ? 2 : (FIT > 8 ? 8 : FIT);
   static constexpr uint32_t TOTAL = FIXED + STAGES * STAGE_BYTES;
-  static_assert(STAGES >= 2, "shared memory budget");
+  static_assert(STAGES >= 2 && FIT >= STAGES, "shared memory budget");
 };
 
 // Tile coordinates of linear tile t: n fastest (consecutive tiles share the A row-panel, which
@@ -281,11 +288,22 @@ __device__ __forceinline__ void aux_load32(const __nv_bfloat16* aux_row, int nc,
   }
 }
 
-template <int BN, int EPI>
+// The 32 bf16 aux values of tile row rl at tile columns [c32, c32 + 32), from an aux tile that TMA wrote
+// into shared memory as {64-column, 128-row} boxes in the 128-byte swizzle (16-byte piece q of row r at
+// q ^ (r & 7)). The 8 lanes of each 16-byte load phase read 8 consecutive rows: all 32 banks.
+__device__ __forceinline__ void aux_smem32(const uint8_t* aux_sm, int rl, int c32, uint4 (&o)[4]) {
+  const uint8_t* base = aux_sm + (c32 >> 6) * (128 * 128) + rl * 128;
+  const int q0 = (c32 & 63) >> 3;
+#pragma unroll
+  for (int i = 0; i < 4; i++) o[i] = *reinterpret_cast<const uint4*>(base + (((q0 + i) ^ (rl & 7)) << 4));
+}
+
+template <int BN, int EPI, int NB_ = GemmSmem<BN, EPI>::STG_BUFS>
 __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row, int m_tile, int n_tile, int bz,
                                               int batch, bool have_acc, int sub, int half, int lane, float* red,
                                               float* rowscr, uint8_t* stg, const CUtensorMap* tmC,
-                                              const CUtensorMap* tmC2, uint32_t& seq) {
+                                              const CUtensorMap* tmC2, uint32_t& seq,
+                                              const uint8_t* aux_sm = nullptr) {
   constexpr int BM = 128;
   const int row = m_tile * BM + sub * 32 + lane;
   const bool row_ok = row < ep.out_rows;
@@ -531,7 +549,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
       const int row0 = m_tile * 128 + sub * 32;
       constexpr bool HAS_AUX = (EPI == EPI_DGRAD || EPI == EPI_BF16);
       constexpr int NCH = BN / 64;  // 32-column chunks in this warp's half of the tile
-      constexpr int NB = GemmSmem<BN, EPI>::STG_BUFS;
+      constexpr int NB = NB_;
       const bool use_aux = HAS_AUX && ep.aux != nullptr && row_ok;
       const __nv_bfloat16* aux_row =
           use_aux ? ep.aux + (long)batch * ep.aux_bstride + (long)row * ep.ld_aux : nullptr;
@@ -541,7 +559,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
       if (nch > 0) {
         tc::tmem_ld16(t_row + cb, rr[0]);
         tc::tmem_ld16(t_row + cb + 16, rr[1]);
-        if (use_aux) aux_load32(aux_row, n_base + cb, ep.out_cols, pre);
+        if (use_aux && !aux_sm) aux_load32(aux_row, n_base + cb, ep.out_cols, pre);
       }
 #pragma unroll 1
       for (int ch = 0; ch < nch; ch++) {  // nch is warp-uniform
@@ -549,9 +567,13 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
         const int n0 = n_base + c32;
         const bool full = n0 + 32 <= ep.out_cols;
         uint4 cur[4];
+        if (use_aux && aux_sm) {  // the tile's aux is already in shared memory (zero past the extents)
+          aux_smem32(aux_sm, sub * 32 + lane, c32, cur);
+        } else {
 #pragma unroll
-        for (int i = 0; i < 4; i++) cur[i] = use_aux ? pre[i] : make_uint4(0u, 0u, 0u, 0u);
-        if (use_aux && ch + 1 < nch) aux_load32(aux_row, n0 + 32, ep.out_cols, pre);
+          for (int i = 0; i < 4; i++) cur[i] = use_aux ? pre[i] : make_uint4(0u, 0u, 0u, 0u);
+          if (use_aux && ch + 1 < nch) aux_load32(aux_row, n0 + 32, ep.out_cols, pre);
+        }
         const __nv_bfloat16* auxh = reinterpret_cast<const __nv_bfloat16*>(cur);
         float bz[32];
         if constexpr (EPI == EPI_FWD) {
@@ -722,12 +744,16 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
 // Persistent kernel: gridDim.x CTAs (at most one per SM) walk the linear tile list. The TMEM holds
 // two 128 x BN fp32 accumulators, so the MMA warp fills one while the epilogue warps drain the
 // other: the epilogue of tile j overlaps the main loop of tile j+1.
-template <int BN, bool A_MN, bool B_MN, int EPI>
+// AT: the aux tile of each output tile comes through TMA (tmC2 is then its {64, 128}-box operand map) into
+// one of two shared-memory buffers, loaded by the producer with the tile's operands; aux_full / aux_empty
+// hand the buffers between the producer and the epilogue warps.
+template <int BN, bool A_MN, bool B_MN, int EPI, bool AT = false>
 __global__ void __launch_bounds__(320, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, int M, int N,
                    int K, EpiArgs ep) {
-  using S = GemmSmem<BN, EPI>;
+  static_assert(!AT || EPI == EPI_DGRAD, "aux through TMA is the data gradient's");
+  using S = GemmSmem<BN, EPI, AT>;
   constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES;
   constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
   constexpr uint32_t TMEM_COLS = 2 * BN;  // 128, 256 or 512: a power of two
@@ -735,7 +761,8 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
-  uint8_t* stg_base = smem + STAGES * S::STAGE_BYTES;  // [8 warps][STG_WARP], 1 KB aligned
+  uint8_t* sAux = smem + STAGES * S::STAGE_BYTES;        // [2][128 x BN] (AT), 1 KB aligned
+  uint8_t* stg_base = sAux + S::AUX_BYTES;               // [8 warps][STG_WARP], 1 KB aligned
   float* red = (float*)(stg_base + S::STG_BYTES);        // [4][BN]
   float* rowscr = red + 4 * BN;                          // [4 warps][8]
   uint64_t* full = (uint64_t*)(stg_base + S::STG_BYTES + S::RED_BYTES);
@@ -743,7 +770,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* acc_full = empty + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint64_t* epi_done = acc_empty + 2;   // the 8 epilogue warps have finished with TMEM and their stores
-  uint32_t* tmem_slot = (uint32_t*)(epi_done + 1);
+  uint64_t* aux_full = epi_done + 1;    // [2] (AT)
+  uint64_t* aux_empty = aux_full + 2;   // [2] (AT)
+  uint32_t* tmem_slot = (uint32_t*)(aux_empty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -763,10 +792,16 @@ __global__ void __launch_bounds__(320, 1)
       tc::mbar_init(&acc_empty[b], 8);  // one arrival per epilogue warp
     }
     tc::mbar_init(epi_done, 8);
+    if (AT)
+      for (int b = 0; b < 2; b++) {
+        tc::mbar_init(&aux_full[b], 1);
+        tc::mbar_init(&aux_empty[b], 8);  // one arrival per epilogue warp
+      }
     *abort_flag = 0;
     tc::fence_mbar_init();
     tc::tma_prefetch_desc(&tmA);
     tc::tma_prefetch_desc(&tmB);
+    if (AT) tc::tma_prefetch_desc(&tmC2);
   }
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, TMEM_COLS);
@@ -792,11 +827,26 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       // ---------------- TMA producer: one ring across all tiles of this CTA
       long it = 0;
+      long ja = 0;  // aux tiles issued (AT)
       for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
         const TileIdx ti = tile_of(t, num_n, num_m);
         const int batch = ep.k_splits > 1 ? 0 : ti.z;
         int b0, b1;
         kb_range(ti.z, b0, b1);
+        if (AT) {  // this tile's aux, into the buffer the epilogue released two tiles ago
+          const int ab = (int)(ja & 1);
+          if (ja >= 2 &&
+              !tc::mbar_wait(&aux_empty[ab], (uint32_t)(((ja >> 1) - 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 10)) {
+            *abort_flag = 1;
+            break;
+          }
+          tc::mbar_expect_tx(&aux_full[ab], S::AUX_TILE);
+#pragma unroll
+          for (int h = 0; h < BN / 64; h++)
+            tc::tma_load_3d(sAux + ab * S::AUX_TILE + h * (128 * 128), &tmC2, &aux_full[ab], ti.n * BN + 64 * h,
+                            ti.m * BM, batch);
+          ja++;
+        }
         for (int kb = b0; kb < b1; kb++, it++) {
           const int s = (int)(it % STAGES);
           if (it >= STAGES &&
@@ -826,6 +876,9 @@ __global__ void __launch_bounds__(320, 1)
       // Drain: every load issued must have landed before the CTA retires.
       for (long i = it - STAGES > 0 ? it - STAGES : 0; i < it; i++)
         tc::mbar_wait(&full[i % STAGES], (uint32_t)((i / STAGES) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 2);
+      if (AT)
+        for (long i = ja - 2 > 0 ? ja - 2 : 0; i < ja; i++)
+          tc::mbar_wait(&aux_full[i & 1], (uint32_t)((i >> 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 11);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -882,18 +935,24 @@ __global__ void __launch_bounds__(320, 1)
       int b0, b1;
       kb_range(ti.z, b0, b1);
       const int buf = j & 1;
-      const bool ok = tc::mbar_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 6);
+      const bool ok = tc::mbar_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), ep.err, PL_ERR_MBAR_TIMEOUT | 6) &&
+                      (!AT || tc::mbar_wait(&aux_full[buf], (uint32_t)((j >> 1) & 1), ep.err,
+                                            PL_ERR_MBAR_TIMEOUT | 12));
       if (!ok || *abort_flag) {
         *abort_flag = 1;
         break;
       }
       tc::tc_fence_after();
       const uint32_t t_row = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(sub * 32) << 16);
-      epilogue_tile<BN, EPI>(ep, t_row, ti.m, ti.n, ti.z, ep.k_splits > 1 ? 0 : ti.z, b1 > b0, sub, half, lane, red,
-                             rowscr, stg_base + (warp - 2) * S::STG_WARP, &tmC, &tmC2, stg_seq);
+      epilogue_tile<BN, EPI, S::STG_BUFS>(ep, t_row, ti.m, ti.n, ti.z, ep.k_splits > 1 ? 0 : ti.z, b1 > b0, sub, half,
+                                          lane, red, rowscr, stg_base + (warp - 2) * S::STG_WARP, &tmC, &tmC2,
+                                          stg_seq, AT ? sAux + buf * S::AUX_TILE : nullptr);
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&acc_empty[buf])) : "memory");
+      if (lane == 0) {
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&acc_empty[buf])) : "memory");
+        if (AT) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&aux_empty[buf])) : "memory");
+      }
     }
     // bulk stores must finish reading shared memory (and land) before the CTA retires
     if (lane == 0) tc::bulk_wait<0>();

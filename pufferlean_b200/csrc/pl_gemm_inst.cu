@@ -6,10 +6,16 @@ namespace pl {
 using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, int, int,
                            int, EpiArgs);
 
-template <int BN, bool AM, bool BM_, int EPI>
+template <int BN, bool AM, bool BM_, int EPI, bool AT = false>
 static GemmKernel inst(uint32_t* smem) {
-  *smem = GemmSmem<BN, EPI>::TOTAL;
-  return &tc_gemm_kernel<BN, AM, BM_, EPI>;
+  *smem = GemmSmem<BN, EPI, AT>::TOTAL;
+  return &tc_gemm_kernel<BN, AM, BM_, EPI, AT>;
+}
+
+// The data gradient with its aux tiles through TMA (short-K products: the head's, K <= 128).
+GemmKernel gemm_instance_at(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem) {
+  if (bn == 128 && !a_mn && b_mn && epi == EPI_DGRAD) return inst<128, false, true, EPI_DGRAD, true>(smem);
+  return nullptr;
 }
 
 #define PL_INST(BN, AM, BMN, EPI) \

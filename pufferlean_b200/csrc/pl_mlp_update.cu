@@ -850,22 +850,17 @@ static int minibatch_tight(pl_update* u, const int* idx, int Nmb, double lr, boo
   }
   rc = launch_gradnorm(u->grad, (long)u->P, 1.0 / (double)Nglob, d.maxGradNorm, u->gn_part, u->cc, st);
   if (rc) return rc;
-  // f64 tight Muon (the parity tier runs it redundantly on every rank): widen the gradient, scale by cc on the host-free path (the scale is a device
-  // scalar, read back once per minibatch: this tier is the parity tier, not the fast path)
-  double cc = 0;
-  PL_CUDA(cudaMemcpyAsync(&cc, u->cc, sizeof(double), cudaMemcpyDeviceToHost, st));
-  PL_CUDA(cudaStreamSynchronize(st));
+  // f64 tight Muon (the parity tier runs it redundantly on every rank): widen the gradient; the clip
+  // scale stays on the device (u->cc[0]), read there by the Muon kernels
   double* g64 = u->stage;  // P <= stage size is checked at creation
   rc = launch_f32_to_f64(u->grad, (long)u->P, g64, st);
   if (rc) return rc;
-  rc = set_ns_coeffs(u->coeffs.data(), u->iters, st);
-  if (rc) return rc;
   for (size_t l = 0; l < u->layers.size(); l++) {
     const Layer& ly = u->layers[l];
-    rc = muon_mat_exact(ly.out, ly.in, u->pm + ly.oW, u->pm + u->P + ly.oW, g64 + ly.oW, cc, lr, d.wd, d.mu, d.eps,
-                        u->iters, u->exact_ws, st);
+    rc = muon_mat_exact(ly.out, ly.in, u->pm + ly.oW, u->pm + u->P + ly.oW, g64 + ly.oW, 0.0, lr, d.wd, d.mu, d.eps,
+                        u->iters, u->exact_ws, st, u->cc);
     if (rc) return rc;
-    rc = stepvec_launch(u->pm + ly.ob, u->pm + u->P + ly.ob, g64 + ly.ob, lr, d.wd, d.mu, cc, ly.out, st);
+    rc = stepvec_launch(u->pm + ly.ob, u->pm + u->P + ly.ob, g64 + ly.ob, lr, d.wd, d.mu, 0.0, ly.out, st, u->cc);
     if (rc) return rc;
   }
   return refresh_shadows(u, st);
@@ -1261,6 +1256,10 @@ int pl_update_run(pl_update* u, double lr, void* stream) {
   const uint64_t l0 = pl_kernel_launch_count();
   u->loss_on = g_loss_on;
   int lastNmb = 0;
+  if (!u->fast) {  // the f64 Newton-Schulz table of the tight tier, once per update
+    int rc0 = set_ns_coeffs(u->coeffs.data(), u->iters, st);
+    if (rc0) return rc0;
+  }
   // pending host observations: each first-epoch minibatch's rows are rounded and copied on the copy
   // stream just before its kernels are queued, and the compute stream waits for exactly those rows
   const bool upl = u->pend_obs != nullptr;

@@ -10,12 +10,15 @@
 namespace pl {
 
 __constant__ double c_ns_coeffs[64][3];
+constexpr size_t kSmallMuonBytes = 160 * 1024;  // shared memory of the one-CTA exact step
 
-// newMom = mu*mom + g ; upd = g + mu*newMom   (gs scales g first when != 1: g*gs)
+// newMom = mu*mom + g ; upd = g + mu*newMom   (gs scales g first when != 1: g*gs; gs is read from gsp when
+// that is not NULL, the device-side clip scale of the update)
 __global__ void nesterov_f64_kernel(const double* __restrict__ g, const double* __restrict__ m, double* nm,
-                                    double* u, double mu, double gs, long n) {
+                                    double* u, double mu, double gs_val, const double* gsp, long n) {
   long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  const double gs = gsp ? *gsp : gs_val;
   const double gi = gs == 1.0 ? g[i] : __dmul_rn(g[i], gs);
   const double newm = __dadd_rn(__dmul_rn(mu, m[i]), gi);
   nm[i] = newm;
@@ -72,14 +75,82 @@ __global__ void finalize_f64_kernel(const double* __restrict__ W, const double* 
 }
 // stepVec (Puffer/Float/Muon.lean:105-108); g pre-scaled by gs when gs != 1.
 __global__ void stepvec_f64_kernel(double* b, double* m, const double* __restrict__ g, double lr, double wd,
-                                   double mu, double gs, long n) {
+                                   double mu, double gs_val, const double* gsp, long n) {
   long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  const double gs = gsp ? *gsp : gs_val;
   const double gi = gs == 1.0 ? g[i] : __dmul_rn(g[i], gs);
   const double newm = __dadd_rn(__dmul_rn(mu, m[i]), gi);
   const double upd = __dadd_rn(gi, __dmul_rn(mu, newm));
   b[i] = __dadd_rn(__dmul_rn(b[i], __dsub_rn(1.0, __dmul_rn(lr, wd))), __dmul_rn(lr, upd));
   m[i] = newm;
+}
+
+// The whole exact step of one matrix small enough for shared memory, in one CTA: every element goes
+// through the same sequence of rounded operations as in the kernels above (Nesterov, per-row sums of
+// squares folded in row order, the scale, iters x (transpose, three matmuls with their sums from 0 in
+// l order, lincomb3), finalize), so the result is the same bits, in one launch instead of 5 iters + 5.
+__global__ void __launch_bounds__(256) muon_exact_small_kernel(int rows, int cols, double* W, double* M,
+                                                               const double* __restrict__ G, double gs_val,
+                                                               const double* gsp, double mu, double eps,
+                                                               int iters, double c1, double c2) {
+  extern __shared__ double sm[];
+  const int n = rows * cols, mn = rows < cols ? rows : cols;
+  double *U = sm, *X = U + n, *Xt = X + n, *P = Xt + n, *Q = P + n, *Am = Q + n, *rs = Am + mn * mn,
+         *inv = rs + rows;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const double gs = gsp ? *gsp : gs_val;
+  for (int i = tid; i < n; i += nt) {
+    const double gi = gs == 1.0 ? G[i] : __dmul_rn(G[i], gs);
+    const double newm = __dadd_rn(__dmul_rn(mu, M[i]), gi);
+    M[i] = newm;
+    U[i] = __dadd_rn(gi, __dmul_rn(mu, newm));
+  }
+  __syncthreads();
+  for (int r = tid; r < rows; r += nt) {
+    double acc = 0.0;
+    for (int j = 0; j < cols; j++) acc = __dadd_rn(acc, __dmul_rn(U[r * cols + j], U[r * cols + j]));
+    rs[r] = acc;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double acc = 0.0;
+    for (int i = 0; i < rows; i++) acc = __dadd_rn(acc, rs[i]);
+    inv[0] = __ddiv_rn(1.0, __dadd_rn(__dsqrt_rn(acc), eps));
+  }
+  __syncthreads();
+  for (int i = tid; i < n; i += nt) X[i] = __dmul_rn(inv[0], U[i]);
+  __syncthreads();
+  // C[m x q] = A[m x k] B[k x q], each output's sum from 0 in l order (matmul_f64_kernel's order)
+  auto matmul = [&](const double* A, const double* B, int m, int k, int q, double* Cm) {
+    for (int idx = tid; idx < m * q; idx += nt) {
+      const int i = idx / q, j = idx % q;
+      double acc = 0.0;
+      for (int l = 0; l < k; l++) acc = __dadd_rn(acc, __dmul_rn(A[i * k + l], B[l * q + j]));
+      Cm[idx] = acc;
+    }
+    __syncthreads();
+  };
+  for (int it = 0; it < iters; it++) {
+    for (int idx = tid; idx < n; idx += nt) {
+      const int i = idx / cols, j = idx % cols;
+      Xt[j * rows + i] = X[idx];
+    }
+    __syncthreads();
+    if (rows <= cols) {
+      matmul(X, Xt, rows, cols, rows, Am);
+      matmul(Am, X, rows, rows, cols, P);
+      matmul(Am, P, rows, rows, cols, Q);
+    } else {
+      matmul(Xt, X, cols, rows, cols, Am);
+      matmul(X, Am, rows, cols, cols, P);
+      matmul(P, Am, rows, cols, cols, Q);
+    }
+    const double a = c_ns_coeffs[it][0], b = c_ns_coeffs[it][1], c = c_ns_coeffs[it][2];
+    for (int i = tid; i < n; i += nt) X[i] = __dadd_rn(__dadd_rn(__dmul_rn(a, X[i]), __dmul_rn(b, P[i])), __dmul_rn(c, Q[i]));
+    __syncthreads();
+  }
+  for (int i = tid; i < n; i += nt) W[i] = __dadd_rn(__dmul_rn(c1, W[i]), __dmul_rn(c2, X[i]));
 }
 
 int set_ns_coeffs(const double* coeffs, int iters, cudaStream_t st) {
@@ -98,16 +169,37 @@ size_t exact_ws_doubles(int rows, int cols) {
   return (size_t)(5 * n + (long)mn * mn + rows + 8);
 }
 
-// In place on (W, M): W <- stepMat(W, g*gs, M). ws holds exact_ws_doubles(rows, cols) doubles.
+// In place on (W, M): W <- stepMat(W, g*gs, M) (gs read on the device from gsp when that is not NULL). ws
+// holds exact_ws_doubles(rows, cols) doubles. A matrix whose working set fits in shared memory runs in one
+// CTA (muon_exact_small_kernel), otherwise one launch per operation.
 int muon_mat_exact(int rows, int cols, double* W, double* M, const double* G, double gs, double lr, double wd,
-                   double mu, double eps, int iters, double* ws, cudaStream_t st) {
+                   double mu, double eps, int iters, double* ws, cudaStream_t st, const double* gsp) {
   const long n = (long)rows * cols;
   const int mn = rows < cols ? rows : cols;
+  const double r = (double)rows / (double)cols;
+  const double scale = sqrt(1.0 <= r ? r : 1.0);
+  volatile double lrwd = lr * wd;
+  const double c1 = 1.0 - lrwd, c2 = lr * scale;
+  const size_t small_bytes = sizeof(double) * (size_t)(5 * n + (long)mn * mn + rows + 8);
+  if (small_bytes <= kSmallMuonBytes && iters <= 64) {
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      PL_CUDA(cudaFuncSetAttribute((const void*)muon_exact_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kSmallMuonBytes));
+      attr_set[dev] = true;
+    }
+    muon_exact_small_kernel<<<1, 256, small_bytes, st>>>(rows, cols, W, M, G, gs, gsp, mu, eps, iters, c1, c2);
+    count_launch();
+    PL_LAUNCH("muon_exact_small_kernel");
+    return PL_OK;
+  }
   double *U = ws, *X = U + n, *Xt = X + n, *P = Xt + n, *Q = P + n, *Am = Q + n, *rs = Am + (long)mn * mn,
          *inv = rs + rows;
   const int B = 256;
   const unsigned gN = (unsigned)ceil_div(n, B);
-  nesterov_f64_kernel<<<gN, B, 0, st>>>(G, M, M, U, mu, gs, n);
+  nesterov_f64_kernel<<<gN, B, 0, st>>>(G, M, M, U, mu, gs, gsp, n);
   frob_rows_f64_kernel<<<(unsigned)ceil_div(rows, 128), 128, 0, st>>>(U, rows, cols, rs);
   frob_fold_f64_kernel<<<1, 32, 0, st>>>(rs, rows, eps, inv);
   scale_f64_kernel<<<gN, B, 0, st>>>(U, inv, X, n);
@@ -126,10 +218,6 @@ int muon_mat_exact(int rows, int cols, double* W, double* M, const double* G, do
     lincomb3_f64_kernel<<<gN, B, 0, st>>>(X, P, Q, it, n);
     count_launch(5);
   }
-  const double r = (double)rows / (double)cols;
-  const double scale = sqrt(1.0 <= r ? r : 1.0);
-  volatile double lrwd = lr * wd;
-  const double c1 = 1.0 - lrwd, c2 = lr * scale;
   finalize_f64_kernel<<<gN, B, 0, st>>>(W, X, c1, c2, W, n);
   count_launch();
   PL_LAUNCH("muon_mat_exact");
@@ -137,9 +225,9 @@ int muon_mat_exact(int rows, int cols, double* W, double* M, const double* G, do
 }
 
 int stepvec_launch(double* b, double* m, const double* g, double lr, double wd, double mu, double gs, long n,
-                   cudaStream_t st) {
+                   cudaStream_t st, const double* gsp) {
   if (n <= 0) return PL_OK;
-  stepvec_f64_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(b, m, g, lr, wd, mu, gs, n);
+  stepvec_f64_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(b, m, g, lr, wd, mu, gs, gsp, n);
   count_launch();
   PL_LAUNCH("stepvec_f64_kernel");
   return PL_OK;

@@ -9,10 +9,11 @@ extern const double kMuonCoeffs[5][3];
 int set_ns_coeffs(const double* coeffs, int iters, cudaStream_t st);
 // f64 workspace (in doubles) muon_mat_exact needs for one rows x cols matrix.
 size_t exact_ws_doubles(int rows, int cols);
-// Tight-tier Muon step of one matrix, in place on W and M (bit-exact with the reference oracle).
+// Tight-tier Muon step of one matrix, in place on W and M (bit-exact with the reference oracle). The
+// gradient scale is gs, or the device value *gsp when gsp is not NULL (no host round trip).
 int muon_mat_exact(int rows, int cols, double* W, double* M, const double* G, double gs, double lr, double wd,
-                   double mu, double eps, int iters, double* ws, cudaStream_t st);
-// stepVec on n bias entries, in place on b and m.
+                   double mu, double eps, int iters, double* ws, cudaStream_t st, const double* gsp = nullptr);
+// stepVec on n bias entries, in place on b and m (scale gs, or *gsp on the device).
 int stepvec_launch(double* b, double* m, const double* g, double lr, double wd, double mu, double gs, long n,
-                   cudaStream_t st);
+                   cudaStream_t st, const double* gsp = nullptr);
 }  // namespace pl

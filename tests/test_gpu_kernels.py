@@ -238,6 +238,35 @@ def test_gemm_forward_and_dgrad_epilogues(act):
     assert _rel(cs.sum(0), dz.sum(0)) < 1e-4
 
 
+@pytest.mark.parametrize("M,H,K", [(1000, 2048, 65), (333, 200, 8), (257, 520, 128)])
+def test_gemm_dgrad_short_k_aux_through_tma(M, H, K):
+    """The data gradient of a short-K product (the head's, K <= 128) runs 128-wide tiles whose aux (the
+    pre-activation) comes through TMA into shared memory: same values as the reference, ragged rows and
+    columns included; the operand A is stored 128 wide with K live columns, as the update stores dOut."""
+    torch.manual_seed(M + H + K)
+    dY = torch.zeros(M, 128, device="cuda")
+    dY[:, :K] = torch.randn(M, K, device="cuda")
+    dY = _bf(dY)
+    W2 = torch.zeros(128, (H + 7) // 8 * 8, device="cuda")
+    W2[:K, :H] = torch.randn(K, H, device="cuda") / math.sqrt(K)
+    W2 = _bf(W2)
+    Z = _bf(torch.randn(M, (H + 7) // 8 * 8, device="cuda"))
+    dZ = torch.full((M, Z.shape[1]), float("nan"), dtype=torch.bfloat16, device="cuda")
+    mt = (M + 127) // 128
+    cs = torch.full((mt, Z.shape[1]), float("nan"), device="cuda")
+    G.gemm(dY, W2, M, H, K, False, True, 256, G.EPI_DGRAD, out=dZ, ldo=Z.shape[1], out_cols=H, aux=Z,
+           ld_aux=Z.shape[1], act=1, colsum=cs, ld_colsum=Z.shape[1])
+    torch.cuda.synchronize()
+    assert G.device_error() == 0
+    dh = dY.float()[:, :K] @ W2.float()[:K, :H]
+    zz = Z.float()[:, :H]
+    u = 0.7978845608028654 * (zz + 0.044715 * zz ** 3)
+    t = torch.tanh(u)
+    dz = dh * (0.5 * (1 + t) + 0.5 * zz * (1 - t * t) * 0.7978845608028654 * (1 + 3 * 0.044715 * zz * zz))
+    assert _rel(dZ.float()[:, :H], dz) < 1e-2
+    assert _rel(cs[:, :H].sum(0), dz.sum(0)) < 1e-4
+
+
 @pytest.mark.parametrize("A,Op", [(5, 64), (64, 128), (79, 128), (100, 128)])
 def test_gemm_ppo_head_epilogue(A, Op):
     """A + 1 <= 80 with a 128-wide tile takes the register-resident epilogue, the others the general one."""
