@@ -238,6 +238,29 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int S, long
     out[i] = s;
   }
 }
+// The same sum for many slices over few outputs (S >= 32, n a multiple of 4): one warp per four
+// adjacent outputs, lane l sums slices l, l + 32, ... in order, then a fixed butterfly adds the lanes.
+__global__ void splitk_reduce_warp_kernel(const float* __restrict__ part, int S, long n4, float* out) {
+  const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= n4) return;  // whole warps leave together
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int z = lane; z < S; z += 32) {
+    const float4 p = reinterpret_cast<const float4*>(part + (long)z * n4 * 4)[w];
+    s.x += p.x;
+    s.y += p.y;
+    s.z += p.z;
+    s.w += p.w;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    s.x += __shfl_xor_sync(0xffffffffu, s.x, o);
+    s.y += __shfl_xor_sync(0xffffffffu, s.y, o);
+    s.z += __shfl_xor_sync(0xffffffffu, s.z, o);
+    s.w += __shfl_xor_sync(0xffffffffu, s.w, o);
+  }
+  if (lane == 0) reinterpret_cast<float4*>(out)[w] = s;
+}
 // Global gradient norm of g*sc: fixed grid of kRedBlocks blocks x 256 threads, strided f64 sums.
 __global__ void __launch_bounds__(256) gradnorm_part_kernel(const float* __restrict__ g, long P, double sc,
                                                             double* part) {
@@ -813,6 +836,12 @@ int launch_colsum_reduce(const float* part, int tiles, long ld, int ncols, float
   return PL_OK;
 }
 int launch_splitk_reduce(const float* part, int S, long n, float* out, cudaStream_t st) {
+  if (S >= 32 && (n & 3) == 0 && ((uintptr_t)part & 15) == 0 && ((uintptr_t)out & 15) == 0) {
+    splitk_reduce_warp_kernel<<<(unsigned)ceil_div(n / 4 * 32, 256), 256, 0, st>>>(part, S, n / 4, out);
+    count_launch();
+    PL_LAUNCH("splitk_reduce_warp_kernel");
+    return PL_OK;
+  }
   splitk_reduce_kernel<<<grid_for(n), 256, 0, st>>>(part, S, n, out);
   count_launch();
   PL_LAUNCH("splitk_reduce_kernel");
@@ -892,11 +921,13 @@ int launch_sgemm(int M, int N, int K, const float* A, long ars, long acs, const 
 }
 // A long-K product with few output tiles (the weight gradients, K = the minibatch rows) would leave
 // all but a few SMs idle walking K: split K over blockIdx.z into slices of the workspace (S * M * N
-// floats, C dense: ldc = N), then sum the slices in order (deterministic).
+// floats, C dense: ldc = N), then sum the slices in a fixed order (deterministic). Each slice is a
+// chain of dependent global loads, 16 rows per step, so slices are kept short (64 rows) as long as
+// the grid stays within eight CTAs per SM.
 int launch_sgemm_splitk(int M, int N, int K, const float* A, long ars, long acs, const float* B, long brs, long bcs,
                         float* C, long ldc, float* ws, long ws_elems, cudaStream_t st) {
   const long tiles = ceil_div(N, 64) * ceil_div(M, 64), mn = (long)M * N;
-  long S = std::min<long>(ceil_div(K, 256), ceil_div(2 * 148, tiles));
+  long S = std::min<long>(ceil_div(K, 64), ceil_div(8 * 148, tiles));
   if (ws && mn > 0) S = std::min<long>(S, ws_elems / mn);
   if (S < 2 || !ws || ldc != N) return launch_sgemm(M, N, K, A, ars, acs, B, brs, bcs, C, ldc, 1.f, st);
   const int kc = (int)round_up(ceil_div(K, S), 16);

@@ -300,6 +300,9 @@ static int alloc_session(pl_update* u) {
   size_t maxw = 0;
   for (auto& ly : u->layers) maxw = std::max(maxw, (size_t)ly.out * ly.in);
   u->splitk_elems = maxw * 8;
+  // the tight tier's SIMT weight gradients of small layers split K (the minibatch rows) into up to
+  // 256 slices (at most 16 MB of workspace)
+  if (!fast) u->splitk_elems = std::max(u->splitk_elems, std::min(maxw * 256, (size_t)1 << 22));
   u->splitk = dalloc<float>(u, u->splitk_elems);  // tight tier: the split-K weight gradients
   // parameters in compute precision
   for (auto& ly : u->layers) {
