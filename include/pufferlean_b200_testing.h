@@ -59,6 +59,10 @@ int pl_test_update_gather(struct pl_update* u, size_t epoch, size_t mb, void* ro
  * while the backward pass continues (the default), 0 = one all-reduce of the whole gradient after the
  * backward pass; a negative mode only queries. Returns the previous mode. */
 int pl_test_dp_overlap(int mode);
+/* Tight-tier (f64 Muon) sessions created afterwards: 1 = the Muon step of layers small enough for one CTA
+ * each runs as one launch (the default), 0 = one launch sequence per matrix and bias; a negative mode
+ * only queries. Returns the previous mode. */
+int pl_test_exact_group(int mode);
 /* Replaces NCCL and the stream query used by pl_comm_* with host-side fakes, for failure tests without a
  * GPU: 1 = creation never completes (a peer that never joins), 2 = a peer fails once the communicator
  * is up (asynchronous-error queries report it), 3 = enqueued work never completes, 4 = a healthy

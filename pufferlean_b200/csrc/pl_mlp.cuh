@@ -126,6 +126,22 @@ int launch_sgemm(int M, int N, int K, const float* A, long ars, long acs, const 
                  long ldc, float alpha, cudaStream_t st);
 int launch_sgemm_splitk(int M, int N, int K, const float* A, long ars, long acs, const float* B, long brs, long bcs,
                         float* C, long ldc, float* ws, long ws_elems, cudaStream_t st);
+// Z = A W^T + b (A: M x K rows of lda floats, W: N x K dense), H = act(Z); both M x N dense.
+int launch_sgemm_bias_act(int M, int N, int K, const float* A, long lda, const float* W, const float* b, float* Z,
+                          float* H, int act, cudaStream_t st);
+// dH = (dZ W) * act'(Z) (dZ: M x K rows of lda floats, W: K x N dense, Z and dH: M x N dense).
+int launch_sgemm_act_grad(int M, int N, int K, const float* A, long lda, const float* W, const float* Z, float* dH,
+                          int act, cudaStream_t st);
+// Out = H W^T + b for O <= 8 outputs and K <= 1024 (a multiple of 4): one warp per row.
+bool skinny_rows_ok(int K, int O);
+int launch_skinny_rows(const float* H, int rows, int K, const float* W, const float* b, int O, float* Out,
+                       cudaStream_t st);
+// Weight and bias gradient of one layer: dW[out x in] = dZ^T Hin, db[out] = column sums of dZ (dZ: K rows of
+// ldz floats, Hin: K rows of ldh floats), split over K into ws (splitk_wb_elems floats) and summed in a
+// fixed order.
+long splitk_wb_elems(int K, int out, int in);
+int launch_wgrad_bias_f32(int out, int in, int K, const float* dZ, long ldz, const float* Hin, long ldh, float* dW,
+                          float* db, float* ws, long ws_elems, cudaStream_t st);
 int launch_bias_act_f32(float* Z, float* H, const float* b, long M, int N, int act, cudaStream_t st);
 int launch_act_grad_f32(float* dH, const float* Z, long n, int act, cudaStream_t st);
 int launch_ppo_rows_f32(const float* Out, int M, int A, const int* act, const float* adv, const double* ms,

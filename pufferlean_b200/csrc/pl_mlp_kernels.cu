@@ -156,14 +156,21 @@ __global__ void __launch_bounds__(256) gather_kernel(const int* __restrict__ idx
     part[2 * blockIdx.x + 1] = s2;
   }
 }
-// ms = [mean, std + 1e-8] (population std), folded over the block partials in order.
+// Sum of p[b * stride] over b < n by one warp in a fixed order: lane l folds b = l, l + 32, ... in turn,
+// then a butterfly adds the lanes; every lane returns the total.
+__device__ __forceinline__ double warp_fold_f64(const double* __restrict__ p, int n, int stride) {
+  const int lane = threadIdx.x & 31;
+  double s = 0.0;
+  for (int b = lane; b < n; b += 32) s += p[(long)b * stride];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+// ms = [mean, std + 1e-8] (population std), folded over the block partials (one warp).
 __global__ void adv_stats_kernel(const double* __restrict__ part, int nb, int n, double* ms) {
-  if (threadIdx.x || blockIdx.x) return;
-  double s1 = 0.0, s2 = 0.0;
-  for (int b = 0; b < nb; b++) {
-    s1 += part[2 * b];
-    s2 += part[2 * b + 1];
-  }
+  if (blockIdx.x || threadIdx.x >= 32) return;
+  const double s1 = warp_fold_f64(part, nb, 2), s2 = warp_fold_f64(part + 1, nb, 2);
+  if (threadIdx.x) return;
   const double mean = s1 / (double)n;
   double var = s2 / (double)n - mean * mean;
   if (var < 0.0) var = 0.0;
@@ -173,12 +180,9 @@ __global__ void adv_stats_kernel(const double* __restrict__ part, int nb, int n,
 
 // Data-parallel form: the local (sum, sum of squares, count) folded in order, to be all-reduced.
 __global__ void adv_sums_kernel(const double* __restrict__ part, int nb, int n, double* sums) {
-  if (threadIdx.x || blockIdx.x) return;
-  double s1 = 0.0, s2 = 0.0;
-  for (int b = 0; b < nb; b++) {
-    s1 += part[2 * b];
-    s2 += part[2 * b + 1];
-  }
+  if (blockIdx.x || threadIdx.x >= 32) return;
+  const double s1 = warp_fold_f64(part, nb, 2), s2 = warp_fold_f64(part + 1, nb, 2);
+  if (threadIdx.x) return;
   sums[0] = s1;
   sums[1] = s2;
   sums[2] = (double)n;
@@ -285,9 +289,9 @@ __global__ void __launch_bounds__(256) gradnorm_part_kernel(const float* __restr
 }
 // cc = (maxNorm > 0 && gnorm > maxNorm ? maxNorm/gnorm : 1) * sc   (maxNorm <= 0: cc = sc)
 __global__ void gradnorm_final_kernel(const double* __restrict__ part, int nb, double maxNorm, double sc, double* cc) {
-  if (threadIdx.x || blockIdx.x) return;
-  double s = 0.0;
-  for (int b = 0; b < nb; b++) s += part[b];
+  if (blockIdx.x || threadIdx.x >= 32) return;
+  const double s = warp_fold_f64(part, nb, 1);
+  if (threadIdx.x) return;
   const double gnorm = sqrt(s);
   cc[0] = ((maxNorm > 0.0 && gnorm > maxNorm) ? maxNorm / gnorm : 1.0) * sc;
   cc[1] = gnorm;
@@ -448,9 +452,16 @@ __global__ void f32_to_f64_kernel(const float* __restrict__ s, long n, double* d
 // ---------------------------------------------------------------- tight tier (fp32 SIMT)
 // C[m,n] = alpha * sum_k A(m,k) B(n,k), A(m,k) = A[m*ars + k*acs], B(n,k) = B[n*brs + k*bcs]. Split K:
 // blockIdx.z sums k in [z*kc, (z+1)*kc) into C + z*cz (kc = K and cz = 0 without a split).
+// Epilogues (SE): SGEMM_PLAIN stores alpha * acc; SGEMM_BIAS_ACT stores Z = acc + bias[n] into C and
+// act(Z) into X (bias_act_f32_kernel's arithmetic); SGEMM_ACT_GRAD stores acc * act'(X[m, n]) with X
+// the pre-activation (act_grad_f32_kernel's). ones_col >= 0 makes column ones_col of B all ones
+// (the weight-gradient split then also sums the bias gradient, as one more output column).
+enum { SGEMM_PLAIN = 0, SGEMM_BIAS_ACT = 1, SGEMM_ACT_GRAD = 2 };
+template <int SE>
 __global__ void __launch_bounds__(256) sgemm_kernel(int M, int N, int K, const float* __restrict__ A, long ars, long acs,
                                                     const float* __restrict__ B, long brs, long bcs, float* C, long ldc,
-                                                    float alpha, int kc, long cz) {
+                                                    float alpha, int kc, long cz, int ones_col,
+                                                    const float* __restrict__ bias, float* X, int act) {
   __shared__ float As[16][65], Bs[16][65];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
@@ -462,7 +473,7 @@ __global__ void __launch_bounds__(256) sgemm_kernel(int M, int N, int K, const f
       const int kk = i / 64, mm = i % 64;
       const int m = m0 + mm, n = n0 + mm, k = k0 + kk;
       As[kk][mm] = (m < M && k < ke) ? A[(long)m * ars + (long)k * acs] : 0.f;
-      Bs[kk][mm] = (n < N && k < ke) ? B[(long)n * brs + (long)k * bcs] : 0.f;
+      Bs[kk][mm] = (n < N && k < ke) ? (n == ones_col ? 1.f : B[(long)n * brs + (long)k * bcs]) : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -485,8 +496,83 @@ __global__ void __launch_bounds__(256) sgemm_kernel(int M, int N, int K, const f
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
-      if (m < M && n < N) C[(long)m * ldc + n] = alpha * acc[i][j];
+      if (m < M && n < N) {
+        const long o = (long)m * ldc + n;
+        if constexpr (SE == SGEMM_BIAS_ACT) {
+          const float z = acc[i][j] + bias[n];
+          C[o] = z;
+          X[o] = act_fwd(z, act);
+        } else if constexpr (SE == SGEMM_ACT_GRAD) {
+          const float d = alpha * acc[i][j], z = X[o];
+          C[o] = (act == 0) ? (z > 0.f ? d : 0.f) : (act == 2 ? d : d * act_grad(z, act));
+        } else {
+          C[o] = alpha * acc[i][j];
+        }
+      }
     }
+}
+// Out[r, o] = sum_k H[r, k] W[o, k] + b[o] for a few outputs (O <= kSkinnyO) over K a multiple of 4:
+// one warp per row, each lane a strided run of 16-byte pieces of the row, then a fixed butterfly per
+// output. W and b sit in shared memory.
+constexpr int kSkinnyO = 8, kSkinnyK = 1024;  // W in shared memory: 32 KB
+__global__ void __launch_bounds__(256) skinny_rows_kernel(const float* __restrict__ H, int rows, int K,
+                                                          const float* __restrict__ W, const float* __restrict__ b,
+                                                          int O, float* Out) {
+  __shared__ float4 sW[kSkinnyO * kSkinnyK / 4];
+  __shared__ float sb[kSkinnyO];
+  const int K4 = K / 4;
+  for (int i = threadIdx.x; i < O * K4; i += blockDim.x) sW[i] = reinterpret_cast<const float4*>(W)[i];
+  if (threadIdx.x < O) sb[threadIdx.x] = b[threadIdx.x];
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const long wpb = blockDim.x >> 5;
+  for (long r = (long)blockIdx.x * wpb + (threadIdx.x >> 5); r < rows; r += (long)gridDim.x * wpb) {
+    const float4* h = reinterpret_cast<const float4*>(H + r * K);
+    float acc[kSkinnyO];
+#pragma unroll
+    for (int o = 0; o < kSkinnyO; o++) acc[o] = 0.f;
+    for (int q = lane; q < K4; q += 32) {
+      const float4 x = h[q];
+#pragma unroll
+      for (int o = 0; o < kSkinnyO; o++) {
+        if (o < O) {
+          const float4 w = sW[o * K4 + q];
+          acc[o] += x.x * w.x + x.y * w.y + x.z * w.z + x.w * w.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 0; o < kSkinnyO; o++) {
+#pragma unroll
+      for (int off = 16; off; off >>= 1) acc[o] += __shfl_xor_sync(0xffffffffu, acc[o], off);
+    }
+    if (lane < O) {
+      float v = acc[0];
+#pragma unroll
+      for (int o = 1; o < kSkinnyO; o++)
+        if (lane == o) v = acc[o];
+      Out[r * O + lane] = v + sb[lane];
+    }
+  }
+}
+// Split-K slices of a weight gradient with its bias column: part[s][m][in + 1]; out dW[m][in] and
+// db[m], each the sum over s in a fixed order (lane-strided runs, then a butterfly), one warp per output.
+__global__ void splitk_reduce_wb_kernel(const float* __restrict__ part, int S, int M, int in, float* dW, float* db) {
+  const long n = (long)M * (in + 1);
+  const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= n) return;  // whole warps leave together
+  float s = 0.f;
+  for (int z = lane; z < S; z += 32) s += part[(long)z * n + w];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) {
+    const int m = (int)(w / (in + 1)), c = (int)(w % (in + 1));
+    if (c < in)
+      dW[(long)m * in + c] = s;
+    else
+      db[m] = s;
+  }
 }
 // Z <- Z + b (row-major M x N), H = act(Z)
 __global__ void bias_act_f32_kernel(float* Z, float* H, const float* __restrict__ b, long M, int N, int act) {
@@ -914,9 +1000,60 @@ int launch_f32_to_f64(const float* s, long n, double* d, cudaStream_t st) {
 int launch_sgemm(int M, int N, int K, const float* A, long ars, long acs, const float* B, long brs, long bcs, float* C,
                  long ldc, float alpha, cudaStream_t st) {
   dim3 grid((unsigned)ceil_div(N, 64), (unsigned)ceil_div(M, 64));
-  sgemm_kernel<<<grid, 256, 0, st>>>(M, N, K, A, ars, acs, B, brs, bcs, C, ldc, alpha, K, 0);
+  sgemm_kernel<SGEMM_PLAIN><<<grid, 256, 0, st>>>(M, N, K, A, ars, acs, B, brs, bcs, C, ldc, alpha, K, 0, -1, nullptr,
+                                                  nullptr, 0);
   count_launch();
   PL_LAUNCH("sgemm_kernel");
+  return PL_OK;
+}
+int launch_sgemm_bias_act(int M, int N, int K, const float* A, long lda, const float* W, const float* b, float* Z,
+                          float* H, int act, cudaStream_t st) {
+  dim3 grid((unsigned)ceil_div(N, 64), (unsigned)ceil_div(M, 64));
+  sgemm_kernel<SGEMM_BIAS_ACT><<<grid, 256, 0, st>>>(M, N, K, A, lda, 1, W, K, 1, Z, N, 1.f, K, 0, -1, b, H, act);
+  count_launch();
+  PL_LAUNCH("sgemm_kernel");
+  return PL_OK;
+}
+int launch_sgemm_act_grad(int M, int N, int K, const float* A, long lda, const float* W, const float* Z, float* dH,
+                          int act, cudaStream_t st) {
+  dim3 grid((unsigned)ceil_div(N, 64), (unsigned)ceil_div(M, 64));
+  sgemm_kernel<SGEMM_ACT_GRAD><<<grid, 256, 0, st>>>(M, N, K, A, lda, 1, W, 1, N, dH, N, 1.f, K, 0, -1, nullptr,
+                                                     const_cast<float*>(Z), act);
+  count_launch();
+  PL_LAUNCH("sgemm_kernel");
+  return PL_OK;
+}
+bool skinny_rows_ok(int K, int O) { return O >= 1 && O <= kSkinnyO && K % 4 == 0 && K <= kSkinnyK; }
+int launch_skinny_rows(const float* H, int rows, int K, const float* W, const float* b, int O, float* Out,
+                       cudaStream_t st) {
+  PL_REQUIRE(skinny_rows_ok(K, O), PL_ERR_INVALID, "skinny row product: K %d, O %d out of range", K, O);
+  PL_REQUIRE(((uintptr_t)H & 15) == 0 && ((uintptr_t)W & 15) == 0, PL_ERR_INVALID, "skinny row product: unaligned");
+  const unsigned nb = (unsigned)std::min<long>(ceil_div(rows, 8), 148L * 8);
+  if (nb == 0) return PL_OK;
+  skinny_rows_kernel<<<nb, 256, 0, st>>>(H, rows, K, W, b, O, Out);
+  count_launch();
+  PL_LAUNCH("skinny_rows_kernel");
+  return PL_OK;
+}
+long splitk_wb_elems(int K, int out, int in) {
+  return std::min<long>(ceil_div(K, 64), ceil_div(8 * 148, ceil_div(in + 1, 64) * ceil_div(out, 64))) * out *
+         (long)(in + 1);
+}
+int launch_wgrad_bias_f32(int out, int in, int K, const float* dZ, long ldz, const float* Hin, long ldh, float* dW,
+                          float* db, float* ws, long ws_elems, cudaStream_t st) {
+  const int N = in + 1;
+  const long tiles = ceil_div(N, 64) * ceil_div(out, 64), mn = (long)out * N;
+  long S = std::min<long>(ceil_div(K, 64), ceil_div(8 * 148, tiles));
+  S = std::min<long>(S, ws_elems / mn);
+  PL_REQUIRE(S >= 1, PL_ERR_INVALID, "weight-gradient workspace too small");
+  const int kc = (int)round_up(ceil_div(K, S), 16);
+  S = ceil_div(K, kc);
+  dim3 grid((unsigned)ceil_div(N, 64), (unsigned)ceil_div(out, 64), (unsigned)S);
+  sgemm_kernel<SGEMM_PLAIN><<<grid, 256, 0, st>>>(out, N, K, dZ, 1, ldz, Hin, 1, ldh, ws, N, 1.f, kc, mn, in, nullptr,
+                                                  nullptr, 0);
+  splitk_reduce_wb_kernel<<<(unsigned)ceil_div(mn * 32, 256), 256, 0, st>>>(ws, (int)S, out, in, dW, db);
+  count_launch(2);
+  PL_LAUNCH("splitk_reduce_wb_kernel");
   return PL_OK;
 }
 // A long-K product with few output tiles (the weight gradients, K = the minibatch rows) would leave
@@ -933,7 +1070,8 @@ int launch_sgemm_splitk(int M, int N, int K, const float* A, long ars, long acs,
   const int kc = (int)round_up(ceil_div(K, S), 16);
   S = ceil_div(K, kc);
   dim3 grid((unsigned)ceil_div(N, 64), (unsigned)ceil_div(M, 64), (unsigned)S);
-  sgemm_kernel<<<grid, 256, 0, st>>>(M, N, K, A, ars, acs, B, brs, bcs, ws, N, 1.f, kc, mn);
+  sgemm_kernel<SGEMM_PLAIN><<<grid, 256, 0, st>>>(M, N, K, A, ars, acs, B, brs, bcs, ws, N, 1.f, kc, mn, -1, nullptr,
+                                                  nullptr, 0);
   count_launch();
   PL_LAUNCH("sgemm_kernel");
   return launch_splitk_reduce(ws, (int)S, mn, C, st);

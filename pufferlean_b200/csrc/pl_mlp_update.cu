@@ -97,6 +97,7 @@ struct pl_update {
   double* adv_sums = nullptr;  // [sum, sum of squares, count] of the minibatch's raw advantages
   std::vector<int> owner;      // Newton-Schulz owner rank of each layer
   std::vector<std::vector<int>> ns_groups;  // layers of equal shape, orthogonalised as one batch
+  std::vector<ExactLayer> exact_group;      // tight tier: every layer when each fits one CTA's step
   long ns_batch = 1;                        // largest group
   std::vector<float*> xres;    // per-layer orthogonalised update (m x n wide layout, fp32)
   // profiling: CUDA events around each launch group, per class
@@ -138,6 +139,7 @@ static std::mutex g_mu;
 static bool g_loss_on = false;
 static bool g_host_bf16 = true;
 static bool g_dp_overlap = true;  // sessions created afterwards overlap the gradient all-reduce
+static bool g_exact_group = true;  // tight-tier sessions created afterwards may use the one-launch Muon step
 static std::atomic<uint64_t> g_upload_bytes{0};  // host-to-device bytes of the last set_columns call  // bf16 tier: host observations rounded to bf16 on the host threads
 static double g_losses[7] = {0, 0, 0, 0, 0, 0, 0};
 
@@ -300,9 +302,12 @@ static int alloc_session(pl_update* u) {
   size_t maxw = 0;
   for (auto& ly : u->layers) maxw = std::max(maxw, (size_t)ly.out * ly.in);
   u->splitk_elems = maxw * 8;
-  // the tight tier's SIMT weight gradients of small layers split K (the minibatch rows) into up to
-  // 256 slices (at most 16 MB of workspace)
-  if (!fast) u->splitk_elems = std::max(u->splitk_elems, std::min(maxw * 256, (size_t)1 << 22));
+  // the tight tier's SIMT weight gradients (with the bias column) split K, the minibatch rows, into
+  // slices of 64 (at most 16 MB of workspace)
+  if (!fast)
+    for (auto& ly : u->layers)
+      u->splitk_elems = std::max(u->splitk_elems,
+                                 (size_t)std::min<long>(splitk_wb_elems((int)u->mbMax, ly.out, ly.in), 1L << 22));
   u->splitk = dalloc<float>(u, u->splitk_elems);  // tight tier: the split-K weight gradients
   // parameters in compute precision
   for (auto& ly : u->layers) {
@@ -361,6 +366,14 @@ static int alloc_session(pl_update* u) {
     size_t ws = 0;
     for (auto& ly : u->layers) ws = std::max(ws, exact_ws_doubles(ly.out, ly.in));
     u->exact_ws = dalloc<double>(u, ws);
+    // layers small enough for one CTA each take the one-launch group step
+    u->exact_group.clear();
+    for (size_t l = 0; l < u->layers.size(); l++) {
+      const Layer& ly = u->layers[l];
+      u->exact_group.push_back(ExactLayer{ly.out, ly.in, (long)ly.oW, (long)ly.ob, u->Wf[l], u->bf[l]});
+    }
+    if (!g_exact_group || !muon_group_fits(u->exact_group.data(), (int)u->exact_group.size(), u->iters))
+      u->exact_group.clear();
   }
   if (u->dp) {
     u->adv_sums = dalloc<double>(u, 4);
@@ -796,16 +809,18 @@ static int minibatch_tight(pl_update* u, const int* idx, int Nmb, double lr, boo
   const float* hin = (const float*)u->X;
   int nin = D;
   for (int l = 0; l < L; l++) {
-    rc = launch_sgemm(Nmb, H, nin, hin, nin, 1, u->Wf[l], nin, 1, (float*)u->Zs[l], H, 1.f, st);
-    if (rc) return rc;
-    rc = launch_bias_act_f32((float*)u->Zs[l], (float*)u->Hs[l], u->bf[l], Nmb, H, act, st);
+    // Z = hin W^T + b and H = act(Z) in the product's epilogue
+    rc = launch_sgemm_bias_act(Nmb, H, nin, hin, nin, u->Wf[l], u->bf[l], (float*)u->Zs[l], (float*)u->Hs[l], act, st);
     if (rc) return rc;
     hin = (const float*)u->Hs[l];
     nin = H;
   }
-  rc = launch_sgemm(Nmb, O, H, hin, H, 1, u->Wf[L], H, 1, u->Out, O, 1.f, st);
-  if (rc) return rc;
-  rc = launch_bias_act_f32(u->Out, nullptr, u->bf[L], Nmb, O, 0, st);
+  if (skinny_rows_ok(H, O)) {  // a few head outputs: one warp per row instead of 64 x 64 tiles
+    rc = launch_skinny_rows(hin, Nmb, H, u->Wf[L], u->bf[L], O, u->Out, st);
+  } else {
+    rc = launch_sgemm(Nmb, O, H, hin, H, 1, u->Wf[L], H, 1, u->Out, O, 1.f, st);
+    if (!rc) rc = launch_bias_act_f32(u->Out, nullptr, u->bf[L], Nmb, O, 0, st);
+  }
   if (rc) return rc;
   if (u->head_mode != 0) {
     rc = launch_gather_rows_f32(idx, Nmb, u->actw_c, u->W, u->mb_actw, st);
@@ -826,20 +841,15 @@ static int minibatch_tight(pl_update* u, const int* idx, int Nmb, double lr, boo
   for (int l = L; l >= 0; l--) {
     const Layer& ly = u->layers[l];
     const float* hprev = l == 0 ? (const float*)u->X : (const float*)u->Hs[l - 1];
-    // bias grad
-    rc = launch_colsum_f32(dcur, Nmb, nd, u->grad + ly.ob, u->colpart,
-                           (long)colsum_scratch_elems((int)ceil_div(u->mbMax, 128), std::max(u->Hp, u->Op)), st);
-    if (rc) return rc;
-    // dW[o, i] = sum_n dcur[n, o] hprev[n, i]
-    rc = launch_sgemm_splitk(ly.out, ly.in, Nmb, dcur, 1, nd, hprev, 1, ly.in, u->grad + ly.oW, ly.in, u->splitk,
-                             (long)u->splitk_elems, st);
+    // dW[o, i] = sum_n dcur[n, o] hprev[n, i] and the bias gradient db[o] = sum_n dcur[n, o], as one
+    // split-K product with a column of ones
+    rc = launch_wgrad_bias_f32(ly.out, ly.in, Nmb, dcur, nd, hprev, ly.in, u->grad + ly.oW, u->grad + ly.ob,
+                               u->splitk, (long)u->splitk_elems, st);
     if (rc) return rc;
     if (l == 0) break;
-    // dH[n, i] = sum_o dcur[n, o] W[o, i]
+    // dZ_{l-1}[n, i] = (sum_o dcur[n, o] W[o, i]) * act'(Z_{l-1}[n, i])
     float* dn = (float*)u->dZ[dsel];
-    rc = launch_sgemm(Nmb, ly.in, ly.out, dcur, nd, 1, u->Wf[l], 1, ly.in, dn, ly.in, 1.f, st);
-    if (rc) return rc;
-    rc = launch_act_grad_f32(dn, (const float*)u->Zs[l - 1], (long)Nmb * ly.in, act, st);
+    rc = launch_sgemm_act_grad(Nmb, ly.in, ly.out, dcur, nd, u->Wf[l], (const float*)u->Zs[l - 1], dn, act, st);
     if (rc) return rc;
     dcur = dn;
     nd = ly.in;
@@ -853,8 +863,12 @@ static int minibatch_tight(pl_update* u, const int* idx, int Nmb, double lr, boo
   }
   rc = launch_gradnorm(u->grad, (long)u->P, 1.0 / (double)Nglob, d.maxGradNorm, u->gn_part, u->cc, st);
   if (rc) return rc;
-  // f64 tight Muon (the parity tier runs it redundantly on every rank): widen the gradient; the clip
-  // scale stays on the device (u->cc[0]), read there by the Muon kernels
+  // f64 tight Muon (the parity tier runs it redundantly on every rank); the clip scale stays on the
+  // device (u->cc[0]), read there by the Muon kernels. Small layers: one launch for every matrix and
+  // bias, which also refreshes the f32 copies.
+  if (u->exact_group.size() == u->layers.size())
+    return muon_group_exact(u->exact_group.data(), (int)u->exact_group.size(), u->pm, (long)u->P, u->grad, lr, d.wd,
+                            d.mu, d.eps, u->iters, u->cc, st);
   double* g64 = u->stage;  // P <= stage size is checked at creation
   rc = launch_f32_to_f64(u->grad, (long)u->P, g64, st);
   if (rc) return rc;
@@ -1685,5 +1699,12 @@ extern "C" int pl_test_update_gather(pl_update* u, size_t epoch, size_t mb, void
 extern "C" int pl_test_dp_overlap(int mode) {
   const int prev = g_dp_overlap ? 1 : 0;
   if (mode >= 0) g_dp_overlap = mode != 0;
+  return prev;
+}
+// Test hook: 1 = tight-tier sessions created afterwards run the Muon step of small layers as one launch
+// (the default), 0 = one launch sequence per matrix and bias; < 0 queries. Returns the previous mode.
+extern "C" int pl_test_exact_group(int mode) {
+  const int prev = g_exact_group ? 1 : 0;
+  if (mode >= 0) g_exact_group = mode != 0;
   return prev;
 }

@@ -90,18 +90,17 @@ __global__ void stepvec_f64_kernel(double* b, double* m, const double* __restric
 // through the same sequence of rounded operations as in the kernels above (Nesterov, per-row sums of
 // squares folded in row order, the scale, iters x (transpose, three matmuls with their sums from 0 in
 // l order, lincomb3), finalize), so the result is the same bits, in one launch instead of 5 iters + 5.
-__global__ void __launch_bounds__(256) muon_exact_small_kernel(int rows, int cols, double* W, double* M,
-                                                               const double* __restrict__ G, double gs_val,
-                                                               const double* gsp, double mu, double eps,
-                                                               int iters, double c1, double c2) {
-  extern __shared__ double sm[];
+// G is the f64 gradient or the f32 one (widened exactly on load); Wf, when set, receives (float) W.
+template <typename GT>
+__device__ void exact_small_cta(int rows, int cols, double* W, double* M, const GT* __restrict__ G, double gs,
+                                double mu, double eps, int iters, double c1, double c2, double* sm, float* Wf) {
   const int n = rows * cols, mn = rows < cols ? rows : cols;
   double *U = sm, *X = U + n, *Xt = X + n, *P = Xt + n, *Q = P + n, *Am = Q + n, *rs = Am + mn * mn,
          *inv = rs + rows;
   const int tid = threadIdx.x, nt = blockDim.x;
-  const double gs = gsp ? *gsp : gs_val;
   for (int i = tid; i < n; i += nt) {
-    const double gi = gs == 1.0 ? G[i] : __dmul_rn(G[i], gs);
+    const double g = (double)G[i];
+    const double gi = gs == 1.0 ? g : __dmul_rn(g, gs);
     const double newm = __dadd_rn(__dmul_rn(mu, M[i]), gi);
     M[i] = newm;
     U[i] = __dadd_rn(gi, __dmul_rn(mu, newm));
@@ -109,12 +108,14 @@ __global__ void __launch_bounds__(256) muon_exact_small_kernel(int rows, int col
   __syncthreads();
   for (int r = tid; r < rows; r += nt) {
     double acc = 0.0;
+#pragma unroll 4
     for (int j = 0; j < cols; j++) acc = __dadd_rn(acc, __dmul_rn(U[r * cols + j], U[r * cols + j]));
     rs[r] = acc;
   }
   __syncthreads();
   if (tid == 0) {
     double acc = 0.0;
+#pragma unroll 8
     for (int i = 0; i < rows; i++) acc = __dadd_rn(acc, rs[i]);
     inv[0] = __ddiv_rn(1.0, __dadd_rn(__dsqrt_rn(acc), eps));
   }
@@ -126,6 +127,7 @@ __global__ void __launch_bounds__(256) muon_exact_small_kernel(int rows, int col
     for (int idx = tid; idx < m * q; idx += nt) {
       const int i = idx / q, j = idx % q;
       double acc = 0.0;
+#pragma unroll 8
       for (int l = 0; l < k; l++) acc = __dadd_rn(acc, __dmul_rn(A[i * k + l], B[l * q + j]));
       Cm[idx] = acc;
     }
@@ -150,7 +152,54 @@ __global__ void __launch_bounds__(256) muon_exact_small_kernel(int rows, int col
     for (int i = tid; i < n; i += nt) X[i] = __dadd_rn(__dadd_rn(__dmul_rn(a, X[i]), __dmul_rn(b, P[i])), __dmul_rn(c, Q[i]));
     __syncthreads();
   }
-  for (int i = tid; i < n; i += nt) W[i] = __dadd_rn(__dmul_rn(c1, W[i]), __dmul_rn(c2, X[i]));
+  for (int i = tid; i < n; i += nt) {
+    const double w = __dadd_rn(__dmul_rn(c1, W[i]), __dmul_rn(c2, X[i]));
+    W[i] = w;
+    if (Wf) Wf[i] = (float)w;
+  }
+}
+__global__ void __launch_bounds__(256) muon_exact_small_kernel(int rows, int cols, double* W, double* M,
+                                                               const double* __restrict__ G, double gs_val,
+                                                               const double* gsp, double mu, double eps,
+                                                               int iters, double c1, double c2) {
+  extern __shared__ double sm[];
+  exact_small_cta<double>(rows, cols, W, M, G, gsp ? *gsp : gs_val, mu, eps, iters, c1, c2, sm, nullptr);
+}
+
+// Every layer's tight-tier step in one launch, one CTA per job: a matrix job is exact_small_cta on the
+// f32 gradient, a bias job (cols == 0) is stepVec (stepvec_f64_kernel's arithmetic); both also write the
+// f32 copies the next forward reads. The gradient scale is read on the device.
+struct ExactJob {
+  double* W;
+  double* M;
+  const float* G;
+  float* Wf;
+  int rows, cols;
+  double c1, c2;
+};
+constexpr int kMaxExactJobs = 32;
+struct ExactJobs {
+  ExactJob j[kMaxExactJobs];
+};
+__global__ void __launch_bounds__(256) muon_exact_group_kernel(const ExactJobs jobs, const double* __restrict__ gsp,
+                                                               double mu, double eps, int iters, double lr, double wd) {
+  extern __shared__ double sm[];
+  const ExactJob jb = jobs.j[blockIdx.x];
+  const double gs = *gsp;
+  if (jb.cols > 0) {
+    exact_small_cta<float>(jb.rows, jb.cols, jb.W, jb.M, jb.G, gs, mu, eps, iters, jb.c1, jb.c2, sm, jb.Wf);
+    return;
+  }
+  for (int i = threadIdx.x; i < jb.rows; i += blockDim.x) {
+    const double g = (double)jb.G[i];
+    const double gi = gs == 1.0 ? g : __dmul_rn(g, gs);
+    const double newm = __dadd_rn(__dmul_rn(mu, jb.M[i]), gi);
+    const double upd = __dadd_rn(gi, __dmul_rn(mu, newm));
+    const double b = __dadd_rn(__dmul_rn(jb.W[i], __dsub_rn(1.0, __dmul_rn(lr, wd))), __dmul_rn(lr, upd));
+    jb.W[i] = b;
+    jb.M[i] = newm;
+    jb.Wf[i] = (float)b;
+  }
 }
 
 int set_ns_coeffs(const double* coeffs, int iters, cudaStream_t st) {
@@ -221,6 +270,45 @@ int muon_mat_exact(int rows, int cols, double* W, double* M, const double* G, do
   finalize_f64_kernel<<<gN, B, 0, st>>>(W, X, c1, c2, W, n);
   count_launch();
   PL_LAUNCH("muon_mat_exact");
+  return PL_OK;
+}
+
+static size_t small_bytes_of(int rows, int cols) {
+  const long n = (long)rows * cols;
+  const int mn = rows < cols ? rows : cols;
+  return sizeof(double) * (size_t)(5 * n + (long)mn * mn + rows + 8);
+}
+bool muon_group_fits(const ExactLayer* ls, int n, int iters) {
+  if (n <= 0 || 2 * n > kMaxExactJobs || iters > 64) return false;
+  for (int i = 0; i < n; i++)
+    if (small_bytes_of(ls[i].rows, ls[i].cols) > kSmallMuonBytes) return false;
+  return true;
+}
+int muon_group_exact(const ExactLayer* ls, int n, double* pm, long P, const float* g, double lr, double wd, double mu,
+                     double eps, int iters, const double* gsp, cudaStream_t st) {
+  PL_REQUIRE(muon_group_fits(ls, n, iters), PL_ERR_INVALID, "exact Muon group does not fit one CTA per matrix");
+  ExactJobs jobs{};
+  size_t smem = 0;
+  volatile double lrwd = lr * wd;  // rounded on its own, as in muon_mat_exact
+  for (int i = 0; i < n; i++) {
+    const ExactLayer& l = ls[i];
+    const double r = (double)l.rows / (double)l.cols;
+    const double scale = sqrt(1.0 <= r ? r : 1.0);
+    jobs.j[2 * i] = ExactJob{pm + l.oW, pm + P + l.oW, g + l.oW, l.Wf, l.rows, l.cols, 1.0 - lrwd, lr * scale};
+    jobs.j[2 * i + 1] = ExactJob{pm + l.ob, pm + P + l.ob, g + l.ob, l.bf, l.rows, 0, 0.0, 0.0};
+    smem = std::max(smem, small_bytes_of(l.rows, l.cols));
+  }
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    PL_CUDA(cudaFuncSetAttribute((const void*)muon_exact_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSmallMuonBytes));
+    attr_set[dev] = true;
+  }
+  muon_exact_group_kernel<<<2 * n, 256, smem, st>>>(jobs, gsp, mu, eps, iters, lr, wd);
+  count_launch();
+  PL_LAUNCH("muon_exact_group_kernel");
   return PL_OK;
 }
 

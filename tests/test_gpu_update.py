@@ -140,6 +140,28 @@ def test_deep_update_tight_tier_vs_oracle(L, act):
     assert rel(got[:P] - pm[:P], ref[:P] - pm[:P]) < 1e-3
 
 
+def test_tight_tier_one_launch_muon_is_bit_identical():
+    """The tight tier's one-launch Muon step of every small layer (f32 gradient widened in the kernel,
+    f32 copies written there) against the per-matrix launch sequence on the widened gradient: the same
+    bits after two epochs of four minibatches."""
+    NT, D, H, A, E, MB, L = 1024, 20, 96, 7, 2, 4, 1
+    P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, D, H, A, L, 41, 0)
+    perm = O.shuffle_perm(NT, E, 79)
+    Lb = plb.lib()
+    Lb.pl_test_exact_group.argtypes = [C.c_int]
+    prev = Lb.pl_test_exact_group(1)
+    try:
+        one, _ = _run_resident(pm, P, (L, 0), obs, acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, 0.02, 0.2, 0.5,
+                               0)
+        Lb.pl_test_exact_group(0)
+        seq, _ = _run_resident(pm, P, (L, 0), obs, acts, adv, ret, olp, ov, perm, NT, D, H, A, E, MB, 0.02, 0.2, 0.5,
+                               0)
+    finally:
+        Lb.pl_test_exact_group(prev)
+    assert np.isfinite(one).all() and not np.array_equal(one[:P], pm[:P])
+    assert np.array_equal(one, seq)
+
+
 @pytest.mark.parametrize("L,act", [(1, 0), (3, 1)])
 def test_deep_update_bf16_tier_vs_oracle(L, act):
     NT, D, H, A, E, MB = 2048, 20, 192, 7, 1, 2
