@@ -554,6 +554,69 @@ def measure_ns_c3(reps=5):
             "frac": tf / (burst or peak_tf), "peak_kind": kind + " (bf16 burst)"}
 
 
+def measure_ns_c3_sharded(comm, rank, world, reps=5, chunks=1):
+    """configs[2] at N > 1: every group's 64 matrices sharded over the ranks and all-gathered
+    (pl_ns_batched_bf16_dev_sharded; each rank orthogonalises its share of a chunk while the previous
+    chunk is all-gathered), timed on the device as the max over ranks. Every rank starts from the same
+    inputs and ends holding every result. The target time is the slower of the flops over N GPUs at the
+    measured burst bf16 rate and the bytes each GPU receives over NVLink at the measured 770 GB/s."""
+    import torch
+    import torch.distributed as dist
+
+    import pufferlean_b200 as plb
+
+    L = plb.lib()
+    co = np.ascontiguousarray(np.array(QUINTIC, dtype=np.float64))
+    dp = C.POINTER(C.c_double)
+    L.pl_ns_batched_bf16_dev_sharded.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_double, dp,
+                                                 C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p]
+    L.pl_ns_shard_chunks.argtypes = [C.c_size_t, C.c_size_t, C.c_size_t, C.POINTER(C.c_size_t),
+                                     C.POINTER(C.c_size_t)]
+    groups = [(64, 128, 128), (64, 512, 512), (64, 512, 2048)]
+    g = torch.Generator(device="cuda").manual_seed(3)
+    Xs = [torch.randn(b, r, c, device="cuda", generator=g).to(torch.bfloat16) for b, r, c in groups]
+    flops = sum(b * 5 * (4 * min(r, c) ** 2 * max(r, c) + 2 * min(r, c) ** 3) for b, r, c in groups)
+    recv = 0
+    for b, r, c in groups:
+        if min(r, c) <= 128:  # run whole on every rank (latency-bound fused kernel): nothing gathered
+            continue
+        cs, used = C.c_size_t(), C.c_size_t()
+        check(L.pl_ns_shard_chunks(b, world, chunks, C.byref(cs), C.byref(used)), L)
+        recv += used.value * (world - 1) * cs.value * r * c * 2
+
+    def run():
+        for X, (b, r, c) in zip(Xs, groups):
+            check(L.pl_ns_batched_bf16_dev_sharded(X.data_ptr(), b, r, c, 1e-7, co.ctypes.data_as(dp), 5, comm, chunks,
+                                                   None), L)
+
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / reps / 1e3], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t = float(t.item())
+    peak_tf, _, kind = peaks()
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    burst = json.load(open(p)).get("bf16_tflops") if os.path.exists(p) else None
+    burst = burst or peak_tf
+    target = max(flops / (world * burst * 1e12), recv / 770e9)
+    return {"config": "configs[2] sharded: 64 x {128^2, 512^2, 512x2048} over %d GPUs, %d chunk(s) per group, "
+                      "all-gathered (the 128^2 group whole on every rank)" % (world, chunks),
+            "n_gpus": world, "flops": flops, "ms": t * 1e3, "achieved_tflops": flops / t / 1e12,
+            "allgather_bytes_received_per_gpu": recv, "allgather_gbs_per_gpu": recv / t / 1e9,
+            "target_ms": target * 1e3, "frac_of_target": target / t,
+            "target_how": "max(flops / (N x measured burst bf16), bytes received per GPU / 770 GB/s peer copy)",
+            "peak_kind": kind + " (bf16 burst)"}
+
+
 WIDE = dict(N=8192, T=64, D=128, H=512, Nmb=65536, epochs=4, lr=0.02)
 
 
@@ -1110,10 +1173,12 @@ def main():
             out["strong_scaling"]["config"] = s_out["config"]
             out["strong_scaling"]["profile"] = s_out["profile"]
     if world > 1 and not args.no_extra:
-        # configs[3] on every rank (its data-parallel form), before the communicator goes away
+        # configs[3] and configs[2] on every rank (their multi-GPU forms), before the communicator goes away
         c4 = measure_mingru_c4(args, comm=state["comm"], rank=rank, world=world)
+        c3s = measure_ns_c3_sharded(state["comm"], rank, world)
         if rank == 0:
             out["c4_mingru"] = c4
+            out["c3_newton_schulz_sharded"] = c3s
     if state.get("comm"):
         plb.lib().pl_comm_destroy.argtypes = [C.c_void_p]
         plb.lib().pl_comm_destroy(state["comm"])

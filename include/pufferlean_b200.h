@@ -112,6 +112,26 @@ int pl_muon_stepmat(const double* W, const double* G, const double* M, size_t ro
 int pl_ns_batched_bf16_dev(void* X, size_t batch, size_t rows, size_t cols, double eps, const double* coeffs,
                            size_t iters, void* stream);
 
+/* The same batched Newton-Schulz over the ranks of a communicator (pl_comm_create): every rank passes
+ * the same batch and ends with every result, bit-identical to pl_ns_batched_bf16_dev on one GPU. The
+ * batch is cut into `chunks` chunks of world * cs matrices; in each chunk a rank orthogonalises its cs
+ * matrices in place and the chunk is all-gathered (ncclAllGather, in place) on a second stream while
+ * the next chunk is orthogonalised; the matrices left over (fewer than world * chunks) are
+ * orthogonalised on every rank under the last all-gather. A batch whose short side is at most 128
+ * runs whole on every rank (its fused kernel is latency-bound: sharding would only add the gather).
+ * Work is enqueued on `stream`, which waits for the gathers. A collective: every rank calls it with
+ * the same shape and chunk count.
+ * BASELINE configs[2] at N > 1 ("sharded across 1/2/4/8 GPUs, followed by an all-gather"); no
+ * counterpart in the reference, which has no multi-GPU code. */
+int pl_ns_batched_bf16_dev_sharded(void* X, size_t batch, size_t rows, size_t cols, double eps,
+                                   const double* coeffs, size_t iters, void* comm, size_t chunks, void* stream);
+/* The plan pl_ns_batched_bf16_dev_sharded follows: *per_rank matrices per rank and chunk and *used
+ * chunks (the request clamped to [1, 16] and lowered until a chunk holds at least one matrix per
+ * rank; 0 chunks when the batch has fewer matrices than ranks). Chunk c's rank r matrices are
+ * [c world per_rank + r per_rank, c world per_rank + (r + 1) per_rank); the rest of the batch, from
+ * used * world * per_rank on, runs on every rank. Host only. */
+int pl_ns_shard_chunks(size_t batch, size_t world, size_t chunks, size_t* per_rank, size_t* used);
+
 /* The same batched Newton-Schulz without allocating device memory, for callers that cannot call
  * cudaMalloc: hosts whose device memory belongs to another allocator or to a budget fixed at
  * start-up, and loops that must stay off the driver's allocator (whose calls can block and

@@ -46,6 +46,7 @@ struct NcclApi {
   ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*Broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
@@ -100,6 +101,9 @@ static ncclResult_t AllReduce(const void*, void*, size_t, ncclDataType_t, ncclRe
 static ncclResult_t Broadcast(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) {
   return ncclSuccess;
 }
+static ncclResult_t AllGather(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) {
+  return ncclSuccess;
+}
 static ncclResult_t GroupStart() { return ncclSuccess; }
 static ncclResult_t GroupEnd() { return ncclSuccess; }
 static const char* GetErrorString(ncclResult_t r) {
@@ -117,6 +121,7 @@ static NcclApi make_fake() {
   a.CommGetAsyncError = fake::CommGetAsyncError;
   a.AllReduce = fake::AllReduce;
   a.Broadcast = fake::Broadcast;
+  a.AllGather = fake::AllGather;
   a.GroupStart = fake::GroupStart;
   a.GroupEnd = fake::GroupEnd;
   a.GetErrorString = fake::GetErrorString;
@@ -141,13 +146,14 @@ static const NcclApi* nccl() {
     PL_SYM(CommGetAsyncError);
     PL_SYM(AllReduce);
     PL_SYM(Broadcast);
+    PL_SYM(AllGather);
     PL_SYM(GroupStart);
     PL_SYM(GroupEnd);
     PL_SYM(GetErrorString);
 #undef PL_SYM
     g_nccl.StreamDone = real_stream_done;
     g_nccl.ok = g_nccl.GetUniqueId && g_nccl.CommInitRankConfig && g_nccl.CommDestroy && g_nccl.CommAbort &&
-                g_nccl.CommGetAsyncError && g_nccl.AllReduce && g_nccl.Broadcast && g_nccl.GroupStart &&
+                g_nccl.CommGetAsyncError && g_nccl.AllReduce && g_nccl.Broadcast && g_nccl.AllGather && g_nccl.GroupStart &&
                 g_nccl.GroupEnd && g_nccl.GetErrorString;
   });
   return g_nccl.ok ? &g_nccl : nullptr;
@@ -250,6 +256,20 @@ int comm_allreduce_f64(void* comm, double* buf, size_t n, cudaStream_t st) {
   int rc = usable(comm, &c);
   if (rc) return rc;
   return after_call(c, nccl()->AllReduce(buf, buf, n, ncclFloat64, ncclSum, c->nc, st), "ncclAllReduce(f64)");
+}
+int comm_allgather_bf16(void* comm, const void* send, void* recv, size_t count, cudaStream_t st) {
+  PlComm* c = nullptr;
+  int rc = usable(comm, &c);
+  if (rc) return rc;
+  return after_call(c, nccl()->AllGather(send, recv, count, ncclBfloat16, c->nc, st), "ncclAllGather(bf16)");
+}
+int comm_rank_world(void* comm, int* rank, int* world) {
+  PlComm* c = nullptr;
+  int rc = usable(comm, &c);
+  if (rc) return rc;
+  *rank = c->rank;
+  *world = c->world;
+  return PL_OK;
 }
 int comm_broadcast_group(void* comm, const std::vector<float*>& bufs, const std::vector<size_t>& counts,
                          const std::vector<int>& roots, cudaStream_t st) {

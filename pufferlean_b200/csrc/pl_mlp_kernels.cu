@@ -11,7 +11,7 @@
 
 namespace pl {
 
-constexpr int kRedBlocks = 296;  // 2 x 148 SMs: fixed partition of every grid-wide reduction
+constexpr int kStreamBlocks = 1184;  // 8 x 148 SMs: fixed partition of the streaming reductions (loads in flight)
 
 __device__ __forceinline__ double block_sum_f64(double v, double* sh) {
   // fixed-shape tree over a 256-thread block
@@ -265,7 +265,7 @@ __global__ void splitk_reduce_warp_kernel(const float* __restrict__ part, int S,
   }
   if (lane == 0) reinterpret_cast<float4*>(out)[w] = s;
 }
-// Global gradient norm of g*sc: fixed grid of kRedBlocks blocks x 256 threads, strided f64 sums.
+// Global gradient norm of g*sc: fixed grid of kStreamBlocks blocks x 256 threads, strided f64 sums.
 __global__ void __launch_bounds__(256) gradnorm_part_kernel(const float* __restrict__ g, long P, double sc,
                                                             double* part) {
   __shared__ double sh[256];
@@ -346,10 +346,9 @@ __global__ void __launch_bounds__(256) ns_input_kernel(const double* __restrict_
                                                        long ldx) {
   __shared__ double inv_s;
   __shared__ __nv_bfloat16 tile[32][34];
-  if (threadIdx.x == 0) {
-    double s = 0.0;
-    for (int b = 0; b < nparts; b++) s += part[b];
-    inv_s = 1.0 / (sqrt(s) + eps);
+  if (threadIdx.x < 32) {
+    const double s = warp_fold_f64(part, nparts, 1);
+    if (threadIdx.x == 0) inv_s = 1.0 / (sqrt(s) + eps);
   }
   __syncthreads();
   const double inv = inv_s;
@@ -888,7 +887,7 @@ int launch_gather(bool bf16, const int* idx, int Nmb, const void* obs, int rowEl
                   const double* adv_c, const float* ret_c, const float* olp_c, const float* ov_c, int* mb_act,
                   float* mb_adv, float* mb_ret, float* mb_olp, float* mb_ov, double* part, double* ms,
                   cudaStream_t st, double* sums, const int* oidx) {
-  const int nb = (int)(Nmb < kRedBlocks * 8 ? (Nmb + 7) / 8 : kRedBlocks);
+  const int nb = (int)(Nmb < kStreamBlocks * 8 ? (Nmb + 7) / 8 : kStreamBlocks);
   if (bf16)
     gather_kernel<true><<<nb, 256, 0, st>>>(idx, Nmb, obs, rowElems, X, act_c, adv_c, ret_c, olp_c, ov_c, mb_act,
                                             mb_adv, mb_ret, mb_olp, mb_ov, part, oidx);
@@ -934,15 +933,15 @@ int launch_splitk_reduce(const float* part, int S, long n, float* out, cudaStrea
   return PL_OK;
 }
 int launch_gradnorm(const float* g, long P, double sc, double maxNorm, double* part, double* cc, cudaStream_t st) {
-  gradnorm_part_kernel<<<kRedBlocks, 256, 0, st>>>(g, P, sc, part);
-  gradnorm_final_kernel<<<1, 32, 0, st>>>(part, kRedBlocks, maxNorm, sc, cc);
+  gradnorm_part_kernel<<<kStreamBlocks, 256, 0, st>>>(g, P, sc, part);
+  gradnorm_final_kernel<<<1, 32, 0, st>>>(part, kStreamBlocks, maxNorm, sc, cc);
   count_launch(2);
   PL_LAUNCH("gradnorm_kernel");
   return PL_OK;
 }
 int launch_nesterov(const float* g, const double* cc, double* mom, double* u, double mu, long n, double* part,
                     int* nparts, cudaStream_t st) {
-  const int nb = (int)(n < (long)kRedBlocks * 256 ? ceil_div(n, 256) : kRedBlocks);
+  const int nb = (int)(n < (long)kStreamBlocks * 256 ? ceil_div(n, 256) : kStreamBlocks);
   nesterov_kernel<<<nb, 256, 0, st>>>(g, cc, mom, u, mu, n, part);
   *nparts = nb;
   count_launch();
