@@ -578,7 +578,7 @@ def measure_ns_c3_sharded(comm, rank, world, reps=5, chunks=1):
     flops = sum(b * 5 * (4 * min(r, c) ** 2 * max(r, c) + 2 * min(r, c) ** 3) for b, r, c in groups)
     recv = 0
     for b, r, c in groups:
-        if min(r, c) <= 128:  # run whole on every rank (latency-bound fused kernel): nothing gathered
+        if min(r, c) <= 128 and max(r, c) <= 512:  # whole on every rank (latency-bound fused kernel)
             continue
         cs, used = C.c_size_t(), C.c_size_t()
         check(L.pl_ns_shard_chunks(b, world, chunks, C.byref(cs), C.byref(used)), L)

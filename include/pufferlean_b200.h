@@ -117,8 +117,9 @@ int pl_ns_batched_bf16_dev(void* X, size_t batch, size_t rows, size_t cols, doub
  * batch is cut into `chunks` chunks of world * cs matrices; in each chunk a rank orthogonalises its cs
  * matrices in place and the chunk is all-gathered (ncclAllGather, in place) on a second stream while
  * the next chunk is orthogonalised; the matrices left over (fewer than world * chunks) are
- * orthogonalised on every rank under the last all-gather. A batch whose short side is at most 128
- * runs whole on every rank (its fused kernel is latency-bound: sharding would only add the gather).
+ * orthogonalised on every rank under the last all-gather. A batch of matrices with a short side of at
+ * most 128 and a long side of at most 512 runs whole on every rank (its fused one-CTA-per-matrix
+ * kernel is latency-bound: sharding would only add the gather).
  * Work is enqueued on `stream`, which waits for the gathers. A collective: every rank calls it with
  * the same shape and chunk count.
  * BASELINE configs[2] at N > 1 ("sharded across 1/2/4/8 GPUs, followed by an all-gather"); no

@@ -29,16 +29,21 @@ typedef struct {
 
 int pl_test_gemm(const pl_test_gemm_args* g, void* stream);
 /* Selects the GEMM's tile mode for every later launch in this process: 0 = single-CTA tiles only,
- * the default, 1 = CTA pairs (cta_group::2, 256-row tiles) where eligible; a negative mode only
- * queries. Returns the previous mode. */
+ * 1 = CTA pairs (cta_group::2, 256-row tiles) where eligible, 2 = CTA pairs for products whose two
+ * operands are MN-major (the weight gradients) only; a negative mode only queries. Returns the
+ * previous mode. */
 int pl_test_gemm_pair_mode(int mode);
 /* Newton-Schulz for matrices with both sides <= 128: 1 = one fused CTA per matrix (the default),
  * 0 = the per-step GEMM chain; a negative mode only queries. Returns the previous mode. */
 int pl_test_ns_small_mode(int mode);
 /* Newton-Schulz for batches with m = min(rows, cols) > 128: 1 = all steps in one persistent
- * cooperative launch (the default; not used while the stream is being captured), 0 = three GEMM
+ * cooperative launch (the default; see pl_test_ns_chain_capture for stream capture), 0 = three GEMM
  * launches per step; a negative mode only queries. Returns the previous mode. */
 int pl_test_ns_chain_mode(int mode);
+/* While a stream is being captured into a CUDA graph: 1 = the persistent Newton-Schulz chain is recorded
+ * as a cooperative kernel node (the default), 0 = the per-step GEMM launches are recorded instead; a
+ * negative mode only queries. Returns the previous mode. */
+int pl_test_ns_chain_capture(int mode);
 /* Host observations in the bf16 tier: 1 = rounded to bf16 on the host threads, a quarter of the bytes
  * copied (the default), 0 = f64 rows copied and converted on the device; a negative mode only
  * queries. Returns the previous mode. */

@@ -18,13 +18,15 @@ GemmKernel gemm_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_b
 GemmKernel gemm_instance_at(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
 GemmKernel gemm_pair_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
 
-// 0: single CTAs only (default: on B200 the single-CTA main loop already streams at the MMA rate these
-// shapes allow, and the pair's cluster set-up costs more than its halved B traffic saves); 1: CTA pairs
-// for 256-wide tiles of at least 256 rows.
+// 0: single CTAs only; 1: CTA pairs for every 256-wide tile of at least 256 rows; 2: CTA pairs for the
+// weight gradients only (both operands MN-major). Measured on the C5 update (262,144-row minibatches):
+// pairs run the weight gradient at 1,152 against 1,052 TFLOP/s, the forward (1,026 vs 1,053) and the
+// data gradient (850 vs 916) slower; the pair form also draws less power per flop (median SM clock
+// 1,440 against 1,372 MHz under the same power cap).
 static int g_pair_mode = 0;
 int gemm_set_pair_mode(int mode) {
   const int prev = g_pair_mode;
-  if (mode >= 0) g_pair_mode = mode ? 1 : 0;
+  if (mode >= 0) g_pair_mode = mode <= 2 ? mode : 0;
   return prev;
 }
 
@@ -91,7 +93,7 @@ int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const O
              "GEMM B storage %ldx%ld too small for N=%d K=%d", B.rows, B.cols, N, K);
   uint32_t smem = 0;
   GemmKernel k = nullptr;
-  const bool pair = g_pair_mode == 1 && bn == 256 && epi != EPI_PPO && M > 128 &&
+  const bool pair = (g_pair_mode == 1 || (g_pair_mode == 2 && a_mn && b_mn)) && bn == 256 && epi != EPI_PPO && M > 128 &&
                     (k = gemm_pair_instance(bn, epi, a_mn, b_mn, &smem)) != nullptr;
   // the data gradient of a short-K product (the head's, K <= 128) is a memory-bound epilogue: 128-wide
   // tiles whose aux comes through TMA into shared memory (needs the staged stores, checked below)

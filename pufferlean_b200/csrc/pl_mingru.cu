@@ -1076,7 +1076,10 @@ int ensure_work(pl_mg* s, const MgShape& sh, long Bmb, long T, bool fast) {
     w.ns.Xf = mg_alloc<float>(w.allocs, (size_t)mmax * ldx, f);
     w.ns.U = mg_alloc<double>(w.allocs, nprod, f);
     w.ns.part = mg_alloc<double>(w.allocs, 4096, f);
+    // the persistent Newton-Schulz chain's per-matrix counters (one matrix per call, each stream its own)
+    w.ns.cnt = mg_alloc<unsigned>(w.allocs, (size_t)ns_chain_counter_words(1), f);
     w.ns2 = w.ns;
+    w.ns2.cnt = mg_alloc<unsigned>(w.allocs, (size_t)ns_chain_counter_words(1), f);
     w.ns2.X0 = mg_alloc<bf16>(w.allocs, (size_t)rup(mmax, 128) * ldx, f, true);
     w.ns2.X1 = mg_alloc<bf16>(w.allocs, (size_t)rup(mmax, 128) * ldx, f, true);
     w.ns2.G = mg_alloc<bf16>(w.allocs, (size_t)rup(mmax, 128) * ldg, f, true);

@@ -32,6 +32,7 @@ int ns_set_small_mode(int mode);
 // 0 = every batch takes the per-step GEMM launches, 1 = batches with m > 128 run as one persistent
 // cooperative launch when the workspace has counters (default); a negative mode only queries.
 int ns_set_chain_mode(int mode);
+int ns_set_chain_capture(int mode);
 long ns_chain_counter_words(long batch);
 // One group of same-shape wide matrices for the persistent chain: iterate 0 is X, later iterates
 // alternate between xbuf[1] and xbuf[0]; G / B the m x m workspaces; the last step writes out_f32,

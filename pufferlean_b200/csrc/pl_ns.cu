@@ -25,13 +25,15 @@ int ns_run(int m, int n, const double* coeffs, int iters, NsWork& w, __nv_bfloat
   return ns_run_batched(m, n, 1, coeffs, iters, w, X, ldx, 0, out_f32, ld_out, 0, st);
 }
 
-// ---------------------------------------------------------------- fused path for small matrices
-// Matrices with m, n <= 128 run every step inside one CTA: X (zero-padded to 128 x 128) stays in shared
-// memory in the 128-byte-swizzled K-major layout the tensor core reads, and each step is three chained
-// tcgen05.mma groups whose accumulators sit in TMEM columns [0,128) (G = X X^T), [128,256) (G G) and
-// [256,384) (X' = Pm X). Between them the four warps rewrite the next operand in shared memory: G in
-// bf16, then Pm = a I + b G + c G G (G as rounded to bf16, G G from the accumulator), then X' over X. X serves as the second
-// operand of X' = Pm X read MN-major, where it lies. One launch replaces 3 x iters GEMM launches.
+// ---------------------------------------------------------------- fused path for short matrices
+// Matrices with m <= 128 and n <= 512 run every step inside one CTA: X (zero-padded to 128 rows and
+// to a whole number of 64-column atoms) stays in shared memory in the 128-byte-swizzled K-major layout
+// the tensor core reads, and each step is three chained tcgen05.mma groups: G = X X^T into TMEM columns
+// [0,128), G G into [128,256), then X' = Pm X over columns [0, n) in products of at most 256 columns
+// (G and G G have been read by then). Between them the four warps rewrite the next operand in shared
+// memory: G in bf16, then Pm = a I + b G + c G G (G as rounded to bf16, G G from the accumulator),
+// then X' over X. X serves as the second operand of X' = Pm X read MN-major, where it lies. One launch
+// replaces 3 x iters GEMM launches.
 struct NsSmallCoef {
   float c[3 * 16];
 };
@@ -68,15 +70,22 @@ __device__ __forceinline__ void ns_ld32(uint32_t taddr, float (&v)[32]) {
   }
 }
 
+constexpr int kNsSmallMaxN = 512;
+// Shared memory of the fused kernel for an n-column matrix: X in 64-column atoms, G / Pm, the barrier.
+__host__ __device__ constexpr uint32_t ns_small_smem(int n) {
+  return 1024u + (uint32_t)((n + 63) / 64) * 16384u + 32768u + 64u;
+}
+
 __global__ void __launch_bounds__(128, 1)
     ns_small_kernel(const __nv_bfloat16* __restrict__ X, long ldx, long xbs, int m, int n, NsSmallCoef coef,
                     int iters, __nv_bfloat16* out_bf16, long ldo, long obs, float* out_f32, long ldf, long obsf,
                     unsigned* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* Xs = smem;           // 32 KB: X, then each X'
-  uint8_t* Gs = smem + 32768;   // 32 KB: G, then Pm
-  uint64_t* bar = (uint64_t*)(smem + 65536);
+  const int natoms = (n + 63) / 64, npad = 64 * natoms;  // 64-column atoms of X
+  uint8_t* Xs = smem;                        // natoms x 16 KB: X, then each X'
+  uint8_t* Gs = smem + natoms * 16384;       // 32 KB: G, then Pm
+  uint64_t* bar = (uint64_t*)(Gs + 32768);
   uint32_t* tslot = (uint32_t*)(bar + 1);
   volatile int* abort_flag = (volatile int*)(tslot + 1);
   const int t = threadIdx.x, warp = t >> 5;
@@ -96,7 +105,7 @@ __global__ void __launch_bounds__(128, 1)
     const __nv_bfloat16* xr = X + b * xbs + (long)r * ldx;
     const bool vec = ((ldx & 7) == 0) && ((((uintptr_t)X) & 15) == 0) && ((xbs & 7) == 0);
 #pragma unroll 4
-    for (int ch = 0; ch < 16; ch++) {
+    for (int ch = 0; ch < 8 * natoms; ch++) {
       uint4 w = make_uint4(0, 0, 0, 0);
       if (r < m) {
         if (vec && ch * 8 + 8 <= n) {
@@ -117,19 +126,31 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t tbase = *tslot;
   const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);
   constexpr uint32_t ID_KK = tc::idesc_bf16(128, 128, 0, 0);
-  constexpr uint32_t ID_KM = tc::idesc_bf16(128, 128, 0, 1);
   const uint32_t xa = tc::smem_u32(Xs), ga = tc::smem_u32(Gs);
   uint32_t phase = 0;
-  // D[tmem col dcol] = A B^T over K = 128 (8 slices of 16); B read MN-major when b_mn
-  auto mma = [&](uint32_t dcol, uint32_t a, uint32_t bb, bool b_mn) {
+  // D[tmem col dcol] = A B^T over K = 16 kslices, N = 128, both operands K-major (G = X X^T over the
+  // n columns, G G over 128); or, b_mn, X' = Pm X: K = 128, B = X read MN-major, in products of up to
+  // 256 columns side by side in TMEM
+  auto mma = [&](uint32_t dcol, uint32_t a, uint32_t bb, bool b_mn, int kslices) {
     if (t == 0) {
       tc::tc_fence_after();
+      if (!b_mn) {
+        for (int kk = 0; kk < kslices; kk++) {
+          const uint64_t ad = tc::sw128_desc(a + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::sw128_desc(bb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          tc::umma_bf16(tbase + dcol, ad, bd, ID_KK, kk > 0 ? 1u : 0u);
+        }
+      } else {
+        for (int c0 = 0; c0 < npad; c0 += 256) {
+          const int nc = npad - c0 < 256 ? npad - c0 : 256;
+          const uint32_t idesc = tc::idesc_bf16(128, nc, 0, 1);
 #pragma unroll
-      for (int kk = 0; kk < 8; kk++) {
-        const uint64_t ad = tc::sw128_desc(a + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-        const uint64_t bd = b_mn ? tc::sw128_desc(bb + kk * 2048, 16384, 1024)
-                                 : tc::sw128_desc(bb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-        tc::umma_bf16(tbase + dcol, ad, bd, b_mn ? ID_KM : ID_KK, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 8; kk++) {
+            const uint64_t ad = tc::sw128_desc(a + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = tc::sw128_desc(bb + (c0 / 64) * 16384 + kk * 2048, 16384, 1024);
+            tc::umma_bf16(tbase + dcol + (uint32_t)c0, ad, bd, idesc, kk > 0 ? 1u : 0u);
+          }
+        }
       }
       tc::umma_commit(bar);
     }
@@ -145,7 +166,7 @@ __global__ void __launch_bounds__(128, 1)
   };
   for (int it = 0; it < iters && !*abort_flag; it++) {
     const float ca = coef.c[3 * it], cb = coef.c[3 * it + 1], cc = coef.c[3 * it + 2];
-    mma(0, xa, xa, false);  // G = X X^T
+    mma(0, xa, xa, false, 4 * natoms);  // G = X X^T
     float v[32], g2[32];
 #pragma unroll 1
     for (int c0 = 0; c0 < 128; c0 += 32) {
@@ -153,7 +174,7 @@ __global__ void __launch_bounds__(128, 1)
       ns_put32(Gs, r, c0, v);
     }
     publish();
-    mma(128, ga, ga, false);  // G G (G symmetric: its rows serve as its columns)
+    mma(128, ga, ga, false, 8);  // G G (G symmetric: its rows serve as its columns)
 #pragma unroll 1
     for (int c0 = 0; c0 < 128; c0 += 32) {
       ns_ld32(trow + c0, v);
@@ -168,11 +189,11 @@ __global__ void __launch_bounds__(128, 1)
       ns_put32(Gs, r, c0, v);
     }
     publish();
-    mma(256, ga, xa, true);  // X' = Pm X
+    mma(0, ga, xa, true, 8);  // X' = Pm X
     const bool last = it + 1 == iters;
 #pragma unroll 1
-    for (int c0 = 0; c0 < 128; c0 += 32) {
-      ns_ld32(trow + 256 + c0, v);
+    for (int c0 = 0; c0 < npad; c0 += 32) {
+      ns_ld32(trow + c0, v);
       if (!last) {
         ns_put32(Xs, r, c0, v);
       } else if (r < m) {
@@ -197,7 +218,6 @@ __global__ void __launch_bounds__(128, 1)
     tc::tmem_dealloc(tbase, 512);
   }
 }
-constexpr uint32_t kNsSmallSmem = 1024 + 65536 + 64;
 static int g_ns_small = 1;  // 0: small matrices also take the per-step GEMM chain (tests compare the two)
 int ns_set_small_mode(int mode) {
   const int prev = g_ns_small;
@@ -213,18 +233,20 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
   PL_REQUIRE(m <= n, PL_ERR_INVALID, "Newton-Schulz expects the wide layout (m=%d > n=%d)", m, n);
   PL_REQUIRE(!scale0 || (m > 128 && iters >= 2), PL_ERR_INVALID,
              "Newton-Schulz: an unnormalised input needs m > 128 and at least two steps");
-  if (g_ns_small && n <= 128 && iters <= kNsSmallMaxIters && batch <= 65535) {
+  if (g_ns_small && m <= 128 && n <= kNsSmallMaxN && iters <= kNsSmallMaxIters && batch <= 65535) {
     NsSmallCoef cf{};
     for (int i = 0; i < 3 * iters; i++) cf.c[i] = (float)coeffs[i];
     const long xbs_eff = batch > 1 ? xbs : (long)ldx * m;
     __nv_bfloat16* dst = final_bf16 ? final_bf16 : X;  // the result ends in place unless told otherwise
-    static bool configured = false;
-    if (!configured) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    PL_CUDA(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
       PL_CUDA(cudaFuncSetAttribute((const void*)ns_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)kNsSmallSmem));
-      configured = true;
+                                   (int)ns_small_smem(kNsSmallMaxN)));
+      configured[dev] = true;
     }
-    ns_small_kernel<<<(unsigned)batch, 128, kNsSmallSmem, st>>>(
+    ns_small_kernel<<<(unsigned)batch, 128, ns_small_smem(n), st>>>(
         X, ldx, xbs_eff, m, n, cf, iters, out_f32 ? nullptr : dst, ldx, xbs_eff, out_f32, ld_out,
         batch > 1 ? obs : (long)ld_out * m, w.err ? w.err : device_error_word());
     count_launch();

@@ -11,8 +11,8 @@
 // matrix's result depends only on that matrix (the batched kernels take the same path whatever the
 // batch size), so the sharded result is bit-identical to one GPU's.
 //
-// Matrices whose short side is at most 128 are not sharded: the fused kernel that takes them (one CTA
-// per matrix, all steps in shared memory) is latency-bound, its time does not shrink with the batch
+// Matrices with a short side of at most 128 and a long side of at most 512 are not sharded: the fused
+// kernel that takes them (one CTA per matrix, all steps in shared memory) is latency-bound, its time does not shrink with the batch
 // (configs[2]'s 64 x 128^2: 55 us for all 64 on one GPU, 50 us for 32), so sharding would only add
 // the all-gather. Chunks overlap little in practice: the persistent Newton-Schulz kernel is a
 // cooperative launch over every SM, so a chunk's all-gather kernels get SMs only between chunks
@@ -77,7 +77,8 @@ extern "C" int pl_ns_batched_bf16_dev_sharded(void* Xv, size_t batch, size_t row
   size_t cs = 0, nch = 0;
   rc = pl_ns_shard_chunks(batch, (size_t)world, chunks, &cs, &nch);
   if (rc) return rc;
-  if (nch == 0 || (rows < cols ? rows : cols) <= 128)  // nothing to shard, or the latency-bound fused kernel
+  const size_t mside = rows < cols ? rows : cols, nside = rows < cols ? cols : rows;
+  if (nch == 0 || (mside <= 128 && nside <= 512))  // nothing to shard, or the latency-bound fused kernel
     return pl_ns_batched_bf16_dev(Xv, batch, rows, cols, eps, coeffs, iters, stream);
   ShardStreams* ss = nullptr;
   rc = shard_streams(&ss);

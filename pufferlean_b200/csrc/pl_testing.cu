@@ -45,6 +45,7 @@ extern "C" int pl_test_gemm(const pl_test_gemm_args* g, void* stream) {
 extern "C" int pl_test_gemm_pair_mode(int mode) { return pl::gemm_set_pair_mode(mode); }
 extern "C" int pl_test_ns_small_mode(int mode) { return pl::ns_set_small_mode(mode); }
 extern "C" int pl_test_ns_chain_mode(int mode) { return pl::ns_set_chain_mode(mode); }
+extern "C" int pl_test_ns_chain_capture(int mode) { return pl::ns_set_chain_capture(mode); }
 
 extern "C" int pl_test_device_error(unsigned* code) {
   unsigned* w = pl::device_error_word();

@@ -134,3 +134,41 @@ def test_folded_normalisation_vs_oracle(batch, rows, cols, steps):
     for i in range(batch):
         ref = O.newton_schulz(Xin[i].ravel(), rows, cols, 1e-7, co).reshape(rows, cols)
         assert rel(got[i], ref) < 2e-2, (i, rel(got[i], ref))
+
+
+@pytest.mark.parametrize("batch,rows,cols", [(2, 512, 1024), (1, 1024, 512)])
+def test_chain_recorded_in_a_graph_equals_eager(batch, rows, cols):
+    """The persistent chain recorded into a CUDA graph (a cooperative kernel node) and replayed gives the
+    eager launch's bits, twice in a row (the graph's counter resets run with it)."""
+    L = plb.lib()
+    L.pl_test_ns_chain_capture.argtypes = [C.c_int]
+    co = np.ascontiguousarray(O.QUINTIC_COEFFS)
+    torch.manual_seed(rows + cols + batch)
+    X0 = torch.randn(batch, rows, cols, device="cuda").to(torch.bfloat16)
+    prev_c, prev_g = _chain(1), L.pl_test_ns_chain_capture(1)
+    try:
+        Xe = X0.clone()
+        _ns(Xe, batch, rows, cols, co)
+        Xg = X0.clone()
+        st = torch.cuda.Stream()
+        fn = L.pl_ns_batched_bf16_dev
+        fn.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_double, DP, C.c_size_t, C.c_void_p]
+        with torch.cuda.stream(st):  # warm-up: the workspace is allocated outside the capture
+            assert fn(Xg.data_ptr(), batch, rows, cols, 1e-7, co.ctypes.data_as(DP), co.shape[0], st.cuda_stream) == 0
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            rc = fn(Xg.data_ptr(), batch, rows, cols, 1e-7, co.ctypes.data_as(DP), co.shape[0],
+                    torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, L.pl_last_error()
+        for _ in range(2):
+            Xg.copy_(X0)
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(Xg, Xe)
+        code = C.c_uint(0)
+        assert L.pl_test_device_error(C.byref(code)) == 0 and code.value == 0, hex(code.value)
+        del g
+    finally:
+        _chain(prev_c)
+        L.pl_test_ns_chain_capture(prev_g)

@@ -1,7 +1,8 @@
-"""The fused small-matrix Newton-Schulz (one CTA per matrix, every step chained in TMEM) against the f64
-oracle and against the per-step tcgen05 GEMM chain on the same inputs: square, wide, tall (transposed on
-the way in and out), ragged sides, the configs[2] 128 x 128 batch, and the fp32-output form inside a
-CartPole-shaped bf16 update."""
+"""The fused short-matrix Newton-Schulz (one CTA per matrix with a short side <= 128 and a long side
+<= 512, every step chained in TMEM) against the f64 oracle and against the per-step tcgen05 GEMM chain on
+the same inputs: square, wide, tall (transposed on the way in and out), ragged sides, long sides of 200
+to 512 (the MinGRU encoder's 512 x 120 among them), the configs[2] 128 x 128 batch, and the fp32-output
+form inside a CartPole-shaped bf16 update."""
 import ctypes as C
 
 import numpy as np
@@ -40,7 +41,8 @@ def _ns(X, batch, rows, cols, co):
 
 
 @pytest.mark.parametrize("batch,rows,cols", [(64, 128, 128), (3, 64, 128), (2, 128, 8), (5, 8, 128), (4, 40, 96),
-                                             (1, 8, 8), (2, 120, 128)])
+                                             (1, 8, 8), (2, 120, 128), (2, 120, 512), (3, 512, 120), (2, 64, 320),
+                                             (1, 128, 512), (2, 96, 200), (2, 8, 384), (4, 128, 256)])
 def test_small_ns_fused_vs_oracle_and_chain(batch, rows, cols):
     torch.manual_seed(rows * 7 + cols)
     X0 = torch.randn(batch, rows, cols, device="cuda").to(torch.bfloat16)
