@@ -554,6 +554,40 @@ __global__ void __launch_bounds__(256) skinny_rows_kernel(const float* __restric
     }
   }
 }
+// Weight and bias gradient partials of a small layer (out + in <= 192): block z copies rows
+// [64 z, 64 z + 64) of dZ (ldz) and Hin (ldh) into shared memory with coalesced loads, then each thread
+// sums its outputs (o, c) over those rows in row order, c = in being the bias (a column of ones), into
+// part[z][o][c]; splitk_reduce_wb_kernel sums the slices.
+constexpr int kWgRows = 64, kWgMaxCols = 192;
+__global__ void __launch_bounds__(256) wgrad_small_kernel(int out, int in, int K, const float* __restrict__ dZ,
+                                                          long ldz, const float* __restrict__ Hin, long ldh,
+                                                          float* part) {
+  __shared__ float sm[kWgRows * kWgMaxCols];
+  float* sZ = sm;                   // [rows][out]
+  float* sH = sm + kWgRows * out;   // [rows][in]
+  const int r0 = blockIdx.x * kWgRows, nr = min(kWgRows, K - r0);
+  for (int i = threadIdx.x; i < nr * out; i += blockDim.x) {
+    const int r = i / out, o = i - r * out;
+    sZ[i] = dZ[(long)(r0 + r) * ldz + o];
+  }
+  for (int i = threadIdx.x; i < nr * in; i += blockDim.x) {
+    const int r = i / in, c = i - r * in;
+    sH[i] = Hin[(long)(r0 + r) * ldh + c];
+  }
+  __syncthreads();
+  const int n = in + 1, total = out * n;
+  float* dst = part + (long)blockIdx.x * total;
+  for (int q = threadIdx.x; q < total; q += blockDim.x) {
+    const int o = q / n, c = q - o * n;
+    float acc = 0.f;
+    if (c < in) {
+      for (int r = 0; r < nr; r++) acc += sZ[r * out + o] * sH[r * in + c];
+    } else {
+      for (int r = 0; r < nr; r++) acc += sZ[r * out + o];
+    }
+    dst[q] = acc;
+  }
+}
 // Split-K slices of a weight gradient with its bias column: part[s][m][in + 1]; out dW[m][in] and
 // db[m], each the sum over s in a fixed order (lane-strided runs, then a butterfly), one warp per output.
 __global__ void splitk_reduce_wb_kernel(const float* __restrict__ part, int S, int M, int in, float* dW, float* db) {
@@ -1035,12 +1069,24 @@ int launch_skinny_rows(const float* H, int rows, int K, const float* W, const fl
   return PL_OK;
 }
 long splitk_wb_elems(int K, int out, int in) {
+  if (out + in <= kWgMaxCols) return ceil_div(K, kWgRows) * out * (long)(in + 1);  // wgrad_small_kernel
   return std::min<long>(ceil_div(K, 64), ceil_div(8 * 148, ceil_div(in + 1, 64) * ceil_div(out, 64))) * out *
          (long)(in + 1);
 }
 int launch_wgrad_bias_f32(int out, int in, int K, const float* dZ, long ldz, const float* Hin, long ldh, float* dW,
                           float* db, float* ws, long ws_elems, cudaStream_t st) {
   const int N = in + 1;
+  const long slices = ceil_div(K, kWgRows);
+  if (out + in <= kWgMaxCols && slices * out * (long)N <= ws_elems && slices <= 65535) {
+    // small layer: one 64-row slice per block staged through shared memory (all of a slice's outputs
+    // from one copy of its rows), instead of 64 x 64 tiles that such a layer mostly leaves empty
+    wgrad_small_kernel<<<(unsigned)slices, 256, 0, st>>>(out, in, K, dZ, ldz, Hin, ldh, ws);
+    splitk_reduce_wb_kernel<<<(unsigned)ceil_div((long)out * N * 32, 256), 256, 0, st>>>(ws, (int)slices, out, in, dW,
+                                                                                       db);
+    count_launch(2);
+    PL_LAUNCH("wgrad_small_kernel");
+    return PL_OK;
+  }
   const long tiles = ceil_div(N, 64) * ceil_div(out, 64), mn = (long)out * N;
   long S = std::min<long>(ceil_div(K, 64), ceil_div(8 * 148, tiles));
   S = std::min<long>(S, ws_elems / mn);
