@@ -151,30 +151,34 @@ __device__ __forceinline__ float tanh_fast(float x) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+// Activation over a register row with the (warp-uniform) activation code tested once per row,
+// so the per-element code is branch-free: v = act(z), or v = acc * act'(z) for the gradient.
+// Both in fused multiply-adds with the constants folded (the epilogues are instruction-bound):
+//   u = z (k + k c z^2), k = sqrt(2 / pi), c = 0.044715, t = tanh u;
+//   GELU(z) = z (1/2 + t/2);  GELU'(z) = (1/2 + t/2) + (1 - t^2) z (k/2 + 3 k c z^2 / 2).
+__device__ __forceinline__ float gelu_fast(float z) {
+  constexpr float k = 0.7978845608028654f, kc = 0.7978845608028654f * 0.044715f;
+  const float z2 = z * z;
+  const float t = tanh_fast(z * __fmaf_rn(kc, z2, k));
+  return z * __fmaf_rn(0.5f, t, 0.5f);
+}
+__device__ __forceinline__ float gelu_grad_fast(float z) {
+  constexpr float k = 0.7978845608028654f, kc = 0.7978845608028654f * 0.044715f;
+  constexpr float h = 0.5f * 0.7978845608028654f, h3 = 1.5f * 0.7978845608028654f * 0.044715f;
+  const float z2 = z * z;
+  const float t = tanh_fast(z * __fmaf_rn(kc, z2, k));
+  return __fmaf_rn(__fmaf_rn(-t, t, 1.f), z * __fmaf_rn(h3, z2, h), __fmaf_rn(0.5f, t, 0.5f));
+}
 __device__ __forceinline__ float act_fwd_fast(float z, int act) {
   if (act == 0) return z > 0.f ? z : 0.f;
   if (act == 2) return z;
-  const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
-  return 0.5f * z * (1.f + tanh_fast(u));
+  return gelu_fast(z);
 }
 __device__ __forceinline__ float act_grad_fast(float z, int act) {
   if (act == 0) return z > 0.f ? 1.f : 0.f;
   if (act == 2) return 1.f;
-  const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
-  const float t = tanh_fast(u);
-  return 0.5f * (1.f + t) + 0.5f * z * (1.f - t * t) * 0.7978845608028654f * (1.f + 3.f * 0.044715f * z * z);
-}
-
-// Activation over a register row with the (warp-uniform) activation code tested once per row,
-// so the per-element code is branch-free: v = act(z), or v = acc * act'(z) for the gradient.
-__device__ __forceinline__ float gelu_fast(float z) {
-  const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
-  return 0.5f * z * (1.f + tanh_fast(u));
-}
-__device__ __forceinline__ float gelu_grad_fast(float z) {
-  const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
-  const float t = tanh_fast(u);
-  return 0.5f * (1.f + t) + 0.5f * z * (1.f - t * t) * 0.7978845608028654f * (1.f + 3.f * 0.044715f * z * z);
+  return gelu_grad_fast(z);
 }
 template <int N>
 __device__ __forceinline__ void act_fwd_row(const float (&z)[N], float (&v)[N], int act) {

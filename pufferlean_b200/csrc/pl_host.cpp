@@ -78,7 +78,7 @@ static const uint64_t kGolden = 0x9E3779B97F4A7C15ULL;
 
 int pl_shuffle_perm(size_t NT, size_t epochs, uint64_t rng, double* out) {
   if (!out && NT * epochs) return PL_ERR_INVALID;
-  if (NT >= ((size_t)1 << 18) && NT < ((size_t)1 << 32)) {
+  if (NT * epochs >= ((size_t)1 << 16) && NT < ((size_t)1 << 32)) {
     uint32_t* k = (uint32_t*)malloc(sizeof(uint32_t) * NT * epochs);
     uint32_t* a = (uint32_t*)malloc(sizeof(uint32_t) * NT * epochs);
     if (!k || !a) {
@@ -170,7 +170,7 @@ int pl_gae_soa(const double* vals, const double* rews, const double* terms, size
   const size_t NT = N * T;
   double* adv = out;
   double* ret = out + NT;
-  if (NT >= ((size_t)1 << 18) && N >= 64) {
+  if (NT >= ((size_t)1 << 15) && N >= 64) {
     pl::host_parallel([&](int t, int Tn) {
       gae_envs(vals, rews, terms, N * t / Tn, N * (t + 1) / Tn, T, gamma, lam, adv, ret);
     });

@@ -562,18 +562,28 @@ constexpr int kWgRows = 64, kWgMaxCols = 192;
 __global__ void __launch_bounds__(256) wgrad_small_kernel(int out, int in, int K, const float* __restrict__ dZ,
                                                           long ldz, const float* __restrict__ Hin, long ldh,
                                                           float* part) {
-  __shared__ float sm[kWgRows * kWgMaxCols];
+  __shared__ __align__(16) float sm[kWgRows * kWgMaxCols];
   float* sZ = sm;                   // [rows][out]
-  float* sH = sm + kWgRows * out;   // [rows][in]
+  float* sH = sm + kWgRows * out;   // [rows][in] (16-byte aligned when out is a multiple of 4)
   const int r0 = blockIdx.x * kWgRows, nr = min(kWgRows, K - r0);
-  for (int i = threadIdx.x; i < nr * out; i += blockDim.x) {
-    const int r = i / out, o = i - r * out;
-    sZ[i] = dZ[(long)(r0 + r) * ldz + o];
-  }
-  for (int i = threadIdx.x; i < nr * in; i += blockDim.x) {
-    const int r = i / in, c = i - r * in;
-    sH[i] = Hin[(long)(r0 + r) * ldh + c];
-  }
+  // dense rows (ld = width) make the slice one contiguous block: 16-byte loads, several in flight
+  auto stage = [&](const float* __restrict__ src, long ld, int w, float* dst) {
+    const float* base = src + (long)r0 * ld;
+    const int n = nr * w;
+    if (ld == w && (n & 3) == 0 && ((uintptr_t)base & 15) == 0 && ((uintptr_t)dst & 15) == 0) {
+      const float4* s4 = reinterpret_cast<const float4*>(base);
+      float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll 4
+      for (int i = threadIdx.x; i < n / 4; i += blockDim.x) d4[i] = s4[i];
+    } else {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int r = i / w, c = i - r * w;
+        dst[i] = base[(long)r * ld + c];
+      }
+    }
+  };
+  stage(dZ, ldz, out, sZ);
+  stage(Hin, ldh, in, sH);
   __syncthreads();
   const int n = in + 1, total = out * n;
   float* dst = part + (long)blockIdx.x * total;
