@@ -58,7 +58,23 @@ struct EpiArgs {
   int tma_out;       // bf16 outputs leave through shared memory and TMA bulk stores (host-checked)
   float diag;        // EPI_F32 / EPI_BF16: added on the diagonal (row == column) of every matrix
   const float* alpha_b;  // EPI_F32 / EPI_BF16, optional: per-matrix factor on alpha (indexed by batch)
+  // EPI_BF16 with aux, optional (the Newton-Schulz polynomial of step 0 on an unnormalised input): aux is
+  // G = X X^T of the raw X; the epilogue takes s = 1 / (sqrt(trace G) + fold_eps) from G's bf16 diagonal
+  // (a fixed-order fold in f64), scales alpha by s^4 and beta by s^2, and writes (float) s to
+  // fold_scale[batch] for the next product. Every warp computes the same s.
+  float* fold_scale;
+  double fold_eps;
 };
+
+// s = 1 / (sqrt(sum_i diag_i) + eps) over the m bf16 diagonal entries of a matrix (leading dimension
+// ld): lane l folds i = l, l + 32, ... in f64, then a fixed butterfly; the same bits in every warp.
+__device__ __forceinline__ double ns_trace_inv(const __nv_bfloat16* g, long ld, int m, double eps, int lane) {
+  double t = 0.0;
+  for (int i = lane; i < m; i += 32) t += (double)__bfloat162float(__ldcg(g + (long)i * ld + i));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return 1.0 / (sqrt(t) + eps);
+}
 
 // Activation codes: 0 ReLU, 1 GELU (tanh form), 2 identity (a linear layer with bias).
 __device__ __forceinline__ float act_fwd(float z, int act) {
@@ -311,7 +327,16 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
   constexpr int BM = 128;
   const int row = m_tile * BM + sub * 32 + lane;
   const bool row_ok = row < ep.out_rows;
-  const float alpha = ep.alpha_b ? ep.alpha * ep.alpha_b[batch] : ep.alpha;
+  float alpha = ep.alpha_b ? ep.alpha * __ldcg(ep.alpha_b + batch) : ep.alpha;
+  float beta = ep.beta;
+  if constexpr (EPI == EPI_BF16) {
+    if (ep.fold_scale && ep.aux) {
+      const double inv = ns_trace_inv(ep.aux + (long)batch * ep.aux_bstride, ep.ld_aux, ep.out_rows, ep.fold_eps, lane);
+      alpha = ep.alpha * (float)(inv * inv * inv * inv);
+      beta = ep.beta * (float)(inv * inv);
+      if (lane == 0) ep.fold_scale[batch] = (float)inv;
+    }
+  }
   if constexpr (EPI == EPI_PPO) {
     // one thread = one minibatch row; BN covers every logit + the value column. The second group of
     // epilogue warps has no columns of its own here and only joins the barriers.
@@ -617,7 +642,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
         } else if (use_aux) {
 #pragma unroll
           for (int j = 0; j < 32; j++)
-            v[j] = axpb(alpha, __uint_as_float(rr[j >> 4][j & 15]), ep.beta, __bfloat162float(auxh[j]));
+            v[j] = axpb(alpha, __uint_as_float(rr[j >> 4][j & 15]), beta, __bfloat162float(auxh[j]));
         } else {
 #pragma unroll
           for (int j = 0; j < 32; j++) v[j] = __fmul_rn(alpha, __uint_as_float(rr[j >> 4][j & 15]));
@@ -693,7 +718,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
           }
 #pragma unroll
           for (int j = 0; j < 16; j++) {
-            const float t = ep.aux ? axpb(alpha, v[j], ep.beta, x[j]) : __fmul_rn(alpha, v[j]);
+            const float t = ep.aux ? axpb(alpha, v[j], beta, x[j]) : __fmul_rn(alpha, v[j]);
             v[j] = row == n0 + j ? __fadd_rn(t, ep.diag) : t;
           }
           const long off = (long)bz * ep.out_bstride + (long)row * ep.ldo + n0;

@@ -47,7 +47,8 @@ struct NsChainGroupHost {
   float* out_f32;
   long ld_out, obs;
   __nv_bfloat16* final_bf16;
-  const float* scale0;
+  float* scale0;
+  double fold_eps;  // >= 0: scale0 is written by the first step (see ns_run_batched)
   unsigned* cnt;
 };
 // Up to 4 groups in one persistent cooperative launch (sets *used; nothing is launched when a group
@@ -59,17 +60,21 @@ int ns_chain_launch(int ngroups, const NsChainGroupHost* groups, const double* c
 // *result (the final bf16 buffer, or the iterate buffer that holds it; NULL for fp32 output).
 int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
                  long xbs, __nv_bfloat16* const xbuf[2], float* out_f32, long ld_out, long obs,
-                 __nv_bfloat16* final_bf16, const float* scale0, cudaStream_t st, __nv_bfloat16** result, bool* used);
+                 __nv_bfloat16* final_bf16, float* scale0, cudaStream_t st, __nv_bfloat16** result, bool* used,
+                 double fold_eps = -1.0);
 // final_bf16 (optional): the last step's bf16 output goes there (not an iterate buffer) instead of
 // back into X; result_at (optional): receives the iterate buffer that holds the bf16 result, and X
 // is then left as it is. Iterate 0 is X; iterate s >= 1 lives in w.X0 / w.X1 (X itself when X is one
 // of them). scale0 (optional, m > 128): X is not yet normalised, and scale0[b] (with scale0[b]^2 at
 // scale0[batch + b]) is the per-matrix factor the first step's G and X' epilogues apply; final_bf16
-// may then be X itself (X is read by the first step only; iters >= 2).
+// may then be X itself (X is read by the first step only; iters >= 2). With fold_eps >= 0 scale0 is
+// an output instead: the first step's G is X X^T of the raw X, and its polynomial's epilogue takes
+// s = 1 / (sqrt(trace G) + fold_eps) from G's diagonal, applies s^2 and s^4 there and writes s to
+// scale0[b] for the first X' (no separate normalisation pass over X).
 int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
                    long xbs, float* out_f32, long ld_out, long obs, cudaStream_t st,
                    __nv_bfloat16* final_bf16 = nullptr, __nv_bfloat16** result_at = nullptr,
-                   const float* scale0 = nullptr);
+                   float* scale0 = nullptr, double fold_eps = -1.0);
 // Per-matrix 1 / (||X||_F + eps) and its square into scale[0, batch) and scale[batch, 2 batch): the
 // sum-of-squares pass of launch_ns_prepare without the scaled copy.
 int launch_ns_scale_factors(const __nv_bfloat16* X, long batch, int rows, int cols, double eps, double* part,

@@ -79,8 +79,9 @@ __host__ __device__ constexpr uint32_t ns_small_smem(int n) {
 __global__ void __launch_bounds__(128, 1)
     ns_small_kernel(const __nv_bfloat16* __restrict__ X, long ldx, long xbs, int m, int n, NsSmallCoef coef,
                     int iters, __nv_bfloat16* out_bf16, long ldo, long obs, float* out_f32, long ldf, long obsf,
-                    unsigned* err) {
+                    unsigned* err, double norm_eps) {
   extern __shared__ uint8_t smem_raw[];
+  __shared__ double wsum[4];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int natoms = (n + 63) / 64, npad = 64 * natoms;  // 64-column atoms of X
   uint8_t* Xs = smem;                        // natoms x 16 KB: X, then each X'
@@ -115,6 +116,33 @@ __global__ void __launch_bounds__(128, 1)
           for (int e = 0; e < 8; e++) h[e] = (ch * 8 + e < n) ? xr[ch * 8 + e] : __float2bfloat16_rn(0.f);
         }
       }
+      *reinterpret_cast<uint4*>(Xs + ns_sw_off(r, ch)) = w;
+    }
+  }
+  if (norm_eps >= 0.0) {
+    // an unnormalised input: X / (||X||_F + eps), the norm from the staged bf16 values in f64 (each row
+    // in column order, the rows by a fixed butterfly and the four warps in order), then each row rescaled
+    // in place as bf16(x * (float) inv)
+    double sq = 0.0;
+    for (int ch = 0; ch < 8 * natoms; ch++) {
+      const uint4 w = *reinterpret_cast<const uint4*>(Xs + ns_sw_off(r, ch));
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&w);
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const double v = (double)__bfloat162float(h[e]);
+        sq += v * v;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if ((t & 31) == 0) wsum[warp] = sq;
+    __syncthreads();
+    const float inv = (float)(1.0 / (sqrt(((wsum[0] + wsum[1]) + wsum[2]) + wsum[3]) + norm_eps));
+    for (int ch = 0; ch < 8 * natoms; ch++) {
+      uint4 w = *reinterpret_cast<const uint4*>(Xs + ns_sw_off(r, ch));
+      __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&w);
+#pragma unroll
+      for (int e = 0; e < 8; e++) h[e] = __float2bfloat16_rn(__bfloat162float(h[e]) * inv);
       *reinterpret_cast<uint4*>(Xs + ns_sw_off(r, ch)) = w;
     }
   }
@@ -227,13 +255,17 @@ int ns_set_small_mode(int mode) {
 
 int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
                    long xbs, float* out_f32, long ld_out, long obs, cudaStream_t st, __nv_bfloat16* final_bf16,
-                   __nv_bfloat16** result_at, const float* scale0) {
-  PL_REQUIRE(!final_bf16 || (final_bf16 != w.X0 && final_bf16 != w.X1 && (final_bf16 != X || (scale0 && iters >= 2))),
+                   __nv_bfloat16** result_at, float* scale0, double fold_eps) {
+  const bool small = g_ns_small && m <= 128 && n <= kNsSmallMaxN && iters <= kNsSmallMaxIters && batch <= 65535;
+  PL_REQUIRE(!final_bf16 || (final_bf16 != w.X0 && final_bf16 != w.X1 &&
+                             (final_bf16 != X || (scale0 && iters >= 2) || small)),
              PL_ERR_INVALID, "Newton-Schulz: the final output may not alias the iterates");
+  PL_REQUIRE(scale0 || fold_eps < 0.0 || small, PL_ERR_INVALID,
+             "Newton-Schulz: in-kernel normalisation needs the fused short-matrix kernel");
   PL_REQUIRE(m <= n, PL_ERR_INVALID, "Newton-Schulz expects the wide layout (m=%d > n=%d)", m, n);
   PL_REQUIRE(!scale0 || (m > 128 && iters >= 2), PL_ERR_INVALID,
              "Newton-Schulz: an unnormalised input needs m > 128 and at least two steps");
-  if (g_ns_small && m <= 128 && n <= kNsSmallMaxN && iters <= kNsSmallMaxIters && batch <= 65535) {
+  if (small) {
     NsSmallCoef cf{};
     for (int i = 0; i < 3 * iters; i++) cf.c[i] = (float)coeffs[i];
     const long xbs_eff = batch > 1 ? xbs : (long)ldx * m;
@@ -248,7 +280,7 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
     }
     ns_small_kernel<<<(unsigned)batch, 128, ns_small_smem(n), st>>>(
         X, ldx, xbs_eff, m, n, cf, iters, out_f32 ? nullptr : dst, ldx, xbs_eff, out_f32, ld_out,
-        batch > 1 ? obs : (long)ld_out * m, w.err ? w.err : device_error_word());
+        batch > 1 ? obs : (long)ld_out * m, w.err ? w.err : device_error_word(), scale0 ? -1.0 : fold_eps);
     count_launch();
     PL_LAUNCH("ns_small_kernel");
     if (result_at) *result_at = out_f32 ? nullptr : dst;
@@ -270,7 +302,7 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
     bool used = false;
     __nv_bfloat16* res = nullptr;
     const int rc = ns_chain_try(m, n, batch, coeffs, iters, w, X, ldx, xbs_eff, xbuf, out_f32, ld_out,
-                                batch > 1 ? obs : (long)ld_out * m, final_bf16, scale0, st, &res, &used);
+                                batch > 1 ? obs : (long)ld_out * m, final_bf16, scale0, st, &res, &used, fold_eps);
     if (rc) return rc;
     if (used) {
       if (out_f32 || final_bf16) return PL_OK;
@@ -301,7 +333,8 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
     e.out_rows = m;
     e.out_cols = m;
     e.alpha = 1.f;
-    e.alpha_b = (first && scale0) ? scale0 + batch : nullptr;
+    const bool fold = first && scale0 && fold_eps >= 0.0;
+    e.alpha_b = (first && scale0 && !fold) ? scale0 + batch : nullptr;
     int rc = gemm_launch(pick_bn(m), EPI_BF16, false, false, opX, opX, m, m, n, batch, e, st);
     if (rc) return rc;
     // Pm = a I + b G + c G G
@@ -309,6 +342,10 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
     e.alpha = c;
     e.alpha_b = nullptr;
     e.beta = b;
+    if (fold) {  // s from trace G: applied here as s^2 and s^4, written to scale0 for X'
+      e.fold_scale = scale0;
+      e.fold_eps = fold_eps;
+    }
     e.diag = a;
     e.aux = w.G;
     e.ld_aux = w.ldg;
@@ -555,13 +592,17 @@ extern "C" int pl_ns_batched_bf16_dev(void* Xv, size_t batch, size_t rows, size_
   __nv_bfloat16* res = nullptr;
   int rc;
   if (!tall && m > 128 && iters >= 2) {
-    // the normalisation folds into the first step: its G and X' epilogues scale by 1/||X|| squared and
-    // once, and the iterates start from the caller's X without a scaled copy
+    // the normalisation folds into the first step: G = X X^T of the raw X, whose trace is ||X||_F^2;
+    // the polynomial's epilogue scales by 1/(||X|| + eps) to the fourth and squared and the first X'
+    // once, so the iterates start from the caller's X without a pass over it
     float* scale = (float*)scratch(16, sizeof(float) * 2 * batch);
     if (!scale) return PL_ERR_NOMEM;
-    rc = launch_ns_scale_factors(X, (long)batch, (int)rows, (int)cols, eps, part, scale, st);
-    if (rc) return rc;
-    return ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, X, n, per, nullptr, 0, 0, st, X, &res, scale);
+    return ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, X, n, per, nullptr, 0, 0, st, X, &res, scale, eps);
+  }
+  if (!tall && m <= 128 && n <= 512 && ns_set_small_mode(-1)) {
+    // the fused kernel normalises the rows it stages and writes the result in place: no prepare pass
+    return ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, X, n, per, nullptr, 0, 0, st, X, &res, nullptr,
+                          eps);
   }
   rc = launch_ns_prepare(X, (long)batch, (int)rows, (int)cols, eps, part, w.X0, st);
   if (rc) return rc;

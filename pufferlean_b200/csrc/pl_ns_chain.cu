@@ -66,7 +66,8 @@ struct NsChainGroup {
   int nG, nX, TG, TX, kbG, kbM;  // tile columns of G / X', tiles per matrix, k-blocks of G / the rest
   int TS;  // G / Pm tiles computed per matrix (the upper band: (mt, nt) with mt < 2 nt + 2)
   int final_kind;  // 0: the last iterate into buffer iters & 1; 1: into the final bf16 output; 2: fp32
-  const float* scale0;  // optional per-matrix factor of an unnormalised input: [batch] s, [batch] s^2
+  float* scale0;  // optional per-matrix factor of an unnormalised input: [batch] s, [batch] s^2
+  double fold_eps;  // >= 0: s comes from trace G of step 0 (written by its Pm epilogue), not from scale0
   const __nv_bfloat16* G;  // aux of the Pm epilogue
   long ldg, gbs;
   float* out_f32;
@@ -337,12 +338,16 @@ __global__ void __launch_bounds__(320, 1)
       const CUtensorMap* tmC;
       if (jb.p == 0) {
         e.out_cols = m;
-        if (jb.s == 0 && gp.scale0) e.alpha_b = gp.scale0 + B;
+        if (jb.s == 0 && gp.scale0 && gp.fold_eps < 0.0) e.alpha_b = gp.scale0 + B;
         tmC = &maps.gs;
       } else if (jb.p == 1) {
         e.out_cols = m;
         e.alpha = a.coef[3 * jb.s + 2];
         e.beta = a.coef[3 * jb.s + 1];
+        if (jb.s == 0 && gp.scale0 && gp.fold_eps >= 0.0) {
+          e.fold_scale = gp.scale0;
+          e.fold_eps = gp.fold_eps;
+        }
         e.diag = a.coef[3 * jb.s];
         e.aux = gp.G;
         e.ld_aux = gp.ldg;
@@ -458,6 +463,7 @@ static int chain_group(const NsChainGroupHost& h, int iters, NsChainMaps& mp, Ns
   g.kbM = (int)ceil_div(m, 64);
   g.final_kind = h.out_f32 ? 2 : (h.final_bf16 ? 1 : 0);
   g.scale0 = h.scale0;
+  g.fold_eps = h.fold_eps;
   g.G = h.G;
   g.ldg = h.ldg;
   g.gbs = gbs;
@@ -524,7 +530,8 @@ int ns_chain_launch(int ngroups, const NsChainGroupHost* hs, const double* coeff
 
 int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
                  long xbs, __nv_bfloat16* const xbuf[2], float* out_f32, long ld_out, long obs,
-                 __nv_bfloat16* final_bf16, const float* scale0, cudaStream_t st, __nv_bfloat16** result, bool* used) {
+                 __nv_bfloat16* final_bf16, float* scale0, cudaStream_t st, __nv_bfloat16** result, bool* used,
+                 double fold_eps) {
   *used = false;
   if (!w.cnt || m <= 128) return PL_OK;
   NsChainGroupHost h{};
@@ -544,6 +551,7 @@ int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWor
   h.obs = obs;
   h.final_bf16 = final_bf16;
   h.scale0 = scale0;
+  h.fold_eps = scale0 ? fold_eps : -1.0;
   h.cnt = w.cnt;
   PL_CUDA(cudaMemsetAsync(w.cnt, 0, sizeof(unsigned) * (size_t)ns_chain_counter_words(batch), st));
   const int rc = ns_chain_launch(1, &h, coeffs, iters, w.cnt + 3L * batch, w.err, st, used);

@@ -73,10 +73,10 @@ int run(pl::NsWork& w, __nv_bfloat16* X, size_t batch, size_t rows, size_t cols,
   __nv_bfloat16* res = nullptr;
   int rc;
   if (!tall && m > 128 && iters >= 2) {  // normalisation folded into the first step, as in the allocating entry
-    rc = launch_ns_scale_factors(X, (long)batch, (int)rows, (int)cols, eps, part, scale, st);
-    if (rc) return rc;
-    return ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, X, n, per, nullptr, 0, 0, st, X, &res, scale);
+    return ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, X, n, per, nullptr, 0, 0, st, X, &res, scale, eps);
   }
+  if (!tall && m <= 128 && n <= 512 && ns_set_small_mode(-1))  // normalised by the fused kernel, as above
+    return ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, X, n, per, nullptr, 0, 0, st, X, &res, nullptr, eps);
   rc = launch_ns_prepare(X, (long)batch, (int)rows, (int)cols, eps, part, w.X0, st);
   if (rc) return rc;
   rc = ns_run_batched(m, n, (int)batch, coeffs, (int)iters, w, w.X0, n, per, nullptr, 0, 0, st, tall ? nullptr : X,
