@@ -1154,6 +1154,12 @@ def main():
 
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    early = {}
+    if world == 1 and not args.no_extra:
+        # the configs[1] / configs[2] kernel measurements first, on a GPU not yet held at its power cap by
+        # seconds of the update (their peaks are the burst figures)
+        early["c2_vtrace"] = measure_vtrace_c2()
+        early["c3_newton_schulz"] = measure_ns_c3()
     out, state = run_ours(args, wl, rank, world, local_rank)
     if not args.no_e2e:
         out["e2e"] = run_e2e(args, wl, state, rank, world, local_rank)
@@ -1183,8 +1189,8 @@ def main():
         plb.lib().pl_comm_destroy.argtypes = [C.c_void_p]
         plb.lib().pl_comm_destroy(state["comm"])
     if rank == 0 and not args.no_extra:
-        out["c2_vtrace"] = measure_vtrace_c2()
-        out["c3_newton_schulz"] = measure_ns_c3()
+        out["c2_vtrace"] = early.get("c2_vtrace") or measure_vtrace_c2()
+        out["c3_newton_schulz"] = early.get("c3_newton_schulz") or measure_ns_c3()
         if world == 1:
             out["c4_mingru"] = measure_mingru_c4(args, cpu=not args.no_cpu)
             if args.workload != "c1":
