@@ -68,6 +68,10 @@ int pl_test_dp_overlap(int mode);
  * each runs as one launch (the default), 0 = one launch sequence per matrix and bias; a negative mode
  * only queries. Returns the previous mode. */
 int pl_test_exact_group(int mode);
+/* LSTM recurrences: 1 = four threads per unit where a sequence's 4H threads fit a CTA and Wh fits
+ * shared memory (the default), 0 = one thread per unit; a negative mode only queries. Returns the
+ * previous mode. */
+int pl_test_lstm_quad(int mode);
 /* Replaces NCCL and the stream query used by pl_comm_* with host-side fakes, for failure tests without a
  * GPU: 1 = creation never completes (a peer that never joins), 2 = a peer fails once the communicator
  * is up (asynchronous-error queries report it), 3 = enqueued work never completes, 4 = a healthy

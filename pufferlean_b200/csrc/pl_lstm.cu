@@ -144,11 +144,31 @@ __global__ void lstm_fwd_kernel(const R* __restrict__ Gin, const R* __restrict__
   R c = ok ? c0[(long)b * H + j] : R(0);
   if (r < rows) sh[r * H + j] = ok ? h0[(long)b * H + j] : R(0);
   const R bi = bih[j], bf = bih[H + j], bg = bih[2 * H + j], bo = bih[3 * H + j];
+  // this step's input projections and the previous step's terminal flag are loaded one step ahead, so
+  // their latency hides under the step before
+  R gi = R(0), gf = R(0), gg = R(0), go = R(0);
+  double tprev = 0.0;
+  if (ok) {
+    const R* g = Gin + (long)b * H4;
+    gi = g[j];
+    gf = g[H + j];
+    gg = g[2 * H + j];
+    go = g[3 * H + j];
+  }
   __syncthreads();
   for (int t = 0; t < T; t++) {
-    if (t > 0 && ok && term[(long)(t - 1) * B + b] != 0.0) {
+    if (t > 0 && ok && tprev != 0.0) {
       sh[r * H + j] = R(0);
       c = R(0);
+    }
+    const R ci = gi, cf = gf, cg = gg, co = go;
+    if (ok && t + 1 < T) {
+      const R* g = Gin + ((long)(t + 1) * B + b) * H4;
+      gi = g[j];
+      gf = g[H + j];
+      gg = g[2 * H + j];
+      go = g[3 * H + j];
+      tprev = term[(long)t * B + b];
     }
     __syncthreads();
     R a0 = R(0), a1 = R(0), a2 = R(0), a3 = R(0), hold = R(0);
@@ -158,6 +178,7 @@ __global__ void lstm_fwd_kernel(const R* __restrict__ Gin, const R* __restrict__
       const R* w1 = Wm + (long)(H + j) * ws;
       const R* w2 = Wm + (long)(2 * H + j) * ws;
       const R* w3 = Wm + (long)(3 * H + j) * ws;
+#pragma unroll 8
       for (int k = 0; k < H; k++) {
         const R hv = lop<RB>(hr[k]);
         if (WS) {  // staged already rounded
@@ -177,9 +198,8 @@ __global__ void lstm_fwd_kernel(const R* __restrict__ Gin, const R* __restrict__
     __syncthreads();  // every read of the step's h is done before it is overwritten
     if (ok) {
       const long row = (long)t * B + b;
-      const R* g = Gin + row * H4;
-      const R iv = lsig((bi + g[j]) + a0), fv = lsig((bf + g[H + j]) + a1);
-      const R gv = ltanh((bg + g[2 * H + j]) + a2), ov = lsig((bo + g[3 * H + j]) + a3);
+      const R iv = lsig((bi + ci) + a0), fv = lsig((bf + cf) + a1);
+      const R gv = ltanh((bg + cg) + a2), ov = lsig((bo + co) + a3);
       const R cn = fv * c + iv * gv, tcv = ltanh(cn), hv = ov * tcv;
       const long o = row * H + j;
       II[o] = iv;
@@ -217,15 +237,41 @@ __global__ void lstm_bwd_kernel(const R* __restrict__ II, const R* __restrict__ 
   const R* Wm = WS ? sWh : Wh;
   const int ws = WS ? SW : H;
   R dhn = R(0), dcn = R(0);
+  // the step's saved activations (and the next step's terminal flag) are loaded one step ahead
+  R nho = R(0), ntc = R(0), nov = R(0), niv = R(0), nfv = R(0), ngv = R(0), ncp = R(0);
+  double nterm = 0.0;
+  if (ok) {
+    const long o = ((long)(T - 1) * B + b) * H + j;
+    nho = dHo[o];
+    ntc = TC[o];
+    nov = OO[o];
+    niv = II[o];
+    nfv = FF[o];
+    ngv = GG[o];
+    ncp = CP[o];
+    if (T > 1) nterm = term[(long)(T - 2) * B + b];
+  }
   __syncthreads();
   for (int t = T - 1; t >= 0; t--) {
     R dcp = R(0);
+    const R cho = nho, tcv = ntc, ov = nov, iv = niv, fv = nfv, gv = ngv, cpv = ncp;
+    const double cterm = nterm;
+    if (ok && t > 0) {
+      const long o = ((long)(t - 1) * B + b) * H + j;
+      nho = dHo[o];
+      ntc = TC[o];
+      nov = OO[o];
+      niv = II[o];
+      nfv = FF[o];
+      ngv = GG[o];
+      ncp = CP[o];
+      if (t > 1) nterm = term[(long)(t - 2) * B + b];
+    }
     if (ok) {
-      const long row = (long)t * B + b, o = row * H + j;
-      const R dh = dHo[o] + dhn;
-      const R tcv = TC[o], ov = OO[o], iv = II[o], fv = FF[o], gv = GG[o];
+      const long row = (long)t * B + b;
+      const R dh = cho + dhn;
       const R dc = dcn + dh * ov * (R(1) - tcv * tcv);
-      const R dO = dh * tcv, dF = dc * CP[o], dI = dc * gv, dGg = dc * iv;
+      const R dO = dh * tcv, dF = dc * cpv, dI = dc * gv, dGg = dc * iv;
       dcp = dc * fv;
       const R q0 = dI * iv * (R(1) - iv), q1 = dF * fv * (R(1) - fv), q2 = dGg * (R(1) - gv * gv),
               q3 = dO * ov * (R(1) - ov);
@@ -244,15 +290,180 @@ __global__ void lstm_bwd_kernel(const R* __restrict__ II, const R* __restrict__ 
     R dhp = R(0);
     if (ok) {
       const R* s = sdg + r * H4;
-      if (WS)
+      if (WS) {
+#pragma unroll 8
         for (int k = 0; k < H4; k++) dhp += s[k] * Wm[(long)k * ws + j];
-      else
+      } else {
+#pragma unroll 8
         for (int k = 0; k < H4; k++) dhp += s[k] * lop<RB>(Wm[(long)k * ws + j]);
-      const bool flow = t > 0 && term[(long)(t - 1) * B + b] == 0.0;
+      }
+      const bool flow = t > 0 && cterm == 0.0;
       dhn = flow ? dhp : R(0);
       dcn = flow ? dcp : R(0);
     }
     __syncthreads();  // the step's dG row is read before the next step overwrites it
+  }
+}
+
+// Four threads per unit (H a multiple of 8, 4H <= 1024 threads per sequence, Wh staged): lane
+// (j % 8) + 8 q of warp j / 8 owns gate q of unit j, so each dot product of a step is one thread's and
+// a step's latency is a quarter of the one-thread-per-unit form's. Wh's gate blocks sit 8 elements
+// apart in shared memory (gate q's rows from q (H (H + 1) + 8)), so the four gates' lanes of a warp read
+// distinct banks.
+__device__ __forceinline__ long lstm_q_off(int q, int H) { return (long)q * ((long)H * (H + 1) + 8); }
+
+// Forward, four threads per unit: each lane forms its gate's pre-activation (bias + input projection)
+// + h_prev . Wh row in the same order as lstm_fwd_kernel, the unit's four values meet by shuffles, and
+// every lane of the unit carries the cell; gate q's lane writes two of the eight saved rows.
+template <typename R, bool RB>
+__global__ void lstm_fwd4_kernel(const R* __restrict__ Gin, const R* __restrict__ Wh, const R* __restrict__ bih,
+                                 const double* __restrict__ term, const R* __restrict__ h0,
+                                 const R* __restrict__ c0, R* II, R* FF, R* GG, R* OO, R* TC, R* HT, R* HP, R* CP,
+                                 int B, int T, int H, int rows) {
+  extern __shared__ __align__(16) unsigned char lstm_smem[];
+  const int H4 = 4 * H, SW = H + 1;
+  R* sWh = (R*)lstm_smem;
+  R* sh = sWh + lstm_q_off(4, H);  // [rows][H]
+  const int tid = threadIdx.x, r = tid / H4, l = tid - r * H4;
+  const int lane = l & 31, q = lane >> 3, j = 8 * (l >> 5) + (lane & 7);
+  const int b = blockIdx.x * rows + r;
+  const bool ok = r < rows && b < B;
+  for (int i = tid; i < H4 * H; i += blockDim.x) {
+    const int m = i / H, k = i - m * H;
+    sWh[lstm_q_off(m / H, H) + (long)(m % H) * SW + k] = lop<RB>(Wh[i]);
+  }
+  R c = ok ? c0[(long)b * H + j] : R(0);
+  if (r < rows && q == 0) sh[r * H + j] = ok ? h0[(long)b * H + j] : R(0);
+  const R bq = bih[q * H + j];
+  const R* wrow = sWh + lstm_q_off(q, H) + (long)j * SW;
+  R gq = ok ? Gin[(long)b * H4 + q * H + j] : R(0);
+  double tprev = 0.0;
+  __syncthreads();
+  for (int t = 0; t < T; t++) {
+    if (t > 0 && ok && tprev != 0.0) {
+      if (q == 0) sh[r * H + j] = R(0);
+      c = R(0);
+    }
+    const R cg = gq;
+    if (ok && t + 1 < T) {
+      gq = Gin[((long)(t + 1) * B + b) * H4 + q * H + j];
+      tprev = term[(long)t * B + b];
+    }
+    __syncthreads();
+    R a = R(0), hold = R(0);
+    if (r < rows) {
+      const R* hr = sh + r * H;
+#pragma unroll 8
+      for (int k = 0; k < H; k++) a += wrow[k] * lop<RB>(hr[k]);
+      hold = hr[j];
+    }
+    __syncthreads();  // every read of the step's h is done before it is overwritten
+    const R z = (bq + cg) + a;
+    const int base = lane & 7;
+    const R z0 = __shfl_sync(0xffffffffu, z, base), z1 = __shfl_sync(0xffffffffu, z, base + 8);
+    const R z2 = __shfl_sync(0xffffffffu, z, base + 16), z3 = __shfl_sync(0xffffffffu, z, base + 24);
+    if (ok) {
+      const long o = ((long)t * B + b) * H + j;
+      const R iv = lsig(z0), fv = lsig(z1), gv = ltanh(z2), ov = lsig(z3);
+      const R cn = fv * c + iv * gv, tcv = ltanh(cn), hv = ov * tcv;
+      if (q == 0) {
+        II[o] = iv;
+        TC[o] = tcv;
+        sh[r * H + j] = hv;
+      } else if (q == 1) {
+        FF[o] = fv;
+        HT[o] = hv;
+      } else if (q == 2) {
+        GG[o] = gv;
+        HP[o] = hold;
+      } else {
+        OO[o] = ov;
+        CP[o] = c;
+      }
+      c = cn;
+    }
+  }
+}
+
+// Reverse, four threads per unit: every lane of the unit carries dh and dc and forms the unit's four gate
+// derivatives, gate q's lane stores its own; dh_prev[j] is the sum over the four gate blocks of
+// Wh[k][j] s[k], one block per lane, added by a fixed butterfly (a different summation order from
+// lstm_bwd_kernel's single pass).
+template <typename R, bool RB>
+__global__ void lstm_bwd4_kernel(const R* __restrict__ II, const R* __restrict__ FF, const R* __restrict__ GG,
+                                 const R* __restrict__ OO, const R* __restrict__ TC, const R* __restrict__ CP,
+                                 const R* __restrict__ dHo, const R* __restrict__ Wh,
+                                 const double* __restrict__ term, R* dG, int B, int T, int H, int rows) {
+  extern __shared__ __align__(16) unsigned char lstm_smem[];
+  const int H4 = 4 * H, SW = H + 1, SQ = H + 8;
+  R* sWh = (R*)lstm_smem;
+  R* sdg = sWh + lstm_q_off(4, H);  // [rows][4 (H + 8)]: gate q's block at q (H + 8)
+  const int tid = threadIdx.x, r = tid / H4, l = tid - r * H4;
+  const int lane = l & 31, q = lane >> 3, j = 8 * (l >> 5) + (lane & 7);
+  const int b = blockIdx.x * rows + r;
+  const bool ok = r < rows && b < B;
+  for (int i = tid; i < H4 * H; i += blockDim.x) {
+    const int m = i / H, k = i - m * H;
+    sWh[lstm_q_off(m / H, H) + (long)(m % H) * SW + k] = lop<RB>(Wh[i]);
+  }
+  R dhn = R(0), dcn = R(0);
+  R nho = R(0), ntc = R(0), nov = R(0), niv = R(0), nfv = R(0), ngv = R(0), ncp = R(0);
+  double nterm = 0.0;
+  if (ok) {
+    const long o = ((long)(T - 1) * B + b) * H + j;
+    nho = dHo[o];
+    ntc = TC[o];
+    nov = OO[o];
+    niv = II[o];
+    nfv = FF[o];
+    ngv = GG[o];
+    ncp = CP[o];
+    if (T > 1) nterm = term[(long)(T - 2) * B + b];
+  }
+  const R* wcol = sWh + lstm_q_off(q, H) + j;  // column j of gate block q, rows k = 0..H-1 at stride SW
+  __syncthreads();
+  for (int t = T - 1; t >= 0; t--) {
+    R dcp = R(0);
+    const R cho = nho, tcv = ntc, ov = nov, iv = niv, fv = nfv, gv = ngv, cpv = ncp;
+    const double cterm = nterm;
+    if (ok && t > 0) {
+      const long o = ((long)(t - 1) * B + b) * H + j;
+      nho = dHo[o];
+      ntc = TC[o];
+      nov = OO[o];
+      niv = II[o];
+      nfv = FF[o];
+      ngv = GG[o];
+      ncp = CP[o];
+      if (t > 1) nterm = term[(long)(t - 2) * B + b];
+    }
+    if (ok) {
+      const long row = (long)t * B + b;
+      const R dh = cho + dhn;
+      const R dc = dcn + dh * ov * (R(1) - tcv * tcv);
+      const R dO = dh * tcv, dF = dc * cpv, dI = dc * gv, dGg = dc * iv;
+      dcp = dc * fv;
+      const R qv = q == 0 ? dI * iv * (R(1) - iv)
+                          : (q == 1 ? dF * fv * (R(1) - fv) : (q == 2 ? dGg * (R(1) - gv * gv) : dO * ov * (R(1) - ov)));
+      dG[row * H4 + q * H + j] = qv;
+      sdg[(long)r * 4 * SQ + q * SQ + j] = lop<RB>(qv);
+    }
+    __syncthreads();
+    R p = R(0);
+    if (r < rows) {
+      const R* sq = sdg + (long)r * 4 * SQ + q * SQ;
+#pragma unroll 8
+      for (int k = 0; k < H; k++) p += sq[k] * wcol[(long)k * SW];
+    }
+    // the four gate blocks' partials of unit j (lanes base, base + 8, base + 16, base + 24), fixed order
+    p += __shfl_xor_sync(0xffffffffu, p, 8);
+    p += __shfl_xor_sync(0xffffffffu, p, 16);
+    if (ok) {
+      const bool flow = t > 0 && cterm == 0.0;
+      dhn = flow ? p : R(0);
+      dcn = flow ? dcp : R(0);
+    }
+    __syncthreads();  // the step's block rows are read before the next step overwrites them
   }
 }
 
@@ -315,6 +526,7 @@ int lstm_gemm(int M, int N, int K, const R* A, long ars, long acs, const R* B, l
 }
 
 bool g_reuse_inputs = false;  // lean_cuda_lstm_reuse_inputs: this call's inputs equal the last call's
+bool g_lstm_quad = true;      // four threads per unit in the recurrences where they fit (tests compare)
 
 template <typename R>
 int lstm_grad(const double* params, const double* obs, const double* acts, const double* advs, const double* rets,
@@ -392,17 +604,27 @@ int lstm_grad(const double* params, const double* obs, const double* acts, const
   };
   rc = fwd_products();
   if (rc) return rc;
+  // Four threads per unit when a sequence's 4H threads fit a CTA and Wh fits shared memory (rows
+  // sequences per CTA, one until there are more than ~2 per SM); otherwise one thread per unit.
+  const size_t wsm4 = sizeof(R) * (size_t)(4 * (H * (H + 1) + 8));
+  const int rows4 = (int)std::max<long>(1, std::min<long>(1024 / H4, B / (2 * 148)));
+  const bool Q4 = H % 8 == 0 && H4 <= 1024 && wsm4 + sizeof(R) * (size_t)rows4 * 4 * (H + 8) <= 200 * 1024 &&
+                  g_lstm_quad;
   // sequences per CTA of the recurrence: one until there are more than ~2 per SM (each CTA reads Wh from
   // shared memory once per sequence and step, so fewer sequences per CTA means more SMs share that work)
-  const int rows = (int)std::max<long>(1, std::min<long>(std::min<long>(1024 / H, 8), B / (2 * 148)));
+  const int rows = Q4 ? rows4 : (int)std::max<long>(1, std::min<long>(std::min<long>(1024 / H, 8), B / (2 * 148)));
   const size_t wsm = sizeof(R) * (size_t)H4 * (H + 1);
   const bool WS = wsm + sizeof(R) * (size_t)rows * H4 <= 200 * 1024;
-  const size_t smem_f = (WS ? wsm : 0) + sizeof(R) * (size_t)rows * H;
-  const size_t smem_b = (WS ? wsm : 0) + sizeof(R) * (size_t)rows * H4;
-  auto kf = WS ? (tc ? lstm_fwd_kernel<R, true, true> : lstm_fwd_kernel<R, true, false>)
-                : (tc ? lstm_fwd_kernel<R, false, true> : lstm_fwd_kernel<R, false, false>);
-  auto kb = WS ? (tc ? lstm_bwd_kernel<R, true, true> : lstm_bwd_kernel<R, true, false>)
-                : (tc ? lstm_bwd_kernel<R, false, true> : lstm_bwd_kernel<R, false, false>);
+  const size_t smem_f = Q4 ? wsm4 + sizeof(R) * (size_t)rows * H : (WS ? wsm : 0) + sizeof(R) * (size_t)rows * H;
+  const size_t smem_b =
+      Q4 ? wsm4 + sizeof(R) * (size_t)rows * 4 * (H + 8) : (WS ? wsm : 0) + sizeof(R) * (size_t)rows * H4;
+  auto kf = Q4 ? (tc ? lstm_fwd4_kernel<R, true> : lstm_fwd4_kernel<R, false>)
+               : (WS ? (tc ? lstm_fwd_kernel<R, true, true> : lstm_fwd_kernel<R, true, false>)
+                     : (tc ? lstm_fwd_kernel<R, false, true> : lstm_fwd_kernel<R, false, false>));
+  auto kb = Q4 ? (tc ? lstm_bwd4_kernel<R, true> : lstm_bwd4_kernel<R, false>)
+               : (WS ? (tc ? lstm_bwd_kernel<R, true, true> : lstm_bwd_kernel<R, true, false>)
+                     : (tc ? lstm_bwd_kernel<R, false, true> : lstm_bwd_kernel<R, false, false>));
+  const int threads = rows * (int)(Q4 ? H4 : H);
   static std::mutex mu;
   {
     std::lock_guard<std::mutex> lk(mu);
@@ -410,8 +632,8 @@ int lstm_grad(const double* params, const double* obs, const double* acts, const
     PL_CUDA(cudaFuncSetAttribute((const void*)kb, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b));
   }
   const unsigned nb = (unsigned)ceil_div(B, rows);
-  kf<<<nb, rows * (int)H, smem_f, st>>>(Gin, Wh, bih, term, hc0, hc0 + B * H, II, FF, GG, OO, TC, HT, HP, CP, (int)B,
-                                        (int)T, (int)H, rows);
+  kf<<<nb, threads, smem_f, st>>>(Gin, Wh, bih, term, hc0, hc0 + B * H, II, FF, GG, OO, TC, HT, HP, CP, (int)B, (int)T,
+                                  (int)H, rows);
   count_launch();
   PL_LAUNCH("lstm_fwd_kernel");
   // head: Out = HT Wo^T; row gradient; dHo = dOut Wo
@@ -423,7 +645,7 @@ int lstm_grad(const double* params, const double* obs, const double* acts, const
   PL_LAUNCH("lstm_head_kernel");
   rc = lstm_gemm<R>((int)NR, (int)H, (int)O, dOut, O, 1, Wo, 1, H, dHo, H, 1, st, tc);
   if (rc) return rc;
-  kb<<<nb, rows * (int)H, smem_b, st>>>(II, FF, GG, OO, TC, CP, dHo, Wh, term, dG, (int)B, (int)T, (int)H, rows);
+  kb<<<nb, threads, smem_b, st>>>(II, FF, GG, OO, TC, CP, dHo, Wh, term, dG, (int)B, (int)T, (int)H, rows);
   count_launch();
   PL_LAUNCH("lstm_bwd_kernel");
   // ---- weight gradients over all rows: fixed row slices, summed in slice order
@@ -490,6 +712,12 @@ int pl_lstm_ppo_grad_batch(const double* params, const double* obs, const double
 int pl_lstm_reuse_inputs(int on) {
   pl::g_reuse_inputs = on != 0;
   return PL_OK;
+}
+
+int pl_test_lstm_quad(int mode) {
+  const int prev = pl::g_lstm_quad ? 1 : 0;
+  if (mode >= 0) pl::g_lstm_quad = mode != 0;
+  return prev;
 }
 
 }  // extern "C"

@@ -114,3 +114,23 @@ def test_lstm_lean_symbols():
                                         FA(f["terms"]), FA(f["boot"]), N, Tg, float(f["gae_meta"][2]),
                                         float(f["gae_meta"][3])))
     assert np.array_equal(gae, f["gae"])
+
+
+@pytest.mark.parametrize("B,T,H,D,A", [(13, 16, 32, 7, 5), (300, 10, 64, 4, 2), (5, 7, 8, 3, 2)])
+def test_lstm_four_threads_per_unit_vs_one(B, T, H, D, A):
+    """The recurrences with four threads per unit (each gate's dot product one thread's, the reverse sum
+    over gate blocks added by a butterfly) against one thread per unit: the forward is the same order of
+    operations, the reverse only re-associates the dh sum, so the tiers agree to their own rounding."""
+    k = _inputs(B, T, H, D, A, 7 * B + H)
+    L = plb.lib()
+    L.pl_test_lstm_quad.argtypes = [C.c_int]
+    prev = L.pl_test_lstm_quad(1)
+    try:
+        quad = [plb.cuda_lstm_ppo_grad_batch(*_args(k), B, T, H, D, A, 0.5, 0.01, 0.2, tier=t) for t in (0, 1, 2)]
+        L.pl_test_lstm_quad(0)
+        one = [plb.cuda_lstm_ppo_grad_batch(*_args(k), B, T, H, D, A, 0.5, 0.01, 0.2, tier=t) for t in (0, 1, 2)]
+    finally:
+        L.pl_test_lstm_quad(prev)
+    assert frob(quad[0], one[0]) < 1e-13, frob(quad[0], one[0])
+    assert frob(quad[1], one[1]) < 1e-5, frob(quad[1], one[1])
+    assert frob(quad[2], one[2]) < 1e-4, frob(quad[2], one[2])
