@@ -334,6 +334,9 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
       const double inv = ns_trace_inv(ep.aux + (long)batch * ep.aux_bstride, ep.ld_aux, ep.out_rows, ep.fold_eps, lane);
       alpha = ep.alpha * (float)(inv * inv * inv * inv);
       beta = ep.beta * (float)(inv * inv);
+      // a (near-)zero X with a tiny eps: s^4 beyond float range multiplies a G that is zero; keep Pm = a I
+      if (!isfinite(alpha)) alpha = 0.f;
+      if (!isfinite(beta)) beta = 0.f;
       if (lane == 0) ep.fold_scale[batch] = (float)inv;
     }
   }

@@ -172,3 +172,21 @@ def test_chain_recorded_in_a_graph_equals_eager(batch, rows, cols):
     finally:
         _chain(prev_c)
         L.pl_test_ns_chain_capture(prev_g)
+
+
+@pytest.mark.parametrize("batch,rows,cols", [(2, 512, 1024), (2, 64, 256), (1, 1024, 512)])
+@pytest.mark.parametrize("eps", [1e-7, 1e-12])
+def test_zero_matrices_stay_zero(batch, rows, cols, eps):
+    """A zero input (the normalisation's scale then 1 / eps) orthogonalises to zero, with no NaN: the
+    trace-scaled first step, the fused kernel's in-kernel normalisation and the transposed path."""
+    X = torch.zeros(batch, rows, cols, device="cuda", dtype=torch.bfloat16)
+    X[-1, 0, 0] = 1.0  # one non-zero matrix beside the zero ones
+    co = np.ascontiguousarray(O.QUINTIC_COEFFS)
+    rc = plb.lib().pl_ns_batched_bf16_dev(X.data_ptr(), batch, rows, cols, eps, co.ctypes.data_as(DP), co.shape[0],
+                                          None)
+    assert rc == 0, plb.lib().pl_last_error()
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(X.float()).all())
+    if batch > 1:
+        assert bool((X[:-1] == 0).all())
+    assert float(X[-1].float().abs().max()) > 0.5
