@@ -19,6 +19,8 @@
 // (2 GPUs, 64 x 512 x 2048: one chunk 566 us, two 694 us, against 779 us on one GPU).
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "../../include/pufferlean_b200.h"
 #include "pl_comm.h"
 #include "pl_common.cuh"
@@ -36,11 +38,13 @@ struct ShardStreams {
   bool ready = false;
 };
 ShardStreams g_shard[64];
+std::mutex g_shard_mu;
 
 int shard_streams(ShardStreams** out) {
   int dev = 0;
   PL_CUDA(cudaGetDevice(&dev));
   PL_REQUIRE(dev >= 0 && dev < 64, PL_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_shard_mu);
   ShardStreams& s = g_shard[dev];
   if (!s.ready) {
     PL_CUDA(cudaStreamCreateWithFlags(&s.cs, cudaStreamNonBlocking));
