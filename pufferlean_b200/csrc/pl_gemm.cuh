@@ -241,7 +241,8 @@ struct GemmSmem {
   static constexpr uint32_t STG_ONE = NOUT * 32 * 32 * 2;
   static constexpr uint32_t STG_WARP = STG_BUFS * STG_ONE;
   static constexpr uint32_t STG_BYTES = 8 * STG_WARP;
-  static constexpr uint32_t RED_BYTES = (EPI == EPI_DGRAD || EPI == EPI_PPO) ? (4 * BN * 4 + 4 * 8 * 4) : 0;
+  static constexpr uint32_t RED_BYTES =
+      (EPI == EPI_DGRAD || EPI == EPI_PPO) ? (4 * BN * 4 + 4 * 8 * 4 + (EPI == EPI_PPO ? 128 * 8 * 4 : 0)) : 0;
   static constexpr uint32_t AUX_TILE = AT ? 128u * BN * 2u : 0u;
   static constexpr uint32_t AUX_BYTES = 2 * AUX_TILE;
   static constexpr uint32_t FIXED = 1024 + 256 + STG_BYTES + RED_BYTES + AUX_BYTES;
@@ -341,13 +342,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
     }
   }
   if constexpr (EPI == EPI_PPO) {
-    // one thread = one minibatch row; BN covers every logit + the value column. The second group of
-    // epilogue warps has no columns of its own here and only joins the barriers.
-    if (half) {
-      tc::named_bar_sync(1, 256);
-      tc::named_bar_sync(1, 256);
-      return;
-    }
+    // one minibatch row per TMEM lane; BN covers every logit + the value column
     const int A = ep.A;
     int a = 0;
     float adv = 0.f, ret = 0.f, olp = 0.f, vold = 0.f;
@@ -361,35 +356,55 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
     }
     if constexpr (BN >= 80) {
       if (A + 1 <= 80) {
-        // ---- fast path for heads of up to 79 actions + the value: the row's logits and value in
-        // registers after one wait for five TMEM loads, two passes (max, then exp sum and the
-        // probability-weighted logit sum), the gradient from the registers; padding columns get zeros
-        uint32_t r5[5][16];
+        // ---- heads of up to 79 actions + the value: the two warps of a row group split its 80 columns
+        // (the first group columns [0, 48), the second [48, 80)); each folds its share of the row's
+        // max, exp sum and probability-weighted logit sum, the shares meet through shared memory
+        // (xch: per row the two maxima, the action logit, the value, the two exp sums and the two
+        // weighted sums), and each writes the gradient of its own columns
+        const int q0 = half ? 3 : 0, nq = half ? 2 : 3;
+        const int rl = sub * 32 + lane;
+        float* xr = rowscr + 32 + rl * 8;
+        uint32_t r5[3][16];
 #pragma unroll
-        for (int q = 0; q < 5; q++) tc::tmem_ld16(t_row + 16 * q, r5[q]);
+        for (int q = 0; q < 3; q++)
+          if (q < nq) tc::tmem_ld16(t_row + 16 * (q0 + q), r5[q]);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 5; q++) tc::tmem_tie16(r5[q]);
-        float x[80];
+        for (int q = 0; q < 3; q++) tc::tmem_tie16(r5[q]);
+        float x[48];
 #pragma unroll
-        for (int k = 0; k < 80; k++)
-          x[k] = (have_acc ? __uint_as_float(r5[k >> 4][k & 15]) : 0.f) + (k <= A ? __ldg(ep.bias + k) : 0.f);
-        float mx = -INFINITY, xa = 0.f, vnew = 0.f;
-#pragma unroll
-        for (int k = 0; k < 80; k++) {
-          if (k < A) mx = fmaxf(mx, x[k]);
-          if (k == a) xa = x[k];
-          if (k == A) vnew = x[k];
+        for (int i = 0; i < 48; i++) {
+          const int k = 16 * q0 + i;
+          x[i] = (i < 16 * nq) ? (have_acc ? __uint_as_float(r5[i >> 4][i & 15]) : 0.f) + (k <= A ? __ldg(ep.bias + k) : 0.f)
+                               : 0.f;
         }
-        float se = 0.f, sx = 0.f;
+        float pm = -INFINITY, xa_own = 0.f, v_own = 0.f;
 #pragma unroll
-        for (int k = 0; k < 80; k++) {
-          if (k < A) {
-            const float e = __expf(x[k] - mx);
-            se += e;
-            sx += e * x[k];
+        for (int i = 0; i < 48; i++) {
+          const int k = 16 * q0 + i;
+          if (i < 16 * nq && k < A) pm = fmaxf(pm, x[i]);
+          if (i < 16 * nq && k == a) xa_own = x[i];
+          if (i < 16 * nq && k == A) v_own = x[i];
+        }
+        xr[half] = pm;
+        if (half == (a < 48 ? 0 : 1)) xr[2] = xa_own;  // the action's logit (0 past the 80 columns)
+        if (half == (A < 48 ? 0 : 1)) xr[3] = v_own;   // the value column
+        tc::named_bar_sync(1, 256);
+        const float mx = fmaxf(xr[0], xr[1]), xa = xr[2], vnew = xr[3];
+        float pse = 0.f, psx = 0.f;
+#pragma unroll
+        for (int i = 0; i < 48; i++) {
+          const int k = 16 * q0 + i;
+          if (i < 16 * nq && k < A) {
+            const float e = __expf(x[i] - mx);
+            pse += e;
+            psx += e * x[i];
           }
         }
+        xr[4 + half] = pse;
+        xr[6 + half] = psx;
+        tc::named_bar_sync(1, 256);
+        const float se = xr[4] + xr[5], sx = xr[6] + xr[7];
         const float lse = mx + logf(se), pout = sx / se;
         const float logpA = xa - lse;
         const float ratio = expf(logpA - olp);
@@ -405,11 +420,11 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
           if (!(du >= cc) && !(dd > -ep.vfclip && dd < ep.vfclip)) dv = 0.f;
         }
         const float dval = -ep.vf * dv;
-        if (row_ok) {
+        if (row_ok && !half) {
           if (ep.newlp) ep.newlp[row] = logpA;
           if (ep.newval) ep.newval[row] = vnew;
         }
-        if (ep.loss_part) {
+        if (ep.loss_part && !half) {
           const float ent_row = lse - pout;
           float lt[6] = {row_ok ? -fminf(surr1, surr2) : 0.f, row_ok ? 0.5f * (vnew - ret) * (vnew - ret) : 0.f,
                          row_ok ? ent_row : 0.f, row_ok ? (ratio - 1.f) - logf(ratio) : 0.f,
@@ -425,20 +440,24 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
         __nv_bfloat16* outp = (__nv_bfloat16*)ep.out + (long)row * ep.ldo;
         const bool vec = (ep.ldo % 8) == 0;
 #pragma unroll
-        for (int q = 0; q < 5; q++) {
-          float v[16];
+        for (int q = 0; q < 3; q++) {
+          if (q < nq) {
+            const int cq = 16 * (q0 + q);
+            float v[16];
 #pragma unroll
-          for (int j = 0; j < 16; j++) {
-            const int k = 16 * q + j;
-            const float pk = __expf(x[k] - lse);
-            const float d = k < A ? dPol * ((k == a ? 1.f : 0.f) - pk) + ep.ent * pk * (pout - x[k]) : (k == A ? dval : 0.f);
-            v[j] = row_ok ? d : 0.f;
+            for (int j = 0; j < 16; j++) {
+              const int k = cq + j;
+              const float xk = x[16 * q + j];
+              const float pk = __expf(xk - lse);
+              const float d = k < A ? dPol * ((k == a ? 1.f : 0.f) - pk) + ep.ent * pk * (pout - xk) : (k == A ? dval : 0.f);
+              v[j] = row_ok ? d : 0.f;
+            }
+            if (row_ok && cq < ep.ldo) store_row16_bf16(outp + cq, v, min(16, (int)(ep.ldo - cq)), vec);
+            const float cs = warp_colsum16(v, lane);
+            if ((lane & 1) == 0) red[sub * BN + cq + (lane >> 1)] = cs;
           }
-          if (row_ok && 16 * q < ep.ldo) store_row16_bf16(outp + 16 * q, v, min(16, (int)(ep.ldo - 16 * q)), vec);
-          const float cs = warp_colsum16(v, lane);
-          if ((lane & 1) == 0) red[sub * BN + 16 * q + (lane >> 1)] = cs;
         }
-        if (row_ok) {
+        if (row_ok && !half) {
           float z[16];
 #pragma unroll
           for (int j = 0; j < 16; j++) z[j] = 0.f;
@@ -446,7 +465,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
         }
         tc::named_bar_sync(1, 256);
         const int t = threadIdx.x - 64;
-        for (int c = t; c < BN; c += 128) {
+        for (int c = t; c < BN; c += 256) {
           if (c < ep.out_cols)
             ep.colsum[(long)m_tile * ep.ld_colsum + c] = ((red[c] + red[BN + c]) + red[2 * BN + c]) + red[3 * BN + c];
         }
@@ -455,6 +474,12 @@ __device__ __forceinline__ void epilogue_tile(const EpiArgs& ep, uint32_t t_row,
         tc::named_bar_sync(1, 256);  // scratch is reused by the next tile
         return;
       }
+    }
+    // ---- wider heads: one thread per row; the second group of epilogue warps only joins the barriers
+    if (half) {
+      tc::named_bar_sync(1, 256);
+      tc::named_bar_sync(1, 256);
+      return;
     }
     float mx = -INFINITY, se = 0.f, xa = 0.f, vnew = 0.f;
     for (int c0 = 0; c0 < BN; c0 += 16) {
