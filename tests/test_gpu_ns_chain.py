@@ -60,7 +60,8 @@ def rel(a, b):
 
 
 @pytest.mark.parametrize("batch,rows,cols", [(8, 512, 512), (5, 384, 768), (3, 256, 1024), (4, 1024, 512),
-                                             (2, 200, 328), (16, 512, 2048), (1, 136, 2048)])
+                                             (2, 200, 328), (16, 512, 2048), (1, 136, 2048), (1, 72, 2048),
+                                             (2, 128, 1024), (3, 64, 640), (1, 2048, 72)])
 @pytest.mark.parametrize("steps", [5, 4])
 def test_chain_is_bit_identical_to_per_step_launches(batch, rows, cols, steps):
     torch.manual_seed(rows + 3 * cols + steps)
