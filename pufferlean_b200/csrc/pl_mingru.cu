@@ -1047,6 +1047,8 @@ int ensure_work(pl_mg* s, const MgShape& sh, long Bmb, long T, bool fast) {
   w.gbout = mg_alloc<float>(w.allocs, w.Op, f);
   const long chunks = (R + 255) / 256;
   w.colpart_elems = chunks * std::max<long>(H, w.Op);
+  // the bf16 tier's last layer-gradient product also leaves per-128-row bias partials of the encoder here
+  if (fast) w.colpart_elems = std::max<long>(w.colpart_elems, colsum_scratch_elems((int)((R + 127) / 128), H));
   w.colpart = mg_alloc<float>(w.allocs, w.colpart_elems, f);
   w.splitk_elems = std::max<long>(std::max<long>(8 * KH * H, 64 * (A + 1) * H), 64 * H * std::max<long>(sh.D, 64));
   if (fast) w.splitk = mg_alloc<float>(w.allocs, w.splitk_elems, f);
@@ -1320,6 +1322,7 @@ int bptt(pl_mg* s, double vf, double ent, double clip, double vfclip, bool losse
   }
   if (rc) return rc;
   // ---- layers, top down
+  bool enc_fused = false;
   for (long l = L - 1; l >= 0; l--) {
     rc = launch_scan_bwd<S>(w.Y[l], w.Os[l], w.h[l], w.dh[cur], w.dY, sh.K == 3 ? w.dhn : nullptr, w.term_f, Bmb,
                             (int)H, T, (int)sh.K, st);
@@ -1347,7 +1350,19 @@ int bptt(pl_mg* s, double vf, double ent, double clip, double vfclip, bool losse
         e.ld_aux = H;
         e.beta = 1.f;
       }
-      rc = gemm_launch(256, EPI_BF16, false, true, opA, opB, (int)R, (int)H, (int)KH, 1, e, st);
+      if (l == 0 && sh.K != 3 && sh.enc_act) {
+        // the encoder's data gradient in this product's epilogue: dE = (dY W_0) x GELU'(Z) with the
+        // encoder bias partials per 128-row tile (no separate activation and column-sum passes)
+        e.aux = (const bf16*)w.Z;
+        e.ld_aux = H;
+        e.act = 1;
+        e.colsum = w.colpart;
+        e.ld_colsum = H;
+        enc_fused = true;
+        rc = gemm_launch(256, EPI_DGRAD, false, true, opA, opB, (int)R, (int)H, (int)KH, 1, e, st);
+      } else {
+        rc = gemm_launch(256, EPI_BF16, false, true, opA, opB, (int)R, (int)H, (int)KH, 1, e, st);
+      }
     } else {
       rc = launch_sgemm((int)R, (int)H, (int)KH, (const float*)w.dY, KH, 1, (const float*)w.Wl[l], 1, H,
                         (float*)w.dh[nxt], H, 1.f, st);
@@ -1361,12 +1376,16 @@ int bptt(pl_mg* s, double vf, double ent, double clip, double vfclip, bool losse
     cur = nxt;
   }
   // ---- encoder gradients
-  if (sh.enc_act) {
-    mg_act_grad_kernel<S><<<blocks_for(R * H), 256, 0, st>>>((S*)w.dh[cur], (const S*)w.Z, R * H, 1);
-    count_launch();
-    PL_LAUNCH("mg_act_grad_kernel");
+  if (enc_fused) {
+    rc = launch_colsum_reduce(w.colpart, (int)((R + 127) / 128), H, (int)H, grad + sh.oBenc(), st);
+  } else {
+    if (sh.enc_act) {
+      mg_act_grad_kernel<S><<<blocks_for(R * H), 256, 0, st>>>((S*)w.dh[cur], (const S*)w.Z, R * H, 1);
+      count_launch();
+      PL_LAUNCH("mg_act_grad_kernel");
+    }
+    rc = colsum<S>(s, (const S*)w.dh[cur], R, H, (int)H, grad + sh.oBenc(), st);
   }
-  rc = colsum<S>(s, (const S*)w.dh[cur], R, H, (int)H, grad + sh.oBenc(), st);
   if (rc) return rc;
   if (fast) {
     // dW_enc [H x D] = dE^T X (X padded to Dp; only D columns are written)
