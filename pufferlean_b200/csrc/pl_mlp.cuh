@@ -65,7 +65,8 @@ int ns_chain_try(int m, int n, int batch, const double* coeffs, int iters, NsWor
 // final_bf16 (optional): the last step's bf16 output goes there (not an iterate buffer) instead of
 // back into X; result_at (optional): receives the iterate buffer that holds the bf16 result, and X
 // is then left as it is. Iterate 0 is X; iterate s >= 1 lives in w.X0 / w.X1 (X itself when X is one
-// of them). scale0 (optional, m > 128): X is not yet normalised, and scale0[b] (with scale0[b]^2 at
+// of them). scale0 (optional; not for batches the fused short-matrix kernel takes, see
+// ns_small_eligible): X is not yet normalised, and scale0[b] (with scale0[b]^2 at
 // scale0[batch + b]) is the per-matrix factor the first step's G and X' epilogues apply; final_bf16
 // may then be X itself (X is read by the first step only; iters >= 2). With fold_eps >= 0 scale0 is
 // an output instead: the first step's G is X X^T of the raw X, and its polynomial's epilogue takes
@@ -75,6 +76,9 @@ int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsW
                    long xbs, float* out_f32, long ld_out, long obs, cudaStream_t st,
                    __nv_bfloat16* final_bf16 = nullptr, __nv_bfloat16** result_at = nullptr,
                    float* scale0 = nullptr, double fold_eps = -1.0);
+// True when ns_run_batched takes the fused one-CTA kernel for this batch (which normalises in the kernel
+// when given fold_eps >= 0 and no scale0).
+bool ns_small_eligible(int m, int n, int batch, int iters);
 // Per-matrix 1 / (||X||_F + eps) and its square into scale[0, batch) and scale[batch, 2 batch): the
 // sum-of-squares pass of launch_ns_prepare without the scaled copy.
 int launch_ns_scale_factors(const __nv_bfloat16* X, long batch, int rows, int cols, double eps, double* part,
@@ -123,8 +127,40 @@ int launch_ns_input(const double* u, const double* part, int nparts, int rows, i
                     __nv_bfloat16* X, long ldx, cudaStream_t st);
 int launch_ns_finalize(const float* Xf, long ldx, int rows, int cols, double c1, double c2, double* W,
                        __nv_bfloat16* Wb, long ldw, cudaStream_t st);
-int launch_stepvec_fast(const float* g, const double* cc, double* b, double* m, float* bf, double lr, double wd,
-                        double mu, int n, cudaStream_t st);
+// Muon around Newton-Schulz for one group of equal-shape layers of the bf16 tier, one launch per phase
+// (blockIdx.y = layer of the group). X and Xf are the wide layout (min(rows, cols) x max(rows, cols),
+// ld ldx; transposed when rows > cols).
+constexpr int kMuonGroupMax = 8;
+struct MuonGroupArgs {
+  int nb = 0, rows = 0, cols = 0;  // layers in this launch; each weight is rows x cols (row-major)
+  long ldx = 0;                    // leading dimension of X and Xf
+  long ldw = 0;                    // leading dimension of the bf16 shadow weights
+  const float* gW[kMuonGroupMax];  // weight gradient
+  double* mW[kMuonGroupMax];       // weight momentum (f64)
+  __nv_bfloat16* X[kMuonGroupMax]; // Newton-Schulz input; NULL: this rank does not orthogonalise the layer
+  const float* Xf[kMuonGroupMax];  // Newton-Schulz result (fp32)
+  double* W[kMuonGroupMax];        // f64 master weights
+  __nv_bfloat16* Wb[kMuonGroupMax];  // bf16 shadow weights (NULL: none)
+  const float* gb[kMuonGroupMax];  // bias gradient (rows values)
+  double* b[kMuonGroupMax];        // f64 bias
+  double* mb[kMuonGroupMax];       // bias momentum
+  float* bf[kMuonGroupMax];        // fp32 bias shadow (NULL: none)
+};
+// Blocks per layer of the group launches: a function of the shape and the whole group's size only, so
+// that the partial sums (and the scale folded from them) do not depend on how the group is chunked;
+// nb_total times it is at most max(kMuonBlocksMax, nb_total).
+constexpr int kMuonBlocksMax = 1184;  // 8 x 148 SMs
+int muon_group_blocks(int rows, int cols, int nb_total);
+// Nesterov momentum of each weight (m <- mu m + g cc, u = g cc + mu m, f64 as nesterov_kernel) and
+// X = bf16(u) unscaled; with part non-NULL, per-block sums of u^2 into part[q * blocks + block].
+int launch_muon_x0(const MuonGroupArgs& a, int blocks, const double* cc, double mu, double* part, cudaStream_t st);
+// scale[q] = 1 / (sqrt(sum of layer q's partials) + eps) and scale[nb + q] = its square: the first
+// Newton-Schulz step's factors for an unnormalised input (ns_run_batched's scale0).
+int launch_muon_scale(const double* part, int blocks, int nb, double eps, float* scale, cudaStream_t st);
+// W <- (1 - lr wd) W + lr s Xf with the bf16 shadow, and the bias step (Nesterov on the bias gradient
+// times cc, same operation order as the f64 reference) with its fp32 shadow.
+int launch_muon_finalize(const MuonGroupArgs& a, int blocks, double lr, double wd, double mu, double s,
+                         const double* cc, cudaStream_t st);
 int launch_w_to_bf16(const double* W, int rows, int cols, __nv_bfloat16* Wb, long ldw, cudaStream_t st);
 int launch_f64_to_f32(const double* s, long n, float* d, cudaStream_t st);
 int launch_f32_to_f64(const float* s, long n, double* d, cudaStream_t st);

@@ -422,18 +422,190 @@ __global__ void __launch_bounds__(256) ns_finalize_kernel(const float* __restric
     __syncthreads();
   }
 }
-// stepVec on a bias with the scaled gradient g*cc, plus its fp32 shadow.
-__global__ void stepvec_fast_kernel(const float* __restrict__ g, const double* __restrict__ cc, double* b, double* m,
-                                    float* bf, double lr, double wd, double mu, int n) {
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const double gi = (double)g[i] * cc[0];
-  const double newm = mu * m[i] + gi;
-  const double upd = gi + mu * newm;
-  const double nb = b[i] * (1.0 - lr * wd) + lr * upd;
-  b[i] = nb;
-  m[i] = newm;
-  if (bf) bf[i] = (float)nb;
+// ---------------------------------------------------------------- Muon of a group of equal-shape layers
+// The bf16 tier's Muon around Newton-Schulz in three launches per group (blockIdx.y = layer): the
+// Nesterov step writes the Newton-Schulz input X = bf16(u) directly, unscaled, with per-block sums of
+// u^2; one warp per layer turns them into the first step's factors 1 / (||u|| + eps) and its square
+// (applied in that step's G and X' epilogues); the finalisation applies the result and the bias step.
+// Per weight element that is 4 + 8 + 8 + 2 bytes for the first phase (gradient, momentum in and out, X)
+// where a separate normalisation pass would also write and re-read u in f64.
+
+// The Nesterov arithmetic of one element, in the reference's order (m <- mu m + g cc; u = g cc + mu m).
+__device__ __forceinline__ double nesterov_u(float g, double c, double mu, double& m) {
+  const double gi = (double)g * c;
+  m = mu * m + gi;
+  return gi + mu * m;
+}
+
+template <bool TR>
+__global__ void __launch_bounds__(256) muon_x0_kernel(const MuonGroupArgs a, const double* __restrict__ cc, double mu,
+                                                      double* part) {
+  __shared__ double sh[256];
+  __shared__ float tile[32][33];
+  const int q = blockIdx.y;
+  const float* __restrict__ g = a.gW[q];
+  double* __restrict__ mom = a.mW[q];
+  __nv_bfloat16* X = a.X[q];
+  const double c = cc[0];
+  const int rows = a.rows, cols = a.cols;
+  double s = 0.0;
+  if (!TR) {
+    constexpr int B = 256;
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+      const float* gr = g + (long)r * cols;
+      double* mr = mom + (long)r * cols;
+      __nv_bfloat16* xr = X ? X + (long)r * a.ldx : nullptr;
+      int k = threadIdx.x;
+      for (; k + 3 * B < cols; k += 4 * B) {  // four elements' loads in flight per thread
+        float gv[4];
+        double mv[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          gv[j] = gr[k + j * B];
+          mv[j] = mr[k + j * B];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const double ui = nesterov_u(gv[j], c, mu, mv[j]);
+          mr[k + j * B] = mv[j];
+          s += ui * ui;
+          if (xr) xr[k + j * B] = __float2bfloat16_rn((float)ui);
+        }
+      }
+      for (; k < cols; k += B) {
+        double m = mr[k];
+        const double ui = nesterov_u(gr[k], c, mu, m);
+        mr[k] = m;
+        s += ui * ui;
+        if (xr) xr[k] = __float2bfloat16_rn((float)ui);
+      }
+    }
+  } else {
+    // rows > cols: X is cols x ldx; 32 x 32 tiles through shared memory so that the momentum reads
+    // and the transposed X writes are both coalesced
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int tcols = (cols + 31) >> 5, ntiles = ((rows + 31) >> 5) * tcols;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {  // block-uniform trip count
+      const int r0 = (t / tcols) * 32, c0 = (t % tcols) * 32;
+      const int cc0 = c0 + tx;
+      float gv[4];
+      double mv[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int r = r0 + ty + 8 * j;
+        const bool ok = r < rows && cc0 < cols;
+        gv[j] = ok ? g[(long)r * cols + cc0] : 0.f;
+        mv[j] = ok ? mom[(long)r * cols + cc0] : 0.0;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int r = r0 + ty + 8 * j;
+        float v = 0.f;
+        if (r < rows && cc0 < cols) {
+          const double ui = nesterov_u(gv[j], c, mu, mv[j]);
+          mom[(long)r * cols + cc0] = mv[j];
+          s += ui * ui;
+          v = (float)ui;
+        }
+        tile[ty + 8 * j][tx] = v;
+      }
+      __syncthreads();
+      if (X)
+        for (int j = ty; j < 32; j += 8) {
+          const int cx = c0 + j, r = r0 + tx;
+          if (r < rows && cx < cols) X[(long)cx * a.ldx + r] = __float2bfloat16_rn(tile[tx][j]);
+        }
+      __syncthreads();
+    }
+  }
+  if (part) {
+    s = block_sum_f64(s, sh);
+    if (threadIdx.x == 0) part[(long)q * gridDim.x + blockIdx.x] = s;
+  }
+}
+
+// One warp per layer: the layer's partials folded in block order.
+__global__ void muon_scale_kernel(const double* __restrict__ part, int blocks, int nb, double eps, float* scale) {
+  const int q = blockIdx.x;
+  const double s = warp_fold_f64(part + (long)q * blocks, blocks, 1);
+  if (threadIdx.x == 0) {
+    const double inv = 1.0 / (sqrt(s) + eps);
+    scale[q] = (float)inv;
+    scale[nb + q] = (float)(inv * inv);
+  }
+}
+
+template <bool TR>
+__global__ void __launch_bounds__(256) muon_finalize_kernel(const MuonGroupArgs a, double c1, double c2,
+                                                            const double* __restrict__ cc, double lr, double wd,
+                                                            double mu) {
+  __shared__ float tile[32][33];
+  const int q = blockIdx.y;
+  const float* __restrict__ Xf = a.Xf[q];
+  double* __restrict__ W = a.W[q];
+  __nv_bfloat16* Wb = a.Wb[q];
+  const int rows = a.rows, cols = a.cols;
+  if (blockIdx.x == 0 && a.b[q]) {  // the bias: stepVec on g cc, as the f64 reference orders it
+    const double c = cc[0];
+    for (int i = threadIdx.x; i < rows; i += blockDim.x) {
+      double m = a.mb[q][i];
+      const double upd = nesterov_u(a.gb[q][i], c, mu, m);
+      const double nbv = a.b[q][i] * (1.0 - lr * wd) + lr * upd;
+      a.b[q][i] = nbv;
+      a.mb[q][i] = m;
+      if (a.bf[q]) a.bf[q][i] = (float)nbv;
+    }
+  }
+  if (!TR) {
+    constexpr int B = 256;
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+      const float* xr = Xf + (long)r * a.ldx;
+      double* wr = W + (long)r * cols;
+      __nv_bfloat16* br = Wb ? Wb + (long)r * a.ldw : nullptr;
+      int k = threadIdx.x;
+      for (; k + 3 * B < cols; k += 4 * B) {
+        float xv[4];
+        double wv[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          xv[j] = xr[k + j * B];
+          wv[j] = wr[k + j * B];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const double w = c1 * wv[j] + c2 * (double)xv[j];
+          wr[k + j * B] = w;
+          if (br) br[k + j * B] = __float2bfloat16_rn((float)w);
+        }
+      }
+      for (; k < cols; k += B) {
+        const double w = c1 * wr[k] + c2 * (double)xr[k];
+        wr[k] = w;
+        if (br) br[k] = __float2bfloat16_rn((float)w);
+      }
+    }
+    return;
+  }
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int tcols = (cols + 31) >> 5, ntiles = ((rows + 31) >> 5) * tcols;
+  for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {  // block-uniform trip count
+    const int r0 = (t / tcols) * 32, c0 = (t % tcols) * 32;
+    for (int j = ty; j < 32; j += 8) {
+      const int cx = c0 + j, r = r0 + tx;
+      if (r < rows && cx < cols) tile[j][tx] = Xf[(long)cx * a.ldx + r];
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += 8) {
+      const int r = r0 + j, cx = c0 + tx;
+      if (r < rows && cx < cols) {
+        const long i = (long)r * cols + cx;
+        const double w = c1 * W[i] + c2 * (double)tile[tx][j];
+        W[i] = w;
+        if (Wb) Wb[(long)r * a.ldw + cx] = __float2bfloat16_rn((float)w);
+      }
+    }
+    __syncthreads();
+  }
 }
 // f64 master weights -> bf16 shadow (padded, ld) / fp32 copies
 __global__ void w_to_bf16_kernel(const double* __restrict__ W, int rows, int cols, __nv_bfloat16* Wb, long ldw) {
@@ -1015,11 +1187,39 @@ int launch_ns_finalize(const float* Xf, long ldx, int rows, int cols, double c1,
   PL_LAUNCH("ns_finalize_kernel");
   return PL_OK;
 }
-int launch_stepvec_fast(const float* g, const double* cc, double* b, double* m, float* bf, double lr, double wd,
-                        double mu, int n, cudaStream_t st) {
-  stepvec_fast_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(g, cc, b, m, bf, lr, wd, mu, n);
+int muon_group_blocks(int rows, int cols, int nb_total) {
+  const long units = rows > cols ? (long)ceil_div(rows, 32) * ceil_div(cols, 32) : (long)rows;
+  const long per = std::max(1L, (long)kMuonBlocksMax / std::max(1, nb_total));
+  return (int)std::max(1L, std::min(units, per));
+}
+int launch_muon_x0(const MuonGroupArgs& a, int blocks, const double* cc, double mu, double* part, cudaStream_t st) {
+  PL_REQUIRE(a.nb >= 1 && a.nb <= kMuonGroupMax && blocks >= 1, PL_ERR_INVALID, "launch_muon_x0: group of %d", a.nb);
+  const dim3 grid((unsigned)blocks, (unsigned)a.nb);
+  if (a.rows > a.cols)
+    muon_x0_kernel<true><<<grid, 256, 0, st>>>(a, cc, mu, part);
+  else
+    muon_x0_kernel<false><<<grid, 256, 0, st>>>(a, cc, mu, part);
   count_launch();
-  PL_LAUNCH("stepvec_fast_kernel");
+  PL_LAUNCH("muon_x0_kernel");
+  return PL_OK;
+}
+int launch_muon_scale(const double* part, int blocks, int nb, double eps, float* scale, cudaStream_t st) {
+  muon_scale_kernel<<<(unsigned)nb, 32, 0, st>>>(part, blocks, nb, eps, scale);
+  count_launch();
+  PL_LAUNCH("muon_scale_kernel");
+  return PL_OK;
+}
+int launch_muon_finalize(const MuonGroupArgs& a, int blocks, double lr, double wd, double mu, double s,
+                         const double* cc, cudaStream_t st) {
+  PL_REQUIRE(a.nb >= 1 && a.nb <= kMuonGroupMax && blocks >= 1, PL_ERR_INVALID, "launch_muon_finalize: group of %d",
+             a.nb);
+  const dim3 grid((unsigned)blocks, (unsigned)a.nb);
+  if (a.rows > a.cols)
+    muon_finalize_kernel<true><<<grid, 256, 0, st>>>(a, 1.0 - lr * wd, lr * s, cc, lr, wd, mu);
+  else
+    muon_finalize_kernel<false><<<grid, 256, 0, st>>>(a, 1.0 - lr * wd, lr * s, cc, lr, wd, mu);
+  count_launch();
+  PL_LAUNCH("muon_finalize_kernel");
   return PL_OK;
 }
 int launch_w_to_bf16(const double* W, int rows, int cols, __nv_bfloat16* Wb, long ldw, cudaStream_t st) {

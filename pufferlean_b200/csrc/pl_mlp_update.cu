@@ -99,6 +99,7 @@ struct pl_update {
   std::vector<std::vector<int>> ns_groups;  // layers of equal shape, orthogonalised as one batch
   std::vector<ExactLayer> exact_group;      // tight tier: every layer when each fits one CTA's step
   long ns_batch = 1;                        // largest group
+  float* ns_scale = nullptr;                // first-step Newton-Schulz factors of a group: [group] s, [group] s^2
   std::vector<float*> xres;    // per-layer orthogonalised update (m x n wide layout, fp32)
   // profiling: CUDA events around each launch group, per class
   bool prof = false;
@@ -321,12 +322,11 @@ static int alloc_session(pl_update* u) {
     u->bf.push_back(dalloc<float>(u, ly.out_p));
   }
   // Muon workspace
-  long mmax = 0, nmax = 0, nprod = 0;
+  long mmax = 0, nmax = 0;
   for (auto& ly : u->layers) {
     long m = std::min(ly.out, ly.in), n = std::max(ly.out, ly.in);
     mmax = std::max(mmax, m);
     nmax = std::max(nmax, n);
-    nprod = std::max(nprod, (long)ly.out * ly.in);
   }
   const long ldx = round_up(nmax, 64), ldg = round_up(mmax, 64);
   // equal-shaped layers (the hidden 2048 x 2048 matrices of configs[4]) share one batched
@@ -357,8 +357,10 @@ static int alloc_session(pl_update* u) {
     u->ns.G = dalloc<__nv_bfloat16>(u, (size_t)(slotg * u->ns_batch));
     u->ns.B = dalloc<__nv_bfloat16>(u, (size_t)(slotg * u->ns_batch));
     u->ns.Xf = dalloc<float>(u, (size_t)(mmax * ldx * u->ns_batch));
-    u->ns.U = dalloc<double>(u, nprod);
-    u->ns.part = dalloc<double>(u, 4096);
+    // per-block sums of u^2 of one group: at most kMuonBlocksMax in all (muon_group_blocks), or one
+    // block per layer of a larger group
+    u->ns.part = dalloc<double>(u, std::max<size_t>(4096, kMuonBlocksMax + u->layers.size()));
+    u->ns_scale = dalloc<float>(u, 2 * u->layers.size());
     u->ns.cnt = dalloc<unsigned>(u, (size_t)ns_chain_counter_words(u->ns_batch));
     for (void* p : {(void*)u->ns.X0, (void*)u->ns.X1, (void*)u->ns.G, (void*)u->ns.B})
       if (p) cudaMemset(p, 0, 1);  // touch
@@ -454,28 +456,68 @@ static int wgrad_fast(pl_update* u, const void* dZ, long ldz, int out, const voi
   return launch_splitk_reduce(u->splitk, S, (long)out * in, dst, st);
 }
 
+// Launch arguments of layers grp[q0, q0 + kMuonGroupMax) for the Muon group kernels: xin(q) is layer
+// grp[q]'s Newton-Schulz input (NULL where this rank does not orthogonalise it), xres(q) its result,
+// both in the wide layout with leading dimension ldx.
+template <class FX, class FR>
+static MuonGroupArgs muon_args(const pl_update* u, const std::vector<int>& grp, int q0, long ldx, FX xin, FR xres) {
+  MuonGroupArgs a{};
+  const Layer& f = u->layers[grp[0]];
+  a.nb = std::min<int>(kMuonGroupMax, (int)grp.size() - q0);
+  a.rows = f.out;
+  a.cols = f.in;
+  a.ldx = ldx;
+  a.ldw = f.in_p;
+  for (int j = 0; j < a.nb; j++) {
+    const int l = grp[q0 + j];
+    const Layer& ly = u->layers[l];
+    a.gW[j] = u->grad + ly.oW;
+    a.mW[j] = u->pm + u->P + ly.oW;
+    a.X[j] = xin(q0 + j);
+    a.Xf[j] = xres(q0 + j);
+    a.W[j] = u->pm + ly.oW;
+    a.Wb[j] = u->Wb[l];
+    a.gb[j] = u->grad + ly.ob;
+    a.b[j] = u->pm + ly.ob;
+    a.mb[j] = u->pm + u->P + ly.ob;
+    a.bf[j] = u->bf[l];
+  }
+  return a;
+}
+
+// The Muon update's factor for a rows x cols weight: sqrt(max(1, rows / cols)).
+static double muon_shape_scale(const Layer& ly) {
+  const double r = (double)ly.out / (double)ly.in;
+  return sqrt(r > 1.0 ? r : 1.0);
+}
+
 // Data-parallel Muon: every rank advances the momentum of every layer; each layer's Newton-Schulz
-// runs on its owner rank only (pl_muon_shard_plan); one grouped broadcast hands every rank every
-// orthogonalised update; every rank then applies the identical f64 step, so the weights stay
-// bit-identical across ranks.
+// runs on its owner rank only (pl_muon_shard_plan), which also writes its unscaled input and the
+// factor; one grouped broadcast hands every rank every orthogonalised update; every rank then applies
+// the identical f64 step, so the weights stay bit-identical across ranks.
 static int muon_sharded(pl_update* u, double lr, cudaStream_t st) {
   const pl_update_desc& d = u->d;
   int rc = PL_OK;
   for (size_t l = 0; l < u->layers.size(); l++) {
     const Layer& ly = u->layers[l];
-    const long n = (long)ly.out * ly.in;
     const int m = std::min(ly.out, ly.in), nn = std::max(ly.out, ly.in);
-    int nparts = 0;
+    const bool own = u->owner[l] == d.rank;
+    const bool small = ns_small_eligible(m, nn, 1, u->iters);
+    const int blocks = muon_group_blocks(ly.out, ly.in, 1);
+    const std::vector<int> one{(int)l};
     {
       Span sp(u, 6, st, 0);
-      rc = launch_nesterov(u->grad + ly.oW, u->cc, u->pm + u->P + ly.oW, u->ns.U, d.mu, n, u->ns.part, &nparts, st);
-      if (!rc && u->owner[l] == d.rank)
-        rc = launch_ns_input(u->ns.U, u->ns.part, nparts, ly.out, ly.in, d.eps, u->ns.X0, u->ns.ldx, st);
+      rc = launch_muon_x0(
+          muon_args(u, one, 0, u->ns.ldx, [&](int) { return own ? u->ns.X0 : (__nv_bfloat16*)nullptr; },
+                    [&](int) { return (const float*)u->xres[l]; }),
+          blocks, u->cc, d.mu, own && !small ? u->ns.part : nullptr, st);
+      if (!rc && own && !small) rc = launch_muon_scale(u->ns.part, blocks, 1, d.eps, u->ns_scale, st);
     }
     if (rc) return rc;
-    if (u->owner[l] != d.rank) continue;
+    if (!own) continue;
     Span sp(u, 4, st, (double)u->iters * (4.0 * m * (double)m * nn + 2.0 * m * (double)m * m));
-    rc = ns_run(m, nn, u->coeffs.data(), u->iters, u->ns, u->ns.X0, u->ns.ldx, u->xres[l], nn, st);
+    rc = ns_run_batched(m, nn, 1, u->coeffs.data(), u->iters, u->ns, u->ns.X0, u->ns.ldx, 0, u->xres[l], nn, 0, st,
+                        nullptr, nullptr, small ? nullptr : u->ns_scale, small ? d.eps : -1.0);
     if (rc) return rc;
   }
   {
@@ -491,16 +533,15 @@ static int muon_sharded(pl_update* u, double lr, cudaStream_t st) {
     rc = comm_broadcast_group(d.comm, bufs, counts, roots, st);
     if (rc) return rc;
   }
-  for (size_t l = 0; l < u->layers.size(); l++) {
-    const Layer& ly = u->layers[l];
-    const double r = (double)ly.out / (double)ly.in;
-    const double scale = sqrt(r > 1.0 ? r : 1.0);
+  for (const auto& grp : u->ns_groups) {
+    const Layer& g0 = u->layers[grp[0]];
+    const int nn = std::max(g0.out, g0.in);
+    const int blocks = muon_group_blocks(g0.out, g0.in, (int)grp.size());
     Span sp(u, 6, st, 0);
-    rc = launch_ns_finalize(u->xres[l], std::max(ly.out, ly.in), ly.out, ly.in, 1.0 - lr * d.wd, lr * scale,
-                            u->pm + ly.oW, u->Wb[l], ly.in_p, st);
-    if (!rc)
-      rc = launch_stepvec_fast(u->grad + ly.ob, u->cc, u->pm + ly.ob, u->pm + u->P + ly.ob, u->bf[l], lr, d.wd, d.mu,
-                               ly.out, st);
+    for (int q0 = 0; q0 < (int)grp.size() && !rc; q0 += kMuonGroupMax)
+      rc = launch_muon_finalize(muon_args(u, grp, q0, nn, [](int) { return (__nv_bfloat16*)nullptr; },
+                                          [&](int q) { return (const float*)u->xres[grp[q]]; }),
+                                blocks, lr, d.wd, d.mu, muon_shape_scale(g0), u->cc, st);
     if (rc) return rc;
   }
   return PL_OK;
@@ -761,41 +802,41 @@ static int minibatch_fast(pl_update* u, const int* idx, const int* oidx, const v
   }
   if (rc) return rc;
   if (u->dp) return muon_sharded(u, lr, st);
+  // Muon per group of equal-shape layers: the Nesterov step writes the unscaled Newton-Schulz input
+  // (and the sums of u^2 whose factor the first step applies, or the fused short-matrix kernel
+  // normalises in place), one batched Newton-Schulz, one finalisation of weights and biases
   for (const auto& grp : u->ns_groups) {
     const Layer& g0 = u->layers[grp[0]];
     const int m = std::min(g0.out, g0.in), nn = std::max(g0.out, g0.in);
     const int nb = (int)grp.size();
     const long xstride = (long)m * u->ns.ldx;  // one wide m x ldx matrix per batch slot
-    for (int q = 0; q < nb; q++) {
-      const Layer& ly = u->layers[grp[q]];
-      const long n = (long)ly.out * ly.in;
-      int nparts = 0;
+    const bool small = ns_small_eligible(m, nn, nb, u->iters);
+    const int blocks = muon_group_blocks(g0.out, g0.in, nb);
+    auto xin = [&](int q) { return u->ns.X0 + q * xstride; };
+    auto xres = [&](int q) { return (const float*)(u->ns.Xf + q * xstride); };
+    {
       Span sp(u, 6, st, 0);
-      rc = launch_nesterov(u->grad + ly.oW, u->cc, u->pm + u->P + ly.oW, u->ns.U, d.mu, n, u->ns.part, &nparts, st);
-      if (!rc)
-        rc = launch_ns_input(u->ns.U, u->ns.part, nparts, ly.out, ly.in, d.eps, u->ns.X0 + q * xstride, u->ns.ldx, st);
-      if (rc) return rc;
+      for (int q0 = 0; q0 < nb && !rc; q0 += kMuonGroupMax)
+        rc = launch_muon_x0(muon_args(u, grp, q0, u->ns.ldx, xin, xres), blocks, u->cc, d.mu,
+                            small ? nullptr : u->ns.part + (long)q0 * blocks, st);
+      if (!rc && !small) rc = launch_muon_scale(u->ns.part, blocks, nb, d.eps, u->ns_scale, st);
     }
+    if (rc) return rc;
     {
       // algorithmic Newton-Schulz flops per step and matrix: 4 m^2 n + 2 m^3
       Span sp(u, 4, st, (double)nb * u->iters * (4.0 * m * (double)m * nn + 2.0 * m * (double)m * m));
       rc = ns_run_batched(m, nn, nb, u->coeffs.data(), u->iters, u->ns, u->ns.X0, u->ns.ldx, xstride, u->ns.Xf,
-                          u->ns.ldx, xstride, st);
+                          u->ns.ldx, xstride, st, nullptr, nullptr, small ? nullptr : u->ns_scale,
+                          small ? d.eps : -1.0);
     }
     if (rc) return rc;
-    for (int q = 0; q < nb; q++) {
-      const int l = grp[q];
-      const Layer& ly = u->layers[l];
-      const double r = (double)ly.out / (double)ly.in;
-      const double scale = sqrt(r > 1.0 ? r : 1.0);
+    {
       Span sp(u, 6, st, 0);
-      rc = launch_ns_finalize(u->ns.Xf + q * xstride, u->ns.ldx, ly.out, ly.in, 1.0 - lr * d.wd, lr * scale,
-                              u->pm + ly.oW, u->Wb[l], ly.in_p, st);
-      if (!rc)
-        rc = launch_stepvec_fast(u->grad + ly.ob, u->cc, u->pm + ly.ob, u->pm + u->P + ly.ob, u->bf[l], lr, d.wd, d.mu,
-                                 ly.out, st);
-      if (rc) return rc;
+      for (int q0 = 0; q0 < nb && !rc; q0 += kMuonGroupMax)
+        rc = launch_muon_finalize(muon_args(u, grp, q0, u->ns.ldx, xin, xres), blocks, lr, d.wd, d.mu,
+                                  muon_shape_scale(g0), u->cc, st);
     }
+    if (rc) return rc;
   }
   return PL_OK;
 }

@@ -253,18 +253,22 @@ int ns_set_small_mode(int mode) {
   return prev;
 }
 
+bool ns_small_eligible(int m, int n, int batch, int iters) {
+  return g_ns_small && m <= 128 && n <= kNsSmallMaxN && iters <= kNsSmallMaxIters && batch <= 65535;
+}
+
 int ns_run_batched(int m, int n, int batch, const double* coeffs, int iters, NsWork& w, __nv_bfloat16* X, long ldx,
                    long xbs, float* out_f32, long ld_out, long obs, cudaStream_t st, __nv_bfloat16* final_bf16,
                    __nv_bfloat16** result_at, float* scale0, double fold_eps) {
-  const bool small = g_ns_small && m <= 128 && n <= kNsSmallMaxN && iters <= kNsSmallMaxIters && batch <= 65535;
+  const bool small = ns_small_eligible(m, n, batch, iters);
   PL_REQUIRE(!final_bf16 || (final_bf16 != w.X0 && final_bf16 != w.X1 &&
                              (final_bf16 != X || (scale0 && iters >= 2) || small)),
              PL_ERR_INVALID, "Newton-Schulz: the final output may not alias the iterates");
   PL_REQUIRE(scale0 || fold_eps < 0.0 || small, PL_ERR_INVALID,
              "Newton-Schulz: in-kernel normalisation needs the fused short-matrix kernel");
   PL_REQUIRE(m <= n, PL_ERR_INVALID, "Newton-Schulz expects the wide layout (m=%d > n=%d)", m, n);
-  PL_REQUIRE(!scale0 || (m > 128 && iters >= 2), PL_ERR_INVALID,
-             "Newton-Schulz: an unnormalised input needs m > 128 and at least two steps");
+  PL_REQUIRE(!scale0 || (!small && iters >= 2), PL_ERR_INVALID,
+             "Newton-Schulz: an unnormalised input needs the GEMM chain and at least two steps");
   if (small) {
     NsSmallCoef cf{};
     for (int i = 0; i < 3 * iters; i++) cf.c[i] = (float)coeffs[i];
