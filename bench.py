@@ -247,7 +247,6 @@ def run_ours(args, wl, rank, world, local_rank, comm=None):
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    check(L.pl_update_profile(u, 1), L)
     l0 = L.pl_kernel_launch_count()
     # inputs smaller than L2 are timed step by step with a 256 MB write between steps, so
     # every step starts with a cold L2; larger ones (configs[4]: 17 GB of observations) need no flush
@@ -270,6 +269,17 @@ def run_ours(args, wl, rank, world, local_rank, comm=None):
         torch.cuda.synchronize()
     launches = L.pl_kernel_launch_count() - l0
     ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / args.steps
+    # the per-class breakdown (CUDA events around each launch group) comes from untimed steps after the
+    # timed ones, so that no profiling event sits inside the timed region
+    psteps = min(args.steps, 2)
+    if world > 1:
+        torch.distributed.barrier()
+    check(L.pl_update_profile(u, 1), L)
+    for _ in range(psteps):
+        if flush is not None:
+            flush.fill_(1.0)
+        step()
+    torch.cuda.synchronize()
     pms, pfl, pln = (C.c_double * 8)(), (C.c_double * 8)(), (C.c_double * 8)()
     check(L.pl_update_profile_read(u, pms, pfl, pln), L)
     cms, cbytes, cn = C.c_double(), C.c_double(), C.c_double()
@@ -287,8 +297,8 @@ def run_ours(args, wl, rank, world, local_rank, comm=None):
     gemm_n = sum(pln[i] for i in range(4))
     achieved = gemm_fl / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
     ns_tf = pfl[4] / (pms[4] / 1e3) / 1e12 if pms[4] > 0 else 0.0
-    prof = {k: {"ms_per_step": pms[i] / args.steps, "tflops": (pfl[i] / (pms[i] / 1e3) / 1e12) if pms[i] > 0 and
-                pfl[i] > 0 else None, "launches_per_step": pln[i] / args.steps}
+    prof = {k: {"ms_per_step": pms[i] / psteps, "tflops": (pfl[i] / (pms[i] / 1e3) / 1e12) if pms[i] > 0 and
+                pfl[i] > 0 else None, "launches_per_step": pln[i] / psteps}
             for i, k in enumerate(["fwd_gemm", "ppo_head_gemm", "dgrad_gemm", "wgrad_gemm", "newton_schulz",
                                    "gather_stats", "optimizer_elementwise", "dp_collectives"])}
     L.pl_update_destroy(u)
@@ -318,16 +328,17 @@ def run_ours(args, wl, rank, world, local_rank, comm=None):
                      "traffic_source": "ncu dram__bytes_read+write of every GEMM launch of a 65,536-row update, x4 "
                                        "to 262,144 rows (profiles/tc_gemm_dram_c5p.md)",
                      "kernel": "tc_gemm_kernel (all forward/PPO-head/dgrad/wgrad launches of the step)",
-                     "launches_per_step": gemm_n / args.steps, "peak_kind": peak_kind + " (bf16 sustained)"},
+                     "launches_per_step": gemm_n / psteps, "peak_kind": peak_kind + " (bf16 sustained)"},
         "newton_schulz": {"tflops": ns_tf, "frac": ns_tf / peak_tf if peak_tf else None,
-                          "ms_per_step": pms[4] / args.steps},
+                          "ms_per_step": pms[4] / psteps},
         "profile": prof,
+        "profile_how": "CUDA events around each launch group, recorded in %d untimed step(s) after the timed ones" % psteps,
         "gpu_launches": int(launches),
         "dp_allreduce": None if world == 1 else {
-            "ms_per_step_on_comm_stream": cms.value / args.steps,
-            "ms_per_step_exposed": pms[7] / args.steps,
-            "bytes_per_rank_per_step": cbytes.value / args.steps,
-            "launches_per_step": cn.value / args.steps,
+            "ms_per_step_on_comm_stream": cms.value / psteps,
+            "ms_per_step_exposed": pms[7] / psteps,
+            "bytes_per_rank_per_step": cbytes.value / psteps,
+            "launches_per_step": cn.value / psteps,
             "bus_gbs": (cbytes.value * 2 * (world - 1) / world / (cms.value / 1e3) / 1e9) if cms.value > 0 else None,
             "how": "per-layer fp32 ncclAllReduce on a second stream, each started when its layer's gradient is "
                    "complete; bus GB/s = bytes x 2(N-1)/N / time on that stream"},

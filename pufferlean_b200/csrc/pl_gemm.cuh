@@ -91,28 +91,30 @@ __device__ __forceinline__ float act_grad(float z, int act) {
   return 0.5f * (1.f + t) + 0.5f * z * (1.f - t * t) * 0.7978845608028654f * (1.f + 3.f * 0.044715f * z * z);
 }
 
+// One level of warp_colsum16's butterfly: lanes with `hi` set keep the upper half of x and send the
+// lower half to lane ^ off (the others the reverse); the additions go two values at a time (two-lane
+// fp32 adds, each rounded as the scalar add).
+template <int HALF>
+__device__ __forceinline__ void colsum_level(const float (&x)[2 * HALF], int off, bool hi, float (&y)[HALF]) {
+#pragma unroll
+  for (int j = 0; j < HALF; j += 2) {
+    float2 keep, recv;
+    keep.x = hi ? x[j + HALF] : x[j];
+    keep.y = hi ? x[j + 1 + HALF] : x[j + 1];
+    recv.x = __shfl_xor_sync(0xffffffffu, hi ? x[j] : x[j + HALF], off);
+    recv.y = __shfl_xor_sync(0xffffffffu, hi ? x[j + 1] : x[j + 1 + HALF], off);
+    const float2 r = __fadd2_rn(keep, recv);
+    y[j] = r.x;
+    y[j + 1] = r.y;
+  }
+}
 // Sums each of 16 per-lane values over the 32 lanes of a warp with 16 shuffles (a butterfly that
 // halves the live values each step). Lane L returns the total of column (L >> 1). Fixed order.
 __device__ __forceinline__ float warp_colsum16(const float (&v)[16], int lane) {
   float a[8], b[4], c[2];
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    bool hi = lane & 16;
-    float send = hi ? v[j] : v[j + 8], keep = hi ? v[j + 8] : v[j];
-    a[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int j = 0; j < 4; j++) {
-    bool hi = lane & 8;
-    float send = hi ? a[j] : a[j + 4], keep = hi ? a[j + 4] : a[j];
-    b[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-#pragma unroll
-  for (int j = 0; j < 2; j++) {
-    bool hi = lane & 4;
-    float send = hi ? b[j] : b[j + 2], keep = hi ? b[j + 2] : b[j];
-    c[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
+  colsum_level<8>(v, 16, lane & 16, a);
+  colsum_level<4>(a, 8, lane & 8, b);
+  colsum_level<2>(b, 4, lane & 4, c);
   bool hi = lane & 2;
   float send = hi ? c[0] : c[1], keep = hi ? c[1] : c[0];
   float d = keep + __shfl_xor_sync(0xffffffffu, send, 2);
@@ -186,6 +188,26 @@ __device__ __forceinline__ float gelu_grad_fast(float z) {
   const float t = tanh_fast(z * __fmaf_rn(kc, z2, k));
   return __fmaf_rn(__fmaf_rn(-t, t, 1.f), z * __fmaf_rn(h3, z2, h), __fmaf_rn(0.5f, t, 0.5f));
 }
+// The same operations two lanes at a time: sm_100's two-lane fp32 instructions round each lane as the
+// scalar instruction does, so these are bit-identical to gelu_fast / gelu_grad_fast in half the
+// arithmetic instructions (the epilogues that evaluate them are issue-bound).
+__device__ __forceinline__ float2 gelu_fast2(float2 z) {
+  constexpr float k = 0.7978845608028654f, kc = 0.7978845608028654f * 0.044715f;
+  const float2 z2 = __fmul2_rn(z, z);
+  const float2 u = __fmul2_rn(z, __ffma2_rn(make_float2(kc, kc), z2, make_float2(k, k)));
+  const float2 t = make_float2(tanh_fast(u.x), tanh_fast(u.y));
+  return __fmul2_rn(z, __ffma2_rn(make_float2(0.5f, 0.5f), t, make_float2(0.5f, 0.5f)));
+}
+__device__ __forceinline__ float2 gelu_grad_fast2(float2 z) {
+  constexpr float k = 0.7978845608028654f, kc = 0.7978845608028654f * 0.044715f;
+  constexpr float h = 0.5f * 0.7978845608028654f, h3 = 1.5f * 0.7978845608028654f * 0.044715f;
+  const float2 z2 = __fmul2_rn(z, z);
+  const float2 u = __fmul2_rn(z, __ffma2_rn(make_float2(kc, kc), z2, make_float2(k, k)));
+  const float2 t = make_float2(tanh_fast(u.x), tanh_fast(u.y));
+  const float2 s = __ffma2_rn(make_float2(-t.x, -t.y), t, make_float2(1.f, 1.f));
+  const float2 w = __fmul2_rn(z, __ffma2_rn(make_float2(h3, h3), z2, make_float2(h, h)));
+  return __ffma2_rn(s, w, __ffma2_rn(make_float2(0.5f, 0.5f), t, make_float2(0.5f, 0.5f)));
+}
 __device__ __forceinline__ float act_fwd_fast(float z, int act) {
   if (act == 0) return z > 0.f ? z : 0.f;
   if (act == 2) return z;
@@ -198,9 +220,14 @@ __device__ __forceinline__ float act_grad_fast(float z, int act) {
 }
 template <int N>
 __device__ __forceinline__ void act_fwd_row(const float (&z)[N], float (&v)[N], int act) {
+  static_assert(N % 2 == 0, "rows of an even number of values");
   if (act == 1) {
 #pragma unroll
-    for (int j = 0; j < N; j++) v[j] = gelu_fast(z[j]);
+    for (int j = 0; j < N; j += 2) {
+      const float2 g = gelu_fast2(make_float2(z[j], z[j + 1]));
+      v[j] = g.x;
+      v[j + 1] = g.y;
+    }
   } else if (act == 0) {
 #pragma unroll
     for (int j = 0; j < N; j++) v[j] = z[j] > 0.f ? z[j] : 0.f;
@@ -211,9 +238,14 @@ __device__ __forceinline__ void act_fwd_row(const float (&z)[N], float (&v)[N], 
 }
 template <int N>
 __device__ __forceinline__ void act_grad_row(float (&v)[N], const float (&z)[N], int act) {
+  static_assert(N % 2 == 0, "rows of an even number of values");
   if (act == 1) {
 #pragma unroll
-    for (int j = 0; j < N; j++) v[j] *= gelu_grad_fast(z[j]);
+    for (int j = 0; j < N; j += 2) {
+      const float2 g = __fmul2_rn(make_float2(v[j], v[j + 1]), gelu_grad_fast2(make_float2(z[j], z[j + 1])));
+      v[j] = g.x;
+      v[j + 1] = g.y;
+    }
   } else if (act == 0) {
 #pragma unroll
     for (int j = 0; j < N; j++) v[j] = z[j] > 0.f ? v[j] : 0.f;
