@@ -68,6 +68,10 @@ int pl_test_dp_overlap(int mode);
  * each runs as one launch (the default), 0 = one launch sequence per matrix and bias; a negative mode
  * only queries. Returns the previous mode. */
 int pl_test_exact_group(int mode);
+/* bf16-tier update: 1 = the Newton-Schulz chains of all equal-shape layer groups run in one persistent
+ * launch per Muon step (the default), 0 = one launch per group; a negative mode only queries. Returns the
+ * previous mode. */
+int pl_test_ns_group_launch(int mode);
 /* LSTM recurrences: 1 = four threads per unit where a sequence's 4H threads fit a CTA and Wh fits
  * shared memory (the default), 0 = one thread per unit; a negative mode only queries. Returns the
  * previous mode. */

@@ -51,9 +51,10 @@ struct NsChainGroupHost {
   double fold_eps;  // >= 0: scale0 is written by the first step (see ns_run_batched)
   unsigned* cnt;
 };
-// Up to 4 groups in one persistent cooperative launch (sets *used; nothing is launched when a group
-// cannot take the chain, the stream is being captured or the chain is switched off). abort_word: one
-// zeroed word.
+// Up to kNsChainMaxGroups groups in one persistent cooperative launch (sets *used; nothing is launched
+// when a group cannot take the chain, the stream is being captured or the chain is switched off).
+// abort_word: one zeroed word.
+constexpr int kNsChainMaxGroups = 4;
 int ns_chain_launch(int ngroups, const NsChainGroupHost* groups, const double* coeffs, int iters,
                     unsigned* abort_word, unsigned* err, cudaStream_t st, bool* used);
 // Runs the whole chain as one persistent launch when eligible (sets *used); the result then lies in

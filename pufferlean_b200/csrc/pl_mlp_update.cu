@@ -98,7 +98,9 @@ struct pl_update {
   std::vector<int> owner;      // Newton-Schulz owner rank of each layer
   std::vector<std::vector<int>> ns_groups;  // layers of equal shape, orthogonalised as one batch
   std::vector<ExactLayer> exact_group;      // tight tier: every layer when each fits one CTA's step
-  long ns_batch = 1;                        // largest group
+  long ns_batch = 1;                        // workspace slots: every layer's (one at a time under data parallelism)
+  std::vector<long> ns_slot0;               // first slot of each group (its matrices' X, G, Pm and result)
+  long ns_slotx = 0, ns_slotg = 0, ns_slotf = 0;  // elements per slot of X0 / X1, of G / B and of Xf
   float* ns_scale = nullptr;                // first-step Newton-Schulz factors of a group: [group] s, [group] s^2
   std::vector<float*> xres;    // per-layer orthogonalised update (m x n wide layout, fp32)
   // profiling: CUDA events around each launch group, per class
@@ -141,6 +143,7 @@ static bool g_loss_on = false;
 static bool g_host_bf16 = true;
 static bool g_dp_overlap = true;  // sessions created afterwards overlap the gradient all-reduce
 static bool g_exact_group = true;  // tight-tier sessions created afterwards may use the one-launch Muon step
+static bool g_ns_one_launch = true;  // bf16 tier: the groups' Newton-Schulz chains share one launch
 static std::atomic<uint64_t> g_upload_bytes{0};  // host-to-device bytes of the last set_columns call  // bf16 tier: host observations rounded to bf16 on the host threads
 static double g_losses[7] = {0, 0, 0, 0, 0, 0, 0};
 
@@ -344,12 +347,23 @@ static int alloc_session(pl_update* u) {
     }
     if (!placed) u->ns_groups.push_back({(int)l});
   }
+  // each group has slots of its own, so that all groups' Newton-Schulz chains can run in one launch
   u->ns_batch = 1;
-  if (!u->dp)
-    for (auto& g : u->ns_groups) u->ns_batch = std::max<long>(u->ns_batch, (long)g.size());
+  u->ns_slot0.clear();
+  if (!u->dp) {
+    long next = 0;
+    for (auto& g : u->ns_groups) {
+      u->ns_slot0.push_back(next);
+      next += (long)g.size();
+    }
+    u->ns_batch = std::max<long>(1, next);
+  }
   if (fast) {
     // one batch slot holds the largest matrix; a group's batch uses slots of its own (smaller) size
     const long slotx = round_up(mmax, 128) * ldx, slotg = round_up(mmax, 128) * ldg;
+    u->ns_slotx = slotx;
+    u->ns_slotg = slotg;
+    u->ns_slotf = mmax * ldx;
     u->ns.ldx = ldx;
     u->ns.ldg = ldg;
     u->ns.X0 = dalloc<__nv_bfloat16>(u, (size_t)(slotx * u->ns_batch));
@@ -361,6 +375,7 @@ static int alloc_session(pl_update* u) {
     // block per layer of a larger group
     u->ns.part = dalloc<double>(u, std::max<size_t>(4096, kMuonBlocksMax + u->layers.size()));
     u->ns_scale = dalloc<float>(u, 2 * u->layers.size());
+    // per group 3 x batch chain counters at 3 x its first slot; the last word is the shared abort word
     u->ns.cnt = dalloc<unsigned>(u, (size_t)ns_chain_counter_words(u->ns_batch));
     for (void* p : {(void*)u->ns.X0, (void*)u->ns.X1, (void*)u->ns.G, (void*)u->ns.B})
       if (p) cudaMemset(p, 0, 1);  // touch
@@ -390,8 +405,8 @@ static int alloc_session(pl_update* u) {
   }
   if (fast) {
     PL_CUDA(cudaMemset(u->X, 0, sizeof(__nv_bfloat16) * M * u->Dp));
-    PL_CUDA(cudaMemset(u->ns.X0, 0, sizeof(__nv_bfloat16) * round_up(mmax, 128) * ldx));
-    PL_CUDA(cudaMemset(u->ns.X1, 0, sizeof(__nv_bfloat16) * round_up(mmax, 128) * ldx));
+    PL_CUDA(cudaMemset(u->ns.X0, 0, sizeof(__nv_bfloat16) * u->ns_slotx * u->ns_batch));
+    PL_CUDA(cudaMemset(u->ns.X1, 0, sizeof(__nv_bfloat16) * u->ns_slotx * u->ns_batch));
   }
   return PL_OK;
 }
@@ -804,38 +819,104 @@ static int minibatch_fast(pl_update* u, const int* idx, const int* oidx, const v
   if (u->dp) return muon_sharded(u, lr, st);
   // Muon per group of equal-shape layers: the Nesterov step writes the unscaled Newton-Schulz input
   // (and the sums of u^2 whose factor the first step applies, or the fused short-matrix kernel
-  // normalises in place), one batched Newton-Schulz, one finalisation of weights and biases
-  for (const auto& grp : u->ns_groups) {
+  // normalises in place); the groups that take the persistent chain run in one launch, so that the
+  // short dependent products of the small groups overlap the large group's; then one finalisation of
+  // weights and biases per group
+  const size_t ngr = u->ns_groups.size();
+  std::vector<NsWork> ws(ngr, u->ns);
+  std::vector<char> small(ngr);
+  std::vector<int> blocks(ngr);
+  double ns_flops = 0.0;
+  for (size_t gi = 0; gi < ngr; gi++) {
+    const auto& grp = u->ns_groups[gi];
     const Layer& g0 = u->layers[grp[0]];
     const int m = std::min(g0.out, g0.in), nn = std::max(g0.out, g0.in);
     const int nb = (int)grp.size();
+    const long s0 = u->ns_slot0[gi];
+    NsWork& w = ws[gi];  // this group's slots
+    w.X0 += s0 * u->ns_slotx;
+    w.X1 += s0 * u->ns_slotx;
+    w.G += s0 * u->ns_slotg;
+    w.B += s0 * u->ns_slotg;
+    w.Xf += s0 * u->ns_slotf;
+    w.cnt += 3 * s0;
+    small[gi] = ns_small_eligible(m, nn, nb, u->iters);
+    blocks[gi] = muon_group_blocks(g0.out, g0.in, nb);
+    // algorithmic Newton-Schulz flops per step and matrix: 4 m^2 n + 2 m^3
+    ns_flops += (double)nb * u->iters * (4.0 * m * (double)m * nn + 2.0 * m * (double)m * m);
     const long xstride = (long)m * u->ns.ldx;  // one wide m x ldx matrix per batch slot
-    const bool small = ns_small_eligible(m, nn, nb, u->iters);
-    const int blocks = muon_group_blocks(g0.out, g0.in, nb);
-    auto xin = [&](int q) { return u->ns.X0 + q * xstride; };
-    auto xres = [&](int q) { return (const float*)(u->ns.Xf + q * xstride); };
-    {
-      Span sp(u, 6, st, 0);
-      for (int q0 = 0; q0 < nb && !rc; q0 += kMuonGroupMax)
-        rc = launch_muon_x0(muon_args(u, grp, q0, u->ns.ldx, xin, xres), blocks, u->cc, d.mu,
-                            small ? nullptr : u->ns.part + (long)q0 * blocks, st);
-      if (!rc && !small) rc = launch_muon_scale(u->ns.part, blocks, nb, d.eps, u->ns_scale, st);
-    }
+    Span sp(u, 6, st, 0);
+    for (int q0 = 0; q0 < nb && !rc; q0 += kMuonGroupMax)
+      rc = launch_muon_x0(muon_args(u, grp, q0, u->ns.ldx, [&](int q) { return w.X0 + q * xstride; },
+                                    [&](int q) { return (const float*)(w.Xf + q * xstride); }),
+                          blocks[gi], u->cc, d.mu, small[gi] ? nullptr : u->ns.part + (long)q0 * blocks[gi], st);
+    if (!rc && !small[gi])
+      rc = launch_muon_scale(u->ns.part, blocks[gi], nb, d.eps, u->ns_scale + 2 * s0, st);
     if (rc) return rc;
-    {
-      // algorithmic Newton-Schulz flops per step and matrix: 4 m^2 n + 2 m^3
-      Span sp(u, 4, st, (double)nb * u->iters * (4.0 * m * (double)m * nn + 2.0 * m * (double)m * m));
-      rc = ns_run_batched(m, nn, nb, u->coeffs.data(), u->iters, u->ns, u->ns.X0, u->ns.ldx, xstride, u->ns.Xf,
-                          u->ns.ldx, xstride, st, nullptr, nullptr, small ? nullptr : u->ns_scale,
-                          small ? d.eps : -1.0);
+  }
+  {
+    Span sp(u, 4, st, ns_flops);
+    std::vector<NsChainGroupHost> hs;
+    std::vector<size_t> hg;
+    for (size_t gi = 0; gi < ngr; gi++) {
+      if (small[gi]) continue;
+      const Layer& g0 = u->layers[u->ns_groups[gi][0]];
+      const int m = std::min(g0.out, g0.in), nn = std::max(g0.out, g0.in);
+      const long xstride = (long)m * u->ns.ldx;
+      NsChainGroupHost h{};
+      h.m = m;
+      h.n = nn;
+      h.batch = (int)u->ns_groups[gi].size();
+      h.X = ws[gi].X0;
+      h.xbuf[0] = ws[gi].X0;
+      h.xbuf[1] = ws[gi].X1;
+      h.ldx = u->ns.ldx;
+      h.xbs = xstride;
+      h.G = ws[gi].G;
+      h.B = ws[gi].B;
+      h.ldg = u->ns.ldg;
+      h.out_f32 = ws[gi].Xf;
+      h.ld_out = u->ns.ldx;
+      h.obs = xstride;
+      h.scale0 = u->ns_scale + 2 * u->ns_slot0[gi];
+      h.fold_eps = -1.0;
+      h.cnt = ws[gi].cnt;
+      hs.push_back(h);
+      hg.push_back(gi);
     }
-    if (rc) return rc;
-    {
-      Span sp(u, 6, st, 0);
-      for (int q0 = 0; q0 < nb && !rc; q0 += kMuonGroupMax)
-        rc = launch_muon_finalize(muon_args(u, grp, q0, u->ns.ldx, xin, xres), blocks, lr, d.wd, d.mu,
-                                  muon_shape_scale(g0), u->cc, st);
+    std::vector<char> done(ngr, 0);
+    for (size_t k0 = 0; g_ns_one_launch && k0 < hs.size() && !rc; k0 += kNsChainMaxGroups) {
+      const int k = (int)std::min(hs.size() - k0, (size_t)kNsChainMaxGroups);
+      // the counters of these groups and the abort word start at zero
+      PL_CUDA(cudaMemsetAsync(u->ns.cnt, 0, sizeof(unsigned) * (size_t)ns_chain_counter_words(u->ns_batch), st));
+      bool used = false;
+      rc = ns_chain_launch(k, hs.data() + k0, u->coeffs.data(), u->iters, u->ns.cnt + 3 * u->ns_batch, u->ns.err,
+                           st, &used);
+      if (used)
+        for (int j = 0; j < k; j++) done[hg[k0 + j]] = 1;
     }
+    // the short-matrix groups, and any group the chain did not take (a capture without the chain node)
+    for (size_t gi = 0; gi < ngr && !rc; gi++) {
+      if (done[gi]) continue;
+      const Layer& g0 = u->layers[u->ns_groups[gi][0]];
+      const int m = std::min(g0.out, g0.in), nn = std::max(g0.out, g0.in);
+      const long xstride = (long)m * u->ns.ldx;
+      rc = ns_run_batched(m, nn, (int)u->ns_groups[gi].size(), u->coeffs.data(), u->iters, ws[gi], ws[gi].X0,
+                          u->ns.ldx, xstride, ws[gi].Xf, u->ns.ldx, xstride, st, nullptr, nullptr,
+                          small[gi] ? nullptr : u->ns_scale + 2 * u->ns_slot0[gi], small[gi] ? d.eps : -1.0);
+    }
+  }
+  if (rc) return rc;
+  for (size_t gi = 0; gi < ngr; gi++) {
+    const auto& grp = u->ns_groups[gi];
+    const Layer& g0 = u->layers[grp[0]];
+    const long xstride = (long)std::min(g0.out, g0.in) * u->ns.ldx;
+    const NsWork& w = ws[gi];
+    Span sp(u, 6, st, 0);
+    for (int q0 = 0; q0 < (int)grp.size() && !rc; q0 += kMuonGroupMax)
+      rc = launch_muon_finalize(muon_args(u, grp, q0, u->ns.ldx, [&](int q) { return w.X0 + q * xstride; },
+                                          [&](int q) { return (const float*)(w.Xf + q * xstride); }),
+                                blocks[gi], lr, d.wd, d.mu, muon_shape_scale(g0), u->cc, st);
     if (rc) return rc;
   }
   return PL_OK;
@@ -1740,6 +1821,13 @@ extern "C" int pl_test_update_gather(pl_update* u, size_t epoch, size_t mb, void
 extern "C" int pl_test_dp_overlap(int mode) {
   const int prev = g_dp_overlap ? 1 : 0;
   if (mode >= 0) g_dp_overlap = mode != 0;
+  return prev;
+}
+// Test hook: 1 = the bf16 tier's Newton-Schulz chains of all layer groups run in one launch per Muon step
+// (the default), 0 = one launch per group; < 0 queries. Returns the previous mode.
+extern "C" int pl_test_ns_group_launch(int mode) {
+  const int prev = g_ns_one_launch ? 1 : 0;
+  if (mode >= 0) g_ns_one_launch = mode != 0;
   return prev;
 }
 // Test hook: 1 = tight-tier sessions created afterwards run the Muon step of small layers as one launch

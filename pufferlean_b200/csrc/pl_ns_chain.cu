@@ -45,7 +45,7 @@ constexpr int kChainBN = 256;
 constexpr int kChainMaxIters = 16;
 constexpr unsigned kParts = 8;  // epilogue warps per tile, each publishing its own part
 
-constexpr int kChainMaxGroups = 4;
+constexpr int kChainMaxGroups = kNsChainMaxGroups;
 
 // Tensor maps of one group (a batch of same-shape matrices).
 struct NsChainMaps {

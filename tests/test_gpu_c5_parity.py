@@ -107,6 +107,25 @@ def test_c5_widths_one_minibatch_gradient_and_step():
         assert float(dg @ dr / (np.linalg.norm(dg) * np.linalg.norm(dr))) > 0.99
 
 
+def test_c5_one_chain_launch_for_all_groups_is_bit_identical():
+    """The three Newton-Schulz groups of the C5 network (four 2048 x 2048 matrices, the 2048 x 1024
+    encoder, the 65 x 2048 head) in one persistent launch give the same bits as one launch per group."""
+    NT = 2048
+    lay, P, pm, obs, acts, adv, ret, olp, ov = _problem(NT, 0xC6)
+    perm = O.shuffle_perm(NT, 1, 0xC6)
+    Lb = plb.lib()
+    Lb.pl_test_ns_group_launch.argtypes = [C.c_int]
+    prev = Lb.pl_test_ns_group_launch(1)
+    try:
+        one = _device_update(pm, P, obs, acts, adv, ret, olp, ov, perm, NT, 0.02, 0.2, 0.0)
+        Lb.pl_test_ns_group_launch(0)
+        per = _device_update(pm, P, obs, acts, adv, ret, olp, ov, perm, NT, 0.02, 0.2, 0.0)
+    finally:
+        Lb.pl_test_ns_group_launch(prev)
+    assert np.isfinite(one).all() and not np.array_equal(one[:P], pm[:P])
+    assert np.array_equal(one, per)
+
+
 @pytest.mark.parametrize("batch,rows,cols", [(2, 512, 2048), (1, 2048, 2048), (1, 2048, 1024), (1, 1024, 2048)])
 def test_newton_schulz_at_config_shapes_vs_f64(batch, rows, cols):
     torch.manual_seed(rows * 3 + cols)
