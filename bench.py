@@ -540,20 +540,33 @@ def measure_ns_c3(reps=5):
     Xs = [torch.randn(b, r, c, device="cuda", generator=g).to(torch.bfloat16) for b, r, c in groups]
     flops = sum(b * 5 * (4 * min(r, c) ** 2 * max(r, c) + 2 * min(r, c) ** 3) for b, r, c in groups)
 
-    def run():
+    n = len(groups)
+    L.pl_ns_groups_bf16_dev.argtypes = [C.c_size_t, C.POINTER(C.c_void_p)] + [C.POINTER(C.c_size_t)] * 3 + [
+        C.c_double, dp, C.c_size_t, C.c_void_p]
+    ptrs = (C.c_void_p * n)(*[X.data_ptr() for X in Xs])
+    gb, gr, gc = [(C.c_size_t * n)(*[grp[i] for grp in groups]) for i in range(3)]
+
+    def run_grouped():  # the whole config in one call: the two chain batches share one persistent launch
+        check(L.pl_ns_groups_bf16_dev(n, ptrs, gb, gr, gc, 1e-7, co.ctypes.data_as(dp), 5, None), L)
+
+    def run_per_shape():  # one pl_ns_batched_bf16_dev call per shape
         for X, (b, r, c) in zip(Xs, groups):
             check(L.pl_ns_batched_bf16_dev(X.data_ptr(), b, r, c, 1e-7, co.ctypes.data_as(dp), 5, None), L)
 
-    for _ in range(3):
-        run()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        run()
-    e1.record()
-    torch.cuda.synchronize()
-    t = e0.elapsed_time(e1) / reps / 1e3
+    def timed(run):
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps / 1e3
+
+    t = timed(run_per_shape)
+    t_grouped = timed(run_grouped)
     peak_tf, _, kind = peaks()
     burst = None
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -562,7 +575,12 @@ def measure_ns_c3(reps=5):
     tf = flops / t / 1e12
     return {"config": "configs[2]: 64 x {128^2, 512^2, 512x2048}, 5 quintic steps, bf16 in / fp32 acc",
             "flops": flops, "ms": t * 1e3, "achieved_tflops": tf, "peak_tflops": burst or peak_tf,
-            "frac": tf / (burst or peak_tf), "peak_kind": kind + " (bf16 burst)"}
+            "frac": tf / (burst or peak_tf), "peak_kind": kind + " (bf16 burst)",
+            "how": "one pl_ns_batched_bf16_dev call per shape (the 512^2 and 512x2048 batches each one persistent "
+                   "chain launch, the 128^2 batch the fused one-CTA kernel)",
+            "ms_grouped": t_grouped * 1e3,
+            "grouped_how": "one pl_ns_groups_bf16_dev call for the three shapes (the two chains share one launch: "
+                           "slower here, where each batch fills the GPU alone)"}
 
 
 def measure_ns_c3_sharded(comm, rank, world, reps=5, chunks=1):

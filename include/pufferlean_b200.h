@@ -112,6 +112,15 @@ int pl_muon_stepmat(const double* W, const double* G, const double* M, size_t ro
 int pl_ns_batched_bf16_dev(void* X, size_t batch, size_t rows, size_t cols, double eps, const double* coeffs,
                            size_t iters, void* stream);
 
+/* Several such batches in one call: group k is batch[k] matrices of rows[k] x cols[k] at X[k], each
+ * orthogonalised in place with the same bits pl_ns_batched_bf16_dev gives it alone. The wide groups
+ * whose short side exceeds 128 (two steps or more) share one persistent launch, four groups at most
+ * per launch, so that one group's short dependent products run while another's tiles fill the SMs;
+ * the other groups run as pl_ns_batched_bf16_dev runs them, before those. At most 16 groups. No
+ * counterpart in the reference, whose batched Newton-Schulz takes one shape per call. */
+int pl_ns_groups_bf16_dev(size_t ngroups, void* const* X, const size_t* batch, const size_t* rows,
+                          const size_t* cols, double eps, const double* coeffs, size_t iters, void* stream);
+
 /* The same batched Newton-Schulz over the ranks of a communicator (pl_comm_create): every rank passes
  * the same batch and ends with every result, bit-identical to pl_ns_batched_bf16_dev on one GPU. The
  * batch is cut into `chunks` chunks of world * cs matrices; in each chunk a rank orthogonalises its cs

@@ -622,3 +622,100 @@ extern "C" int pl_ns_batched_bf16_dev(void* Xv, size_t batch, size_t rows, size_
   }
   return PL_OK;
 }
+
+extern "C" int pl_ns_groups_bf16_dev(size_t ngroups, void* const* Xs, const size_t* batch, const size_t* rows,
+                                     const size_t* cols, double eps, const double* coeffs, size_t iters,
+                                     void* stream) {
+  using namespace pl;
+  if (ngroups == 0) return PL_OK;
+  PL_REQUIRE(ngroups <= 16, PL_ERR_INVALID, "pl_ns_groups_bf16_dev: %zu groups (at most 16)", ngroups);
+  PL_REQUIRE(Xs && batch && rows && cols, PL_ERR_INVALID, "pl_ns_groups_bf16_dev: NULL group table");
+  PL_REQUIRE(coeffs && iters > 0 && iters <= 64, PL_ERR_INVALID, "Newton-Schulz needs a coefficient table");
+  cudaStream_t st = (cudaStream_t)stream;
+  // The groups pl_ns_batched_bf16_dev runs as one folded chain (wide, short side > 128, two steps or
+  // more) share launches here; every other group runs through it first, as it would alone.
+  std::vector<size_t> chain;
+  for (size_t k = 0; k < ngroups; k++) {
+    if (batch[k] == 0 || rows[k] == 0 || cols[k] == 0) continue;
+    PL_REQUIRE(rows[k] % 8 == 0 && cols[k] % 8 == 0, PL_ERR_INVALID,
+               "batched NS needs rows and cols multiples of 8 (group %zu)", k);
+    if (rows[k] <= cols[k] && rows[k] > 128 && iters >= 2) {
+      chain.push_back(k);
+    } else {
+      const int rc = pl_ns_batched_bf16_dev(Xs[k], batch[k], rows[k], cols[k], eps, coeffs, iters, stream);
+      if (rc) return rc;
+    }
+  }
+  if (chain.empty()) return PL_OK;
+  // workspace regions of their own (256-byte aligned pieces per group): iterates, G, Pm, the first
+  // step's factors, the chain counters and, last, the shared abort word
+  auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
+  size_t xb = 0, gb = 0, sb = 0, cw = 0;
+  for (size_t k : chain) {
+    const size_t m = rows[k], n = cols[k];
+    xb += up(m * n * batch[k] * 2);
+    gb += up(m * m * batch[k] * 2);
+    sb += up(sizeof(float) * 2 * batch[k]);
+    cw += 3 * batch[k];
+  }
+  uint8_t* X0 = (uint8_t*)scratch(30, xb);
+  uint8_t* X1 = (uint8_t*)scratch(31, xb);
+  uint8_t* G = (uint8_t*)scratch(32, gb);
+  uint8_t* B = (uint8_t*)scratch(33, gb);
+  uint8_t* S = (uint8_t*)scratch(34, sb);
+  unsigned* cnt = (unsigned*)scratch(35, sizeof(unsigned) * (cw + 1));
+  if (!X0 || !X1 || !G || !B || !S || !cnt) return PL_ERR_NOMEM;
+  std::vector<NsChainGroupHost> hs;
+  std::vector<NsWork> ws;
+  size_t xo = 0, go = 0, so = 0, co = 0;
+  for (size_t k : chain) {
+    const int m = (int)rows[k], n = (int)cols[k];
+    const long per = (long)m * n;
+    NsWork w;
+    w.ldx = n;
+    w.ldg = m;
+    w.X0 = (__nv_bfloat16*)(X0 + xo);
+    w.X1 = (__nv_bfloat16*)(X1 + xo);
+    w.G = (__nv_bfloat16*)(G + go);
+    w.B = (__nv_bfloat16*)(B + go);
+    w.cnt = cnt + co;
+    NsChainGroupHost h{};
+    h.m = m;
+    h.n = n;
+    h.batch = (int)batch[k];
+    h.X = (__nv_bfloat16*)Xs[k];
+    h.xbuf[0] = w.X0;
+    h.xbuf[1] = w.X1;
+    h.ldx = n;
+    h.xbs = per;
+    h.G = w.G;
+    h.B = w.B;
+    h.ldg = m;
+    h.final_bf16 = h.X;  // in place, as pl_ns_batched_bf16_dev leaves it
+    h.scale0 = (float*)(S + so);
+    h.fold_eps = eps;
+    h.cnt = w.cnt;
+    hs.push_back(h);
+    ws.push_back(w);
+    xo += up((size_t)per * batch[k] * 2);
+    go += up((size_t)m * m * batch[k] * 2);
+    so += up(sizeof(float) * 2 * batch[k]);
+    co += 3 * batch[k];
+  }
+  for (size_t k0 = 0; k0 < hs.size(); k0 += kNsChainMaxGroups) {
+    const int k = (int)std::min(hs.size() - k0, (size_t)kNsChainMaxGroups);
+    PL_CUDA(cudaMemsetAsync(cnt, 0, sizeof(unsigned) * (cw + 1), st));
+    bool used = false;
+    int rc = ns_chain_launch(k, hs.data() + k0, coeffs, (int)iters, cnt + cw, nullptr, st, &used);
+    if (rc) return rc;
+    if (used) continue;
+    for (int j = 0; j < k && !rc; j++) {  // the chain declined (stream capture without it, or switched off)
+      const NsChainGroupHost& h = hs[k0 + j];
+      __nv_bfloat16* res = nullptr;
+      rc = ns_run_batched(h.m, h.n, h.batch, coeffs, (int)iters, ws[k0 + j], h.X, h.n, h.xbs, nullptr, 0, 0, st, h.X,
+                          &res, h.scale0, eps);
+    }
+    if (rc) return rc;
+  }
+  return PL_OK;
+}

@@ -191,3 +191,38 @@ def test_zero_matrices_stay_zero(batch, rows, cols, eps):
     if batch > 1:
         assert bool((X[:-1] == 0).all())
     assert float(X[-1].float().abs().max()) > 0.5
+
+
+def _groups(Xs, shapes, co):
+    L = plb.lib()
+    L.pl_ns_groups_bf16_dev.argtypes = [C.c_size_t, C.POINTER(C.c_void_p)] + [C.POINTER(C.c_size_t)] * 3 + [
+        C.c_double, DP, C.c_size_t, C.c_void_p]
+    n = len(shapes)
+    ptrs = (C.c_void_p * n)(*[X.data_ptr() for X in Xs])
+    b, r, c = [(C.c_size_t * n)(*[s[i] for s in shapes]) for i in range(3)]
+    rc = L.pl_ns_groups_bf16_dev(n, ptrs, b, r, c, 1e-7, co.ctypes.data_as(DP), co.shape[0], None)
+    assert rc == 0, L.pl_last_error()
+    torch.cuda.synchronize()
+    code = C.c_uint(0)
+    assert L.pl_test_device_error(C.byref(code)) == 0 and code.value == 0, hex(code.value)
+
+
+@pytest.mark.parametrize("shapes", [
+    [(8, 128, 128), (8, 512, 512), (8, 512, 2048)],  # configs[2]'s three shapes, fewer matrices each
+    [(2, 256, 1024), (3, 192, 640), (1, 2048, 512), (4, 64, 320), (1, 384, 384)],  # tall, short, ragged tiles
+    [(1, 136, 2048), (2, 200, 264), (1, 512, 512), (2, 256, 256), (1, 1024, 2048)],  # five chain groups: two launches
+])
+def test_groups_entry_matches_one_call_per_shape(shapes):
+    """pl_ns_groups_bf16_dev gives every group the bits pl_ns_batched_bf16_dev gives it alone: the wide
+    groups with a short side above 128 share persistent launches (at most four per launch), the others
+    take the single-shape paths."""
+    g = torch.Generator(device="cuda").manual_seed(0x6E5)
+    co = np.ascontiguousarray(O.QUINTIC_COEFFS)
+    X0 = [torch.randn(b, r, c, device="cuda", generator=g).to(torch.bfloat16) for b, r, c in shapes]
+    Xg = [x.clone() for x in X0]
+    _groups(Xg, shapes, co)
+    for x, xg, (b, r, c) in zip(X0, Xg, shapes):
+        xs = x.clone()
+        _ns(xs, b, r, c, co)
+        assert torch.equal(xg, xs), (b, r, c)
+        assert not torch.equal(xg, x)
