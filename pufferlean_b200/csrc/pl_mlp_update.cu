@@ -347,17 +347,15 @@ static int alloc_session(pl_update* u) {
     }
     if (!placed) u->ns_groups.push_back({(int)l});
   }
-  // each group has slots of its own, so that all groups' Newton-Schulz chains can run in one launch
-  u->ns_batch = 1;
+  // each group has slots of its own (under data parallelism each layer: layer l in slot l), so that
+  // all the Newton-Schulz chains of a Muon step can run in one launch
   u->ns_slot0.clear();
-  if (!u->dp) {
-    long next = 0;
-    for (auto& g : u->ns_groups) {
-      u->ns_slot0.push_back(next);
-      next += (long)g.size();
-    }
-    u->ns_batch = std::max<long>(1, next);
+  long next = 0;
+  for (auto& g : u->ns_groups) {
+    u->ns_slot0.push_back(next);
+    next += (long)g.size();
   }
+  u->ns_batch = std::max<long>(1, u->dp ? (long)u->layers.size() : next);
   if (fast) {
     // one batch slot holds the largest matrix; a group's batch uses slots of its own (smaller) size
     const long slotx = round_up(mmax, 128) * ldx, slotg = round_up(mmax, 128) * ldg;
@@ -506,13 +504,92 @@ static double muon_shape_scale(const Layer& ly) {
   return sqrt(r > 1.0 ? r : 1.0);
 }
 
+// One batch of equal-shape matrices for ns_run_groups: its workspace slots, the wide input (w.X0,
+// leading dimension ldx, xbs between matrices), the fp32 result and the first step's factors.
+struct NsGroupRun {
+  NsWork w;
+  int m = 0, n = 0, batch = 0;
+  long ldx = 0, xbs = 0;
+  float* out = nullptr;
+  long ld_out = 0, obs = 0;
+  bool small = false;     // the fused one-CTA kernel, which normalises the raw input itself
+  float* scale = nullptr;  // otherwise [batch] 1 / (||u|| + eps), [batch] its square
+};
+
+// Newton-Schulz of several batches: those the persistent chain takes share launches
+// (kNsChainMaxGroups each), so that short dependent chains run beside a large batch's tiles; the
+// short-matrix batches, and any the chain declines, run through ns_run_batched on their own slots.
+static int ns_run_groups(pl_update* u, const std::vector<NsGroupRun>& gs, cudaStream_t st) {
+  int rc = PL_OK;
+  std::vector<NsChainGroupHost> hs;
+  std::vector<size_t> hg;
+  for (size_t k = 0; k < gs.size(); k++) {
+    const NsGroupRun& g = gs[k];
+    if (g.small) continue;
+    NsChainGroupHost h{};
+    h.m = g.m;
+    h.n = g.n;
+    h.batch = g.batch;
+    h.X = g.w.X0;
+    h.xbuf[0] = g.w.X0;
+    h.xbuf[1] = g.w.X1;
+    h.ldx = g.ldx;
+    h.xbs = g.xbs;
+    h.G = g.w.G;
+    h.B = g.w.B;
+    h.ldg = g.w.ldg;
+    h.out_f32 = g.out;
+    h.ld_out = g.ld_out;
+    h.obs = g.obs;
+    h.scale0 = g.scale;
+    h.fold_eps = -1.0;
+    h.cnt = g.w.cnt;
+    hs.push_back(h);
+    hg.push_back(k);
+  }
+  std::vector<char> done(gs.size(), 0);
+  for (size_t k0 = 0; g_ns_one_launch && k0 < hs.size() && !rc; k0 += kNsChainMaxGroups) {
+    const int k = (int)std::min(hs.size() - k0, (size_t)kNsChainMaxGroups);
+    // every group's counters and the abort word (the last word) start at zero
+    PL_CUDA(cudaMemsetAsync(u->ns.cnt, 0, sizeof(unsigned) * (size_t)ns_chain_counter_words(u->ns_batch), st));
+    bool used = false;
+    rc = ns_chain_launch(k, hs.data() + k0, u->coeffs.data(), u->iters, u->ns.cnt + 3 * u->ns_batch, u->ns.err, st,
+                         &used);
+    if (used)
+      for (int j = 0; j < k; j++) done[hg[k0 + j]] = 1;
+  }
+  for (size_t k = 0; k < gs.size() && !rc; k++) {
+    if (done[k]) continue;
+    NsWork w = gs[k].w;
+    const NsGroupRun& g = gs[k];
+    rc = ns_run_batched(g.m, g.n, g.batch, u->coeffs.data(), u->iters, w, g.w.X0, g.ldx, g.xbs, g.out, g.ld_out,
+                        g.obs, st, nullptr, nullptr, g.small ? nullptr : g.scale, g.small ? u->d.eps : -1.0);
+  }
+  return rc;
+}
+
+// The workspace view whose first slot is s0.
+static NsWork ns_slots(const pl_update* u, long s0) {
+  NsWork w = u->ns;
+  w.X0 += s0 * u->ns_slotx;
+  w.X1 += s0 * u->ns_slotx;
+  w.G += s0 * u->ns_slotg;
+  w.B += s0 * u->ns_slotg;
+  w.Xf += s0 * u->ns_slotf;
+  w.cnt += 3 * s0;
+  return w;
+}
+
 // Data-parallel Muon: every rank advances the momentum of every layer; each layer's Newton-Schulz
-// runs on its owner rank only (pl_muon_shard_plan), which also writes its unscaled input and the
-// factor; one grouped broadcast hands every rank every orthogonalised update; every rank then applies
-// the identical f64 step, so the weights stay bit-identical across ranks.
+// runs on its owner rank only (pl_muon_shard_plan), which also writes its unscaled input (in the
+// layer's own slot) and the factor, all the rank's layers in one chain launch; one grouped broadcast
+// hands every rank every orthogonalised update; every rank then applies the identical f64 step, so
+// the weights stay bit-identical across ranks.
 static int muon_sharded(pl_update* u, double lr, cudaStream_t st) {
   const pl_update_desc& d = u->d;
   int rc = PL_OK;
+  std::vector<NsGroupRun> runs;
+  double ns_flops = 0.0;
   for (size_t l = 0; l < u->layers.size(); l++) {
     const Layer& ly = u->layers[l];
     const int m = std::min(ly.out, ly.in), nn = std::max(ly.out, ly.in);
@@ -520,19 +597,34 @@ static int muon_sharded(pl_update* u, double lr, cudaStream_t st) {
     const bool small = ns_small_eligible(m, nn, 1, u->iters);
     const int blocks = muon_group_blocks(ly.out, ly.in, 1);
     const std::vector<int> one{(int)l};
+    NsGroupRun r;
+    r.w = ns_slots(u, (long)l);
     {
       Span sp(u, 6, st, 0);
       rc = launch_muon_x0(
-          muon_args(u, one, 0, u->ns.ldx, [&](int) { return own ? u->ns.X0 : (__nv_bfloat16*)nullptr; },
+          muon_args(u, one, 0, u->ns.ldx, [&](int) { return own ? r.w.X0 : (__nv_bfloat16*)nullptr; },
                     [&](int) { return (const float*)u->xres[l]; }),
           blocks, u->cc, d.mu, own && !small ? u->ns.part : nullptr, st);
-      if (!rc && own && !small) rc = launch_muon_scale(u->ns.part, blocks, 1, d.eps, u->ns_scale, st);
+      if (!rc && own && !small) rc = launch_muon_scale(u->ns.part, blocks, 1, d.eps, u->ns_scale + 2 * l, st);
     }
     if (rc) return rc;
     if (!own) continue;
-    Span sp(u, 4, st, (double)u->iters * (4.0 * m * (double)m * nn + 2.0 * m * (double)m * m));
-    rc = ns_run_batched(m, nn, 1, u->coeffs.data(), u->iters, u->ns, u->ns.X0, u->ns.ldx, 0, u->xres[l], nn, 0, st,
-                        nullptr, nullptr, small ? nullptr : u->ns_scale, small ? d.eps : -1.0);
+    r.m = m;
+    r.n = nn;
+    r.batch = 1;
+    r.ldx = u->ns.ldx;
+    r.xbs = (long)m * u->ns.ldx;
+    r.out = u->xres[l];
+    r.ld_out = nn;
+    r.obs = (long)m * nn;
+    r.small = small;
+    r.scale = u->ns_scale + 2 * l;
+    runs.push_back(r);
+    ns_flops += (double)u->iters * (4.0 * m * (double)m * nn + 2.0 * m * (double)m * m);
+  }
+  if (!runs.empty()) {
+    Span sp(u, 4, st, ns_flops);
+    rc = ns_run_groups(u, runs, st);
     if (rc) return rc;
   }
   {
@@ -823,8 +915,7 @@ static int minibatch_fast(pl_update* u, const int* idx, const int* oidx, const v
   // short dependent products of the small groups overlap the large group's; then one finalisation of
   // weights and biases per group
   const size_t ngr = u->ns_groups.size();
-  std::vector<NsWork> ws(ngr, u->ns);
-  std::vector<char> small(ngr);
+  std::vector<NsGroupRun> runs(ngr);
   std::vector<int> blocks(ngr);
   double ns_flops = 0.0;
   for (size_t gi = 0; gi < ngr; gi++) {
@@ -833,85 +924,40 @@ static int minibatch_fast(pl_update* u, const int* idx, const int* oidx, const v
     const int m = std::min(g0.out, g0.in), nn = std::max(g0.out, g0.in);
     const int nb = (int)grp.size();
     const long s0 = u->ns_slot0[gi];
-    NsWork& w = ws[gi];  // this group's slots
-    w.X0 += s0 * u->ns_slotx;
-    w.X1 += s0 * u->ns_slotx;
-    w.G += s0 * u->ns_slotg;
-    w.B += s0 * u->ns_slotg;
-    w.Xf += s0 * u->ns_slotf;
-    w.cnt += 3 * s0;
-    small[gi] = ns_small_eligible(m, nn, nb, u->iters);
+    const long xstride = (long)m * u->ns.ldx;  // one wide m x ldx matrix per batch slot
+    NsGroupRun& r = runs[gi];
+    r.w = ns_slots(u, s0);
+    r.m = m;
+    r.n = nn;
+    r.batch = nb;
+    r.ldx = u->ns.ldx;
+    r.xbs = xstride;
+    r.out = r.w.Xf;
+    r.ld_out = u->ns.ldx;
+    r.obs = xstride;
+    r.small = ns_small_eligible(m, nn, nb, u->iters);
+    r.scale = u->ns_scale + 2 * s0;
     blocks[gi] = muon_group_blocks(g0.out, g0.in, nb);
     // algorithmic Newton-Schulz flops per step and matrix: 4 m^2 n + 2 m^3
     ns_flops += (double)nb * u->iters * (4.0 * m * (double)m * nn + 2.0 * m * (double)m * m);
-    const long xstride = (long)m * u->ns.ldx;  // one wide m x ldx matrix per batch slot
     Span sp(u, 6, st, 0);
     for (int q0 = 0; q0 < nb && !rc; q0 += kMuonGroupMax)
-      rc = launch_muon_x0(muon_args(u, grp, q0, u->ns.ldx, [&](int q) { return w.X0 + q * xstride; },
-                                    [&](int q) { return (const float*)(w.Xf + q * xstride); }),
-                          blocks[gi], u->cc, d.mu, small[gi] ? nullptr : u->ns.part + (long)q0 * blocks[gi], st);
-    if (!rc && !small[gi])
-      rc = launch_muon_scale(u->ns.part, blocks[gi], nb, d.eps, u->ns_scale + 2 * s0, st);
+      rc = launch_muon_x0(muon_args(u, grp, q0, u->ns.ldx, [&](int q) { return r.w.X0 + q * xstride; },
+                                    [&](int q) { return (const float*)(r.w.Xf + q * xstride); }),
+                          blocks[gi], u->cc, d.mu, r.small ? nullptr : u->ns.part + (long)q0 * blocks[gi], st);
+    if (!rc && !r.small) rc = launch_muon_scale(u->ns.part, blocks[gi], nb, d.eps, r.scale, st);
     if (rc) return rc;
   }
   {
     Span sp(u, 4, st, ns_flops);
-    std::vector<NsChainGroupHost> hs;
-    std::vector<size_t> hg;
-    for (size_t gi = 0; gi < ngr; gi++) {
-      if (small[gi]) continue;
-      const Layer& g0 = u->layers[u->ns_groups[gi][0]];
-      const int m = std::min(g0.out, g0.in), nn = std::max(g0.out, g0.in);
-      const long xstride = (long)m * u->ns.ldx;
-      NsChainGroupHost h{};
-      h.m = m;
-      h.n = nn;
-      h.batch = (int)u->ns_groups[gi].size();
-      h.X = ws[gi].X0;
-      h.xbuf[0] = ws[gi].X0;
-      h.xbuf[1] = ws[gi].X1;
-      h.ldx = u->ns.ldx;
-      h.xbs = xstride;
-      h.G = ws[gi].G;
-      h.B = ws[gi].B;
-      h.ldg = u->ns.ldg;
-      h.out_f32 = ws[gi].Xf;
-      h.ld_out = u->ns.ldx;
-      h.obs = xstride;
-      h.scale0 = u->ns_scale + 2 * u->ns_slot0[gi];
-      h.fold_eps = -1.0;
-      h.cnt = ws[gi].cnt;
-      hs.push_back(h);
-      hg.push_back(gi);
-    }
-    std::vector<char> done(ngr, 0);
-    for (size_t k0 = 0; g_ns_one_launch && k0 < hs.size() && !rc; k0 += kNsChainMaxGroups) {
-      const int k = (int)std::min(hs.size() - k0, (size_t)kNsChainMaxGroups);
-      // the counters of these groups and the abort word start at zero
-      PL_CUDA(cudaMemsetAsync(u->ns.cnt, 0, sizeof(unsigned) * (size_t)ns_chain_counter_words(u->ns_batch), st));
-      bool used = false;
-      rc = ns_chain_launch(k, hs.data() + k0, u->coeffs.data(), u->iters, u->ns.cnt + 3 * u->ns_batch, u->ns.err,
-                           st, &used);
-      if (used)
-        for (int j = 0; j < k; j++) done[hg[k0 + j]] = 1;
-    }
-    // the short-matrix groups, and any group the chain did not take (a capture without the chain node)
-    for (size_t gi = 0; gi < ngr && !rc; gi++) {
-      if (done[gi]) continue;
-      const Layer& g0 = u->layers[u->ns_groups[gi][0]];
-      const int m = std::min(g0.out, g0.in), nn = std::max(g0.out, g0.in);
-      const long xstride = (long)m * u->ns.ldx;
-      rc = ns_run_batched(m, nn, (int)u->ns_groups[gi].size(), u->coeffs.data(), u->iters, ws[gi], ws[gi].X0,
-                          u->ns.ldx, xstride, ws[gi].Xf, u->ns.ldx, xstride, st, nullptr, nullptr,
-                          small[gi] ? nullptr : u->ns_scale + 2 * u->ns_slot0[gi], small[gi] ? d.eps : -1.0);
-    }
+    rc = ns_run_groups(u, runs, st);
   }
   if (rc) return rc;
   for (size_t gi = 0; gi < ngr; gi++) {
     const auto& grp = u->ns_groups[gi];
     const Layer& g0 = u->layers[grp[0]];
     const long xstride = (long)std::min(g0.out, g0.in) * u->ns.ldx;
-    const NsWork& w = ws[gi];
+    const NsWork& w = runs[gi].w;
     Span sp(u, 6, st, 0);
     for (int q0 = 0; q0 < (int)grp.size() && !rc; q0 += kMuonGroupMax)
       rc = launch_muon_finalize(muon_args(u, grp, q0, u->ns.ldx, [&](int q) { return w.X0 + q * xstride; },
