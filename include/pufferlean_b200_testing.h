@@ -30,8 +30,8 @@ typedef struct {
 int pl_test_gemm(const pl_test_gemm_args* g, void* stream);
 /* Selects the GEMM's tile mode for every later launch in this process: 0 = single-CTA tiles only,
  * 1 = CTA pairs (cta_group::2, 256-row tiles) where eligible, 2 = CTA pairs for products whose two
- * operands are MN-major (the weight gradients) only; a negative mode only queries. Returns the
- * previous mode. */
+ * operands are MN-major (the weight gradients) only (the default); a negative mode only queries.
+ * Returns the previous mode. */
 int pl_test_gemm_pair_mode(int mode);
 /* Newton-Schulz for matrices with both sides <= 128: 1 = one fused CTA per matrix (the default),
  * 0 = the per-step GEMM chain; a negative mode only queries. Returns the previous mode. */

@@ -18,12 +18,13 @@ GemmKernel gemm_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_b
 GemmKernel gemm_instance_at(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
 GemmKernel gemm_pair_instance(int bn, int epi, bool a_mn, bool b_mn, uint32_t* smem_bytes);
 
-// 0: single CTAs only; 1: CTA pairs for every 256-wide tile of at least 256 rows; 2: CTA pairs for the
-// weight gradients only (both operands MN-major). Measured on the C5 update (262,144-row minibatches):
-// pairs run the weight gradient at 1,152 against 1,052 TFLOP/s, the forward (1,026 vs 1,053) and the
-// data gradient (850 vs 916) slower; the pair form also draws less power per flop (median SM clock
-// 1,440 against 1,372 MHz under the same power cap).
-static int g_pair_mode = 0;
+// 0: single CTAs only; 1: CTA pairs for every 256-wide tile of at least 256 rows; 2 (the default): CTA
+// pairs for the weight gradients only (both operands MN-major). Measured on the C5 update (262,144-row
+// minibatches): pairs run the weight gradient at 1,152 against 1,052 TFLOP/s, the forward (1,026 vs
+// 1,053) and the data gradient (850 vs 916) slower; with pairs for the weight gradients alone the
+// update took 1,852-1,857 against 1,868-1,871 ms in alternating runs on one box (weight gradients
+// 566 against 588 ms per update).
+static int g_pair_mode = 2;
 int gemm_set_pair_mode(int mode) {
   const int prev = g_pair_mode;
   if (mode >= 0) g_pair_mode = mode <= 2 ? mode : 0;

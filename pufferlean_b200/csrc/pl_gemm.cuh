@@ -1300,8 +1300,9 @@ bool gemm_store_map(CUtensorMap* map, const void* ptr, long rows, long cols, lon
 // stored MN-major (storage rows = K) or K-major (storage rows = M or N).
 int gemm_launch(int bn, int epi, bool a_mn, bool b_mn, const Operand& A, const Operand& B, int M, int N, int K,
                 int batch, const EpiArgs& ep, cudaStream_t st);
-// 0 = single-CTA tiles only (default), 1 = CTA pairs where eligible; a negative mode only queries.
-// Returns the previous mode.
+// 0 = single-CTA tiles only, 1 = CTA pairs where eligible, 2 = CTA pairs for the products whose two
+// operands are MN-major (the weight gradients; the default); a negative mode only queries. Returns the
+// previous mode.
 int gemm_set_pair_mode(int mode);
 
 }  // namespace pl
