@@ -632,13 +632,18 @@ extern "C" int pl_ns_groups_bf16_dev(size_t ngroups, void* const* Xs, const size
   PL_REQUIRE(Xs && batch && rows && cols, PL_ERR_INVALID, "pl_ns_groups_bf16_dev: NULL group table");
   PL_REQUIRE(coeffs && iters > 0 && iters <= 64, PL_ERR_INVALID, "Newton-Schulz needs a coefficient table");
   cudaStream_t st = (cudaStream_t)stream;
+  // every group is checked before any of them runs
+  for (size_t k = 0; k < ngroups; k++) {
+    if (batch[k] == 0 || rows[k] == 0 || cols[k] == 0) continue;
+    PL_REQUIRE(Xs[k] != nullptr, PL_ERR_INVALID, "pl_ns_groups_bf16_dev: group %zu has no matrices", k);
+    PL_REQUIRE(rows[k] % 8 == 0 && cols[k] % 8 == 0, PL_ERR_INVALID,
+               "batched NS needs rows and cols multiples of 8 (group %zu: %zu x %zu)", k, rows[k], cols[k]);
+  }
   // The groups pl_ns_batched_bf16_dev runs as one folded chain (wide, short side > 128, two steps or
   // more) share launches here; every other group runs through it first, as it would alone.
   std::vector<size_t> chain;
   for (size_t k = 0; k < ngroups; k++) {
     if (batch[k] == 0 || rows[k] == 0 || cols[k] == 0) continue;
-    PL_REQUIRE(rows[k] % 8 == 0 && cols[k] % 8 == 0, PL_ERR_INVALID,
-               "batched NS needs rows and cols multiples of 8 (group %zu)", k);
     if (rows[k] <= cols[k] && rows[k] > 128 && iters >= 2) {
       chain.push_back(k);
     } else {

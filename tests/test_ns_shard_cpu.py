@@ -86,3 +86,32 @@ def test_sharded_decomposition_equals_one_process(world, batch, chunks):
     ref = _ns_all(X, batch)
     for r in range(world):
         assert np.array_equal(np.frombuffer(outs[r]).reshape(batch, ROWS, COLS), ref), r
+
+
+def test_groups_entry_rejects_bad_tables_before_any_work():
+    """pl_ns_groups_bf16_dev checks every group before it runs any: these fail with PL_ERR_INVALID
+    without a device (a call that reached the GPU would fail with PL_ERR_NO_DEVICE here instead)."""
+    L = plb.lib()
+    fn = L.pl_ns_groups_bf16_dev
+    fn.argtypes = [C.c_size_t, C.POINTER(C.c_void_p)] + [C.POINTER(C.c_size_t)] * 3 + [
+        C.c_double, C.POINTER(C.c_double), C.c_size_t, C.c_void_p]
+    co = np.ascontiguousarray(np.array([[3.4445, -4.7750, 2.0315]] * 5))
+    cp = co.ctypes.data_as(C.POINTER(C.c_double))
+
+    def call(n, shapes, ptrs=None, coeffs=cp, iters=5, table=True):
+        if not table:
+            return fn(n, None, None, None, None, 1e-7, coeffs, iters, None)
+        k = max(len(shapes), 1)
+        X = (C.c_void_p * k)(*(ptrs if ptrs is not None else [0x1000] * k))
+        b, r, c = [(C.c_size_t * k)(*[s[i] for s in shapes] or [0]) for i in range(3)]
+        return fn(n, X, b, r, c, 1e-7, coeffs, iters, None)
+
+    assert call(0, []) == 0  # nothing to do
+    assert call(17, [(1, 8, 8)] * 17) == -1  # more than 16 groups
+    assert call(1, [], table=False) == -1  # no group table
+    assert call(1, [(1, 512, 512)], coeffs=None) == -1  # no coefficients
+    assert call(1, [(1, 512, 512)], iters=0) == -1
+    # the bad group is the last: the first two (one chain group, one fused) must not have run
+    assert call(3, [(2, 512, 512), (2, 64, 64), (1, 512, 100)]) == -1
+    assert "multiples of 8" in plb.lib().pl_last_error().decode()
+    assert call(2, [(2, 512, 512), (1, 256, 256)], ptrs=[0x1000, 0]) == -1  # NULL matrices
