@@ -90,23 +90,41 @@ __global__ void __launch_bounds__(256) lstm_gemm_kernel(int M, int N, int K, int
       if (m < M && n < N) Cz[(long)m * ldc + n] = acc[i][j];
     }
 }
-// out[i] = (double) sum_z part[z*n + i], z ascending
+// out[i] = (double) sum_z part[z*n + i], z ascending. Sixteen slices' loads go out before their sums,
+// which are still taken one by one in slice order (the loads, not the adds, are what the sum waits on).
 template <typename R>
 __global__ void lstm_slice_sum_kernel(const R* __restrict__ part, int nz, long n, double* out) {
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     R s = R(0);
-    for (int z = 0; z < nz; z++) s += part[(long)z * n + i];
+    int z = 0;
+    for (; z + 16 <= nz; z += 16) {
+      R v[16];
+#pragma unroll
+      for (int k = 0; k < 16; k++) v[k] = part[(long)(z + k) * n + i];
+#pragma unroll
+      for (int k = 0; k < 16; k++) s += v[k];
+    }
+    for (; z < nz; z++) s += part[(long)z * n + i];
     out[i] = (double)s;
   }
 }
-// part[chunk][c] = sum of rows [chunk*rows_per, ...) of column c; then out[c] = sum over chunks in order
+// part[chunk][c] = sum of rows [chunk*rows_per, ...) of column c, in row order (sixteen rows' loads
+// ahead of their sums); then out[c] = sum over chunks in order
 template <typename R>
 __global__ void lstm_colsum_part_kernel(const R* __restrict__ M, long rows, int N, int rows_per, R* part) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= N) return;
   const long r0 = (long)blockIdx.y * rows_per, r1 = min(rows, r0 + (long)rows_per);
   R s = R(0);
-  for (long r = r0; r < r1; r++) s += M[r * N + c];
+  long r = r0;
+  for (; r + 16 <= r1; r += 16) {
+    R v[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) v[k] = M[(r + k) * N + c];
+#pragma unroll
+    for (int k = 0; k < 16; k++) s += v[k];
+  }
+  for (; r < r1; r++) s += M[r * N + c];
   part[(long)blockIdx.y * N + c] = s;
 }
 template <typename V>
