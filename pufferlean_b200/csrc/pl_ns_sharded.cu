@@ -1,6 +1,6 @@
-// Batched Newton-Schulz sharded over the ranks of a communicator, the results all-gathered
-// (BASELINE configs[2] at N > 1: "matrices are sharded across 1/2/4/8 GPUs, followed by an
-// all-gather"; the reference has no multi-GPU code, SURVEY 8(e) plans it).
+// Batched Newton-Schulz sharded over the ranks of a communicator, the results all-gathered (the
+// batched Newton-Schulz benchmark at N > 1: "matrices are sharded across 1/2/4/8 GPUs, followed by an
+// all-gather"; the reference has no multi-GPU code).
 //
 // Every rank holds the same batch of inputs and ends with every result. The batch is cut into C
 // chunks of R * cs matrices (R ranks, cs per rank and chunk); in chunk c rank r orthogonalises
